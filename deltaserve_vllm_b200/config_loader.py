@@ -1,0 +1,241 @@
+"""Sectioned YAML launch config.
+
+Accepts the reference launcher's YAML layout unchanged
+(``deltaserve-plugin/deltaserve/config_loader.py:60-131``):
+
+* six finetune sections (``finetune_param``, ``finetune_features``,
+  ``throttles``, ``slo``, ``debug``, ``telemetry``) fold into one flat
+  :class:`FinetuneConfig`; a key in the "wrong" one of the six still loads
+  with a warning; the legacy single ``finetune`` section loads with a note;
+* ``adapter_routing`` becomes an :class:`AdapterRoutingConfig`;
+* ``ft_job`` sets flat finetune fields (``adapter_path`` → ``finetuning_lora_path``
+  ...) plus job metadata;
+* ``server`` and ``adapters`` are returned verbatim as extras;
+* every other section (``model``, ``engine``, ``lora``, ``parallel`` ...) is
+  merged into the :class:`EngineConfig` kwargs; a key in two sections is an
+  error, an unknown key is a ``TypeError``.
+
+Relative paths (keys containing ``path`` or ending in ``_dir``) in the
+finetune sections, ``adapters``, ``adapter_routing`` and ``ft_job`` resolve
+against the YAML file's directory.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+from typing import Any
+
+import yaml
+
+from . import dprint
+from .config import AdapterRoutingConfig, EngineConfig, FinetuneConfig
+
+FINETUNE_SECTIONS: dict[str, tuple[str, ...]] = {
+    "finetune_param": (
+        "enable_finetuning", "start_on_launch", "finetuning_lora_path",
+        "data_path", "max_prepare", "num_epochs", "learning_rate",
+        "weight_decay", "gamma", "max_saved_finetuning_tokens",
+        "adapter_save_path", "adapter_save_every_backwards",
+        "adapter_save_every_epoch", "adapter_save_keep_last",
+        "loss_mask_prefix", "ft_target_modules",
+    ),
+    "finetune_features": (
+        "backward_mps_percentage", "backward_fp32", "backward_cuda_graph",
+        "backward_cuda_graph_attn_bn_max", "backward_cuda_graph_attn_l_max",
+        "backward_run_ahead_boundaries", "save_activations", "save_attn_qkv",
+        "save_attn_ctx", "save_resid_mid", "graph_ft_batches",
+        "graph_ft_max_tokens", "graph_ft_only_batches", "forward_interruptible",
+        "ft_only_admission_grace_ms", "pause_on_arrival", "pause_prefill_always",
+        "pause_until_prefill_done",
+    ),
+    "throttles": (
+        "coserving_admission_phase", "ft_tokens_admission_constrain_factor",
+        "match_prefill_workload_factor", "fwd_token_throttle_enable",
+        "fwd_token_throttle", "rps_throttle_enable", "rps_throttle_close_rps",
+        "rps_throttle_open_rps", "rps_throttle_window_s",
+        "rps_throttle_close_time",
+    ),
+    "slo": (
+        "ttft_slo", "avg_tbt_slo", "avg_tbt_window_s", "max_tbt_slo",
+        "decode_only_ft_safety_margin", "admission_margin", "admission_margin_k",
+        "profile_on_launch", "profile_num_repeats", "validate_estimator",
+        "estimator_validation_path", "estimator_state_save_path",
+        "estimator_state_load_path",
+    ),
+    "debug": (
+        "print_weight_hash", "print_activation_hash", "print_step_mode",
+        "print_scheduler_add", "print_engine_batch_exec",
+        "print_engine_batch_done", "print_engine_req_recv",
+    ),
+    "telemetry": (
+        "metrics_dir", "metrics_interval_s", "steps_log_max_mb",
+        "step_trace_path", "bwd_log_path", "batch_prediction_stats_path",
+    ),
+}
+LEGACY_SECTIONS: tuple[str, ...] = ("finetune",)
+ALL_FINETUNE_SECTIONS = (*FINETUNE_SECTIONS, *LEGACY_SECTIONS)
+SECTION_OF = {k: s for s, keys in FINETUNE_SECTIONS.items() for k in keys}
+RETIRED_KEYS = {"backward_sleep_seconds": "only the removed OPT loss-only service slept"}
+PASSTHROUGH_SECTIONS = ("server", "adapters")
+ADAPTER_ROUTING_SECTION = "adapter_routing"
+FT_JOB_SECTION = "ft_job"
+SPECIAL_SECTIONS = (*ALL_FINETUNE_SECTIONS, *PASSTHROUGH_SECTIONS,
+                    ADAPTER_ROUTING_SECTION, FT_JOB_SECTION)
+
+# ft_job keys that set a flat FinetuneConfig field, and pure job metadata.
+JOB_FLAT_KEYS = {
+    "adapter_path": "finetuning_lora_path",
+    "data_path": "data_path",
+    "num_epochs": "num_epochs",
+    "learning_rate": "learning_rate",
+    "weight_decay": "weight_decay",
+    "gamma": "gamma",
+}
+JOB_META_KEYS = ("name", "stages", "auto_routing", "adapter_init", "save_path")
+
+
+def _is_path_key(key: str) -> bool:
+    k = key.lower()
+    return "path" in k or k.endswith("_dir")
+
+
+def load_yaml_config(path: str | Path, verbose: bool = False) -> dict[str, Any]:
+    """Read a sectioned YAML file into ``{section: {key: value}}`` with
+    relative paths made absolute against the file's directory."""
+    path = Path(path)
+    if not path.is_file():
+        raise FileNotFoundError(f"DeltaServe config not found: {path}")
+    with path.open() as f:
+        raw = yaml.safe_load(f) or {}
+    if not isinstance(raw, dict):
+        raise ValueError(f"{path}: top level must be a mapping of sections, "
+                         f"got {type(raw).__name__}")
+    for section, body in raw.items():
+        if body is not None and not isinstance(body, dict):
+            raise ValueError(f"{path}: section '{section}' must be a mapping "
+                             f"(got {type(body).__name__})")
+    base = path.resolve().parent
+    for section in (*ALL_FINETUNE_SECTIONS, "adapters", ADAPTER_ROUTING_SECTION,
+                    FT_JOB_SECTION):
+        body = raw.get(section) or {}
+        for key, val in body.items():
+            if _is_path_key(key) and isinstance(val, str) and not Path(val).is_absolute():
+                body[key] = str((base / val).resolve())
+    for entry in (raw.get(ADAPTER_ROUTING_SECTION) or {}).get("adapters") or []:
+        if isinstance(entry, dict):
+            for key, val in entry.items():
+                if "path" in key.lower() and isinstance(val, str) \
+                        and not Path(val).is_absolute():
+                    entry[key] = str((base / val).resolve())
+    if verbose:
+        dprint(f"loaded config ({path}):")
+        for section, body in raw.items():
+            kvs = "  ".join(f"{k}={v}" for k, v in (body or {}).items()) or "(empty)"
+            dprint(f"  [{section}] {kvs}")
+    return raw
+
+
+def finetune_kwargs(config: dict[str, Any]) -> dict[str, Any]:
+    """Flat :class:`FinetuneConfig` kwargs from the finetune sections and ``ft_job``."""
+    out: dict[str, Any] = {}
+    for section in LEGACY_SECTIONS:
+        if config.get(section):
+            dprint(f"[config] note: section '{section}' is the old layout "
+                   f"(now finetune_param + finetune_features); loaded as is")
+    for section in ALL_FINETUNE_SECTIONS:
+        for key, value in (config.get(section) or {}).items():
+            if key in RETIRED_KEYS:
+                dprint(f"[config] WARNING: '{section}.{key}' is ignored "
+                       f"({RETIRED_KEYS[key]}); remove it")
+                continue
+            home = SECTION_OF.get(key)
+            if home is not None and home != section and section not in LEGACY_SECTIONS:
+                dprint(f"[config] WARNING: '{section}.{key}' belongs in section "
+                       f"'{home}' (loaded anyway)")
+            if key in out:
+                raise ValueError(f"finetune key '{key}' appears in two sections")
+            out[key] = value
+    job = config.get(FT_JOB_SECTION)
+    if job:
+        meta: dict[str, Any] = {}
+        for key, value in job.items():
+            if key in JOB_FLAT_KEYS:
+                flat = JOB_FLAT_KEYS[key]
+                if flat in out:
+                    raise ValueError(f"'{FT_JOB_SECTION}.{key}' and "
+                                     f"'{SECTION_OF.get(flat)}.{flat}' set the "
+                                     f"same thing; keep one")
+                out[flat] = value
+            elif key in JOB_META_KEYS:
+                meta[key] = value
+            else:
+                raise ValueError(f"unknown '{FT_JOB_SECTION}' key '{key}'; known: "
+                                 f"{sorted((*JOB_META_KEYS, *JOB_FLAT_KEYS))}")
+        out["ft_job"] = meta
+    return out
+
+
+def finetune_value(config: dict[str, Any], key: str, default: Any = None) -> Any:
+    for section in ALL_FINETUNE_SECTIONS:
+        body = config.get(section) or {}
+        if key in body:
+            return body[key]
+    return default
+
+
+def adapter_routing_config(config: dict[str, Any]) -> AdapterRoutingConfig:
+    return AdapterRoutingConfig(**dict(config.get(ADAPTER_ROUTING_SECTION) or {}))
+
+
+def engine_kwargs(config: dict[str, Any]) -> dict[str, Any]:
+    """Every non-special section merged into one flat dict; duplicates are errors."""
+    out: dict[str, Any] = {}
+    for section, body in config.items():
+        if section in SPECIAL_SECTIONS:
+            continue
+        for key, value in (body or {}).items():
+            if key in out:
+                raise ValueError(f"duplicate engine key '{key}' (appears in section "
+                                 f"'{section}' and another section)")
+            out[key] = value
+    return out
+
+
+def split_config(config: dict[str, Any]
+                 ) -> tuple[EngineConfig, FinetuneConfig, AdapterRoutingConfig, dict]:
+    """Split a loaded YAML into (engine, finetune, routing, extras)."""
+    from .engine.ft_job import FinetuneJobSpec
+
+    extras = {name: dict(config.get(name) or {}) for name in PASSTHROUGH_SECTIONS}
+    # vLLM keys the reference YAMLs carry that have no meaning here.
+    ekw = engine_kwargs(config)
+    for ignored in ("disable_log_stats",):
+        ekw.pop(ignored, None)
+    engine = EngineConfig(**ekw)
+    ft = FinetuneConfig(**finetune_kwargs(config))
+    routing = adapter_routing_config(config)
+    if ft.enable_finetuning:
+        FinetuneJobSpec.from_finetune_config(ft).validate(routing.enable_adapter_routing)
+    return engine, ft, routing, extras
+
+
+def load_launch_config(path: str | Path, verbose: bool = False):
+    return split_config(load_yaml_config(path, verbose=verbose))
+
+
+def additional_config(config: dict[str, Any], **overrides: Any) -> dict:
+    """The finetune sections as one JSON-able dict (the reference passed this to
+    ``vllm serve --additional-config``; here it round-trips a config between
+    processes)."""
+    kw = {**finetune_kwargs(config), **{k: v for k, v in overrides.items() if v is not None}}
+    out = {"deltaserve": {k: v for k, v in kw.items() if v is not None}}
+    routing = {k: v for k, v in (config.get(ADAPTER_ROUTING_SECTION) or {}).items()
+               if v is not None}
+    if routing:
+        out["deltaserve_adapter_routing"] = routing
+    return out
+
+
+def finetune_cli_args(config: dict[str, Any], **overrides: Any) -> list[str]:
+    return ["--additional-config", json.dumps(additional_config(config, **overrides))]

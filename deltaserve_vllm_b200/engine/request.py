@@ -1,0 +1,82 @@
+"""Request state for the continuous-batching scheduler."""
+
+from __future__ import annotations
+
+import enum
+import itertools
+import time
+from dataclasses import dataclass, field
+
+
+class Status(enum.Enum):
+    WAITING = 0
+    RUNNING = 1
+    FINISHED = 2
+    ABORTED = 3
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0
+    seed: int | None = None
+    ignore_eos: bool = True
+    stop_token_ids: tuple[int, ...] = ()
+
+
+_counter = itertools.count()
+
+
+@dataclass
+class Request:
+    request_id: str
+    prompt_ids: list[int]
+    params: SamplingParams = field(default_factory=SamplingParams)
+    adapter: str | None = None       # LoRA adapter name (None = base model)
+    arrival_time: float = field(default_factory=time.perf_counter)
+    # Finetuning sample: prefill-only, produces no output token, never shares
+    # KV pages with anything (so a cached prefix can never skip its activations).
+    is_ft: bool = False
+    ft_sample: object = None
+    # -- runtime state --------------------------------------------------
+    status: Status = Status.WAITING
+    output_ids: list[int] = field(default_factory=list)
+    num_computed: int = 0            # tokens whose KV is in the cache
+    block_ids: list[int] = field(default_factory=list)
+    lora_slot: int = -1
+    first_token_time: float | None = None
+    token_times: list[float] = field(default_factory=list)
+    finish_time: float | None = None
+    seq_no: int = field(default_factory=lambda: next(_counter))
+    # Route decision headers, filled by adapter routing.
+    trace: dict = field(default_factory=dict)
+
+    @property
+    def all_ids(self) -> list[int]:
+        return self.prompt_ids + self.output_ids
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt_ids) + len(self.output_ids)
+
+    @property
+    def num_prompt(self) -> int:
+        return len(self.prompt_ids)
+
+    @property
+    def in_prefill(self) -> bool:
+        return self.num_computed < self.num_prompt
+
+    @property
+    def remaining_prefill(self) -> int:
+        return max(0, self.num_prompt - self.num_computed)
+
+    def finished(self) -> bool:
+        return self.status in (Status.FINISHED, Status.ABORTED)
+
+    def ttft(self) -> float | None:
+        return None if self.first_token_time is None else self.first_token_time - self.arrival_time
+
+    def tbts(self) -> list[float]:
+        t = ([self.first_token_time] if self.first_token_time is not None else []) + self.token_times
+        return [b - a for a, b in zip(t, t[1:])]

@@ -1,0 +1,186 @@
+"""Hot ops of the engine.
+
+Every function takes preallocated outputs (so the engine can keep persistent
+buffers and capture CUDA graphs) and routes on the device of its first input:
+CUDA tensors run the sm_100a kernels of ``ops/csrc`` (module ``_C``), CPU
+tensors run the fp32 restatement in :mod:`.reference` — the oracle the tests
+compare against. On a CUDA tensor a missing extension is an error, never a
+silent fallback.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from . import reference as ref
+from .reference import EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM  # noqa: F401
+
+_C = None
+_C_ERR: Exception | None = None
+try:  # the in-tree build (python setup.py build_ext --inplace)
+    from . import _C  # type: ignore
+except Exception as e:  # pragma: no cover - depends on the build
+    _C_ERR = e
+
+
+def native_available() -> bool:
+    return _C is not None
+
+
+def _native():
+    if _C is None:
+        raise RuntimeError(
+            "deltaserve_vllm_b200 CUDA extension is not built or failed to load "
+            f"({_C_ERR!r}); run `python setup.py build_ext --inplace`")
+    return _C
+
+
+def check_device_error(clear: bool = True) -> int:
+    """Error code written by a kernel whose bounded wait gave up (0 = none)."""
+    if _C is None or not torch.cuda.is_available():
+        return 0
+    return int(_C.read_error(clear))
+
+
+# ----------------------------------------------------------------- GEMM
+
+def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None,
+         lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0):
+    """``out = a @ b.T`` (``b`` is [N, K]) or ``a @ b`` (``b_mn``: ``b`` is [K, N]),
+    plus the segmented LoRA expand ``z @ b2.T`` and the epilogue ``epi``:
+    bf16 / fp32 store, fp32 accumulate, or SwiGLU over 64-interleaved
+    gate/up columns. ``save`` receives raw accumulator rows [save_lo, save_hi)."""
+    if a.is_cuda:
+        _native().gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save,
+                       save_lo, save_hi, save_dst, force_bn)
+        return out
+    return ref.gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi,
+                    save_dst)
+
+
+def linear(x, w, out=None, epi=EPI_BF16, **kw):
+    if out is None:
+        n = w.shape[0]
+        if epi == EPI_SWIGLU:
+            n //= 2
+        dt = torch.float32 if epi in (EPI_F32, EPI_F32_ACCUM) else x.dtype
+        out = torch.empty(x.shape[0], n, dtype=dt, device=x.device)
+    return gemm(x, w, out, epi=epi, **kw)
+
+
+# ----------------------------------------------------------------- norms / rope
+
+def rms_norm(x, w, out, eps, *, residual=None, save=None, save_lo=0, save_hi=0, save_dst=0):
+    """``out = rmsnorm(x [+ residual]) * w``; with ``residual`` the sum is written
+    back into ``residual`` (the residual stream). ``save`` captures rows
+    [save_lo, save_hi) of the (updated) stream."""
+    if x.is_cuda:
+        _native().rms_norm(x, residual, w, out, eps, save, save_lo, save_hi, save_dst)
+        return out
+    return ref.rms_norm(x, residual, w, out, eps, save, save_lo, save_hi, save_dst)
+
+
+def qk_norm_rope_cache(qkv, positions, cos_sin, q_norm, k_norm, eps, num_heads, num_kv_heads,
+                       k_cache=None, v_cache=None, slot_mapping=None):
+    if qkv.is_cuda:
+        _native().qk_norm_rope_cache(qkv, positions, cos_sin, q_norm, k_norm, eps, num_heads,
+                                     num_kv_heads, k_cache, v_cache, slot_mapping)
+        return
+    ref.qk_norm_rope_cache(qkv, positions, cos_sin, q_norm, k_norm, eps, num_heads, num_kv_heads,
+                           k_cache, v_cache, slot_mapping)
+
+
+# ----------------------------------------------------------------- attention
+
+def prefill_tiles(cu_q: list[int], bm: int = 64) -> list[tuple[int, int]]:
+    """(sequence, first query) of every 64-query tile of a varlen batch."""
+    out = []
+    for s in range(len(cu_q) - 1):
+        n = cu_q[s + 1] - cu_q[s]
+        for q0 in range(0, n, bm):
+            out.append((s, q0))
+    return out
+
+
+def paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, out, num_heads,
+                  scale):
+    if q.is_cuda:
+        _native().paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, out,
+                                num_heads, scale)
+        return out
+    return ref.paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, num_heads, scale)
+
+
+def decode_splits(batch: int, num_kv_heads: int, max_ctx: int, num_sms: int = 148) -> tuple[int, int]:
+    """Split-KV factor so that batch x kv_heads x splits fills the GPU twice."""
+    want = max(1, (2 * num_sms) // max(1, batch * num_kv_heads))
+    keys = max(64, -(-max_ctx // want))
+    keys = -(-keys // 64) * 64
+    return max(1, -(-max_ctx // keys)), keys
+
+
+def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale,
+                 part_o=None, part_ml=None, splits=1, keys_per_split=0):
+    if q.is_cuda:
+        _native().paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, part_o, part_ml,
+                               num_heads, scale, splits, keys_per_split)
+        return out
+    return ref.paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale)
+
+
+# ----------------------------------------------------------------- LoRA / misc
+
+def lora_shrink(x, A, slot_ids, Z, seg):
+    if x.is_cuda:
+        _native().lora_shrink(x, A, slot_ids, Z, seg)
+        return Z
+    return ref.lora_shrink(x, A, slot_ids, Z, seg)
+
+
+def embedding(ids, table, out, v0=0):
+    if ids.is_cuda:
+        _native().embedding(ids, table, out, v0)
+        return out
+    return ref.embedding(ids, table, out, v0)
+
+
+def ce_fwd_bwd(logits, targets, loss, grad=None, gscale=1.0):
+    if logits.is_cuda:
+        _native().ce_fwd_bwd(logits, targets, loss, grad, gscale)
+        return
+    ref.ce_fwd_bwd(logits, targets, loss, grad, gscale)
+
+
+def seg_sumsq(g, seg_len, out):
+    if g.is_cuda:
+        _native().seg_sumsq(g, seg_len, out)
+        return out
+    ref.seg_sumsq(g, seg_len, out)
+    return out
+
+
+def adamw(p, g, m, v, *, seg_len, seg_sumsq_t=None, max_norm=0.0, grad_scale=1.0, lr=1e-4,
+          b1=0.9, b2=0.999, eps=1e-8, wd=0.0, step=1):
+    if p.is_cuda:
+        _native().adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd,
+                        step)
+        return
+    ref.adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd, step)
+
+
+def lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale):
+    if A_src.is_cuda:
+        _native().lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale)
+        return
+    ref.lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale)
+
+
+def sample(logits, temps, seeds, out):
+    if logits.is_cuda:
+        _native().sample(logits, temps, seeds, out)
+        return out
+    ref.sample(logits, temps, seeds, out)
+    return out

@@ -1,0 +1,472 @@
+// Paged-KV attention for sm_100a: varlen causal prefill (chunked prefill
+// included) and split-KV GQA decode, bf16 in, fp32 softmax.
+//
+// KV cache layout per layer: k_cache / v_cache [num_blocks, Hkv, BS, 128] bf16,
+// so one (page, head) is a contiguous BS x 128 tile. A sequence's pages come
+// from block_tables[seq, :]. Query i of a sequence with q_len new tokens and
+// total context ctx sits at position ctx - q_len + i and sees keys <= that.
+//
+// Prefill: one CTA = 64 queries x 1 head, 4 warps x 16 rows, K/V tiles of 64
+// keys double-buffered through cp.async into XOR-swizzled shared memory,
+// QK^T and PV on the warp-level tensor-core path (m16n8k16), online softmax
+// in fp32 registers.
+// Decode: one CTA = (sequence, KV head, KV split): the GQA group's queries
+// share every K/V byte read; partial (max, sum, out) go to a workspace and a
+// second kernel merges the splits.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dsv {
+
+constexpr int HD = 128;          // head dim (all supported models)
+constexpr int PF_BM = 64;        // queries per CTA
+constexpr int PF_BN = 64;        // keys per iteration
+constexpr int PF_THREADS = 128;  // 4 warps
+
+// Swizzled offset (in bf16 elements) of 16-byte chunk `c` (0..15) of row `r`
+// in a [rows x 128] bf16 tile: chunks are XOR-permuted by row % 8 so that
+// ldmatrix of 8 rows at one column hits 8 different bank groups.
+__device__ __forceinline__ int swz(int r, int c) { return r * HD + ((c ^ (r & 7)) << 3); }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct PrefillArgs {
+  const __nv_bfloat16* q;   // [T, ...] row stride q_stride, head h at h*128
+  int q_stride;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  const int* block_tables;  // [S, max_blocks]
+  int max_blocks;
+  const int* cu_q;          // [S+1] query offsets
+  const int* ctx_lens;      // [S] total context after this step
+  const int* tile_info;     // [num_tiles, 2] = (seq, first query of the tile)
+  __nv_bfloat16* out;       // [T, Hq*128] row stride out_stride
+  int out_stride;
+  int num_kv_heads, group, block_size;
+  float scale_log2;         // softmax scale * log2(e)
+};
+
+__global__ void __launch_bounds__(PF_THREADS) paged_prefill_kernel(PrefillArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  __nv_bfloat16* sK = sQ + PF_BM * HD;      // [2][64*128]
+  __nv_bfloat16* sV = sK + 2 * PF_BN * HD;  // [2][64*128]
+
+  const int tile = blockIdx.x;
+  const int head = blockIdx.y;
+  const int kvh = head / a.group;
+  const int seq = a.tile_info[2 * tile];
+  const int qt0 = a.tile_info[2 * tile + 1];  // first query index within the sequence
+  const int q_begin = a.cu_q[seq];
+  const int q_len = a.cu_q[seq + 1] - q_begin;
+  const int ctx = a.ctx_lens[seq];
+  const int pos0 = ctx - q_len;  // position of query 0
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int* btab = a.block_tables + (size_t)seq * a.max_blocks;
+
+  // Q tile -> smem (rows past the sequence are zero).
+  for (int i = tid; i < PF_BM * 16; i += PF_THREADS) {
+    int r = i / 16, c = i % 16;
+    int qi = qt0 + r;
+    bool ok = qi < q_len;
+    const __nv_bfloat16* src = a.q + (size_t)(q_begin + (ok ? qi : 0)) * a.q_stride + head * HD + c * 8;
+    cp_async16(sQ + swz(r, c), src, ok);
+  }
+  // Keys visible to the last query of this tile.
+  const int last_q = min(qt0 + PF_BM, q_len) - 1;
+  const int kv_end = pos0 + last_q + 1;
+  const int n_kb = (kv_end + PF_BN - 1) / PF_BN;
+
+  auto load_kv = [&](int kb, int buf) {
+    for (int i = tid; i < PF_BN * 16; i += PF_THREADS) {
+      int r = i / 16, c = i % 16;
+      int kpos = kb * PF_BN + r;
+      bool ok = kpos < kv_end;
+      int kp = ok ? kpos : 0;
+      int page = btab[kp / a.block_size];
+      size_t off = (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
+      cp_async16(sK + buf * PF_BN * HD + swz(r, c), a.k_cache + off, ok);
+      cp_async16(sV + buf * PF_BN * HD + swz(r, c), a.v_cache + off, ok);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  uint32_t qf[8][4];
+  const int g = lane >> 2, tq = lane & 3;
+  const int row0 = warp * 16;  // first row of this warp in the tile
+
+  for (int kb = 0; kb < n_kb; ++kb) {
+    const int buf = kb & 1;
+    if (kb + 1 < n_kb) load_kv(kb + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (kb == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        int r = row0 + (lane & 15), c = ks * 2 + (lane >> 4);
+        ldsm_x4(qf[ks], sQ + swz(r, c));
+      }
+    }
+    const __nv_bfloat16* k_t = sK + buf * PF_BN * HD;
+    const __nv_bfloat16* v_t = sV + buf * PF_BN * HD;
+    // S = Q K^T  (16 x 64 per warp)
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        uint32_t b[4];
+        int key = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+        int c = ks * 2 + ((lane >> 3) & 1);
+        ldsm_x4(b, k_t + swz(key, c));
+        mma_bf16(s[2 * jp], qf[ks], b[0], b[1]);
+        mma_bf16(s[2 * jp + 1], qf[ks], b[2], b[3]);
+      }
+    }
+    // Mask + online softmax (rows g and g+8 of this warp).
+    const bool need_mask = (kb + 1) * PF_BN > pos0 + qt0 + row0 + 1 || (kb + 1) * PF_BN > kv_end;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[j][e] * a.scale_log2;
+        if (need_mask) {
+          int qrow = qt0 + row0 + g + ((e >> 1) << 3);
+          int kpos = kb * PF_BN + j * 8 + 2 * tq + (e & 1);
+          if (kpos > pos0 + qrow || kpos >= kv_end) v = -INFINITY;
+        }
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      float m_new = fmaxf(m_r[h], mx[h]);
+      corr[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_r[h] - m_new);
+      m_r[h] = m_new;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float mm = m_r[e >> 1];
+        float p = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
+        s[j][e] = p;
+        rs[e >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_r[h] = l_r[h] * corr[h] + rs[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b[4];
+        int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        int c = dp * 2 + (lane >> 4);
+        ldsm_x4_t(b, v_t + swz(key, c));
+        mma_bf16(o[2 * dp], pa, b[0], b[1]);
+        mma_bf16(o[2 * dp + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  // Normalise and store.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int qi = qt0 + row0 + g + h * 8;
+    if (qi >= q_len) continue;
+    const float inv = l_r[h] > 0.f ? 1.f / l_r[h] : 0.f;
+    __nv_bfloat16* dst = a.out + (size_t)(q_begin + qi) * a.out_stride + head * HD;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      *reinterpret_cast<uint32_t*>(dst + j * 8 + 2 * tq) = pack_bf16(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ decode
+
+constexpr int DC_KEYS = 64;  // keys per inner chunk
+constexpr int DC_THREADS = 128;
+constexpr int DC_MAX_GROUP = 8;
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;  // [B, ...] row stride q_stride
+  int q_stride;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  const int* block_tables;
+  int max_blocks;
+  const int* ctx_lens;     // [B]
+  float* part_o;           // [B, Hq, splits, 128]
+  float* part_ml;          // [B, Hq, splits, 2]
+  __nv_bfloat16* out;      // [B, Hq*128] row stride out_stride
+  int out_stride;
+  int num_heads, num_kv_heads, group, block_size, splits, keys_per_split;
+  float scale_log2;
+};
+
+__global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) {
+  __shared__ __align__(16) __nv_bfloat16 sK[DC_KEYS * HD];
+  __shared__ __align__(16) __nv_bfloat16 sV[DC_KEYS * HD];
+  __shared__ float sQ[DC_MAX_GROUP][HD];
+  __shared__ float sS[DC_MAX_GROUP][DC_KEYS];
+  __shared__ float sPart[2][DC_MAX_GROUP][DC_KEYS];
+
+  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int G = a.group;
+  const int ctx = a.ctx_lens[b];
+  const int k_begin = split * a.keys_per_split;
+  const int k_end = min(ctx, k_begin + a.keys_per_split);
+  const int* btab = a.block_tables + (size_t)b * a.max_blocks;
+
+  for (int i = tid; i < G * HD; i += DC_THREADS) {
+    int gq = i / HD, d = i % HD;
+    sQ[gq][d] = bf2f(a.q[(size_t)b * a.q_stride + (kvh * G + gq) * HD + d]) * a.scale_log2;
+  }
+  float m_run[DC_MAX_GROUP], l_run[DC_MAX_GROUP], acc[DC_MAX_GROUP];
+#pragma unroll
+  for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
+    m_run[gq] = -INFINITY;
+    l_run[gq] = 0.f;
+    acc[gq] = 0.f;
+  }
+  __syncthreads();
+  for (int k0 = k_begin; k0 < k_end; k0 += DC_KEYS) {
+    // Stage K and V of up to 64 keys.
+    for (int i = tid; i < DC_KEYS * 16; i += DC_THREADS) {
+      int r = i / 16, c = i % 16;
+      int kpos = k0 + r;
+      bool ok = kpos < k_end;
+      int kp = ok ? kpos : k_begin;
+      int page = btab[kp / a.block_size];
+      size_t off = (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
+      cp_async16(sK + r * HD + c * 8, a.k_cache + off, ok);
+      cp_async16(sV + r * HD + c * 8, a.v_cache + off, ok);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    // Scores: thread = (key, half of the head dim).
+    {
+      const int key = tid % DC_KEYS, half = tid / DC_KEYS;
+      float part[DC_MAX_GROUP];
+#pragma unroll
+      for (int gq = 0; gq < DC_MAX_GROUP; ++gq) part[gq] = 0.f;
+      const __nv_bfloat16* kr = sK + key * HD + half * 64;
+#pragma unroll 4
+      for (int d = 0; d < 64; d += 2) {
+        float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kr + d));
+#pragma unroll
+        for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
+          if (gq < G) part[gq] += kv.x * sQ[gq][half * 64 + d] + kv.y * sQ[gq][half * 64 + d + 1];
+        }
+      }
+#pragma unroll
+      for (int gq = 0; gq < DC_MAX_GROUP; ++gq)
+        if (gq < G) sPart[half][gq][key] = part[gq];
+    }
+    __syncthreads();
+    for (int i = tid; i < G * DC_KEYS; i += DC_THREADS) {
+      int gq = i / DC_KEYS, key = i % DC_KEYS;
+      sS[gq][key] = (k0 + key < k_end) ? sPart[0][gq][key] + sPart[1][gq][key] : -INFINITY;
+    }
+    __syncthreads();
+    // Online softmax + PV: thread = head-dim column d; every thread walks the
+    // 64 scores of each head (broadcast reads).
+    const int d = tid;
+#pragma unroll
+    for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
+      if (gq >= G) break;
+      float mx = -INFINITY;
+      for (int key = 0; key < DC_KEYS; ++key) mx = fmaxf(mx, sS[gq][key]);
+      float m_new = fmaxf(m_run[gq], mx);
+      float corr = (m_run[gq] == -INFINITY) ? 0.f : exp2f(m_run[gq] - m_new);
+      float lsum = 0.f, o = 0.f;
+      for (int key = 0; key < DC_KEYS; ++key) {
+        float p = (sS[gq][key] == -INFINITY) ? 0.f : exp2f(sS[gq][key] - m_new);
+        lsum += p;
+        o += p * bf2f(sV[key * HD + d]);
+      }
+      l_run[gq] = l_run[gq] * corr + lsum;
+      acc[gq] = acc[gq] * corr + o;
+      m_run[gq] = m_new;
+    }
+    __syncthreads();
+  }
+  // Partial results of this split.
+  for (int gq = 0; gq < G; ++gq) {
+    const int h = kvh * G + gq;
+    size_t idx = ((size_t)b * a.num_heads + h) * a.splits + split;
+    a.part_o[idx * HD + tid] = acc[gq];
+    if (tid == 0) {
+      a.part_ml[idx * 2 + 0] = m_run[gq];
+      a.part_ml[idx * 2 + 1] = l_run[gq];
+    }
+  }
+}
+
+__global__ void decode_combine_kernel(DecodeArgs a) {
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  size_t base = ((size_t)b * a.num_heads + h) * a.splits;
+  float m = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) m = fmaxf(m, a.part_ml[(base + s) * 2]);
+  float l = 0.f, o = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    float ms = a.part_ml[(base + s) * 2];
+    if (ms == -INFINITY) continue;
+    float w = exp2f(ms - m);
+    l += a.part_ml[(base + s) * 2 + 1] * w;
+    o += a.part_o[(base + s) * HD + d] * w;
+  }
+  a.out[(size_t)b * a.out_stride + h * HD + d] = f2bf(l > 0.f ? o / l : 0.f);
+}
+
+}  // namespace dsv
+
+// ---------------------------------------------------------------- bindings
+
+void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                       torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
+                       int64_t num_heads, double scale) {
+  using namespace dsv;
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16, "prefill: bf16");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == HD, "prefill: cache [blocks, Hkv, BS, 128]");
+  TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "prefill: contiguous rows");
+  const int num_tiles = (int)tile_info.size(0);
+  if (num_tiles == 0) return;
+  c10::cuda::CUDAGuard guard(q.device());
+  PrefillArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.q_stride = (int)q.stride(0);
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.max_blocks = (int)block_tables.size(1);
+  a.cu_q = cu_q.data_ptr<int>();
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.tile_info = tile_info.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_stride = (int)out.stride(0);
+  a.num_kv_heads = (int)k_cache.size(1);
+  a.block_size = (int)k_cache.size(2);
+  a.group = (int)(num_heads / a.num_kv_heads);
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  const int smem = (PF_BM * HD + 4 * PF_BN * HD) * 2;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  dim3 grid(num_tiles, (unsigned)num_heads);
+  paged_prefill_kernel<<<grid, PF_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// part_o / part_ml: caller-provided workspaces of at least B*Hq*splits*128 and
+// B*Hq*splits*2 floats.
+void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                      torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
+                      int64_t num_heads, double scale, int64_t splits, int64_t keys_per_split) {
+  using namespace dsv;
+  const int B = (int)ctx_lens.size(0);
+  if (B == 0) return;
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == HD, "decode: cache [blocks, Hkv, BS, 128]");
+  TORCH_CHECK(keys_per_split % DC_KEYS == 0, "decode: keys_per_split must be a multiple of 64");
+  const int Hkv = (int)k_cache.size(1);
+  const int G = (int)(num_heads / Hkv);
+  TORCH_CHECK(G >= 1 && G <= DC_MAX_GROUP, "decode: GQA group must be 1..8");
+  TORCH_CHECK(part_o.numel() >= (int64_t)B * num_heads * splits * HD && part_ml.numel() >= (int64_t)B * num_heads * splits * 2,
+              "decode: workspace too small");
+  c10::cuda::CUDAGuard guard(q.device());
+  DecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.q_stride = (int)q.stride(0);
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.max_blocks = (int)block_tables.size(1);
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.part_o = part_o.data_ptr<float>();
+  a.part_ml = part_ml.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_stride = (int)out.stride(0);
+  a.num_heads = (int)num_heads;
+  a.num_kv_heads = Hkv;
+  a.group = G;
+  a.block_size = (int)k_cache.size(2);
+  a.splits = (int)splits;
+  a.keys_per_split = (int)keys_per_split;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  paged_decode_kernel<<<dim3(B, Hkv, (unsigned)splits), DC_THREADS, 0, s>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  decode_combine_kernel<<<dim3(B, (unsigned)num_heads), HD, 0, s>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,48 @@
+// Python bindings of the sm_100a kernels (module deltaserve_vllm_b200.ops._C).
+#include <torch/extension.h>
+
+void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
+              c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
+              int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
+              int64_t save_dst, int64_t force_bn);
+int64_t dsv_read_error_gemm(bool clear);
+static int64_t dsv_read_error(bool clear) { return dsv_read_error_gemm(clear); }
+void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                       torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
+                       int64_t num_heads, double scale);
+void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                      torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
+                      int64_t num_heads, double scale, int64_t splits, int64_t keys_per_split);
+void dsv_rms_norm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor out,
+                  double eps, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi, int64_t save_dst);
+void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
+                            c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double eps,
+                            int64_t num_heads, int64_t num_kv_heads, c10::optional<torch::Tensor> k_cache,
+                            c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slot_mapping);
+void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t seg);
+void dsv_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t v0);
+void dsv_ce_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss,
+                    c10::optional<torch::Tensor> grad, double gscale);
+void dsv_seg_sumsq(torch::Tensor g, int64_t seg_len, torch::Tensor out);
+void dsv_adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, int64_t seg_len,
+               c10::optional<torch::Tensor> seg_sumsq, double max_norm, double grad_scale, double lr, double b1,
+               double b2, double eps, double wd, int64_t step);
+void dsv_lora_publish(torch::Tensor A_src, torch::Tensor A_dst, torch::Tensor Bt_src, torch::Tensor B2_dst,
+                      int64_t col0, int64_t b1, int64_t b2, bool interleave64, double scale);
+void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemm", &dsv_gemm, "tcgen05 GEMM with fused epilogues / LoRA expand");
+  m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
+  m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
+  m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");
+  m.def("rms_norm", &dsv_rms_norm, "RMSNorm / fused residual add + RMSNorm (+ row capture)");
+  m.def("qk_norm_rope_cache", &dsv_qk_norm_rope_cache, "q/k norm + RoPE + paged KV write");
+  m.def("lora_shrink", &dsv_lora_shrink, "segmented multi-LoRA shrink");
+  m.def("embedding", &dsv_embedding, "vocab-parallel embedding gather");
+  m.def("ce_fwd_bwd", &dsv_ce_fwd_bwd, "cross-entropy loss + gradient rows");
+  m.def("seg_sumsq", &dsv_seg_sumsq, "per-segment sum of squares");
+  m.def("adamw", &dsv_adamw, "flat AdamW with per-segment clipping");
+  m.def("lora_publish", &dsv_lora_publish, "publish fp32 LoRA masters into a served slot");
+  m.def("sample", &dsv_sample, "greedy / Gumbel-max sampling");
+}

@@ -1,0 +1,492 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = A[M, K] . B^T            (B stored [N, K] row-major: "K-major")
+//   C[M, K] = A[M, N] . W              (W stored [N, K] row-major: "MN-major" B)
+//   + optional fused multi-LoRA expand:  C += Z[M, S*SEG] . B2[N, S*SEG]^T, where
+//     only the LoRA slots present in an M tile are visited (segmented expand).
+//
+// Design (one CTA per SM, 256 threads):
+//   warp 0      TMA producer: A/B tiles (128 x 64 and BN x 64 bf16, 128-byte
+//               swizzle) into a STAGES-deep shared-memory ring;
+//   warp 1      one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into a
+//               TMEM accumulator, and tcgen05.commit releases the smem stage;
+//   warp 2      allocates / frees TMEM (two accumulators of BN fp32 columns, so
+//               the epilogue of tile i overlaps the main loop of tile i+1);
+//   warps 4-7   epilogue: tcgen05.ld the accumulator (each warp owns 32 TMEM
+//               lanes = 32 rows), convert, fuse (SwiGLU, FT-row save) and store.
+// Tiles are walked M-fastest so CTAs running together share one weight tile
+// (read once from HBM, the activation tiles hit L2).
+//
+// No TMA load here uses cluster multicast, and every wait is bounded
+// (common.cuh): a stuck pipeline records an error code and the kernel returns.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace dsv {
+
+
+enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3 };
+
+struct GemmArgs {
+  int M, N, K;            // C is M x N; K is the reduction length of the main term
+  int lora_seg;           // LoRA: columns of Z / B2 per slot (multiple of 64); 0 = no LoRA term
+  int num_slots;          // LoRA slots (<= 32)
+  const uint32_t* tile_slots;  // [ceil(M/128)] bitmask of slots present in each M tile
+  void* C;
+  int ldc;                // elements
+  __nv_bfloat16* save;    // optional: raw accumulator rows [save_lo, save_hi) -> save[save_dst + r - save_lo]
+  int ld_save, save_lo, save_hi, save_dst;
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+template <int BN, bool B_MN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float* v, int n_valid) {
+  // 32 values -> bf16; vector path when all 32 columns are in range and 16B aligned.
+  if (n_valid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    uint32_t packed[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      packed[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  } else {
+    for (int i = 0; i < 32 && i < n_valid; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+__device__ __forceinline__ void store_row_f32(float* dst, const float* v, int n_valid, bool accum) {
+  if (!accum && n_valid >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    for (int i = 0; i < 32 && i < n_valid; ++i) dst[i] = accum ? dst[i] + v[i] : v[i];
+  }
+}
+
+template <int BN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(256, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
+  using Cfg = GemmCfg<BN, B_MN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2]
+  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m_tiles = (args.M + BM - 1) / BM;
+  const int num_n_tiles = (args.N + BN - 1) / BN;
+  const int num_tiles = num_m_tiles * num_n_tiles;
+  const int kb_main = (args.K + BK - 1) / BK;
+  const int kb_per_slot = args.lora_seg / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 2) tmem_alloc(tmem_base_smem, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (args.lora_seg > 0) {
+      tma_prefetch_desc(&tmZ);
+      tma_prefetch_desc(&tmB2);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int fills[STAGES > 0 ? STAGES : 1];
+    for (int s = 0; s < STAGES; ++s) fills[s] = 0;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
+      const int m0 = mt * BM, n0 = nt * BN;
+      const uint32_t slots = (args.lora_seg > 0) ? args.tile_slots[mt] : 0u;
+      const int n_lora = __popc(slots) * kb_per_slot;
+      for (int kb = 0; kb < kb_main + n_lora; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
+        uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
+        uint8_t* sB = sA + Cfg::A_BYTES;
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+        if (kb < kb_main) {
+          const int k0 = kb * BK;
+          tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * (64 * BK * 2), &tmB, &full_bar[stage], n0 + j * 64, k0);
+          } else {
+            tma_load_2d(sB, &tmB, &full_bar[stage], k0, n0);
+          }
+        } else {
+          // LoRA expand block: the (lb / kb_per_slot)-th present slot.
+          int lb = kb - kb_main;
+          int which = lb / kb_per_slot, sub = lb % kb_per_slot;
+          uint32_t m = slots;
+          for (int i = 0; i < which; ++i) m &= m - 1;
+          const int slot = __ffs(m) - 1;
+          const int k0 = slot * args.lora_seg + sub * BK;
+          tma_load_2d(sA, &tmZ, &full_bar[stage], k0, m0);
+          tma_load_2d(sB, &tmB2, &full_bar[stage], k0, n0);
+        }
+        fills[stage]++;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // Drain: every copy this thread issued has landed before the CTA can exit.
+    for (int s = 0; s < STAGES; ++s) {
+      if (fills[s] == 0) continue;
+      uint32_t par = (uint32_t)((fills[s] - 1) & 1);
+      uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full_bar[s], par)) {
+        if (globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitFull); break; }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+      const int mt = t % num_m_tiles;
+      const uint32_t slots = (args.lora_seg > 0) ? args.tile_slots[mt] : 0u;
+      const int n_kb = kb_main + __popc(slots) * kb_per_slot;
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, kErrWaitAccEmpty)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < n_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, kErrWaitFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+        const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+        const bool lora_blk = kb >= kb_main;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t da = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+          uint64_t db;
+          if (B_MN && !lora_blk) {
+            db = smem_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
+          } else {
+            db = smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B);
+          }
+          // The LoRA blocks of an MN-major launch are never issued (host refuses).
+          tc_mma_f16(d_tmem, da, db, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty_bar[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      tc_commit(&accf_bar[acc]);
+    }
+    // Every MMA issued by this thread has finished before TMEM is freed.
+    tc_commit(drain_bar);
+    uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(drain_bar, 0)) {
+      if (globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitAccFull); break; }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp - 4;  // TMEM lane quarter
+    int iter = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
+      const int m0 = mt * BM, n0 = nt * BN;
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      if (!mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const bool do_save = args.save != nullptr && row_ok && row >= args.save_lo && row < args.save_hi;
+      if constexpr (EPI == kEpiSwiGLU) {
+        // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 128) {
+#pragma unroll 1
+          for (int h = 0; h < 64; h += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld_32x32b_x32(t_row + c + h, g);
+            tmem_ld_32x32b_x32(t_row + c + 64 + h, u);
+            tmem_ld_wait();
+            float o[32], gf[32], uf[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              gf[i] = __uint_as_float(g[i]);
+              uf[i] = __uint_as_float(u[i]);
+              float sg = gf[i] / (1.0f + __expf(-gf[i]));
+              o[i] = sg * uf[i];
+            }
+            const int gcol = n0 + c;  // first gate column of this 128 block
+            if (row_ok && gcol < args.N) {
+              const int ocol = gcol / 2 + h;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + ocol;
+              store_row_bf16(dst, o, min(32, args.N / 2 - ocol));
+              if (do_save) {
+                __nv_bfloat16* sv = args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save;
+                store_row_bf16(sv + gcol + h, gf, min(32, args.N - (gcol + h)));
+                store_row_bf16(sv + gcol + 64 + h, uf, min(32, args.N - (gcol + 64 + h)));
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          const int col = n0 + c;
+          if (row_ok && col < args.N) {
+            const int nv = min(32, args.N - col);
+            if constexpr (EPI == kEpiBF16) {
+              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col, v, nv);
+            } else {
+              store_row_f32(reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col, v, nv,
+                            EPI == kEpiF32Accum);
+            }
+            if (do_save) {
+              store_row_bf16(args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save + col, v, nv);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "dsv: cannot resolve cuTensorMapEncodeTiled from the CUDA driver");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+struct TmKey {
+  uint64_t ptr, rows, cols, ld;
+  uint32_t box_rows;
+  bool operator==(const TmKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows;
+  }
+};
+struct TmKeyHash {
+  size_t operator()(const TmKey& k) const {
+    return std::hash<uint64_t>()(k.ptr) ^ (std::hash<uint64_t>()(k.rows) * 31) ^ (std::hash<uint64_t>()(k.cols) * 131) ^
+           (std::hash<uint64_t>()(k.ld) * 1031) ^ (std::hash<uint32_t>()(k.box_rows) * 7);
+  }
+};
+
+// Tensor map of a row-major bf16 matrix [rows, cols] with leading dimension
+// `ld` elements; box = 64 columns (128 bytes, 128-byte swizzle) x box_rows.
+// Maps are cached by (pointer, shape, box): weights and the engine's
+// persistent activation buffers are encoded once.
+static CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+  static std::unordered_map<TmKey, CUtensorMap, TmKeyHash> cache;
+  static std::mutex mu;
+  TmKey key{reinterpret_cast<uint64_t>(ptr), rows, cols, ld, box_rows};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "dsv gemm: operand base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "dsv gemm: row pitch must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), gdim, gstride, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "dsv gemm: cuTensorMapEncodeTiled failed (", (int)r, ")");
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 8192) cache.clear();
+  cache.emplace(key, m);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool B_MN, int EPI>
+static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
+                   const GemmArgs& args, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN, B_MN>;
+  auto kern = gemm_tc_kernel<BN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    attr_set = true;
+  }
+  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <bool B_MN, int EPI>
+static void dispatch_bn(int bn, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z,
+                        const CUtensorMap& b2, const GemmArgs& args, cudaStream_t s) {
+  if (bn == 256) launch<256, B_MN, EPI>(a, b, z, b2, args, s);
+  else if (bn == 128) launch<128, B_MN, EPI>(a, b, z, b2, args, s);
+  else launch<64, B_MN, EPI>(a, b, z, b2, args, s);
+}
+
+// Pick the N tile: the widest tile that still gives every SM work.
+static int pick_bn(int M, int N, int epi, bool b_mn) {
+  if (epi == kEpiSwiGLU) return (N % 256 == 0 && ((M + 127) / 128) * (N / 256) >= num_sms()) ? 256 : 128;
+  const int mt = (M + 127) / 128;
+  if (mt * ((N + 255) / 256) >= num_sms()) return 256;
+  if (mt * ((N + 127) / 128) >= num_sms() / 2 || b_mn) return 128;
+  return 64;
+}
+
+}  // namespace dsv
+
+// out = a @ b^T (b_mn=false, b is [N, K]) or a @ b (b_mn=true, b is [K_red, N]);
+// optional LoRA expand z @ b2^T over the slots listed per M tile.
+void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
+              c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
+              int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
+              int64_t save_dst, int64_t force_bn) {
+  using namespace dsv;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "dsv_gemm: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "dsv_gemm: row-major 2-D operands");
+  const int M = (int)a.size(0);
+  const int K = (int)a.size(1);
+  const int N = b_mn ? (int)b.size(1) : (int)b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "dsv_gemm: reduction length mismatch");
+  TORCH_CHECK(out.stride(-1) == 1, "dsv_gemm: output rows must be contiguous");
+  if (M == 0 || N == 0) return;
+  if (epi == kEpiSwiGLU) TORCH_CHECK(N % 128 == 0 && out.size(1) * 2 == N, "dsv_gemm: SwiGLU needs N % 128 == 0");
+  const bool f32_out = (epi == kEpiF32 || epi == kEpiF32Accum);
+  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "dsv_gemm: output dtype");
+  TORCH_CHECK(K > 0, "dsv_gemm: empty reduction");
+  c10::cuda::CUDAGuard guard(a.device());
+  int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
+  if (b_mn && bn < 64) bn = 64;
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.C = out.data_ptr();
+  args.ldc = (int)out.stride(0);
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), BM);
+  CUtensorMap tb = b_mn ? make_tmap_bf16(b.data_ptr(), K, N, b.stride(0), BK)
+                        : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
+  CUtensorMap tz = ta, tb2 = tb;
+  if (lora_seg > 0) {
+    TORCH_CHECK(!b_mn, "dsv_gemm: the fused LoRA expand is for K-major B only");
+    TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "dsv_gemm: LoRA operands missing");
+    TORCH_CHECK(lora_seg % 64 == 0, "dsv_gemm: lora_seg must be a multiple of 64");
+    auto& zt = *z;
+    auto& bt = *b2;
+    TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm: LoRA shapes");
+    TORCH_CHECK(tile_slots->scalar_type() == at::kInt && tile_slots->numel() >= (M + BM - 1) / BM, "dsv_gemm: tile_slots");
+    tz = make_tmap_bf16(zt.data_ptr(), M, zt.size(1), zt.stride(0), BM);
+    tb2 = make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), bn);
+    args.lora_seg = (int)lora_seg;
+    args.num_slots = (int)(zt.size(1) / lora_seg);
+    args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
+  }
+  if (save.has_value()) {
+    TORCH_CHECK(save->scalar_type() == at::kBFloat16 && save->stride(1) == 1, "dsv_gemm: save buffer");
+    args.save = reinterpret_cast<__nv_bfloat16*>(save->data_ptr());
+    args.ld_save = (int)save->stride(0);
+    args.save_lo = (int)save_lo;
+    args.save_hi = (int)save_hi;
+    args.save_dst = (int)save_dst;
+  }
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  if (b_mn) {
+    if (epi == kEpiBF16) dispatch_bn<true, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiF32) dispatch_bn<true, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiF32Accum) dispatch_bn<true, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
+    else TORCH_CHECK(false, "dsv_gemm: unsupported epilogue for MN-major B");
+  } else {
+    if (epi == kEpiBF16) dispatch_bn<false, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiF32) dispatch_bn<false, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiF32Accum) dispatch_bn<false, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiSwiGLU) {
+      if (bn == 64) bn = 128;
+      dispatch_bn<false, kEpiSwiGLU>(bn, ta, tb, tz, tb2, args, s);
+    }
+  }
+}
+
+DSV_ERROR_ACCESSOR(dsv_read_error_gemm)

@@ -1,0 +1,378 @@
+// Segmented multi-LoRA shrink, embedding, fused cross-entropy, AdamW with
+// per-layer clipping, LoRA publish, and sampling kernels.
+//
+// LoRA layout used by the engine (one group = projections sharing an input,
+// e.g. q/k/v share the attention input):
+//   A     [slots, P*R, K]  bf16   shrink weights, rank-padded to R
+//   Z     [T, slots*SEG]   bf16   shrink output; row t is non-zero only in the
+//                                 SEG columns of its own slot (SEG = P*R rounded
+//                                 up to 64), so the expand can run as extra
+//                                 K blocks of the base GEMM (gemm_tc.cu)
+//   B2    [N, slots*SEG]   bf16   expand weights (scale folded in), row n only
+//                                 uses the R columns of its own projection.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dsv {
+
+constexpr int SHR_ROWS = 16;
+constexpr int SHR_KC = 1024;  // K chunk staged in smem
+constexpr int SHR_THREADS = 256;
+constexpr int SHR_MAXPR = 192;  // 3 projections x rank 64
+
+// CTA = 16 token rows. For every output column o of the group, a warp holds the
+// A row chunk of the current slot in registers and dots it with each staged x
+// row; rows are sorted by slot, so the A chunk is reloaded only at slot changes.
+__global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfloat16* __restrict__ x, int sx,
+                                                                  const __nv_bfloat16* __restrict__ A,
+                                                                  const int* __restrict__ slot_ids, __nv_bfloat16* Z,
+                                                                  int sz, int T, int K, int PR, int SEG, int slots) {
+  __shared__ __align__(16) __nv_bfloat16 xs[SHR_ROWS * SHR_KC];
+  __shared__ float acc[SHR_ROWS][SHR_MAXPR];
+  __shared__ int rslot[SHR_ROWS];
+  const int r0 = blockIdx.x * SHR_ROWS;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int i = threadIdx.x; i < SHR_ROWS * SHR_MAXPR; i += SHR_THREADS) acc[i / SHR_MAXPR][i % SHR_MAXPR] = 0.f;
+  if (threadIdx.x < SHR_ROWS) {
+    const int r = r0 + threadIdx.x;
+    rslot[threadIdx.x] = (r < T) ? slot_ids[r] : -1;
+  }
+  __syncthreads();
+  for (int k0 = 0; k0 < K; k0 += SHR_KC) {
+    const int kc = min(SHR_KC, K - k0);
+    for (int i = threadIdx.x; i < SHR_ROWS * (kc / 8); i += SHR_THREADS) {
+      const int r = i / (kc / 8), c = (i % (kc / 8)) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r0 + r < T && rslot[r] >= 0) v = *reinterpret_cast<const uint4*>(x + (size_t)(r0 + r) * sx + k0 + c);
+      *reinterpret_cast<uint4*>(xs + r * SHR_KC + c) = v;
+    }
+    __syncthreads();
+    for (int o = warp; o < PR; o += SHR_THREADS / 32) {
+      int cur = -2;
+      float av[SHR_KC / 32];
+      for (int r = 0; r < SHR_ROWS; ++r) {
+        const int s = rslot[r];
+        if (s < 0) continue;
+        if (s != cur) {
+          const __nv_bfloat16* ar = A + ((size_t)s * PR + o) * K + k0;
+#pragma unroll
+          for (int j = 0; j < SHR_KC / 32; j += 8) {
+            const int c = lane * 8 + j * 32;
+            if (c < kc) {
+              float t[8];
+              float2 f;
+#pragma unroll
+              for (int e = 0; e < 8; e += 2) {
+                f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ar + c + e));
+                t[e] = f.x;
+                t[e + 1] = f.y;
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) av[j + e] = t[e];
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) av[j + e] = 0.f;
+            }
+          }
+          cur = s;
+        }
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < SHR_KC / 32; j += 8) {
+          const int c = lane * 8 + j * 32;
+          if (c < kc) {
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xs + r * SHR_KC + c + e));
+              d += f.x * av[j + e] + f.y * av[j + e + 1];
+            }
+          }
+        }
+        d = warp_sum(d);
+        if (lane == 0) acc[r][o] += d;
+      }
+    }
+    __syncthreads();
+  }
+  // Write every column of the row: own slot's segment, zeros elsewhere.
+  const int W = slots * SEG;
+  for (int i = threadIdx.x; i < SHR_ROWS * W; i += SHR_THREADS) {
+    const int r = i / W, c = i % W;
+    if (r0 + r >= T) continue;
+    const int s = rslot[r];
+    float v = 0.f;
+    if (s >= 0 && c >= s * SEG && c < s * SEG + PR) v = acc[r][c - s * SEG];
+    Z[(size_t)(r0 + r) * sz + c] = f2bf(v);
+  }
+}
+
+// Vocab-parallel embedding: ids outside [v0, v0 + Vl) give zero rows (the TP
+// all-reduce sums the shards).
+__global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* out, int D, int64_t v0, int64_t Vl) {
+  const int t = blockIdx.x;
+  const int64_t id = ids[t] - v0;
+  const bool ok = id >= 0 && id < Vl;
+  for (int i = threadIdx.x * 8; i < D; i += blockDim.x * 8) {
+    uint4 v = ok ? *reinterpret_cast<const uint4*>(table + id * D + i) : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(out + (size_t)t * D + i) = v;
+  }
+}
+
+// Cross-entropy over fp32 logits rows, forward and backward in one pass pair:
+// loss[r] = lse - logit[target]; grad (bf16) = (softmax - onehot) * gscale.
+// target < 0 rows produce zero loss and zero gradient.
+__global__ void ce_fwd_bwd_kernel(const float* __restrict__ logits, int64_t sl, const int64_t* __restrict__ targets,
+                                  float* loss, __nv_bfloat16* grad, int64_t sg, int V, float gscale) {
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const float* lr = logits + (size_t)r * sl;
+  const int64_t tgt = targets[r];
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, lr[i]);
+  mx = warp_max(mx);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -INFINITY;
+    t = warp_max(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float se = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) se += __expf(lr[i] - mx);
+  se = warp_sum(se);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = se;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float lse = mx + __logf(red[0]);
+  if (threadIdx.x == 0) loss[r] = (tgt >= 0) ? (lse - lr[tgt]) : 0.f;
+  if (grad != nullptr) {
+    __nv_bfloat16* gr = grad + (size_t)r * sg;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      float p = (tgt >= 0) ? __expf(lr[i] - lse) - (i == tgt ? 1.f : 0.f) : 0.f;
+      gr[i] = f2bf(p * gscale);
+    }
+  }
+}
+
+// Sum of squares per segment of equal length (one segment per layer).
+__global__ void seg_sumsq_kernel(const float* __restrict__ g, int64_t seg_len, float* out) {
+  __shared__ float red[32];
+  const int s = blockIdx.y;
+  const float* p = g + (size_t)s * seg_len;
+  float acc = 0.f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < seg_len; i += (int64_t)gridDim.x * blockDim.x)
+    acc += p[i] * p[i];
+  acc = warp_sum(acc);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) atomicAdd(&out[s], t);
+  }
+}
+
+// AdamW over one flat fp32 buffer; the gradient of segment s is scaled by
+// coef[s] = min(1, max_norm / (||g_s|| + 1e-6)) (per-layer clipping) and by
+// grad_scale (loss scaling / TP averaging).
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, int64_t n, int64_t seg_len, const float* __restrict__ seg_sumsq,
+                             float max_norm, float grad_scale, float lr, float b1, float b2, float eps, float wd,
+                             float bc1, float bc2) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float coef = grad_scale;
+    if (seg_sumsq != nullptr && max_norm > 0.f) {
+      const float nrm = sqrtf(seg_sumsq[i / seg_len]) * grad_scale;
+      coef *= fminf(1.f, max_norm / (nrm + 1e-6f));
+    }
+    const float gi = g[i] * coef;
+    float pi = p[i];
+    pi -= lr * wd * pi;
+    const float mi = b1 * m[i] + (1.f - b1) * gi;
+    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float denom = sqrtf(vi / bc2) + eps;
+    p[i] = pi - lr * (mi / bc1) / denom;
+  }
+}
+
+// Publish one LoRA group of one layer into a served slot:
+//   A_dst[r, k]               = bf16(A_src[r, k])
+//   B2_dst[n, col0 + p(n)*R + j] = bf16(clamp(Bt_src[j, n] * scale))
+// p(n): rows [0, b1) -> 0, [b1, b2) -> 1, [b2, N) -> 2, or (n / 64) % 2 when
+// interleave64 (gate/up).
+__global__ void lora_publish_kernel(const float* __restrict__ A_src, __nv_bfloat16* A_dst, int64_t a_numel,
+                                    const float* __restrict__ Bt_src, __nv_bfloat16* B2_dst, int64_t ldb2, int col0,
+                                    int N, int R, int b1, int b2, int interleave64, float scale) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < a_numel; i += stride) A_dst[i] = f2bf(A_src[i]);
+  for (int64_t i = tid; i < (int64_t)N * R; i += stride) {
+    const int n = (int)(i / R), j = (int)(i % R);
+    const int p = interleave64 ? ((n >> 6) & 1) : (n < b1 ? 0 : (n < b2 ? 1 : 2));
+    float v = Bt_src[(int64_t)j * N + n] * scale;
+    v = fminf(fmaxf(v, -65504.f), 65504.f);
+    B2_dst[(int64_t)n * ldb2 + col0 + p * R + j] = f2bf(v);
+  }
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  // SplitMix64 finaliser (Steele, Lea, Flood 2014).
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// One CTA per row: greedy (temperature <= 0) or Gumbel-max sampling at the
+// row's temperature.
+__global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, const float* __restrict__ temps,
+                              const int64_t* __restrict__ seeds, int64_t* out, int V) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int r = blockIdx.x;
+  const float* lr = logits + (size_t)r * sl;
+  const float t = temps[r];
+  const uint64_t seed = (uint64_t)seeds[r];
+  float best = -INFINITY;
+  int arg = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = lr[i];
+    if (t > 0.f) {
+      const uint64_t h = mix64(seed * 0x100000001B3ull + (uint64_t)i);
+      const float u = ((h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
+      v = v / t - __logf(-__logf(u));
+    }
+    if (v > best) {
+      best = v;
+      arg = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, arg, o);
+    if (ov > best || (ov == best && oi < arg)) {
+      best = ov;
+      arg = oi;
+    }
+  }
+  if (threadIdx.x % 32 == 0) {
+    bv[threadIdx.x / 32] = best;
+    bi[threadIdx.x / 32] = arg;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x / 32); ++w)
+      if (bv[w] > best || (bv[w] == best && bi[w] < arg)) {
+        best = bv[w];
+        arg = bi[w];
+      }
+    out[r] = arg;
+  }
+}
+
+}  // namespace dsv
+
+void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t seg) {
+  using namespace dsv;
+  const int T = (int)x.size(0);
+  if (T == 0) return;
+  const int K = (int)x.size(1);
+  const int slots = (int)A.size(0), PR = (int)A.size(1);
+  TORCH_CHECK(A.size(2) == K && K % 8 == 0 && PR <= SHR_MAXPR && PR <= seg, "lora_shrink: shapes");
+  TORCH_CHECK(Z.size(1) == slots * seg && Z.size(0) >= T, "lora_shrink: Z shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  lora_shrink_kernel<<<(T + SHR_ROWS - 1) / SHR_ROWS, SHR_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),
+      reinterpret_cast<__nv_bfloat16*>(Z.data_ptr()), (int)Z.stride(0), T, K, PR, (int)seg, slots);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t v0) {
+  using namespace dsv;
+  const int T = (int)ids.size(0);
+  if (T == 0) return;
+  const int D = (int)table.size(1);
+  c10::cuda::CUDAGuard guard(ids.device());
+  embedding_kernel<<<T, std::min(1024, std::max(32, D / 8)), 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, v0, table.size(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_ce_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss,
+                    c10::optional<torch::Tensor> grad, double gscale) {
+  using namespace dsv;
+  const int R = (int)logits.size(0);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(logits.device());
+  dsv::ce_fwd_bwd_kernel<<<R, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), targets.data_ptr<int64_t>(), loss.data_ptr<float>(),
+      grad.has_value() ? reinterpret_cast<__nv_bfloat16*>(grad->data_ptr()) : nullptr,
+      grad.has_value() ? grad->stride(0) : 0, (int)logits.size(1), (float)gscale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_seg_sumsq(torch::Tensor g, int64_t seg_len, torch::Tensor out) {
+  const int segs = (int)out.numel();
+  if (segs == 0) return;
+  c10::cuda::CUDAGuard guard(g.device());
+  out.zero_();
+  dim3 grid(std::max<int64_t>(1, std::min<int64_t>(64, seg_len / 4096 + 1)), segs);
+  dsv::seg_sumsq_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(g.data_ptr<float>(), seg_len,
+                                                                           out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, int64_t seg_len,
+               c10::optional<torch::Tensor> seg_sumsq, double max_norm, double grad_scale, double lr, double b1,
+               double b2, double eps, double wd, int64_t step) {
+  const int64_t n = p.numel();
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(p.device());
+  const float bc1 = 1.f - (float)std::pow(b1, (double)step);
+  const float bc2 = 1.f - (float)std::pow(b2, (double)step);
+  const int blocks = (int)std::min<int64_t>(4096, (n + 255) / 256);
+  dsv::adamw_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), n, seg_len,
+      seg_sumsq.has_value() ? seg_sumsq->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale, (float)lr,
+      (float)b1, (float)b2, (float)eps, (float)wd, bc1, bc2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_lora_publish(torch::Tensor A_src, torch::Tensor A_dst, torch::Tensor Bt_src, torch::Tensor B2_dst,
+                      int64_t col0, int64_t b1, int64_t b2, bool interleave64, double scale) {
+  c10::cuda::CUDAGuard guard(A_src.device());
+  const int R = (int)Bt_src.size(0), N = (int)Bt_src.size(1);
+  const int64_t work = std::max<int64_t>(A_src.numel(), (int64_t)N * R);
+  const int blocks = (int)std::min<int64_t>(2048, (work + 255) / 256);
+  dsv::lora_publish_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      A_src.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(A_dst.data_ptr()), A_src.numel(),
+      Bt_src.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(B2_dst.data_ptr()), B2_dst.stride(0), (int)col0, N,
+      R, (int)b1, (int)b2, interleave64 ? 1 : 0, (float)scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out) {
+  const int R = (int)logits.size(0);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(logits.device());
+  dsv::sample_kernel<<<R, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), temps.data_ptr<float>(), seeds.data_ptr<int64_t>(),
+      out.data_ptr<int64_t>(), (int)logits.size(1));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

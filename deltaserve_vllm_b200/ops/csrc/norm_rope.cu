@@ -1,0 +1,216 @@
+// Normalisation, RoPE and KV-cache write kernels (bandwidth-bound, CUDA cores).
+//
+// * rms_norm / fused_add_rms_norm: one CTA per token row, fp32 statistics,
+//   bf16 in/out. The fused variant updates the residual stream in place and can
+//   copy a row range of the new residual into an activation-capture buffer
+//   (the finetuning rows' layer input) in the same pass.
+// * qk_norm_rope_cache: one warp per (token, head) of the fused qkv row: optional
+//   per-head RMSNorm (Qwen3 q_norm/k_norm), NeoX rotate-half RoPE from an fp32
+//   cos/sin table, q/k written back in place, k and v scattered into the paged
+//   cache at slot_mapping[token].
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dsv {
+
+template <int VEC>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, float (&v)[VEC]) {
+#pragma unroll
+  for (int i = 0; i < VEC; i += 2) {
+    float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p + i));
+    v[i] = f.x;
+    v[i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < blockDim.x / 32) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// x: [T, D] (row stride sx); residual: [T, D] updated in place (if ADD);
+// out: [T, D]; save rows [save_lo, save_hi) of the residual to save[save_dst + r - save_lo].
+template <bool ADD>
+__global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int sx, __nv_bfloat16* residual, int sr,
+                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* out, int so, int D, float eps,
+                                __nv_bfloat16* save, int ssave, int save_lo, int save_hi, int save_dst) {
+  extern __shared__ float buf[];  // D floats + 32
+  float* red = buf + D;
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + (size_t)row * sx;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < D; i += blockDim.x * 8) {
+    float v[8];
+    load_bf16<8>(xr + i, v);
+    if (ADD) {
+      float r[8];
+      load_bf16<8>(residual + (size_t)row * sr + i, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += r[j];
+      // The residual stream is kept in bf16: round before the statistics so
+      // the normalised value matches what the next layer reads back.
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = bf2f(f2bf(v[j]));
+      uint4 pk;
+      uint32_t* p = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        p[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(residual + (size_t)row * sr + i) = pk;
+      if (save != nullptr && row >= save_lo && row < save_hi)
+        *reinterpret_cast<uint4*>(save + (size_t)(row - save_lo + save_dst) * ssave + i) = pk;
+    } else if (save != nullptr && row >= save_lo && row < save_hi) {
+      *reinterpret_cast<uint4*>(save + (size_t)(row - save_lo + save_dst) * ssave + i) =
+          *reinterpret_cast<const uint4*>(xr + i);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      buf[i + j] = v[j];
+      ss += v[j] * v[j];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / D + eps);
+  for (int i = threadIdx.x * 8; i < D; i += blockDim.x * 8) {
+    float wv[8];
+    load_bf16<8>(w + i, wv);
+    uint4 pk;
+    uint32_t* p = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(buf[i + 2 * j] * inv * wv[2 * j], buf[i + 2 * j + 1] * inv * wv[2 * j + 1]);
+      p[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)row * so + i) = pk;
+  }
+}
+
+// One warp per (token, head). Lane l owns dims {2l, 2l+1} and {64+2l, 65+2l}:
+// the rotate-half partners sit in the same lane.
+__global__ void qk_norm_rope_cache_kernel(__nv_bfloat16* qkv, int sq, const int64_t* __restrict__ positions,
+                                          const float* __restrict__ cos_sin, const __nv_bfloat16* __restrict__ qn_w,
+                                          const __nv_bfloat16* __restrict__ kn_w, float eps, int Hq, int Hkv,
+                                          __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
+                                          const int64_t* __restrict__ slot_mapping, int block_size, int T) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  const int H = Hq + 2 * Hkv;
+  if (gw >= T * H) return;
+  const int tok = gw / H, h = gw % H;
+  __nv_bfloat16* row = qkv + (size_t)tok * sq + h * 128;
+  const int64_t slot = slot_mapping != nullptr ? slot_mapping[tok] : -1;
+  if (h >= Hq + Hkv) {
+    // v: copy into the cache only.
+    if (slot >= 0) {
+      const int kvh = h - Hq - Hkv;
+      const int64_t blk = slot / block_size, off = slot % block_size;
+      __nv_bfloat16* dst = v_cache + ((blk * Hkv + kvh) * block_size + off) * 128;
+      reinterpret_cast<uint32_t*>(dst)[lane] = reinterpret_cast<const uint32_t*>(row)[lane];
+      reinterpret_cast<uint32_t*>(dst)[lane + 32] = reinterpret_cast<const uint32_t*>(row)[lane + 32];
+    }
+    return;
+  }
+  float2 a = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row)[lane]);
+  float2 b = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(row + 64)[lane]);
+  const __nv_bfloat16* nw = (h < Hq) ? qn_w : kn_w;
+  if (nw != nullptr) {
+    float ss = warp_sum(a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y);
+    float inv = rsqrtf(ss / 128.f + eps);
+    float2 wa = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(nw)[lane]);
+    float2 wb = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(nw + 64)[lane]);
+    // Round to bf16 after the norm, as the served module's output would be.
+    a.x = bf2f(f2bf(a.x * inv * wa.x));
+    a.y = bf2f(f2bf(a.y * inv * wa.y));
+    b.x = bf2f(f2bf(b.x * inv * wb.x));
+    b.y = bf2f(f2bf(b.y * inv * wb.y));
+  }
+  const float* cs = cos_sin + positions[tok] * 128;  // [cos(64) | sin(64)]
+  const float c0 = cs[2 * lane], c1 = cs[2 * lane + 1];
+  const float s0 = cs[64 + 2 * lane], s1 = cs[64 + 2 * lane + 1];
+  float2 ra = make_float2(a.x * c0 - b.x * s0, a.y * c1 - b.y * s1);
+  float2 rb = make_float2(b.x * c0 + a.x * s0, b.y * c1 + a.y * s1);
+  __nv_bfloat162 ha = __floats2bfloat162_rn(ra.x, ra.y), hb = __floats2bfloat162_rn(rb.x, rb.y);
+  reinterpret_cast<__nv_bfloat162*>(row)[lane] = ha;
+  reinterpret_cast<__nv_bfloat162*>(row + 64)[lane] = hb;
+  if (h >= Hq && slot >= 0) {
+    const int kvh = h - Hq;
+    const int64_t blk = slot / block_size, off = slot % block_size;
+    __nv_bfloat16* dst = k_cache + ((blk * Hkv + kvh) * block_size + off) * 128;
+    reinterpret_cast<__nv_bfloat162*>(dst)[lane] = ha;
+    reinterpret_cast<__nv_bfloat162*>(dst + 64)[lane] = hb;
+  }
+}
+
+}  // namespace dsv
+
+void dsv_rms_norm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor out,
+                  double eps, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi, int64_t save_dst) {
+  using namespace dsv;
+  const int T = (int)x.size(0), D = (int)x.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(D % 8 == 0 && x.stride(1) == 1 && out.stride(1) == 1, "rms_norm: D % 8 == 0, contiguous rows");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int threads = std::min(1024, std::max(32, ((D / 8 + 31) / 32) * 32));
+  const size_t smem = (D + 32) * sizeof(float);
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  __nv_bfloat16* sv = save.has_value() ? reinterpret_cast<__nv_bfloat16*>(save->data_ptr()) : nullptr;
+  const int ssv = save.has_value() ? (int)save->stride(0) : 0;
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto W = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  auto O = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  if (residual.has_value()) {
+    rms_norm_kernel<true><<<T, threads, smem, s>>>(X, (int)x.stride(0), reinterpret_cast<__nv_bfloat16*>(residual->data_ptr()),
+                                                   (int)residual->stride(0), W, O, (int)out.stride(0), D, (float)eps, sv, ssv,
+                                                   (int)save_lo, (int)save_hi, (int)save_dst);
+  } else {
+    rms_norm_kernel<false><<<T, threads, smem, s>>>(X, (int)x.stride(0), nullptr, 0, W, O, (int)out.stride(0), D, (float)eps,
+                                                    sv, ssv, (int)save_lo, (int)save_hi, (int)save_dst);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
+                            c10::optional<torch::Tensor> q_norm, c10::optional<torch::Tensor> k_norm, double eps,
+                            int64_t num_heads, int64_t num_kv_heads, c10::optional<torch::Tensor> k_cache,
+                            c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slot_mapping) {
+  using namespace dsv;
+  const int T = (int)qkv.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(qkv.stride(1) == 1 && positions.scalar_type() == at::kLong && cos_sin.scalar_type() == at::kFloat,
+              "qk_norm_rope_cache: bad inputs");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  const int H = (int)(num_heads + 2 * num_kv_heads);
+  const int64_t warps = (int64_t)T * H;
+  const int threads = 256;
+  const int blocks = (int)((warps * 32 + threads - 1) / threads);
+  int bs = 0;
+  __nv_bfloat16 *kc = nullptr, *vc = nullptr;
+  const int64_t* sm = nullptr;
+  if (k_cache.has_value()) {
+    kc = reinterpret_cast<__nv_bfloat16*>(k_cache->data_ptr());
+    vc = reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr());
+    bs = (int)k_cache->size(2);
+    sm = slot_mapping->data_ptr<int64_t>();
+  }
+  qk_norm_rope_cache_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), (int)qkv.stride(0), positions.data_ptr<int64_t>(),
+      cos_sin.data_ptr<float>(),
+      q_norm.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm->data_ptr()) : nullptr,
+      k_norm.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr()) : nullptr, (float)eps,
+      (int)num_heads, (int)num_kv_heads, kc, vc, sm, bs, T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

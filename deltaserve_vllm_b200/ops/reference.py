@@ -1,0 +1,221 @@
+"""Plain PyTorch restatements of every kernel in ``ops/csrc`` — the oracle the
+tests compare the CUDA kernels against, and the path CPU tensors take.
+
+Each function mirrors the exact contract (layouts, rounding points) of its
+kernel so that CPU runs of the engine and GPU runs agree up to bf16 rounding.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM = 0, 1, 2, 3
+
+
+def deinterleave64(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split a [..., 2I] tensor laid out as [g(64) u(64) g(64) u(64) ...] into (g, u)."""
+    shp = x.shape
+    v = x.reshape(*shp[:-1], shp[-1] // 128, 2, 64)
+    return v[..., 0, :].reshape(*shp[:-1], -1), v[..., 1, :].reshape(*shp[:-1], -1)
+
+
+def interleave64(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    shp = g.shape
+    gv = g.reshape(*shp[:-1], shp[-1] // 64, 1, 64)
+    uv = u.reshape(*shp[:-1], shp[-1] // 64, 1, 64)
+    return torch.cat([gv, uv], dim=-2).reshape(*shp[:-1], 2 * shp[-1])
+
+
+def gemm(a, b, out, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0,
+         save=None, save_lo=0, save_hi=0, save_dst=0):
+    acc = a.float() @ (b.float() if b_mn else b.float().t())
+    if lora_seg and z is not None:
+        acc = acc + z[: a.shape[0]].float() @ b2.float().t()
+    if save is not None and save_hi > save_lo:
+        save[save_dst: save_dst + save_hi - save_lo] = acc[save_lo:save_hi].to(save.dtype)
+    if epi == EPI_SWIGLU:
+        g, u = deinterleave64(acc)
+        out.copy_((F.silu(g) * u).to(out.dtype))
+    elif epi == EPI_F32_ACCUM:
+        out.add_(acc)
+    else:
+        out.copy_(acc.to(out.dtype))
+    return out
+
+
+def rms_norm(x, residual, w, out, eps, save=None, save_lo=0, save_hi=0, save_dst=0):
+    if residual is not None:
+        r = (x.float() + residual.float()).to(residual.dtype)
+        residual.copy_(r)
+        src = r
+    else:
+        src = x
+    if save is not None and save_hi > save_lo:
+        save[save_dst: save_dst + save_hi - save_lo] = src[save_lo:save_hi]
+    xf = src.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    out.copy_((xf * inv * w.float()).to(out.dtype))
+    return out
+
+
+def rope_cos_sin_table(max_pos: int, head_dim: int, theta: float, rope_scaling=None,
+                       device=None) -> torch.Tensor:
+    """fp32 [max_pos, head_dim] table laid out as [cos(hd/2) | sin(hd/2)]."""
+    from ..models.rope import rope_inv_freq
+    inv = rope_inv_freq(head_dim, theta, rope_scaling, device=device)
+    pos = torch.arange(max_pos, dtype=torch.float32, device=device)
+    f = torch.outer(pos, inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1).contiguous()
+
+
+def _apply_rope(x, cos, sin):
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h], x[..., h:]
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
+def qk_norm_rope_cache(qkv, positions, cos_sin, q_norm, k_norm, eps, Hq, Hkv,
+                       k_cache=None, v_cache=None, slot_mapping=None):
+    T = qkv.shape[0]
+    if T == 0:
+        return
+    hd = qkv.shape[1] // (Hq + 2 * Hkv)
+    v3 = qkv.view(T, Hq + 2 * Hkv, hd)
+    q = v3[:, :Hq].float()
+    k = v3[:, Hq:Hq + Hkv].float()
+    if q_norm is not None:
+        def _n(t, w):
+            inv = torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps)
+            return (t * inv * w.float()).to(qkv.dtype).float()
+        q, k = _n(q, q_norm), _n(k, k_norm)
+    cs = cos_sin[positions]
+    cos, sin = cs[:, None, : hd // 2], cs[:, None, hd // 2:]
+    v3[:, :Hq] = _apply_rope(q, cos, sin).to(qkv.dtype)
+    v3[:, Hq:Hq + Hkv] = _apply_rope(k, cos, sin).to(qkv.dtype)
+    if k_cache is not None:
+        bs = k_cache.shape[2]
+        ok = slot_mapping >= 0
+        sl = slot_mapping[ok]
+        blk, off = sl // bs, sl % bs
+        k_cache[blk, :, off] = v3[ok, Hq:Hq + Hkv]
+        v_cache[blk, :, off] = v3[ok, Hq + Hkv:]
+
+
+def _gather_kv(cache, btab, n, hd_heads):
+    bs = cache.shape[2]
+    pos = torch.arange(n, device=cache.device)
+    pages = btab[pos // bs].long()
+    return cache[pages, :, pos % bs]  # [n, Hkv, hd]
+
+
+def paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, num_heads, scale):
+    Hkv = k_cache.shape[1]
+    G = num_heads // Hkv
+    S = ctx_lens.shape[0]
+    for s in range(S):
+        q0, q1 = int(cu_q[s]), int(cu_q[s + 1])
+        ql = q1 - q0
+        if ql == 0:
+            continue
+        ctx = int(ctx_lens[s])
+        k = _gather_kv(k_cache, block_tables[s], ctx, Hkv).float()
+        v = _gather_kv(v_cache, block_tables[s], ctx, Hkv).float()
+        qs = q[q0:q1].reshape(ql, num_heads, -1).float()
+        k = k.repeat_interleave(G, dim=1)
+        v = v.repeat_interleave(G, dim=1)
+        sc = torch.einsum("qhd,khd->hqk", qs, k) * scale
+        qpos = torch.arange(ctx - ql, ctx, device=q.device)[:, None]
+        kpos = torch.arange(ctx, device=q.device)[None, :]
+        sc = sc.masked_fill((kpos > qpos)[None], float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        o = torch.einsum("hqk,khd->qhd", p, v)
+        out[q0:q1] = o.reshape(ql, -1).to(out.dtype)
+    return out
+
+
+def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale):
+    B = ctx_lens.shape[0]
+    cu = torch.arange(B + 1, dtype=torch.int32)
+    return paged_prefill(q, k_cache, v_cache, block_tables, cu, ctx_lens, out, num_heads, scale)
+
+
+def lora_shrink(x, A, slot_ids, Z, seg):
+    slots, PR, K = A.shape
+    Z.zero_()
+    T = x.shape[0]
+    for s in range(slots):
+        rows = (slot_ids[:T] == s).nonzero().flatten()
+        if rows.numel() == 0:
+            continue
+        Z[rows, s * seg: s * seg + PR] = (x[rows].float() @ A[s].float().t()).to(Z.dtype)
+    return Z
+
+
+def embedding(ids, table, out, v0):
+    local = ids - v0
+    ok = (local >= 0) & (local < table.shape[0])
+    out.zero_()
+    out[ok] = table[local[ok]]
+    return out
+
+
+def ce_fwd_bwd(logits, targets, loss, grad=None, gscale=1.0):
+    lf = logits.float()
+    lse = torch.logsumexp(lf, dim=-1)
+    ok = targets >= 0
+    tl = lf.gather(1, targets.clamp(min=0)[:, None])[:, 0]
+    loss.copy_(torch.where(ok, lse - tl, torch.zeros_like(lse)))
+    if grad is not None:
+        p = torch.softmax(lf, dim=-1)
+        p[torch.arange(p.shape[0]), targets.clamp(min=0)] -= 1.0
+        p = p * ok[:, None].float() * gscale
+        grad.copy_(p.to(grad.dtype))
+
+
+def seg_sumsq(g, seg_len, out):
+    out.copy_(g.view(-1, seg_len).float().pow(2).sum(-1))
+
+
+def adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd, step):
+    coef = torch.full((p.numel() // seg_len,), float(grad_scale))
+    if seg_sumsq_t is not None and max_norm > 0:
+        nrm = seg_sumsq_t.sqrt() * grad_scale
+        coef = coef * torch.clamp(max_norm / (nrm + 1e-6), max=1.0)
+    gi = (g.view(-1, seg_len) * coef[:, None]).view(-1)
+    p.mul_(1 - lr * wd)
+    m.mul_(b1).add_(gi, alpha=1 - b1)
+    v.mul_(b2).addcmul_(gi, gi, value=1 - b2)
+    bc1 = 1 - b1 ** step
+    bc2 = 1 - b2 ** step
+    p.addcdiv_(m / bc1, (v / bc2).sqrt() + eps, value=-lr)
+
+
+def lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale):
+    A_dst.copy_(A_src.view_as(A_dst).to(A_dst.dtype))
+    R, N = Bt_src.shape
+    n = torch.arange(N)
+    if interleave:
+        p = (n // 64) % 2
+    else:
+        p = torch.where(n < b1, 0, torch.where(n < b2, 1, 2))
+    vals = (Bt_src.t() * scale).clamp(-65504, 65504).to(B2_dst.dtype)  # [N, R]
+    cols = col0 + p[:, None] * R + torch.arange(R)[None, :]
+    B2_dst[n[:, None], cols] = vals
+
+
+def sample(logits, temps, seeds, out):
+    # The CPU path is greedy-only for temperature <= 0 and uses torch's RNG
+    # otherwise (the GPU kernel uses a counter-based hash per row).
+    lf = logits.float()
+    greedy = lf.argmax(-1)
+    res = greedy.clone()
+    for r in range(lf.shape[0]):
+        t = float(temps[r])
+        if t > 0:
+            gen = torch.Generator().manual_seed(int(seeds[r]))
+            u = torch.rand(lf.shape[1], generator=gen).clamp(1e-7, 1 - 1e-7)
+            res[r] = (lf[r] / t - torch.log(-torch.log(u))).argmax()
+    out.copy_(res)
