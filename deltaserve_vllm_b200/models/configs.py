@@ -61,6 +61,14 @@ PRESETS: dict[str, ModelArch] = {
                             rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True),
     "llama3-tiny": ModelArch("llama3-tiny", "llama", 2, 256, 4, 2, 64, 512, 1024,
                              rms_eps=1e-5, rope_theta=5e5),
+    # Small head_dim-128 models for GPU tests of the full engine path.
+    "qwen3-test": ModelArch("qwen3-test", "qwen3", 2, 512, 4, 2, 128, 1024, 4096,
+                            rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True),
+    "llama3-test": ModelArch("llama3-test", "llama", 2, 512, 4, 2, 128, 1024, 4096,
+                             rms_eps=1e-5, rope_theta=5e5),
+    # Llama-3-8B layer geometry with 2 layers and a small vocab (GPU smoke / tests).
+    "llama3-8b-2l": ModelArch("llama3-8b-2l", "llama", 2, 4096, 32, 8, 128, 14336, 8192,
+                              rms_eps=1e-5, rope_theta=5e5),
     "qwen3-0.6b": ModelArch("qwen3-0.6b", "qwen3", 28, 1024, 16, 8, 128, 3072, 151936,
                             rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True,
                             max_position=40960),

@@ -1,0 +1,358 @@
+"""Hand-written LoRA backward over the activations captured in the serving forward.
+
+The math follows the reference's manual backward (Llama-3:
+``deltaserve-plugin/deltaserve/bwd_services/llama3.py:149-219``; Qwen3 adds the
+per-head q/k RMSNorm backward, ``bwd_services/qwen3.py:133-204``), extended to
+LoRA on all seven projections and to prompt-masked labels, and laid out for
+this engine's fused weights:
+
+* The LoRA factors of one projection *group* (qkv / o / gate_up / down, see
+  ``models/lora.py``) are kept as one fp32 master pair ``A [P*R, K]`` and
+  ``Bt [R, N]`` (``Bt[j, n] = B_p(n)[n, j]``). Every group backward is five
+  GEMMs on the group's input ``X`` and output gradient ``dY``::
+
+      Z   = X A^T                 dZ  = dY Bfull         (Bfull = scatter(Bt) * s)
+      dX += dZ A                  dA  = dZ^T X           dBfull^T = s Z^T dY
+
+* The base-weight input gradients ``dX = dY W`` are "MN-major" GEMMs on the
+  tcgen05 kernel (no transposed weight copy).
+* Precision: GEMM operands bf16 with fp32 accumulation; residual-stream
+  gradient, RMSNorm backward, attention scores/softmax and the LM head / CE in
+  fp32 (the reference's precision contract).
+
+Tensor parallelism: ``comm.all_reduce`` sums the per-rank partials of the two
+residual-stream gradients per layer (after the MLP and after the qkv input
+gradient); replicated factor gradients (column-parallel ``A``, row-parallel
+``B``) are summed by the trainer in buckets.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..ops import EPI_F32, EPI_F32_ACCUM
+from ..ops.reference import deinterleave64, interleave64
+from .configs import ModelArch
+from .lora import GROUP_PROJS, GROUPS, COLUMN_PARALLEL, GroupGeom, group_geoms, peft_key, shard_lora_factor
+from .rope import apply_rope, rope_backward
+from .weights import ModelWeights, TPInfo
+
+REPLICATED = {"qkv": "A", "gate_up": "A", "o": "B", "down": "B"}
+
+
+class LoraMasters:
+    """fp32 masters of one trained adapter for every layer and group, as views
+    into flat ``params`` / ``grads`` buffers laid out in two blocks:
+
+    * ``[0, rep_total)``: the factors replicated across TP ranks (column-parallel
+      ``A``, row-parallel ``B``), one contiguous segment per layer — a bucket of
+      consecutive layers is one contiguous slab for the gradient all-reduce;
+    * ``[rep_total, total)``: the per-rank shards, one segment per layer.
+
+    AdamW is then two launches and per-layer clipping two segmented reductions."""
+
+    def __init__(self, arch: ModelArch, tp: TPInfo, rank: int, device):
+        self.arch, self.tp, self.R = arch, tp, rank
+        self.geom = group_geoms(arch, tp)
+        L = arch.num_layers
+        rep, shard = [], []
+        for g in GROUPS:
+            gg = self.geom[g]
+            for ab, shape in (("A", (gg.P * rank, gg.K)), ("Bt", (rank, gg.N))):
+                is_rep = (REPLICATED[g] == "A") == (ab == "A")
+                (rep if is_rep else shard).append((g, ab, shape))
+        self.rep_per_layer = sum(s[0] * s[1] for _, _, s in rep)
+        self.shard_per_layer = sum(s[0] * s[1] for _, _, s in shard)
+        self.rep_total = self.rep_per_layer * L
+        total = self.rep_total + self.shard_per_layer * L
+        self.layout: list[tuple[str, str, int, int, tuple[int, ...]]] = []  # (g, ab, base, stride, shape)
+        off = 0
+        for g, ab, shape in rep:
+            self.layout.append((g, ab, off, self.rep_per_layer, shape))
+            off += shape[0] * shape[1]
+        off = self.rep_total
+        for g, ab, shape in shard:
+            self.layout.append((g, ab, off, self.shard_per_layer, shape))
+            off += shape[0] * shape[1]
+        self.params = torch.zeros(total, dtype=torch.float32, device=device)
+        self.grads = torch.zeros_like(self.params)
+        self.exp_avg = torch.zeros_like(self.params)
+        self.exp_avg_sq = torch.zeros_like(self.params)
+        self._views_p = self._views(self.params)
+        self._views_g = self._views(self.grads)
+
+    def _views(self, flat):
+        out = []
+        for l in range(self.arch.num_layers):
+            d = {}
+            for g, ab, base, stride, shape in self.layout:
+                s = base + l * stride
+                d[(g, ab)] = flat[s:s + shape[0] * shape[1]].view(shape)
+            out.append(d)
+        return out
+
+    def rep_block(self, flat: torch.Tensor, l0: int = 0, l1: int | None = None) -> torch.Tensor:
+        l1 = self.arch.num_layers if l1 is None else l1
+        return flat[l0 * self.rep_per_layer:l1 * self.rep_per_layer]
+
+    def shard_block(self, flat: torch.Tensor) -> torch.Tensor:
+        return flat[self.rep_total:]
+
+    def p(self, layer, group, ab):
+        return self._views_p[layer][(group, ab)]
+
+    def g(self, layer, group, ab):
+        return self._views_g[layer][(group, ab)]
+
+    @torch.no_grad()
+    def load_peft(self, tensors: dict[str, torch.Tensor], rank: int) -> None:
+        """Full PEFT factors -> this rank's masters (zero for absent projections)."""
+        if rank > self.R:
+            raise ValueError(f"adapter rank {rank} > trainer rank {self.R}")
+        self.params.zero_()
+        for l in range(self.arch.num_layers):
+            for g in GROUPS:
+                gg = self.geom[g]
+                A, Bt = self.p(l, g, "A"), self.p(l, g, "Bt")
+                for p, proj in enumerate(GROUP_PROJS[g]):
+                    ka, kb = peft_key(l, proj, "A"), peft_key(l, proj, "B")
+                    if ka not in tensors:
+                        continue
+                    a = shard_lora_factor(self.arch, proj, "A", tensors[ka].float(), self.tp)
+                    b = shard_lora_factor(self.arch, proj, "B", tensors[kb].float(), self.tp)
+                    A[p * self.R:p * self.R + rank] = a.to(A.device)
+                    rows = gg.proj_rows(p).to(Bt.device)
+                    Bt[:rank, rows] = b.t().to(Bt.device)
+
+    @torch.no_grad()
+    def export_peft(self, rank: int, targets=None, grads: bool = False) -> dict[str, torch.Tensor]:
+        """This rank's shard of every factor (or of its gradient), PEFT names,
+        fp32 on CPU."""
+        get = self.g if grads else self.p
+        out = {}
+        for l in range(self.arch.num_layers):
+            for g in GROUPS:
+                gg = self.geom[g]
+                A, Bt = get(l, g, "A").cpu(), get(l, g, "Bt").cpu()
+                for p, proj in enumerate(GROUP_PROJS[g]):
+                    if targets is not None and proj not in targets:
+                        continue
+                    out[peft_key(l, proj, "A")] = A[p * self.R:p * self.R + rank].clone()
+                    out[peft_key(l, proj, "B")] = Bt[:rank, gg.proj_rows(p)].t().contiguous()
+        return out
+
+
+@dataclass
+class CycleInputs:
+    n: int                        # captured tokens
+    n_pad: int                    # rows processed (multiple of 8)
+    starts: list[int]
+    lens: list[int]
+    labels: torch.Tensor          # [n_pad] int64, -1 = no loss
+    cos: torch.Tensor             # [n_pad, hd/2] fp32
+    sin: torch.Tensor
+
+
+def make_labels(ids: torch.Tensor, starts, lens, n_pad: int, mask_prefix: int = 0) -> torch.Tensor:
+    """Row t of a sample predicts token t+1; the last row of a sample and its
+    first ``mask_prefix`` rows carry no loss."""
+    lab = torch.full((n_pad,), -1, dtype=torch.long, device=ids.device)
+    for st, ln in zip(starts, lens):
+        if ln < 2:
+            continue
+        lab[st:st + ln - 1] = ids[st + 1:st + ln]
+        if mask_prefix > 0:
+            lab[st:st + min(mask_prefix, ln - 1)] = -1
+    return lab
+
+
+def rmsnorm_fwd(x, w, eps):
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+def rmsnorm_bwd(x, dy, w, eps):
+    """Gradient of rmsnorm(x)*w w.r.t. x, fp32."""
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    xhat = xf * inv
+    g = dy.float() * w.float()
+    dot = (g * xhat).sum(-1, keepdim=True)
+    return (g - xhat * dot / xf.shape[-1]) * inv
+
+
+def attn_backward(qh, kh, vh, d_ctx, starts, lens, scale):
+    """Causal GQA attention backward per sample, fp32. Inputs [n, H, hd]."""
+    n, Hq, hd = qh.shape
+    Hkv = kh.shape[1]
+    G = Hq // Hkv
+    dq = torch.zeros(n, Hq, hd, dtype=torch.float32, device=qh.device)
+    dk = torch.zeros(n, Hkv, hd, dtype=torch.float32, device=qh.device)
+    dv = torch.zeros_like(dk)
+    for st, ln in zip(starts, lens):
+        q = qh[st:st + ln].float().transpose(0, 1)                       # [Hq, l, hd]
+        k = kh[st:st + ln].float().transpose(0, 1).repeat_interleave(G, 0)
+        v = vh[st:st + ln].float().transpose(0, 1).repeat_interleave(G, 0)
+        do = d_ctx[st:st + ln].float().transpose(0, 1)
+        s = (q @ k.transpose(1, 2)) * scale
+        mask = torch.triu(torch.ones(ln, ln, dtype=torch.bool, device=qh.device), 1)
+        p = s.masked_fill(mask, float("-inf")).softmax(-1)
+        dvv = p.transpose(1, 2) @ do
+        dp = do @ v.transpose(1, 2)
+        ds = p * (dp - (dp * p).sum(-1, keepdim=True))
+        dqq = (ds @ k) * scale
+        dkk = (ds.transpose(1, 2) @ q) * scale
+        dq[st:st + ln] = dqq.transpose(0, 1)
+        dk[st:st + ln] = dkk.view(Hkv, G, ln, hd).sum(1).transpose(0, 1)
+        dv[st:st + ln] = dvv.view(Hkv, G, ln, hd).sum(1).transpose(0, 1)
+    return dq, dk, dv
+
+
+def _bf(t, cdt):
+    return t if t.dtype == cdt else t.to(cdt)
+
+
+class LoraBackward:
+    """Per-cycle backward state (compute copies of the LoRA factors) and the
+    head / layer backward steps. Works on CPU (fp32 oracle ops) and CUDA."""
+
+    def __init__(self, weights: ModelWeights, masters: LoraMasters, scaling: float, comm=None,
+                 cdt=torch.bfloat16):
+        self.w, self.m, self.s = weights, masters, scaling
+        self.arch = weights.arch
+        self.comm = comm
+        self.cdt = cdt if weights.embed.is_cuda else torch.float32
+        self.geom = masters.geom
+        self.hq = self.arch.num_heads // weights.tp.size
+        self.hkv = self.arch.num_kv_heads // weights.tp.size
+        self.hd = self.arch.head_dim
+        self.scale = 1.0 / math.sqrt(self.hd)
+        self._bfull_idx = {}
+
+    # ------------------------------------------------------------ GEMM helpers
+    def _mm(self, a, b, b_mn, epi=EPI_F32, out=None):
+        a = _bf(a, self.cdt).contiguous()
+        b = _bf(b, self.cdt).contiguous()
+        if out is None:
+            n = b.shape[1] if b_mn else b.shape[0]
+            out = torch.empty(a.shape[0], n, dtype=torch.float32, device=a.device)
+        ops.gemm(a, b, out, b_mn=b_mn, epi=epi)
+        return out
+
+    def _bfull(self, layer, g):
+        """[N, P*R] scattered, scaled expand factor (compute dtype)."""
+        gg = self.geom[g]
+        R = self.m.R
+        Bt = self.m.p(layer, g, "Bt")
+        full = torch.zeros(gg.N, gg.P * R, dtype=torch.float32, device=Bt.device)
+        for p in range(gg.P):
+            rows = gg.proj_rows(p).to(Bt.device)
+            full[rows, p * R:(p + 1) * R] = Bt[:, rows].t() * self.s
+        return _bf(full, self.cdt)
+
+    def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
+                       dX: torch.Tensor) -> None:
+        """LoRA part of one group: accumulates into ``dX`` (fp32) and writes the
+        factor gradients into the trainer's grad buffer."""
+        gg = self.geom[g]
+        R = self.m.R
+        A = _bf(self.m.p(layer, g, "A"), self.cdt)
+        Bfull = self._bfull(layer, g)
+        Z = self._mm(X, A, b_mn=False)                       # [n, PR]
+        dZ = self._mm(dY, Bfull, b_mn=True)                  # [n, PR]
+        self._mm(dZ, A, b_mn=True, epi=EPI_F32_ACCUM, out=dX)
+        gA = self.m.g(layer, g, "A")
+        self._mm(dZ.t(), X, b_mn=True, out=gA)               # [PR, K]
+        gBfT = self._mm(Z.t(), dY, b_mn=True) * self.s       # [PR, N]
+        gBt = self.m.g(layer, g, "Bt")
+        for p in range(gg.P):
+            rows = gg.proj_rows(p).to(gBt.device)
+            gBt[:, rows] = gBfT[p * R:(p + 1) * R][:, rows]
+
+    # ------------------------------------------------------------ head
+    def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor) -> tuple[float, int, torch.Tensor]:
+        """Final RMSNorm + LM head + CE. Returns (mean loss, n_valid, d final_in fp32)."""
+        w = self.w
+        eps = self.arch.rms_eps
+        head = w.lm_head_full if w.lm_head_full is not None else w.lm_head
+        n_valid = int((labels >= 0).sum())
+        h = rmsnorm_fwd(final_in, w.final_norm, eps)
+        if n_valid == 0:
+            return 0.0, 0, torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device)
+        logits = torch.empty(h.shape[0], head.shape[0], dtype=torch.float32, device=h.device)
+        ops.gemm(_bf(h, self.cdt).contiguous(), _bf(head, self.cdt), logits, epi=EPI_F32)
+        loss = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
+        dlog = torch.empty(h.shape[0], head.shape[0], dtype=self.cdt, device=h.device)
+        ops.ce_fwd_bwd(logits, labels, loss, dlog, 1.0 / n_valid)
+        del logits
+        dh = self._mm(dlog, head, b_mn=True)                # [n, D]
+        del dlog
+        d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
+        return float(loss.sum().item()) / n_valid, n_valid, d_final
+
+    # ------------------------------------------------------------ layer
+    def recompute_qkv(self, qkv_raw: torch.Tensor, positions: torch.Tensor, lw, cos_sin):
+        """Post-norm/RoPE q, k (as the serving kernel produced them) and v."""
+        t = qkv_raw.clone()
+        ops.qk_norm_rope_cache(t, positions, cos_sin, lw.q_norm, lw.k_norm, self.arch.rms_eps,
+                               self.hq, self.hkv)
+        n = t.shape[0]
+        ql, kl = self.hq * self.hd, self.hkv * self.hd
+        return (t[:, :ql].view(n, self.hq, self.hd), t[:, ql:ql + kl].view(n, self.hkv, self.hd),
+                t[:, ql + kl:].view(n, self.hkv, self.hd))
+
+    def layer_backward(self, layer: int, dh: torch.Tensor, saved: dict, ci: CycleInputs,
+                       positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+        """dh: fp32 [n, D] gradient w.r.t. the layer output. Returns the gradient
+        w.r.t. the layer input (fp32), grads of this layer's factors written."""
+        w = self.w
+        lw = w.layers[layer]
+        eps = self.arch.rms_eps
+        x, qkv_raw, ctx = saved["layer_in"], saved["qkv"], saved["ctx"]
+        resid_mid, gate_up = saved["resid_mid"], saved["gate_up"]
+        n = x.shape[0]
+        # ---- MLP -------------------------------------------------------
+        x2 = rmsnorm_fwd(resid_mid, lw.post_ln, eps)
+        g, u = deinterleave64(gate_up.float())
+        sg = torch.sigmoid(g)
+        silu_g = g * sg
+        act = _bf(silu_g * u, x.dtype)
+        dh_c = _bf(dh, self.cdt)
+        d_act = self._mm(dh_c, lw.down, b_mn=True)                  # [n, I_l]
+        self.group_backward(layer, "down", act, dh_c, d_act)
+        d_u = d_act * silu_g
+        d_g = d_act * u * sg * (1 + g * (1 - sg))
+        d_gu = _bf(interleave64(d_g, d_u), self.cdt)
+        d_x2 = self._mm(d_gu, lw.gate_up, b_mn=True)                # [n, D]
+        self.group_backward(layer, "gate_up", x2, d_gu, d_x2)
+        if self.comm is not None:
+            self.comm.all_reduce(d_x2)
+        d_mid = rmsnorm_bwd(resid_mid, d_x2, lw.post_ln, eps) + dh
+        # ---- attention ---------------------------------------------------
+        d_mid_c = _bf(d_mid, self.cdt)
+        d_ctx = self._mm(d_mid_c, lw.o, b_mn=True)                  # [n, q_l]
+        self.group_backward(layer, "o", ctx, d_mid_c, d_ctx)
+        qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
+        dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
+                                   self.scale)
+        cos, sin = ci.cos, ci.sin
+        dq = rope_backward(dq, cos, sin)
+        dk = rope_backward(dk, cos, sin)
+        if self.arch.qk_norm:
+            ql = self.hq * self.hd
+            q_pre = qkv_raw[:, :ql].view(n, self.hq, self.hd)
+            k_pre = qkv_raw[:, ql:ql + self.hkv * self.hd].view(n, self.hkv, self.hd)
+            dq = rmsnorm_bwd(q_pre, dq, lw.q_norm, eps)
+            dk = rmsnorm_bwd(k_pre, dk, lw.k_norm, eps)
+        d_qkv = _bf(torch.cat([dq.reshape(n, -1), dk.reshape(n, -1), dv.reshape(n, -1)], 1), self.cdt)
+        x1 = rmsnorm_fwd(x, lw.in_ln, eps)
+        d_x1 = self._mm(d_qkv, lw.qkv, b_mn=True)                   # [n, D]
+        self.group_backward(layer, "qkv", x1, d_qkv, d_x1)
+        if self.comm is not None:
+            self.comm.all_reduce(d_x1)
+        return rmsnorm_bwd(x, d_x1, lw.in_ln, eps) + d_mid

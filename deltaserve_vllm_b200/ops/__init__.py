@@ -18,31 +18,32 @@ import torch
 from . import reference as ref
 from .reference import EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM  # noqa: F401
 
-_C = None
+_EXT = None
 _C_ERR: Exception | None = None
 try:  # the in-tree build (python setup.py build_ext --inplace)
-    from . import _C  # type: ignore
+    import importlib as _il
+    _EXT = _il.import_module(".ops._C", __name__.rsplit(".", 1)[0])
 except Exception as e:  # pragma: no cover - depends on the build
     _C_ERR = e
 
 
 def native_available() -> bool:
-    return _C is not None
+    return _EXT is not None
 
 
 def _native():
-    if _C is None:
+    if _EXT is None:
         raise RuntimeError(
             "deltaserve_vllm_b200 CUDA extension is not built or failed to load "
             f"({_C_ERR!r}); run `python setup.py build_ext --inplace`")
-    return _C
+    return _EXT
 
 
 def check_device_error(clear: bool = True) -> int:
     """Error code written by a kernel whose bounded wait gave up (0 = none)."""
-    if _C is None or not torch.cuda.is_available():
+    if _EXT is None or not torch.cuda.is_available():
         return 0
-    return int(_C.read_error(clear))
+    return int(_EXT.read_error(clear))
 
 
 # ----------------------------------------------------------------- GEMM

@@ -1,0 +1,96 @@
+"""Tensor-parallel communicators.
+
+* :class:`TPComm` — ``torch.distributed`` collectives on one process group:
+  NCCL over NVLink/NVSwitch on GPUs (the baseline path), gloo for CPU ranks in
+  tests. In-place all-reduce of activations and gradients, column all-gather of
+  vocab-parallel logits, object gather for checkpoint merges, and a CPU-side
+  group for host votes.
+* :func:`init_tp` — one process per GPU, rendezvous from the torchrun env
+  (``RANK``/``WORLD_SIZE``/``MASTER_ADDR``/``MASTER_PORT``) with a short timeout so
+  ranks that wait on a dead peer fail instead of hanging.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+
+class TPComm:
+    def __init__(self, group=None, cpu_group=None):
+        self.group = group
+        self.cpu_group = cpu_group
+        self.size = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.num_collectives = 0
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.size > 1:
+            dist.all_reduce(t, group=self.group)
+            self.num_collectives += 1
+        return t
+
+    def all_gather_cols(self, t: torch.Tensor) -> torch.Tensor:
+        """[R, V/tp] per rank -> [R, V] (rank-major columns)."""
+        if self.size == 1:
+            return t
+        parts = [torch.empty_like(t) for _ in range(self.size)]
+        dist.all_gather(parts, t.contiguous(), group=self.group)
+        self.num_collectives += 1
+        return torch.cat(parts, dim=1)
+
+    def all_gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        if self.size == 1:
+            return t
+        out = torch.empty((self.size * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        self.num_collectives += 1
+        return out
+
+    def broadcast_object(self, obj, src: int = 0):
+        if self.size == 1:
+            return obj
+        box = [obj]
+        dist.broadcast_object_list(box, src=src, group=self.cpu_group or self.group)
+        return box[0]
+
+    def gather_objects(self, obj, dst: int = 0):
+        if self.size == 1:
+            return [obj]
+        out = [None] * self.size if self.rank == dst else None
+        dist.gather_object(obj, out, dst=dst, group=self.cpu_group or self.group)
+        return out
+
+    def all_reduce_max_int(self, v: int) -> int:
+        """Host vote: every rank gets the max (used for rank-symmetric decisions)."""
+        if self.size == 1:
+            return int(v)
+        t = torch.tensor([int(v)], dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.cpu_group or self.group)
+        return int(t.item())
+
+    def barrier(self) -> None:
+        if self.size > 1:
+            dist.barrier(group=self.cpu_group or self.group)
+
+
+def init_tp(backend: str | None = None, timeout_s: float = 120.0) -> TPComm:
+    """Initialise the default process group from the torchrun environment."""
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws == 1 and not dist.is_initialized():
+        return TPComm()
+    if not dist.is_initialized():
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        kw = {}
+        if backend == "nccl":
+            local = int(os.environ.get("LOCAL_RANK", os.environ.get("RANK", "0")))
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+    cpu_group = dist.new_group(backend="gloo") if backend == "nccl" else None
+    return TPComm(None, cpu_group)

@@ -1,0 +1,243 @@
+"""sm_100a kernels vs their fp32 PyTorch restatements (ops/reference.py)."""
+import math
+
+import pytest
+import torch
+
+from deltaserve_vllm_b200 import ops
+from deltaserve_vllm_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert ops.check_device_error() == 0
+
+
+def rnd(*shape, scale=1.0, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(dtype)
+
+
+def test_native_loaded():
+    assert ops.native_available()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (77, 640, 320), (128, 128, 64), (300, 1000, 512),
+                                   (1024, 4096, 1024), (4096, 1536, 4096)])
+@pytest.mark.parametrize("bn", [0, 64, 128, 256])
+def test_gemm_kmajor(M, N, K, bn):
+    a, b = rnd(M, K, seed=1), rnd(N, K, scale=0.05, seed=2)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(a, b, out, force_bn=bn)
+    exp = a.float() @ b.float().t()
+    torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 256, 128), (200, 512, 384), (4096, 1024, 2048)])
+def test_gemm_mn_major_f32(M, N, K):
+    a, w = rnd(M, K, seed=3), rnd(K, N, scale=0.05, seed=4)   # out = a @ w (w is [K, N] row-major)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(a, w, out, b_mn=True, epi=ops.EPI_F32)
+    torch.testing.assert_close(out, a.float() @ w.float(), rtol=1e-2, atol=1e-2)
+    acc = torch.ones_like(out)
+    ops.gemm(a, w, acc, b_mn=True, epi=ops.EPI_F32_ACCUM)
+    torch.testing.assert_close(acc, 1 + a.float() @ w.float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M", [5, 130, 600])
+def test_gemm_swiglu_save(M):
+    K, I = 512, 768
+    x, w = rnd(M, K, seed=5), rnd(2 * I, K, scale=0.05, seed=6)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    save = torch.zeros(M + 10, 2 * I, dtype=torch.bfloat16, device=DEV)
+    lo, hi = M // 3, M
+    ops.gemm(x, w, out, epi=ops.EPI_SWIGLU, save=save, save_lo=lo, save_hi=hi, save_dst=7)
+    exp_out = torch.empty_like(out, dtype=torch.float32)
+    exp_save = torch.zeros(M + 10, 2 * I)
+    ref.gemm(x.float().cpu(), w.float().cpu(), exp_out.cpu(), epi=ref.EPI_SWIGLU)
+    acc = x.float() @ w.float().t()
+    g, u = ref.deinterleave64(acc)
+    torch.testing.assert_close(out.float(), torch.nn.functional.silu(g) * u, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(save[7:7 + hi - lo].float(), acc[lo:hi], rtol=2e-2, atol=2e-2)
+    assert save[:7].abs().sum() == 0
+
+
+def test_gemm_lora_expand_segmented():
+    M, N, K, slots, P, R = 300, 384, 256, 4, 3, 16
+    seg = 64
+    x, w = rnd(M, K, seed=7), rnd(N, K, scale=0.05, seed=8)
+    A = rnd(slots, P * R, K, scale=0.05, seed=9)
+    B2 = rnd(N, slots * seg, scale=0.05, seed=10)
+    slot_ids = torch.randint(-1, slots, (M,), device=DEV, dtype=torch.int32)
+    slot_ids, _ = slot_ids.sort()
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, slot_ids, Z, seg)
+    Zr = torch.empty_like(Z).cpu()
+    ref.lora_shrink(x.cpu().float(), A.cpu().float(), slot_ids.cpu(), Zr, seg)
+    torch.testing.assert_close(Z.float().cpu(), Zr.float(), rtol=2e-2, atol=2e-2)
+    nt = -(-M // 128)
+    mask = torch.zeros(nt, dtype=torch.int32)
+    for t in range(nt):
+        for s in slot_ids[t * 128:(t + 1) * 128].cpu().unique().tolist():
+            if s >= 0:
+                mask[t] |= 1 << s
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, z=Z, b2=B2, tile_slots=mask.to(DEV), lora_seg=seg)
+    exp = x.float() @ w.float().t() + Z.float() @ B2.float().t()
+    torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("D", [256, 1024, 4096, 5120])
+def test_rms_norm_fused_add_save(D):
+    T = 37
+    x, r, w = rnd(T, D, seed=11), rnd(T, D, seed=12), rnd(D, scale=0.1, seed=13) + 1
+    out = torch.empty_like(x)
+    res = r.clone()
+    save = torch.zeros(40, D, dtype=torch.bfloat16, device=DEV)
+    ops.rms_norm(x, w, out, 1e-6, residual=res, save=save, save_lo=30, save_hi=37, save_dst=2)
+    ro, rr = torch.empty(T, D), r.float().cpu().to(torch.bfloat16)
+    ref.rms_norm(x.cpu(), rr, w.cpu(), ro, 1e-6)
+    torch.testing.assert_close(res.cpu(), rr)
+    torch.testing.assert_close(out.float().cpu(), ro, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(save[2:9].cpu(), rr[30:37])
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_qk_norm_rope_cache(qk_norm):
+    T, Hq, Hkv, bs = 45, 8, 2, 16
+    qkv = rnd(T, (Hq + 2 * Hkv) * 128, seed=14)
+    pos = torch.randint(0, 900, (T,), device=DEV)
+    cs = ref.rope_cos_sin_table(1024, 128, 1e6, device=DEV)
+    qn = rnd(128, scale=0.1, seed=15) + 1 if qk_norm else None
+    kn = rnd(128, scale=0.1, seed=16) + 1 if qk_norm else None
+    kc = torch.zeros(8, Hkv, bs, 128, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(8 * bs, device=DEV)[:T]
+    a = qkv.clone()
+    ops.qk_norm_rope_cache(a, pos, cs, qn, kn, 1e-6, Hq, Hkv, kc, vc, slots)
+    b = qkv.cpu().clone()
+    kr, vr = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    ref.qk_norm_rope_cache(b, pos.cpu(), cs.cpu(), None if qn is None else qn.cpu(),
+                           None if kn is None else kn.cpu(), 1e-6, Hq, Hkv, kr, vr, slots.cpu())
+    torch.testing.assert_close(a.float().cpu(), b.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(kc.float().cpu(), kr.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(vc.cpu(), vr)
+
+
+def _paged_setup(lens, qlens, Hq, Hkv, bs, seed=0):
+    nb = sum(-(-l // bs) for l in lens) + 4
+    kc = rnd(nb, Hkv, bs, 128, seed=seed)
+    vc = rnd(nb, Hkv, bs, 128, seed=seed + 1)
+    perm = torch.randperm(nb).tolist()
+    maxb = max(-(-l // bs) for l in lens)
+    bt = torch.zeros(len(lens), maxb, dtype=torch.int32)
+    k = 0
+    for i, l in enumerate(lens):
+        n = -(-l // bs)
+        bt[i, :n] = torch.tensor(perm[k:k + n])
+        k += n
+    cu = [0]
+    for q in qlens:
+        cu.append(cu[-1] + q)
+    q = rnd(cu[-1], Hq * 128, seed=seed + 2)
+    return kc, vc, bt.to(DEV), torch.tensor(cu, dtype=torch.int32, device=DEV), \
+        torch.tensor(lens, dtype=torch.int32, device=DEV), q
+
+
+@pytest.mark.parametrize("bs", [16, 64])
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4)])
+def test_paged_prefill(bs, Hq, Hkv):
+    lens = [1, 63, 64, 65, 200, 513]
+    qlens = [1, 63, 10, 65, 200, 100]
+    kc, vc, bt, cu, ctx, q = _paged_setup(lens, qlens, Hq, Hkv, bs)
+    tiles = torch.tensor(ops.prefill_tiles(cu.tolist()), dtype=torch.int32, device=DEV)
+    out = torch.zeros(q.shape[0], Hq * 128, dtype=torch.bfloat16, device=DEV)
+    ops.paged_prefill(q, kc, vc, bt, cu, ctx, tiles, out, Hq, 1 / math.sqrt(128))
+    exp = torch.zeros_like(out, dtype=torch.float32).cpu()
+    ref.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), cu.cpu(), ctx.cpu(), exp, Hq, 1 / math.sqrt(128))
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+def test_paged_decode(G):
+    Hkv, bs = 2, 64
+    Hq = G * Hkv
+    lens = [1, 64, 65, 700, 2049, 33]
+    kc, vc, bt, _, ctx, _ = _paged_setup(lens, [1] * len(lens), Hq, Hkv, bs)
+    q = rnd(len(lens), Hq * 128, seed=21)
+    out = torch.zeros(len(lens), Hq * 128, dtype=torch.bfloat16, device=DEV)
+    splits, kps = ops.decode_splits(len(lens), Hkv, max(lens))
+    po = torch.empty(len(lens) * Hq * splits * 128, device=DEV)
+    pml = torch.empty(len(lens) * Hq * splits * 2, device=DEV)
+    ops.paged_decode(q, kc, vc, bt, ctx, out, Hq, 1 / math.sqrt(128), po, pml, splits, kps)
+    exp = torch.zeros(len(lens), Hq * 128)
+    ref.paged_decode(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), ctx.cpu(), exp, Hq, 1 / math.sqrt(128))
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+def test_embedding_vocab_parallel():
+    table = rnd(100, 256, seed=22)
+    ids = torch.tensor([0, 5, 99, 100, 150, 210], device=DEV)
+    out = torch.empty(6, 256, dtype=torch.bfloat16, device=DEV)
+    ops.embedding(ids, table, out, 100)
+    exp = torch.zeros(6, 256, dtype=torch.bfloat16)
+    ref.embedding(ids.cpu(), table.cpu(), exp, 100)
+    torch.testing.assert_close(out.cpu(), exp)
+
+
+def test_cross_entropy():
+    R, V = 33, 50000
+    logits = rnd(R, V, scale=3.0, dtype=torch.float32, seed=23)
+    tgt = torch.randint(0, V, (R,), device=DEV)
+    tgt[3] = -1
+    loss = torch.empty(R, device=DEV)
+    grad = torch.empty(R, V, dtype=torch.bfloat16, device=DEV)
+    ops.ce_fwd_bwd(logits, tgt, loss, grad, 0.25)
+    l2, g2 = torch.empty(R), torch.empty(R, V, dtype=torch.bfloat16)
+    ref.ce_fwd_bwd(logits.cpu(), tgt.cpu(), l2, g2, 0.25)
+    torch.testing.assert_close(loss.cpu(), l2, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(grad.float().cpu(), g2.float(), rtol=2e-2, atol=1e-4)
+
+
+def test_adamw_clip():
+    L, seg = 5, 10000
+    p = rnd(L * seg, dtype=torch.float32, seed=24)
+    g = rnd(L * seg, scale=3.0, dtype=torch.float32, seed=25)
+    m = torch.zeros_like(p); v = torch.zeros_like(p)
+    ss = torch.empty(L, device=DEV)
+    ops.seg_sumsq(g, seg, ss)
+    pr, mr, vr = p.cpu().clone(), m.cpu().clone(), v.cpu().clone()
+    ssr = torch.empty(L)
+    ref.seg_sumsq(g.cpu(), seg, ssr)
+    torch.testing.assert_close(ss.cpu(), ssr, rtol=1e-4, atol=1e-3)
+    for step in (1, 2):
+        ops.adamw(p, g, m, v, seg_len=seg, seg_sumsq_t=ss, max_norm=1.0, grad_scale=0.5, lr=1e-3,
+                  wd=0.01, step=step)
+        ref.adamw(pr, g.cpu(), mr, vr, seg, ssr, 1.0, 0.5, 1e-3, 0.9, 0.999, 1e-8, 0.01, step)
+    torch.testing.assert_close(p.cpu(), pr, rtol=1e-5, atol=1e-6)
+
+
+def test_lora_publish():
+    N, R, K, slots = 384, 16, 256, 3
+    A = rnd(3 * R, K, dtype=torch.float32, seed=26)
+    Bt = rnd(R, N, dtype=torch.float32, seed=27)
+    Ad = torch.zeros(slots, 3 * R, K, dtype=torch.bfloat16, device=DEV)
+    B2 = torch.zeros(N, slots * 64, dtype=torch.bfloat16, device=DEV)
+    ops.lora_publish(A, Ad[1], Bt, B2, 64, 128, 256, False, 2.0)
+    Adr, B2r = torch.zeros_like(Ad).cpu(), torch.zeros_like(B2).cpu()
+    ref.lora_publish(A.cpu(), Adr[1], Bt.cpu(), B2r, 64, 128, 256, False, 2.0)
+    torch.testing.assert_close(Ad.cpu(), Adr)
+    torch.testing.assert_close(B2.cpu(), B2r)
+
+
+def test_sample_greedy():
+    logits = rnd(7, 30000, dtype=torch.float32, seed=28)
+    out = torch.empty(7, dtype=torch.int64, device=DEV)
+    ops.sample(logits, torch.zeros(7, device=DEV), torch.arange(7, device=DEV), out)
+    assert torch.equal(out, logits.argmax(-1))
+    ops.sample(logits, torch.ones(7, device=DEV), torch.arange(7, device=DEV), out)
+    assert ((out >= 0) & (out < 30000)).all()
