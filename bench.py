@@ -1,0 +1,276 @@
+#!/usr/bin/env python
+"""Headline benchmark: co-served finetuning tokens/s at >= 99 % SLO attainment,
+with p99 TTFT / TBT, Llama-3-8B architecture (random init, bf16) at TP=N.
+
+Trace: Poisson arrivals at 8 req/s per GPU; prompt lengths
+lognormal (median 512, clipped to 32..4096); output lengths uniform 32..256;
+uniform-random token ids; every inference request uses an r=16 inference LoRA.
+Finetuning stream: uniform-random 512-token sequences, 8 per backward cycle,
+AdamW, trainable r=16 / alpha=32 LoRA on all seven projections. SLOs: TTFT
+500 ms, TBT 60 ms.
+
+Timing: W warm-up engine steps, then EXACTLY K steps bracketed by a device-wide
+synchronize + stamp on every rank (the stamps travel in the rank-0 step plan,
+so every rank stamps at the same point); device time of the region is the
+max over ranks. ``value`` = FT tokens forwarded-and-captured for training in
+the region / region seconds (each captured token is trained in the next
+backward cycle). The e2e number is the same count over the wall clock of the
+region measured around the public ``CoServingEngine.step()`` calls, which
+copy every step's inputs host->device (pinned) and read sampled tokens back.
+
+``--impl reference`` runs the reference plugin (vLLM + DeltaServe) when it can
+run here, else prints an ``unavailable`` line.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W]; for N > 1 launch
+under torchrun (one rank per GPU).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric/config
+METRIC = "co-served FT tokens/s at ≥99% SLO attainment; p99 TTFT & TBT (Llama-3-8B TP8)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=600)
+    p.add_argument("--warmup", type=int, default=40)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="llama3-8b")
+    p.add_argument("--rate-per-gpu", type=float, default=8.0)
+    p.add_argument("--ft-seq", type=int, default=512)
+    p.add_argument("--ft-batch", type=int, default=8)
+    p.add_argument("--max-batched-tokens", type=int, default=8192)
+    p.add_argument("--ttft-slo", type=float, default=0.5)
+    p.add_argument("--tbt-slo", type=float, default=0.06)
+    p.add_argument("--profile-repeats", type=int, default=1)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"])
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: str):
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._gpus = gpus
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                      "-i", self._gpus], capture_output=True, text=True, timeout=5).stdout
+                for line in out.strip().splitlines():
+                    self.rows.append([c.strip() for c in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=6)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def make_trace(rate: float, duration_s: float, vocab: int, seed: int):
+    rng = np.random.default_rng(seed)
+    t, out = 0.0, []
+    while t < duration_s:
+        t += rng.exponential(1.0 / rate)
+        plen = int(np.clip(np.round(rng.lognormal(np.log(512), 0.8)), 32, 4096))
+        olen = int(rng.integers(32, 257))
+        out.append((t, rng.integers(0, vocab, size=plen).tolist(), olen))
+    return out
+
+
+def percentile(x, q):
+    return float(np.percentile(np.asarray(x), q)) if len(x) else None
+
+
+def reference_arm(args) -> None:
+    line = {"impl": "reference", "metric": METRIC, "n_gpus": args.gpus}
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    try:
+        sys.path.insert(0, ref_dir)
+        import deltaserve  # noqa: F401
+        import vllm
+        ver = vllm.__version__
+    except Exception as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference plugin not importable: {e!r}"}))
+        return
+    if not ver.startswith("0.33"):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"reference targets vLLM 0.33.0; only vLLM {ver} is installed here and no "
+                          f"0.33 wheel exists offline (plugin installed with --no-deps)"}))
+        return
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            reference_arm(args)
+        return
+    import torch
+    from deltaserve_vllm_b200 import dprint, ops
+    from deltaserve_vllm_b200.config import EngineConfig, FinetuneConfig
+    from deltaserve_vllm_b200.engine.ft.store import FinetuningStore
+    from deltaserve_vllm_b200.engine.llm_engine import CoServingEngine
+    from deltaserve_vllm_b200.engine.request import SamplingParams
+    from deltaserve_vllm_b200.models.configs import resolve_arch
+    from deltaserve_vllm_b200.parallel.comm import init_tp
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}; launch N>1 under torchrun")
+    comm = init_tp(timeout_s=300) if ws > 1 else None
+    rank = comm.rank if comm is not None else 0
+    if not torch.cuda.is_available() or not ops.native_available():
+        raise SystemExit("bench needs a B200 and the built extension")
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    arch = resolve_arch(args.model)
+    cap = args.ft_seq * args.ft_batch
+    ecfg = EngineConfig(model=args.model, tensor_parallel_size=args.gpus, max_model_len=4096 + 512,
+                        block_size=64, max_num_seqs=256, max_num_batched_tokens=args.max_batched_tokens,
+                        max_loras=2, max_lora_rank=16, gpu_memory_utilization=0.85, seed=args.seed,
+                        tp_comm=args.tp_comm)
+    fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
+                          num_epochs=1000, ttft_slo=args.ttft_slo, max_tbt_slo=args.tbt_slo,
+                          avg_tbt_slo=args.tbt_slo, admission_margin="relative", admission_margin_k=1.5,
+                          pause_on_arrival=True, backward_run_ahead_boundaries=2,
+                          profile_num_repeats=args.profile_repeats)
+    store = FinetuningStore.synthetic(arch.vocab, 512, args.ft_seq, args.ft_seq, seed=args.seed + 7,
+                                      max_saved_finetuning_tokens=cap, total_epochs=1000)
+    t0 = time.perf_counter()
+    eng = CoServingEngine(ecfg, fcfg, comm=comm, arch=arch, ft_store=store)
+    eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
+    if rank != 0:
+        eng.follow()
+        if comm is not None:
+            torch.distributed.destroy_process_group()
+        return
+    dprint(f"engine up in {time.perf_counter() - t0:.1f}s; KV blocks {eng.kv.num_blocks}")
+    eng.profile_execution_model(repeats=args.profile_repeats)
+    dprint(f"profiling done at {time.perf_counter() - t0:.1f}s; estimator ready={eng.estimator.is_ready}")
+    rate = args.rate_per_gpu * args.gpus
+    trace = make_trace(rate, 3600.0, arch.vocab, args.seed)
+    ti = 0
+    clock0 = time.perf_counter()
+
+    def ingest():
+        nonlocal ti
+        now = time.perf_counter() - clock0
+        while ti < len(trace) and trace[ti][0] <= now:
+            t_arr, ids, olen = trace[ti]
+            eng.add_request(f"q{ti}", ids, SamplingParams(max_tokens=olen), adapter="inf",
+                            arrival_time=clock0 + t_arr)
+            ti += 1
+
+    for _ in range(args.warmup):
+        ingest()
+        eng.step()
+    eng.synchronize()
+    stats0 = dict(eng.stats)
+    l0 = ops.LAUNCHES[0]
+    n_req0 = ti
+    gpu_idx = os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(args.gpus)))
+    with ClockSampler(gpu_idx) as clocks:
+        eng.mark("t0")
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            ingest()
+            eng.step()
+        w1 = time.perf_counter()
+        eng.mark("t1")
+    regions = eng.gather_region("t0", "t1")
+    launches = ops.LAUNCHES[0] - l0
+    dev_ms = max(r[0] for r in regions)
+    wall_ms = (w1 - w0) * 1e3
+    st = {k: eng.stats[k] - stats0[k] for k in stats0}
+    # requests that arrived inside the timed region
+    t_lo, t_hi = w0, w1
+    reqs = [r for r in list(eng.finished) + list(eng.requests.values())
+            if t_lo <= r.arrival_time <= t_hi and not r.request_id.startswith("__")]
+    ttfts = [r.ttft() for r in reqs if r.ttft() is not None]
+    tbts = [g for r in reqs for g in r.tbts()]
+    ok = 0
+    counted = 0
+    for r in reqs:
+        tt = r.ttft()
+        if tt is None:
+            if t_hi - r.arrival_time > args.ttft_slo:
+                counted += 1  # waited past the SLO without a token: violation
+            continue
+        counted += 1
+        g = r.tbts()
+        if tt <= args.ttft_slo and (not g or float(np.mean(g)) <= args.tbt_slo):
+            ok += 1
+    attain = ok / counted if counted else None
+    value = st["ft_tokens_forwarded"] / (dev_ms / 1e3)
+    e2e = st["ft_tokens_forwarded"] / (wall_ms / 1e3)
+    cs = clocks.summary()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "FT tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (round(value / BASELINE_VALUE, 3) if BASELINE_VALUE else None),
+        "dtype": "bf16", "data": "synthetic (random-init weights, uniform-random token ids)",
+        "config": {"model": args.model, "global_batch": args.ft_batch, "seq_len": args.ft_seq,
+                   "parallelism": f"tp{args.gpus}", "rate_req_s": rate,
+                   "prompts": "lognormal(median 512, sigma 0.8) clip 32..4096",
+                   "outputs": "uniform 32..256", "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
+                   "l2": "inputs larger than L2 (16 GB of weights stream every step)",
+                   "tp_comm": args.tp_comm},
+        "slo_attainment": attain, "p99_ttft_ms": (percentile(ttfts, 99) or 0) * 1e3 if ttfts else None,
+        "p99_tbt_ms": (percentile(tbts, 99) or 0) * 1e3 if tbts else None,
+        "p50_ttft_ms": (percentile(ttfts, 50) or 0) * 1e3 if ttfts else None,
+        "requests_in_region": len(reqs), "ft_tokens": st["ft_tokens_forwarded"],
+        "ft_tokens_trained": st["ft_tokens_trained"], "backward_cycles_total": eng.coord.completed_cycles,
+        "last_loss": eng.coord.last_loss, "valid_slo": (attain is not None and attain >= 0.99),
+        "e2e": {"value": round(e2e, 2), "unit": "FT tokens/s (wall clock, public step() API)",
+                "h2d_bytes_per_step": int(st["h2d_bytes"] / max(1, st["steps"])),
+                "d2h_bytes_per_step": int(st["d2h_bytes"] / max(1, st["steps"]))},
+        "gpu_launches": int(launches), "clocks": cs, "device_ms_per_rank": [round(r[0], 2) for r in regions],
+    }
+    eng.shutdown()
+    print(json.dumps(line), flush=True)
+    if comm is not None:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+"""Finetuning jobs: a job is an ordered list of *stages* (``init`` ->
+``training`` -> optional ``ready``; with adapter routing also ``indexing`` and
+``admission``), run by :class:`FtJobManager` one job at a time from a queue
+(reference: ``deltaserve-plugin/deltaserve/ft_job.py:66-429``)."""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+DEFAULT_STAGES = ("init", "training")
+GATED_STAGES = {"indexing": "adapter_routing.enable_adapter_routing",
+                "admission": "adapter_routing.enable_adapter_routing"}
+JOB_META_KEYS = ("name", "stages", "auto_routing", "adapter_init", "save_path")
+
+
+class Stage:
+    name: str = ""
+
+    def requirements(self, stage_names: tuple[str, ...]) -> tuple[str, ...]:
+        return ()
+
+    def start(self, job: "FinetuneJob", ctx: Any) -> None:
+        pass
+
+    def poll(self, job: "FinetuneJob", ctx: Any) -> bool:
+        return True
+
+
+_STAGES: dict[str, type[Stage]] = {}
+
+
+def register_stage(cls: type[Stage]) -> type[Stage]:
+    if not cls.name:
+        raise ValueError(f"{cls.__name__} has no stage name")
+    _STAGES[cls.name] = cls
+    return cls
+
+
+def known_stages() -> tuple[str, ...]:
+    return tuple(_STAGES)
+
+
+def load_gated_stages(adapter_routing: bool) -> None:
+    if adapter_routing and "indexing" not in _STAGES:
+        from ..adapters.routing import stages  # noqa: F401  (registers)
+
+
+@register_stage
+class InitStage(Stage):
+    """Adapter weights loaded and dataset tokenized (both happen at engine
+    start); the stage only checks the dataset is there."""
+    name = "init"
+
+    def poll(self, job, ctx) -> bool:
+        store = getattr(ctx, "store", None)
+        return store is None or len(store) > 0
+
+
+@register_stage
+class TrainingStage(Stage):
+    """Done once the corpus finished every epoch and the last backward landed."""
+    name = "training"
+
+    def requirements(self, names):
+        return ("init",) if "init" in names else ()
+
+    def start(self, job, ctx) -> None:
+        coord = getattr(ctx, "coord", None)
+        if coord is not None and getattr(ctx, "start_on_launch", True):
+            coord.start()
+
+    def poll(self, job, ctx) -> bool:
+        store, coord = getattr(ctx, "store", None), getattr(ctx, "coord", None)
+        if store is None or coord is None:
+            return True
+        return store.finished() and not coord.pending_backward and coord.fill_count == 0
+
+
+@register_stage
+class ReadyStage(Stage):
+    """The trained adapter is saved (when the job names a save path)."""
+    name = "ready"
+
+    def requirements(self, names):
+        return ("training",)
+
+    def start(self, job, ctx) -> None:
+        save = getattr(ctx, "save_job_adapter", None)
+        if save is not None and job.spec.save_path:
+            save(job)
+
+    def poll(self, job, ctx) -> bool:
+        return True
+
+
+@dataclass
+class FinetuneJobSpec:
+    name: str = "default"
+    stages: tuple[str, ...] = DEFAULT_STAGES
+    adapter_path: str | None = None
+    data_path: str | None = None
+    num_epochs: int = 1
+    learning_rate: float = 1e-4
+    weight_decay: float = 0.0
+    gamma: float = 1.0
+    auto_routing: bool = False
+    adapter_init: str | None = None
+    save_path: str | None = None
+
+    @classmethod
+    def from_finetune_config(cls, cfg) -> "FinetuneJobSpec":
+        meta = dict(cfg.ft_job or {})
+        unknown = sorted(set(meta) - set(JOB_META_KEYS))
+        if unknown:
+            raise ValueError(f"unknown ft_job key(s) {unknown}")
+        stages = meta.get("stages", DEFAULT_STAGES)
+        if isinstance(stages, str) or not all(isinstance(s, str) for s in stages):
+            raise ValueError("ft_job.stages must be a list of stage names")
+        return cls(name=meta.get("name", "default"), stages=tuple(stages),
+                   adapter_path=cfg.finetuning_lora_path, data_path=cfg.data_path,
+                   num_epochs=cfg.num_epochs, learning_rate=cfg.learning_rate,
+                   weight_decay=cfg.weight_decay, gamma=cfg.gamma,
+                   auto_routing=bool(meta.get("auto_routing", False)),
+                   adapter_init=meta.get("adapter_init"), save_path=meta.get("save_path"))
+
+    def validate(self, adapter_routing: bool = False) -> None:
+        load_gated_stages(adapter_routing)
+        for s in self.stages:
+            if s in GATED_STAGES and not adapter_routing:
+                raise ValueError(f"ft_job stage '{s}' needs {GATED_STAGES[s]}: true")
+            if s not in _STAGES:
+                raise ValueError(f"unknown ft_job stage '{s}' (known: {sorted(_STAGES)})")
+        if len(set(self.stages)) != len(self.stages):
+            raise ValueError("ft_job.stages lists a stage twice")
+        for s in self.stages:
+            for req in _STAGES[s]().requirements(self.stages):
+                if req not in self.stages:
+                    raise ValueError(f"stage '{s}' needs stage '{req}'")
+        if self.adapter_init not in (None, "random", "zeros") and not self.adapter_path:
+            raise ValueError("ft_job.adapter_init must be 'random' or 'zeros'")
+
+
+@dataclass
+class FinetuneJob:
+    spec: FinetuneJobSpec
+    job_id: int = 0
+    state: str = "queued"          # queued | running | done | failed | cancelled
+    stage_state: dict = field(default_factory=dict)
+    created: float = field(default_factory=time.time)
+    started: float | None = None
+    finished: float | None = None
+    error: str | None = None
+
+    def status(self) -> dict:
+        return {"job_id": self.job_id, "name": self.spec.name, "state": self.state,
+                "stages": dict(self.stage_state), "error": self.error,
+                "created": self.created, "started": self.started, "finished": self.finished}
+
+
+class FtJobManager:
+    """Runs queued jobs one at a time; ``tick(ctx)`` advances stages."""
+
+    def __init__(self):
+        self.jobs: list[FinetuneJob] = []
+        self._next_id = 1
+
+    def submit(self, spec: FinetuneJobSpec, adapter_routing: bool = False) -> FinetuneJob:
+        spec.validate(adapter_routing)
+        job = FinetuneJob(spec, self._next_id)
+        self._next_id += 1
+        job.stage_state = {s: "pending" for s in spec.stages}
+        self.jobs.append(job)
+        return job
+
+    def current(self) -> FinetuneJob | None:
+        for j in self.jobs:
+            if j.state in ("queued", "running"):
+                return j
+        return None
+
+    def cancel(self, job_id: int) -> bool:
+        for j in self.jobs:
+            if j.job_id == job_id and j.state in ("queued", "running"):
+                j.state = "cancelled"
+                j.finished = time.time()
+                return True
+        return False
+
+    def tick(self, ctx: Any) -> None:
+        job = self.current()
+        if job is None:
+            return
+        if job.state == "queued":
+            job.state = "running"
+            job.started = time.time()
+        names = job.spec.stages
+        for s in names:
+            st = job.stage_state[s]
+            if st == "done":
+                continue
+            stage = _STAGES[s]()
+            reqs = stage.requirements(names)
+            if any(job.stage_state.get(r) != "done" for r in reqs):
+                continue
+            try:
+                if st == "pending":
+                    stage.start(job, ctx)
+                    job.stage_state[s] = "running"
+                if stage.poll(job, ctx):
+                    job.stage_state[s] = "done"
+            except Exception as e:  # a failing stage fails the job, not the engine
+                job.state = "failed"
+                job.error = f"{s}: {e!r}"
+                job.finished = time.time()
+                return
+        if all(v == "done" for v in job.stage_state.values()):
+            job.state = "done"
+            job.finished = time.time()
+
+    def status(self) -> list[dict]:
+        return [j.status() for j in self.jobs]

@@ -1,0 +1,743 @@
+"""The co-serving engine: inference with continuous batching and multi-LoRA,
+plus LoRA finetuning on the same GPU(s).
+
+One process per GPU. Rank 0 owns every decision (scheduling, FT admission,
+backward triggers, pauses) and sends each step's *plan* (packed integer
+metadata + a few flags) to the other tensor-parallel ranks, which replay it;
+every rank therefore issues the same kernels and collectives in the same order
+(rank-symmetric by construction — no per-layer host votes).
+
+Step (rank 0):
+
+1. ingest arrivals; throttles; job tick;
+2. inference schedule (decode, then chunked prefill);
+3. FT admission against the SLOs using the step's exact composition; the
+   admitted samples are appended as whole prefill-only rows and get capture
+   offsets in the activation buffer;
+4. forward on the high-priority stream (activations of FT rows captured by
+   the kernels), sampling, scheduler update, per-step CUDA-event timing into
+   the estimator (read one step late so the host never waits for it);
+5. a full buffer starts a backward cycle; the cycle advances on the
+   low-priority stream between steps, one layer per boundary, unless an
+   inference prefill is pending (pause-on-arrival) or the run-ahead bound is
+   reached; its completion (an event) publishes the adapter and reopens
+   admission.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import dprint, ops
+from ..config import AdapterRoutingConfig, EngineConfig, FinetuneConfig
+from ..models.configs import ModelArch, resolve_arch
+from ..models.decoder import CaptureBuffers, DecoderModel
+from ..models.lora import LoraServeBuffers, random_adapter
+from ..models.weights import TPInfo, init_weights
+from .ft.admission import FinetuneAdmission
+from .ft.coordinator import FinetuneCoordinator
+from .ft.estimator import MergedExecutionEstimator, StepExecutionTracker, StepFeatures, set_ft_mixed_split
+from .ft.store import FinetuningStore
+from .ft.tbt_window import TbtWindow
+from .ft_job import FinetuneJobSpec, FtJobManager
+from .kv_cache import KVCache
+from .model_runner import ModelRunner
+from .request import Request, SamplingParams, Status
+from .scheduler import Scheduler, SchedulerOutput
+from .trainer import LoraTrainer
+
+FT_ADAPTER_NAME = "__finetune__"
+
+
+@dataclass
+class StepRecord:
+    features: StepFeatures
+    start: object          # cuda event or float
+    end: object
+    predicted: float | None
+    kind: str
+
+
+class CoServingEngine:
+    def __init__(self, ecfg: EngineConfig, ftcfg: FinetuneConfig | None = None,
+                 rcfg: AdapterRoutingConfig | None = None, comm=None,
+                 arch: ModelArch | None = None, adapters: dict | None = None,
+                 tokenizer=None, ft_store: FinetuningStore | None = None,
+                 ft_adapter: tuple[dict, int, float] | None = None):
+        self.ecfg = ecfg
+        self.ftcfg = ftcfg or FinetuneConfig()
+        self.rcfg = rcfg or AdapterRoutingConfig()
+        self.comm = comm
+        self.tp = TPInfo(comm.rank, comm.size) if comm is not None else TPInfo()
+        self.is_driver = self.tp.rank == 0
+        dev = ecfg.device or ("cuda" if torch.cuda.is_available() else "cpu")
+        if dev == "cuda":
+            dev = f"cuda:{torch.cuda.current_device()}"
+        self.device = torch.device(dev)
+        self.cuda = self.device.type == "cuda"
+        self.dtype = torch.bfloat16 if self.cuda else torch.float32
+        self.arch = arch or resolve_arch(ecfg.model)
+        self.tokenizer = tokenizer
+        t0 = time.perf_counter()
+        self.weights = init_weights(self.arch, self.tp, seed=ecfg.seed, device=self.device,
+                                    dtype=self.dtype,
+                                    keep_full_head=self.ftcfg.enable_finetuning)
+        # ---- LoRA slots: inference adapters + the pinned FT slot
+        self.adapter_slots: dict[str, int] = {}
+        self.adapter_meta: dict[str, dict] = {}
+        n_slots = max(1, ecfg.max_loras) if ecfg.enable_lora else 0
+        self.lora = (LoraServeBuffers(self.arch, self.tp, n_slots, ecfg.max_lora_rank, self.device,
+                                      self.dtype) if n_slots else None)
+        self.ft_slot = -1
+        # ---- finetuning
+        self.ft_enabled = bool(self.ftcfg.enable_finetuning) and self.lora is not None
+        cap_tokens = self.ftcfg.max_saved_finetuning_tokens
+        self.capture = (CaptureBuffers.allocate(self.weights, cap_tokens + 8, self.device, self.dtype)
+                        if self.ft_enabled else None)
+        # ---- KV cache sized from what is left
+        self.kv = self._alloc_kv()
+        self.model = DecoderModel(self.weights, self.kv.k, self.kv.v, self.lora, comm)
+        num_sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
+                   if self.cuda else 148)
+        self.scheduler = Scheduler(self.kv.allocator, ecfg.block_size, ecfg.max_num_seqs,
+                                   ecfg.max_num_batched_tokens, ecfg.max_model_len,
+                                   ecfg.enable_chunked_prefill)
+        self.runner = ModelRunner(self.model, ecfg.block_size, self.device, num_sms)
+        # Backward collectives use their own communicator: forward and backward
+        # run on different streams and must never share an NCCL queue.
+        self.bwd_comm = comm
+        if comm is not None and comm.size > 1:
+            import torch.distributed as dist
+            from ..parallel.comm import TPComm
+            self.bwd_comm = TPComm(dist.new_group(list(range(comm.size))), comm.cpu_group)
+        self._actions: list = []
+        self.estimator = MergedExecutionEstimator()
+        self.estimator.set_margin(self.ftcfg.admission_margin, self.ftcfg.admission_margin_k)
+        set_ft_mixed_split(self.ftcfg.graph_ft_batches)
+        self.tracker = StepExecutionTracker()
+        self.tbt_window = TbtWindow(self.ftcfg.avg_tbt_window_s) if self.ftcfg.avg_tbt_window_s > 0 else None
+        self.coord = FinetuneCoordinator(cap_tokens, ft_started=self.ftcfg.start_on_launch,
+                                         bwd_log_path=self.ftcfg.bwd_log_path)
+        self.jobs = FtJobManager()
+        self.store = ft_store
+        self.trainer: LoraTrainer | None = None
+        if self.ft_enabled:
+            self.ft_slot = n_slots - 1
+            self.adapter_slots[FT_ADAPTER_NAME] = self.ft_slot
+            self.runner.ft_slot = self.ft_slot
+            self._init_finetuning(ft_adapter)
+        for name, spec in (adapters or {}).items():
+            self.load_inference_adapter(name, **spec)
+        # ---- streams: forward high priority, backward low priority
+        if self.cuda:
+            self.fwd_stream = torch.cuda.Stream(self.device, priority=-2)
+            self.bwd_stream = torch.cuda.Stream(self.device, priority=0)
+        else:
+            self.fwd_stream = self.bwd_stream = None
+        self._bwd_gen = None
+        self._bwd_events: deque = deque()
+        self._bwd_done_evt = None
+        self._bwd_meta: dict | None = None
+        self._bwd_result = None
+        self._publish_evt = None
+        self._pending_timing: deque[StepRecord] = deque()
+        self.requests: dict[str, Request] = {}
+        self.finished: list[Request] = []
+        self.step_no = 0
+        self.profiling = False
+        self.last_admit = None
+        self.stats = {"ft_tokens_forwarded": 0, "ft_tokens_trained": 0, "steps": 0,
+                      "bwd_layers": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+        self.arrival_flag = False
+        self._forced_ft = None
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        self.init_s = time.perf_counter() - t0
+        self.step_listeners: list = []
+        self.request_listeners: list = []
+        self.backward_listeners: list = []
+
+    # ------------------------------------------------------------------ setup
+    def _alloc_kv(self) -> KVCache:
+        e = self.ecfg
+        hkv = self.arch.num_kv_heads // self.tp.size
+        per_block = KVCache.bytes_per_block(self.arch.num_layers, hkv, e.block_size,
+                                            self.arch.head_dim, 2 if self.cuda else 4)
+        if e.num_gpu_blocks_override:
+            nb = e.num_gpu_blocks_override
+        elif self.cuda:
+            free, total = torch.cuda.mem_get_info(self.device)
+            reserve = total * (1 - e.gpu_memory_utilization) + 6 * (1 << 30)  # workspaces
+            nb = int(max(0, free - reserve) // per_block)
+            # Enough for max_num_seqs full contexts is plenty.
+            nb = min(nb, e.max_num_seqs * -(-e.max_model_len // e.block_size) + 64)
+        else:
+            nb = 4 * (-(-e.max_model_len // e.block_size)) + 16
+        if nb < 2:
+            raise MemoryError("no room for the KV cache")
+        return KVCache(self.arch.num_layers, nb, hkv, e.block_size, self.arch.head_dim, self.device,
+                       self.dtype)
+
+    def _init_finetuning(self, ft_adapter) -> None:
+        from ..adapters import peft_io
+        cfg = self.ftcfg
+        tensors, rank, alpha, acfg = None, self.ecfg.max_lora_rank, 2.0 * self.ecfg.max_lora_rank, None
+        if ft_adapter is not None:
+            tensors, rank, alpha = ft_adapter
+        elif cfg.finetuning_lora_path and os.path.isfile(
+                os.path.join(cfg.finetuning_lora_path, peft_io.CONFIG_FILE)):
+            tensors, acfg = peft_io.read_adapter(cfg.finetuning_lora_path)
+            rank, alpha = peft_io.adapter_rank_alpha(acfg)
+        self.trainer = LoraTrainer(self.weights, self.lora, self.ft_slot, rank, alpha,
+                                   lr=cfg.learning_rate, weight_decay=cfg.weight_decay,
+                                   gamma=cfg.gamma, comm=self.bwd_comm, mask_prefix=cfg.loss_mask_prefix,
+                                   targets=cfg.ft_target_modules, adapter_config=acfg,
+                                   cos_sin_table=self.model_cos_sin())
+        if tensors:
+            self.trainer.load_adapter(tensors, rank, alpha)
+        else:
+            self.trainer.init_random(self.ecfg.seed + 1)
+        self.trainer.publish()
+        self.adapter_meta[FT_ADAPTER_NAME] = {"rank": rank, "alpha": alpha, "trainable": True}
+        if self.store is None:
+            tok = self.tokenizer.encode if self.tokenizer is not None else None
+            self.store = FinetuningStore(cfg.data_path, tok, FT_ADAPTER_NAME, cfg.num_epochs,
+                                         cfg.max_saved_finetuning_tokens, cfg.max_prepare)
+            if cfg.data_path:
+                self.store.load()
+        self.coord.min_sample_len = max(1, self.store.min_len() or 1)
+        self.admission = FinetuneAdmission(cfg, self.estimator, self.coord, self.store,
+                                           self.ecfg.max_num_batched_tokens, self.tbt_window)
+        self.jobs.submit(FinetuneJobSpec.from_finetune_config(cfg), self.rcfg.enable_adapter_routing)
+
+    def model_cos_sin(self):
+        from ..ops.reference import rope_cos_sin_table
+        return rope_cos_sin_table(max(self.arch.max_position, 8192), self.arch.head_dim,
+                                  self.arch.rope_theta, self.arch.rope_scaling, device=self.device)
+
+    def load_inference_adapter(self, name: str, path: str | None = None, tensors=None,
+                               rank: int | None = None, alpha: float | None = None,
+                               seed: int | None = None) -> int:
+        """Put an inference LoRA into a free slot (PEFT dir, tensors, or random)."""
+        from ..adapters import peft_io
+        if self.lora is None:
+            raise RuntimeError("LoRA is disabled (enable_lora: false)")
+        if name in self.adapter_slots:
+            return self.adapter_slots[name]
+        used = set(self.adapter_slots.values())
+        free = [s for s in range(self.lora.slots) if s not in used]
+        if not free:
+            raise RuntimeError("no free LoRA slot (raise max_loras)")
+        slot = free[0]
+        if path is not None:
+            tensors, acfg = peft_io.read_adapter(path)
+            rank, alpha = peft_io.adapter_rank_alpha(acfg)
+        elif tensors is None:
+            rank = rank or self.ecfg.max_lora_rank
+            alpha = alpha if alpha is not None else 2.0 * rank
+            tensors = random_adapter(self.arch, rank, seed if seed is not None else 1000 + slot)
+        self.lora.load_slot(slot, tensors, rank, alpha)
+        self.adapter_slots[name] = slot
+        self.adapter_meta[name] = {"rank": rank, "alpha": alpha, "path": path}
+        return slot
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, request_id: str, prompt_ids: list[int], params: SamplingParams | None = None,
+                    adapter: str | None = None, arrival_time: float | None = None) -> Request:
+        r = Request(request_id, list(prompt_ids), params or SamplingParams(), adapter,
+                    arrival_time if arrival_time is not None else time.perf_counter())
+        if adapter is not None:
+            if adapter not in self.adapter_slots:
+                raise KeyError(f"unknown adapter {adapter!r}")
+            r.lora_slot = self.adapter_slots[adapter]
+        self.scheduler.add(r)
+        self.requests[request_id] = r
+        self.coord.note_arrival(r.arrival_time)
+        self.arrival_flag = True
+        for cb in self.request_listeners:
+            cb("add", r)
+        return r
+
+    def abort_request(self, request_id: str) -> bool:
+        r = self.scheduler.abort(request_id)
+        return r is not None
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    # ------------------------------------------------------------------ control
+    def start_finetuning(self) -> None:
+        self.coord.start()
+
+    def stop_finetuning(self) -> None:
+        self.coord.stop()
+
+    def finetuning_status(self) -> dict:
+        st = self.coord.status()
+        st.update({"enabled": self.ft_enabled,
+                   "trainer_step": self.trainer.step if self.trainer else 0,
+                   "store_untrained": self.store.num_untrained() if self.store else 0,
+                   "store_epoch": self.store.current_epoch if self.store else 0,
+                   "losses_tail": self.trainer.losses[-8:] if self.trainer else [],
+                   "jobs": self.jobs.status()})
+        return st
+
+    def save_adapter(self, path: str | None = None, save_id: str = "") -> str | None:
+        if self.trainer is None:
+            raise RuntimeError("finetuning is not enabled")
+        if path is None:
+            if not self.ftcfg.adapter_save_path:
+                raise ValueError("no path given and finetune_param.adapter_save_path is unset")
+            path = os.path.join(self.ftcfg.adapter_save_path, f"manual-{int(time.time())}")
+        self._drain_backward()
+        return self.trainer.save_adapter(path, save_id)
+
+    # ------------------------------------------------------------------ stepping
+    def _ft_rows_in(self, out: SchedulerOutput) -> int:
+        return sum(s.num_new for s in out.ft)
+
+    def _earliest_waiting_arrival(self, out: SchedulerOutput) -> float | None:
+        t = [s.req.arrival_time for s in out.prefill if s.req.first_token_time is None]
+        t += [r.arrival_time for r in self.scheduler.waiting]
+        return min(t) if t else None
+
+    def _drain_timing(self, block: bool = False) -> None:
+        while self._pending_timing:
+            rec = self._pending_timing[0]
+            if self.cuda:
+                if not block and not rec.end.query():
+                    return
+                dur = rec.start.elapsed_time(rec.end) / 1e3
+            else:
+                dur = rec.end - rec.start
+            self._pending_timing.popleft()
+            self.tracker.add(rec.features, dur, rec.predicted)
+            for cb in self.step_listeners:
+                cb(rec, dur)
+            if self.tracker.check_refit():
+                self.estimator.data_fit(self.tracker)
+
+    def step(self) -> list[Request]:
+        """One engine step (rank 0). Returns requests that finished."""
+        now = time.perf_counter()
+        self.step_no += 1
+        self._drain_timing()
+        self._poll_backward()
+        cfg = self.ftcfg
+        if self.ft_enabled:
+            if cfg.rps_throttle_enable:
+                self.coord.check_rps_throttle(now, cfg.rps_throttle_close_rps, cfg.rps_throttle_open_rps,
+                                              cfg.rps_throttle_window_s, cfg.rps_throttle_close_time)
+            self.coord.check_stuck(True)
+            self.jobs.tick(self)
+            if self.coord.try_flush():
+                self._start_backward()
+        out = self.scheduler.schedule()
+        bwd_busy = self._bwd_gen is not None or self._bwd_done_evt is not None
+        adm = None
+        ft_dst = 0
+        if self.profiling and getattr(self, "_forced_ft", None):
+            self.scheduler.add_ft(out, self._forced_ft)
+            self._forced_ft = None
+        if self.ft_enabled and not self.profiling:
+            adm = self.admission.admit(out, self._earliest_waiting_arrival(out), now,
+                                       bwd_in_flight=bwd_busy)
+            self.last_admit = adm
+            if adm.samples:
+                reqs = [Request(f"__ft__{s.request_id[:8]}_{self.step_no}", s.prompt_ids,
+                                SamplingParams(max_tokens=1), FT_ADAPTER_NAME, now, is_ft=True,
+                                ft_sample=s) for s in adm.samples]
+                rejected = self.scheduler.add_ft(out, reqs)
+                if rejected:
+                    self.store.release_claimed([r.ft_sample for r in rejected])
+                kept = [s.req.ft_sample for s in out.ft]
+                ft_dst = self.coord.reserve(self._ft_rows_in(out), kept)
+                nxt = self.store.pop_next()
+                self.coord.note_injection(nxt.input_len if nxt else None)
+            # Tier B: an FT-only step about to run while an arrival is pending.
+            if (cfg.forward_interruptible and out.ft and not out.decode and not out.prefill
+                    and self.scheduler.waiting):
+                self._rollback_ft(out)
+        if out.is_empty():
+            self._advance_backward(idle=not self.has_unfinished())
+            self._flush_actions()
+            return []
+        return self._run(out, ft_dst, bwd_busy)
+
+    def _rollback_ft(self, out: SchedulerOutput) -> None:
+        reqs = self.scheduler.rollback_ft(out)
+        samples = [r.ft_sample for r in reqs]
+        self.coord.unreserve(sum(r.num_prompt for r in reqs), samples)
+        self.store.release_claimed(samples)
+
+    def _run(self, out: SchedulerOutput, ft_dst: int, bwd_busy: bool,
+             record_capture: bool = True) -> list[Request]:
+        feats = StepFeatures(t_in=float(out.t_in), p=len(out.prefill) + len(out.ft),
+                             t_ft=float(out.t_ft), b_d=out.b_d, k=float(out.k_decode),
+                             prefill_lens=out.prefill_lens() or None, bwd=bwd_busy)
+        pred = self.estimator.predict(feats) if self.estimator.is_ready else None
+        # Pause: a step carrying inference prefill stops feeding the backward.
+        has_inf_prefill = bool(out.prefill)
+        uses_ft_slot = bool(out.ft) or any(s.req.lora_slot == self.ft_slot for s in out.seqs
+                                           if self.ft_slot >= 0)
+        if self.cuda:
+            with torch.cuda.stream(self.fwd_stream):
+                if uses_ft_slot and self._publish_evt is not None:
+                    self.fwd_stream.wait_event(self._publish_evt)
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)))
+                ev1.record()
+        else:
+            ev0 = time.perf_counter()
+            toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)))
+            ev1 = time.perf_counter()
+        self.stats["h2d_bytes"] += self.runner.last_h2d_bytes
+        self.stats["d2h_bytes"] += self.runner.last_d2h_bytes
+        self._pending_timing.append(StepRecord(feats, ev0, ev1, pred, "step"))
+        now = time.perf_counter()
+        done = self.scheduler.update(out, toks, now)
+        self.stats["steps"] += 1
+        if self.tbt_window is not None:
+            self.tbt_window.step_done(now, out.b_d, bool(self.scheduler.running))
+        if out.ft and (self.profiling or not record_capture):
+            pass  # profiling FT rows: captured at offset 0, never trained
+        elif out.ft:
+            n = self._ft_rows_in(out)
+            self.stats["ft_tokens_forwarded"] += n
+            if self.coord.record_capture(n, [s.num_new for s in out.ft]):
+                self._start_backward(capture_evt=ev1 if self.cuda else None)
+        for r in done:
+            self.requests.pop(r.request_id, None)
+            for cb in self.request_listeners:
+                cb("finish", r)
+        self.finished.extend(done)
+        self.arrival_flag = False
+        pause = has_inf_prefill and (self.ftcfg.pause_on_arrival or self.ftcfg.pause_until_prefill_done
+                                     or self.ftcfg.pause_prefill_always)
+        self._advance_backward(idle=False, paused=pause and bool(self.scheduler.waiting))
+        return done
+
+    # ------------------------------------------------------------------ backward
+    def _start_backward(self, capture_evt=None) -> None:
+        if self.trainer is None:
+            return
+        n = self.coord.fill_count
+        lens = list(self.coord.sample_lens)
+        starts = list(np.cumsum([0] + lens[:-1])) if lens else []
+        self._bwd_meta = {"n": n, "starts": [int(s) for s in starts], "lens": lens,
+                          "epoch": self.store.current_epoch if self.store else 0}
+        if self.cuda:
+            if capture_evt is not None:
+                self.bwd_stream.wait_event(capture_evt)
+            else:
+                self.bwd_stream.wait_stream(self.fwd_stream)
+        self._bwd_gen = self.trainer.cycle(self.capture, n, self._bwd_meta["starts"], lens,
+                                           self._bwd_meta["epoch"], sync=False)
+        self._bwd_events.clear()
+        self._record(("bwd_start", dict(self._bwd_meta)))
+
+    def _advance_backward(self, idle: bool, paused: bool = False) -> None:
+        """Enqueue backward layers: all remaining when the engine is idle,
+        otherwise a bounded number per step, never more than
+        ``backward_run_ahead_boundaries`` layers ahead of the GPU."""
+        if self._bwd_gen is None or (paused and not idle):
+            return
+        ahead = max(1, self.ftcfg.backward_run_ahead_boundaries)
+        budget = 1 << 30 if idle else ahead
+        while budget > 0 and self._bwd_gen is not None:
+            if self.cuda and len(self._bwd_events) >= ahead and not idle:
+                if not self._bwd_events[0].query():
+                    break
+                self._bwd_events.popleft()
+            try:
+                self._record(("bwd_next",))
+                if self.cuda:
+                    with torch.cuda.stream(self.bwd_stream):
+                        next(self._bwd_gen)
+                        ev = torch.cuda.Event()
+                        ev.record()
+                    self._bwd_events.append(ev)
+                    while len(self._bwd_events) > ahead:
+                        self._bwd_events.popleft()
+                else:
+                    next(self._bwd_gen)
+                self.stats["bwd_layers"] += 1
+            except StopIteration as e:
+                self._bwd_result = e.value
+                self._bwd_gen = None
+                if self.cuda:
+                    ev = torch.cuda.Event()
+                    ev.record(self.bwd_stream)
+                    self._bwd_done_evt = ev
+                    self._publish_evt = ev
+                else:
+                    self._finish_backward()
+            budget -= 1
+
+    def _poll_backward(self) -> None:
+        if self._bwd_done_evt is not None and self._bwd_done_evt.query():
+            self._finish_backward()
+
+    def _finish_backward(self) -> None:
+        res = self.trainer.finish_cycle(self._bwd_result) if self.trainer else self._bwd_result
+        self._bwd_done_evt = None
+        meta = self._bwd_meta or {}
+        trained = self.coord.backward_done(res.n_tokens, res.loss, res.gpu_ms, res.wall_ms,
+                                           meta.get("epoch"))
+        if self.store is not None:
+            self.store.commit_claimed([s for s in trained if s is not None])
+            self.coord.min_sample_len = max(1, self.store.min_len() or 1)
+            if not self.store.has_next():
+                self.store.advance_epoch()
+        self.stats["ft_tokens_trained"] += res.n_tokens
+        for cb in self.backward_listeners:
+            cb(res)
+        self._periodic_save()
+
+    def _periodic_save(self) -> None:
+        cfg = self.ftcfg
+        if not cfg.adapter_save_path or self.trainer is None:
+            return
+        from ..adapters import peft_io
+        st = self.trainer.step
+        if cfg.adapter_save_every_backwards > 0 and st % cfg.adapter_save_every_backwards == 0:
+            self.trainer.save_adapter(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"))
+            peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
+
+    def _drain_backward(self) -> None:
+        while self._bwd_gen is not None:
+            self._advance_backward(idle=True)
+        self._flush_actions()
+        if self._bwd_done_evt is not None:
+            self._bwd_done_evt.synchronize()
+            self._finish_backward()
+
+    def synchronize(self) -> None:
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        self._drain_timing(block=True)
+
+    # ------------------------------------------------------------------ profiling
+    def profile_execution_model(self, shapes=None, repeats: int | None = None,
+                                max_shapes: int | None = None) -> None:
+        """Launch profiling: drive synthetic shapes through real steps, fit the
+        estimator (reference: ``deltaserve-plugin/deltaserve/engine_core.py:242-423``).
+        A failure here switches the engine to inference-only (finetuning disabled)."""
+        from .profiling import ProfilingShapeGenerator
+        repeats = self.ftcfg.profile_num_repeats if repeats is None else repeats
+        try:
+            if os.environ.get("DSERVE_TEST_FAIL_PROFILING") == "1":
+                raise RuntimeError("DSERVE_TEST_FAIL_PROFILING=1")
+            gen = ProfilingShapeGenerator(self.ecfg.max_num_batched_tokens,
+                                          self.ftcfg.max_saved_finetuning_tokens,
+                                          min(self.ecfg.max_model_len, 4096),
+                                          self.store.min_len() if self.store else None)
+            warm, rec = gen.prepare(with_ft=self.ft_enabled)
+            if shapes is not None:
+                rec = shapes
+            if max_shapes is not None:
+                rec = rec[:max_shapes]
+            self.profiling = True
+            for sh in warm:
+                self._profile_shape(sh, record=False)
+            for _ in range(max(1, repeats)):
+                for sh in rec:
+                    self._profile_shape(sh, record=True)
+            self.synchronize()
+            self.estimator.data_fit(self.tracker)
+        except Exception as e:  # profiling failure must not take serving down
+            dprint(f"[profile] failed ({e!r}); finetuning disabled, serving continues")
+            self.coord.disable(f"profiling failed: {e!r}")
+        finally:
+            self.profiling = False
+            self._forced_ft = None
+
+    def _profile_shape(self, sh, record: bool) -> None:
+        rng = np.random.default_rng(len(self.tracker.durations) + 17)
+        V = self.arch.vocab
+        mk = lambda n: rng.integers(0, V, size=int(n)).tolist()
+        n0 = len(self.tracker.durations)
+        ids = []
+        for i, n in enumerate(sh.inf_lens):
+            rid = f"__prof__{self.step_no}_{i}"
+            self.add_request(rid, mk(n), SamplingParams(max_tokens=1 + sh.n_decode + (1 if sh.mix_lens else 0)))
+            ids.append(rid)
+        ft = [Request(f"__proft__{self.step_no}_{j}", mk(n), SamplingParams(max_tokens=1),
+                      FT_ADAPTER_NAME, time.perf_counter(), is_ft=True)
+              for j, n in enumerate(sh.ft_lens)] if (self.ft_enabled and sh.ft_lens) else []
+        if sh.kind in ("coserve", "ft_only"):
+            self._forced_ft = ft
+            ft = []
+        steps = 0
+        while self.has_unfinished() and steps < 64:
+            if sh.kind == "decode" and ft and all(not r.in_prefill for r in self.scheduler.running):
+                self._forced_ft, ft = ft, []
+            if sh.kind == "mixed" and sh.mix_lens and all(not r.in_prefill for r in self.scheduler.running):
+                for i, n in enumerate(sh.mix_lens):
+                    self.add_request(f"__profm__{self.step_no}_{i}", mk(n), SamplingParams(max_tokens=1))
+                sh = type(sh)(sh.kind, sh.inf_lens, sh.ft_lens, [], sh.n_decode)
+            self.step()
+            steps += 1
+        if self._forced_ft:
+            self._forced_ft_step()
+        self.synchronize()
+        if not record:
+            del self.tracker.features[n0:], self.tracker.durations[n0:], self.tracker.predicted[n0:]
+            del self.tracker.was_graph[n0:], self.tracker.timestamps[n0:]
+        self.finished = [r for r in self.finished if not r.request_id.startswith("__prof")]
+
+    def _forced_ft_step(self) -> None:
+        out = SchedulerOutput()
+        self.scheduler.add_ft(out, self._forced_ft)
+        self._forced_ft = None
+        if not out.is_empty():
+            self._run(out, 0, False, record_capture=False)
+
+    # ------------------------------------------------------------------ TP replay
+    @property
+    def tp_size(self) -> int:
+        return self.comm.size if self.comm is not None else 1
+
+    def _record(self, action) -> None:
+        if self.tp_size > 1 and self.is_driver:
+            self._actions.append(action)
+
+    def _flush_actions(self) -> None:
+        if self.tp_size > 1 and self.is_driver and self._actions:
+            self.comm.broadcast_object(self._actions)
+            self._actions = []
+
+    def _plan_hook(self, has_ft: bool):
+        if self.tp_size == 1:
+            return None
+
+        def hook(meta, pk):
+            arr, spans = pk.freeze()
+            self._actions.append(("fwd", arr, spans, meta, has_ft))
+            self._flush_actions()
+        return hook
+
+    def _mark_local(self, name: str) -> None:
+        """Synchronise every stream of this GPU, then stamp wall time and a CUDA
+        event (used to time a region on the device on every rank)."""
+        if not hasattr(self, "marks"):
+            self.marks = {}
+            self._mark_events = {}
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(self.fwd_stream)
+            torch.cuda.synchronize(self.device)
+            self._mark_events[name] = ev
+        self.marks[name] = {"wall": time.perf_counter()}
+
+    def mark(self, name: str) -> None:
+        """All ranks stamp ``name`` at the same point of the step stream."""
+        self._record(("mark", name))
+        self._flush_actions()
+        self._mark_local(name)
+
+    def region_ms(self, a: str, b: str) -> tuple[float, float]:
+        """(device ms, wall ms) between two marks on this rank."""
+        wall = (self.marks[b]["wall"] - self.marks[a]["wall"]) * 1e3
+        if self.cuda:
+            return self._mark_events[a].elapsed_time(self._mark_events[b]), wall
+        return wall, wall
+
+    def gather_region(self, a: str, b: str) -> list[tuple[float, float]]:
+        """Every rank's (device ms, wall ms) for a region (driver only)."""
+        mine = self.region_ms(a, b)
+        if self.tp_size == 1:
+            return [mine]
+        self._record(("gather", a, b))
+        self._flush_actions()
+        self.marks["__region__"] = mine
+        res = self.comm.gather_objects(self.marks)
+        return [mine] + [r["__region__"] for r in res[1:]]
+
+    def shutdown(self) -> None:
+        """Stop the follower ranks (driver) after finishing queued work."""
+        if self.tp_size > 1 and self.is_driver:
+            self._actions.append(("stop",))
+            self._flush_actions()
+
+    def follow(self) -> None:
+        """Follower-rank loop: replay rank 0's actions until it stops."""
+        assert not self.is_driver
+        while True:
+            actions = self.comm.broadcast_object(None)
+            for a in actions:
+                kind = a[0]
+                if kind == "stop":
+                    self._drain_backward_follower()
+                    return
+                if kind == "mark":
+                    self._mark_local(a[1])
+                    continue
+                if kind == "gather":
+                    self.marks["__region__"] = self.region_ms(a[1], a[2])
+                    self.comm.gather_objects(self.marks)
+                    continue
+                if kind == "fwd":
+                    _, arr, spans, meta, has_ft = a
+                    from .model_runner import _Packer
+                    b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
+                    if self.cuda:
+                        with torch.cuda.stream(self.fwd_stream):
+                            if has_ft and self._publish_evt is not None:
+                                self.fwd_stream.wait_event(self._publish_evt)
+                            ev = torch.cuda.Event()
+                            self.model.forward(b, self.capture if has_ft else None)
+                            ev.record()
+                        self._last_fwd_evt = ev
+                    else:
+                        self.model.forward(b, self.capture if has_ft else None)
+                elif kind == "bwd_start":
+                    m = a[1]
+                    if self.cuda:
+                        self.bwd_stream.wait_stream(self.fwd_stream)
+                    self._bwd_gen = self.trainer.cycle(self.capture, m["n"], m["starts"], m["lens"],
+                                                       m["epoch"], sync=False)
+                elif kind == "bwd_next":
+                    try:
+                        if self.cuda:
+                            with torch.cuda.stream(self.bwd_stream):
+                                next(self._bwd_gen)
+                        else:
+                            next(self._bwd_gen)
+                    except StopIteration as e:
+                        self._bwd_gen = None
+                        if self.cuda:
+                            ev = torch.cuda.Event()
+                            ev.record(self.bwd_stream)
+                            self._publish_evt = ev
+                        self.trainer.losses.append(0.0)
+
+    def _drain_backward_follower(self) -> None:
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+
+    # ------------------------------------------------------------------ helpers
+    def has_ft_work(self) -> bool:
+        c = self.coord
+        if not self.ft_enabled or c.disabled:
+            return False
+        if self._bwd_gen is not None or self._bwd_done_evt is not None or c.pending_backward:
+            return True
+        return c.ft_started and (c.fill_count > 0 or (self.store is not None and not self.store.finished()))
+
+    def run_until_idle(self, max_steps: int = 100000, finetune: bool = True) -> None:
+        for _ in range(max_steps):
+            if not self.has_unfinished() and not (finetune and self.has_ft_work()):
+                break
+            self.step()
+        self._drain_backward()

@@ -25,6 +25,21 @@ class _Packer:
     def add(self, name: str, arr) -> None:
         self.parts.append((name, np.ascontiguousarray(np.asarray(arr, dtype=np.int64).ravel())))
 
+    def freeze(self) -> tuple[np.ndarray, list[tuple[str, int]]]:
+        """One contiguous int64 array + (name, length) spans (what rank 0 sends
+        to the other tensor-parallel ranks)."""
+        arr = np.concatenate([a for _, a in self.parts]) if self.parts else np.zeros(0, np.int64)
+        return arr, [(n, a.size) for n, a in self.parts]
+
+    @classmethod
+    def thaw(cls, arr: np.ndarray, spans: list[tuple[str, int]]) -> "_Packer":
+        pk = cls()
+        off = 0
+        for n, k in spans:
+            pk.parts.append((n, arr[off:off + k]))
+            off += k
+        return pk
+
     def ship(self, device, pinned: torch.Tensor | None):
         total = sum(a.size for _, a in self.parts)
         if device.type == "cuda":
@@ -56,7 +71,7 @@ class ModelRunner:
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
 
-    def prepare(self, out: SchedulerOutput, ft_dst: int = 0) -> tuple[ForwardBatch, list]:
+    def build_host(self, out: SchedulerOutput, ft_dst: int = 0) -> tuple[dict, _Packer, list]:
         bs = self.block_size
         ids, pos, slots, lslot = [], [], [], []
         sample_rows, sample_reqs = [], []
@@ -120,43 +135,66 @@ class ModelRunner:
                 mask[t] = m if m < (1 << 31) else m - (1 << 32)
             pk.add("tile_slots", mask)
         pk.add("logits_idx", sample_rows)
+        meta = {"nd": nd, "maxb": maxb, "splits": splits, "kps": kps, "npf": len(pf),
+                "use_lora": use_lora, "T": T, "ft_rows": sum(s.num_new for s in out.ft),
+                "ft_dst": ft_dst}
+        return meta, pk, sample_reqs
+
+    def prepare(self, out: SchedulerOutput, ft_dst: int = 0) -> tuple[ForwardBatch, list]:
+        meta, pk, reqs = self.build_host(out, ft_dst)
+        return self.batch_from(meta, pk), reqs
+
+    def batch_from(self, meta: dict, pk: _Packer) -> ForwardBatch:
+        """Device batch from host metadata (also used by the follower ranks)."""
         d, self._pinned, nbytes = pk.ship(self.device, self._pinned)
         self.last_h2d_bytes = nbytes
         i32 = lambda t: t.to(torch.int32)
-        ft_rows = sum(s.num_new for s in out.ft)
+        nd, maxb, npf, use_lora = meta["nd"], meta["maxb"], meta["npf"], meta["use_lora"]
+        splits, kps, T, ft_rows, ft_dst = meta["splits"], meta["kps"], meta["T"], meta["ft_rows"], meta["ft_dst"]
+        pf = npf
         b = ForwardBatch(
             input_ids=d["ids"], positions=d["pos"], slot_mapping=d["slot_mapping"],
             num_decode=nd,
             dec_block_tables=i32(d["dec_btab"]).view(nd, maxb) if nd else None,
             dec_ctx_lens=i32(d["dec_ctx"]) if nd else None,
             dec_splits=splits, dec_keys_per_split=kps,
-            num_prefill_seqs=len(pf),
+            num_prefill_seqs=pf,
             pf_cu_q=i32(d["pf_cu"]) if pf else None,
             pf_ctx_lens=i32(d["pf_ctx"]) if pf else None,
-            pf_block_tables=i32(d["pf_btab"]).view(len(pf), maxb) if pf else None,
+            pf_block_tables=i32(d["pf_btab"]).view(pf, maxb) if pf else None,
             pf_tile_info=i32(d["pf_tiles"]).view(-1, 2) if pf else None,
             slot_ids=i32(d["lslot"]) if use_lora else None,
             tile_slots=i32(d["tile_slots"]) if use_lora else None,
             logits_idx=d["logits_idx"],
             ft_lo=T - ft_rows, ft_hi=T, ft_dst=ft_dst)
-        return b, sample_reqs
+        return b
 
     def execute(self, out: SchedulerOutput, cap: CaptureBuffers | None = None, ft_dst: int = 0,
-                temps=None, seeds=None):
-        """Forward + sampling. Returns ({seq_no: token}, logits)."""
+                on_host_plan=None):
+        """Forward + sampling. Returns ({seq_no: token}, logits). ``on_host_plan``
+        (rank 0 under TP) receives the host metadata before the forward is
+        enqueued, so the other ranks can replay the same step."""
         if out.is_empty():
             return {}, None
-        b, reqs = self.prepare(out, ft_dst)
+        meta, pk, reqs = self.build_host(out, ft_dst)
+        if on_host_plan is not None:
+            on_host_plan(meta, pk)
+        b = self.batch_from(meta, pk)
         logits = self.model.forward(b, cap if out.ft else None)
+        return self.sample(logits, reqs), logits
+
+    def sample(self, logits, reqs) -> dict:
         if not reqs:
-            return {}, logits
+            self.last_d2h_bytes = 0
+            return {}
         R = len(reqs)
         t = torch.tensor([r.params.temperature for r in reqs], dtype=torch.float32)
         sd = torch.tensor([(r.params.seed if r.params.seed is not None else r.seq_no) * 1000003
                            + len(r.output_ids) for r in reqs], dtype=torch.int64)
         toks = torch.empty(R, dtype=torch.int64, device=logits.device)
-        ops.sample(logits, t.to(logits.device), sd.to(logits.device), toks)
+        ops.sample(logits, t.to(logits.device, non_blocking=True), sd.to(logits.device, non_blocking=True),
+                   toks)
         host = toks.cpu()
         self.last_h2d_bytes += R * 12
         self.last_d2h_bytes = R * 8
-        return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}, logits
+        return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}

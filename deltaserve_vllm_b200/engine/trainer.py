@@ -129,9 +129,16 @@ class LoraTrainer:
                             self.arch.rope_scaling)
         return CycleInputs(n, n_pad, list(starts), list(lens), labels, c, s)
 
-    def cycle(self, cap: CaptureBuffers, n: int, starts, lens, epoch: int | None = None):
+    def n_valid(self, lens) -> int:
+        """Rows that carry a label (host-side, no device sync)."""
+        return sum(max(0, ln - 1 - min(self.mask_prefix, max(0, ln - 1))) for ln in lens)
+
+    def cycle(self, cap: CaptureBuffers, n: int, starts, lens, epoch: int | None = None,
+              sync: bool = True):
         """Generator: yields at each pause boundary; its return value (via
-        StopIteration.value) is a :class:`CycleResult`."""
+        StopIteration.value) is a pending :class:`CycleResult` — with
+        ``sync=False`` the loss and GPU time are resolved later by
+        :meth:`finish_cycle`, so the host never waits on the backward."""
         t_wall = time.perf_counter()
         dev = self.masters.params.device
         ev0 = ev1 = None
@@ -142,7 +149,8 @@ class LoraTrainer:
         ci = self._cycle_inputs(cap, n, starts, lens)
         m = self.masters
         m.grads.zero_()
-        loss, n_valid, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels)
+        n_valid = self.n_valid(lens)
+        loss_sum, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels, n_valid)
         yield "head"
         L = self.arch.num_layers
         cs = self.cos_sin
@@ -161,16 +169,29 @@ class LoraTrainer:
         self.publish()
         if ev1 is not None:
             ev1.record()
+        res = CycleResult(0.0, n, n_valid, 0.0, 0.0, self.step)
+        res._pending = (loss_sum, ev0, ev1, t_wall)
+        return self.finish_cycle(res) if sync else res
+
+    def finish_cycle(self, res: CycleResult) -> CycleResult:
+        """Resolve a cycle's loss and GPU time (waits for its end event)."""
+        pend = getattr(res, "_pending", None)
+        if pend is None:
+            return res
+        loss_sum, ev0, ev1, t_wall = pend
+        if ev1 is not None:
             ev1.synchronize()
-            gpu_ms = ev0.elapsed_time(ev1)
+            res.gpu_ms = ev0.elapsed_time(ev1)
         else:
-            gpu_ms = (time.perf_counter() - t_wall) * 1e3
-        self.total_tokens += n
-        self.losses.append(loss)
-        if not math.isfinite(loss):
+            res.gpu_ms = (time.perf_counter() - t_wall) * 1e3
+        res.wall_ms = (time.perf_counter() - t_wall) * 1e3
+        res.loss = float(loss_sum) / max(1, res.n_valid) if res.n_valid else 0.0
+        res._pending = None
+        self.total_tokens += res.n_tokens
+        self.losses.append(res.loss)
+        if not math.isfinite(res.loss):
             dprint(f"[trainer] WARNING: non-finite loss at step {self.step}; training continues")
-        return CycleResult(loss, n, n_valid, gpu_ms, (time.perf_counter() - t_wall) * 1e3,
-                           self.step)
+        return res
 
     def run_cycle(self, cap, n, starts, lens, epoch=None) -> CycleResult:
         g = self.cycle(cap, n, starts, lens, epoch)

@@ -275,15 +275,18 @@ class LoraBackward:
             gBt[:, rows] = gBfT[p * R:(p + 1) * R][:, rows]
 
     # ------------------------------------------------------------ head
-    def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor) -> tuple[float, int, torch.Tensor]:
-        """Final RMSNorm + LM head + CE. Returns (mean loss, n_valid, d final_in fp32)."""
+    def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor,
+                      n_valid: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Final RMSNorm + LM head + CE. Returns (summed loss as a 0-d device
+        tensor, d final_in fp32); the loss is the sum over the ``n_valid``
+        labelled rows and the gradient is already divided by ``n_valid``."""
         w = self.w
         eps = self.arch.rms_eps
         head = w.lm_head_full if w.lm_head_full is not None else w.lm_head
-        n_valid = int((labels >= 0).sum())
         h = rmsnorm_fwd(final_in, w.final_norm, eps)
         if n_valid == 0:
-            return 0.0, 0, torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device)
+            return (torch.zeros((), device=final_in.device),
+                    torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device))
         logits = torch.empty(h.shape[0], head.shape[0], dtype=torch.float32, device=h.device)
         ops.gemm(_bf(h, self.cdt).contiguous(), _bf(head, self.cdt), logits, epi=EPI_F32)
         loss = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
@@ -293,7 +296,7 @@ class LoraBackward:
         dh = self._mm(dlog, head, b_mn=True)                # [n, D]
         del dlog
         d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
-        return float(loss.sum().item()) / n_valid, n_valid, d_final
+        return loss.sum(), d_final
 
     # ------------------------------------------------------------ layer
     def recompute_qkv(self, qkv_raw: torch.Tensor, positions: torch.Tensor, lw, cos_sin):

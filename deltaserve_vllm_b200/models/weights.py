@@ -64,6 +64,19 @@ class ModelWeights:
     layers: list[LayerWeights] = field(default_factory=list)
     lm_head_full: torch.Tensor | None = None  # [V, D], for the finetuning head
 
+    def to(self, device, dtype) -> "ModelWeights":
+        """Copy of every tensor on ``device`` in ``dtype`` (tied heads stay tied)."""
+        cv = lambda t: None if t is None else t.to(device=device, dtype=dtype).contiguous()
+        embed = cv(self.embed)
+        lm_head = embed if self.lm_head.data_ptr() == self.embed.data_ptr() else cv(self.lm_head)
+        out = ModelWeights(self.arch, self.tp, embed, lm_head, cv(self.final_norm),
+                           lm_head_full=cv(self.lm_head_full))
+        for L in self.layers:
+            out.layers.append(LayerWeights(*(cv(getattr(L, f)) for f in
+                                             ("qkv", "o", "gate_up", "down", "in_ln", "post_ln",
+                                              "q_norm", "k_norm"))))
+        return out
+
     @property
     def q_local(self) -> int:
         return self.arch.q_size // self.tp.size

@@ -31,11 +31,15 @@ def native_available() -> bool:
     return _EXT is not None
 
 
-def _native():
+LAUNCHES = [0]  # kernels of this package launched so far (bench accounting)
+
+
+def _native(kernels: int = 1):
     if _EXT is None:
         raise RuntimeError(
             "deltaserve_vllm_b200 CUDA extension is not built or failed to load "
             f"({_C_ERR!r}); run `python setup.py build_ext --inplace`")
+    LAUNCHES[0] += kernels
     return _EXT
 
 
@@ -126,7 +130,7 @@ def decode_splits(batch: int, num_kv_heads: int, max_ctx: int, num_sms: int = 14
 def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale,
                  part_o=None, part_ml=None, splits=1, keys_per_split=0):
     if q.is_cuda:
-        _native().paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, part_o, part_ml,
+        _native(2).paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, part_o, part_ml,
                                num_heads, scale, splits, keys_per_split)
         return out
     return ref.paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale)
@@ -157,7 +161,7 @@ def ce_fwd_bwd(logits, targets, loss, grad=None, gscale=1.0):
 
 def seg_sumsq(g, seg_len, out):
     if g.is_cuda:
-        _native().seg_sumsq(g, seg_len, out)
+        _native(2).seg_sumsq(g, seg_len, out)
         return out
     ref.seg_sumsq(g, seg_len, out)
     return out
@@ -166,7 +170,7 @@ def seg_sumsq(g, seg_len, out):
 def adamw(p, g, m, v, *, seg_len, seg_sumsq_t=None, max_norm=0.0, grad_scale=1.0, lr=1e-4,
           b1=0.9, b2=0.999, eps=1e-8, wd=0.0, step=1):
     if p.is_cuda:
-        _native().adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd,
+        _native(1).adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd,
                         step)
         return
     ref.adamw(p, g, m, v, seg_len, seg_sumsq_t, max_norm, grad_scale, lr, b1, b2, eps, wd, step)

@@ -1,0 +1,69 @@
+"""End-to-end co-serving on CPU (fp32 oracle ops): inference requests and
+finetuning samples share steps, backward cycles run, the adapter is published
+and saved, and FT rows never produce outputs."""
+import os
+import tempfile
+
+import torch
+
+from deltaserve_vllm_b200.config import EngineConfig, FinetuneConfig
+from deltaserve_vllm_b200.engine.ft.store import FinetuningStore
+from deltaserve_vllm_b200.engine.llm_engine import CoServingEngine, FT_ADAPTER_NAME
+from deltaserve_vllm_b200.engine.request import SamplingParams
+from deltaserve_vllm_b200.adapters import peft_io
+
+
+def make_engine(tmp, **ft):
+    ecfg = EngineConfig(model="qwen3-tiny", device="cpu", max_model_len=512, block_size=16,
+                        max_num_batched_tokens=256, max_loras=3, max_lora_rank=8)
+    fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=96,
+                          learning_rate=1e-3, adapter_save_path=os.path.join(tmp, "ckpt"),
+                          bwd_log_path=os.path.join(tmp, "bwd.csv"), **ft)
+    store = FinetuningStore.synthetic(1024, 12, 16, 40, seed=0, max_saved_finetuning_tokens=96,
+                                      total_epochs=2)
+    eng = CoServingEngine(ecfg, fcfg, ft_store=store)
+    eng.load_inference_adapter("toy", rank=8, alpha=16)
+    return eng
+
+
+def test_coserving_cpu_end_to_end():
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        g = torch.Generator().manual_seed(0)
+        for i in range(6):
+            eng.add_request(f"r{i}", torch.randint(0, 1024, (20 + 7 * i,), generator=g).tolist(),
+                            SamplingParams(max_tokens=5), adapter="toy" if i % 2 else None)
+        eng.run_until_idle(max_steps=2000)
+        st = eng.finetuning_status()
+        assert st["completed_cycles"] >= 2, st
+        assert all(l == l for l in eng.trainer.losses)  # finite
+        assert len(eng.finished) == 6 and all(len(r.output_ids) == 5 for r in eng.finished)
+        assert not any(r.is_ft for r in eng.finished)
+        assert eng.store.finished()
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+        path = eng.save_adapter(save_id="x1")
+        tensors, cfg = peft_io.read_adapter(path)
+        assert len(tensors) == 2 * 7 * eng.arch.num_layers
+        assert os.path.exists(os.path.join(tmp, "bwd.csv"))
+
+
+def test_launch_profiling_fits_estimator_cpu():
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        eng.profile_execution_model(repeats=1)
+        assert eng.estimator.is_ready
+        assert not eng.coord.disabled
+        assert not eng.has_unfinished()
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+        assert eng.stats["ft_tokens_forwarded"] == 0
+
+
+def test_profiling_failure_disables_finetuning(monkeypatch):
+    monkeypatch.setenv("DSERVE_TEST_FAIL_PROFILING", "1")
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        eng.profile_execution_model(repeats=1)
+        assert eng.coord.disabled and "profiling" in eng.coord.disabled_reason
+        eng.add_request("x", list(range(10)), SamplingParams(max_tokens=2))
+        eng.run_until_idle(max_steps=100)
+        assert len(eng.finished) == 1 and eng.stats["ft_tokens_forwarded"] == 0
