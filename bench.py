@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--profile-repeats", type=int, default=1)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--run-ahead", type=int, default=6, help="backward layers queued ahead of the GPU")
+    p.add_argument("--phase", default="both", choices=["prefill", "both"],
+                   help="coserving_admission_phase (both: FT may ride decode-only steps too)")
     return p.parse_args()
 
 
@@ -171,7 +174,8 @@ def main():
     fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
                           num_epochs=1000, ttft_slo=args.ttft_slo, max_tbt_slo=args.tbt_slo,
                           avg_tbt_slo=args.tbt_slo, admission_margin="relative", admission_margin_k=1.5,
-                          pause_on_arrival=True, backward_run_ahead_boundaries=2,
+                          pause_on_arrival=True, backward_run_ahead_boundaries=args.run_ahead,
+                          coserving_admission_phase=args.phase,
                           profile_num_repeats=args.profile_repeats)
     store = FinetuningStore.synthetic(arch.vocab, 512, args.ft_seq, args.ft_seq, seed=args.seed + 7,
                                       max_saved_finetuning_tokens=cap, total_epochs=1000)
@@ -254,7 +258,8 @@ def main():
                    "prompts": "lognormal(median 512, sigma 0.8) clip 32..4096",
                    "outputs": "uniform 32..256", "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
                    "l2": "inputs larger than L2 (16 GB of weights stream every step)",
-                   "tp_comm": args.tp_comm},
+                   "tp_comm": args.tp_comm, "admission_phase": args.phase,
+                   "run_ahead_layers": args.run_ahead},
         "slo_attainment": attain, "p99_ttft_ms": (percentile(ttfts, 99) or 0) * 1e3 if ttfts else None,
         "p99_tbt_ms": (percentile(tbts, 99) or 0) * 1e3 if tbts else None,
         "p50_ttft_ms": (percentile(ttfts, 50) or 0) * 1e3 if ttfts else None,

@@ -27,6 +27,8 @@ Step (rank 0):
 from __future__ import annotations
 
 import math
+import sys
+import threading
 import os
 import time
 from collections import deque
@@ -118,6 +120,7 @@ class CoServingEngine:
             from ..parallel.comm import TPComm
             self.bwd_comm = TPComm(dist.new_group(list(range(comm.size))), comm.cpu_group)
         self._actions: list = []
+        self._actions_lock = threading.Lock()
         self.estimator = MergedExecutionEstimator()
         self.estimator.set_margin(self.ftcfg.admission_margin, self.ftcfg.admission_margin_k)
         set_ft_mixed_split(self.ftcfg.graph_ft_batches)
@@ -141,6 +144,10 @@ class CoServingEngine:
             self.bwd_stream = torch.cuda.Stream(self.device, priority=0)
         else:
             self.fwd_stream = self.bwd_stream = None
+        # Backward layers are CUDA-graph replays enqueued inline by this thread
+        # (a background feeder thread loses the GIL to the serving loop after
+        # every PyTorch call, so the work stays on the engine thread).
+        self.feeder = None
         self._bwd_gen = None
         self._bwd_events: deque = deque()
         self._bwd_done_evt = None
@@ -340,7 +347,7 @@ class CoServingEngine:
             if self.coord.try_flush():
                 self._start_backward()
         out = self.scheduler.schedule()
-        bwd_busy = self._bwd_gen is not None or self._bwd_done_evt is not None
+        bwd_busy = self.bwd_active or self._bwd_done_evt is not None
         adm = None
         ft_dst = 0
         if self.profiling and getattr(self, "_forced_ft", None):
@@ -385,6 +392,12 @@ class CoServingEngine:
         pred = self.estimator.predict(feats) if self.estimator.is_ready else None
         # Pause: a step carrying inference prefill stops feeding the backward.
         has_inf_prefill = bool(out.prefill)
+        pause_now = has_inf_prefill and (self.ftcfg.pause_on_arrival or self.ftcfg.pause_until_prefill_done
+                                         or self.ftcfg.pause_prefill_always)
+        # Queue backward layers while the forward runs (before the host blocks
+        # on the sampled tokens); the low-priority stream fills GPU gaps.
+        feed = (lambda: self._advance_backward(idle=False, paused=pause_now)) \
+            if (self.cuda and not self.profiling) else None
         uses_ft_slot = bool(out.ft) or any(s.req.lora_slot == self.ft_slot for s in out.seqs
                                            if self.ft_slot >= 0)
         if self.cuda:
@@ -394,11 +407,13 @@ class CoServingEngine:
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
-                toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)))
+                toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
+                                              before_sample=feed)
                 ev1.record()
         else:
             ev0 = time.perf_counter()
-            toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)))
+            toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
+                                          before_sample=feed)
             ev1 = time.perf_counter()
         self.stats["h2d_bytes"] += self.runner.last_h2d_bytes
         self.stats["d2h_bytes"] += self.runner.last_d2h_bytes
@@ -440,15 +455,29 @@ class CoServingEngine:
                 self.bwd_stream.wait_event(capture_evt)
             else:
                 self.bwd_stream.wait_stream(self.fwd_stream)
-        self._bwd_gen = self.trainer.cycle(self.capture, n, self._bwd_meta["starts"], lens,
-                                           self._bwd_meta["epoch"], sync=False)
+        gen = self.trainer.cycle(self.capture, n, self._bwd_meta["starts"], lens,
+                                 self._bwd_meta["epoch"], sync=False)
         self._bwd_events.clear()
         self._record(("bwd_start", dict(self._bwd_meta)))
+        if self.feeder is not None:
+            self.feeder.start_cycle(gen)
+        else:
+            self._bwd_gen = gen
+
+    @property
+    def bwd_active(self) -> bool:
+        return self._bwd_gen is not None or (self.feeder is not None and self.feeder.busy)
 
     def _advance_backward(self, idle: bool, paused: bool = False) -> None:
-        """Enqueue backward layers: all remaining when the engine is idle,
-        otherwise a bounded number per step, never more than
-        ``backward_run_ahead_boundaries`` layers ahead of the GPU."""
+        """Let the backward progress. With the feeder thread (CUDA) this only
+        sets the pause flag; otherwise enqueue layers here: all remaining when
+        the engine is idle, else at most ``backward_run_ahead_boundaries``."""
+        if self.feeder is not None:
+            if self.feeder.error is not None:
+                err, self.feeder.error = self.feeder.error, None
+                self.coord.disable(f"backward failed: {err!r}")
+            self.feeder.set_paused(paused and not idle)
+            return
         if self._bwd_gen is None or (paused and not idle):
             return
         ahead = max(1, self.ftcfg.backward_run_ahead_boundaries)
@@ -514,6 +543,8 @@ class CoServingEngine:
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
 
     def _drain_backward(self) -> None:
+        if self.feeder is not None:
+            self.feeder.wait_idle()
         while self._bwd_gen is not None:
             self._advance_backward(idle=True)
         self._flush_actions()
@@ -554,6 +585,18 @@ class CoServingEngine:
                     self._profile_shape(sh, record=True)
             self.synchronize()
             self.estimator.data_fit(self.tracker)
+            if self.ft_enabled and self.trainer is not None:
+                # One full backward cycle on this thread at the buffer's size:
+                # loads every backward kernel before the feeder thread runs.
+                cap = self.ftcfg.max_saved_finetuning_tokens
+                ln = max(8, min(cap, self.store.min_len() or cap))
+                k = max(1, cap // ln)
+                self._record(("bwd_warmup", k * ln, [i * ln for i in range(k)], [ln] * k))
+                self._flush_actions()
+                self.bwd_warmup_ms = self._bwd_call(self.trainer.warmup, self.capture, k * ln,
+                                                         [i * ln for i in range(k)], [ln] * k)
+                dprint(f"[profile] backward warm-up cycle ({k * ln} tokens): "
+                       f"{self.bwd_warmup_ms:.1f} ms")
         except Exception as e:  # profiling failure must not take serving down
             dprint(f"[profile] failed ({e!r}); finetuning disabled, serving continues")
             self.coord.disable(f"profiling failed: {e!r}")
@@ -595,6 +638,15 @@ class CoServingEngine:
             del self.tracker.was_graph[n0:], self.tracker.timestamps[n0:]
         self.finished = [r for r in self.finished if not r.request_id.startswith("__prof")]
 
+    def _bwd_call(self, fn, *args):
+        """Run ``fn`` with the backward stream current (CUDA graphs are captured
+        on it; capture is not allowed on the legacy default stream)."""
+        if not self.cuda:
+            return fn(*args)
+        self.bwd_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.bwd_stream):
+            return fn(*args)
+
     def _forced_ft_step(self) -> None:
         out = SchedulerOutput()
         self.scheduler.add_ft(out, self._forced_ft)
@@ -609,12 +661,15 @@ class CoServingEngine:
 
     def _record(self, action) -> None:
         if self.tp_size > 1 and self.is_driver:
-            self._actions.append(action)
+            with self._actions_lock:
+                self._actions.append(action)
 
     def _flush_actions(self) -> None:
-        if self.tp_size > 1 and self.is_driver and self._actions:
-            self.comm.broadcast_object(self._actions)
-            self._actions = []
+        if self.tp_size > 1 and self.is_driver:
+            with self._actions_lock:
+                acts, self._actions = self._actions, []
+            if acts:
+                self.comm.broadcast_object(acts)
 
     def _plan_hook(self, has_ft: bool):
         if self.tp_size == 1:
@@ -622,7 +677,7 @@ class CoServingEngine:
 
         def hook(meta, pk):
             arr, spans = pk.freeze()
-            self._actions.append(("fwd", arr, spans, meta, has_ft))
+            self._record(("fwd", arr, spans, meta, has_ft))
             self._flush_actions()
         return hook
 
@@ -667,7 +722,7 @@ class CoServingEngine:
     def shutdown(self) -> None:
         """Stop the follower ranks (driver) after finishing queued work."""
         if self.tp_size > 1 and self.is_driver:
-            self._actions.append(("stop",))
+            self._record(("stop",))
             self._flush_actions()
 
     def follow(self) -> None:
@@ -682,6 +737,9 @@ class CoServingEngine:
                     return
                 if kind == "mark":
                     self._mark_local(a[1])
+                    continue
+                if kind == "bwd_warmup":
+                    self._bwd_call(self.trainer.warmup, self.capture, a[1], a[2], a[3])
                     continue
                 if kind == "gather":
                     self.marks["__region__"] = self.region_ms(a[1], a[2])
@@ -731,7 +789,7 @@ class CoServingEngine:
         c = self.coord
         if not self.ft_enabled or c.disabled:
             return False
-        if self._bwd_gen is not None or self._bwd_done_evt is not None or c.pending_backward:
+        if self.bwd_active or self._bwd_done_evt is not None or c.pending_backward:
             return True
         return c.ft_started and (c.fill_count > 0 or (self.store is not None and not self.store.finished()))
 
@@ -741,3 +799,5 @@ class CoServingEngine:
                 break
             self.step()
         self._drain_backward()
+
+

@@ -170,7 +170,7 @@ class ModelRunner:
         return b
 
     def execute(self, out: SchedulerOutput, cap: CaptureBuffers | None = None, ft_dst: int = 0,
-                on_host_plan=None):
+                on_host_plan=None, before_sample=None):
         """Forward + sampling. Returns ({seq_no: token}, logits). ``on_host_plan``
         (rank 0 under TP) receives the host metadata before the forward is
         enqueued, so the other ranks can replay the same step."""
@@ -181,6 +181,8 @@ class ModelRunner:
             on_host_plan(meta, pk)
         b = self.batch_from(meta, pk)
         logits = self.model.forward(b, cap if out.ft else None)
+        if before_sample is not None:
+            before_sample()
         return self.sample(logits, reqs), logits
 
     def sample(self, logits, reqs) -> dict:

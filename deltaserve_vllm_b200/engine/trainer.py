@@ -77,6 +77,13 @@ class LoraTrainer:
         self.total_tokens = 0
         self.losses: list[float] = []
         L = self.arch.num_layers
+        # Captured per-layer backward graphs, keyed by the batch shape.
+        self.use_graphs = dev.type == "cuda"
+        self.max_graph_shapes = 4
+        self._graphs: dict = {}
+        self._groups_cache: dict = {}
+        self._pool = None
+        self._cap_stream = None
         self._sq_rep = torch.zeros(L, dtype=torch.float32, device=dev)
         self._sq_shard = torch.zeros(L, dtype=torch.float32, device=dev)
 
@@ -119,7 +126,7 @@ class LoraTrainer:
         if n_pad > cap.layer_in.shape[1]:
             raise ValueError("capture buffer too small for the padded cycle")
         if n_pad > n:  # padded rows must be zero (they carry no sample)
-            for t in (cap.layer_in, cap.qkv, cap.ctx, cap.resid_mid, cap.gate_up):
+            for t in (cap.layer_in, cap.qkv, cap.ctx, cap.resid_mid, cap.gate_up, cap.act):
                 t[:, n:n_pad].zero_()
             cap.final_in[n:n_pad].zero_()
             cap.ids[n:n_pad].zero_()
@@ -129,16 +136,93 @@ class LoraTrainer:
                             self.arch.rope_scaling)
         return CycleInputs(n, n_pad, list(starts), list(lens), labels, c, s)
 
+    def _attn_groups(self, ci: CycleInputs):
+        key = (ci.n_pad, tuple(ci.starts), tuple(ci.lens))
+        g = self._groups_cache.get(key)
+        if g is None:
+            from ..models.lora_backward import attention_groups
+            g = attention_groups(ci.starts, ci.lens, self.masters.params.device)
+            if len(self._groups_cache) > 64:
+                self._groups_cache.clear()
+            self._groups_cache[key] = g
+        return g
+
     def n_valid(self, lens) -> int:
         """Rows that carry a label (host-side, no device sync)."""
         return sum(max(0, ln - 1 - min(self.mask_prefix, max(0, ln - 1))) for ln in lens)
+
+    # ------------------------------------------------------------ CUDA graphs
+    def _layer_step(self, cap, ci, l, dh):
+        """Backward of layer ``l`` (+ the bucketed replicated-gradient
+        all-reduce at bucket boundaries). Returns the new residual gradient."""
+        L = self.arch.num_layers
+        m = self.masters
+        saved = {k: getattr(cap, k)[l, :ci.n_pad] for k in
+                 ("layer_in", "qkv", "ctx", "resid_mid", "gate_up", "act")}
+        dh = self.bwd.layer_backward(l, dh, saved, ci, cap.positions[:ci.n_pad], self.cos_sin)
+        if self.comm is not None and self.comm.size > 1 and (l % BUCKET_LAYERS == 0):
+            # Layers [l, l + BUCKET_LAYERS) are done: one all-reduce of their
+            # replicated factor gradients.
+            self.comm.all_reduce(m.rep_block(m.grads, l, min(L, l + BUCKET_LAYERS)))
+        return dh
+
+    def _graph_set(self, cap, ci, n_valid):
+        """Per-batch-shape CUDA graphs: one for the head, one per layer, all in
+        one memory pool (replayed in capture order, never concurrently). The
+        residual gradient lives in a static buffer that every graph reads and
+        overwrites. Captured on the first cycle of a shape (the kernels were
+        already loaded by :meth:`warmup`)."""
+        key = (ci.n_pad, tuple(ci.lens))
+        gs = self._graphs.get(key)
+        if gs is not None:
+            return gs
+        if not self.use_graphs or len(self._graphs) >= self.max_graph_shapes:
+            return None
+        dev = self.masters.params.device
+        gs = {"labels": torch.empty(ci.n_pad, dtype=torch.long, device=dev),
+              "cos": torch.empty_like(ci.cos), "sin": torch.empty_like(ci.sin),
+              "dh": torch.empty(ci.n_pad, self.arch.hidden, dtype=torch.float32, device=dev),
+              "loss": torch.zeros((), dtype=torch.float32, device=dev), "n_valid": n_valid}
+        gs["labels"].copy_(ci.labels)
+        gs["cos"].copy_(ci.cos)
+        gs["sin"].copy_(ci.sin)
+        sci = CycleInputs(ci.n, ci.n_pad, ci.starts, ci.lens, gs["labels"], gs["cos"], gs["sin"],
+                          ci.attn_groups)
+        gs["ci"] = sci
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        stream = torch.cuda.current_stream(dev)
+        if stream == torch.cuda.default_stream(dev):
+            # Capture is not allowed on the legacy default stream; capture on a
+            # side stream (replay works on any stream).
+            if self._cap_stream is None:
+                self._cap_stream = torch.cuda.Stream(dev)
+            self._cap_stream.wait_stream(stream)
+            stream = self._cap_stream
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._pool, stream=stream):
+            loss, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], sci.labels, n_valid)
+            gs["loss"].copy_(loss)
+            gs["dh"].copy_(dh)
+        gs["head"] = g
+        gs["layers"] = {}
+        for l in range(self.arch.num_layers - 1, -1, -1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self._pool, stream=stream):
+                dh = self._layer_step(cap, sci, l, gs["dh"])
+                gs["dh"].copy_(dh)
+            gs["layers"][l] = g
+        self._graphs[key] = gs
+        return gs
 
     def cycle(self, cap: CaptureBuffers, n: int, starts, lens, epoch: int | None = None,
               sync: bool = True):
         """Generator: yields at each pause boundary; its return value (via
         StopIteration.value) is a pending :class:`CycleResult` — with
         ``sync=False`` the loss and GPU time are resolved later by
-        :meth:`finish_cycle`, so the host never waits on the backward."""
+        :meth:`finish_cycle`, so the host never waits on the backward.
+        On CUDA every step replays a captured graph (a few microseconds of
+        host time per layer)."""
         t_wall = time.perf_counter()
         dev = self.masters.params.device
         ev0 = ev1 = None
@@ -147,30 +231,35 @@ class LoraTrainer:
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record()
         ci = self._cycle_inputs(cap, n, starts, lens)
+        if dev.type == "cuda":
+            ci.attn_groups = self._attn_groups(ci)
         m = self.masters
         m.grads.zero_()
         n_valid = self.n_valid(lens)
-        loss_sum, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels, n_valid)
-        yield "head"
         L = self.arch.num_layers
-        cs = self.cos_sin
-        pos = cap.positions[:ci.n_pad]
-        pending = []
-        for l in range(L - 1, -1, -1):
-            saved = {k: getattr(cap, k)[l, :ci.n_pad] for k in
-                     ("layer_in", "qkv", "ctx", "resid_mid", "gate_up")}
-            dh = self.bwd.layer_backward(l, dh, saved, ci, pos, cs)
-            if self.comm is not None and self.comm.size > 1 and (l % BUCKET_LAYERS == 0):
-                # Layers [l, l + BUCKET_LAYERS) are done: one all-reduce of their
-                # replicated factor gradients.
-                self.comm.all_reduce(m.rep_block(m.grads, l, min(L, l + BUCKET_LAYERS)))
-            yield l
+        gs = self._graph_set(cap, ci, n_valid) if dev.type == "cuda" else None
+        if gs is not None:
+            gs["labels"].copy_(ci.labels)
+            gs["cos"].copy_(ci.cos)
+            gs["sin"].copy_(ci.sin)
+            gs["head"].replay()
+            loss_sum = gs["loss"]
+            yield "head"
+            for l in range(L - 1, -1, -1):
+                gs["layers"][l].replay()
+                yield l
+        else:
+            loss_sum, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels, n_valid)
+            yield "head"
+            for l in range(L - 1, -1, -1):
+                dh = self._layer_step(cap, ci, l, dh)
+                yield l
         self._optimizer_step(epoch)
         self.publish()
         if ev1 is not None:
             ev1.record()
         res = CycleResult(0.0, n, n_valid, 0.0, 0.0, self.step)
-        res._pending = (loss_sum, ev0, ev1, t_wall)
+        res._pending = (loss_sum.clone(), ev0, ev1, t_wall)
         return self.finish_cycle(res) if sync else res
 
     def finish_cycle(self, res: CycleResult) -> CycleResult:
@@ -192,6 +281,31 @@ class LoraTrainer:
         if not math.isfinite(res.loss):
             dprint(f"[trainer] WARNING: non-finite loss at step {self.step}; training continues")
         return res
+
+    @torch.no_grad()
+    def warmup(self, cap: CaptureBuffers, n: int, starts, lens) -> float:
+        """Run one full cycle on the calling thread and restore every piece of
+        optimizer and adapter state afterwards. Loads every kernel module the
+        backward uses before the background feeder thread ever launches one,
+        and measures the cycle. Returns its GPU milliseconds."""
+        m = self.masters
+        snap = [t.clone() for t in (m.params, m.exp_avg, m.exp_avg_sq)]
+        step, epoch, tokens, losses = self.step, self.epoch, self.total_tokens, list(self.losses)
+        # Eager first (loads kernels, creates library handles), then once more
+        # through the CUDA-graph path, which captures this shape's graphs.
+        use = self.use_graphs
+        self.use_graphs = False
+        res = self.run_cycle(cap, n, starts, lens)
+        self.use_graphs = use
+        if use:
+            res = self.run_cycle(cap, n, starts, lens)
+        for t, s in zip((m.params, m.exp_avg, m.exp_avg_sq), snap):
+            t.copy_(s)
+        self.step, self.epoch, self.total_tokens, self.losses = step, epoch, tokens, losses
+        self.publish()
+        if m.params.is_cuda:
+            torch.cuda.synchronize(m.params.device)
+        return res.gpu_ms
 
     def run_cycle(self, cap, n, starts, lens, epoch=None) -> CycleResult:
         g = self.cycle(cap, n, starts, lens, epoch)

@@ -68,6 +68,7 @@ class CaptureBuffers:
     ctx: torch.Tensor        # [L, cap, q_l]
     resid_mid: torch.Tensor  # [L, cap, D]
     gate_up: torch.Tensor    # [L, cap, 2*I_l]
+    act: torch.Tensor        # [L, cap, I_l]  silu(gate) * up (the down projection's input)
     final_in: torch.Tensor   # [cap, D]
     ids: torch.Tensor        # [cap] int64
     positions: torch.Tensor  # [cap] int64
@@ -80,13 +81,15 @@ class CaptureBuffers:
         z = lambda *s: torch.zeros(*s, dtype=dtype, device=device)
         return CaptureBuffers(
             layer_in=z(L, cap, D), qkv=z(L, cap, qkv_l), ctx=z(L, cap, w.q_local),
-            resid_mid=z(L, cap, D), gate_up=z(L, cap, 2 * w.i_local), final_in=z(cap, D),
+            resid_mid=z(L, cap, D), gate_up=z(L, cap, 2 * w.i_local), act=z(L, cap, w.i_local),
+            final_in=z(cap, D),
             ids=torch.zeros(cap, dtype=torch.long, device=device),
             positions=torch.zeros(cap, dtype=torch.long, device=device))
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in
-                   (self.layer_in, self.qkv, self.ctx, self.resid_mid, self.gate_up, self.final_in))
+                   (self.layer_in, self.qkv, self.ctx, self.resid_mid, self.gate_up, self.act,
+                    self.final_in))
 
 
 class Communicator:
@@ -198,6 +201,8 @@ class DecoderModel:
             self._proj(x, lw.gate_up, act, l, "gate_up", b, epi=EPI_SWIGLU,
                        save=cap.gate_up[l] if cap_on else None, save_lo=lo, save_hi=hi,
                        save_dst=dst)
+            if cap_on:
+                cap.act[l, dst:dst + hi - lo] = act[lo:hi]
             self._proj(act, lw.down, mlp, l, "down", b)
             self.comm.all_reduce(mlp)
         ops.rms_norm(mlp, w.final_norm, x, eps, residual=residual,

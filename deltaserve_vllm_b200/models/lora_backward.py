@@ -156,6 +156,22 @@ class CycleInputs:
     labels: torch.Tensor          # [n_pad] int64, -1 = no loss
     cos: torch.Tensor             # [n_pad, hd/2] fp32
     sin: torch.Tensor
+    # Equal-length sample groups for the batched attention backward:
+    # (length, row index tensor [B*length]); built once per batch shape so the
+    # backward can be captured in a CUDA graph.
+    attn_groups: list | None = None
+
+
+def attention_groups(starts, lens, device) -> list:
+    groups: dict[int, list[int]] = {}
+    for st, ln in zip(starts, lens):
+        groups.setdefault(int(ln), []).append(int(st))
+    out = []
+    for ln, sts in groups.items():
+        idx = (torch.tensor(sts, device=device)[:, None]
+               + torch.arange(ln, device=device)[None, :]).reshape(-1)
+        out.append((ln, len(sts), idx))
+    return out
 
 
 def make_labels(ids: torch.Tensor, starts, lens, n_pad: int, mask_prefix: int = 0) -> torch.Tensor:
@@ -186,30 +202,39 @@ def rmsnorm_bwd(x, dy, w, eps):
     return (g - xhat * dot / xf.shape[-1]) * inv
 
 
-def attn_backward(qh, kh, vh, d_ctx, starts, lens, scale):
-    """Causal GQA attention backward per sample, fp32. Inputs [n, H, hd]."""
+def attn_backward(qh, kh, vh, d_ctx, starts, lens, scale, groups=None):
+    """Causal GQA attention backward, fp32 scores/softmax. Inputs [n, H, hd].
+
+    Samples of equal length are processed as one batch (one set of batched
+    matmuls); on CUDA the fp32 matmuls run on TF32 tensor cores, which is exact
+    for the bf16-valued q/k/v/dO operands (8 of TF32's 10 mantissa bits)."""
     n, Hq, hd = qh.shape
     Hkv = kh.shape[1]
     G = Hq // Hkv
     dq = torch.zeros(n, Hq, hd, dtype=torch.float32, device=qh.device)
     dk = torch.zeros(n, Hkv, hd, dtype=torch.float32, device=qh.device)
     dv = torch.zeros_like(dk)
-    for st, ln in zip(starts, lens):
-        q = qh[st:st + ln].float().transpose(0, 1)                       # [Hq, l, hd]
-        k = kh[st:st + ln].float().transpose(0, 1).repeat_interleave(G, 0)
-        v = vh[st:st + ln].float().transpose(0, 1).repeat_interleave(G, 0)
-        do = d_ctx[st:st + ln].float().transpose(0, 1)
-        s = (q @ k.transpose(1, 2)) * scale
+    if groups is None:
+        groups = attention_groups(starts, lens, qh.device)
+    for ln, B, idx in groups:
+        def take(t, H):
+            return t.index_select(0, idx).view(B, ln, H, hd).transpose(1, 2).float()  # [B, H, l, hd]
+        q = take(qh, Hq)
+        k = take(kh, Hkv).repeat_interleave(G, 1)
+        v = take(vh, Hkv).repeat_interleave(G, 1)
+        do = take(d_ctx, Hq)
+        s = torch.matmul(q, k.transpose(-1, -2)) * scale
         mask = torch.triu(torch.ones(ln, ln, dtype=torch.bool, device=qh.device), 1)
-        p = s.masked_fill(mask, float("-inf")).softmax(-1)
-        dvv = p.transpose(1, 2) @ do
-        dp = do @ v.transpose(1, 2)
+        p = s.masked_fill_(mask, float("-inf")).softmax(-1)
+        dvv = torch.matmul(p.transpose(-1, -2), do)
+        dp = torch.matmul(do, v.transpose(-1, -2))
         ds = p * (dp - (dp * p).sum(-1, keepdim=True))
-        dqq = (ds @ k) * scale
-        dkk = (ds.transpose(1, 2) @ q) * scale
-        dq[st:st + ln] = dqq.transpose(0, 1)
-        dk[st:st + ln] = dkk.view(Hkv, G, ln, hd).sum(1).transpose(0, 1)
-        dv[st:st + ln] = dvv.view(Hkv, G, ln, hd).sum(1).transpose(0, 1)
+        dqq = torch.matmul(ds, k) * scale
+        dkk = torch.matmul(ds.transpose(-1, -2), q) * scale
+        put = lambda t, H: t.transpose(1, 2).reshape(B * ln, H, hd)
+        dq.index_copy_(0, idx, put(dqq, Hq))
+        dk.index_copy_(0, idx, put(dkk.view(B, Hkv, G, ln, hd).sum(2), Hkv))
+        dv.index_copy_(0, idx, put(dvv.view(B, Hkv, G, ln, hd).sum(2), Hkv))
     return dq, dk, dv
 
 
@@ -232,7 +257,14 @@ class LoraBackward:
         self.hkv = self.arch.num_kv_heads // weights.tp.size
         self.hd = self.arch.head_dim
         self.scale = 1.0 / math.sqrt(self.hd)
-        self._bfull_idx = {}
+        self._rows: dict[tuple[str, int], torch.Tensor] = {}
+        if weights.embed.is_cuda:
+            # fp32 attention-backward matmuls on TF32 tensor cores (exact for
+            # the bf16-valued operands; fp32 accumulation).
+            torch.backends.cuda.matmul.allow_tf32 = True
+        # Backward GEMMs launch one CTA per tile so the inference stream can
+        # interleave between tiles (the backward runs at low priority).
+        self.max_ctas = 1 << 30
 
     # ------------------------------------------------------------ GEMM helpers
     def _mm(self, a, b, b_mn, epi=EPI_F32, out=None):
@@ -241,8 +273,16 @@ class LoraBackward:
         if out is None:
             n = b.shape[1] if b_mn else b.shape[0]
             out = torch.empty(a.shape[0], n, dtype=torch.float32, device=a.device)
-        ops.gemm(a, b, out, b_mn=b_mn, epi=epi)
+        ops.gemm(a, b, out, b_mn=b_mn, epi=epi, max_ctas=self.max_ctas)
         return out
+
+    def rows(self, g: str, p: int, device) -> torch.Tensor:
+        key = (g, p)
+        t = self._rows.get(key)
+        if t is None or t.device != torch.device(device):
+            t = self.geom[g].proj_rows(p).to(device)
+            self._rows[key] = t
+        return t
 
     def _bfull(self, layer, g):
         """[N, P*R] scattered, scaled expand factor (compute dtype)."""
@@ -251,9 +291,25 @@ class LoraBackward:
         Bt = self.m.p(layer, g, "Bt")
         full = torch.zeros(gg.N, gg.P * R, dtype=torch.float32, device=Bt.device)
         for p in range(gg.P):
-            rows = gg.proj_rows(p).to(Bt.device)
-            full[rows, p * R:(p + 1) * R] = Bt[:, rows].t() * self.s
+            # Strided views of the projection's rows/columns: no index tensors.
+            if gg.interleave:
+                full.view(gg.N // 128, 2, 64, gg.P * R)[:, p, :, p * R:(p + 1) * R] = \
+                    (self._cols3(Bt, gg, p) * self.s).permute(1, 2, 0)
+            else:
+                b0, b1 = self._bounds(gg, p)
+                full[b0:b1, p * R:(p + 1) * R] = Bt[:, b0:b1].t() * self.s
         return _bf(full, self.cdt)
+
+    @staticmethod
+    def _bounds(gg: GroupGeom, p: int) -> tuple[int, int]:
+        b = [0, gg.b1, gg.b2, gg.N] if gg.P == 3 else [0, gg.N]
+        return b[p], b[p + 1]
+
+    @staticmethod
+    def _cols3(t: torch.Tensor, gg: GroupGeom, p: int) -> torch.Tensor:
+        """Columns of projection ``p`` (64-interleaved layout) of an [R, N]
+        tensor as a writable view [R, N/128, 64]."""
+        return t.view(t.shape[0], gg.N // 128, 2, 64)[:, :, p]
 
     def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
                        dX: torch.Tensor) -> None:
@@ -271,8 +327,12 @@ class LoraBackward:
         gBfT = self._mm(Z.t(), dY, b_mn=True) * self.s       # [PR, N]
         gBt = self.m.g(layer, g, "Bt")
         for p in range(gg.P):
-            rows = gg.proj_rows(p).to(gBt.device)
-            gBt[:, rows] = gBfT[p * R:(p + 1) * R][:, rows]
+            src = gBfT[p * R:(p + 1) * R]
+            if gg.interleave:
+                self._cols3(gBt, gg, p).copy_(self._cols3(src, gg, p))
+            else:
+                b0, b1 = self._bounds(gg, p)
+                gBt[:, b0:b1].copy_(src[:, b0:b1])
 
     # ------------------------------------------------------------ head
     def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor,
@@ -312,50 +372,57 @@ class LoraBackward:
     def layer_backward(self, layer: int, dh: torch.Tensor, saved: dict, ci: CycleInputs,
                        positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
         """dh: fp32 [n, D] gradient w.r.t. the layer output. Returns the gradient
-        w.r.t. the layer input (fp32), grads of this layer's factors written."""
+        w.r.t. the layer input (fp32); this layer's factor gradients are written."""
         w = self.w
         lw = w.layers[layer]
         eps = self.arch.rms_eps
         x, qkv_raw, ctx = saved["layer_in"], saved["qkv"], saved["ctx"]
-        resid_mid, gate_up = saved["resid_mid"], saved["gate_up"]
-        n = x.shape[0]
+        resid_mid, gate_up, act = saved["resid_mid"], saved["gate_up"], saved.get("act")
+        n, D = x.shape
+        dev = x.device
+        cdt = self.cdt
         # ---- MLP -------------------------------------------------------
-        x2 = rmsnorm_fwd(resid_mid, lw.post_ln, eps)
-        g, u = deinterleave64(gate_up.float())
-        sg = torch.sigmoid(g)
-        silu_g = g * sg
-        act = _bf(silu_g * u, x.dtype)
-        dh_c = _bf(dh, self.cdt)
-        d_act = self._mm(dh_c, lw.down, b_mn=True)                  # [n, I_l]
+        dh_c = _bf(dh, cdt)
+        d_act = self._mm(dh_c, lw.down, b_mn=True)                  # [n, I_l] fp32
+        if act is None:
+            g, u = deinterleave64(gate_up.float())
+            act = _bf(F.silu(g) * u, x.dtype)
         self.group_backward(layer, "down", act, dh_c, d_act)
-        d_u = d_act * silu_g
-        d_g = d_act * u * sg * (1 + g * (1 - sg))
-        d_gu = _bf(interleave64(d_g, d_u), self.cdt)
+        d_gu = torch.empty(n, gate_up.shape[1], dtype=cdt, device=dev)
+        ops.swiglu_bwd(gate_up, d_act, d_gu)
+        x2 = torch.empty(n, D, dtype=x.dtype, device=dev)
+        ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
         d_x2 = self._mm(d_gu, lw.gate_up, b_mn=True)                # [n, D]
         self.group_backward(layer, "gate_up", x2, d_gu, d_x2)
         if self.comm is not None:
             self.comm.all_reduce(d_x2)
-        d_mid = rmsnorm_bwd(resid_mid, d_x2, lw.post_ln, eps) + dh
+        d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
+        d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
         # ---- attention ---------------------------------------------------
-        d_mid_c = _bf(d_mid, self.cdt)
         d_ctx = self._mm(d_mid_c, lw.o, b_mn=True)                  # [n, q_l]
         self.group_backward(layer, "o", ctx, d_mid_c, d_ctx)
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
         dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
-                                   self.scale)
-        cos, sin = ci.cos, ci.sin
-        dq = rope_backward(dq, cos, sin)
-        dk = rope_backward(dk, cos, sin)
+                                   self.scale, ci.attn_groups)
+        dq = rope_backward(dq, ci.cos, ci.sin)
+        dk = rope_backward(dk, ci.cos, ci.sin)
+        ql, kl = self.hq * self.hd, self.hkv * self.hd
+        d_qkv = torch.empty(n, ql + 2 * kl, dtype=cdt, device=dev)
         if self.arch.qk_norm:
-            ql = self.hq * self.hd
-            q_pre = qkv_raw[:, :ql].view(n, self.hq, self.hd)
-            k_pre = qkv_raw[:, ql:ql + self.hkv * self.hd].view(n, self.hkv, self.hd)
-            dq = rmsnorm_bwd(q_pre, dq, lw.q_norm, eps)
-            dk = rmsnorm_bwd(k_pre, dk, lw.k_norm, eps)
-        d_qkv = _bf(torch.cat([dq.reshape(n, -1), dk.reshape(n, -1), dv.reshape(n, -1)], 1), self.cdt)
-        x1 = rmsnorm_fwd(x, lw.in_ln, eps)
+            q_pre = qkv_raw[:, :ql].reshape(n * self.hq, self.hd)
+            k_pre = qkv_raw[:, ql:ql + kl].reshape(n * self.hkv, self.hd)
+            dqn = ops.rms_norm_bwd(q_pre, dq.reshape(n * self.hq, self.hd), lw.q_norm, eps)
+            dkn = ops.rms_norm_bwd(k_pre, dk.reshape(n * self.hkv, self.hd), lw.k_norm, eps)
+            d_qkv[:, :ql] = dqn.view(n, ql)
+            d_qkv[:, ql:ql + kl] = dkn.view(n, kl)
+        else:
+            d_qkv[:, :ql] = dq.reshape(n, ql)
+            d_qkv[:, ql:ql + kl] = dk.reshape(n, kl)
+        d_qkv[:, ql + kl:] = dv.reshape(n, kl)
+        x1 = torch.empty(n, D, dtype=x.dtype, device=dev)
+        ops.rms_norm(x, lw.in_ln, x1, eps)
         d_x1 = self._mm(d_qkv, lw.qkv, b_mn=True)                   # [n, D]
         self.group_backward(layer, "qkv", x1, d_qkv, d_x1)
         if self.comm is not None:
             self.comm.all_reduce(d_x1)
-        return rmsnorm_bwd(x, d_x1, lw.in_ln, eps) + d_mid
+        return ops.rms_norm_bwd(x, d_x1, lw.in_ln, eps, add=d_mid)

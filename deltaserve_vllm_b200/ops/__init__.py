@@ -53,14 +53,15 @@ def check_device_error(clear: bool = True) -> int:
 # ----------------------------------------------------------------- GEMM
 
 def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None,
-         lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0):
+         lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0, max_ctas=0):
     """``out = a @ b.T`` (``b`` is [N, K]) or ``a @ b`` (``b_mn``: ``b`` is [K, N]),
     plus the segmented LoRA expand ``z @ b2.T`` and the epilogue ``epi``:
     bf16 / fp32 store, fp32 accumulate, or SwiGLU over 64-interleaved
-    gate/up columns. ``save`` receives raw accumulator rows [save_lo, save_hi)."""
+    gate/up columns. ``save`` receives raw accumulator rows [save_lo, save_hi).
+    ``max_ctas`` > number of SMs launches one CTA per tile (non-persistent)."""
     if a.is_cuda:
         _native().gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save,
-                       save_lo, save_hi, save_dst, force_bn)
+                       save_lo, save_hi, save_dst, force_bn, max_ctas)
         return out
     return ref.gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi,
                     save_dst)
@@ -181,6 +182,27 @@ def lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale):
         _native().lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale)
         return
     ref.lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale)
+
+
+def rms_norm_bwd(x, dy, w, eps, *, add=None, out=None, out_bf16=None):
+    """fp32 gradient of ``rmsnorm(x) * w`` w.r.t. ``x`` given fp32 ``dy``
+    (+ ``add``); optionally also written as bf16 into ``out_bf16``."""
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    if x.is_cuda:
+        _native().rms_norm_bwd(x, dy.contiguous(), w, add, out, out_bf16, eps)
+        return out
+    ref.rms_norm_bwd(x, dy, w, eps, add, out, out_bf16)
+    return out
+
+
+def swiglu_bwd(gu, dact, dgu, act=None):
+    """From saved interleaved gate/up (``gu``) and fp32 ``dact``: ``dgu`` (same
+    interleave) and, optionally, the activation ``silu(g) * u``."""
+    if gu.is_cuda:
+        _native().swiglu_bwd(gu, dact.contiguous(), dgu, act)
+        return
+    ref.swiglu_bwd(gu, dact, dgu, act)
 
 
 def sample(logits, temps, seeds, out):

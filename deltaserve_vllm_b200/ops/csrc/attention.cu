@@ -272,8 +272,11 @@ struct DecodeArgs {
 };
 
 __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) {
-  __shared__ __align__(16) __nv_bfloat16 sK[DC_KEYS * HD];
-  __shared__ __align__(16) __nv_bfloat16 sV[DC_KEYS * HD];
+  // K/V chunks double-buffered in dynamic smem: chunk i+1 streams in while
+  // chunk i is scored and accumulated.
+  extern __shared__ __align__(16) uint8_t dc_smem[];
+  __nv_bfloat16* sKb = reinterpret_cast<__nv_bfloat16*>(dc_smem);   // [2][64*128]
+  __nv_bfloat16* sVb = sKb + 2 * DC_KEYS * HD;                          // [2][64*128]
   __shared__ float sQ[DC_MAX_GROUP][HD];
   __shared__ float sS[DC_MAX_GROUP][DC_KEYS];
   __shared__ float sPart[2][DC_MAX_GROUP][DC_KEYS];
@@ -298,8 +301,7 @@ __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) 
     acc[gq] = 0.f;
   }
   __syncthreads();
-  for (int k0 = k_begin; k0 < k_end; k0 += DC_KEYS) {
-    // Stage K and V of up to 64 keys.
+  auto stage = [&](int k0, int buf) {
     for (int i = tid; i < DC_KEYS * 16; i += DC_THREADS) {
       int r = i / 16, c = i % 16;
       int kpos = k0 + r;
@@ -307,12 +309,23 @@ __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) 
       int kp = ok ? kpos : k_begin;
       int page = btab[kp / a.block_size];
       size_t off = (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
-      cp_async16(sK + r * HD + c * 8, a.k_cache + off, ok);
-      cp_async16(sV + r * HD + c * 8, a.v_cache + off, ok);
+      cp_async16(sKb + buf * DC_KEYS * HD + r * HD + c * 8, a.k_cache + off, ok);
+      cp_async16(sVb + buf * DC_KEYS * HD + r * HD + c * 8, a.v_cache + off, ok);
     }
     cp_async_commit();
-    cp_async_wait<0>();
+  };
+  if (k_begin < k_end) stage(k_begin, 0);
+  int buf = 0;
+  for (int k0 = k_begin; k0 < k_end; k0 += DC_KEYS, buf ^= 1) {
+    if (k0 + DC_KEYS < k_end) {
+      stage(k0 + DC_KEYS, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
+    const __nv_bfloat16* sK = sKb + buf * DC_KEYS * HD;
+    const __nv_bfloat16* sV = sVb + buf * DC_KEYS * HD;
     // Scores: thread = (key, half of the head dim).
     {
       const int key = tid % DC_KEYS, half = tid / DC_KEYS;
@@ -465,7 +478,13 @@ void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   a.keys_per_split = (int)keys_per_split;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  paged_decode_kernel<<<dim3(B, Hkv, (unsigned)splits), DC_THREADS, 0, s>>>(a);
+  const int dsmem = 4 * DC_KEYS * HD * 2;
+  static bool dattr = false;
+  if (!dattr) {
+    cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dsmem);
+    dattr = true;
+  }
+  paged_decode_kernel<<<dim3(B, Hkv, (unsigned)splits), DC_THREADS, dsmem, s>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   decode_combine_kernel<<<dim3(B, (unsigned)num_heads), HD, 0, s>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

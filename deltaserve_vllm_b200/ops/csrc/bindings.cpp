@@ -4,7 +4,10 @@
 void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
-              int64_t save_dst, int64_t force_bn);
+              int64_t save_dst, int64_t force_bn, int64_t max_ctas);
+void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> add,
+                      torch::Tensor dx, c10::optional<torch::Tensor> dx_bf, double eps);
+void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10::optional<torch::Tensor> act);
 int64_t dsv_read_error_gemm(bool clear);
 static int64_t dsv_read_error(bool clear) { return dsv_read_error_gemm(clear); }
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
@@ -45,4 +48,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &dsv_adamw, "flat AdamW with per-segment clipping");
   m.def("lora_publish", &dsv_lora_publish, "publish fp32 LoRA masters into a served slot");
   m.def("sample", &dsv_sample, "greedy / Gumbel-max sampling");
+  m.def("rms_norm_bwd", &dsv_rms_norm_bwd, "RMSNorm backward (+ residual add)");
+  m.def("swiglu_bwd", &dsv_swiglu_bwd, "SwiGLU backward over interleaved gate/up");
 }

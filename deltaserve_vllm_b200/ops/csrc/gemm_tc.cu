@@ -42,7 +42,31 @@ struct GemmArgs {
   int ldc;                // elements
   __nv_bfloat16* save;    // optional: raw accumulator rows [save_lo, save_hi) -> save[save_dst + r - save_lo]
   int ld_save, save_lo, save_hi, save_dst;
+  int max_ctas;           // host only: grid cap (0 = one CTA per SM, persistent)
+  int k_splits;           // > 1: split-K, fp32 partials to `partial`, reduced by a second kernel
+  float* partial;         // [k_splits, M, N]
 };
+
+// Work unit = (M tile, N tile, K split); M fastest, then N, then split.
+struct Tile {
+  int mt, nt, ks, kb_lo, n_main;
+  uint32_t slots;
+};
+
+__device__ __forceinline__ Tile decode_tile(int t, const GemmArgs& a, int m_tiles, int n_tiles, int kb_main) {
+  Tile r;
+  const int mn = m_tiles * n_tiles;
+  r.ks = t / mn;
+  const int rem = t - r.ks * mn;
+  r.mt = rem % m_tiles;
+  r.nt = rem / m_tiles;
+  const int per = (kb_main + a.k_splits - 1) / a.k_splits;
+  r.kb_lo = r.ks * per;
+  r.n_main = min(kb_main, r.kb_lo + per) - r.kb_lo;
+  // LoRA expand blocks ride with the last split only.
+  r.slots = (a.lora_seg > 0 && r.ks == a.k_splits - 1) ? a.tile_slots[r.mt] : 0u;
+  return r;
+}
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -103,7 +127,7 @@ __global__ void __launch_bounds__(256, 1)
   const int lane = threadIdx.x % 32;
   const int num_m_tiles = (args.M + BM - 1) / BM;
   const int num_n_tiles = (args.N + BN - 1) / BN;
-  const int num_tiles = num_m_tiles * num_n_tiles;
+  const int num_tiles = num_m_tiles * num_n_tiles * args.k_splits;
   const int kb_main = (args.K + BK - 1) / BK;
   const int kb_per_slot = args.lora_seg / BK;
 
@@ -139,17 +163,17 @@ __global__ void __launch_bounds__(256, 1)
     int fills[STAGES > 0 ? STAGES : 1];
     for (int s = 0; s < STAGES; ++s) fills[s] = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
-      const int m0 = mt * BM, n0 = nt * BN;
-      const uint32_t slots = (args.lora_seg > 0) ? args.tile_slots[mt] : 0u;
+      const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
+      const int m0 = tl.mt * BM, n0 = tl.nt * BN;
+      const uint32_t slots = tl.slots;
       const int n_lora = __popc(slots) * kb_per_slot;
-      for (int kb = 0; kb < kb_main + n_lora; ++kb) {
+      for (int j = 0; j < tl.n_main + n_lora; ++j) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
         uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
         uint8_t* sB = sA + Cfg::A_BYTES;
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-        if (kb < kb_main) {
-          const int k0 = kb * BK;
+        if (j < tl.n_main) {
+          const int k0 = (tl.kb_lo + j) * BK;
           tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
           if constexpr (B_MN) {
 #pragma unroll
@@ -159,7 +183,7 @@ __global__ void __launch_bounds__(256, 1)
           }
         } else {
           // LoRA expand block: the (lb / kb_per_slot)-th present slot.
-          int lb = kb - kb_main;
+          int lb = j - tl.n_main;
           int which = lb / kb_per_slot, sub = lb % kb_per_slot;
           uint32_t m = slots;
           for (int i = 0; i < which; ++i) m &= m - 1;
@@ -189,9 +213,8 @@ __global__ void __launch_bounds__(256, 1)
     int iter = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
-      const int mt = t % num_m_tiles;
-      const uint32_t slots = (args.lora_seg > 0) ? args.tile_slots[mt] : 0u;
-      const int n_kb = kb_main + __popc(slots) * kb_per_slot;
+      const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
+      const int n_kb = tl.n_main + __popc(tl.slots) * kb_per_slot;
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, kErrWaitAccEmpty)) { ok = false; break; }
@@ -202,7 +225,7 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
         const uint32_t b_addr = a_addr + Cfg::A_BYTES;
-        const bool lora_blk = kb >= kb_main;
+        const bool lora_blk = kb >= tl.n_main;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t da = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
@@ -232,8 +255,8 @@ __global__ void __launch_bounds__(256, 1)
     const int q = warp - 4;  // TMEM lane quarter
     int iter = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
-      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
-      const int m0 = mt * BM, n0 = nt * BN;
+      const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
+      const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       if (!mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull)) break;
@@ -242,7 +265,22 @@ __global__ void __launch_bounds__(256, 1)
       const bool row_ok = row < args.M;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const bool do_save = args.save != nullptr && row_ok && row >= args.save_lo && row < args.save_hi;
-      if constexpr (EPI == kEpiSwiGLU) {
+      if (args.k_splits > 1) {
+        // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          const int col = n0 + c;
+          if (row_ok && col < args.N)
+            store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + col, v,
+                          min(32, args.N - col), false);
+        }
+      } else if constexpr (EPI == kEpiSwiGLU) {
         // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
 #pragma unroll 1
         for (int c = 0; c < BN; c += 128) {
@@ -306,6 +344,46 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+}
+
+// Split-K epilogue: sum the fp32 partials of every split and apply the
+// epilogue (bf16 / fp32 / fp32-accumulate store, or SwiGLU over interleaved
+// gate/up pairs), plus the optional raw-accumulator row capture.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, int epi, void* C,
+                                     int ldc, __nv_bfloat16* save, int ld_save, int save_lo, int save_hi,
+                                     int save_dst) {
+  const size_t plane = (size_t)M * N;
+  if (epi == kEpiSwiGLU) {
+    const int half = N / 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)M * half;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int row = (int)(i / half), j = (int)(i % half);
+      const int cg = (j / 64) * 128 + (j % 64);
+      float g = 0.f, u = 0.f;
+      for (int s = 0; s < splits; ++s) {
+        g += partial[s * plane + (size_t)row * N + cg];
+        u += partial[s * plane + (size_t)row * N + cg + 64];
+      }
+      reinterpret_cast<__nv_bfloat16*>(C)[(size_t)row * ldc + j] = f2bf(g / (1.f + __expf(-g)) * u);
+      if (save != nullptr && row >= save_lo && row < save_hi) {
+        __nv_bfloat16* sv = save + (size_t)(row - save_lo + save_dst) * ld_save;
+        sv[cg] = f2bf(g);
+        sv[cg + 64] = f2bf(u);
+      }
+    }
+    return;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)plane;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / N), col = (int)(i % N);
+    float v = 0.f;
+    for (int s = 0; s < splits; ++s) v += partial[s * plane + i];
+    if (epi == kEpiBF16) reinterpret_cast<__nv_bfloat16*>(C)[(size_t)row * ldc + col] = f2bf(v);
+    else if (epi == kEpiF32) reinterpret_cast<float*>(C)[(size_t)row * ldc + col] = v;
+    else reinterpret_cast<float*>(C)[(size_t)row * ldc + col] += v;
+    if (save != nullptr && row >= save_lo && row < save_hi)
+      save[(size_t)(row - save_lo + save_dst) * ld_save + col] = f2bf(v);
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -393,7 +471,10 @@ static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap
     attr_set = true;
   }
   const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
-  const int grid = std::min(tiles, num_sms());
+  // Persistent (one CTA per SM) by default; a larger cap makes CTAs retire
+  // after one tile so a higher-priority stream can interleave at tile
+  // granularity (used for the low-priority backward).
+  const int grid = std::min(tiles, args.max_ctas > 0 ? args.max_ctas : num_sms());
   kern<<<grid, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -422,7 +503,7 @@ static int pick_bn(int M, int N, int epi, bool b_mn) {
 void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
-              int64_t save_dst, int64_t force_bn) {
+              int64_t save_dst, int64_t force_bn, int64_t max_ctas) {
   using namespace dsv;
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "dsv_gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm: bf16 operands");
@@ -440,12 +521,36 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   c10::cuda::CUDAGuard guard(a.device());
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
   if (b_mn && bn < 64) bn = 64;
+  if (epi == kEpiSwiGLU && bn < 128) bn = 128;
+  // Split-K for skinny problems (decode: one M tile) that would leave most SMs
+  // idle: each split streams a slice of K, fp32 partials are reduced after.
+  int splits = 1;
+  {
+    const int kbs = (K + BK - 1) / BK;
+    const int m_t = (M + BM - 1) / BM;
+    if (!b_mn && m_t == 1 && max_ctas == 0) {
+      if (force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
+      const int tiles = m_t * ((N + bn - 1) / bn);
+      if (tiles < num_sms() / 2 && kbs >= 8) {
+        splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
+        const int per = (kbs + splits - 1) / splits;
+        splits = (kbs + per - 1) / per;  // no empty split
+      }
+    }
+  }
   GemmArgs args{};
+  args.k_splits = splits;
+  at::Tensor partial;
+  if (splits > 1) {
+    partial = at::empty({splits, M, N}, a.options().dtype(at::kFloat));
+    args.partial = partial.data_ptr<float>();
+  }
   args.M = M;
   args.N = N;
   args.K = K;
   args.C = out.data_ptr();
   args.ldc = (int)out.stride(0);
+  args.max_ctas = (int)max_ctas;
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), BM);
   CUtensorMap tb = b_mn ? make_tmap_bf16(b.data_ptr(), K, N, b.stride(0), BK)
                         : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
@@ -482,10 +587,15 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     if (epi == kEpiBF16) dispatch_bn<false, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32) dispatch_bn<false, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32Accum) dispatch_bn<false, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
-    else if (epi == kEpiSwiGLU) {
-      if (bn == 64) bn = 128;
-      dispatch_bn<false, kEpiSwiGLU>(bn, ta, tb, tz, tb2, args, s);
-    }
+    else if (epi == kEpiSwiGLU) dispatch_bn<false, kEpiSwiGLU>(bn, ta, tb, tz, tb2, args, s);
+  }
+  if (splits > 1) {
+    const int64_t work = (epi == kEpiSwiGLU) ? (int64_t)M * (N / 2) : (int64_t)M * N;
+    const int blocks = (int)std::min<int64_t>(4096, (work + 255) / 256);
+    splitk_reduce_kernel<<<blocks, 256, 0, s>>>(args.partial, splits, M, N, (int)epi, out.data_ptr(), args.ldc,
+                                                args.save, args.ld_save, args.save_lo, args.save_hi,
+                                                args.save_dst);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
 

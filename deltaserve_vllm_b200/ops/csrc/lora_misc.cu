@@ -21,26 +21,32 @@ namespace dsv {
 constexpr int SHR_ROWS = 16;
 constexpr int SHR_KC = 1024;  // K chunk staged in smem
 constexpr int SHR_THREADS = 256;
+constexpr int SHR_OUT = SHR_THREADS / 32;  // outputs per CTA (one per warp)
 constexpr int SHR_MAXPR = 192;  // 3 projections x rank 64
 
-// CTA = 16 token rows. For every output column o of the group, a warp holds the
-// A row chunk of the current slot in registers and dots it with each staged x
-// row; rows are sorted by slot, so the A chunk is reloaded only at slot changes.
+// grid = (row tiles of 16, output groups of 8). A warp owns one output column
+// o of the group: it keeps the A row chunk of the current slot in registers and
+// dots it with each staged x row (rows are sorted by slot, so the A chunk is
+// reloaded only at slot changes). Output groups run on different CTAs, so a
+// decode step (one row tile) still spreads over P*R/8 CTAs. The y == 0 CTA
+// also writes the zero columns of every row (other slots and padding).
 __global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfloat16* __restrict__ x, int sx,
                                                                   const __nv_bfloat16* __restrict__ A,
                                                                   const int* __restrict__ slot_ids, __nv_bfloat16* Z,
                                                                   int sz, int T, int K, int PR, int SEG, int slots) {
   __shared__ __align__(16) __nv_bfloat16 xs[SHR_ROWS * SHR_KC];
-  __shared__ float acc[SHR_ROWS][SHR_MAXPR];
   __shared__ int rslot[SHR_ROWS];
   const int r0 = blockIdx.x * SHR_ROWS;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int i = threadIdx.x; i < SHR_ROWS * SHR_MAXPR; i += SHR_THREADS) acc[i / SHR_MAXPR][i % SHR_MAXPR] = 0.f;
+  const int o = blockIdx.y * SHR_OUT + warp;
   if (threadIdx.x < SHR_ROWS) {
     const int r = r0 + threadIdx.x;
     rslot[threadIdx.x] = (r < T) ? slot_ids[r] : -1;
   }
   __syncthreads();
+  float acc[SHR_ROWS];
+#pragma unroll
+  for (int r = 0; r < SHR_ROWS; ++r) acc[r] = 0.f;
   for (int k0 = 0; k0 < K; k0 += SHR_KC) {
     const int kc = min(SHR_KC, K - k0);
     for (int i = threadIdx.x; i < SHR_ROWS * (kc / 8); i += SHR_THREADS) {
@@ -50,9 +56,10 @@ __global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfl
       *reinterpret_cast<uint4*>(xs + r * SHR_KC + c) = v;
     }
     __syncthreads();
-    for (int o = warp; o < PR; o += SHR_THREADS / 32) {
+    if (o < PR) {
       int cur = -2;
       float av[SHR_KC / 32];
+#pragma unroll
       for (int r = 0; r < SHR_ROWS; ++r) {
         const int s = rslot[r];
         if (s < 0) continue;
@@ -62,16 +69,14 @@ __global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfl
           for (int j = 0; j < SHR_KC / 32; j += 8) {
             const int c = lane * 8 + j * 32;
             if (c < kc) {
-              float t[8];
-              float2 f;
+              uint4 raw = *reinterpret_cast<const uint4*>(ar + c);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-              for (int e = 0; e < 8; e += 2) {
-                f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ar + c + e));
-                t[e] = f.x;
-                t[e + 1] = f.y;
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                av[j + 2 * e] = f.x;
+                av[j + 2 * e + 1] = f.y;
               }
-#pragma unroll
-              for (int e = 0; e < 8; ++e) av[j + e] = t[e];
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) av[j + e] = 0.f;
@@ -84,29 +89,79 @@ __global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfl
         for (int j = 0; j < SHR_KC / 32; j += 8) {
           const int c = lane * 8 + j * 32;
           if (c < kc) {
+            uint4 raw = *reinterpret_cast<const uint4*>(xs + r * SHR_KC + c);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xs + r * SHR_KC + c + e));
-              d += f.x * av[j + e] + f.y * av[j + e + 1];
+            for (int e = 0; e < 4; ++e) {
+              float2 f = __bfloat1622float2(h[e]);
+              d += f.x * av[j + 2 * e] + f.y * av[j + 2 * e + 1];
             }
           }
         }
-        d = warp_sum(d);
-        if (lane == 0) acc[r][o] += d;
+        acc[r] += d;
       }
     }
     __syncthreads();
   }
-  // Write every column of the row: own slot's segment, zeros elsewhere.
-  const int W = slots * SEG;
-  for (int i = threadIdx.x; i < SHR_ROWS * W; i += SHR_THREADS) {
-    const int r = i / W, c = i % W;
-    if (r0 + r >= T) continue;
-    const int s = rslot[r];
-    float v = 0.f;
-    if (s >= 0 && c >= s * SEG && c < s * SEG + PR) v = acc[r][c - s * SEG];
-    Z[(size_t)(r0 + r) * sz + c] = f2bf(v);
+  if (o < PR) {
+#pragma unroll
+    for (int r = 0; r < SHR_ROWS; ++r) {
+      const int s = rslot[r];
+      if (s < 0) continue;
+      const float v = warp_sum(acc[r]);
+      if (lane == 0) Z[(size_t)(r0 + r) * sz + s * SEG + o] = f2bf(v);
+    }
   }
+  if (blockIdx.y == 0) {
+    const int W = slots * SEG;
+    for (int i = threadIdx.x; i < SHR_ROWS * W; i += SHR_THREADS) {
+      const int r = i / W, c = i % W;
+      if (r0 + r >= T) continue;
+      const int s = rslot[r];
+      if (s >= 0 && c >= s * SEG && c < s * SEG + PR) continue;
+      Z[(size_t)(r0 + r) * sz + c] = f2bf(0.f);
+    }
+  }
+}
+
+// Small-batch shrink (decode): one warp per (row, output column) pair does the
+// whole K-long dot product with 16-byte loads of the x row and the A row (both
+// L2-resident), so a 16-row step still spreads over T*P*R warps. The warp of
+// output 0 also writes the row's zero columns.
+__global__ void __launch_bounds__(256) lora_shrink_gemv_kernel(const __nv_bfloat16* __restrict__ x, int sx,
+                                                               const __nv_bfloat16* __restrict__ A,
+                                                               const int* __restrict__ slot_ids, __nv_bfloat16* Z,
+                                                               int sz, int T, int K, int PR, int SEG, int slots) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair = blockIdx.x * 8 + warp;
+  if (pair >= T * PR) return;
+  const int row = pair / PR, o = pair % PR;
+  const int s = slot_ids[row];
+  if (o == 0) {
+    const int W = slots * SEG;
+    for (int c = lane; c < W; c += 32) {
+      if (s >= 0 && c >= s * SEG && c < s * SEG + PR) continue;
+      Z[(size_t)row * sz + c] = f2bf(0.f);
+    }
+  }
+  if (s < 0) return;
+  const __nv_bfloat16* xr = x + (size_t)row * sx;
+  const __nv_bfloat16* ar = A + ((size_t)s * PR + o) * K;
+  float d = 0.f;
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+    const uint4 av = *reinterpret_cast<const uint4*>(ar + k);
+    const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
+    const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&av);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 xf = __bfloat1622float2(xh[e]);
+      const float2 af = __bfloat1622float2(ah[e]);
+      d += xf.x * af.x + xf.y * af.y;
+    }
+  }
+  d = warp_sum(d);
+  if (lane == 0) Z[(size_t)row * sz + s * SEG + o] = f2bf(d);
 }
 
 // Vocab-parallel embedding: ids outside [v0, v0 + Vl) give zero rows (the TP
@@ -295,7 +350,17 @@ void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, t
   TORCH_CHECK(A.size(2) == K && K % 8 == 0 && PR <= SHR_MAXPR && PR <= seg, "lora_shrink: shapes");
   TORCH_CHECK(Z.size(1) == slots * seg && Z.size(0) >= T, "lora_shrink: Z shape");
   c10::cuda::CUDAGuard guard(x.device());
-  lora_shrink_kernel<<<(T + SHR_ROWS - 1) / SHR_ROWS, SHR_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(
+  if (T * PR <= 64 * 192 && x.stride(0) % 8 == 0) {
+    const int blocks = (T * PR + 7) / 8;
+    lora_shrink_gemv_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),
+        reinterpret_cast<__nv_bfloat16*>(Z.data_ptr()), (int)Z.stride(0), T, K, PR, (int)seg, slots);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  dim3 grid((T + SHR_ROWS - 1) / SHR_ROWS, (PR + SHR_OUT - 1) / SHR_OUT);
+  lora_shrink_kernel<<<grid, SHR_THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),
       reinterpret_cast<__nv_bfloat16*>(Z.data_ptr()), (int)Z.stride(0), T, K, PR, (int)seg, slots);

@@ -214,3 +214,100 @@ void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::T
       (int)num_heads, (int)num_kv_heads, kc, vc, sm, bs, T);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ------------------------------------------------------------------ backward
+namespace dsv {
+
+// dx = rmsnorm_backward(x, dy) [+ add]; fp32 out, optional bf16 copy.
+// One CTA per row; x bf16, dy fp32 or bf16 (dy_bf16 != nullptr), w bf16.
+__global__ void rms_norm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int sx, const float* __restrict__ dy,
+                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ add,
+                                    float* dx, __nv_bfloat16* dx_bf, int D, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + (size_t)row * sx;
+  const float* dyr = dy + (size_t)row * D;
+  float ss = 0.f, dot = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float xv = bf2f(xr[i]);
+    ss += xv * xv;
+    dot += dyr[i] * bf2f(w[i]) * xv;
+  }
+  auto bsum = [&](float v) {
+    v = warp_sum(v);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+    __syncthreads();
+    float t = (threadIdx.x < blockDim.x / 32) ? red[threadIdx.x] : 0.f;
+    if (threadIdx.x < 32) t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+    __syncthreads();
+    float r = red[0];
+    __syncthreads();
+    return r;
+  };
+  ss = bsum(ss);
+  dot = bsum(dot);
+  const float inv = rsqrtf(ss / D + eps);
+  // d/dx of x*inv*w : inv * (g - xhat * mean(g * xhat)), g = dy*w, xhat = x*inv
+  const float c = dot * inv * inv / D;  // = mean(g*xhat) * inv / ... folded
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float xv = bf2f(xr[i]);
+    float v = inv * (dyr[i] * bf2f(w[i]) - xv * c);
+    if (add != nullptr) v += add[(size_t)row * D + i];
+    dx[(size_t)row * D + i] = v;
+    if (dx_bf != nullptr) dx_bf[(size_t)row * D + i] = f2bf(v);
+  }
+}
+
+// SwiGLU backward over 64-interleaved gate/up: from the saved pre-activation
+// gu (bf16) and d_act (fp32) produce d_gu (bf16, same interleave) and the
+// activation silu(g)*u (bf16, the down projection's input).
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, int sgu, const float* __restrict__ dact,
+                                  __nv_bfloat16* dgu, __nv_bfloat16* act, int I, int64_t total) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / I;
+    const int j = (int)(idx % I);
+    const int col_g = (j / 64) * 128 + (j % 64);
+    const float g = bf2f(gu[row * sgu + col_g]);
+    const float u = bf2f(gu[row * sgu + col_g + 64]);
+    const float sg = 1.f / (1.f + __expf(-g));
+    const float silu = g * sg;
+    const float da = dact[row * I + j];
+    dgu[row * (2 * (int64_t)I) + col_g] = f2bf(da * u * sg * (1.f + g * (1.f - sg)));
+    dgu[row * (2 * (int64_t)I) + col_g + 64] = f2bf(da * silu);
+    if (act != nullptr) act[row * I + j] = f2bf(silu * u);
+  }
+}
+
+}  // namespace dsv
+
+void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> add,
+                      torch::Tensor dx, c10::optional<torch::Tensor> dx_bf, double eps) {
+  const int T = (int)x.size(0), D = (int)x.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(dy.scalar_type() == at::kFloat && dx.scalar_type() == at::kFloat && dy.is_contiguous() &&
+                  dx.is_contiguous(), "rms_norm_bwd: fp32 contiguous dy/dx");
+  c10::cuda::CUDAGuard guard(x.device());
+  dsv::rms_norm_bwd_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0), dy.data_ptr<float>(),
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), add.has_value() ? add->data_ptr<float>() : nullptr,
+      dx.data_ptr<float>(), dx_bf.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf->data_ptr()) : nullptr, D,
+      (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10::optional<torch::Tensor> act) {
+  const int64_t T = gu.size(0);
+  const int I = (int)dact.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(I % 64 == 0 && gu.size(1) == 2 * I && dact.is_contiguous() && dgu.is_contiguous(), "swiglu_bwd");
+  c10::cuda::CUDAGuard guard(gu.device());
+  const int64_t total = T * I;
+  const int blocks = (int)std::min<int64_t>(8192, (total + 255) / 256);
+  dsv::swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), (int)gu.stride(0), dact.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()),
+      act.has_value() ? reinterpret_cast<__nv_bfloat16*>(act->data_ptr()) : nullptr, I, total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -219,3 +219,29 @@ def sample(logits, temps, seeds, out):
             u = torch.rand(lf.shape[1], generator=gen).clamp(1e-7, 1 - 1e-7)
             res[r] = (lf[r] / t - torch.log(-torch.log(u))).argmax()
     out.copy_(res)
+
+
+def rms_norm_bwd(x, dy, w, eps, add=None, out=None, out_bf16=None):
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    xhat = xf * inv
+    g = dy.float() * w.float()
+    dx = (g - xhat * (g * xhat).mean(-1, keepdim=True)) * inv
+    if add is not None:
+        dx = dx + add
+    if out is not None:
+        out.copy_(dx)
+    if out_bf16 is not None:
+        out_bf16.copy_(dx.to(out_bf16.dtype))
+    return dx
+
+
+def swiglu_bwd(gu, dact, dgu, act=None):
+    g, u = deinterleave64(gu.float())
+    sg = torch.sigmoid(g)
+    silu = g * sg
+    d_u = dact * silu
+    d_g = dact * u * sg * (1 + g * (1 - sg))
+    dgu.copy_(interleave64(d_g, d_u).to(dgu.dtype))
+    if act is not None:
+        act.copy_((silu * u).to(act.dtype))

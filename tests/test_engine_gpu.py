@@ -89,7 +89,7 @@ def test_gpu_coserving_engine_runs_cycles():
     eng.run_until_idle(max_steps=5000)
     eng.synchronize()
     assert ops.check_device_error() == 0
-    assert eng.coord.completed_cycles >= 4
+    assert eng.coord.completed_cycles >= 4, eng.finetuning_status()
     assert all(l == l and l > 0 for l in eng.trainer.losses)
     assert len([r for r in eng.finished if r.request_id.startswith("r")]) == 12
     assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks

@@ -241,3 +241,58 @@ def test_sample_greedy():
     assert torch.equal(out, logits.argmax(-1))
     ops.sample(logits, torch.ones(7, device=DEV), torch.arange(7, device=DEV), out)
     assert ((out >= 0) & (out < 30000)).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 6144, 4096), (64, 4096, 14336), (100, 1024, 2048)])
+def test_gemm_splitk_decode_shapes(M, N, K):
+    a, b = rnd(M, K, seed=31), rnd(N, K, scale=0.05, seed=32)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(a, b, out)
+    torch.testing.assert_close(out.float(), a.float() @ b.float().t(), rtol=2e-2, atol=3e-2)
+    o32 = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(a, b, o32, epi=ops.EPI_F32)
+    torch.testing.assert_close(o32, a.float() @ b.float().t(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("M", [3, 40])
+def test_gemm_splitk_swiglu_lora_save(M):
+    K, I, slots, seg = 4096, 1792, 2, 64
+    x, w = rnd(M, K, seed=33), rnd(2 * I, K, scale=0.02, seed=34)
+    A = rnd(slots, 2 * 16, K, scale=0.02, seed=35)
+    B2 = rnd(2 * I, slots * seg, scale=0.05, seed=36)
+    sid = torch.zeros(M, dtype=torch.int32, device=DEV)
+    sid[M // 2:] = 1
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, sid, Z, seg)
+    mask = torch.tensor([3], dtype=torch.int32, device=DEV)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    save = torch.zeros(M, 2 * I, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, epi=ops.EPI_SWIGLU, z=Z, b2=B2, tile_slots=mask, lora_seg=seg,
+             save=save, save_lo=1, save_hi=M, save_dst=0)
+    acc = x.float() @ w.float().t() + Z.float() @ B2.float().t()
+    g, u = ref.deinterleave64(acc)
+    torch.testing.assert_close(out.float(), torch.nn.functional.silu(g) * u, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(save[:M - 1].float(), acc[1:M], rtol=2e-2, atol=3e-2)
+
+
+def test_rms_norm_bwd_and_swiglu_bwd():
+    T, D = 50, 4096
+    x = rnd(T, D, seed=37)
+    dy = rnd(T, D, dtype=torch.float32, seed=38)
+    w = rnd(D, scale=0.1, seed=39) + 1
+    add = rnd(T, D, dtype=torch.float32, seed=40)
+    bf = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    out = ops.rms_norm_bwd(x, dy, w, 1e-5, add=add, out_bf16=bf)
+    exp = ref.rms_norm_bwd(x.cpu(), dy.cpu(), w.cpu(), 1e-5, add.cpu())
+    torch.testing.assert_close(out.cpu(), exp, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(bf.float().cpu(), exp, rtol=1e-2, atol=1e-2)
+    I = 1792
+    gu = rnd(T, 2 * I, seed=41)
+    dact = rnd(T, I, dtype=torch.float32, seed=42)
+    dgu = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=DEV)
+    act = torch.empty(T, I, dtype=torch.bfloat16, device=DEV)
+    ops.swiglu_bwd(gu, dact, dgu, act)
+    dgu_r, act_r = torch.empty(T, 2 * I, dtype=torch.bfloat16), torch.empty(T, I, dtype=torch.bfloat16)
+    ref.swiglu_bwd(gu.cpu(), dact.cpu(), dgu_r, act_r)
+    torch.testing.assert_close(dgu.float().cpu(), dgu_r.float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(act.float().cpu(), act_r.float(), rtol=2e-2, atol=2e-2)
