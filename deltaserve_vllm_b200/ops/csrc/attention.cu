@@ -489,3 +489,70 @@ void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   decode_combine_kernel<<<dim3(B, (unsigned)num_heads), HD, 0, s>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ---------------------------------------------------------------- allocation-free entry point
+// See noalloc.h for who calls this and the contract (no counterpart in the
+// reference project).
+#include "noalloc.h"
+
+namespace dsv {
+// The scratch of dsv_paged_decode_noalloc: split partials (128 floats of output
+// and 2 of max/sum per (sequence, head, split)). Host code must not use this
+// name as an address: it looks the device address up with cudaGetSymbolAddress.
+static __device__ __align__(256) float g_noalloc_scratch[DSV_NOALLOC_SCRATCH_FLOATS];
+constexpr int kMaxDevices = 64;
+static float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+}  // namespace dsv
+
+extern "C" int dsv_paged_decode_noalloc(const void* q, int q_stride, const void* k_cache, const void* v_cache,
+                                        int num_kv_heads, int block_size, const int* block_tables, int max_blocks,
+                                        const int* ctx_lens, int batch, void* out, int out_stride, int num_heads,
+                                        float scale, int splits, int keys_per_split, cudaStream_t stream) {
+  using namespace dsv;
+  if (batch == 0) return DSV_NOALLOC_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !ctx_lens || !out || batch < 0 || num_kv_heads <= 0 ||
+      num_heads % num_kv_heads != 0 || splits < 1 || keys_per_split <= 0 || keys_per_split % DC_KEYS != 0 ||
+      block_size <= 0)
+    return DSV_NOALLOC_EINVAL;
+  const int G = num_heads / num_kv_heads;
+  if (G < 1 || G > DC_MAX_GROUP) return DSV_NOALLOC_EINVAL;
+  const long long parts = (long long)batch * num_heads * splits;
+  if (parts * (HD + 2) > DSV_NOALLOC_SCRATCH_FLOATS) return DSV_NOALLOC_ETOOBIG;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSV_NOALLOC_ECUDA;
+  if (g_noalloc_ptr[dev] == nullptr) {
+    // One-time set-up on this device (the device is current here).
+    float* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return DSV_NOALLOC_ECUDA;
+    g_noalloc_ptr[dev] = p;
+  }
+  float* scratch = g_noalloc_ptr[dev];
+  DecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_stride;
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks;
+  a.ctx_lens = ctx_lens;
+  a.part_o = scratch;
+  a.part_ml = scratch + parts * HD;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.out_stride = out_stride;
+  a.num_heads = num_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = G;
+  a.block_size = block_size;
+  a.splits = splits;
+  a.keys_per_split = keys_per_split;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int dsmem = 4 * DC_KEYS * HD * 2;
+  if (cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dsmem) != cudaSuccess)
+    return DSV_NOALLOC_ECUDA;
+  paged_decode_kernel<<<dim3(batch, num_kv_heads, (unsigned)splits), DC_THREADS, dsmem, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+  decode_combine_kernel<<<dim3(batch, (unsigned)num_heads), HD, 0, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+  return DSV_NOALLOC_OK;
+}
