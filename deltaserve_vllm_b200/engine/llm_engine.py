@@ -147,7 +147,7 @@ class CoServingEngine:
         # Backward layers are CUDA-graph replays enqueued inline by this thread
         # (a background feeder thread loses the GIL to the serving loop after
         # every PyTorch call, so the work stays on the engine thread).
-        self.feeder = None
+        self._bwd_remaining = 0
         self._bwd_gen = None
         self._bwd_events: deque = deque()
         self._bwd_done_evt = None
@@ -459,44 +459,44 @@ class CoServingEngine:
                                  self._bwd_meta["epoch"], sync=False)
         self._bwd_events.clear()
         self._record(("bwd_start", dict(self._bwd_meta)))
-        if self.feeder is not None:
-            self.feeder.start_cycle(gen)
-        else:
-            self._bwd_gen = gen
+        self._bwd_gen = gen
+        # head + one step per layer + the optimizer/publish step
+        self._bwd_remaining = self.arch.num_layers + 2
 
     @property
     def bwd_active(self) -> bool:
-        return self._bwd_gen is not None or (self.feeder is not None and self.feeder.busy)
+        return self._bwd_gen is not None
 
     def _advance_backward(self, idle: bool, paused: bool = False) -> None:
-        """Let the backward progress. With the feeder thread (CUDA) this only
-        sets the pause flag; otherwise enqueue layers here: all remaining when
-        the engine is idle, else at most ``backward_run_ahead_boundaries``."""
-        if self.feeder is not None:
-            if self.feeder.error is not None:
-                err, self.feeder.error = self.feeder.error, None
-                self.coord.disable(f"backward failed: {err!r}")
-            self.feeder.set_paused(paused and not idle)
-            return
+        """Enqueue backward steps on the low-priority stream: all remaining when
+        the engine is idle, otherwise until ``backward_run_ahead_boundaries``
+        steps are outstanding on the GPU. The number of steps is decided first
+        and sent to the follower ranks before any of them runs, so every rank
+        issues the backward collectives in the same order."""
         if self._bwd_gen is None or (paused and not idle):
             return
         ahead = max(1, self.ftcfg.backward_run_ahead_boundaries)
-        budget = 1 << 30 if idle else ahead
-        while budget > 0 and self._bwd_gen is not None:
-            if self.cuda and len(self._bwd_events) >= ahead and not idle:
-                if not self._bwd_events[0].query():
-                    break
+        if self.cuda:
+            while self._bwd_events and self._bwd_events[0].query():
                 self._bwd_events.popleft()
+            k = self._bwd_remaining if idle else max(0, ahead - len(self._bwd_events))
+        else:
+            k = self._bwd_remaining if idle else ahead
+        k = min(k, self._bwd_remaining)
+        if k <= 0:
+            return
+        for _ in range(k):
+            self._record(("bwd_next",))
+        self._flush_actions()
+        for _ in range(k):
+            self._bwd_remaining -= 1
             try:
-                self._record(("bwd_next",))
                 if self.cuda:
                     with torch.cuda.stream(self.bwd_stream):
                         next(self._bwd_gen)
                         ev = torch.cuda.Event()
                         ev.record()
                     self._bwd_events.append(ev)
-                    while len(self._bwd_events) > ahead:
-                        self._bwd_events.popleft()
                 else:
                     next(self._bwd_gen)
                 self.stats["bwd_layers"] += 1
@@ -510,7 +510,7 @@ class CoServingEngine:
                     self._publish_evt = ev
                 else:
                     self._finish_backward()
-            budget -= 1
+                break
 
     def _poll_backward(self) -> None:
         if self._bwd_done_evt is not None and self._bwd_done_evt.query():
@@ -543,8 +543,6 @@ class CoServingEngine:
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
 
     def _drain_backward(self) -> None:
-        if self.feeder is not None:
-            self.feeder.wait_idle()
         while self._bwd_gen is not None:
             self._advance_backward(idle=True)
         self._flush_actions()
@@ -766,6 +764,8 @@ class CoServingEngine:
                     self._bwd_gen = self.trainer.cycle(self.capture, m["n"], m["starts"], m["lens"],
                                                        m["epoch"], sync=False)
                 elif kind == "bwd_next":
+                    if self._bwd_gen is None:
+                        continue
                     try:
                         if self.cuda:
                             with torch.cuda.stream(self.bwd_stream):

@@ -84,6 +84,7 @@ class LoraTrainer:
         self._groups_cache: dict = {}
         self._pool = None
         self._cap_stream = None
+        self._seen_shapes: set = set()
         self._sq_rep = torch.zeros(L, dtype=torch.float32, device=dev)
         self._sq_shard = torch.zeros(L, dtype=torch.float32, device=dev)
 
@@ -177,6 +178,11 @@ class LoraTrainer:
         if gs is not None:
             return gs
         if not self.use_graphs or len(self._graphs) >= self.max_graph_shapes:
+            return None
+        if key not in self._seen_shapes:
+            # First cycle of a shape runs eagerly (creates library handles and
+            # loads kernels outside any capture); the second captures.
+            self._seen_shapes.add(key)
             return None
         dev = self.masters.params.device
         gs = {"labels": torch.empty(ci.n_pad, dtype=torch.long, device=dev),

@@ -1,0 +1,64 @@
+"""Tensor parallelism on real GPUs (NCCL over NVLink): TP=2 serving forward
+logits and LoRA-backward gradients equal the TP=1 run on the same model.
+Needs 2 GPUs (skipped otherwise)."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    torch.cuda.set_device(rank)
+    if world > 1:
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200.models.configs import PRESETS
+    from deltaserve_vllm_b200.models.lora import random_adapter
+    from deltaserve_vllm_b200.models.weights import TPInfo
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from test_trainer_gpu import run as run_trainer
+    arch = PRESETS["llama3-test"]
+    g = torch.Generator().manual_seed(1)
+    seqs = [torch.randint(0, arch.vocab, (n,), generator=g).tolist() for n in (64, 200, 33, 130)]
+    ad = random_adapter(arch, 16, seed=3, b_std=0.02)
+    comm = TPComm() if world > 1 else None
+    tr, res = run_trainer(arch, seqs, ad, "cuda", torch.bfloat16, tp=TPInfo(rank, world), comm=comm)
+    grads = tr.masters.export_peft(16, grads=True)
+    if comm is not None:
+        shards = comm.gather_objects(grads)
+        if rank == 0:
+            from deltaserve_vllm_b200.adapters.peft_io import merge_tp_shards
+            grads = merge_tp_shards(shards)
+    if rank == 0:
+        torch.save({"loss": res[0].loss, "grads": grads}, os.path.join(outdir, f"tp{world}.pt"))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_backward_matches_tp1_on_gpu():
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_run, args=(1, _port(), d), nprocs=1, join=True, start_method="spawn")
+        a, b = torch.load(os.path.join(d, "tp2.pt")), torch.load(os.path.join(d, "tp1.pt"))
+        assert abs(a["loss"] - b["loss"]) < 0.01 * abs(b["loss"])
+        for k, g in b["grads"].items():
+            x, y = a["grads"][k].flatten().double(), g.flatten().double()
+            cos = float(x @ y / (x.norm() * y.norm() + 1e-30))
+            assert cos > 0.99, (k, cos)

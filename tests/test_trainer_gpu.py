@@ -17,14 +17,16 @@ from deltaserve_vllm_b200.models.weights import init_weights
 pytestmark = pytest.mark.gpu
 
 
-def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0):
-    w = init_weights(arch, seed=5, device="cpu", dtype=torch.float32).to(device, dtype)
-    kv = KVCache(arch.num_layers, 64, arch.num_kv_heads, 64, 128, device, dtype)
+def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None):
+    from deltaserve_vllm_b200.models.weights import TPInfo
+    tp = tp or TPInfo()
+    w = init_weights(arch, tp=tp, seed=5, device="cpu", dtype=torch.float32).to(device, dtype)
+    kv = KVCache(arch.num_layers, 64, arch.num_kv_heads // tp.size, 64, 128, device, dtype)
     served = LoraServeBuffers(arch, w.tp, slots=2, max_rank=16, device=device, dtype=dtype)
-    model = DecoderModel(w, kv.k, kv.v, served)
+    model = DecoderModel(w, kv.k, kv.v, served, comm)
     n = sum(len(s) for s in seqs)
     cap = CaptureBuffers.allocate(w, n + 8, device, dtype)
-    tr = LoraTrainer(w, served, 1, 16, 32, lr=lr, mask_prefix=16, cos_sin_table=model.cos_sin)
+    tr = LoraTrainer(w, served, 1, 16, 32, lr=lr, mask_prefix=16, cos_sin_table=model.cos_sin, comm=comm)
     tr.load_adapter(ad, 16, 32)
     tr.publish()
     runner = ModelRunner(model, 64, device, ft_slot=1)
