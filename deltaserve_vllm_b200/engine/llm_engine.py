@@ -187,6 +187,10 @@ class CoServingEngine:
             nb = min(nb, e.max_num_seqs * -(-e.max_model_len // e.block_size) + 64)
         else:
             nb = 4 * (-(-e.max_model_len // e.block_size)) + 16
+        if self.comm is not None and self.comm.size > 1:
+            # Rank 0 hands out page ids for every rank: all ranks must hold the
+            # same number of pages (the smallest any rank can afford).
+            nb = -self.comm.all_reduce_max_int(-nb)
         if nb < 2:
             raise MemoryError("no room for the KV cache")
         return KVCache(self.arch.num_layers, nb, hkv, e.block_size, self.arch.head_dim, self.device,

@@ -40,12 +40,11 @@ class _Packer:
             off += k
         return pk
 
-    def ship(self, device, pinned: torch.Tensor | None):
+    def ship(self, device, pinned: "PinnedRing | None"):
         total = sum(a.size for _, a in self.parts)
+        slot = None
         if device.type == "cuda":
-            if pinned is None or pinned.numel() < total:
-                pinned = torch.empty(max(total, 1 << 16) * 2, dtype=torch.int64, pin_memory=True)
-            host = pinned[:total]
+            host, slot = pinned.acquire(total)
         else:
             host = torch.empty(total, dtype=torch.int64)
         hn = host.numpy()
@@ -56,7 +55,38 @@ class _Packer:
             spans[name] = (off, a.size)
             off += a.size
         dev = host.to(device, non_blocking=True) if device.type == "cuda" else host
+        if slot is not None:
+            pinned.release(slot)
         return {k: dev[o:o + n] for k, (o, n) in spans.items()}, pinned, total * 8
+
+
+class PinnedRing:
+    """Pinned host staging buffers for the per-step H2D copy. A buffer is
+    reused only after the copy that last read it has executed (an event
+    recorded right after the copy), so a host that runs ahead of the GPU (a
+    follower rank, or steps that sample nothing) never overwrites step
+    metadata the GPU has not fetched yet."""
+
+    def __init__(self, n: int = 4):
+        self.bufs: list[torch.Tensor | None] = [None] * n
+        self.events: list = [None] * n
+        self.i = 0
+
+    def acquire(self, numel: int):
+        k = self.i
+        self.i = (self.i + 1) % len(self.bufs)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        b = self.bufs[k]
+        if b is None or b.numel() < numel:
+            b = torch.empty(max(numel, 1 << 16) * 2, dtype=torch.int64, pin_memory=True)
+            self.bufs[k] = b
+        return b[:numel], k
+
+    def release(self, k: int) -> None:
+        ev = torch.cuda.Event()
+        ev.record()
+        self.events[k] = ev
 
 
 class ModelRunner:
@@ -67,7 +97,7 @@ class ModelRunner:
         self.device = torch.device(device)
         self.num_sms = num_sms
         self.ft_slot = ft_slot
-        self._pinned: torch.Tensor | None = None
+        self._pinned = PinnedRing() if self.device.type == "cuda" else None
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
 
