@@ -255,6 +255,9 @@ class CoServingEngine:
             alpha = alpha if alpha is not None else 2.0 * rank
             tensors = random_adapter(self.arch, rank, seed if seed is not None else 1000 + slot)
         self.lora.load_slot(slot, tensors, rank, alpha)
+        if self.cuda:
+            # Written on the current stream; forwards run on their own stream.
+            torch.cuda.synchronize(self.device)
         self.adapter_slots[name] = slot
         self.adapter_meta[name] = {"rank": rank, "alpha": alpha, "path": path}
         return slot
@@ -750,16 +753,16 @@ class CoServingEngine:
                 if kind == "fwd":
                     _, arr, spans, meta, has_ft = a
                     from .model_runner import _Packer
-                    b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
                     if self.cuda:
+                        # The metadata copy must be ordered before the forward:
+                        # both go on the forward stream (as on rank 0).
                         with torch.cuda.stream(self.fwd_stream):
+                            b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
                             if has_ft and self._publish_evt is not None:
                                 self.fwd_stream.wait_event(self._publish_evt)
-                            ev = torch.cuda.Event()
                             self.model.forward(b, self.capture if has_ft else None)
-                            ev.record()
-                        self._last_fwd_evt = ev
                     else:
+                        b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
                         self.model.forward(b, self.capture if has_ft else None)
                 elif kind == "bwd_start":
                     m = a[1]
