@@ -157,6 +157,10 @@ def main():
     from deltaserve_vllm_b200.models.configs import resolve_arch
     from deltaserve_vllm_b200.parallel.comm import init_tp
 
+    dump_s = float(os.environ.get("DSV_BENCH_STACKDUMP_S", "0"))
+    if dump_s > 0:  # diagnostics: dump every thread's stack if still running then
+        import faulthandler
+        faulthandler.dump_traceback_later(dump_s, repeat=False)
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     if ws != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}; launch N>1 under torchrun")
@@ -184,6 +188,7 @@ def main():
     eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
     if rank != 0:
         eng.follow()
+        eng.close()
         if comm is not None:
             torch.distributed.destroy_process_group()
         return
@@ -204,9 +209,12 @@ def main():
                             arrival_time=clock0 + t_arr)
             ti += 1
 
-    for _ in range(args.warmup):
+    verbose = os.environ.get("DSV_BENCH_VERBOSE") == "1"
+    for i in range(args.warmup):
         ingest()
         eng.step()
+        if verbose:
+            dprint(f"warmup step {i}: {eng.coord.status()['cycle']} cycles, bwd_active={eng.bwd_active}")
     eng.synchronize()
     stats0 = dict(eng.stats)
     l0 = ops.LAUNCHES[0]
@@ -273,6 +281,7 @@ def main():
     }
     eng.shutdown()
     print(json.dumps(line), flush=True)
+    eng.close()
     if comm is not None:
         torch.distributed.destroy_process_group()
 

@@ -686,6 +686,17 @@ class CoServingEngine:
             self._flush_actions()
         return hook
 
+    def close(self) -> None:
+        """Release GPU resources that hold communicator state. CUDA graphs with
+        captured NCCL collectives must be destroyed before the process group,
+        or its teardown waits forever. Safe to call on every rank."""
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        if self.trainer is not None:
+            self.trainer.release_graphs()
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+
     def _mark_local(self, name: str) -> None:
         """Synchronise every stream of this GPU, then stamp wall time and a CUDA
         event (used to time a region on the device on every rank)."""

@@ -221,6 +221,14 @@ class LoraTrainer:
         self._graphs[key] = gs
         return gs
 
+    def release_graphs(self) -> None:
+        """Drop every captured graph (and its memory pool)."""
+        self._graphs.clear()
+        self._seen_shapes.clear()
+        self._pool = None
+        import gc
+        gc.collect()
+
     def cycle(self, cap: CaptureBuffers, n: int, starts, lens, epoch: int | None = None,
               sync: bool = True):
         """Generator: yields at each pause boundary; its return value (via
