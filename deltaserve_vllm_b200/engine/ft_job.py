@@ -67,8 +67,11 @@ class TrainingStage(Stage):
         return ("init",) if "init" in names else ()
 
     def start(self, job, ctx) -> None:
+        # Open admission unless the launch config keeps it closed until
+        # POST /start_finetuning.
         coord = getattr(ctx, "coord", None)
-        if coord is not None and getattr(ctx, "start_on_launch", True):
+        cfg = getattr(ctx, "ftcfg", None)
+        if coord is not None and getattr(cfg, "start_on_launch", True):
             coord.start()
 
     def poll(self, job, ctx) -> bool:

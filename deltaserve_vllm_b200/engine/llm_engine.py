@@ -26,6 +26,7 @@ Step (rank 0):
 
 from __future__ import annotations
 
+import json
 import math
 import sys
 import threading
@@ -170,6 +171,11 @@ class CoServingEngine:
         self.step_listeners: list = []
         self.request_listeners: list = []
         self.backward_listeners: list = []
+        self.metrics = None
+        self.step_trace = None
+        self.router = None
+        if self.is_driver and (self.ftcfg.metrics_dir or self.ftcfg.step_trace_path):
+            self.start_telemetry(self.ftcfg.metrics_dir)
 
     # ------------------------------------------------------------------ setup
     def _alloc_kv(self) -> KVCache:
@@ -312,6 +318,97 @@ class CoServingEngine:
             path = os.path.join(self.ftcfg.adapter_save_path, f"manual-{int(time.time())}")
         self._drain_backward()
         return self.trainer.save_adapter(path, save_id)
+
+    # ------------------------------------------------------------------ estimator state
+    def save_estimator_state(self, path: str | None = None) -> str | None:
+        """Estimator coefficients plus the tracker's step samples as one JSON
+        file, written atomically; with no ``path`` the configured
+        ``estimator_state_save_path`` is used once (shutdown). Reference:
+        ``deltaserve-plugin/deltaserve/ft_scheduler.py:1131-1156``."""
+        if path is None:
+            path = self.ftcfg.estimator_state_save_path
+            if not path or getattr(self, "_estimator_state_saved", False):
+                return None
+            self._estimator_state_saved = True
+        self._drain_timing(block=True)
+        state = {"version": 1, "estimator": self.estimator.export_state(),
+                 "tracker": self.tracker.export_state()}
+        os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+        tmp = f"{path}.tmp"
+        with open(tmp, "w") as f:
+            json.dump(state, f)
+        os.replace(tmp, path)
+        dprint(f"[estimator] state saved to {path}: {self.tracker.size()} samples")
+        return path
+
+    def load_estimator_state(self, path: str | None = None) -> bool:
+        """Replace the fitted estimator with a saved state (after the launch
+        profile, which still runs to warm the finetuning paths). A missing file
+        is a warning, not an error (first run of a replayed trace)."""
+        path = path or self.ftcfg.estimator_state_load_path
+        if not path:
+            return False
+        if not os.path.isfile(path):
+            dprint(f"[estimator] estimator_state_load_path={path} does not exist; "
+                   "keeping the launch-time profile")
+            return False
+        with open(path) as f:
+            state = json.load(f)
+        self.tracker.import_state(state["tracker"])
+        self.estimator.import_state(state["estimator"])
+        dprint(f"[estimator] state restored from {path}: {self.tracker.size()} samples")
+        return True
+
+    # ------------------------------------------------------------------ telemetry
+    def start_telemetry(self, metrics_dir: str | None = None) -> None:
+        """Attach the run recorder (CSV/JSONL outputs when ``metrics_dir`` is
+        set, live feed only otherwise) and, if configured, the step trace."""
+        from ..utils.metrics import MetricsRecorder
+        from ..utils.step_trace import attach_step_trace
+        self.stop_telemetry()
+        cfg = self.ftcfg
+        self.metrics = MetricsRecorder(self, metrics_dir, cfg.metrics_interval_s, cfg.steps_log_max_mb,
+                                       rank=self.tp.rank)
+        if cfg.step_trace_path and self.step_trace is None:
+            self.step_trace = attach_step_trace(self, cfg.step_trace_path)
+
+    def stop_telemetry(self) -> None:
+        m = self.metrics
+        if m is None:
+            return
+        self.metrics = None
+        for lst, cb in ((self.step_listeners, m.on_step), (self.request_listeners, m.on_request),
+                        (self.backward_listeners, m.on_backward)):
+            if cb in lst:
+                lst.remove(cb)
+        m.close()
+
+    # ------------------------------------------------------------------ adapters
+    def adapter_op(self, name: str, op: str):
+        """Adapter lifecycle by name. With adapter routing the pool owns the
+        lifecycle (``load``/``unload``/``pin``/``unpin``/``remove``/``prewarm``);
+        without it ``unload``/``remove`` free the slot and ``load`` re-reads
+        the adapter's path."""
+        if self.router is not None:
+            return self.router.pool.op(name, op)
+        if name == FT_ADAPTER_NAME:
+            raise ValueError("the trainable adapter cannot be managed by name")
+        if op in ("unload", "remove"):
+            slot = self.adapter_slots.pop(name, None)
+            if slot is None:
+                raise KeyError(f"adapter {name!r} is not loaded")
+            self._drain_backward()
+            if self.cuda:
+                torch.cuda.synchronize(self.device)
+            self.lora.clear_slot(slot)
+            self.adapter_meta.pop(name, None)
+            return {"slot": slot}
+        if op == "load":
+            meta = self.adapter_meta.get(name) or {}
+            if not meta.get("path"):
+                raise KeyError(f"adapter {name!r} has no known path")
+            return {"slot": self.load_inference_adapter(name, path=meta["path"])}
+        raise ValueError(f"unknown adapter op {op!r} (load, unload, remove)")
 
     # ------------------------------------------------------------------ stepping
     def _ft_rows_in(self, out: SchedulerOutput) -> int:
@@ -534,6 +631,7 @@ class CoServingEngine:
             self.coord.min_sample_len = max(1, self.store.min_len() or 1)
             if not self.store.has_next():
                 self.store.advance_epoch()
+                self._epoch_ended = True
         self.stats["ft_tokens_trained"] += res.n_tokens
         for cb in self.backward_listeners:
             cb(res)
@@ -548,6 +646,11 @@ class CoServingEngine:
         if cfg.adapter_save_every_backwards > 0 and st % cfg.adapter_save_every_backwards == 0:
             self.trainer.save_adapter(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"))
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
+        if cfg.adapter_save_every_epoch and getattr(self, "_epoch_ended", False):
+            ep = self.store.current_epoch if self.store else 0
+            self.trainer.save_adapter(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"))
+            peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last, prefix="epoch-")
+        self._epoch_ended = False
 
     def _drain_backward(self) -> None:
         while self._bwd_gen is not None:
@@ -590,6 +693,7 @@ class CoServingEngine:
                     self._profile_shape(sh, record=True)
             self.synchronize()
             self.estimator.data_fit(self.tracker)
+            self.load_estimator_state()
             if self.ft_enabled and self.trainer is not None:
                 # One full backward cycle on this thread at the buffer's size:
                 # loads every backward kernel before the feeder thread runs.
@@ -736,7 +840,17 @@ class CoServingEngine:
         return [mine] + [r["__region__"] for r in res[1:]]
 
     def shutdown(self) -> None:
-        """Stop the follower ranks (driver) after finishing queued work."""
+        """Stop the follower ranks (driver) after finishing queued work; save
+        the estimator state (once, if configured) and close telemetry files."""
+        if self.is_driver:
+            try:
+                self.save_estimator_state()
+            except Exception as e:  # best effort at teardown
+                dprint(f"[estimator] state save failed: {e!r}")
+        self.stop_telemetry()
+        if self.step_trace is not None:
+            self.step_trace.close()
+            self.step_trace = None
         if self.tp_size > 1 and self.is_driver:
             self._record(("stop",))
             self._flush_actions()

@@ -1,0 +1,338 @@
+"""HTTP API: the OpenAI-compatible completions endpoint plus the co-serving
+control surface of the reference (``deltaserve-plugin/deltaserve/api.py:41-455``):
+
+=======================================  ==============================================
+``POST /v1/completions``                  OpenAI completions (``stream`` supported);
+                                          ``model`` = base model, an adapter name, or
+                                          the routing model name (``auto``)
+``GET  /v1/models``, ``GET /health``
+``POST /start_finetuning`` / ``stop``     open / close finetuning admission
+``GET  /finetuning_status``               coordinator, trainer, store and job state
+``POST /save_adapter``                    PEFT checkpoint of the trained adapter now
+                                          (``{"path"?, "wait"?, "timeout_s"?}``)
+``POST /save_estimator_state``            estimator coefficients + samples as JSON
+``GET  /system_metrics``                  telemetry window + totals
+``GET  /telemetry/data``                  live step stream / series (``steps_since``)
+``POST /telemetry/start|stop|memory``     recorder on/off, memory snapshot
+``POST /ft_jobs`` / ``GET /ft_jobs``      submit / list finetuning jobs
+``GET  /adapters``, ``/adapters/available``  adapter pool
+``POST /adapters``, ``POST /adapters/{name}/{op}``, ``DELETE /adapters/{name}``
+``POST /shutdown``                        stop the engine loop
+=======================================  ==============================================
+"""
+
+from __future__ import annotations
+
+import asyncio
+import contextlib
+import json
+import os
+import time
+import uuid
+
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, StreamingResponse
+
+from ..engine.request import SamplingParams
+from .engine_thread import EngineThread
+
+
+def _json_body(body) -> dict:
+    return body if isinstance(body, dict) else {}
+
+
+def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> FastAPI:
+    et = EngineThread(engine)
+
+    @contextlib.asynccontextmanager
+    async def lifespan(_app):
+        et.start()
+        try:
+            yield
+        finally:
+            await asyncio.to_thread(et.stop)
+
+    app = FastAPI(title="DeltaServe-B200", lifespan=lifespan)
+    app.state.engine_thread = et
+    app.state.engine = engine
+    app.state.server = None        # a uvicorn.Server, set by the launcher for /shutdown
+    model_name = served_model_name or engine.ecfg.served_model_name or engine.ecfg.model
+    tok = tokenizer or engine.tokenizer
+    if tok is None:
+        from ..utils.tokenizer import ByteTokenizer
+        tok = ByteTokenizer(engine.arch.vocab)
+    route_name = engine.rcfg.route_model_name if engine.rcfg.enable_adapter_routing else None
+
+    async def body_of(req: Request) -> dict:
+        try:
+            return _json_body(await req.json())
+        except Exception:
+            return {}
+
+    # ------------------------------------------------------------ inference
+    @app.get("/health")
+    async def health():
+        return {"ok": et.alive and et.error is None, "error": et.error}
+
+    @app.get("/v1/models")
+    async def models():
+        names = [model_name] + [n for n in engine.adapter_slots if not n.startswith("__")]
+        if route_name:
+            names.append(route_name)
+        return {"object": "list", "data": [{"id": n, "object": "model", "owned_by": "deltaserve"}
+                                           for n in names]}
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await body_of(req)
+        prompt = body.get("prompt")
+        if prompt is None:
+            return JSONResponse(status_code=400, content={"error": "prompt is required"})
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            ids = [int(t) for t in prompt]
+        elif isinstance(prompt, list):
+            if len(prompt) != 1:
+                return JSONResponse(status_code=400, content={"error": "one prompt per request"})
+            ids = tok.encode(str(prompt[0]))
+        else:
+            ids = tok.encode(str(prompt))
+        if not ids:
+            return JSONResponse(status_code=400, content={"error": "empty prompt"})
+        model = body.get("model") or model_name
+        adapter = None
+        headers = {}
+        if route_name and model == route_name:
+            router = getattr(engine, "router", None)
+            if router is None:
+                return JSONResponse(status_code=503, content={"error": "adapter routing is not running"})
+            text = body.get("prompt") if isinstance(body.get("prompt"), str) else tok.decode(ids)
+            dec = await et.call(lambda e: e.router.route(text))
+            adapter = dec.adapter
+            headers = dec.headers()
+        elif model != model_name:
+            if model not in engine.adapter_slots:
+                return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
+            adapter = model
+        params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
+                                temperature=float(body.get("temperature", 0.0) or 0.0),
+                                seed=body.get("seed"), ignore_eos=bool(body.get("ignore_eos", False)),
+                                stop_token_ids=tuple(body.get("stop_token_ids") or ()))
+        rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+        stream = bool(body.get("stream", False))
+        w = et.register(rid, stream)
+        et.notify_arrival()
+        try:
+            await et.call(lambda e: e.add_request(rid, ids, params, adapter))
+        except Exception as e:
+            et.unregister(rid)
+            return JSONResponse(status_code=400, content={"error": str(e)})
+        created = int(time.time())
+        if stream:
+            async def gen():
+                try:
+                    while True:
+                        toks = await w.tokens.get()
+                        if toks is None:
+                            break
+                        chunk = {"id": rid, "object": "text_completion", "created": created,
+                                 "model": model, "choices": [{"index": 0, "text": tok.decode(toks),
+                                                              "token_ids": toks, "finish_reason": None}]}
+                        yield f"data: {json.dumps(chunk)}\n\n"
+                    r = await w.done
+                    fin = {"id": rid, "object": "text_completion", "created": created, "model": model,
+                           "choices": [{"index": 0, "text": "", "finish_reason": _finish_reason(r)}]}
+                    yield f"data: {json.dumps(fin)}\n\ndata: [DONE]\n\n"
+                finally:
+                    et.unregister(rid)
+            return StreamingResponse(gen(), media_type="text/event-stream", headers=headers)
+        try:
+            r = await w.done
+        finally:
+            et.unregister(rid)
+        out = {"id": rid, "object": "text_completion", "created": created, "model": model,
+               "choices": [{"index": 0, "text": tok.decode(r.output_ids), "token_ids": r.output_ids,
+                            "finish_reason": _finish_reason(r)}],
+               "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),
+                         "total_tokens": r.num_prompt + len(r.output_ids)},
+               "metrics": {"ttft_s": r.ttft(), "tbt_mean_s": (sum(r.tbts()) / len(r.tbts()))
+                           if r.tbts() else None}}
+        return JSONResponse(content=out, headers=headers)
+
+    # ------------------------------------------------------------ finetuning
+    @app.post("/start_finetuning")
+    async def start_finetuning():
+        st = await et.call(lambda e: (e.start_finetuning(), e.finetuning_status())[1])
+        return {"started": True, "status": st}
+
+    @app.post("/stop_finetuning")
+    async def stop_finetuning():
+        st = await et.call(lambda e: (e.stop_finetuning(), e.finetuning_status())[1])
+        return {"stopped": True, "status": st}
+
+    @app.get("/finetuning_status")
+    async def finetuning_status():
+        return await et.call(lambda e: e.finetuning_status())
+
+    @app.post("/save_adapter")
+    async def save_adapter(req: Request):
+        body = await body_of(req)
+        path = body.get("path")
+        if not path:
+            root = engine.ftcfg.adapter_save_path
+            if not root:
+                return JSONResponse(status_code=400, content={
+                    "error": "no path given and finetune_param.adapter_save_path is not set"})
+            path = os.path.join(root, time.strftime("manual-%Y%m%d-%H%M%S"))
+        path = os.path.abspath(str(path))
+        save_id = uuid.uuid4().hex
+        if engine.trainer is None:
+            return JSONResponse(status_code=409, content={"error": "finetuning is not enabled", "path": path})
+        fut = et.submit(lambda e: e.save_adapter(path, save_id))
+        if not body.get("wait", True):
+            return JSONResponse(status_code=202, content={"scheduled": True, "path": path, "save_id": save_id})
+        try:
+            await asyncio.wait_for(asyncio.wrap_future(fut), float(body.get("timeout_s", 300)))
+        except asyncio.TimeoutError:
+            return JSONResponse(status_code=202, content={"pending": True, "path": path, "save_id": save_id})
+        except Exception as ex:
+            return JSONResponse(status_code=500, content={"path": path, "saved": False, "error": str(ex)})
+        from ..adapters.peft_io import read_save_result
+        res = read_save_result(path, save_id) or {}
+        return {"path": path, "saved": True, **res}
+
+    @app.post("/save_estimator_state")
+    async def save_estimator_state(req: Request):
+        body = await body_of(req)
+        path = body.get("path") or engine.ftcfg.estimator_state_save_path
+        if not path:
+            return JSONResponse(status_code=400, content={"error": "no path (estimator_state_save_path unset)"})
+        await et.call(lambda e: e.save_estimator_state(path))
+        return {"saved": True, "path": path}
+
+    # ------------------------------------------------------------ telemetry
+    @app.get("/system_metrics")
+    async def system_metrics():
+        m = getattr(engine, "metrics", None)
+        if m is None:
+            return JSONResponse(status_code=404, content={"error": "telemetry is off (metrics_dir unset)"})
+        return await et.call(lambda e: e.metrics.snapshot())
+
+    @app.get("/telemetry/data")
+    async def telemetry_data(steps_since: int = 0):
+        m = getattr(engine, "metrics", None)
+        if m is None:
+            return JSONResponse(status_code=404, content={"error": "telemetry is off"})
+        return await et.call(lambda e: e.metrics.data(steps_since))
+
+    @app.post("/telemetry/start")
+    async def telemetry_start(req: Request):
+        body = await body_of(req)
+        d = body.get("metrics_dir") or engine.ftcfg.metrics_dir
+        await et.call(lambda e: e.start_telemetry(d))
+        return {"started": True, "metrics_dir": d}
+
+    @app.post("/telemetry/stop")
+    async def telemetry_stop():
+        await et.call(lambda e: e.stop_telemetry())
+        return {"stopped": True}
+
+    @app.post("/telemetry/memory")
+    async def telemetry_memory(req: Request):
+        body = await body_of(req)
+        m = getattr(engine, "metrics", None)
+        if m is None:
+            return JSONResponse(status_code=404, content={"error": "telemetry is off"})
+        return await et.call(lambda e: e.metrics.memory_snapshot(body.get("dir")))
+
+    # ------------------------------------------------------------ jobs
+    @app.post("/ft_jobs")
+    async def submit_job(req: Request):
+        body = await body_of(req)
+        from ..engine.ft_job import FinetuneJobSpec
+        known = set(FinetuneJobSpec.__dataclass_fields__)
+        bad = sorted(set(body) - known)
+        if bad:
+            return JSONResponse(status_code=400, content={"error": f"unknown job key(s) {bad}"})
+        try:
+            spec = FinetuneJobSpec(**{**body, "stages": tuple(body.get("stages", ("init", "training")))})
+            job = await et.call(lambda e: e.jobs.submit(spec, e.rcfg.enable_adapter_routing))
+        except Exception as ex:
+            return JSONResponse(status_code=400, content={"error": str(ex)})
+        return job.status()
+
+    @app.get("/ft_jobs")
+    async def list_jobs():
+        return {"jobs": await et.call(lambda e: e.jobs.status())}
+
+    # ------------------------------------------------------------ adapters
+    @app.get("/adapters")
+    async def adapters():
+        def info(e):
+            out = [{"name": n, "slot": s, **{k: v for k, v in e.adapter_meta.get(n, {}).items()}}
+                   for n, s in e.adapter_slots.items()]
+            router = getattr(e, "router", None)
+            return {"loaded": out, "pool": router.pool.status() if router is not None else None}
+        return await et.call(info)
+
+    @app.get("/adapters/available")
+    async def adapters_available():
+        def avail(e):
+            names = [n for n in e.adapter_slots if not n.startswith("__")]
+            router = getattr(e, "router", None)
+            if router is not None:
+                names = sorted(set(names) | set(router.pool.names()))
+            return {"by_name": names, "routed_model": route_name}
+        return await et.call(avail)
+
+    @app.post("/adapters")
+    async def add_adapter(req: Request):
+        body = await body_of(req)
+        if not body.get("path"):
+            return JSONResponse(status_code=400, content={"error": "JSON body with 'path' required"})
+        name = body.get("name") or os.path.basename(os.path.normpath(body["path"]))
+        try:
+            def add(e):
+                router = getattr(e, "router", None)
+                if router is not None:
+                    return router.pool.add(name, body["path"], data_path=body.get("data_path"),
+                                           centroid_path=body.get("centroid_path"),
+                                           prewarm=bool(body.get("prewarm", False)))
+                return {"slot": e.load_inference_adapter(name, path=body["path"])}
+            res = await et.call(add)
+        except Exception as ex:
+            return JSONResponse(status_code=400, content={"error": str(ex)})
+        return {"name": name, "result": res}
+
+    @app.post("/adapters/{name}/{op}")
+    async def adapter_op(name: str, op: str):
+        try:
+            res = await et.call(lambda e: e.adapter_op(name, op))
+        except Exception as ex:
+            return JSONResponse(status_code=400, content={"error": str(ex)})
+        return {"name": name, "op": op, "result": res}
+
+    @app.delete("/adapters/{name}")
+    async def remove_adapter(name: str):
+        try:
+            res = await et.call(lambda e: e.adapter_op(name, "remove"))
+        except Exception as ex:
+            return JSONResponse(status_code=400, content={"error": str(ex)})
+        return {"name": name, "removed": True, "result": res}
+
+    # ------------------------------------------------------------ lifecycle
+    @app.post("/shutdown")
+    async def shutdown():
+        await et.call(lambda e: e._drain_backward())
+        await asyncio.to_thread(et.stop)
+        srv = app.state.server
+        if srv is not None:
+            srv.should_exit = True
+        return {"shutdown": True}
+
+    return app
+
+
+def _finish_reason(r) -> str:
+    if r.status.name == "ABORTED":
+        return "abort"
+    return "length" if len(r.output_ids) >= r.params.max_tokens else "stop"

@@ -1,0 +1,158 @@
+"""HTTP API, telemetry and launcher on CPU: the FastAPI app drives a tiny
+co-serving engine (fp32 oracle ops) through its own engine thread, mirroring
+the reference's API tests (``tests/test_metrics_e2e.py``,
+``tests/test_adapter_save_e2e.py``) without a model download."""
+import json
+import os
+import tempfile
+import textwrap
+import time
+
+import pytest
+from fastapi.testclient import TestClient
+
+from deltaserve_vllm_b200.adapters import peft_io
+from deltaserve_vllm_b200.config import EngineConfig, FinetuneConfig
+from deltaserve_vllm_b200.engine.ft.store import FinetuningStore
+from deltaserve_vllm_b200.engine.llm_engine import CoServingEngine
+from deltaserve_vllm_b200.server.api import create_app
+from deltaserve_vllm_b200.utils.tokenizer import ByteTokenizer
+
+
+def make_engine(tmp, start=False, **ft):
+    ecfg = EngineConfig(model="qwen3-tiny", device="cpu", max_model_len=512, block_size=16,
+                        max_num_batched_tokens=256, max_loras=3, max_lora_rank=8)
+    fcfg = FinetuneConfig(enable_finetuning=True, start_on_launch=start, max_saved_finetuning_tokens=96,
+                          learning_rate=1e-3, adapter_save_path=os.path.join(tmp, "ckpt"),
+                          metrics_dir=os.path.join(tmp, "metrics"), metrics_interval_s=0.2,
+                          step_trace_path=os.path.join(tmp, "trace.csv"), **ft)
+    store = FinetuningStore.synthetic(1024, 8, 16, 40, seed=0, max_saved_finetuning_tokens=96,
+                                      total_epochs=1000)
+    eng = CoServingEngine(ecfg, fcfg, ft_store=store, tokenizer=ByteTokenizer(1024))
+    eng.load_inference_adapter("toy", rank=8, alpha=16)
+    return eng
+
+
+def _wait(pred, timeout=60.0):
+    t0 = time.time()
+    while time.time() - t0 < timeout:
+        if pred():
+            return True
+        time.sleep(0.05)
+    return False
+
+
+def test_api_completions_and_finetuning_control():
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        app = create_app(eng)
+        with TestClient(app) as c:
+            assert c.get("/health").json()["ok"]
+            names = [m["id"] for m in c.get("/v1/models").json()["data"]]
+            assert "qwen3-tiny" in names and "toy" in names
+            r = c.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 4})
+            assert r.status_code == 200, r.text
+            out = r.json()
+            assert out["usage"]["completion_tokens"] == 4
+            assert out["usage"]["prompt_tokens"] == len("hello world")
+            assert out["metrics"]["ttft_s"] is not None
+            # adapter by name, token-id prompt
+            r = c.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 3, "model": "toy"})
+            assert r.status_code == 200 and len(r.json()["choices"][0]["token_ids"]) == 3
+            assert c.post("/v1/completions", json={"prompt": "x", "model": "nope"}).status_code == 404
+            assert c.post("/v1/completions", json={"max_tokens": 3}).status_code == 400
+            # streaming: every token arrives, then [DONE]
+            with c.stream("POST", "/v1/completions",
+                          json={"prompt": "stream me", "max_tokens": 5, "stream": True}) as s:
+                chunks = [ln for ln in s.iter_lines() if ln.startswith("data: ")]
+            assert chunks[-1] == "data: [DONE]"
+            n_tok = sum(len(json.loads(ch[6:])["choices"][0].get("token_ids") or []) for ch in chunks[:-1])
+            assert n_tok == 5
+            # finetuning: closed at launch, opened by the route, cycles complete
+            st = c.get("/finetuning_status").json()
+            assert not st["ft_started"]
+            assert c.post("/start_finetuning").json()["status"]["ft_started"]
+            assert _wait(lambda: c.get("/finetuning_status").json()["completed_cycles"] >= 1)
+            # telemetry live feed
+            snap = c.get("/system_metrics").json()
+            assert snap["totals"]["requests"] >= 3
+            data = c.get("/telemetry/data", params={"steps_since": 0}).json()
+            assert data["steps"]
+            mem = c.post("/telemetry/memory", json={}).json()
+            assert mem["weights_gb"] > 0
+            # PEFT save through the API, merged and readable
+            r = c.post("/save_adapter", json={"path": os.path.join(tmp, "manual"), "wait": True})
+            assert r.status_code == 200 and r.json()["saved"], r.text
+            tensors, cfg = peft_io.read_adapter(os.path.join(tmp, "manual"))
+            assert len(tensors) == 2 * 7 * eng.arch.num_layers
+            r = c.post("/save_estimator_state", json={"path": os.path.join(tmp, "est.json")})
+            assert r.status_code == 200
+            assert c.post("/stop_finetuning").json()["status"]["ft_started"] is False
+            # adapters: list, unload, reload by path
+            peft_io.write_peft_adapter(os.path.join(tmp, "a2"), tensors, cfg, {"save_id": "t"})
+            r = c.post("/adapters", json={"path": os.path.join(tmp, "a2")})
+            assert r.status_code == 200, r.text
+            assert "a2" in c.get("/adapters/available").json()["by_name"]
+            assert c.delete("/adapters/a2").status_code == 200
+            assert "a2" not in c.get("/adapters/available").json()["by_name"]
+            jobs = c.get("/ft_jobs").json()["jobs"]
+            assert isinstance(jobs, list)
+            assert c.post("/ft_jobs", json={"bogus": 1}).status_code == 400
+            assert c.post("/shutdown").json()["shutdown"]
+        eng.shutdown()
+        # telemetry files on disk
+        mdir = os.path.join(tmp, "metrics")
+        assert os.path.exists(os.path.join(mdir, "requests.csv"))
+        with open(os.path.join(mdir, "requests.csv")) as f:
+            assert len(f.read().strip().splitlines()) >= 4
+        with open(os.path.join(tmp, "trace.csv")) as f:
+            lines = f.read().strip().splitlines()
+        assert lines[0].startswith("seq,kind") and len(lines) > 2
+        with open(os.path.join(tmp, "est.json")) as f:
+            st = json.load(f)
+        assert st["version"] == 1 and st["tracker"]["samples"]
+
+
+def test_estimator_state_round_trip():
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "est.json")
+        eng = make_engine(tmp, estimator_state_save_path=path)
+        eng.profile_execution_model(repeats=1)
+        assert eng.estimator.is_ready
+        eng.shutdown()                      # saves once at shutdown
+        with open(path) as f:
+            saved = json.load(f)
+        eng2 = make_engine(tmp, estimator_state_load_path=path, profile_num_repeats=1)
+        eng2.profile_execution_model(shapes=[], repeats=1)
+        assert eng2.tracker.size() == len(saved["tracker"]["samples"])
+        assert eng2.estimator.export_state()["params"] == saved["estimator"]["params"]
+        # a missing file is a warning, not an error
+        assert not eng2.load_estimator_state(os.path.join(tmp, "missing.json"))
+
+
+def test_launcher_dry_run(capsys):
+    from deltaserve_vllm_b200 import launch
+    with tempfile.TemporaryDirectory() as tmp:
+        cfg = os.path.join(tmp, "c.yaml")
+        with open(cfg, "w") as f:
+            f.write(textwrap.dedent("""
+                finetune_param:
+                  enable_finetuning: true
+                  data_path: data.txt
+                  max_saved_finetuning_tokens: 256
+                slo:
+                  ttft_slo: 0.5
+                server:
+                  host: 127.0.0.1
+                  port: 8123
+                model:
+                  model: qwen3-tiny
+                parallel:
+                  tensor_parallel_size: 1
+            """))
+        assert launch.main(["--config", cfg, "--dry-run", "--tp", "2", "--port", "9000"]) == 0
+        out = json.loads(capsys.readouterr().out)
+        assert out["engine"]["tensor_parallel_size"] == 2
+        assert out["server"]["port"] == 9000
+        assert out["finetune"]["data_path"] == os.path.join(os.path.realpath(tmp), "data.txt")
+        assert out["finetune"]["ttft_slo"] == 0.5
