@@ -185,7 +185,8 @@ def main():
                                       max_saved_finetuning_tokens=cap, total_epochs=1000)
     t0 = time.perf_counter()
     eng = CoServingEngine(ecfg, fcfg, comm=comm, arch=arch, ft_store=store)
-    eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
+    if rank == 0:   # replayed on the other ranks
+        eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
     if rank != 0:
         eng.follow()
         eng.close()

@@ -1,0 +1,215 @@
+"""Adapter routing inside the engine: pool + router + the engine's LoRA slots.
+
+Requests for the routing model name (or for a pool adapter by name) go
+through :meth:`AdapterRouter.submit`, which queues them. At the start of
+every engine step :meth:`AdapterRouter.tick` runs the *encode step*: all
+queued texts are embedded in one encoder call, decided, and each request
+either enters the scheduler at once (base model, or its adapter already holds
+a GPU slot) or is *held* until the pool can give its adapter a slot (evicting
+the least-used slot holder that no running request uses). The request keeps
+its real arrival time throughout, so TTFT includes the hold.
+
+Reference: ``deltaserve-plugin/deltaserve/adapter_routing/engine.py:37-391``
+and ``engine_router.py:178-380`` (held routed requests, encode step, slot
+placement), re-built around this engine's own slot table.
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import os
+import time
+from collections import deque
+
+from ... import dprint
+from .. import peft_io
+from .encoder import SentenceEncoder, encoder_identity, make_encoder
+from .index import CentroidIndex
+from .indexing import index_dir, start_indexing, store_centroid
+from .pool import GPU, AdapterPool
+from .router import NO_TEXT, RouteDecision, Router
+
+
+class EngineSlotBackend:
+    """Pool tiers mapped onto the engine: ``cpu`` = host tensors read from
+    the PEFT directory, ``gpu`` = a LoRA slot of the engine."""
+
+    def __init__(self, engine):
+        self.eng = engine
+        self.host: dict[str, tuple] = {}
+
+    def load(self, e) -> None:
+        tensors, acfg = peft_io.read_adapter(e.path)
+        rank, alpha = peft_io.adapter_rank_alpha(acfg)
+        self.host[e.name] = (tensors, rank, alpha)
+
+    def activate(self, e) -> None:
+        if e.name not in self.host:
+            self.load(e)
+        tensors, rank, alpha = self.host[e.name]
+        self.eng.load_inference_adapter(e.name, path=e.path, tensors=tensors, rank=rank, alpha=alpha)
+
+    def deactivate(self, e) -> None:
+        if e.name in self.eng.adapter_slots:
+            self.eng.unload_inference_adapter(e.name)
+
+    def unload(self, e) -> None:
+        self.host.pop(e.name, None)
+
+
+class AdapterRouter:
+    def __init__(self, engine, cfg, backend=None):
+        self.eng, self.cfg = engine, cfg
+        dev = str(engine.device) if getattr(engine, "cuda", False) else "cpu"
+        self.encoder = make_encoder(cfg, dev)
+        # Indexing runs on a host thread; an HF encoder gets its own CPU copy.
+        self.index_encoder = (make_encoder(cfg, "cpu") if isinstance(self.encoder, SentenceEncoder)
+                              else self.encoder)
+        self.enc_id = encoder_identity(self.encoder)
+        self.dir = index_dir(cfg)
+        used = set(engine.adapter_slots.values())
+        free = (engine.lora.slots - len(used)) if engine.lora is not None else 0
+        if free < 1:
+            raise RuntimeError("adapter routing needs at least one free LoRA slot (raise max_loras)")
+        self.pool = AdapterPool(
+            backend or EngineSlotBackend(engine),
+            CentroidIndex(self.enc_id, cfg.encoder_query_prefix, cfg.encoder_max_tokens),
+            capacity=cfg.max_active_adapters, gpu_slots=free, protected=cfg.pool_protected_slots,
+            half_life_s=cfg.pool_hit_half_life_s, directory=os.path.join(self.dir, "pool"),
+            when_full=cfg.when_full, grace_s=cfg.retire_grace_s, min_pool=cfg.route_min_pool,
+            min_self_recall=cfg.admission_min_self_recall, max_stolen=cfg.admission_max_stolen)
+        log = os.path.join(self.dir, "decisions.jsonl") if cfg.route_decision_log else None
+        self.router = Router(self.encoder, cfg.route_keep_percent, cfg.route_close_band, cfg.route_min_pool,
+                             cfg.route_confidence_slack, cfg.fallback_score_threshold, log,
+                             tier_of=lambda n: self.pool.entries[n].tier if n in self.pool.entries else "")
+        self.pool.listeners.append(lambda p: self.router.set_index(p.index))
+        self.pending: deque = deque()   # (rid, ids, params, text, adapter, arrival, future)
+        self.held: deque = deque()      # (rid, ids, params, adapter, arrival)
+        self.indexing: dict[str, tuple] = {}     # name -> (runner, path, fingerprint)
+        self.stats = {"routed": 0, "fallback": 0, "held": 0, "encode_calls": 0, "encode_ms": 0.0}
+        for a in cfg.adapters or []:
+            self.add(a.get("name") or os.path.basename(os.path.normpath(a["path"])), a["path"],
+                     data_path=a.get("data_path"), centroid_path=a.get("centroid_path"),
+                     prewarm=bool(a.get("prewarm", False)))
+
+    # ------------------------------------------------------------ pool entry
+    def add(self, name: str, path: str, data_path: str | None = None, centroid_path: str | None = None,
+            prewarm: bool = False) -> dict:
+        """Put an adapter in the pool: with a saved centroid it is admitted
+        at once; with a dataset it is indexed in the background (servable by
+        name meanwhile) and admitted when the centroid is ready."""
+        if centroid_path:
+            idx = CentroidIndex.load(centroid_path)
+            src = name if name in idx else (idx.names[0] if len(idx) == 1 else None)
+            if src is None:
+                raise KeyError(f"{centroid_path} has no centroid for '{name}'")
+            return self.pool.admit(name, path, idx.centroid_of(src), idx.refs.get(src), load=True,
+                                   prewarm=prewarm)
+        if name not in self.pool:
+            self.pool.register(name, path, load=True, prewarm=prewarm)
+        if data_path:
+            return self.start_indexing(name, path, data_path)
+        return {"name": name, "level": self.pool.entries[name].level, "indexed": False}
+
+    def start_indexing(self, name: str, path: str, data_path: str) -> dict:
+        runner, hit, fp = start_indexing(self.cfg, self.index_encoder, self.enc_id, name, data_path,
+                                         busy=self.eng.has_unfinished)
+        if hit is not None:
+            return self.pool.admit(name, path, hit[0], hit[1], load=True)
+        self.indexing[name] = (runner, path, fp)
+        return {"name": name, "indexing": runner.describe()}
+
+    def _poll_indexing(self) -> None:
+        for name, (runner, path, fp) in list(self.indexing.items()):
+            if runner.error:
+                dprint(f"[indexing] {name} failed: {runner.error}")
+                del self.indexing[name]
+            elif runner.done:
+                del self.indexing[name]
+                c, r = runner.indexer.centroid(), runner.indexer.references()
+                store_centroid(self.dir, name, fp, c, r, self.enc_id, self.cfg.encoder_query_prefix,
+                               self.cfg.encoder_max_tokens)
+                if name in self.pool:
+                    self.pool.admit(name, path, c, r)
+
+    def centroid_ready(self, name: str) -> bool:
+        e = self.pool.entries.get(name)
+        return e is not None and e.centroid is not None
+
+    def names(self) -> list[str]:
+        return self.pool.names()
+
+    # ------------------------------------------------------------ requests
+    def submit(self, rid: str, ids: list[int], params, text: str | None = None,
+               adapter: str | None = None, arrival: float | None = None) -> cf.Future:
+        """Queue a routed request (``adapter`` None: decide from ``text``) or
+        a request naming a pool adapter. The future resolves with the
+        :class:`RouteDecision` at the next encode step."""
+        fut: cf.Future = cf.Future()
+        self.pending.append((rid, list(ids), params, text, adapter,
+                             arrival if arrival is not None else time.perf_counter(), fut))
+        self.eng.arrival_flag = True
+        return fut
+
+    def has_pending(self) -> bool:
+        return bool(self.pending or self.held)
+
+    def _in_use(self) -> set[str]:
+        return {r.adapter for r in self.eng.requests.values() if r.adapter}
+
+    def _enter(self, rid, ids, params, adapter, arrival) -> None:
+        self.eng.add_request(rid, ids, params, adapter, arrival_time=arrival)
+
+    def tick(self) -> None:
+        """The encode step plus slot placement; runs on the engine thread."""
+        if self.indexing:
+            self._poll_indexing()
+        if self.pending:
+            batch = list(self.pending)
+            self.pending.clear()
+            texts = [b[3] for b in batch if b[4] is None]
+            t0 = time.perf_counter()
+            decisions = iter(self.router.route_many(texts)) if texts else iter(())
+            if texts:
+                self.stats["encode_calls"] += 1
+                self.stats["encode_ms"] += (time.perf_counter() - t0) * 1e3
+            for rid, ids, params, text, named, arrival, fut in batch:
+                d = RouteDecision(named) if named is not None else next(decisions)
+                try:
+                    if d.adapter is None:
+                        self.stats["fallback"] += 1
+                        self._enter(rid, ids, params, None, arrival)
+                    else:
+                        self.stats["routed"] += 1
+                        self.pool.note_hit(d.adapter, self._in_use(), place=True)
+                        if self.pool.entries[d.adapter].tier == GPU:
+                            self._enter(rid, ids, params, d.adapter, arrival)
+                        else:
+                            self.stats["held"] += 1
+                            self.held.append((rid, ids, params, d.adapter, arrival))
+                    fut.set_result(d)
+                except Exception as e:  # reported to the HTTP handler
+                    fut.set_exception(e)
+        if self.held:
+            keep = deque()
+            while self.held:
+                rid, ids, params, adapter, arrival = self.held.popleft()
+                if adapter not in self.pool:
+                    self._enter(rid, ids, params, None, arrival)        # removed meanwhile
+                elif self.pool.ensure_gpu(adapter, self._in_use()):
+                    self._enter(rid, ids, params, adapter, arrival)
+                else:
+                    keep.append((rid, ids, params, adapter, arrival))
+            self.held = keep
+
+    def status(self) -> dict:
+        return {"pool": self.pool.status(), "model": self.router.model.describe(),
+                "pending": len(self.pending), "held": len(self.held), "stats": dict(self.stats),
+                "indexing": {n: r.describe() for n, (r, _, _) in self.indexing.items()}}
+
+    def stop(self) -> None:
+        for runner, _, _ in self.indexing.values():
+            runner.stop()
+
+
+NO_TEXT_DECISION = RouteDecision(None, None, NO_TEXT)

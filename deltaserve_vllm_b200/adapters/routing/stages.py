@@ -1,0 +1,77 @@
+"""Finetuning-job stages that exist only with adapter routing on (importing
+this module registers them):
+
+* ``indexing``  — build the job adapter's centroid from the job's dataset
+  next to training (cached by dataset + encoder fingerprint);
+* ``admission`` — after training: save the trained adapter as PEFT, then
+  admit it to the pool (compared with the active set; the pool keeps serving
+  throughout and a failed admission leaves it unchanged).
+
+Reference: ``deltaserve-plugin/deltaserve/adapter_routing/stages.py:122-244``.
+"""
+
+from __future__ import annotations
+
+import os
+
+from ...engine.ft_job import Stage, register_stage
+from .indexing import store_centroid
+
+
+@register_stage
+class IndexingStage(Stage):
+    name = "indexing"
+
+    def requirements(self, names):
+        return ("init",) if "init" in names else ()
+
+    def start(self, job, ctx) -> None:
+        router = getattr(ctx, "router", None)
+        if router is None:
+            raise RuntimeError("adapter routing is not running")
+        if not job.spec.data_path:
+            raise RuntimeError("the job has no dataset to index")
+        from .indexing import start_indexing
+        runner, hit, fp = start_indexing(router.cfg, router.index_encoder, router.enc_id, job.spec.name,
+                                         job.spec.data_path, busy=ctx.has_unfinished)
+        job.data["indexing"] = (router, runner, hit, fp)
+
+    def poll(self, job, ctx) -> bool:
+        router, runner, hit, fp = job.data["indexing"]
+        if hit is not None:
+            job.data["centroid"] = hit
+            return True
+        if runner.error:
+            raise RuntimeError(runner.error)
+        if not runner.done:
+            return False
+        c, r = runner.indexer.centroid(), runner.indexer.references()
+        store_centroid(router.dir, job.spec.name, fp, c, r, router.enc_id,
+                       router.cfg.encoder_query_prefix, router.cfg.encoder_max_tokens)
+        job.data["centroid"] = (c, r)
+        return True
+
+
+@register_stage
+class AdmissionStage(Stage):
+    name = "admission"
+
+    def requirements(self, names):
+        return tuple(s for s in names if s not in (self.name, "ready"))
+
+    def start(self, job, ctx) -> None:
+        router = getattr(ctx, "router", None)
+        if router is None:
+            raise RuntimeError("adapter routing is not running")
+        path = job.spec.save_path or job.spec.adapter_path
+        if "training" in job.spec.stages:
+            root = job.spec.save_path or os.path.join(ctx.ftcfg.adapter_save_path or router.dir,
+                                                      f"job-{job.spec.name}")
+            path = ctx.save_adapter(root, save_id=f"job-{job.job_id}")
+        if not path:
+            raise RuntimeError("the job has no adapter to admit (no save_path / adapter_path)")
+        c, r = job.data.get("centroid") or (None, None)
+        job.report = router.pool.admit(job.spec.name, path, c, r, job=job.spec.name, load=True)
+
+    def poll(self, job, ctx) -> bool:
+        return True

@@ -49,11 +49,16 @@ def load_gated_stages(adapter_routing: bool) -> None:
 
 @register_stage
 class InitStage(Stage):
-    """Adapter weights loaded and dataset tokenized (both happen at engine
-    start); the stage only checks the dataset is there."""
+    """The job's adapter weights and dataset are in place. The launch job's
+    were loaded at engine start; a later job switches the trainer (adapter
+    init, optimiser settings) and the corpus once the previous job's samples
+    have all been trained (``ctx.begin_job`` returns False until then)."""
     name = "init"
 
     def poll(self, job, ctx) -> bool:
+        begin = getattr(ctx, "begin_job", None)
+        if begin is not None and not begin(job):
+            return False
         store = getattr(ctx, "store", None)
         return store is None or len(store) > 0
 
@@ -141,8 +146,9 @@ class FinetuneJobSpec:
             for req in _STAGES[s]().requirements(self.stages):
                 if req not in self.stages:
                     raise ValueError(f"stage '{s}' needs stage '{req}'")
-        if self.adapter_init not in (None, "random", "zeros") and not self.adapter_path:
-            raise ValueError("ft_job.adapter_init must be 'random' or 'zeros'")
+        if self.adapter_init not in (None, "from_path", "random"):
+            raise ValueError(f"ft_job.adapter_init '{self.adapter_init}' is not supported; "
+                             "available: ['from_path', 'random']")
 
 
 @dataclass
@@ -155,6 +161,9 @@ class FinetuneJob:
     started: float | None = None
     finished: float | None = None
     error: str | None = None
+    # Per-stage working state (stage objects are re-created every tick).
+    data: dict = field(default_factory=dict)
+    report: dict | None = None
 
     def status(self) -> dict:
         return {"job_id": self.job_id, "name": self.spec.name, "state": self.state,

@@ -137,8 +137,12 @@ class CoServingEngine:
             self.adapter_slots[FT_ADAPTER_NAME] = self.ft_slot
             self.runner.ft_slot = self.ft_slot
             self._init_finetuning(ft_adapter)
+        # Every rank builds with the same constructor adapters; later loads
+        # are made by the driver and replayed by the followers.
+        self._replicate = False
         for name, spec in (adapters or {}).items():
             self.load_inference_adapter(name, **spec)
+        self._replicate = True
         # ---- streams: forward high priority, backward low priority
         if self.cuda:
             self.fwd_stream = torch.cuda.Stream(self.device, priority=-2)
@@ -174,6 +178,7 @@ class CoServingEngine:
         self.metrics = None
         self.step_trace = None
         self.router = None
+        self._job_owner = None
         if self.is_driver and (self.ftcfg.metrics_dir or self.ftcfg.step_trace_path):
             self.start_telemetry(self.ftcfg.metrics_dir)
 
@@ -234,6 +239,63 @@ class CoServingEngine:
                                            self.ecfg.max_num_batched_tokens, self.tbt_window)
         self.jobs.submit(FinetuneJobSpec.from_finetune_config(cfg), self.rcfg.enable_adapter_routing)
 
+    def begin_job(self, job) -> bool:
+        """Switch finetuning to ``job`` (its init stage). The launch job is
+        already loaded. A later job waits until nothing of the previous one is
+        in flight, then re-initialises the trainable adapter (its PEFT
+        directory, or ``adapter_init`` random/zeros) with the job's optimiser
+        settings and loads its corpus. The adapter rank stays the trainer's:
+        the masters, graphs and slot keep their shapes."""
+        if job.data.get("begun"):
+            return True
+        if self._job_owner is None:
+            self._job_owner = job.job_id
+            job.data["begun"] = True
+            return True
+        if (self.coord.fill_count or self.coord.reserved_fill or self.coord.pending_backward
+                or self.bwd_active or self._bwd_done_evt is not None):
+            return False
+        spec = job.spec
+        if spec.adapter_path and os.path.isdir(spec.adapter_path):
+            from ..adapters import peft_io
+            _, acfg = peft_io.read_adapter(spec.adapter_path)
+            r, _ = peft_io.adapter_rank_alpha(acfg)
+            if r != self.trainer.rank_r:
+                raise ValueError(f"job adapter rank {r} != the trainer's rank {self.trainer.rank_r}")
+        action = ("job", spec.adapter_path, spec.adapter_init, spec.learning_rate, spec.weight_decay,
+                  spec.gamma, self.ecfg.seed + 1 + job.job_id)
+        if self.tp_size > 1:
+            self._record(action)
+            self._flush_actions()
+        self._apply_job(*action[1:])
+        tok = self.tokenizer.encode if self.tokenizer is not None else None
+        store = FinetuningStore(spec.data_path, tok, FT_ADAPTER_NAME, spec.num_epochs,
+                                self.ftcfg.max_saved_finetuning_tokens, self.ftcfg.max_prepare)
+        if spec.data_path:
+            store.load()
+        self.store = self.admission.store = store
+        self.coord.min_sample_len = max(1, store.min_len() or 1)
+        self._job_owner = job.job_id
+        job.data["begun"] = True
+        dprint(f"[ft-job] {spec.name}: {len(store)} samples, lr {spec.learning_rate}")
+        return True
+
+    def _apply_job(self, adapter_path, adapter_init, lr, wd, gamma, seed) -> None:
+        tr = self.trainer
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        if adapter_path and os.path.isdir(adapter_path):
+            from ..adapters import peft_io
+            tensors, acfg = peft_io.read_adapter(adapter_path)
+            tr.load_adapter(tensors, *peft_io.adapter_rank_alpha(acfg))
+        else:                  # no checkpoint: PEFT init (A random, B zero)
+            tr.init_random(seed)
+        tr.lr, tr.wd, tr.gamma = lr, wd, gamma
+        tr.epoch, tr.total_tokens, tr.losses = 0, 0, []
+        tr.publish()
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+
     def model_cos_sin(self):
         from ..ops.reference import rope_cos_sin_table
         return rope_cos_sin_table(max(self.arch.max_position, 8192), self.arch.head_dim,
@@ -242,7 +304,9 @@ class CoServingEngine:
     def load_inference_adapter(self, name: str, path: str | None = None, tensors=None,
                                rank: int | None = None, alpha: float | None = None,
                                seed: int | None = None) -> int:
-        """Put an inference LoRA into a free slot (PEFT dir, tensors, or random)."""
+        """Put an inference LoRA into a free slot (PEFT dir, tensors, or random).
+        With TP the driver records the load so every rank writes the same
+        slot at the same point of the step sequence."""
         from ..adapters import peft_io
         if self.lora is None:
             raise RuntimeError("LoRA is disabled (enable_lora: false)")
@@ -253,20 +317,64 @@ class CoServingEngine:
         if not free:
             raise RuntimeError("no free LoRA slot (raise max_loras)")
         slot = free[0]
-        if path is not None:
+        explicit = tensors is not None
+        if tensors is None and path is not None:
             tensors, acfg = peft_io.read_adapter(path)
             rank, alpha = peft_io.adapter_rank_alpha(acfg)
         elif tensors is None:
             rank = rank or self.ecfg.max_lora_rank
             alpha = alpha if alpha is not None else 2.0 * rank
-            tensors = random_adapter(self.arch, rank, seed if seed is not None else 1000 + slot)
-        self.lora.load_slot(slot, tensors, rank, alpha)
-        if self.cuda:
-            # Written on the current stream; forwards run on their own stream.
-            torch.cuda.synchronize(self.device)
+            seed = seed if seed is not None else 1000 + slot
+            tensors = random_adapter(self.arch, rank, seed)
+        if self.is_driver and self.tp_size > 1 and self._replicate:
+            # Followers re-read the PEFT directory or regenerate the seeded
+            # adapter; only tensors with neither source travel in the action.
+            payload = None if (path is not None or not explicit) else tensors
+            self._record(("adapter_load", slot, path, rank, alpha, seed, payload))
+            self._flush_actions()
+        self._write_slot(slot, tensors, rank, alpha)
         self.adapter_slots[name] = slot
         self.adapter_meta[name] = {"rank": rank, "alpha": alpha, "path": path}
         return slot
+
+    def _write_slot(self, slot: int, tensors, rank: int, alpha: float) -> None:
+        if self.cuda:
+            # In-flight forwards may read other slots of the same buffers;
+            # the write goes after everything queued so far.
+            torch.cuda.synchronize(self.device)
+        self.lora.load_slot(slot, tensors, rank, alpha)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+
+    def unload_inference_adapter(self, name: str) -> int:
+        if name == FT_ADAPTER_NAME:
+            raise ValueError("the trainable adapter cannot be unloaded")
+        slot = self.adapter_slots.pop(name, None)
+        if slot is None:
+            raise KeyError(f"adapter {name!r} is not loaded")
+        if self.is_driver and self.tp_size > 1 and self._replicate:
+            self._record(("adapter_clear", slot))
+            self._flush_actions()
+        self._clear_slot(slot)
+        self.adapter_meta.pop(name, None)
+        return slot
+
+    def _clear_slot(self, slot: int) -> None:
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        self.lora.clear_slot(slot)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+
+    def _save_trainer(self, path: str, save_id: str = "", extra: dict | None = None) -> str | None:
+        """PEFT save of the trained adapter, merged across TP ranks (every
+        rank takes part in the gather, so the driver records it first)."""
+        if self.is_driver and self.tp_size > 1:
+            self._record(("save",))
+            self._flush_actions()
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
+        return self.trainer.save_adapter(path, save_id, extra)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_ids: list[int], params: SamplingParams | None = None,
@@ -290,7 +398,7 @@ class CoServingEngine:
         return r is not None
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_unfinished()
+        return self.scheduler.has_unfinished() or (self.router is not None and self.router.has_pending())
 
     # ------------------------------------------------------------------ control
     def start_finetuning(self) -> None:
@@ -317,7 +425,7 @@ class CoServingEngine:
                 raise ValueError("no path given and finetune_param.adapter_save_path is unset")
             path = os.path.join(self.ftcfg.adapter_save_path, f"manual-{int(time.time())}")
         self._drain_backward()
-        return self.trainer.save_adapter(path, save_id)
+        return self._save_trainer(path, save_id)
 
     # ------------------------------------------------------------------ estimator state
     def save_estimator_state(self, path: str | None = None) -> str | None:
@@ -386,23 +494,13 @@ class CoServingEngine:
     # ------------------------------------------------------------------ adapters
     def adapter_op(self, name: str, op: str):
         """Adapter lifecycle by name. With adapter routing the pool owns the
-        lifecycle (``load``/``unload``/``pin``/``unpin``/``remove``/``prewarm``);
-        without it ``unload``/``remove`` free the slot and ``load`` re-reads
-        the adapter's path."""
-        if self.router is not None:
+        lifecycle (``load``/``offload``/``retire``/``reactivate``/``pin``/
+        ``unpin``/``remove``); without it ``unload``/``remove`` free the slot
+        and ``load`` re-reads the adapter's path."""
+        if self.router is not None and name in self.router.pool:
             return self.router.pool.op(name, op)
-        if name == FT_ADAPTER_NAME:
-            raise ValueError("the trainable adapter cannot be managed by name")
         if op in ("unload", "remove"):
-            slot = self.adapter_slots.pop(name, None)
-            if slot is None:
-                raise KeyError(f"adapter {name!r} is not loaded")
-            self._drain_backward()
-            if self.cuda:
-                torch.cuda.synchronize(self.device)
-            self.lora.clear_slot(slot)
-            self.adapter_meta.pop(name, None)
-            return {"slot": slot}
+            return {"slot": self.unload_inference_adapter(name)}
         if op == "load":
             meta = self.adapter_meta.get(name) or {}
             if not meta.get("path"):
@@ -441,6 +539,8 @@ class CoServingEngine:
         self.step_no += 1
         self._drain_timing()
         self._poll_backward()
+        if self.router is not None:
+            self.router.tick()          # encode step + slot placement of routed requests
         cfg = self.ftcfg
         if self.ft_enabled:
             if cfg.rps_throttle_enable:
@@ -644,11 +744,11 @@ class CoServingEngine:
         from ..adapters import peft_io
         st = self.trainer.step
         if cfg.adapter_save_every_backwards > 0 and st % cfg.adapter_save_every_backwards == 0:
-            self.trainer.save_adapter(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"))
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"))
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
         if cfg.adapter_save_every_epoch and getattr(self, "_epoch_ended", False):
             ep = self.store.current_epoch if self.store else 0
-            self.trainer.save_adapter(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"))
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"))
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last, prefix="epoch-")
         self._epoch_ended = False
 
@@ -875,6 +975,28 @@ class CoServingEngine:
                     self.marks["__region__"] = self.region_ms(a[1], a[2])
                     self.comm.gather_objects(self.marks)
                     continue
+                if kind == "save":
+                    if self.cuda:
+                        torch.cuda.synchronize(self.device)
+                    self.trainer.export_full()
+                    continue
+                if kind == "adapter_load":
+                    _, slot, path, rank, alpha, seed, payload = a
+                    if payload is not None:
+                        tensors = payload
+                    elif path is not None:
+                        from ..adapters import peft_io
+                        tensors, _ = peft_io.read_adapter(path)
+                    else:
+                        tensors = random_adapter(self.arch, rank, seed)
+                    self._write_slot(slot, tensors, rank, alpha)
+                    continue
+                if kind == "adapter_clear":
+                    self._clear_slot(a[1])
+                    continue
+                if kind == "job":
+                    self._apply_job(*a[1:])
+                    continue
                 if kind == "fwd":
                     _, arr, spans, meta, has_ft = a
                     from .model_runner import _Packer
@@ -917,6 +1039,15 @@ class CoServingEngine:
             torch.cuda.synchronize(self.device)
 
     # ------------------------------------------------------------------ helpers
+    def idle_tick(self) -> None:
+        """Housekeeping while no step runs: job stages (indexing, admission,
+        the next job's init) and routing placement still advance."""
+        self._poll_backward()
+        if self.ft_enabled:
+            self.jobs.tick(self)
+        if self.router is not None:
+            self.router.tick()
+
     def has_ft_work(self) -> bool:
         c = self.coord
         if not self.ft_enabled or c.disabled:

@@ -33,6 +33,7 @@ import uuid
 from fastapi import FastAPI, Request
 from fastapi.responses import JSONResponse, StreamingResponse
 
+from ..adapters.routing.router import DISABLED, RouteDecision, extract_text
 from ..engine.request import SamplingParams
 from .engine_thread import EngineThread
 
@@ -61,7 +62,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     if tok is None:
         from ..utils.tokenizer import ByteTokenizer
         tok = ByteTokenizer(engine.arch.vocab)
-    route_name = engine.rcfg.route_model_name if engine.rcfg.enable_adapter_routing else None
+    route_name = engine.rcfg.route_model_name if engine.router is not None else None
 
     async def body_of(req: Request) -> dict:
         try:
@@ -77,6 +78,8 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     @app.get("/v1/models")
     async def models():
         names = [model_name] + [n for n in engine.adapter_slots if not n.startswith("__")]
+        if engine.router is not None:
+            names += [n for n in engine.router.pool.names() if n not in names]
         if route_name:
             names.append(route_name)
         return {"object": "list", "data": [{"id": n, "object": "model", "owned_by": "deltaserve"}
@@ -99,30 +102,40 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         if not ids:
             return JSONResponse(status_code=400, content={"error": "empty prompt"})
         model = body.get("model") or model_name
-        adapter = None
-        headers = {}
-        if route_name and model == route_name:
-            router = getattr(engine, "router", None)
-            if router is None:
-                return JSONResponse(status_code=503, content={"error": "adapter routing is not running"})
-            text = body.get("prompt") if isinstance(body.get("prompt"), str) else tok.decode(ids)
-            dec = await et.call(lambda e: e.router.route(text))
-            adapter = dec.adapter
-            headers = dec.headers()
-        elif model != model_name:
-            if model not in engine.adapter_slots:
-                return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
-            adapter = model
         params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
                                 temperature=float(body.get("temperature", 0.0) or 0.0),
                                 seed=body.get("seed"), ignore_eos=bool(body.get("ignore_eos", False)),
                                 stop_token_ids=tuple(body.get("stop_token_ids") or ()))
         rid = f"cmpl-{uuid.uuid4().hex[:24]}"
         stream = bool(body.get("stream", False))
+        router = engine.router
+        headers = {}
+        routed = named_pool = False
+        adapter = None
+        if model == engine.rcfg.route_model_name and router is None:
+            # Routing is off: the base model serves it, and the headers say so.
+            headers = RouteDecision(None, None, DISABLED).headers()
+        elif model == engine.rcfg.route_model_name:
+            routed = True
+        elif model != model_name:
+            if model in engine.adapter_slots:
+                adapter = model
+            elif router is not None and model in router.pool:
+                named_pool = True
+            else:
+                return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
         w = et.register(rid, stream)
         et.notify_arrival()
         try:
-            await et.call(lambda e: e.add_request(rid, ids, params, adapter))
+            if routed or named_pool:
+                text = extract_text(body) if routed else None
+                fut = await et.call(lambda e: e.router.submit(rid, ids, params, text=text,
+                                                              adapter=None if routed else model))
+                decision = await asyncio.wrap_future(fut)
+                if routed:
+                    headers = decision.headers()
+            else:
+                await et.call(lambda e: e.add_request(rid, ids, params, adapter))
         except Exception as e:
             et.unregister(rid)
             return JSONResponse(status_code=400, content={"error": str(e)})
@@ -294,7 +307,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             def add(e):
                 router = getattr(e, "router", None)
                 if router is not None:
-                    return router.pool.add(name, body["path"], data_path=body.get("data_path"),
+                    return router.add(name, body["path"], data_path=body.get("data_path"),
                                            centroid_path=body.get("centroid_path"),
                                            prewarm=bool(body.get("prewarm", False)))
                 return {"slot": e.load_inference_adapter(name, path=body["path"])}

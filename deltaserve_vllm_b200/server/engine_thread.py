@@ -44,6 +44,7 @@ class EngineThread:
         self.steps = 0
         engine.request_listeners.append(self._on_request_event)
         self._streamed: dict[str, int] = {}
+        self._last_idle_tick = 0.0
 
     # ------------------------------------------------------------ lifecycle
     def start(self) -> None:
@@ -126,6 +127,10 @@ class EngineThread:
                     if any(w.tokens is not None for w in self._waiters.values()):
                         self._stream_progress()
                 else:
+                    now = time.monotonic()
+                    if now - self._last_idle_tick >= 0.01:
+                        self._last_idle_tick = now
+                        eng.idle_tick()
                     time.sleep(self.idle_sleep_s)
             except BaseException:
                 self.error = traceback.format_exc()

@@ -35,11 +35,11 @@ def _worker(rank, world, port, outdir):
     fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=96, learning_rate=1e-3)
     store = FinetuningStore.synthetic(1024, 10, 16, 40, seed=0, max_saved_finetuning_tokens=96)
     eng = CoServingEngine(ecfg, fcfg, comm=comm, ft_store=store)
-    eng.load_inference_adapter("inf", rank=8, alpha=16)
     try:
         if rank != 0:
             eng.follow()
             return
+        eng.load_inference_adapter("inf", rank=8, alpha=16)     # replayed on rank 1
         eng.profile_execution_model(repeats=1, max_shapes=6)
         g = torch.Generator().manual_seed(0)
         for i in range(5):
@@ -49,10 +49,18 @@ def _worker(rank, world, port, outdir):
         eng.mark("a")
         eng.mark("b")
         regions = eng.gather_region("a", "b")
+        # TP-merged PEFT save (both ranks join the gather), then serve the
+        # saved adapter from disk in a freshly loaded slot on both ranks.
+        ck = eng.save_adapter(os.path.join(outdir, "ck"), save_id="s1")
+        eng.unload_inference_adapter("inf")
+        eng.load_inference_adapter("trained", path=ck)
+        eng.add_request("t0", list(range(5, 40)), SamplingParams(max_tokens=3), adapter="trained")
+        eng.run_until_idle(max_steps=200, finetune=False)
         eng.shutdown()
         torch.save({"cycles": eng.coord.completed_cycles, "losses": eng.trainer.losses,
                     "outs": sorted(len(r.output_ids) for r in eng.finished if r.request_id.startswith("r")),
-                    "regions": regions}, os.path.join(outdir, "res.pt"))
+                    "t0": [len(r.output_ids) for r in eng.finished if r.request_id == "t0"],
+                    "ck": ck, "regions": regions}, os.path.join(outdir, "res.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -65,3 +73,11 @@ def test_tp2_engine_protocol_gloo():
         assert all(l == l for l in r["losses"])
         assert r["outs"] == [4] * 5
         assert len(r["regions"]) == 2
+        assert r["t0"] == [3]
+        from deltaserve_vllm_b200.adapters import peft_io
+        tensors, cfg = peft_io.read_adapter(r["ck"])
+        from deltaserve_vllm_b200.models.configs import resolve_arch
+        arch = resolve_arch("qwen3-tiny")
+        assert len(tensors) == 2 * 7 * arch.num_layers
+        q_b = [v for k, v in tensors.items() if "q_proj.lora_B" in k][0]
+        assert q_b.shape[0] == arch.num_heads * arch.head_dim      # merged across ranks
