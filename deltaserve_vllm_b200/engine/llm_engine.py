@@ -104,6 +104,13 @@ class CoServingEngine:
         cap_tokens = self.ftcfg.max_saved_finetuning_tokens
         self.capture = (CaptureBuffers.allocate(self.weights, cap_tokens + 8, self.device, self.dtype)
                         if self.ft_enabled else None)
+        # ---- fused GEMM + all-reduce workspace (row-parallel o / down under TP)
+        self.peer_ws = None
+        if self.cuda and comm is not None and comm.size > 1 and ecfg.tp_comm == "fused":
+            from ..parallel.peer import PeerWorkspace
+            rows = ecfg.max_num_batched_tokens + (cap_tokens if self.ft_enabled else 0) + 128
+            self.peer_ws = PeerWorkspace(comm, rows, self.arch.hidden)
+            comm.peer_ws = self.peer_ws
         # ---- KV cache sized from what is left
         self.kv = self._alloc_kv()
         self.model = DecoderModel(self.weights, self.kv.k, self.kv.v, self.lora, comm)
@@ -900,6 +907,11 @@ class CoServingEngine:
             self.trainer.release_graphs()
         if self.cuda:
             torch.cuda.synchronize(self.device)
+        if self.peer_ws is not None:
+            self.peer_ws.close()
+            self.peer_ws = None
+            if self.comm is not None:
+                self.comm.peer_ws = None
 
     def _mark_local(self, name: str) -> None:
         """Synchronise every stream of this GPU, then stamp wall time and a CUDA

@@ -135,6 +135,23 @@ class DecoderModel:
         return ops.gemm(x, w, out, epi=epi, save=save, save_lo=save_lo, save_hi=save_hi,
                         save_dst=save_dst, **kw)
 
+    def _proj_reduce(self, x, w, out, layer: int, group: str, b: ForwardBatch):
+        """Row-parallel projection followed by the TP all-reduce. With a peer
+        workspace on the communicator (``tp_comm: fused``) both happen in one
+        kernel over NVLink peer memory; otherwise GEMM then NCCL all-reduce."""
+        ws = getattr(self.comm, "peer_ws", None)
+        if ws is None or not ws.fits(x.shape[0], w.shape[0]):
+            self._proj(x, w, out, layer, group, b)
+            return self.comm.all_reduce(out)
+        kw = {}
+        if self.lora is not None and b.slot_ids is not None:
+            A = self.lora.A[layer][group]
+            seg = self.lora.seg[group]
+            z = torch.empty(x.shape[0], A.shape[0] * seg, dtype=x.dtype, device=x.device)
+            ops.lora_shrink(x, A, b.slot_ids, z, seg)
+            kw = dict(z=z, b2=self.lora.B2[layer][group], tile_slots=b.tile_slots, lora_seg=seg)
+        return ops.gemm_ar(x, w, ws, **kw)
+
     def _decode_ws(self, n: int, device):
         need_o = n * 128
         if self._dec_ws is None or self._dec_ws[0].numel() < need_o:
@@ -184,7 +201,7 @@ class DecoderModel:
             if l == 0:
                 ops.rms_norm(residual, lw.in_ln, x, eps, save=sv, save_lo=lo, save_hi=hi, save_dst=dst)
             else:
-                ops.rms_norm(mlp, lw.in_ln, x, eps, residual=residual, save=sv, save_lo=lo,
+                ops.rms_norm(mlp_red, lw.in_ln, x, eps, residual=residual, save=sv, save_lo=lo,
                              save_hi=hi, save_dst=dst)
             self._proj(x, lw.qkv, qkv, l, "qkv", b, save=cap.qkv[l] if cap_on else None,
                        save_lo=lo, save_hi=hi, save_dst=dst)
@@ -193,9 +210,8 @@ class DecoderModel:
             self.attention(l, qkv, ctx, b)
             if cap_on:
                 cap.ctx[l, dst:dst + hi - lo] = ctx[lo:hi]
-            self._proj(ctx, lw.o, o, l, "o", b)
-            self.comm.all_reduce(o)
-            ops.rms_norm(o, lw.post_ln, x, eps, residual=residual,
+            o_red = self._proj_reduce(ctx, lw.o, o, l, "o", b)
+            ops.rms_norm(o_red, lw.post_ln, x, eps, residual=residual,
                          save=cap.resid_mid[l] if cap_on else None, save_lo=lo, save_hi=hi,
                          save_dst=dst)
             self._proj(x, lw.gate_up, act, l, "gate_up", b, epi=EPI_SWIGLU,
@@ -203,9 +219,8 @@ class DecoderModel:
                        save_dst=dst)
             if cap_on:
                 cap.act[l, dst:dst + hi - lo] = act[lo:hi]
-            self._proj(act, lw.down, mlp, l, "down", b)
-            self.comm.all_reduce(mlp)
-        ops.rms_norm(mlp, w.final_norm, x, eps, residual=residual,
+            mlp_red = self._proj_reduce(act, lw.down, mlp, l, "down", b)
+        ops.rms_norm(mlp_red, w.final_norm, x, eps, residual=residual,
                      save=cap.final_in if cap_on else None, save_lo=lo, save_hi=hi, save_dst=dst)
         if b.logits_idx is None:
             return x

@@ -31,6 +31,11 @@ def native_available() -> bool:
     return _EXT is not None
 
 
+def native_ext():
+    """The loaded extension module (None when it is not built)."""
+    return _EXT
+
+
 LAUNCHES = [0]  # kernels of this package launched so far (bench accounting)
 
 
@@ -65,6 +70,23 @@ def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=Non
         return out
     return ref.gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi,
                     save_dst)
+
+
+def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_splits=0):
+    """All-reduce over the ranks of ``ws`` (a :class:`~..parallel.peer.PeerWorkspace`)
+    of ``a @ b.T`` (+ the segmented LoRA expand), in ONE kernel: the GEMM
+    epilogue pushes bf16 partial tiles to their owner rank over peer memory,
+    owners reduce and broadcast, every rank waits for its full result.
+    Returns a [M, N] view of the workspace's output buffer (valid until the
+    next call on the same workspace)."""
+    if not a.is_cuda:
+        raise RuntimeError("gemm_ar runs on CUDA tensors only")
+    if not ws.fits(a.shape[0], b.shape[0]):
+        raise ValueError(f"gemm_ar: [{a.shape[0]}, {b.shape[0]}] does not fit the workspace "
+                         f"([{ws.max_rows}, {ws.n_cols}])")
+    ws.calls += 1
+    return _native().gemm_ar(a, b, z, b2, tile_slots, lora_seg, ws.table, ws.tile_cnt, ws.rank,
+                             ws.world, ws.owned_cap, ws.max_rows, force_splits)
 
 
 def linear(x, w, out=None, epi=EPI_BF16, **kw):

@@ -8,6 +8,15 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
 void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> add,
                       torch::Tensor dx, c10::optional<torch::Tensor> dx_bf, double eps);
 void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10::optional<torch::Tensor> act);
+torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z,
+                          c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots, int64_t lora_seg,
+                          torch::Tensor peer, int64_t tile_cnt, int64_t rank, int64_t world, int64_t owned_cap,
+                          int64_t out_rows, int64_t force_splits);
+std::tuple<int64_t, std::string> dsv_peer_alloc(int64_t bytes);
+int64_t dsv_peer_open(const std::string& handle);
+void dsv_peer_close(int64_t addr);
+void dsv_peer_free(int64_t addr);
+void dsv_peer_zero(int64_t addr, int64_t bytes);
 int64_t dsv_read_error_gemm(bool clear);
 static int64_t dsv_read_error(bool clear) { return dsv_read_error_gemm(clear); }
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
@@ -36,6 +45,15 @@ void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, 
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &dsv_gemm, "tcgen05 GEMM with fused epilogues / LoRA expand");
+  m.def("gemm_ar", &dsv_gemm_ar, "tcgen05 GEMM fused with an all-reduce over peer memory");
+  m.def("peer_alloc", [](int64_t bytes) {
+    auto r = dsv_peer_alloc(bytes);
+    return std::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));
+  }, "cudaMalloc'd zeroed block + its CUDA IPC handle");
+  m.def("peer_open", [](pybind11::bytes h) { return dsv_peer_open(std::string(h)); }, "open a peer's IPC block");
+  m.def("peer_close", &dsv_peer_close, "unmap a peer block");
+  m.def("peer_free", &dsv_peer_free, "free this rank's block");
+  m.def("peer_zero", &dsv_peer_zero, "zero a range of this rank's block");
   m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
   m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
   m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");

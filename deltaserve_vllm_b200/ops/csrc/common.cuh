@@ -184,6 +184,51 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
          ((uint32_t)(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------- peer flags
+// System-scope flag operations for kernels that exchange tiles with other
+// GPUs through peer-mapped memory (NVLink / NVSwitch P2P loads and stores).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded spin until *p >= target (acquire, system scope). False (and the
+// error word set) when the budget runs out or another waiter already failed.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* p, uint32_t target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (true) {
+    if (ld_acquire_sys(p) >= target) return true;
+    if (n > 64) __nanosleep(32);  // back off: the flag crosses NVLink, no need to hammer it
+    if ((++n & 255u) == 0) {
+      if (*((volatile int*)&g_error) != 0) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        set_error(kErrWaitPeer);
+        return false;
+      }
+    }
+  }
+}
+
+// Named barrier over a subset of the CTA's warps (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }

@@ -31,7 +31,27 @@
 namespace dsv {
 
 
-enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3 };
+enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4 };
+
+constexpr int kMaxPeers = 8;
+constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
+
+// Fused all-reduce over peer memory (kEpiPeerAR). Every rank holds one
+// workspace, mapped into every other rank's address space:
+//   recv[world][owned_cap][BM*BN] bf16 — partial tiles pushed by each rank to
+//                                        the tile's owner (rank L % world);
+//   out[M][ldo] bf16                   — the reduced result;
+//   rflag[owned_cap]                   — arrivals per owned tile (reset by owner);
+//   fflag[tiles]                       — "final tile written" per output tile;
+//   tile_cnt[tiles] (local)            — split-K arrivals (last split reduces).
+struct PeerArgs {
+  int rank, world, owned_cap, ldo;
+  uint32_t* tile_cnt;
+  __nv_bfloat16* recv[kMaxPeers];
+  __nv_bfloat16* out[kMaxPeers];
+  uint32_t* rflag[kMaxPeers];
+  uint32_t* fflag[kMaxPeers];
+};
 
 struct GemmArgs {
   int M, N, K;            // C is M x N; K is the reduction length of the main term
@@ -45,6 +65,7 @@ struct GemmArgs {
   int max_ctas;           // host only: grid cap (0 = one CTA per SM, persistent)
   int k_splits;           // > 1: split-K, fp32 partials to `partial`, reduced by a second kernel
   float* partial;         // [k_splits, M, N]
+  PeerArgs peer;          // kEpiPeerAR only
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -105,6 +126,151 @@ __device__ __forceinline__ void store_row_f32(float* dst, const float* v, int n_
     for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   } else {
     for (int i = 0; i < 32 && i < n_valid; ++i) dst[i] = accum ? dst[i] + v[i] : v[i];
+  }
+}
+
+// ---------------------------------------------------------------- fused all-reduce
+// Epilogue side (warps 4-7, one output row per thread): the tile's bf16
+// partial goes straight into the owner's receive slot over NVLink, then one
+// thread bumps the owner's arrival counter with release semantics. With
+// split-K the splits first meet in the fp32 workspace and the last split to
+// arrive (atomic ticket) sums them and pushes.
+template <int BN>
+__device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile& tl, uint32_t t_row, int row,
+                                               bool row_ok, bool acc_ok, int q, int lane, int m_tiles) {
+  __shared__ int s_last;
+  const PeerArgs& P = args.peer;
+  const int L = tl.nt * m_tiles + tl.mt;
+  const int owner = L % P.world, local = L / P.world;
+  const int n0 = tl.nt * BN;
+  const int rt = q * 32 + lane;
+  __nv_bfloat16* dst = P.recv[owner] + ((size_t)P.rank * P.owned_cap + local) * (BM * BN) + (size_t)rt * BN;
+  bool push = true;
+  if (args.k_splits > 1) {
+#pragma unroll 1
+    for (int c = 0; c < BN && acc_ok; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (row_ok) store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + n0 + c, v, 32, false);
+    }
+    named_bar_sync(1, 128);
+    if (q == 0 && lane == 0) {
+      __threadfence();
+      const unsigned old = atomicAdd(P.tile_cnt + L, 1u);
+      s_last = (old == (unsigned)(args.k_splits - 1)) ? 1 : 0;
+      if (s_last) P.tile_cnt[L] = 0u;   // ticket reset for the next call
+      __threadfence();
+    }
+    named_bar_sync(1, 128);
+    push = s_last != 0;
+    if (push && row_ok) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int sp = 0; sp < args.k_splits; ++sp) {
+          const float4* src =
+              reinterpret_cast<const float4*>(args.partial + ((size_t)sp * args.M + row) * args.N + n0 + c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 f = __ldcg(src + i);
+            v[4 * i] += f.x;
+            v[4 * i + 1] += f.y;
+            v[4 * i + 2] += f.z;
+            v[4 * i + 3] += f.w;
+          }
+        }
+        store_row_bf16(dst + c, v, 32);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN && acc_ok; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (row_ok) store_row_bf16(dst + c, v, 32);
+    }
+  }
+  named_bar_sync(1, 128);
+  if (push && q == 0 && lane == 0) {
+    __threadfence_system();
+    red_release_sys_add(P.rflag[owner] + local, 1u);
+  }
+}
+
+// After the GEMM (all 256 threads): reduce the tiles this rank owns from the
+// world partials in local memory and write the bf16 result into every rank's
+// output (P2P stores), flag each rank; then wait until every output tile of
+// this rank has been delivered by its owner. Phases never wait on work of the
+// same phase, and the grid fits on the GPU next to the other streams' NCCL
+// kernels (every CTA can be resident), so the cross-rank waits cannot
+// deadlock; each wait is bounded.
+template <int BN>
+__device__ __forceinline__ void peer_reduce_tail(const GemmArgs& args, int m_tiles, int n_tiles) {
+  const PeerArgs& P = args.peer;
+  const int T = m_tiles * n_tiles;
+  const int n_owned = (T - P.rank + P.world - 1) / P.world;
+  constexpr int VPR = BN / 8;  // 16-byte vectors per tile row
+  const size_t slot_stride = (size_t)P.owned_cap * BM * BN;
+  for (int j = blockIdx.x; j < n_owned; j += gridDim.x) {
+    const int L = j * P.world + P.rank;
+    if (threadIdx.x == 0) {
+      wait_flag_geq(P.rflag[P.rank] + j, (uint32_t)P.world);
+      st_relaxed_sys(P.rflag[P.rank] + j, 0u);
+    }
+    __syncthreads();
+    const int mt = L % m_tiles, nt = L / m_tiles;
+    const int m0 = mt * BM, n0 = nt * BN;
+    const int rows = min(BM, args.M - m0);
+    const __nv_bfloat16* src = P.recv[P.rank] + (size_t)j * BM * BN;
+    for (int e = threadIdx.x; e < rows * VPR; e += blockDim.x) {
+      const int r = e / VPR, c8 = (e - r * VPR) * 8;
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int sl = 0; sl < P.world; ++sl) {
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + sl * slot_stride + (size_t)r * BN + c8));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          acc[2 * i] += f.x;
+          acc[2 * i + 1] += f.y;
+        }
+      }
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        ow[i] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      const size_t off = (size_t)(m0 + r) * P.ldo + n0 + c8;
+      for (int d = 0; d < P.world; ++d) {
+        const int dr = (P.rank + d) % P.world;  // stagger the peers
+        *reinterpret_cast<uint4*>(P.out[dr] + off) = o;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < P.world) {
+      __threadfence_system();
+      st_release_sys(P.fflag[threadIdx.x] + L, 1u);
+    }
+  }
+  for (int L = blockIdx.x; L < T; L += gridDim.x) {
+    if (threadIdx.x == 0) {
+      wait_flag_geq(P.fflag[P.rank] + L, 1u);
+      st_relaxed_sys(P.fflag[P.rank] + L, 0u);
+    }
   }
 }
 
@@ -259,13 +425,20 @@ __global__ void __launch_bounds__(256, 1)
       const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      if (!mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull)) break;
+      bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
+      if constexpr (EPI != kEpiPeerAR) {
+        if (!acc_ok) break;
+      }
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const bool do_save = args.save != nullptr && row_ok && row >= args.save_lo && row < args.save_hi;
-      if (args.k_splits > 1) {
+      if constexpr (EPI == kEpiPeerAR) {
+        // Keeps iterating after a failed wait (with the TMEM reads skipped) so
+        // the four epilogue warps always meet at their named barriers.
+        peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles);
+      } else if (args.k_splits > 1) {
         // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -344,6 +517,7 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  if constexpr (EPI == kEpiPeerAR) peer_reduce_tail<BN>(args, num_m_tiles, num_n_tiles);
 }
 
 // Split-K epilogue: sum the fp32 partials of every split and apply the
@@ -597,6 +771,105 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
                                                 args.save_dst);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+// out = all_reduce_over_ranks(a @ b^T (+ LoRA expand)), fused: the GEMM's
+// epilogue pushes bf16 partial tiles to their owner rank over peer memory and
+// the same launch reduces the owned tiles and broadcasts them.
+// `peer` is an int64 CPU tensor [4, world] of device addresses
+// (recv, out, rflag, fflag per rank); `tile_cnt` this rank's split-K tickets.
+// Returns the [M, N] result: a view of this rank's output buffer, valid until
+// the next call on the same workspace.
+torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z,
+                          c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots, int64_t lora_seg,
+                          torch::Tensor peer, int64_t tile_cnt, int64_t rank, int64_t world, int64_t owned_cap,
+                          int64_t out_rows, int64_t force_splits) {
+  using namespace dsv;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "dsv_gemm_ar: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm_ar: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "dsv_gemm_ar: row-major 2-D");
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "dsv_gemm_ar: rank/world");
+  TORCH_CHECK(peer.device().is_cpu() && peer.scalar_type() == at::kLong && peer.size(0) == 4 && peer.size(1) == world,
+              "dsv_gemm_ar: peer table must be int64 [4, world] on the CPU");
+  constexpr int BN = 128;
+  const int M = (int)a.size(0), K = (int)a.size(1), N = (int)b.size(0);
+  TORCH_CHECK(b.size(1) == K, "dsv_gemm_ar: reduction length mismatch");
+  TORCH_CHECK(N % BN == 0, "dsv_gemm_ar: N must be a multiple of 128");
+  TORCH_CHECK(M <= out_rows, "dsv_gemm_ar: M exceeds the workspace rows");
+  const int m_tiles = (M + BM - 1) / BM, n_tiles = N / BN, tiles = m_tiles * n_tiles;
+  TORCH_CHECK((tiles + world - 1) / world <= owned_cap, "dsv_gemm_ar: workspace too small for this shape");
+  auto opts = a.options();
+  auto* tab = peer.data_ptr<int64_t>();
+  torch::Tensor out = torch::from_blob(reinterpret_cast<void*>(tab[1 * world + rank]), {M, N}, opts);
+  if (M == 0) return out;
+  c10::cuda::CUDAGuard guard(a.device());
+  int splits = 1;
+  const int kbs = (K + BK - 1) / BK;
+  if (force_splits > 0) {
+    splits = (int)force_splits;
+  } else if (m_tiles == 1 && tiles < num_sms() / 2 && kbs >= 8) {
+    splits = std::max(1, std::min({(num_sms() - kArSmReserve) / tiles, kbs / 4, 16}));
+  }
+  if (splits > 1) {
+    const int per = (kbs + splits - 1) / splits;
+    splits = (kbs + per - 1) / per;
+  }
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.k_splits = splits;
+  at::Tensor partial;
+  if (splits > 1) {
+    partial = at::empty({splits, M, N}, opts.dtype(at::kFloat));
+    args.partial = partial.data_ptr<float>();
+  }
+  PeerArgs& P = args.peer;
+  P.rank = (int)rank;
+  P.world = (int)world;
+  P.owned_cap = (int)owned_cap;
+  P.ldo = N;
+  P.tile_cnt = reinterpret_cast<uint32_t*>(tile_cnt);
+  for (int r = 0; r < world; ++r) {
+    P.recv[r] = reinterpret_cast<__nv_bfloat16*>(tab[0 * world + r]);
+    P.out[r] = reinterpret_cast<__nv_bfloat16*>(tab[1 * world + r]);
+    P.rflag[r] = reinterpret_cast<uint32_t*>(tab[2 * world + r]);
+    P.fflag[r] = reinterpret_cast<uint32_t*>(tab[3 * world + r]);
+  }
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), BM);
+  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), BN);
+  CUtensorMap tz = ta, tb2 = tb;
+  if (lora_seg > 0) {
+    TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "dsv_gemm_ar: LoRA operands missing");
+    TORCH_CHECK(lora_seg % 64 == 0, "dsv_gemm_ar: lora_seg must be a multiple of 64");
+    auto& zt = *z;
+    auto& bt = *b2;
+    TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm_ar: LoRA shapes");
+    TORCH_CHECK(tile_slots->scalar_type() == at::kInt && tile_slots->numel() >= m_tiles, "dsv_gemm_ar: tile_slots");
+    tz = make_tmap_bf16(zt.data_ptr(), M, zt.size(1), zt.stride(0), BM);
+    tb2 = make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), BN);
+    args.lora_seg = (int)lora_seg;
+    args.num_slots = (int)(zt.size(1) / lora_seg);
+    args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
+  }
+  using Cfg = GemmCfg<BN, false>;
+  auto kern = gemm_tc_kernel<BN, false, kEpiPeerAR>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_set = true;
+  }
+  // One CTA per SM at most, and kArSmReserve SMs left to other streams: every
+  // CTA of this grid can be resident at once even while the backward stream
+  // runs an NCCL kernel (capped at the same number of CTAs by init_tp), so a
+  // CTA waiting on a peer never keeps the peer's partner CTA (or the peer's
+  // NCCL kernel) from being scheduled. A cooperative launch would give the
+  // same guarantee but waits for the whole GPU to drain first.
+  const int grid = std::min(tiles * splits, std::max(1, num_sms() - kArSmReserve));
+  gemm_tc_kernel<BN, false, kEpiPeerAR><<<grid, 256, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(
+      ta, tb, tz, tb2, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
 }
 
 DSV_ERROR_ACCESSOR(dsv_read_error_gemm)

@@ -1,0 +1,95 @@
+"""Fused GEMM + all-reduce vs GEMM then NCCL all-reduce, on N GPUs.
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 \\
+        --master-port 29600 -m deltaserve_vllm_b200.parallel.ar_bench [--iters 20]
+
+Shapes are Llama-3-8B's row-parallel projections at this TP degree
+(o: K = 4096/tp, down: K = 14336/tp, N = 4096) for a decode step (M = 64) and
+a prefill step (M = 4096). Each variant is timed with CUDA events over
+``iters`` launches after warm-up; the max over ranks is reported. The
+roofline of the fused path is the slower of its FLOPs at the measured bf16
+peak and the bytes each rank must send over NVLink at 770 GB/s per direction
+(one-shot push of the partial, (tp-1)/tp of it, plus the reduced result to
+tp-1 peers, (tp-1)/tp of it).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..ops.kernel_bench import _peaks
+from .comm import init_tp
+from .peer import PeerWorkspace
+
+NVLINK_GBS = 770.0
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / iters], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args(argv)
+    comm = init_tp()
+    tp, rank = comm.size, comm.rank
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    ws = PeerWorkspace(comm, 4096, 4096)
+    peak = _peaks()
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    for name, M, K in [("o_decode", 64, 4096 // tp), ("down_decode", 64, 14336 // tp),
+                       ("o_prefill", 4096, 4096 // tp), ("down_prefill", 4096, 14336 // tp)]:
+        N = 4096
+        a = torch.randn(M, K, generator=g, device="cuda").bfloat16()
+        b = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+
+        def base():
+            ops.gemm(a, b, out)
+            dist.all_reduce(out)
+
+        def gemm_only():
+            ops.gemm(a, b, out)
+
+        def fused():
+            ops.gemm_ar(a, b, ws)
+
+        t_base, t_gemm, t_fused = _time(base, args.iters), _time(gemm_only, args.iters), _time(fused, args.iters)
+        ref = a.float() @ b.float().t()
+        dist.all_reduce(ref)
+        err = float((ops.gemm_ar(a, b, ws).float() - ref).abs().max() / ref.abs().max())
+        flops = 2 * M * N * K
+        nvl_bytes = 2 * (tp - 1) / tp * M * N * 2
+        bound_ms = max(flops / (peak["bf16_tflops"] * 1e9), nvl_bytes / (NVLINK_GBS * 1e6))
+        if rank == 0:
+            print(json.dumps({"case": name, "tp": tp, "M": M, "N": N, "K": K, "gemm_ms": round(t_gemm, 4),
+                              "gemm_nccl_ms": round(t_base, 4), "fused_ms": round(t_fused, 4),
+                              "speedup_vs_nccl": round(t_base / t_fused, 3),
+                              "roofline_ms": round(bound_ms, 4), "frac_roofline": round(bound_ms / t_fused, 3),
+                              "max_rel_err": round(err, 5), "peaks": peak["src"]}), flush=True)
+    assert ops.check_device_error() == 0
+    ws.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

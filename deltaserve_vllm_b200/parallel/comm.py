@@ -64,6 +64,13 @@ class TPComm:
         dist.gather_object(obj, out, dst=dst, group=self.cpu_group or self.group)
         return out
 
+    def all_gather_object(self, obj) -> list:
+        if self.size == 1:
+            return [obj]
+        out = [None] * self.size
+        dist.all_gather_object(out, obj, group=self.cpu_group or self.group)
+        return out
+
     def all_reduce_max_int(self, v: int) -> int:
         """Host vote: every rank gets the max (used for rank-symmetric decisions)."""
         if self.size == 1:
@@ -85,6 +92,9 @@ def init_tp(backend: str | None = None, timeout_s: float = 120.0) -> TPComm:
     if not dist.is_initialized():
         if backend is None:
             backend = "nccl" if torch.cuda.is_available() else "gloo"
+        # NCCL kernels may occupy at most this many SMs: the fused GEMM +
+        # all-reduce grid leaves that many free, so both can always be resident.
+        os.environ.setdefault("NCCL_MAX_CTAS", "16")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         kw = {}
         if backend == "nccl":

@@ -1,0 +1,92 @@
+"""Peer-mapped workspaces for the fused GEMM + all-reduce kernel.
+
+One cudaMalloc'd block per rank, exported as a CUDA IPC handle and opened by
+every other rank (plain P2P mappings over NVLink / NVSwitch: no multicast
+object, so a rank that exits cannot leave a multicast binding behind). The
+block holds, for output width ``n_cols`` and up to ``max_rows`` rows:
+
+* ``recv``  — ``world x owned_cap`` partial tiles of 128 x 128 bf16: the slots
+  other ranks push the tiles this rank owns into (tile ``L`` belongs to rank
+  ``L % world``);
+* ``out``   — the reduced ``[max_rows, n_cols]`` bf16 result;
+* ``rflag`` — per owned tile, how many ranks have pushed (reset by the owner);
+* ``fflag`` — per output tile, set by its owner once the result is written
+  here (reset by this rank);
+* ``tile_cnt`` — this rank's split-K tickets (the last split reduces).
+
+``ops.gemm_ar`` drives the kernel; the workspace is reused by every call on
+the forward stream (each call's result is consumed before the next call's
+pushes can reach it: a peer only pushes after this rank's partial of the
+same tile arrived, which comes after this rank consumed the previous output).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+TILE = 128
+_ALIGN = 256
+
+
+def _align(n: int) -> int:
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+class PeerWorkspace:
+    def __init__(self, comm, max_rows: int, n_cols: int, device=None):
+        from .. import ops
+        ext = ops.native_ext()
+        if ext is None:
+            raise RuntimeError("the fused all-reduce needs the CUDA extension")
+        if n_cols % TILE:
+            raise ValueError("n_cols must be a multiple of 128")
+        self.comm = comm
+        self.world = comm.size if comm is not None else 1
+        self.rank = comm.rank if comm is not None else 0
+        if self.world > 8:
+            raise ValueError("the fused all-reduce supports up to 8 ranks")
+        self.n_cols = n_cols
+        m_tiles = math.ceil(max_rows / TILE)
+        self.max_rows = m_tiles * TILE
+        self.tiles = m_tiles * (n_cols // TILE)
+        self.owned_cap = math.ceil(self.tiles / self.world)
+        sizes = [self.world * self.owned_cap * TILE * TILE * 2,   # recv
+                 self.max_rows * n_cols * 2,                         # out
+                 self.owned_cap * 4,                                 # rflag
+                 self.tiles * 4,                                     # fflag
+                 self.tiles * 4]                                     # tile_cnt
+        self.offsets = []
+        off = 0
+        for sz in sizes:
+            self.offsets.append(off)
+            off += _align(sz)
+        self.bytes = off
+        self._ext = ext
+        self.base, handle = ext.peer_alloc(self.bytes)
+        handles = comm.all_gather_object(handle) if self.world > 1 else [handle]
+        self.ptrs = [self.base if r == self.rank else ext.peer_open(h) for r, h in enumerate(handles)]
+        self.table = torch.tensor([[p + self.offsets[k] for p in self.ptrs] for k in range(4)],
+                                  dtype=torch.int64)
+        self.tile_cnt = self.base + self.offsets[4]
+        self.calls = 0
+        if comm is not None and self.world > 1:
+            comm.barrier()        # every rank mapped every block before first use
+
+    def fits(self, rows: int, n_cols: int) -> bool:
+        return rows <= self.max_rows and n_cols == self.n_cols
+
+    def close(self) -> None:
+        """Unmap the peers' blocks and free this rank's (after a barrier, so no
+        peer is still writing into it)."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        if self.comm is not None and self.world > 1:
+            self.comm.barrier()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.peer_close(p)
+        self._ext.peer_free(self.base)
+        self.base = None

@@ -296,3 +296,47 @@ def test_rms_norm_bwd_and_swiglu_bwd():
     ref.swiglu_bwd(gu.cpu(), dact.cpu(), dgu_r, act_r)
     torch.testing.assert_close(dgu.float().cpu(), dgu_r.float(), rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(act.float().cpu(), act_r.float(), rtol=2e-2, atol=2e-2)
+
+
+# ---------------------------------------------------------------- fused GEMM + all-reduce
+@pytest.mark.parametrize("M,N,K,splits", [(1, 4096, 4096, 0), (16, 4096, 1792, 0), (200, 1024, 512, 0),
+                                          (1000, 2048, 512, 0), (130, 512, 1024, 4), (7, 256, 4096, 0)])
+def test_gemm_allreduce_single_rank(M, N, K, splits):
+    """One rank: the kernel's push / owner-reduce / broadcast / wait phases all
+    run against this GPU's own workspace; repeated calls exercise the flag and
+    ticket resets."""
+    from deltaserve_vllm_b200.parallel.peer import PeerWorkspace
+    ws = PeerWorkspace(None, 1024 + 8, N)
+    try:
+        for it in range(3):
+            a, b = rnd(M, K, seed=11 + it), rnd(N, K, scale=0.05, seed=12 + it)
+            out = ops.gemm_ar(a, b, ws, force_splits=splits)
+            exp = a.float() @ b.float().t()
+            torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+        torch.cuda.synchronize()
+    finally:
+        ws.close()
+
+
+def test_gemm_allreduce_single_rank_lora():
+    from deltaserve_vllm_b200.parallel.peer import PeerWorkspace
+    M, N, K, slots, P, R, seg = 150, 512, 256, 2, 1, 16, 64
+    x, w = rnd(M, K, seed=21), rnd(N, K, scale=0.05, seed=22)
+    A = rnd(slots, P * R, K, scale=0.05, seed=23)
+    B2 = rnd(N, slots * seg, scale=0.05, seed=24)
+    slot_ids = torch.randint(-1, slots, (M,), device=DEV, dtype=torch.int32).sort()[0]
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, slot_ids, Z, seg)
+    nt = -(-M // 128)
+    mask = torch.zeros(nt, dtype=torch.int32)
+    for t in range(nt):
+        for s in slot_ids[t * 128:(t + 1) * 128].cpu().unique().tolist():
+            if s >= 0:
+                mask[t] |= 1 << s
+    ws = PeerWorkspace(None, 256, N)
+    try:
+        out = ops.gemm_ar(x, w, ws, z=Z, b2=B2, tile_slots=mask.to(DEV), lora_seg=seg)
+        exp = x.float() @ w.float().t() + Z.float() @ B2.float().t()
+        torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+    finally:
+        ws.close()

@@ -62,3 +62,41 @@ def test_tp2_backward_matches_tp1_on_gpu():
             x, y = a["grads"][k].flatten().double(), g.flatten().double()
             cos = float(x @ y / (x.norm() * y.norm() + 1e-30))
             assert cos > 0.99, (k, cos)
+
+
+def _run_gemm_ar(rank, world, port, outdir):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from deltaserve_vllm_b200.parallel.peer import PeerWorkspace
+    comm = TPComm(None, dist.new_group(backend="gloo"))
+    ws = PeerWorkspace(comm, 2048, 4096)
+    errs = []
+    try:
+        for it, (M, K) in enumerate([(1, 2048), (16, 896), (300, 512), (2048, 1024), (5, 7168)]):
+            g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
+            a = (torch.randn(M, K, generator=g, device="cuda")).bfloat16()
+            b = (torch.randn(4096, K, generator=g, device="cuda") * 0.05).bfloat16()
+            fused = ops.gemm_ar(a, b, ws).clone()
+            ref = (a.float() @ b.float().t())
+            dist.all_reduce(ref)
+            errs.append(float((fused.float() - ref).abs().max() / (ref.abs().max() + 1e-6)))
+        torch.cuda.synchronize()
+        err_code = ops.check_device_error()
+    finally:
+        ws.close()
+    torch.save({"errs": errs, "code": err_code}, os.path.join(outdir, f"ar{rank}.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_gemm_allreduce_tp2():
+    """The fused GEMM + all-reduce over peer memory equals GEMM + NCCL all-reduce."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run_gemm_ar, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            res = torch.load(os.path.join(d, f"ar{r}.pt"))
+            assert res["code"] == 0
+            assert max(res["errs"]) < 2e-2, res["errs"]
