@@ -175,7 +175,7 @@ def main():
                         block_size=64, max_num_seqs=256, max_num_batched_tokens=args.max_batched_tokens,
                         max_loras=2, max_lora_rank=16, gpu_memory_utilization=0.85, seed=args.seed,
                         tp_comm=args.tp_comm)
-    fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
+    fcfg = FinetuneConfig(enable_finetuning=True, backward_cuda_graph=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
                           num_epochs=1000, ttft_slo=args.ttft_slo, max_tbt_slo=args.tbt_slo,
                           avg_tbt_slo=args.tbt_slo, admission_margin="relative", admission_margin_k=1.5,
                           pause_on_arrival=True, backward_run_ahead_boundaries=args.run_ahead,

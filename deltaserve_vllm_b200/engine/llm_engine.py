@@ -102,8 +102,13 @@ class CoServingEngine:
         # ---- finetuning
         self.ft_enabled = bool(self.ftcfg.enable_finetuning) and self.lora is not None
         cap_tokens = self.ftcfg.max_saved_finetuning_tokens
-        self.capture = (CaptureBuffers.allocate(self.weights, cap_tokens + 8, self.device, self.dtype)
-                        if self.ft_enabled else None)
+        # save_activations off: FT rows are forwarded but nothing is captured or
+        # trained (measures the capture overhead).
+        fc = self.ftcfg
+        self.capture = (CaptureBuffers.allocate(self.weights, cap_tokens + 8, self.device, self.dtype,
+                                                save_qkv=fc.save_attn_qkv, save_ctx=fc.save_attn_ctx,
+                                                save_resid_mid=fc.save_resid_mid)
+                        if self.ft_enabled and fc.save_activations else None)
         # ---- fused GEMM + all-reduce workspace (row-parallel o / down under TP)
         self.peer_ws = None
         if self.cuda and comm is not None and comm.size > 1 and ecfg.tp_comm == "fused":
@@ -188,6 +193,11 @@ class CoServingEngine:
         self._job_owner = None
         if self.is_driver and (self.ftcfg.metrics_dir or self.ftcfg.step_trace_path):
             self.start_telemetry(self.ftcfg.metrics_dir)
+        if self.ftcfg.print_weight_hash:
+            dprint(f"[weights] rank {self.tp.rank} hash {self.weight_hash():.6e}")
+        if self.ftcfg.backward_mps_percentage:
+            dprint("[config] backward_mps_percentage is ignored: the backward runs on a "
+                   "low-priority stream of this process (no MPS)")
 
     # ------------------------------------------------------------------ setup
     def _alloc_kv(self) -> KVCache:
@@ -229,6 +239,11 @@ class CoServingEngine:
                                    gamma=cfg.gamma, comm=self.bwd_comm, mask_prefix=cfg.loss_mask_prefix,
                                    targets=cfg.ft_target_modules, adapter_config=acfg,
                                    cos_sin_table=self.model_cos_sin())
+        self.trainer.use_graphs = self.cuda and bool(cfg.backward_cuda_graph)
+        if cfg.backward_fp32 and self.cuda:
+            dprint("[config] backward_fp32 is not available on the sm_100a path: backward GEMMs "
+                   "take bf16 operands with fp32 accumulation (masters, norms, softmax and the "
+                   "LM head stay fp32)")
         if tensors:
             self.trainer.load_adapter(tensors, rank, alpha)
         else:
@@ -245,6 +260,14 @@ class CoServingEngine:
         self.admission = FinetuneAdmission(cfg, self.estimator, self.coord, self.store,
                                            self.ecfg.max_num_batched_tokens, self.tbt_window)
         self.jobs.submit(FinetuneJobSpec.from_finetune_config(cfg), self.rcfg.enable_adapter_routing)
+
+    def weight_hash(self) -> float:
+        """Order-sensitive checksum of this rank's base weights (debug)."""
+        h = 0.0
+        for i, t in enumerate([self.weights.embed] + [getattr(L, f) for L in self.weights.layers
+                                                      for f in ("qkv", "o", "gate_up", "down")]):
+            h += (i + 1) * float(t.float().flatten()[:: max(1, t.numel() // 4096)].double().sum())
+        return h
 
     def begin_job(self, job) -> bool:
         """Switch finetuning to ``job`` (its init stage). The launch job is
@@ -394,6 +417,9 @@ class CoServingEngine:
             r.lora_slot = self.adapter_slots[adapter]
         self.scheduler.add(r)
         self.requests[request_id] = r
+        if self.ftcfg.print_engine_req_recv:
+            dprint(f"[req] {request_id}: {len(r.prompt_ids)} prompt tokens, max {r.params.max_tokens}, "
+                   f"adapter {adapter}")
         self.coord.note_arrival(r.arrival_time)
         self.arrival_flag = True
         for cb in self.request_listeners:
@@ -558,6 +584,9 @@ class CoServingEngine:
             if self.coord.try_flush():
                 self._start_backward()
         out = self.scheduler.schedule()
+        if self.ftcfg.print_scheduler_add and out.prefill:
+            dprint(f"[sched] step {self.step_no}: prefill {[s.num_new for s in out.prefill]} "
+                   f"decode {len(out.decode)}")
         bwd_busy = self.bwd_active or self._bwd_done_evt is not None
         adm = None
         ft_dst = 0
@@ -583,6 +612,15 @@ class CoServingEngine:
             if (cfg.forward_interruptible and out.ft and not out.decode and not out.prefill
                     and self.scheduler.waiting):
                 self._rollback_ft(out)
+            # Tier A: before an FT-only step, give a request that is arriving
+            # right now (flagged by the HTTP thread) a short grace to join.
+            elif (cfg.forward_interruptible and cfg.ft_only_admission_grace_ms > 0 and out.ft
+                  and not out.decode and not out.prefill):
+                t_end = time.perf_counter() + cfg.ft_only_admission_grace_ms / 1e3
+                while not self.arrival_flag and time.perf_counter() < t_end:
+                    time.sleep(0.0002)
+                if self.arrival_flag:
+                    self._rollback_ft(out)
         if out.is_empty():
             self._advance_backward(idle=not self.has_unfinished())
             self._flush_actions()
@@ -605,12 +643,23 @@ class CoServingEngine:
         has_inf_prefill = bool(out.prefill)
         pause_now = has_inf_prefill and (self.ftcfg.pause_on_arrival or self.ftcfg.pause_until_prefill_done
                                          or self.ftcfg.pause_prefill_always)
+        # fwd_token_throttle: a large step keeps the backward paused while it runs.
+        big_step = (self.ftcfg.fwd_token_throttle_enable
+                    and out.t_in + out.b_d >= self.ftcfg.fwd_token_throttle)
+        pause_now = pause_now or big_step
         # Queue backward layers while the forward runs (before the host blocks
         # on the sampled tokens); the low-priority stream fills GPU gaps.
         feed = (lambda: self._advance_backward(idle=False, paused=pause_now)) \
             if (self.cuda and not self.profiling) else None
         uses_ft_slot = bool(out.ft) or any(s.req.lora_slot == self.ft_slot for s in out.seqs
                                            if self.ft_slot >= 0)
+        if self.ftcfg.print_engine_batch_exec or self.ftcfg.print_step_mode:
+            mode = ("ft-only" if out.ft and not (out.prefill or out.decode) else
+                    "mixed" if out.ft else "prefill" if out.prefill else "decode")
+            dprint(f"[batch-exec] step {self.step_no} mode={mode} decode={len(out.decode)} "
+                   f"prefill={len(out.prefill)} ft={len(out.ft)} t_in={out.t_in} t_ft={out.t_ft} "
+                   f"bwd={'busy' if bwd_busy else 'idle'} pred_ms="
+                   f"{'-' if pred is None else round(pred * 1e3, 3)}")
         if self.cuda:
             with torch.cuda.stream(self.fwd_stream):
                 if uses_ft_slot and self._publish_evt is not None:
@@ -649,12 +698,23 @@ class CoServingEngine:
         self.arrival_flag = False
         pause = has_inf_prefill and (self.ftcfg.pause_on_arrival or self.ftcfg.pause_until_prefill_done
                                      or self.ftcfg.pause_prefill_always)
-        self._advance_backward(idle=False, paused=pause and bool(self.scheduler.waiting))
+        self._advance_backward(idle=False, paused=(pause and bool(self.scheduler.waiting)) or big_step)
+        if self.ftcfg.validate_estimator:
+            self._drain_timing(block=True)      # synchronous: every prediction checked at once
+        if self.ftcfg.print_engine_batch_done:
+            dprint(f"[batch-done] step {self.step_no}: {len(done)} finished")
         return done
 
     # ------------------------------------------------------------------ backward
     def _start_backward(self, capture_evt=None) -> None:
         if self.trainer is None:
+            return
+        if self.capture is None:        # save_activations off: retire the samples untrained
+            from .trainer import CycleResult
+            self._bwd_meta = {"epoch": self.store.current_epoch if self.store else 0}
+            self._bwd_result = CycleResult(float("nan"), int(self.coord.fill_count), 0, 0.0, 0.0,
+                                           self.trainer.step)
+            self._finish_backward(skip_trainer=True)
             return
         n = self.coord.fill_count
         lens = list(self.coord.sample_lens)
@@ -666,6 +726,9 @@ class CoServingEngine:
                 self.bwd_stream.wait_event(capture_evt)
             else:
                 self.bwd_stream.wait_stream(self.fwd_stream)
+        if self.ftcfg.print_activation_hash:
+            dprint(f"[activations] cycle {self.coord.cycle}: rows {n} hash "
+                   f"{float(self.capture.layer_in[:, :n].float().sum()):.6e}")
         gen = self.trainer.cycle(self.capture, n, self._bwd_meta["starts"], lens,
                                  self._bwd_meta["epoch"], sync=False)
         self._bwd_events.clear()
@@ -727,8 +790,9 @@ class CoServingEngine:
         if self._bwd_done_evt is not None and self._bwd_done_evt.query():
             self._finish_backward()
 
-    def _finish_backward(self) -> None:
-        res = self.trainer.finish_cycle(self._bwd_result) if self.trainer else self._bwd_result
+    def _finish_backward(self, skip_trainer: bool = False) -> None:
+        res = (self.trainer.finish_cycle(self._bwd_result) if self.trainer and not skip_trainer
+               else self._bwd_result)
         self._bwd_done_evt = None
         meta = self._bwd_meta or {}
         trained = self.coord.backward_done(res.n_tokens, res.loss, res.gpu_ms, res.wall_ms,
@@ -801,7 +865,7 @@ class CoServingEngine:
             self.synchronize()
             self.estimator.data_fit(self.tracker)
             self.load_estimator_state()
-            if self.ft_enabled and self.trainer is not None:
+            if self.ft_enabled and self.trainer is not None and self.capture is not None:
                 # One full backward cycle on this thread at the buffer's size:
                 # loads every backward kernel before the feeder thread runs.
                 cap = self.ftcfg.max_saved_finetuning_tokens
@@ -959,6 +1023,11 @@ class CoServingEngine:
                 self.save_estimator_state()
             except Exception as e:  # best effort at teardown
                 dprint(f"[estimator] state save failed: {e!r}")
+            self._drain_timing(block=True)
+            path = self.ftcfg.batch_prediction_stats_path or (
+                self.ftcfg.estimator_validation_path if self.ftcfg.validate_estimator else None)
+            if path:
+                self.tracker.write_prediction_stats_csv(path)
         self.stop_telemetry()
         if self.step_trace is not None:
             self.step_trace.close()

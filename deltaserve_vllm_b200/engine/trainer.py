@@ -128,7 +128,8 @@ class LoraTrainer:
             raise ValueError("capture buffer too small for the padded cycle")
         if n_pad > n:  # padded rows must be zero (they carry no sample)
             for t in (cap.layer_in, cap.qkv, cap.ctx, cap.resid_mid, cap.gate_up, cap.act):
-                t[:, n:n_pad].zero_()
+                if t is not None:
+                    t[:, n:n_pad].zero_()
             cap.final_in[n:n_pad].zero_()
             cap.ids[n:n_pad].zero_()
             cap.positions[n:n_pad].zero_()
@@ -158,9 +159,18 @@ class LoraTrainer:
         all-reduce at bucket boundaries). Returns the new residual gradient."""
         L = self.arch.num_layers
         m = self.masters
-        saved = {k: getattr(cap, k)[l, :ci.n_pad] for k in
+        saved = {k: (None if getattr(cap, k) is None else getattr(cap, k)[l, :ci.n_pad]) for k in
                  ("layer_in", "qkv", "ctx", "resid_mid", "gate_up", "act")}
-        dh = self.bwd.layer_backward(l, dh, saved, ci, cap.positions[:ci.n_pad], self.cos_sin)
+        pos = cap.positions[:ci.n_pad]
+        # Activations the forward did not capture (save_attn_qkv / save_attn_ctx /
+        # save_resid_mid off) are recomputed from the layer input.
+        if saved["qkv"] is None:
+            saved["qkv"] = self.bwd.recompute_qkv_raw(l, saved["layer_in"])
+        if saved["ctx"] is None:
+            saved["ctx"] = self.bwd.recompute_ctx(l, saved["qkv"], ci, pos, self.cos_sin)
+        if saved["resid_mid"] is None:
+            saved["resid_mid"] = self.bwd.recompute_resid_mid(l, saved["layer_in"], saved["ctx"])
+        dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin)
         if self.comm is not None and self.comm.size > 1 and (l % BUCKET_LAYERS == 0):
             # Layers [l, l + BUCKET_LAYERS) are done: one all-reduce of their
             # replicated factor gradients.

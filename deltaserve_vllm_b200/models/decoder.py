@@ -74,14 +74,19 @@ class CaptureBuffers:
     positions: torch.Tensor  # [cap] int64
 
     @staticmethod
-    def allocate(w: ModelWeights, cap: int, device, dtype=torch.bfloat16) -> "CaptureBuffers":
+    def allocate(w: ModelWeights, cap: int, device, dtype=torch.bfloat16, save_qkv: bool = True,
+                 save_ctx: bool = True, save_resid_mid: bool = True) -> "CaptureBuffers":
+        """Buffers switched off by ``save_*`` are None: the backward recomputes
+        those activations from the layer input instead."""
         a = w.arch
         L, D = a.num_layers, a.hidden
         qkv_l = w.q_local + 2 * w.kv_local
         z = lambda *s: torch.zeros(*s, dtype=dtype, device=device)
         return CaptureBuffers(
-            layer_in=z(L, cap, D), qkv=z(L, cap, qkv_l), ctx=z(L, cap, w.q_local),
-            resid_mid=z(L, cap, D), gate_up=z(L, cap, 2 * w.i_local), act=z(L, cap, w.i_local),
+            layer_in=z(L, cap, D), qkv=z(L, cap, qkv_l) if save_qkv else None,
+            ctx=z(L, cap, w.q_local) if save_ctx else None,
+            resid_mid=z(L, cap, D) if save_resid_mid else None,
+            gate_up=z(L, cap, 2 * w.i_local), act=z(L, cap, w.i_local),
             final_in=z(cap, D),
             ids=torch.zeros(cap, dtype=torch.long, device=device),
             positions=torch.zeros(cap, dtype=torch.long, device=device))
@@ -89,7 +94,7 @@ class CaptureBuffers:
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in
                    (self.layer_in, self.qkv, self.ctx, self.resid_mid, self.gate_up, self.act,
-                    self.final_in))
+                    self.final_in) if t is not None)
 
 
 class Communicator:
@@ -203,16 +208,18 @@ class DecoderModel:
             else:
                 ops.rms_norm(mlp_red, lw.in_ln, x, eps, residual=residual, save=sv, save_lo=lo,
                              save_hi=hi, save_dst=dst)
-            self._proj(x, lw.qkv, qkv, l, "qkv", b, save=cap.qkv[l] if cap_on else None,
+            self._proj(x, lw.qkv, qkv, l, "qkv", b,
+                       save=cap.qkv[l] if cap_on and cap.qkv is not None else None,
                        save_lo=lo, save_hi=hi, save_dst=dst)
             ops.qk_norm_rope_cache(qkv, b.positions, self.cos_sin, lw.q_norm, lw.k_norm, eps,
                                    self.hq_l, self.hkv_l, self.kv_k[l], self.kv_v[l], b.slot_mapping)
             self.attention(l, qkv, ctx, b)
-            if cap_on:
+            if cap_on and cap.ctx is not None:
                 cap.ctx[l, dst:dst + hi - lo] = ctx[lo:hi]
             o_red = self._proj_reduce(ctx, lw.o, o, l, "o", b)
             ops.rms_norm(o_red, lw.post_ln, x, eps, residual=residual,
-                         save=cap.resid_mid[l] if cap_on else None, save_lo=lo, save_hi=hi,
+                         save=cap.resid_mid[l] if cap_on and cap.resid_mid is not None else None,
+                         save_lo=lo, save_hi=hi,
                          save_dst=dst)
             self._proj(x, lw.gate_up, act, l, "gate_up", b, epi=EPI_SWIGLU,
                        save=cap.gate_up[l] if cap_on else None, save_lo=lo, save_hi=hi,

@@ -238,6 +238,29 @@ def attn_backward(qh, kh, vh, d_ctx, starts, lens, scale, groups=None):
     return dq, dk, dv
 
 
+def attn_forward(qh, kh, vh, starts, lens, scale, groups=None):
+    """Causal GQA attention forward (fp32 scores, TF32 on CUDA), same sample
+    grouping as :func:`attn_backward`. Inputs [n, H, hd]; returns [n, Hq, hd]
+    fp32. Used when the attention context was not captured in the forward."""
+    n, Hq, hd = qh.shape
+    Hkv = kh.shape[1]
+    G = Hq // Hkv
+    out = torch.zeros(n, Hq, hd, dtype=torch.float32, device=qh.device)
+    if groups is None:
+        groups = attention_groups(starts, lens, qh.device)
+    for ln, B, idx in groups:
+        def take(t, H):
+            return t.index_select(0, idx).view(B, ln, H, hd).transpose(1, 2).float()
+        q = take(qh, Hq)
+        k = take(kh, Hkv).repeat_interleave(G, 1)
+        v = take(vh, Hkv).repeat_interleave(G, 1)
+        s = torch.matmul(q, k.transpose(-1, -2)) * scale
+        mask = torch.triu(torch.ones(ln, ln, dtype=torch.bool, device=qh.device), 1)
+        o = torch.matmul(s.masked_fill_(mask, float("-inf")).softmax(-1), v)
+        out.index_copy_(0, idx, o.transpose(1, 2).reshape(B * ln, Hq, hd))
+    return out
+
+
 def _bf(t, cdt):
     return t if t.dtype == cdt else t.to(cdt)
 
@@ -357,6 +380,33 @@ class LoraBackward:
         del dlog
         d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
         return loss.sum(), d_final
+
+    # ------------------------------------------------------------ recompute
+    def _proj_lora(self, layer: int, g: str, X: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+        """fp32 ``X @ W^T`` plus the trained adapter's term for group ``g``
+        (the forward's projection, for activations that were not captured)."""
+        y = self._mm(X, W, b_mn=False)
+        A = _bf(self.m.p(layer, g, "A"), self.cdt)
+        Z = self._mm(X, A, b_mn=False)
+        self._mm(Z, self._bfull(layer, g), b_mn=False, epi=EPI_F32_ACCUM, out=y)
+        return y
+
+    def recompute_qkv_raw(self, layer: int, layer_in: torch.Tensor) -> torch.Tensor:
+        lw = self.w.layers[layer]
+        x1 = torch.empty_like(layer_in)
+        ops.rms_norm(layer_in, lw.in_ln, x1, self.arch.rms_eps)
+        return self._proj_lora(layer, "qkv", x1, lw.qkv).to(layer_in.dtype)
+
+    def recompute_ctx(self, layer: int, qkv_raw: torch.Tensor, ci, positions, cos_sin) -> torch.Tensor:
+        qh, kh, vh = self.recompute_qkv(qkv_raw, positions, self.w.layers[layer], cos_sin)
+        o = attn_forward(qh, kh, vh, ci.starts, ci.lens, self.scale, ci.attn_groups)
+        return o.reshape(qh.shape[0], -1).to(qkv_raw.dtype)
+
+    def recompute_resid_mid(self, layer: int, layer_in: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
+        o = self._proj_lora(layer, "o", ctx, self.w.layers[layer].o)
+        if self.comm is not None:
+            self.comm.all_reduce(o)        # row-parallel: partial sums
+        return (layer_in.float() + o).to(layer_in.dtype)
 
     # ------------------------------------------------------------ layer
     def recompute_qkv(self, qkv_raw: torch.Tensor, positions: torch.Tensor, lw, cos_sin):

@@ -143,8 +143,9 @@ def paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, 
 
 
 def decode_splits(batch: int, num_kv_heads: int, max_ctx: int, num_sms: int = 148) -> tuple[int, int]:
-    """Split-KV factor so that batch x kv_heads x splits fills the GPU twice."""
-    want = max(1, (2 * num_sms) // max(1, batch * num_kv_heads))
+    """Split-KV factor so that batch x kv_heads x splits gives every SM about
+    four CTAs (two resident at a time, 100 KB of shared memory each)."""
+    want = max(1, (4 * num_sms) // max(1, batch * num_kv_heads))
     keys = max(64, -(-max_ctx // want))
     keys = -(-keys // 64) * 64
     return max(1, -(-max_ctx // keys)), keys

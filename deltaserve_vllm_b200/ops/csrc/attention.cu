@@ -11,8 +11,9 @@
 // QK^T and PV on the warp-level tensor-core path (m16n8k16), online softmax
 // in fp32 registers.
 // Decode: one CTA = (sequence, KV head, KV split): the GQA group's queries
-// share every K/V byte read; partial (max, sum, out) go to a workspace and a
-// second kernel merges the splits.
+// are the rows of one tensor-core tile and share every K/V byte read; with
+// several splits, partial (max, sum, out) go to a workspace and a second
+// kernel merges them.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -251,9 +252,11 @@ __global__ void __launch_bounds__(PF_THREADS) paged_prefill_kernel(PrefillArgs a
 
 // ------------------------------------------------------------------ decode
 
-constexpr int DC_KEYS = 64;  // keys per inner chunk
-constexpr int DC_THREADS = 128;
-constexpr int DC_MAX_GROUP = 8;
+constexpr int DC_KEYS = 64;       // keys per chunk (16 per warp)
+constexpr int DC_THREADS = 128;   // 4 warps
+constexpr int DC_MAX_GROUP = 16;  // query heads per KV head: the rows of the m16 tile
+constexpr int DC_STAGES = 3;      // cp.async ring depth
+constexpr int DC_SMEM = (16 * HD + DC_STAGES * 2 * DC_KEYS * HD) * 2;  // 100 KB: two CTAs per SM
 
 struct DecodeArgs {
   const __nv_bfloat16* q;  // [B, ...] row stride q_stride
@@ -271,116 +274,190 @@ struct DecodeArgs {
   float scale_log2;
 };
 
+// One CTA = (sequence, KV head, KV split). The GQA group's G query heads are
+// the rows of one 16 x 128 tensor-core tile (rows >= G are zero), so every
+// K/V byte is read once for the whole group. The split's keys stream through a
+// 3-stage cp.async ring of 64-key chunks; warp w scores keys [16w, 16w+16) of
+// each chunk (QK^T and PV on m16n8k16), keeping its own online-softmax state;
+// the four warps merge at the end. With one split the result is normalised
+// and stored directly; otherwise (max, sum, out) partials go to the workspace
+// for decode_combine_kernel.
 __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) {
-  // K/V chunks double-buffered in dynamic smem: chunk i+1 streams in while
-  // chunk i is scored and accumulated.
-  extern __shared__ __align__(16) uint8_t dc_smem[];
-  __nv_bfloat16* sKb = reinterpret_cast<__nv_bfloat16*>(dc_smem);   // [2][64*128]
-  __nv_bfloat16* sVb = sKb + 2 * DC_KEYS * HD;                          // [2][64*128]
-  __shared__ float sQ[DC_MAX_GROUP][HD];
-  __shared__ float sS[DC_MAX_GROUP][DC_KEYS];
-  __shared__ float sPart[2][DC_MAX_GROUP][DC_KEYS];
+  extern __shared__ __align__(128) uint8_t dc_smem[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(dc_smem);  // [16][128]
+  __nv_bfloat16* sK = sQ + 16 * HD;                                 // [STAGES][64][128]
+  __nv_bfloat16* sV = sK + DC_STAGES * DC_KEYS * HD;                // [STAGES][64][128]
 
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = a.group;
   const int ctx = a.ctx_lens[b];
   const int k_begin = split * a.keys_per_split;
   const int k_end = min(ctx, k_begin + a.keys_per_split);
+  const int n_chunks = k_end > k_begin ? (k_end - k_begin + DC_KEYS - 1) / DC_KEYS : 0;
   const int* btab = a.block_tables + (size_t)b * a.max_blocks;
 
-  for (int i = tid; i < G * HD; i += DC_THREADS) {
-    int gq = i / HD, d = i % HD;
-    sQ[gq][d] = bf2f(a.q[(size_t)b * a.q_stride + (kvh * G + gq) * HD + d]) * a.scale_log2;
+  for (int i = tid; i < 16 * 16; i += DC_THREADS) {
+    const int r = i / 16, c = i % 16;
+    const bool ok = r < G;
+    const __nv_bfloat16* src = a.q + (size_t)b * a.q_stride + (size_t)(kvh * G + (ok ? r : 0)) * HD + c * 8;
+    cp_async16(sQ + swz(r, c), src, ok);
   }
-  float m_run[DC_MAX_GROUP], l_run[DC_MAX_GROUP], acc[DC_MAX_GROUP];
+  auto load_chunk = [&](int ci, int buf) {
+    for (int i = tid; i < DC_KEYS * 16; i += DC_THREADS) {
+      const int r = i / 16, c = i % 16;
+      const int kpos = k_begin + ci * DC_KEYS + r;
+      const bool ok = kpos < k_end;
+      const int kp = ok ? kpos : k_begin;
+      const int page = btab[kp / a.block_size];
+      const size_t off =
+          (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
+      cp_async16(sK + buf * DC_KEYS * HD + swz(r, c), a.k_cache + off, ok);
+      cp_async16(sV + buf * DC_KEYS * HD + swz(r, c), a.v_cache + off, ok);
+    }
+  };
 #pragma unroll
-  for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
-    m_run[gq] = -INFINITY;
-    l_run[gq] = 0.f;
-    acc[gq] = 0.f;
+  for (int st = 0; st < DC_STAGES - 1; ++st) {
+    if (st < n_chunks) load_chunk(st, st);
+    cp_async_commit();  // group st (the first also carries Q)
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  uint32_t qf[8][4];
+  const int g = lane >> 2, tq = lane & 3;
+  const int kw = warp * 16;  // this warp's keys within a chunk
+
+  for (int ci = 0; ci < n_chunks; ++ci) {
+    const int nxt = ci + DC_STAGES - 1;
+    if (nxt < n_chunks) load_chunk(nxt, nxt % DC_STAGES);
+    cp_async_commit();
+    cp_async_wait<DC_STAGES - 1>();
+    __syncthreads();
+    if (ci == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) ldsm_x4(qf[ks], sQ + swz(lane & 15, ks * 2 + (lane >> 4)));
+    }
+    const int buf = ci % DC_STAGES;
+    const __nv_bfloat16* k_t = sK + buf * DC_KEYS * HD;
+    const __nv_bfloat16* v_t = sV + buf * DC_KEYS * HD;
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t bb[4];
+      ldsm_x4(bb, k_t + swz(kw + (lane & 7) + ((lane >> 4) << 3), ks * 2 + ((lane >> 3) & 1)));
+      mma_bf16(s[0], qf[ks], bb[0], bb[1]);
+      mma_bf16(s[1], qf[ks], bb[2], bb[3]);
+    }
+    const int key0 = k_begin + ci * DC_KEYS + kw;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = s[j][e] * a.scale_log2;
+        if (key0 + j * 8 + 2 * tq + (e & 1) >= k_end) v = -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float m_new = fmaxf(m_r[h], mx[h]);
+      corr[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_r[h] - m_new);
+      m_r[h] = m_new;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mm = m_r[e >> 1];
+        const float pv = (mm == -INFINITY) ? 0.f : exp2f(s[j][e] - mm);
+        s[j][e] = pv;
+        rs[e >> 1] += pv;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_r[h] = l_r[h] * corr[h] + rs[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16(s[0][0], s[0][1]);
+    pa[1] = pack_bf16(s[0][2], s[0][3]);
+    pa[2] = pack_bf16(s[1][0], s[1][1]);
+    pa[3] = pack_bf16(s[1][2], s[1][3]);
+#pragma unroll
+    for (int dp = 0; dp < 8; ++dp) {
+      uint32_t bb[4];
+      ldsm_x4_t(bb, v_t + swz(kw + (lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)));
+      mma_bf16(o[2 * dp], pa, bb[0], bb[1]);
+      mma_bf16(o[2 * dp + 1], pa, bb[2], bb[3]);
+    }
+    __syncthreads();  // the next prefetch overwrites this buffer
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  // Merge the four warps' (max, sum, out) in shared memory (the K ring is free now).
+  float* red_m = reinterpret_cast<float*>(sK);  // [4][16]
+  float* red_l = red_m + 4 * 16;                // [4][16]
+  float* red_o = red_l + 4 * 16;                // [4][16][128]
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = g + h * 8;
+    if (tq == 0) {
+      red_m[warp * 16 + row] = m_r[h];
+      red_l[warp * 16 + row] = l_r[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      red_o[(warp * 16 + row) * HD + j * 8 + 2 * tq] = o[j][2 * h];
+      red_o[(warp * 16 + row) * HD + j * 8 + 2 * tq + 1] = o[j][2 * h + 1];
+    }
   }
   __syncthreads();
-  auto stage = [&](int k0, int buf) {
-    for (int i = tid; i < DC_KEYS * 16; i += DC_THREADS) {
-      int r = i / 16, c = i % 16;
-      int kpos = k0 + r;
-      bool ok = kpos < k_end;
-      int kp = ok ? kpos : k_begin;
-      int page = btab[kp / a.block_size];
-      size_t off = (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
-      cp_async16(sKb + buf * DC_KEYS * HD + r * HD + c * 8, a.k_cache + off, ok);
-      cp_async16(sVb + buf * DC_KEYS * HD + r * HD + c * 8, a.v_cache + off, ok);
+  for (int i = tid; i < G * HD; i += DC_THREADS) {
+    const int r = i / HD, d = i % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w * 16 + r]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float mw = red_m[w * 16 + r];
+        if (mw == -INFINITY) continue;
+        const float sc = exp2f(mw - M);
+        L += red_l[w * 16 + r] * sc;
+        O += red_o[(w * 16 + r) * HD + d] * sc;
+      }
     }
-    cp_async_commit();
-  };
-  if (k_begin < k_end) stage(k_begin, 0);
-  int buf = 0;
-  for (int k0 = k_begin; k0 < k_end; k0 += DC_KEYS, buf ^= 1) {
-    if (k0 + DC_KEYS < k_end) {
-      stage(k0 + DC_KEYS, buf ^ 1);
-      cp_async_wait<1>();
+    const int h = kvh * G + r;
+    if (a.splits == 1) {
+      a.out[(size_t)b * a.out_stride + h * HD + d] = f2bf(L > 0.f ? O / L : 0.f);
     } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const __nv_bfloat16* sK = sKb + buf * DC_KEYS * HD;
-    const __nv_bfloat16* sV = sVb + buf * DC_KEYS * HD;
-    // Scores: thread = (key, half of the head dim).
-    {
-      const int key = tid % DC_KEYS, half = tid / DC_KEYS;
-      float part[DC_MAX_GROUP];
-#pragma unroll
-      for (int gq = 0; gq < DC_MAX_GROUP; ++gq) part[gq] = 0.f;
-      const __nv_bfloat16* kr = sK + key * HD + half * 64;
-#pragma unroll 4
-      for (int d = 0; d < 64; d += 2) {
-        float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kr + d));
-#pragma unroll
-        for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
-          if (gq < G) part[gq] += kv.x * sQ[gq][half * 64 + d] + kv.y * sQ[gq][half * 64 + d + 1];
-        }
+      const size_t idx = ((size_t)b * a.num_heads + h) * a.splits + split;
+      a.part_o[idx * HD + d] = O;
+      if (d == 0) {
+        a.part_ml[idx * 2 + 0] = M;
+        a.part_ml[idx * 2 + 1] = L;
       }
-#pragma unroll
-      for (int gq = 0; gq < DC_MAX_GROUP; ++gq)
-        if (gq < G) sPart[half][gq][key] = part[gq];
-    }
-    __syncthreads();
-    for (int i = tid; i < G * DC_KEYS; i += DC_THREADS) {
-      int gq = i / DC_KEYS, key = i % DC_KEYS;
-      sS[gq][key] = (k0 + key < k_end) ? sPart[0][gq][key] + sPart[1][gq][key] : -INFINITY;
-    }
-    __syncthreads();
-    // Online softmax + PV: thread = head-dim column d; every thread walks the
-    // 64 scores of each head (broadcast reads).
-    const int d = tid;
-#pragma unroll
-    for (int gq = 0; gq < DC_MAX_GROUP; ++gq) {
-      if (gq >= G) break;
-      float mx = -INFINITY;
-      for (int key = 0; key < DC_KEYS; ++key) mx = fmaxf(mx, sS[gq][key]);
-      float m_new = fmaxf(m_run[gq], mx);
-      float corr = (m_run[gq] == -INFINITY) ? 0.f : exp2f(m_run[gq] - m_new);
-      float lsum = 0.f, o = 0.f;
-      for (int key = 0; key < DC_KEYS; ++key) {
-        float p = (sS[gq][key] == -INFINITY) ? 0.f : exp2f(sS[gq][key] - m_new);
-        lsum += p;
-        o += p * bf2f(sV[key * HD + d]);
-      }
-      l_run[gq] = l_run[gq] * corr + lsum;
-      acc[gq] = acc[gq] * corr + o;
-      m_run[gq] = m_new;
-    }
-    __syncthreads();
-  }
-  // Partial results of this split.
-  for (int gq = 0; gq < G; ++gq) {
-    const int h = kvh * G + gq;
-    size_t idx = ((size_t)b * a.num_heads + h) * a.splits + split;
-    a.part_o[idx * HD + tid] = acc[gq];
-    if (tid == 0) {
-      a.part_ml[idx * 2 + 0] = m_run[gq];
-      a.part_ml[idx * 2 + 1] = l_run[gq];
     }
   }
 }
@@ -454,7 +531,7 @@ void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   TORCH_CHECK(keys_per_split % DC_KEYS == 0, "decode: keys_per_split must be a multiple of 64");
   const int Hkv = (int)k_cache.size(1);
   const int G = (int)(num_heads / Hkv);
-  TORCH_CHECK(G >= 1 && G <= DC_MAX_GROUP, "decode: GQA group must be 1..8");
+  TORCH_CHECK(G >= 1 && G <= DC_MAX_GROUP, "decode: GQA group must be 1..16");
   TORCH_CHECK(part_o.numel() >= (int64_t)B * num_heads * splits * HD && part_ml.numel() >= (int64_t)B * num_heads * splits * 2,
               "decode: workspace too small");
   c10::cuda::CUDAGuard guard(q.device());
@@ -478,16 +555,17 @@ void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   a.keys_per_split = (int)keys_per_split;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  const int dsmem = 4 * DC_KEYS * HD * 2;
   static bool dattr = false;
   if (!dattr) {
-    cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dsmem);
+    C10_CUDA_CHECK(cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DC_SMEM));
     dattr = true;
   }
-  paged_decode_kernel<<<dim3(B, Hkv, (unsigned)splits), DC_THREADS, dsmem, s>>>(a);
+  paged_decode_kernel<<<dim3(B, Hkv, (unsigned)splits), DC_THREADS, DC_SMEM, s>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  decode_combine_kernel<<<dim3(B, (unsigned)num_heads), HD, 0, s>>>(a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (splits > 1) {
+    decode_combine_kernel<<<dim3(B, (unsigned)num_heads), HD, 0, s>>>(a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 // ---------------------------------------------------------------- allocation-free entry point
@@ -547,12 +625,13 @@ extern "C" int dsv_paged_decode_noalloc(const void* q, int q_stride, const void*
   a.splits = splits;
   a.keys_per_split = keys_per_split;
   a.scale_log2 = scale * 1.4426950408889634f;
-  const int dsmem = 4 * DC_KEYS * HD * 2;
-  if (cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dsmem) != cudaSuccess)
+  if (cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DC_SMEM) != cudaSuccess)
     return DSV_NOALLOC_ECUDA;
-  paged_decode_kernel<<<dim3(batch, num_kv_heads, (unsigned)splits), DC_THREADS, dsmem, stream>>>(a);
+  paged_decode_kernel<<<dim3(batch, num_kv_heads, (unsigned)splits), DC_THREADS, DC_SMEM, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
-  decode_combine_kernel<<<dim3(batch, (unsigned)num_heads), HD, 0, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+  if (splits > 1) {
+    decode_combine_kernel<<<dim3(batch, (unsigned)num_heads), HD, 0, stream>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+  }
   return DSV_NOALLOC_OK;
 }

@@ -31,7 +31,8 @@
 namespace dsv {
 
 
-enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4 };
+enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4,
+                      kEpiShrink = 5 };
 
 constexpr int kMaxPeers = 8;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
@@ -46,6 +47,7 @@ constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (
 //   tile_cnt[tiles] (local)            — split-K arrivals (last split reduces).
 struct PeerArgs {
   int rank, world, owned_cap, ldo;
+  int reducers;           // CTAs [0, reducers) reduce / broadcast; the rest run the GEMM
   uint32_t* tile_cnt;
   __nv_bfloat16* recv[kMaxPeers];
   __nv_bfloat16* out[kMaxPeers];
@@ -66,6 +68,11 @@ struct GemmArgs {
   int k_splits;           // > 1: split-K, fp32 partials to `partial`, reduced by a second kernel
   float* partial;         // [k_splits, M, N]
   PeerArgs peer;          // kEpiPeerAR only
+  // kEpiShrink: B is the stacked LoRA A [slots * pr, K]; output column
+  // c = slot * pr + j lands in Z[row, slot * seg + j] when the row's slot is
+  // `slot`, else 0; the segment's padding columns [pr, seg) are zeroed.
+  const int* shrink_slot_ids;
+  int shrink_pr, shrink_seg;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -207,21 +214,24 @@ __device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile&
   }
 }
 
-// After the GEMM (all 256 threads): reduce the tiles this rank owns from the
-// world partials in local memory and write the bf16 result into every rank's
-// output (P2P stores), flag each rank; then wait until every output tile of
-// this rank has been delivered by its owner. Phases never wait on work of the
+// Reducer CTAs (all 256 threads), running next to the GEMM CTAs of the same
+// launch: as each owned tile's partials arrive from every rank, sum them from
+// local memory and write the bf16 result into every rank's output (P2P
+// stores), flag each rank; then wait until every output tile of this rank has
+// been delivered by its owner. Phases never wait on work of the
 // same phase, and the grid fits on the GPU next to the other streams' NCCL
 // kernels (every CTA can be resident), so the cross-rank waits cannot
 // deadlock; each wait is bounded.
 template <int BN>
-__device__ __forceinline__ void peer_reduce_tail(const GemmArgs& args, int m_tiles, int n_tiles) {
+__device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, int n_tiles) {
   const PeerArgs& P = args.peer;
   const int T = m_tiles * n_tiles;
   const int n_owned = (T - P.rank + P.world - 1) / P.world;
   constexpr int VPR = BN / 8;  // 16-byte vectors per tile row
   const size_t slot_stride = (size_t)P.owned_cap * BM * BN;
-  for (int j = blockIdx.x; j < n_owned; j += gridDim.x) {
+  // Owned tiles in the order the GEMM CTAs finish them (M fastest), so this
+  // CTA mostly finds its next tile already pushed.
+  for (int j = blockIdx.x; j < n_owned; j += P.reducers) {
     const int L = j * P.world + P.rank;
     if (threadIdx.x == 0) {
       wait_flag_geq(P.rflag[P.rank] + j, (uint32_t)P.world);
@@ -266,7 +276,7 @@ __device__ __forceinline__ void peer_reduce_tail(const GemmArgs& args, int m_til
       st_release_sys(P.fflag[threadIdx.x] + L, 1u);
     }
   }
-  for (int L = blockIdx.x; L < T; L += gridDim.x) {
+  for (int L = blockIdx.x; L < T; L += P.reducers) {
     if (threadIdx.x == 0) {
       wait_flag_geq(P.fflag[P.rank] + L, 1u);
       st_relaxed_sys(P.fflag[P.rank] + L, 0u);
@@ -296,6 +306,17 @@ __global__ void __launch_bounds__(256, 1)
   const int num_tiles = num_m_tiles * num_n_tiles * args.k_splits;
   const int kb_main = (args.K + BK - 1) / BK;
   const int kb_per_slot = args.lora_seg / BK;
+  // Work split of the persistent grid: with the fused all-reduce the first
+  // `reducers` CTAs only reduce / broadcast (no TMEM, no pipeline).
+  int cta0 = blockIdx.x, ncta = gridDim.x;
+  if constexpr (EPI == kEpiPeerAR) {
+    if ((int)blockIdx.x < args.peer.reducers) {
+      peer_reducer<BN>(args, num_m_tiles, num_n_tiles);
+      return;
+    }
+    cta0 -= args.peer.reducers;
+    ncta -= args.peer.reducers;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -328,7 +349,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     int fills[STAGES > 0 ? STAGES : 1];
     for (int s = 0; s < STAGES; ++s) fills[s] = 0;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+    for (int t = cta0; t < num_tiles && ok; t += ncta) {
       const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
       const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const uint32_t slots = tl.slots;
@@ -378,7 +399,7 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t phase = 0;
     int iter = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+    for (int t = cta0; t < num_tiles && ok; t += ncta, ++iter) {
       const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
       const int n_kb = tl.n_main + __popc(tl.slots) * kb_per_slot;
       const int acc = iter & 1;
@@ -420,7 +441,7 @@ __global__ void __launch_bounds__(256, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp - 4;  // TMEM lane quarter
     int iter = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+    for (int t = cta0; t < num_tiles; t += ncta, ++iter) {
       const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
       const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const int acc = iter & 1;
@@ -452,6 +473,25 @@ __global__ void __launch_bounds__(256, 1)
           if (row_ok && col < args.N)
             store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + col, v,
                           min(32, args.N - col), false);
+        }
+      } else if constexpr (EPI == kEpiShrink) {
+        const int srow = row_ok ? args.shrink_slot_ids[row] : -1;
+        const int PR = args.shrink_pr, SEG = args.shrink_seg;
+        __nv_bfloat16* zr = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll 4
+          for (int i = 0; i < 32; ++i) {
+            const int cc = n0 + c + i;
+            if (cc >= args.N) break;
+            const int sl = cc / PR, j = cc - sl * PR;
+            zr[sl * SEG + j] = f2bf(sl == srow ? __uint_as_float(r[i]) : 0.f);
+            for (int zc = PR + j; zc < SEG; zc += PR) zr[sl * SEG + zc] = f2bf(0.f);
+          }
         }
       } else if constexpr (EPI == kEpiSwiGLU) {
         // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
@@ -517,7 +557,6 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
-  if constexpr (EPI == kEpiPeerAR) peer_reduce_tail<BN>(args, num_m_tiles, num_n_tiles);
 }
 
 // Split-K epilogue: sum the fp32 partials of every split and apply the
@@ -773,6 +812,34 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   }
 }
 
+// Multi-LoRA shrink on the tensor cores: Z[T, slots*seg] from x[T, K] and the
+// stacked A factors [slots*pr, K], each row keeping only its own slot's
+// segment (rows with slot -1 get zeros). For large T; small T uses the GEMV
+// kernel in lora_misc.cu.
+void dsv_lora_shrink_tc(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t pr,
+                        int64_t seg) {
+  using namespace dsv;
+  constexpr int BN = 64;
+  const int T = (int)x.size(0), K = (int)x.size(1), N = (int)A.size(0);
+  TORCH_CHECK(A.size(1) == K && x.stride(1) == 1 && A.stride(1) == 1 && A.is_contiguous(), "lora_shrink_tc: shapes");
+  TORCH_CHECK(N % pr == 0 && Z.size(1) == (N / pr) * seg && Z.size(0) >= T && Z.stride(1) == 1, "lora_shrink_tc: Z");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  GemmArgs args{};
+  args.M = T;
+  args.N = N;
+  args.K = K;
+  args.k_splits = 1;
+  args.C = Z.data_ptr();
+  args.ldc = (int)Z.stride(0);
+  args.shrink_slot_ids = slot_ids.data_ptr<int>();
+  args.shrink_pr = (int)pr;
+  args.shrink_seg = (int)seg;
+  CUtensorMap ta = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), BM);
+  CUtensorMap tb = make_tmap_bf16(A.data_ptr(), N, K, A.stride(0), BN);
+  launch<BN, false, kEpiShrink>(ta, tb, ta, tb, args, at::cuda::getCurrentCUDAStream());
+}
+
 // out = all_reduce_over_ranks(a @ b^T (+ LoRA expand)), fused: the GEMM's
 // epilogue pushes bf16 partial tiles to their owner rank over peer memory and
 // the same launch reduces the owned tiles and broadcasts them.
@@ -808,7 +875,7 @@ torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch:
   if (force_splits > 0) {
     splits = (int)force_splits;
   } else if (m_tiles == 1 && tiles < num_sms() / 2 && kbs >= 8) {
-    splits = std::max(1, std::min({(num_sms() - kArSmReserve) / tiles, kbs / 4, 16}));
+    splits = std::max(1, std::min({(num_sms() - kArSmReserve - 8) / tiles, kbs / 4, 16}));
   }
   if (splits > 1) {
     const int per = (kbs + splits - 1) / splits;
@@ -865,7 +932,11 @@ torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch:
   // CTA waiting on a peer never keeps the peer's partner CTA (or the peer's
   // NCCL kernel) from being scheduled. A cooperative launch would give the
   // same guarantee but waits for the whole GPU to drain first.
-  const int grid = std::min(tiles * splits, std::max(1, num_sms() - kArSmReserve));
+  const int n_owned = (tiles - (int)rank + (int)world - 1) / (int)world;
+  const int budget = std::max(2, num_sms() - kArSmReserve);
+  P.reducers = std::max(1, std::min({n_owned, tiles >= 256 ? 16 : 8, budget / 4}));
+  const int gemm_ctas = std::max(1, std::min(tiles * splits, budget - P.reducers));
+  const int grid = P.reducers + gemm_ctas;
   gemm_tc_kernel<BN, false, kEpiPeerAR><<<grid, 256, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(
       ta, tb, tz, tb2, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

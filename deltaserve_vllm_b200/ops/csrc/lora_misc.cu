@@ -341,6 +341,9 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
 
 }  // namespace dsv
 
+void dsv_lora_shrink_tc(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t pr,
+                        int64_t seg);
+
 void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t seg) {
   using namespace dsv;
   const int T = (int)x.size(0);
@@ -357,6 +360,12 @@ void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, t
         reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),
         reinterpret_cast<__nv_bfloat16*>(Z.data_ptr()), (int)Z.stride(0), T, K, PR, (int)seg, slots);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  if (T >= 256 && x.stride(0) % 8 == 0 && A.is_contiguous() && (uintptr_t)x.data_ptr() % 16 == 0) {
+    // Large batches: a tcgen05 GEMM over the stacked factors (x read once per
+    // 64-column tile of slots * P * R, from L2 after the first).
+    dsv_lora_shrink_tc(x, A.view({slots * PR, K}), slot_ids, Z, PR, seg);
     return;
   }
   dim3 grid((T + SHR_ROWS - 1) / SHR_ROWS, (PR + SHR_OUT - 1) / SHR_OUT);

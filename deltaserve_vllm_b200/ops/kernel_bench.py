@@ -120,13 +120,13 @@ def _shrink(T, K, PR, slots=2, seg=64):
 
 def _rope(T, Hq=32, Hkv=8):
     qkv = rnd(T, (Hq + 2 * Hkv) * 128, seed=1)
-    pos = torch.arange(T, dtype=torch.int32, device=DEV)
+    pos = torch.arange(T, dtype=torch.int64, device=DEV)
     cs = ops.ref.rope_cos_sin_table(8192, 128, 5e5, None, device=DEV)
     bs = 64
     nb = -(-T // bs) + 1
     kc = torch.zeros(nb, Hkv, bs, 128, dtype=torch.bfloat16, device=DEV)
     vc = torch.zeros_like(kc)
-    slots = torch.arange(T, dtype=torch.int32, device=DEV)
+    slots = torch.arange(T, dtype=torch.int64, device=DEV)
     return (lambda: ops.qk_norm_rope_cache(qkv, pos, cs, None, None, 1e-6, Hq, Hkv, kc, vc, slots),
             2 * (2 * qkv.numel() + 2 * T * Hkv * 128), 0)
 

@@ -20,7 +20,7 @@ def run_smoke() -> None:
     ecfg = EngineConfig(model="llama3-8b-2l", max_model_len=2048, block_size=64,
                         max_num_batched_tokens=2048, max_loras=2, max_lora_rank=16,
                         num_gpu_blocks_override=128)
-    fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=512, learning_rate=1e-4)
+    fcfg = FinetuneConfig(enable_finetuning=True, backward_cuda_graph=True, max_saved_finetuning_tokens=512, learning_rate=1e-4)
     store = FinetuningStore.synthetic(8192, 2, 256, 256, seed=0, max_saved_finetuning_tokens=512)
     eng = CoServingEngine(ecfg, fcfg, ft_store=store)
     eng.load_inference_adapter("inf", rank=16, alpha=32)

@@ -67,3 +67,32 @@ def test_profiling_failure_disables_finetuning(monkeypatch):
         eng.add_request("x", list(range(10)), SamplingParams(max_tokens=2))
         eng.run_until_idle(max_steps=100)
         assert len(eng.finished) == 1 and eng.stats["ft_tokens_forwarded"] == 0
+
+
+def test_recompute_matches_saved_activations_cpu():
+    """save_attn_qkv / save_attn_ctx / save_resid_mid off: the backward
+    recomputes those activations; losses and trained adapters match the run
+    that captured them."""
+    import tempfile as _tf
+    outs = []
+    for flags in ({}, {"save_attn_qkv": False, "save_attn_ctx": False, "save_resid_mid": False}):
+        with _tf.TemporaryDirectory() as tmp:
+            eng = make_engine(tmp, **flags)
+            eng.run_until_idle(max_steps=2000)
+            outs.append((list(eng.trainer.losses), eng.trainer.export_full()))
+    (l0, a0), (l1, a1) = outs
+    assert len(l0) == len(l1) >= 2
+    for x, y in zip(l0, l1):
+        assert abs(x - y) < 1e-3 * max(1.0, abs(x)), (l0, l1)
+    for k in a0:
+        torch.testing.assert_close(a0[k], a1[k], rtol=1e-3, atol=1e-5)
+
+
+def test_save_activations_off_trains_nothing_cpu():
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp, save_activations=False)
+        eng.run_until_idle(max_steps=2000)
+        assert eng.capture is None
+        assert eng.trainer.step == 0
+        assert eng.store.finished()            # samples were forwarded and retired
+        assert eng.coord.completed_cycles >= 1

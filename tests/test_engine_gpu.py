@@ -76,7 +76,8 @@ def test_gpu_coserving_engine_runs_cycles():
     ecfg = EngineConfig(model="qwen3-test", max_model_len=1024, block_size=64,
                         max_num_batched_tokens=2048, max_loras=2, max_lora_rank=16,
                         num_gpu_blocks_override=256)
-    fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=512, learning_rate=1e-3)
+    fcfg = FinetuneConfig(enable_finetuning=True, backward_cuda_graph=True, max_saved_finetuning_tokens=512,
+                          learning_rate=1e-3)
     store = FinetuningStore.synthetic(4096, 40, 64, 128, seed=0, max_saved_finetuning_tokens=512,
                                       total_epochs=2)
     eng = CoServingEngine(ecfg, fcfg, ft_store=store)
