@@ -145,7 +145,7 @@ class DecoderModel:
         workspace on the communicator (``tp_comm: fused``) both happen in one
         kernel over NVLink peer memory; otherwise GEMM then NCCL all-reduce."""
         ws = getattr(self.comm, "peer_ws", None)
-        if ws is None or not ws.fits(x.shape[0], w.shape[0]):
+        if ws is None or not ws.prefer(x.shape[0], w.shape[0]):
             self._proj(x, w, out, layer, group, b)
             return self.comm.all_reduce(out)
         kw = {}

@@ -72,7 +72,7 @@ def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=Non
                     save_dst)
 
 
-def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_splits=0):
+def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_splits=0, force_reducers=-1):
     """All-reduce over the ranks of ``ws`` (a :class:`~..parallel.peer.PeerWorkspace`)
     of ``a @ b.T`` (+ the segmented LoRA expand), in ONE kernel: the GEMM
     epilogue pushes bf16 partial tiles to their owner rank over peer memory,
@@ -86,7 +86,7 @@ def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_spl
                          f"([{ws.max_rows}, {ws.n_cols}])")
     ws.calls += 1
     return _native().gemm_ar(a, b, z, b2, tile_slots, lora_seg, ws.table, ws.tile_cnt, ws.rank,
-                             ws.world, ws.owned_cap, ws.max_rows, force_splits)
+                             ws.world, ws.owned_cap, ws.max_rows, force_splits, force_reducers)
 
 
 def linear(x, w, out=None, epi=EPI_BF16, **kw):

@@ -11,7 +11,7 @@ void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10
 torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z,
                           c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots, int64_t lora_seg,
                           torch::Tensor peer, int64_t tile_cnt, int64_t rank, int64_t world, int64_t owned_cap,
-                          int64_t out_rows, int64_t force_splits);
+                          int64_t out_rows, int64_t force_splits, int64_t force_reducers);
 std::tuple<int64_t, std::string> dsv_peer_alloc(int64_t bytes);
 int64_t dsv_peer_open(const std::string& handle);
 void dsv_peer_close(int64_t addr);

@@ -32,7 +32,7 @@ namespace dsv {
 
 
 enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4,
-                      kEpiShrink = 5 };
+                      kEpiShrink = 5, kEpiBF16T = 6 };
 
 constexpr int kMaxPeers = 8;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
@@ -73,6 +73,9 @@ struct GemmArgs {
   // `slot`, else 0; the segment's padding columns [pr, seg) are zeroed.
   const int* shrink_slot_ids;
   int shrink_pr, shrink_seg;
+  // Swapped operands (kEpiBF16T, decode): the LoRA slots of every tile are
+  // the OR of tile_slots[0, slot_or) (the token tiles), not tile_slots[mt].
+  int slot_or;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -92,7 +95,14 @@ __device__ __forceinline__ Tile decode_tile(int t, const GemmArgs& a, int m_tile
   r.kb_lo = r.ks * per;
   r.n_main = min(kb_main, r.kb_lo + per) - r.kb_lo;
   // LoRA expand blocks ride with the last split only.
-  r.slots = (a.lora_seg > 0 && r.ks == a.k_splits - 1) ? a.tile_slots[r.mt] : 0u;
+  r.slots = 0u;
+  if (a.lora_seg > 0 && r.ks == a.k_splits - 1) {
+    if (a.slot_or > 0) {
+      for (int i = 0; i < a.slot_or; ++i) r.slots |= a.tile_slots[i];
+    } else {
+      r.slots = a.tile_slots[r.mt];
+    }
+  }
   return r;
 }
 
@@ -106,7 +116,8 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGING = 4 * 2048;  // epilogue: 2 KB per epilogue warp (32 rows x 64 B)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + STAGING;
 };
 
 __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float* v, int n_valid) {
@@ -142,16 +153,45 @@ __device__ __forceinline__ void store_row_f32(float* dst, const float* v, int n_
 // thread bumps the owner's arrival counter with release semantics. With
 // split-K the splits first meet in the fp32 workspace and the last split to
 // arrive (atomic ticket) sums them and pushes.
+// Write 32 rows x 32 columns (this warp's rows, columns c..c+31 of the
+// tile) to the owner's receive tile: each lane puts its row into the warp's
+// 2 KB staging area, then the warp stores row segments so that every store
+// instruction writes eight full 64-byte row pieces (whole sectors over
+// NVLink instead of 16-byte fragments of 32 different rows).
+template <int BN>
+__device__ __forceinline__ void push_rows_32x32(uint4* stg, const float* v, __nv_bfloat16* tile_base, int q,
+                                                int lane, int c, int rows_valid) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    pk[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    stg[lane * 4 + (k ^ (lane & 3))] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2), ch = lane & 3;
+    const uint4 val = stg[r * 4 + (ch ^ (r & 3))];
+    if (q * 32 + r < rows_valid)
+      *reinterpret_cast<uint4*>(tile_base + (size_t)(q * 32 + r) * BN + c + ch * 8) = val;
+  }
+  __syncwarp();
+}
+
 template <int BN>
 __device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile& tl, uint32_t t_row, int row,
-                                               bool row_ok, bool acc_ok, int q, int lane, int m_tiles) {
+                                               bool row_ok, bool acc_ok, int q, int lane, int m_tiles,
+                                               uint4* stg) {
   __shared__ int s_last;
   const PeerArgs& P = args.peer;
   const int L = tl.nt * m_tiles + tl.mt;
   const int owner = L % P.world, local = L / P.world;
   const int n0 = tl.nt * BN;
-  const int rt = q * 32 + lane;
-  __nv_bfloat16* dst = P.recv[owner] + ((size_t)P.rank * P.owned_cap + local) * (BM * BN) + (size_t)rt * BN;
+  const int rows_valid = min(BM, args.M - tl.mt * BM);
+  __nv_bfloat16* tile_base = P.recv[owner] + ((size_t)P.rank * P.owned_cap + local) * (BM * BN);
   bool push = true;
   if (args.k_splits > 1) {
 #pragma unroll 1
@@ -174,25 +214,27 @@ __device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile&
     }
     named_bar_sync(1, 128);
     push = s_last != 0;
-    if (push && row_ok) {
+    if (push) {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        for (int sp = 0; sp < args.k_splits; ++sp) {
-          const float4* src =
-              reinterpret_cast<const float4*>(args.partial + ((size_t)sp * args.M + row) * args.N + n0 + c);
+        if (row_ok) {
+          for (int sp = 0; sp < args.k_splits; ++sp) {
+            const float4* src =
+                reinterpret_cast<const float4*>(args.partial + ((size_t)sp * args.M + row) * args.N + n0 + c);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float4 f = __ldcg(src + i);
-            v[4 * i] += f.x;
-            v[4 * i + 1] += f.y;
-            v[4 * i + 2] += f.z;
-            v[4 * i + 3] += f.w;
+            for (int i = 0; i < 8; ++i) {
+              const float4 f = __ldcg(src + i);
+              v[4 * i] += f.x;
+              v[4 * i + 1] += f.y;
+              v[4 * i + 2] += f.z;
+              v[4 * i + 3] += f.w;
+            }
           }
         }
-        store_row_bf16(dst + c, v, 32);
+        push_rows_32x32<BN>(stg, v, tile_base, q, lane, c, rows_valid);
       }
     }
   } else {
@@ -204,7 +246,7 @@ __device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile&
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      if (row_ok) store_row_bf16(dst + c, v, 32);
+      push_rows_32x32<BN>(stg, v, tile_base, q, lane, c, rows_valid);
     }
   }
   named_bar_sync(1, 128);
@@ -222,47 +264,88 @@ __device__ __forceinline__ void peer_push_tile(const GemmArgs& args, const Tile&
 // same phase, and the grid fits on the GPU next to the other streams' NCCL
 // kernels (every CTA can be resident), so the cross-rank waits cannot
 // deadlock; each wait is bounded.
+// The owned tiles' partials stream into shared memory with 1-D bulk copies
+// (this GPU's own receive buffer: plain cp.async.bulk, no multicast), in
+// row chunks of world x rc x BN bf16 (<= 64 KB), double-buffered so the copy
+// of the next chunk overlaps the sum and P2P broadcast of this one.
 template <int BN>
-__device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, int n_tiles) {
+__device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, int n_tiles, int rid, int nr,
+                                             uint8_t* smem) {
   const PeerArgs& P = args.peer;
   const int T = m_tiles * n_tiles;
   const int n_owned = (T - P.rank + P.world - 1) / P.world;
   constexpr int VPR = BN / 8;  // 16-byte vectors per tile row
   const size_t slot_stride = (size_t)P.owned_cap * BM * BN;
-  // Owned tiles in the order the GEMM CTAs finish them (M fastest), so this
-  // CTA mostly finds its next tile already pushed.
-  for (int j = blockIdx.x; j < n_owned; j += P.reducers) {
-    const int L = j * P.world + P.rank;
-    if (threadIdx.x == 0) {
+  const int rc = min(BM, (32768 / (BN * 2) * 2) / P.world);   // rows per chunk: world*rc*BN*2 <= 64 KB
+  const int chunks = BM / rc;
+  const uint32_t slot_bytes = (uint32_t)(rc * BN * 2);
+  const int buf_bytes = P.world * (int)slot_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * buf_bytes);  // [2]
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int my_tiles = rid < n_owned ? (n_owned - rid + nr - 1) / nr : 0;
+  const int items = my_tiles * chunks;
+  // Thread 0 issues item i (this CTA's tile i / chunks, row chunk i % chunks)
+  // into buffer i & 1. The first chunk of a tile needs the tile's partials
+  // from every rank: without `block` it only issues when they are there.
+  auto issue = [&](int i, bool block) -> bool {
+    const int j = rid + (i / chunks) * nr, c = i % chunks;
+    if (c == 0) {
+      if (!block && ld_acquire_sys(P.rflag[P.rank] + j) < (uint32_t)P.world) return false;
       wait_flag_geq(P.rflag[P.rank] + j, (uint32_t)P.world);
       st_relaxed_sys(P.rflag[P.rank] + j, 0u);
     }
-    __syncthreads();
+    uint8_t* dst = smem + (i & 1) * buf_bytes;
+    fence_proxy_async_smem();  // the buffer's last generic reads come before the copy into it
+    mbar_arrive_expect_tx(&bar[i & 1], (uint32_t)buf_bytes);
+    const __nv_bfloat16* src = P.recv[P.rank] + (size_t)j * BM * BN + (size_t)c * rc * BN;
+    for (int sl = 0; sl < P.world; ++sl)
+      bulk_load_1d(dst + sl * slot_bytes, src + sl * slot_stride, slot_bytes, &bar[i & 1]);
+    return true;
+  };
+  int issued = 0;  // thread 0's count of issued items
+  if (threadIdx.x == 0 && items > 0) issued = issue(0, true) ? 1 : 0;
+  bool ok = true;
+  int waited = 0;
+  for (int i = 0; i < items && ok; ++i) {
+    // Prefetch the next chunk while this one is summed, if its data is ready.
+    if (threadIdx.x == 0 && issued == i + 1 && i + 1 < items && issue(i + 1, false)) issued = i + 2;
+    ok = mbar_wait(&bar[i & 1], (uint32_t)((i >> 1) & 1), kErrWaitPeer);
+    if (!ok) break;
+    waited = i + 1;
+    const int j = rid + (i / chunks) * nr, c = i % chunks;
+    const int L = j * P.world + P.rank;
     const int mt = L % m_tiles, nt = L / m_tiles;
-    const int m0 = mt * BM, n0 = nt * BN;
-    const int rows = min(BM, args.M - m0);
-    const __nv_bfloat16* src = P.recv[P.rank] + (size_t)j * BM * BN;
+    const int m0 = mt * BM + c * rc, n0 = nt * BN;
+    const int rows = max(0, min(rc, args.M - m0));
+    const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(smem + (i & 1) * buf_bytes);
     for (int e = threadIdx.x; e < rows * VPR; e += blockDim.x) {
       const int r = e / VPR, c8 = (e - r * VPR) * 8;
       float acc[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
       for (int sl = 0; sl < P.world; ++sl) {
-        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src + sl * slot_stride + (size_t)r * BN + c8));
+        const uint4 u = *reinterpret_cast<const uint4*>(sb + sl * (slot_bytes / 2) + r * BN + c8);
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h[i]);
-          acc[2 * i] += f.x;
-          acc[2 * i + 1] += f.y;
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
         }
       }
       uint4 o;
       uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-        ow[i] = *reinterpret_cast<uint32_t*>(&h2);
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+        ow[k] = *reinterpret_cast<uint32_t*>(&h2);
       }
       const size_t off = (size_t)(m0 + r) * P.ldo + n0 + c8;
       for (int d = 0; d < P.world; ++d) {
@@ -270,13 +353,29 @@ __device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, 
         *reinterpret_cast<uint4*>(P.out[dr] + off) = o;
       }
     }
-    __syncthreads();
-    if (threadIdx.x < P.world) {
+    __syncthreads();  // buffer i & 1 is free again; every store of this chunk issued
+    if (c == chunks - 1 && threadIdx.x < P.world) {
       __threadfence_system();
       st_release_sys(P.fflag[threadIdx.x] + L, 1u);
     }
+    // Not prefetched (its partials were still on the way): issue it now.
+    if (threadIdx.x == 0 && issued == i + 1 && i + 1 < items) issued = issue(i + 1, true) ? i + 2 : issued;
   }
-  for (int L = blockIdx.x; L < T; L += P.reducers) {
+  // Copies of this GPU's own memory always land: wait for any still in flight
+  // (bounded, ignoring other CTAs' errors) before shared memory is released.
+  if (threadIdx.x == 0) {
+    for (int i = waited; i < issued; ++i) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&bar[i & 1], (uint32_t)((i >> 1) & 1))) {
+        if (globaltimer_ns() - t0 > kWaitNs) {
+          set_error(kErrWaitPeer);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int L = rid; L < T; L += nr) {
     if (threadIdx.x == 0) {
       wait_flag_geq(P.fflag[P.rank] + L, 1u);
       st_relaxed_sys(P.fflag[P.rank] + L, 0u);
@@ -298,6 +397,7 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* acce_bar = accf_bar + 2;        // [2]
   uint64_t* drain_bar = acce_bar + 2;       // [1]
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * Cfg::STAGE_BYTES + 256);  // [4 warps][2 KB]
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -311,7 +411,7 @@ __global__ void __launch_bounds__(256, 1)
   int cta0 = blockIdx.x, ncta = gridDim.x;
   if constexpr (EPI == kEpiPeerAR) {
     if ((int)blockIdx.x < args.peer.reducers) {
-      peer_reducer<BN>(args, num_m_tiles, num_n_tiles);
+      peer_reducer<BN>(args, num_m_tiles, num_n_tiles, blockIdx.x, args.peer.reducers, smem);
       return;
     }
     cta0 -= args.peer.reducers;
@@ -458,7 +558,8 @@ __global__ void __launch_bounds__(256, 1)
       if constexpr (EPI == kEpiPeerAR) {
         // Keeps iterating after a failed wait (with the TMEM reads skipped) so
         // the four epilogue warps always meet at their named barriers.
-        peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles);
+        peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles,
+                           staging + q * 128);
       } else if (args.k_splits > 1) {
         // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
 #pragma unroll 1
@@ -473,6 +574,23 @@ __global__ void __launch_bounds__(256, 1)
           if (row_ok && col < args.N)
             store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + col, v,
                           min(32, args.N - col), false);
+        }
+      } else if constexpr (EPI == kEpiBF16T) {
+        // Swapped operands: accumulator rows are output features (this
+        // thread's TMEM lane), columns are tokens; C is [tokens, features].
+        // A warp writes 32 consecutive features of one token per store.
+        __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(args.C);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll 8
+          for (int i = 0; i < 32; ++i) {
+            const int tok = n0 + c + i;
+            if (tok < args.N) cb[(size_t)tok * args.ldc + row] = f2bf(__uint_as_float(r[i]));
+          }
         }
       } else if constexpr (EPI == kEpiShrink) {
         const int srow = row_ok ? args.shrink_slot_ids[row] : -1;
@@ -557,6 +675,11 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  if constexpr (EPI == kEpiPeerAR) {
+    // No dedicated reducers (one wave of GEMM work): the GEMM CTAs reduce and
+    // broadcast the owned tiles themselves once their own tiles are pushed.
+    if (args.peer.reducers == 0) peer_reducer<BN>(args, num_m_tiles, num_n_tiles, cta0, ncta, smem);
+  }
 }
 
 // Split-K epilogue: sum the fp32 partials of every split and apply the
@@ -583,6 +706,18 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
         sv[cg] = f2bf(g);
         sv[cg + 64] = f2bf(u);
       }
+    }
+    return;
+  }
+  if (epi == kEpiBF16T) {
+    // Partials are [features M, tokens N]; C is [tokens, features]: walk it
+    // feature-fastest so consecutive threads store consecutive features.
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)plane;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int feat = (int)(i % M), tok = (int)(i / M);
+      float v = 0.f;
+      for (int s = 0; s < splits; ++s) v += partial[s * plane + (size_t)feat * N + tok];
+      reinterpret_cast<__nv_bfloat16*>(C)[(size_t)tok * ldc + feat] = f2bf(v);
     }
     return;
   }
@@ -683,7 +818,8 @@ static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set = true;
   }
-  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN);
+  // Work units include the K splits: each split of a tile is its own CTA's work.
+  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN) * std::max(1, args.k_splits);
   // Persistent (one CTA per SM) by default; a larger cap makes CTAs retire
   // after one tile so a higher-priority stream can interleave at tile
   // granularity (used for the low-priority backward).
@@ -732,6 +868,62 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "dsv_gemm: output dtype");
   TORCH_CHECK(K > 0, "dsv_gemm: empty reduction");
   c10::cuda::CUDAGuard guard(a.device());
+  // Decode-sized batches (one M tile, plain bf16 store, no row capture): swap
+  // the operands so the weights fill the 128-row side of the MMA and stream
+  // at full tile width; the tokens become a 64/128-wide N tile and the
+  // epilogue stores the transposed accumulator.
+  if (!b_mn && M <= 128 && epi == kEpiBF16 && !save.has_value() && force_bn == 0 && max_ctas == 0 &&
+      N >= 256 && (N % 8) == 0) {
+    const int bnt = M <= 64 ? 64 : 128;
+    const int tiles = (N + BM - 1) / BM;
+    const int kbs = (K + BK - 1) / BK;
+    int splits = 1;
+    if (tiles < num_sms() && kbs >= 8) {
+      splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
+      const int per = (kbs + splits - 1) / splits;
+      splits = (kbs + per - 1) / per;
+    }
+    GemmArgs args{};
+    args.M = N;
+    args.N = M;
+    args.K = K;
+    args.k_splits = splits;
+    args.C = out.data_ptr();
+    args.ldc = (int)out.stride(0);
+    at::Tensor partial;
+    if (splits > 1) {
+      partial = at::empty({splits, N, M}, a.options().dtype(at::kFloat));
+      args.partial = partial.data_ptr<float>();
+    }
+    CUtensorMap ta = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), BM);
+    CUtensorMap tb = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), bnt);
+    CUtensorMap tz = ta, tb2 = tb;
+    if (lora_seg > 0) {
+      TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "dsv_gemm: LoRA operands missing");
+      TORCH_CHECK(lora_seg % 64 == 0, "dsv_gemm: lora_seg must be a multiple of 64");
+      auto& zt = *z;
+      auto& bt = *b2;
+      TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm: LoRA shapes");
+      TORCH_CHECK(tile_slots->scalar_type() == at::kInt && tile_slots->numel() >= 1, "dsv_gemm: tile_slots");
+      tz = make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), BM);     // expand factor: A side
+      tb2 = make_tmap_bf16(zt.data_ptr(), M, zt.size(1), zt.stride(0), bnt);   // shrunk tokens: B side
+      args.lora_seg = (int)lora_seg;
+      args.num_slots = (int)(zt.size(1) / lora_seg);
+      args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
+      args.slot_or = 1;
+    }
+    cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    if (bnt == 64) launch<64, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
+    else launch<128, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
+    if (splits > 1) {
+      const int64_t work = (int64_t)M * N;
+      const int blocks = (int)std::min<int64_t>(4096, (work + 255) / 256);
+      splitk_reduce_kernel<<<blocks, 256, 0, st>>>(args.partial, splits, N, M, (int)kEpiBF16T, out.data_ptr(),
+                                                   args.ldc, nullptr, 0, 0, 0, 0);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
+    return;
+  }
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
   if (b_mn && bn < 64) bn = 64;
   if (epi == kEpiSwiGLU && bn < 128) bn = 128;
@@ -850,7 +1042,7 @@ void dsv_lora_shrink_tc(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids
 torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z,
                           c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots, int64_t lora_seg,
                           torch::Tensor peer, int64_t tile_cnt, int64_t rank, int64_t world, int64_t owned_cap,
-                          int64_t out_rows, int64_t force_splits) {
+                          int64_t out_rows, int64_t force_splits, int64_t force_reducers) {
   using namespace dsv;
   TORCH_CHECK(a.is_cuda() && b.is_cuda(), "dsv_gemm_ar: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm_ar: bf16 operands");
@@ -934,7 +1126,13 @@ torch::Tensor dsv_gemm_ar(torch::Tensor a, torch::Tensor b, c10::optional<torch:
   // same guarantee but waits for the whole GPU to drain first.
   const int n_owned = (tiles - (int)rank + (int)world - 1) / (int)world;
   const int budget = std::max(2, num_sms() - kArSmReserve);
-  P.reducers = std::max(1, std::min({n_owned, tiles >= 256 ? 16 : 8, budget / 4}));
+  // One wave of GEMM work: the GEMM CTAs reduce afterwards (reducers = 0).
+  // Several waves: dedicated reducer CTAs overlap the exchange with the GEMM.
+  // Measured at TP=2 (M = 64..4096): reducing in the GEMM CTAs after their
+  // tiles beats dedicated reducer CTAs at every size, so that is the default.
+  (void)n_owned;
+  P.reducers = 0;
+  if (force_reducers >= 0) P.reducers = (int)std::min<int64_t>(force_reducers, budget / 2);
   const int gemm_ctas = std::max(1, std::min(tiles * splits, budget - P.reducers));
   const int grid = P.reducers + gemm_ctas;
   gemm_tc_kernel<BN, false, kEpiPeerAR><<<grid, 256, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(

@@ -57,6 +57,8 @@ def main(argv=None) -> None:
     peak = _peaks()
     g = torch.Generator(device="cuda").manual_seed(rank)
     for name, M, K in [("o_decode", 64, 4096 // tp), ("down_decode", 64, 14336 // tp),
+                       ("o_m256", 256, 4096 // tp), ("o_m1024", 1024, 4096 // tp),
+                       ("down_m1024", 1024, 14336 // tp), ("o_m2048", 2048, 4096 // tp),
                        ("o_prefill", 4096, 4096 // tp), ("down_prefill", 4096, 14336 // tp)]:
         N = 4096
         a = torch.randn(M, K, generator=g, device="cuda").bfloat16()
@@ -73,7 +75,14 @@ def main(argv=None) -> None:
         def fused():
             ops.gemm_ar(a, b, ws)
 
+        def fused_r0():      # GEMM CTAs reduce after their tiles
+            ops.gemm_ar(a, b, ws, force_reducers=0)
+
+        def fused_r16():     # 16 dedicated reducer CTAs overlap the exchange
+            ops.gemm_ar(a, b, ws, force_reducers=16)
+
         t_base, t_gemm, t_fused = _time(base, args.iters), _time(gemm_only, args.iters), _time(fused, args.iters)
+        t_r0, t_r16 = _time(fused_r0, args.iters), _time(fused_r16, args.iters)
         ref = a.float() @ b.float().t()
         dist.all_reduce(ref)
         err = float((ops.gemm_ar(a, b, ws).float() - ref).abs().max() / ref.abs().max())
@@ -83,6 +92,7 @@ def main(argv=None) -> None:
         if rank == 0:
             print(json.dumps({"case": name, "tp": tp, "M": M, "N": N, "K": K, "gemm_ms": round(t_gemm, 4),
                               "gemm_nccl_ms": round(t_base, 4), "fused_ms": round(t_fused, 4),
+                              "fused_r0_ms": round(t_r0, 4), "fused_r16_ms": round(t_r16, 4),
                               "speedup_vs_nccl": round(t_base / t_fused, 3),
                               "roofline_ms": round(bound_ms, 4), "frac_roofline": round(bound_ms / t_fused, 3),
                               "max_rel_err": round(err, 5), "peaks": peak["src"]}), flush=True)

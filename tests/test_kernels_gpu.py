@@ -340,3 +340,27 @@ def test_gemm_allreduce_single_rank_lora():
         torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
     finally:
         ws.close()
+
+
+@pytest.mark.parametrize("M,N,K", [(5, 1024, 512), (64, 4096, 2048), (100, 768, 4096)])
+def test_gemm_decode_swapped_lora(M, N, K):
+    """Decode-sized GEMM (swapped operands: weights on the MMA's 128-row side)
+    with the multi-LoRA expand over the slots of the batch."""
+    slots, P, R, seg = 3, 1, 16, 64
+    x, w = rnd(M, K, seed=31), rnd(N, K, scale=0.05, seed=32)
+    A = rnd(slots, P * R, K, scale=0.05, seed=33)
+    B2 = rnd(N, slots * seg, scale=0.05, seed=34)
+    slot_ids = torch.randint(-1, slots, (M,), device=DEV, dtype=torch.int32).sort()[0]
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, slot_ids, Z, seg)
+    mask = torch.zeros(1, dtype=torch.int32)
+    for s in slot_ids.cpu().unique().tolist():
+        if s >= 0:
+            mask[0] |= 1 << s
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, z=Z, b2=B2, tile_slots=mask.to(DEV), lora_seg=seg)
+    exp = x.float() @ w.float().t() + Z.float() @ B2.float().t()
+    torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+    plain = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, plain)
+    torch.testing.assert_close(plain.float(), x.float() @ w.float().t(), rtol=2e-2, atol=3e-2)
