@@ -142,6 +142,21 @@ def reference_arm(args) -> None:
     print(json.dumps(line))
 
 
+def _exit_watchdog(seconds: float = 90.0) -> None:
+    """The result line is out: if tearing down (graphs, peer mappings, process
+    group) takes longer than ``seconds``, dump every thread's stack and exit."""
+    import faulthandler
+    import threading
+
+    def fire():
+        faulthandler.dump_traceback(all_threads=True)
+        sys.stderr.flush()
+        os._exit(0)
+    t = threading.Timer(seconds, fire)
+    t.daemon = True
+    t.start()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -189,6 +204,7 @@ def main():
         eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
     if rank != 0:
         eng.follow()
+        _exit_watchdog()
         eng.close()
         if comm is not None:
             torch.distributed.destroy_process_group()
@@ -256,6 +272,14 @@ def main():
     value = st["ft_tokens_forwarded"] / (dev_ms / 1e3)
     e2e = st["ft_tokens_forwarded"] / (wall_ms / 1e3)
     cs = clocks.summary()
+    # Decode-only steps: host time to enqueue the forward vs its GPU time
+    # (launch-bound when the first is larger).
+    dec_gpu = [d for f, d in zip(eng.tracker.features, eng.tracker.durations)
+               if f.t_in == 0 and f.t_ft == 0 and f.b_d > 0]
+    n_dec = eng.stats.get("decode_steps", 0)
+    dec_info = {"host_enqueue_ms": round(1e3 * eng.stats.get("decode_enqueue_s", 0.0) / max(1, n_dec), 3),
+                "gpu_ms": round(1e3 * float(np.mean(dec_gpu)), 3) if dec_gpu else None,
+                "steps": n_dec}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "FT tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -279,9 +303,11 @@ def main():
                 "h2d_bytes_per_step": int(st["h2d_bytes"] / max(1, st["steps"])),
                 "d2h_bytes_per_step": int(st["d2h_bytes"] / max(1, st["steps"]))},
         "gpu_launches": int(launches), "clocks": cs, "device_ms_per_rank": [round(r[0], 2) for r in regions],
+        "decode_steps": dec_info,
     }
     eng.shutdown()
     print(json.dumps(line), flush=True)
+    _exit_watchdog()
     eng.close()
     if comm is not None:
         torch.distributed.destroy_process_group()

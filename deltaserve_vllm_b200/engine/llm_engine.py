@@ -124,7 +124,8 @@ class CoServingEngine:
         self.scheduler = Scheduler(self.kv.allocator, ecfg.block_size, ecfg.max_num_seqs,
                                    ecfg.max_num_batched_tokens, ecfg.max_model_len,
                                    ecfg.enable_chunked_prefill)
-        self.runner = ModelRunner(self.model, ecfg.block_size, self.device, num_sms)
+        self.runner = ModelRunner(self.model, ecfg.block_size, self.device, num_sms,
+                                  max_model_len=ecfg.max_model_len, decode_graphs=not ecfg.enforce_eager)
         # Backward collectives use their own communicator: forward and backward
         # run on different streams and must never share an NCCL queue.
         self.bwd_comm = comm
@@ -675,6 +676,10 @@ class CoServingEngine:
             toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
                                           before_sample=feed)
             ev1 = time.perf_counter()
+        if not out.prefill and not out.ft:
+            self.stats["decode_steps"] = self.stats.get("decode_steps", 0) + 1
+            self.stats["decode_enqueue_s"] = (self.stats.get("decode_enqueue_s", 0.0)
+                                              + getattr(self.runner, "last_enqueue_s", 0.0))
         self.stats["h2d_bytes"] += self.runner.last_h2d_bytes
         self.stats["d2h_bytes"] += self.runner.last_d2h_bytes
         self._pending_timing.append(StepRecord(feats, ev0, ev1, pred, "step"))
@@ -969,6 +974,8 @@ class CoServingEngine:
             torch.cuda.synchronize(self.device)
         if self.trainer is not None:
             self.trainer.release_graphs()
+        if self.runner.graphs is not None:
+            self.runner.graphs.release()
         if self.cuda:
             torch.cuda.synchronize(self.device)
         if self.peer_ws is not None:
@@ -1085,13 +1092,13 @@ class CoServingEngine:
                         # The metadata copy must be ordered before the forward:
                         # both go on the forward stream (as on rank 0).
                         with torch.cuda.stream(self.fwd_stream):
-                            b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
                             if has_ft and self._publish_evt is not None:
                                 self.fwd_stream.wait_event(self._publish_evt)
-                            self.model.forward(b, self.capture if has_ft else None)
+                            self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
+                                                         self.capture if has_ft else None)
                     else:
-                        b = self.runner.batch_from(meta, _Packer.thaw(arr, spans))
-                        self.model.forward(b, self.capture if has_ft else None)
+                        self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
+                                                     self.capture if has_ft else None)
                 elif kind == "bwd_start":
                     m = a[1]
                     if self.cuda:

@@ -8,6 +8,8 @@ and moved with ONE host-to-device copy; the device tensors are views into it.
 
 from __future__ import annotations
 
+import time
+
 import numpy as np
 import torch
 
@@ -89,9 +91,149 @@ class PinnedRing:
         self.events[k] = ev
 
 
+DECODE_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256)
+
+
+class DecodeGraphs:
+    """CUDA graphs of a decode-only step (forward + sampling), one per padded
+    batch size and LoRA on/off, replayed with one host->device copy of the
+    step's metadata into static buffers. A decode step otherwise costs a few
+    hundred kernel launches from Python, which is more host time than the GPU
+    needs for the step.
+
+    Padded rows carry no token: slot -1 (no KV write), context 0 (attention
+    skips them), LoRA slot -1; their logits and samples are ignored. The
+    attention splits each sequence's context itself (keys_per_split 0), so
+    a graph is valid for any context length up to ``max_model_len``."""
+
+    def __init__(self, model: DecoderModel, device, block_size: int, max_model_len: int, num_sms: int):
+        self.model = model
+        self.device = device
+        self.maxb = -(-max_model_len // block_size)
+        self.max_model_len = max_model_len
+        self.num_sms = num_sms
+        self.graphs: dict[tuple[int, bool], dict] = {}
+        self.pool = None
+        self.replays = 0
+        self._host: torch.Tensor | None = None
+        self._host_f: torch.Tensor | None = None
+        self._evt = None
+
+    @staticmethod
+    def bucket(n: int) -> int | None:
+        for b in DECODE_BUCKETS:
+            if b >= n:
+                return b
+        return None
+
+    def _layout(self, Bp: int, lora: bool) -> dict:
+        sizes = [("ids", Bp), ("pos", Bp), ("slot", Bp), ("btab", Bp * self.maxb), ("ctx", Bp),
+                 ("seeds", Bp)]
+        if lora:
+            sizes += [("lslot", Bp), ("tile", -(-Bp // 128))]
+        lay, off = {}, 0
+        for k, n in sizes:
+            lay[k] = (off, n)
+            off += n
+        return {"spans": lay, "total": off}
+
+    def _forward(self, st: dict, Bp: int, lora: bool):
+        m = self.model
+        i32 = lambda t: t.to(torch.int32)
+        splits = ops.decode_splits(Bp, m.hkv_l, self.max_model_len, self.num_sms)[0]
+        b = ForwardBatch(
+            input_ids=st["ids"], positions=st["pos"], slot_mapping=st["slot"], num_decode=Bp,
+            dec_block_tables=i32(st["btab"]).view(Bp, self.maxb), dec_ctx_lens=i32(st["ctx"]),
+            dec_splits=splits, dec_keys_per_split=0,
+            slot_ids=i32(st["lslot"]) if lora else None, tile_slots=i32(st["tile"]) if lora else None,
+            logits_idx=st["rows"])
+        logits = m.forward(b, None)
+        ops.sample(logits, st["temps"], st["seeds"], st["toks"])
+        return logits
+
+    def _capture(self, Bp: int, lora: bool) -> dict:
+        lay = self._layout(Bp, lora)
+        flat = torch.zeros(lay["total"], dtype=torch.int64, device=self.device)
+        st = {k: flat[o:o + n] for k, (o, n) in lay["spans"].items()}
+        st["rows"] = torch.arange(Bp, dtype=torch.int64, device=self.device)
+        st["temps"] = torch.zeros(Bp, dtype=torch.float32, device=self.device)
+        st["toks"] = torch.zeros(Bp, dtype=torch.int64, device=self.device)
+        st["slot"].fill_(-1)
+        if lora:
+            st["lslot"].fill_(-1)
+        stream = torch.cuda.current_stream(self.device)
+        n0 = ops.LAUNCHES[0]
+        self._forward(st, Bp, lora)            # eager warm-up: lazy set-up outside the capture
+        stream.synchronize()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        k0 = ops.LAUNCHES[0]
+        with torch.cuda.graph(g, pool=self.pool, stream=stream):
+            logits = self._forward(st, Bp, lora)
+        kernels = ops.LAUNCHES[0] - k0
+        ops.LAUNCHES[0] = n0                   # counted per replay from now on
+        # `logits` lives in the graph's pool: every replay rewrites it.
+        ent = {"graph": g, "flat": flat, "st": st, "lay": lay, "kernels": kernels, "logits": logits}
+        self.graphs[(Bp, lora)] = ent
+        return ent
+
+    def run(self, meta: dict, pk: "_Packer", temps=None, seeds=None) -> tuple[torch.Tensor, int]:
+        """Replay the graph for this decode step; returns (tokens [Bp] on the
+        device, H2D bytes)."""
+        nd = meta["nd"]
+        Bp = self.bucket(nd)
+        lora = bool(meta["use_lora"])
+        ent = self.graphs.get((Bp, lora)) or self._capture(Bp, lora)
+        lay = ent["lay"]
+        parts = dict(pk.parts)
+        total = lay["total"]
+        if self._host is None or self._host.numel() < total:
+            self._host = torch.zeros(max(total, 1 << 16), dtype=torch.int64, pin_memory=True)
+            self._host_f = torch.zeros(256, dtype=torch.float32, pin_memory=True)
+        if self._evt is not None:
+            self._evt.synchronize()            # the previous step's copy has read the pinned buffer
+        h = self._host.numpy()
+        sp = lay["spans"]
+
+        def put(name, arr, fill=0):
+            o, n = sp[name]
+            h[o:o + n] = fill
+            h[o:o + len(arr)] = arr
+        put("ids", parts["ids"])
+        put("pos", parts["pos"])
+        put("slot", parts["slot_mapping"], fill=-1)
+        o, n = sp["btab"]
+        h[o:o + n] = 0
+        bt = parts["dec_btab"].reshape(nd, meta["maxb"])
+        h[o:o + n].reshape(Bp, self.maxb)[:nd, :meta["maxb"]] = bt
+        put("ctx", parts["dec_ctx"])
+        put("seeds", seeds if seeds is not None else np.zeros(nd, np.int64))
+        if lora:
+            put("lslot", parts["lslot"], fill=-1)
+            put("tile", parts["tile_slots"])
+        hf = self._host_f.numpy()
+        hf[:Bp] = 0.0
+        if temps is not None:
+            hf[:nd] = temps
+        ent["flat"].copy_(self._host[:total], non_blocking=True)
+        ent["st"]["temps"].copy_(self._host_f[:Bp], non_blocking=True)
+        self._evt = torch.cuda.Event()
+        self._evt.record()
+        ent["graph"].replay()
+        ops.LAUNCHES[0] += ent["kernels"]
+        self.replays += 1
+        self.last_logits = ent["logits"][:nd]
+        return ent["st"]["toks"], total * 8 + Bp * 4
+
+    def release(self) -> None:
+        self.graphs.clear()
+        self.pool = None
+
+
 class ModelRunner:
     def __init__(self, model: DecoderModel, block_size: int, device, num_sms: int = 148,
-                 ft_slot: int = -1):
+                 ft_slot: int = -1, max_model_len: int = 4096, decode_graphs: bool = True):
         self.model = model
         self.block_size = block_size
         self.device = torch.device(device)
@@ -100,6 +242,20 @@ class ModelRunner:
         self._pinned = PinnedRing() if self.device.type == "cuda" else None
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+        self.graphs = (DecodeGraphs(model, self.device, block_size, max_model_len, num_sms)
+                       if (decode_graphs and self.device.type == "cuda") else None)
+
+    def graph_eligible(self, meta: dict) -> bool:
+        return (self.graphs is not None and meta["npf"] == 0 and meta["nd"] > 0
+                and DecodeGraphs.bucket(meta["nd"]) is not None)
+
+    def forward_follower(self, meta: dict, pk: "_Packer", cap) -> None:
+        """A follower rank's replay of a step: the same graph or kernels as rank 0."""
+        if self.graph_eligible(meta):
+            self.graphs.run(meta, pk)
+            return
+        b = self.batch_from(meta, pk)
+        self.model.forward(b, cap)
 
     def build_host(self, out: SchedulerOutput, ft_dst: int = 0) -> tuple[dict, _Packer, list]:
         bs = self.block_size
@@ -206,11 +362,25 @@ class ModelRunner:
         enqueued, so the other ranks can replay the same step."""
         if out.is_empty():
             return {}, None
+        t0 = time.perf_counter()
         meta, pk, reqs = self.build_host(out, ft_dst)
         if on_host_plan is not None:
             on_host_plan(meta, pk)
+        if self.graph_eligible(meta) and len(reqs) == meta["nd"]:
+            temps = np.array([r.params.temperature for r in reqs], dtype=np.float32)
+            seeds = np.array([(r.params.seed if r.params.seed is not None else r.seq_no) * 1000003
+                              + len(r.output_ids) for r in reqs], dtype=np.int64)
+            toks, nbytes = self.graphs.run(meta, pk, temps, seeds)
+            self.last_h2d_bytes = nbytes
+            self.last_enqueue_s = time.perf_counter() - t0
+            if before_sample is not None:
+                before_sample()
+            host = toks[:len(reqs)].cpu()
+            self.last_d2h_bytes = len(reqs) * 8
+            return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}, self.graphs.last_logits
         b = self.batch_from(meta, pk)
         logits = self.model.forward(b, cap if out.ft else None)
+        self.last_enqueue_s = time.perf_counter() - t0   # host time to enqueue the forward
         if before_sample is not None:
             before_sample()
         return self.sample(logits, reqs), logits

@@ -160,8 +160,9 @@ class DecoderModel:
     def _decode_ws(self, n: int, device):
         need_o = n * 128
         if self._dec_ws is None or self._dec_ws[0].numel() < need_o:
-            self._dec_ws = (torch.empty(max(need_o, 1 << 20), dtype=torch.float32, device=device),
-                            torch.empty(max(n * 2, 1 << 14), dtype=torch.float32, device=device))
+            # Sized once for every decode shape (CUDA graphs keep the address).
+            self._dec_ws = (torch.empty(max(need_o, 1 << 22), dtype=torch.float32, device=device),
+                            torch.empty(max(n * 2, 1 << 16), dtype=torch.float32, device=device))
         return self._dec_ws
 
     def attention(self, layer: int, qkv: torch.Tensor, ctx: torch.Tensor, b: ForwardBatch):

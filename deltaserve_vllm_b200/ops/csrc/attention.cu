@@ -292,8 +292,13 @@ __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   const int G = a.group;
   const int ctx = a.ctx_lens[b];
-  const int k_begin = split * a.keys_per_split;
-  const int k_end = min(ctx, k_begin + a.keys_per_split);
+  // keys_per_split 0: each sequence splits its own context evenly (64-key
+  // granularity), so a launch whose arguments are fixed (a CUDA graph) works
+  // for any context length.
+  const int kps = a.keys_per_split > 0 ? a.keys_per_split
+                                       : ((ctx + a.splits - 1) / a.splits + DC_KEYS - 1) / DC_KEYS * DC_KEYS;
+  const int k_begin = split * kps;
+  const int k_end = min(ctx, k_begin + kps);
   const int n_chunks = k_end > k_begin ? (k_end - k_begin + DC_KEYS - 1) / DC_KEYS : 0;
   const int* btab = a.block_tables + (size_t)b * a.max_blocks;
 

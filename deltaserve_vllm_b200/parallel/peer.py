@@ -72,7 +72,7 @@ class PeerWorkspace:
                                   dtype=torch.int64)
         self.tile_cnt = self.base + self.offsets[4]
         self.calls = 0
-        self.fused_max_rows = int(os.environ.get("DSV_FUSED_AR_MAX_ROWS", "1024"))
+        self.fused_max_rows = int(os.environ.get("DSV_FUSED_AR_MAX_ROWS", "2048"))
         if comm is not None and self.world > 1:
             comm.barrier()        # every rank mapped every block before first use
 
@@ -80,10 +80,10 @@ class PeerWorkspace:
         return rows <= self.max_rows and n_cols == self.n_cols
 
     def prefer(self, rows: int, n_cols: int) -> bool:
-        """Whether the fused kernel should take this call: it wins over GEMM +
-        NCCL up to ``fused_max_rows`` rows (measured at TP=2: 1.4x at 64 rows,
-        even at 1024, behind from 2048), NCCL's bandwidth-optimised rings win
-        above."""
+        """Whether the fused kernel should take this call: measured at TP=2 it
+        beats GEMM + NCCL from 256 to 2048 rows (1.2-1.5x) and at 4096 rows
+        for o_proj, not for down_proj at 4096 rows; calls above
+        ``fused_max_rows`` go to NCCL's bandwidth-optimised rings."""
         return self.fits(rows, n_cols) and rows <= self.fused_max_rows
 
     def close(self) -> None:

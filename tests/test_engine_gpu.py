@@ -94,3 +94,43 @@ def test_gpu_coserving_engine_runs_cycles():
     assert all(l == l and l > 0 for l in eng.trainer.losses)
     assert len([r for r in eng.finished if r.request_id.startswith("r")]) == 12
     assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+
+
+@pytest.mark.parametrize("name", ["qwen3-test", "llama3-test"])
+def test_decode_graphs_match_eager(name):
+    """Decode steps replayed from CUDA graphs give the eager forward's logits."""
+    arch = PRESETS[name]
+    _, toks = run(arch, "cpu", torch.float32)
+
+    def go(graphs):
+        model, kv = make(arch, "cuda", torch.bfloat16)
+        sched = Scheduler(kv.allocator, 64, max_num_batched_tokens=160, max_model_len=1024)
+        runner = ModelRunner(model, 64, "cuda", max_model_len=1024, decode_graphs=graphs)
+        g = torch.Generator().manual_seed(0)
+        for i, n in enumerate([200, 37, 1, 130]):
+            r = Request(str(i), torch.randint(0, arch.vocab, (n,), generator=g).tolist(),
+                        SamplingParams(max_tokens=4))
+            r.lora_slot = i % 3 - 1
+            sched.add(r)
+        outs = []
+        for step in range(20):
+            out = sched.schedule()
+            if out.is_empty():
+                break
+            t, logits = runner.execute(out)
+            outs.append((not out.prefill, None if logits is None else logits.float().cpu()))
+            t = {s.req.seq_no: toks[step][s.req.request_id] for s in out.seqs
+                 if s.req.request_id in toks[step]}
+            sched.update(out, t)
+        assert ops.check_device_error() == 0
+        return outs, runner
+    eager, _ = go(False)
+    graph, runner = go(True)
+    assert runner.graphs.replays > 0
+    n_dec = 0
+    for (dec, a), (_, b) in zip(eager, graph):
+        if a is None or b is None or a.numel() == 0:
+            continue
+        n_dec += int(dec)
+        torch.testing.assert_close(b, a, rtol=2e-2, atol=5e-2)
+    assert n_dec > 0
