@@ -76,6 +76,10 @@ struct GemmArgs {
   // Swapped operands (kEpiBF16T, decode): the LoRA slots of every tile are
   // the OR of tile_slots[0, slot_or) (the token tiles), not tile_slots[mt].
   int slot_or;
+  // Split-K with tickets (kEpiBF16T): the last split of a tile to arrive sums
+  // the fp32 partials and stores the result (no second kernel). Zeroed
+  // counters, one per tile, reset by that last split.
+  unsigned* split_cnt;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -547,9 +551,10 @@ __global__ void __launch_bounds__(256, 1)
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
-      if constexpr (EPI != kEpiPeerAR) {
-        if (!acc_ok) break;
-      }
+      // Paths with named barriers among the epilogue warps keep iterating
+      // after a failed wait (TMEM reads skipped) so the warps always meet.
+      const bool lockstep = EPI == kEpiPeerAR || (EPI == kEpiBF16T && args.split_cnt != nullptr);
+      if (!lockstep && !acc_ok) break;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
@@ -561,9 +566,10 @@ __global__ void __launch_bounds__(256, 1)
         peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles,
                            staging + q * 128);
       } else if (args.k_splits > 1) {
-        // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
+        // Split-K: raw fp32 partial sums; the reduce kernel applies the
+        // epilogue, or (tickets) the last split of the tile does.
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = 0; c < BN && acc_ok; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c, r);
           tmem_ld_wait();
@@ -574,6 +580,52 @@ __global__ void __launch_bounds__(256, 1)
           if (row_ok && col < args.N)
             store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + col, v,
                           min(32, args.N - col), false);
+        }
+        if constexpr (EPI == kEpiBF16T) {
+          if (args.split_cnt != nullptr) {
+            __shared__ int s_last_split;
+            const int Lt = tl.nt * num_m_tiles + tl.mt;
+            named_bar_sync(1, 128);
+            if (q == 0 && lane == 0) {
+              __threadfence();
+              const unsigned old = atomicAdd(args.split_cnt + Lt, 1u);
+              s_last_split = (old == (unsigned)(args.k_splits - 1)) ? 1 : 0;
+              if (s_last_split) args.split_cnt[Lt] = 0u;
+              __threadfence();
+            }
+            named_bar_sync(1, 128);
+            if (s_last_split && row_ok) {
+              __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(args.C);
+#pragma unroll 1
+              for (int c = 0; c < BN; c += 32) {
+                const int col = n0 + c;
+                if (col >= args.N) break;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+                for (int sp = 0; sp < args.k_splits; ++sp) {
+                  const float* src = args.partial + ((size_t)sp * args.M + row) * args.N + col;
+                  if (col + 32 <= args.N && (args.N & 3) == 0) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                      const float4 f = __ldcg(reinterpret_cast<const float4*>(src) + i);
+                      v[4 * i] += f.x;
+                      v[4 * i + 1] += f.y;
+                      v[4 * i + 2] += f.z;
+                      v[4 * i + 3] += f.w;
+                    }
+                  } else {
+                    for (int i = 0; i < 32 && col + i < args.N; ++i) v[i] += __ldcg(src + i);
+                  }
+                }
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) {
+                  const int tok = col + i;
+                  if (tok < args.N) cb[(size_t)tok * args.ldc + row] = f2bf(v[i]);
+                }
+              }
+            }
+          }
         }
       } else if constexpr (EPI == kEpiBF16T) {
         // Swapped operands: accumulator rows are output features (this
@@ -808,6 +860,24 @@ static int num_sms() {
   return n;
 }
 
+// Zeroed split-K ticket counters, one buffer per (device, stream) so GEMMs on
+// concurrent streams never share tickets; every ticket is reset by the split
+// that consumes it, so a buffer stays zero between launches.
+static unsigned* split_counters(cudaStream_t stream, int device, int tiles) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, at::Tensor> bufs;
+  constexpr int kCounters = 1 << 14;
+  TORCH_CHECK(tiles <= kCounters, "dsv gemm: too many split-K tiles for the ticket buffer");
+  const uint64_t key = (reinterpret_cast<uint64_t>(stream) << 8) ^ (uint64_t)device;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = bufs.find(key);
+  if (it == bufs.end()) {
+    at::Tensor t = at::zeros({kCounters}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+    it = bufs.emplace(key, t).first;
+  }
+  return reinterpret_cast<unsigned*>(it->second.data_ptr<int>());
+}
+
 template <int BN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
                    const GemmArgs& args, cudaStream_t stream) {
@@ -913,15 +983,9 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
       args.slot_or = 1;
     }
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    if (splits > 1) args.split_cnt = split_counters(st, a.device().index(), tiles);
     if (bnt == 64) launch<64, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
     else launch<128, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
-    if (splits > 1) {
-      const int64_t work = (int64_t)M * N;
-      const int blocks = (int)std::min<int64_t>(4096, (work + 255) / 256);
-      splitk_reduce_kernel<<<blocks, 256, 0, st>>>(args.partial, splits, N, M, (int)kEpiBF16T, out.data_ptr(),
-                                                   args.ldc, nullptr, 0, 0, 0, 0);
-      C10_CUDA_KERNEL_LAUNCH_CHECK();
-    }
     return;
   }
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);

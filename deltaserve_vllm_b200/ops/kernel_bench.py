@@ -145,6 +145,38 @@ def _adamw(n):
     return (lambda: ops.adamw(p, g, m, v, seg_len=n, lr=1e-4, step=1), n * 4 * 7, 0)
 
 
+def _lora_backward(n_seq: int, L: int, graphs: bool):
+    """One LoRA backward cycle (head + 2 layers of Llama-3-8B geometry, r=16,
+    all projections) over captured activations of n_seq x L tokens, eager or
+    as the per-layer CUDA graphs. FLOPs: the frozen dX GEMMs of both layers and
+    the LM head (2 x 4 per weight element per token)."""
+    from ..engine.trainer import LoraTrainer
+    from ..models.configs import resolve_arch
+    from ..models.decoder import CaptureBuffers
+    from ..models.lora import LoraServeBuffers
+    from ..models.weights import TPInfo, init_weights
+    arch = resolve_arch("llama3-8b-2l")
+    w = init_weights(arch, TPInfo(), seed=0, device=torch.device(DEV), dtype=torch.bfloat16, keep_full_head=True)
+    served = LoraServeBuffers(arch, w.tp, 2, 16, torch.device(DEV), torch.bfloat16)
+    tr = LoraTrainer(w, served, 1, 16, 32.0, lr=1e-4)
+    tr.init_random(1)
+    tr.use_graphs = graphs
+    n = n_seq * L
+    cap = CaptureBuffers.allocate(w, n + 8, torch.device(DEV))
+    g = torch.Generator(device=DEV).manual_seed(3)
+    for t in (cap.layer_in, cap.qkv, cap.ctx, cap.resid_mid, cap.gate_up, cap.act, cap.final_in):
+        t.copy_((torch.randn(t.shape, generator=g, device=DEV) * 0.5).to(t.dtype))
+    cap.ids.copy_(torch.randint(0, arch.vocab, cap.ids.shape, device=DEV))
+    cap.positions.copy_(torch.arange(n + 8, device=DEV) % L)
+    starts, lens = [i * L for i in range(n_seq)], [L] * n_seq
+    # dX of every frozen projection (2 FLOPs per weight element per token) in
+    # both layers, plus the LM head forward and dX.
+    per_tok = 2 * (arch.hidden * (arch.q_size + 2 * arch.kv_size) + arch.q_size * arch.hidden
+                   + 3 * arch.hidden * arch.intermediate) * arch.num_layers + 4 * arch.hidden * arch.vocab
+    flops = n * per_tok
+    return (lambda: tr.run_cycle(cap, n, starts, lens), 0, flops)
+
+
 CASES = {
     # Llama-3-8B projections, 4096-token prefill step (TP=1)
     "gemm_prefill_qkv": lambda: _gemm(4096, 6144, 4096),
@@ -167,6 +199,8 @@ CASES = {
     "rope_kvwrite_4096": lambda: _rope(4096),
     "ce_fwd_bwd_512x128256": lambda: _ce(512, 128256),
     "adamw_64M": lambda: _adamw(64 << 20),
+    "lora_backward_2l_8x512_eager": lambda: _lora_backward(8, 512, False),
+    "lora_backward_2l_8x512_graphs": lambda: _lora_backward(8, 512, True),
 }
 
 

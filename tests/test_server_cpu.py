@@ -156,3 +156,16 @@ def test_launcher_dry_run(capsys):
         assert out["server"]["port"] == 9000
         assert out["finetune"]["data_path"] == os.path.join(os.path.realpath(tmp), "data.txt")
         assert out["finetune"]["ttft_slo"] == 0.5
+
+
+def test_shipped_config_templates_load():
+    """Every YAML template under configs/ resolves through the launcher."""
+    import glob
+    from deltaserve_vllm_b200 import launch
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    files = sorted(glob.glob(os.path.join(root, "configs", "*.yaml")))
+    assert len(files) >= 4
+    for f in files:
+        ecfg, ftcfg, rcfg, extras, host, port = launch.resolve(launch.parse(["--config", f]))
+        assert ecfg.model and port > 0
+        assert ftcfg.enable_finetuning
