@@ -842,6 +842,21 @@ class CoServingEngine:
         self._drain_timing(block=True)
 
     # ------------------------------------------------------------------ profiling
+    def warm_decode_graphs(self) -> None:
+        """Capture the decode-step CUDA graphs of every batch bucket now (on
+        every rank in lockstep: the graphs hold TP collectives)."""
+        if self.runner.graphs is None or getattr(self, "_graphs_warm", False):
+            return
+        if self.is_driver and self.tp_size > 1:
+            self._record(("decode_graphs",))
+            self._flush_actions()
+        t0 = time.perf_counter()
+        with torch.cuda.stream(self.fwd_stream):
+            n = self.runner.graphs.capture_all(self.ecfg.max_num_seqs, self.lora is not None)
+        torch.cuda.synchronize(self.device)
+        self._graphs_warm = True
+        dprint(f"[graphs] {n} decode-step graphs captured in {time.perf_counter() - t0:.1f}s")
+
     def profile_execution_model(self, shapes=None, repeats: int | None = None,
                                 max_shapes: int | None = None) -> None:
         """Launch profiling: drive synthetic shapes through real steps, fit the
@@ -849,6 +864,7 @@ class CoServingEngine:
         A failure here switches the engine to inference-only (finetuning disabled)."""
         from .profiling import ProfilingShapeGenerator
         repeats = self.ftcfg.profile_num_repeats if repeats is None else repeats
+        self.warm_decode_graphs()     # profiled decode steps then run as they will in serving
         try:
             if os.environ.get("DSERVE_TEST_FAIL_PROFILING") == "1":
                 raise RuntimeError("DSERVE_TEST_FAIL_PROFILING=1")
@@ -1084,6 +1100,9 @@ class CoServingEngine:
                     continue
                 if kind == "job":
                     self._apply_job(*a[1:])
+                    continue
+                if kind == "decode_graphs":
+                    self.warm_decode_graphs()
                     continue
                 if kind == "fwd":
                     _, arr, spans, meta, has_ft = a

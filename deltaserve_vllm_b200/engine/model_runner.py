@@ -118,6 +118,7 @@ class DecodeGraphs:
         self._host: torch.Tensor | None = None
         self._host_f: torch.Tensor | None = None
         self._evt = None
+        self._side = None
 
     @staticmethod
     def bucket(n: int) -> int | None:
@@ -169,14 +170,37 @@ class DecodeGraphs:
             self.pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
         k0 = ops.LAUNCHES[0]
-        with torch.cuda.graph(g, pool=self.pool, stream=stream):
+        # Capture needs a non-default stream; replays may run on any stream.
+        cap_stream = stream
+        if stream == torch.cuda.default_stream(self.device):
+            if self._side is None:
+                self._side = torch.cuda.Stream(self.device)
+            cap_stream = self._side
+            cap_stream.wait_stream(stream)
+        with torch.cuda.graph(g, pool=self.pool, stream=cap_stream):
             logits = self._forward(st, Bp, lora)
+        if cap_stream is not stream:
+            stream.wait_stream(cap_stream)
         kernels = ops.LAUNCHES[0] - k0
         ops.LAUNCHES[0] = n0                   # counted per replay from now on
         # `logits` lives in the graph's pool: every replay rewrites it.
         ent = {"graph": g, "flat": flat, "st": st, "lay": lay, "kernels": kernels, "logits": logits}
         self.graphs[(Bp, lora)] = ent
         return ent
+
+    def capture_all(self, max_seqs: int, lora: bool) -> int:
+        """Capture every bucket up to ``max_seqs`` (with and without LoRA)
+        before serving, so no request waits on a capture. Returns how many."""
+        top = self.bucket(min(max_seqs, DECODE_BUCKETS[-1])) or DECODE_BUCKETS[-1]
+        n = 0
+        for Bp in DECODE_BUCKETS:
+            if Bp > top:
+                break
+            for lo in ((False, True) if lora else (False,)):
+                if (Bp, lo) not in self.graphs:
+                    self._capture(Bp, lo)
+                    n += 1
+        return n
 
     def run(self, meta: dict, pk: "_Packer", temps=None, seeds=None) -> tuple[torch.Tensor, int]:
         """Replay the graph for this decode step; returns (tokens [Bp] on the

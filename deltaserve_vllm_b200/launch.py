@@ -110,6 +110,8 @@ def main(argv=None) -> int:
             return 0
         if eng.ft_enabled and ftcfg.profile_on_launch and not args.no_profile:
             eng.profile_execution_model()
+        elif eng.cuda:
+            eng.warm_decode_graphs()
         if args.start_finetuning:
             eng.start_finetuning()
         import uvicorn

@@ -158,7 +158,9 @@ def _lora_backward(n_seq: int, L: int, graphs: bool):
     arch = resolve_arch("llama3-8b-2l")
     w = init_weights(arch, TPInfo(), seed=0, device=torch.device(DEV), dtype=torch.bfloat16, keep_full_head=True)
     served = LoraServeBuffers(arch, w.tp, 2, 16, torch.device(DEV), torch.bfloat16)
-    tr = LoraTrainer(w, served, 1, 16, 32.0, lr=1e-4)
+    from .reference import rope_cos_sin_table
+    cs = rope_cos_sin_table(8192, arch.head_dim, arch.rope_theta, arch.rope_scaling, device=DEV)
+    tr = LoraTrainer(w, served, 1, 16, 32.0, lr=1e-4, cos_sin_table=cs)
     tr.init_random(1)
     tr.use_graphs = graphs
     n = n_seq * L
