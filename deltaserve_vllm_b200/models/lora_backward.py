@@ -281,6 +281,7 @@ class LoraBackward:
         self.hd = self.arch.head_dim
         self.scale = 1.0 / math.sqrt(self.hd)
         self._rows: dict[tuple[str, int], torch.Tensor] = {}
+        self._ones_slots: dict = {}
         if weights.embed.is_cuda:
             # fp32 attention-backward matmuls on TF32 tensor cores (exact for
             # the bf16-valued operands; fp32 accumulation).
@@ -334,17 +335,43 @@ class LoraBackward:
         tensor as a writable view [R, N/128, 64]."""
         return t.view(t.shape[0], gg.N // 128, 2, 64)[:, :, p]
 
-    def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
-                       dX: torch.Tensor) -> None:
-        """LoRA part of one group: accumulates into ``dX`` (fp32) and writes the
-        factor gradients into the trainer's grad buffer."""
+    def group_dz(self, layer: int, g: str, dY: torch.Tensor) -> torch.Tensor:
+        """dZ = dY . B_full (fp32 [n, P*R]): the adapter's share of the
+        input gradient before the A factor."""
+        return self._mm(dY, self._bfull(layer, g), b_mn=True)
+
+    def dx_gemm(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor) -> torch.Tensor:
+        """dX = dY . W + dZ . A in ONE GEMM: the rank-R adapter term rides as
+        one extra 64-deep K block (dZ and A zero-padded to 64) instead of a
+        second pass over the fp32 dX."""
+        n = dY.shape[0]
+        PR = dZ.shape[1]
+        seg = -(-PR // 64) * 64
+        A = self.m.p(layer, g, "A")
+        if not dY.is_cuda:
+            out = self._mm(dY, W, b_mn=True)
+            out += dZ @ A
+            return out
+        zp = torch.zeros(n, seg, dtype=self.cdt, device=dY.device)
+        zp[:, :PR] = dZ
+        ap = torch.zeros(seg, A.shape[1], dtype=self.cdt, device=dY.device)
+        ap[:PR] = A
+        key = (-(-n // 128), dY.device)
+        ts = self._ones_slots.get(key)
+        if ts is None:
+            ts = torch.ones(key[0], dtype=torch.int32, device=dY.device)
+            self._ones_slots[key] = ts
+        out = torch.empty(n, W.shape[1], dtype=torch.float32, device=dY.device)
+        ops.gemm(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), out, b_mn=True, epi=EPI_F32,
+                 z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas)
+        return out
+
+    def group_grads(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor, dZ: torch.Tensor) -> None:
+        """Factor gradients of one group into the trainer's grad buffer."""
         gg = self.geom[g]
         R = self.m.R
         A = _bf(self.m.p(layer, g, "A"), self.cdt)
-        Bfull = self._bfull(layer, g)
         Z = self._mm(X, A, b_mn=False)                       # [n, PR]
-        dZ = self._mm(dY, Bfull, b_mn=True)                  # [n, PR]
-        self._mm(dZ, A, b_mn=True, epi=EPI_F32_ACCUM, out=dX)
         gA = self.m.g(layer, g, "A")
         self._mm(dZ.t(), X, b_mn=True, out=gA)               # [PR, K]
         gBfT = self._mm(Z.t(), dY, b_mn=True) * self.s       # [PR, N]
@@ -356,6 +383,16 @@ class LoraBackward:
             else:
                 b0, b1 = self._bounds(gg, p)
                 gBt[:, b0:b1].copy_(src[:, b0:b1])
+
+    def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
+                       dX: torch.Tensor) -> None:
+        """LoRA part of one group on its own: accumulates dZ . A into ``dX``
+        (fp32) and writes the factor gradients (the layer backward uses the
+        fused :meth:`dx_gemm` instead)."""
+        dZ = self.group_dz(layer, g, dY)
+        A = _bf(self.m.p(layer, g, "A"), self.cdt)
+        self._mm(dZ, A, b_mn=True, epi=EPI_F32_ACCUM, out=dX)
+        self.group_grads(layer, g, X, dY, dZ)
 
     # ------------------------------------------------------------ head
     def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor,
@@ -433,24 +470,27 @@ class LoraBackward:
         cdt = self.cdt
         # ---- MLP -------------------------------------------------------
         dh_c = _bf(dh, cdt)
-        d_act = self._mm(dh_c, lw.down, b_mn=True)                  # [n, I_l] fp32
+        dz = self.group_dz(layer, "down", dh_c)
+        d_act = self.dx_gemm(layer, "down", dh_c, lw.down, dz)     # [n, I_l] fp32
         if act is None:
             g, u = deinterleave64(gate_up.float())
             act = _bf(F.silu(g) * u, x.dtype)
-        self.group_backward(layer, "down", act, dh_c, d_act)
+        self.group_grads(layer, "down", act, dh_c, dz)
         d_gu = torch.empty(n, gate_up.shape[1], dtype=cdt, device=dev)
         ops.swiglu_bwd(gate_up, d_act, d_gu)
         x2 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
-        d_x2 = self._mm(d_gu, lw.gate_up, b_mn=True)                # [n, D]
-        self.group_backward(layer, "gate_up", x2, d_gu, d_x2)
+        dz = self.group_dz(layer, "gate_up", d_gu)
+        d_x2 = self.dx_gemm(layer, "gate_up", d_gu, lw.gate_up, dz)  # [n, D]
+        self.group_grads(layer, "gate_up", x2, d_gu, dz)
         if self.comm is not None:
             self.comm.all_reduce(d_x2)
         d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
         d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
         # ---- attention ---------------------------------------------------
-        d_ctx = self._mm(d_mid_c, lw.o, b_mn=True)                  # [n, q_l]
-        self.group_backward(layer, "o", ctx, d_mid_c, d_ctx)
+        dz = self.group_dz(layer, "o", d_mid_c)
+        d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz)        # [n, q_l]
+        self.group_grads(layer, "o", ctx, d_mid_c, dz)
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
         dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
                                    self.scale, ci.attn_groups)
@@ -471,8 +511,9 @@ class LoraBackward:
         d_qkv[:, ql + kl:] = dv.reshape(n, kl)
         x1 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(x, lw.in_ln, x1, eps)
-        d_x1 = self._mm(d_qkv, lw.qkv, b_mn=True)                   # [n, D]
-        self.group_backward(layer, "qkv", x1, d_qkv, d_x1)
+        dz = self.group_dz(layer, "qkv", d_qkv)
+        d_x1 = self.dx_gemm(layer, "qkv", d_qkv, lw.qkv, dz)       # [n, D]
+        self.group_grads(layer, "qkv", x1, d_qkv, dz)
         if self.comm is not None:
             self.comm.all_reduce(d_x1)
         return ops.rms_norm_bwd(x, d_x1, lw.in_ln, eps, add=d_mid)

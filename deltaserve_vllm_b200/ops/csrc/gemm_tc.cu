@@ -76,10 +76,6 @@ struct GemmArgs {
   // Swapped operands (kEpiBF16T, decode): the LoRA slots of every tile are
   // the OR of tile_slots[0, slot_or) (the token tiles), not tile_slots[mt].
   int slot_or;
-  // Split-K with tickets (kEpiBF16T): the last split of a tile to arrive sums
-  // the fp32 partials and stores the result (no second kernel). Zeroed
-  // counters, one per tile, reset by that last split.
-  unsigned* split_cnt;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -481,7 +477,14 @@ __global__ void __launch_bounds__(256, 1)
           const int slot = __ffs(m) - 1;
           const int k0 = slot * args.lora_seg + sub * BK;
           tma_load_2d(sA, &tmZ, &full_bar[stage], k0, m0);
-          tma_load_2d(sB, &tmB2, &full_bar[stage], k0, n0);
+          if constexpr (B_MN) {
+            // MN-major launch: B2 is [S*SEG, N] like B (the backward's dX += dZ . A).
+#pragma unroll
+            for (int jj = 0; jj < BN / 64; ++jj)
+              tma_load_2d(sB + jj * (64 * BK * 2), &tmB2, &full_bar[stage], n0 + jj * 64, k0);
+          } else {
+            tma_load_2d(sB, &tmB2, &full_bar[stage], k0, n0);
+          }
         }
         fills[stage]++;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -521,12 +524,12 @@ __global__ void __launch_bounds__(256, 1)
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t da = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
           uint64_t db;
-          if (B_MN && !lora_blk) {
+          (void)lora_blk;
+          if (B_MN) {
             db = smem_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
           } else {
             db = smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B);
           }
-          // The LoRA blocks of an MN-major launch are never issued (host refuses).
           tc_mma_f16(d_tmem, da, db, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&empty_bar[stage]);
@@ -551,10 +554,9 @@ __global__ void __launch_bounds__(256, 1)
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
-      // Paths with named barriers among the epilogue warps keep iterating
-      // after a failed wait (TMEM reads skipped) so the warps always meet.
-      const bool lockstep = EPI == kEpiPeerAR || (EPI == kEpiBF16T && args.split_cnt != nullptr);
-      if (!lockstep && !acc_ok) break;
+      // The fused all-reduce's epilogue warps meet at named barriers: they keep
+      // iterating after a failed wait (TMEM reads skipped) so they always meet.
+      if (EPI != kEpiPeerAR && !acc_ok) break;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
@@ -566,8 +568,7 @@ __global__ void __launch_bounds__(256, 1)
         peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles,
                            staging + q * 128);
       } else if (args.k_splits > 1) {
-        // Split-K: raw fp32 partial sums; the reduce kernel applies the
-        // epilogue, or (tickets) the last split of the tile does.
+        // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
 #pragma unroll 1
         for (int c = 0; c < BN && acc_ok; c += 32) {
           uint32_t r[32];
@@ -580,52 +581,6 @@ __global__ void __launch_bounds__(256, 1)
           if (row_ok && col < args.N)
             store_row_f32(args.partial + ((size_t)tl.ks * args.M + row) * args.N + col, v,
                           min(32, args.N - col), false);
-        }
-        if constexpr (EPI == kEpiBF16T) {
-          if (args.split_cnt != nullptr) {
-            __shared__ int s_last_split;
-            const int Lt = tl.nt * num_m_tiles + tl.mt;
-            named_bar_sync(1, 128);
-            if (q == 0 && lane == 0) {
-              __threadfence();
-              const unsigned old = atomicAdd(args.split_cnt + Lt, 1u);
-              s_last_split = (old == (unsigned)(args.k_splits - 1)) ? 1 : 0;
-              if (s_last_split) args.split_cnt[Lt] = 0u;
-              __threadfence();
-            }
-            named_bar_sync(1, 128);
-            if (s_last_split && row_ok) {
-              __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(args.C);
-#pragma unroll 1
-              for (int c = 0; c < BN; c += 32) {
-                const int col = n0 + c;
-                if (col >= args.N) break;
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = 0.f;
-                for (int sp = 0; sp < args.k_splits; ++sp) {
-                  const float* src = args.partial + ((size_t)sp * args.M + row) * args.N + col;
-                  if (col + 32 <= args.N && (args.N & 3) == 0) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                      const float4 f = __ldcg(reinterpret_cast<const float4*>(src) + i);
-                      v[4 * i] += f.x;
-                      v[4 * i + 1] += f.y;
-                      v[4 * i + 2] += f.z;
-                      v[4 * i + 3] += f.w;
-                    }
-                  } else {
-                    for (int i = 0; i < 32 && col + i < args.N; ++i) v[i] += __ldcg(src + i);
-                  }
-                }
-#pragma unroll 8
-                for (int i = 0; i < 32; ++i) {
-                  const int tok = col + i;
-                  if (tok < args.N) cb[(size_t)tok * args.ldc + row] = f2bf(v[i]);
-                }
-              }
-            }
-          }
         }
       } else if constexpr (EPI == kEpiBF16T) {
         // Swapped operands: accumulator rows are output features (this
@@ -860,24 +815,6 @@ static int num_sms() {
   return n;
 }
 
-// Zeroed split-K ticket counters, one buffer per (device, stream) so GEMMs on
-// concurrent streams never share tickets; every ticket is reset by the split
-// that consumes it, so a buffer stays zero between launches.
-static unsigned* split_counters(cudaStream_t stream, int device, int tiles) {
-  static std::mutex mu;
-  static std::unordered_map<uint64_t, at::Tensor> bufs;
-  constexpr int kCounters = 1 << 14;
-  TORCH_CHECK(tiles <= kCounters, "dsv gemm: too many split-K tiles for the ticket buffer");
-  const uint64_t key = (reinterpret_cast<uint64_t>(stream) << 8) ^ (uint64_t)device;
-  std::lock_guard<std::mutex> g(mu);
-  auto it = bufs.find(key);
-  if (it == bufs.end()) {
-    at::Tensor t = at::zeros({kCounters}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
-    it = bufs.emplace(key, t).first;
-  }
-  return reinterpret_cast<unsigned*>(it->second.data_ptr<int>());
-}
-
 template <int BN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
                    const GemmArgs& args, cudaStream_t stream) {
@@ -983,9 +920,17 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
       args.slot_or = 1;
     }
     cudaStream_t st = at::cuda::getCurrentCUDAStream();
-    if (splits > 1) args.split_cnt = split_counters(st, a.device().index(), tiles);
     if (bnt == 64) launch<64, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
     else launch<128, false, kEpiBF16T>(ta, tb, tz, tb2, args, st);
+    if (splits > 1) {
+      // A separate, fully parallel reduction measured faster than letting the
+      // last split of each tile reduce it (a serial tail of 128 threads).
+      const int64_t work = (int64_t)M * N;
+      const int blocks = (int)std::min<int64_t>(4096, (work + 255) / 256);
+      splitk_reduce_kernel<<<blocks, 256, 0, st>>>(args.partial, splits, N, M, (int)kEpiBF16T, out.data_ptr(),
+                                                   args.ldc, nullptr, 0, 0, 0, 0);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
     return;
   }
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
@@ -1025,15 +970,19 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
                         : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
   CUtensorMap tz = ta, tb2 = tb;
   if (lora_seg > 0) {
-    TORCH_CHECK(!b_mn, "dsv_gemm: the fused LoRA expand is for K-major B only");
     TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "dsv_gemm: LoRA operands missing");
     TORCH_CHECK(lora_seg % 64 == 0, "dsv_gemm: lora_seg must be a multiple of 64");
     auto& zt = *z;
     auto& bt = *b2;
-    TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm: LoRA shapes");
+    if (b_mn) {  // B2 is [S*SEG, N] (same orientation as B)
+      TORCH_CHECK(zt.size(0) >= M && bt.size(1) == N && zt.size(1) == bt.size(0), "dsv_gemm: LoRA shapes");
+    } else {     // B2 is [N, S*SEG]
+      TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm: LoRA shapes");
+    }
     TORCH_CHECK(tile_slots->scalar_type() == at::kInt && tile_slots->numel() >= (M + BM - 1) / BM, "dsv_gemm: tile_slots");
     tz = make_tmap_bf16(zt.data_ptr(), M, zt.size(1), zt.stride(0), BM);
-    tb2 = make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), bn);
+    tb2 = b_mn ? make_tmap_bf16(bt.data_ptr(), bt.size(0), N, bt.stride(0), BK)
+               : make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), bn);
     args.lora_seg = (int)lora_seg;
     args.num_slots = (int)(zt.size(1) / lora_seg);
     args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());

@@ -364,3 +364,19 @@ def test_gemm_decode_swapped_lora(M, N, K):
     plain = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
     ops.gemm(x, w, plain)
     torch.testing.assert_close(plain.float(), x.float() @ w.float().t(), rtol=2e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 512, 384), (4096, 1024, 2048)])
+def test_gemm_mn_major_with_lora_block(M, N, K):
+    """MN-major GEMM with the adapter term as an extra K block (the backward's
+    fused dX = dY . W + dZ . A)."""
+    a, b = rnd(M, K, seed=41), rnd(K, N, scale=0.05, seed=42)
+    z = torch.zeros(M, 64, dtype=torch.bfloat16, device=DEV)
+    z[:, :48] = rnd(M, 48, seed=43)
+    b2 = torch.zeros(64, N, dtype=torch.bfloat16, device=DEV)
+    b2[:48] = rnd(48, N, scale=0.05, seed=44)
+    ts = torch.ones(-(-M // 128), dtype=torch.int32, device=DEV)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(a, b, out, b_mn=True, epi=ops.EPI_F32, z=z, b2=b2, tile_slots=ts, lora_seg=64, max_ctas=1 << 30)
+    exp = a.float() @ b.float() + z.float() @ b2.float()
+    torch.testing.assert_close(out, exp, rtol=2e-2, atol=3e-2)
