@@ -116,6 +116,9 @@ class CoServingEngine:
             rows = ecfg.max_num_batched_tokens + (cap_tokens if self.ft_enabled else 0) + 128
             self.peer_ws = PeerWorkspace(comm, rows, self.arch.hidden)
             comm.peer_ws = self.peer_ws
+            if not self._self_test_fused(comm):
+                self.peer_ws.close()
+                self.peer_ws = comm.peer_ws = None
         # ---- KV cache sized from what is left
         self.kv = self._alloc_kv()
         self.model = DecoderModel(self.weights, self.kv.k, self.kv.v, self.lora, comm)
@@ -262,6 +265,36 @@ class CoServingEngine:
                                            self.ecfg.max_num_batched_tokens, self.tbt_window)
         self.jobs.submit(FinetuneJobSpec.from_finetune_config(cfg), self.rcfg.enable_adapter_routing)
 
+    def _self_test_fused(self, comm) -> bool:
+        """Check the fused GEMM + all-reduce against GEMM + NCCL on this
+        machine's ranks before serving with it (every rank takes the same
+        decision: the verdict is the MIN over ranks). A failure falls back to
+        the NCCL path for the whole run."""
+        import torch.distributed as dist
+        ok = 1
+        try:
+            g = torch.Generator(device=self.device).manual_seed(1234 + comm.rank)
+            for M in (3, 200):
+                K = 256
+                a = torch.randn(M, K, generator=g, device=self.device).to(self.dtype)
+                b = (torch.randn(self.arch.hidden, K, generator=g, device=self.device) * 0.05).to(self.dtype)
+                fused = ops.gemm_ar(a, b, self.peer_ws).float().clone()
+                ref = a.float() @ b.float().t()
+                dist.all_reduce(ref, group=comm.group)
+                err = float((fused - ref).abs().max()) / max(1e-6, float(ref.abs().max()))
+                if not err < 2e-2:
+                    ok = 0
+            torch.cuda.synchronize(self.device)
+            if ops.check_device_error() != 0:
+                ok = 0
+        except Exception as e:  # a failing launch must not take serving down
+            dprint(f"[tp] fused all-reduce self-test raised {e!r}")
+            ok = 0
+        ok = -comm.all_reduce_max_int(-ok)
+        if not ok:
+            dprint("[tp] fused GEMM + all-reduce failed its self-test: using GEMM + NCCL")
+        return bool(ok)
+
     def weight_hash(self) -> float:
         """Order-sensitive checksum of this rank's base weights (debug)."""
         h = 0.0
@@ -397,7 +430,8 @@ class CoServingEngine:
         if self.cuda:
             torch.cuda.synchronize(self.device)
 
-    def _save_trainer(self, path: str, save_id: str = "", extra: dict | None = None) -> str | None:
+    def _save_trainer(self, path: str, save_id: str = "", extra: dict | None = None,
+                      background: bool = False) -> str | None:
         """PEFT save of the trained adapter, merged across TP ranks (every
         rank takes part in the gather, so the driver records it first)."""
         if self.is_driver and self.tp_size > 1:
@@ -405,7 +439,7 @@ class CoServingEngine:
             self._flush_actions()
         if self.cuda:
             torch.cuda.synchronize(self.device)
-        return self.trainer.save_adapter(path, save_id, extra)
+        return self.trainer.save_adapter(path, save_id, extra, background=background)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_ids: list[int], params: SamplingParams | None = None,
@@ -451,7 +485,7 @@ class CoServingEngine:
                    "jobs": self.jobs.status()})
         return st
 
-    def save_adapter(self, path: str | None = None, save_id: str = "") -> str | None:
+    def save_adapter(self, path: str | None = None, save_id: str = "", background: bool = False) -> str | None:
         if self.trainer is None:
             raise RuntimeError("finetuning is not enabled")
         if path is None:
@@ -459,7 +493,7 @@ class CoServingEngine:
                 raise ValueError("no path given and finetune_param.adapter_save_path is unset")
             path = os.path.join(self.ftcfg.adapter_save_path, f"manual-{int(time.time())}")
         self._drain_backward()
-        return self._save_trainer(path, save_id)
+        return self._save_trainer(path, save_id, background=background)
 
     # ------------------------------------------------------------------ estimator state
     def save_estimator_state(self, path: str | None = None) -> str | None:
@@ -820,11 +854,11 @@ class CoServingEngine:
         from ..adapters import peft_io
         st = self.trainer.step
         if cfg.adapter_save_every_backwards > 0 and st % cfg.adapter_save_every_backwards == 0:
-            self._save_trainer(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"))
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"), background=True)
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
         if cfg.adapter_save_every_epoch and getattr(self, "_epoch_ended", False):
             ep = self.store.current_epoch if self.store else 0
-            self._save_trainer(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"))
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"), background=True)
             peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last, prefix="epoch-")
         self._epoch_ended = False
 
@@ -1052,6 +1086,8 @@ class CoServingEngine:
             if path:
                 self.tracker.write_prediction_stats_csv(path)
         self.stop_telemetry()
+        if self.trainer is not None:
+            self.trainer.wait_saves()
         if self.step_trace is not None:
             self.step_trace.close()
             self.step_trace = None

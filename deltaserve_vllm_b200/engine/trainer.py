@@ -75,6 +75,8 @@ class LoraTrainer:
         self.step = 0
         self.epoch = 0
         self.total_tokens = 0
+        self._writer = None          # background checkpoint writer (one thread)
+        self._pending_save = None
         self.losses: list[float] = []
         L = self.arch.num_layers
         # Captured per-layer backward graphs, keyed by the batch shape.
@@ -365,12 +367,37 @@ class LoraTrainer:
         shards = self.comm.gather_objects(mine)
         return peft_io.merge_tp_shards(shards) if shards is not None else None
 
-    def save_adapter(self, path: str, save_id: str = "", extra: dict | None = None) -> str | None:
+    def save_adapter(self, path: str, save_id: str = "", extra: dict | None = None,
+                     background: bool = False) -> str | None:
+        """PEFT checkpoint of the trained adapter (merged across TP ranks, on
+        rank 0). The tensors are gathered to host memory here; with
+        ``background`` the files are written by a writer thread, so the
+        serving loop does not wait on the disk — ``trainer_state.json`` (the
+        completion marker) or ``save_error.json`` appears when it is done."""
         full = self.export_full()
         if full is None:
             return None
         state = {"save_id": save_id, "step": self.step, "epoch": self.epoch,
                  "total_tokens": self.total_tokens, "time": time.time(),
                  "last_loss": self.losses[-1] if self.losses else None, **(extra or {})}
-        peft_io.write_peft_adapter(path, full, dict(self.adapter_config), state)
+        cfg = dict(self.adapter_config)
+        if not background:
+            peft_io.write_peft_adapter(path, full, cfg, state)
+            return path
+        if self._writer is None:
+            import concurrent.futures as cf
+            self._writer = cf.ThreadPoolExecutor(max_workers=1, thread_name_prefix="dsv-save")
+
+        def write():
+            try:
+                peft_io.write_peft_adapter(path, full, cfg, state)
+            except Exception as e:  # reported through the save handshake
+                peft_io.write_save_error(path, save_id, repr(e))
+        self._pending_save = self._writer.submit(write)
         return path
+
+    def wait_saves(self) -> None:
+        """Block until every background checkpoint write has finished."""
+        if self._pending_save is not None:
+            self._pending_save.result()
+            self._pending_save = None

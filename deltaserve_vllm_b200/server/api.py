@@ -200,17 +200,25 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         save_id = uuid.uuid4().hex
         if engine.trainer is None:
             return JSONResponse(status_code=409, content={"error": "finetuning is not enabled", "path": path})
-        fut = et.submit(lambda e: e.save_adapter(path, save_id))
+        # The engine thread gathers the tensors; the files are written in the
+        # background and this handler polls the save handshake for them.
+        fut = et.submit(lambda e: e.save_adapter(path, save_id, background=True))
         if not body.get("wait", True):
             return JSONResponse(status_code=202, content={"scheduled": True, "path": path, "save_id": save_id})
+        timeout = float(body.get("timeout_s", 300))
+        t0 = time.time()
         try:
-            await asyncio.wait_for(asyncio.wrap_future(fut), float(body.get("timeout_s", 300)))
+            await asyncio.wait_for(asyncio.wrap_future(fut), timeout)
         except asyncio.TimeoutError:
             return JSONResponse(status_code=202, content={"pending": True, "path": path, "save_id": save_id})
         except Exception as ex:
             return JSONResponse(status_code=500, content={"path": path, "saved": False, "error": str(ex)})
-        from ..adapters.peft_io import read_save_result
-        res = read_save_result(path, save_id) or {}
+        from ..adapters.peft_io import wait_save_result
+        res = await asyncio.to_thread(wait_save_result, path, save_id, max(0.0, timeout - (time.time() - t0)))
+        if res is None:
+            return JSONResponse(status_code=202, content={"pending": True, "path": path, "save_id": save_id})
+        if "error" in res:
+            return JSONResponse(status_code=500, content={"path": path, "saved": False, **res})
         return {"path": path, "saved": True, **res}
 
     @app.post("/save_estimator_state")
