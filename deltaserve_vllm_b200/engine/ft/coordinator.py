@@ -108,11 +108,16 @@ class FinetuneCoordinator:
         return off
 
     def unreserve(self, n: int, samples: list | None = None) -> None:
-        """Roll back a reservation whose step did not run."""
+        """Roll back a reservation whose step did not run (or was pre-empted).
+        The admission that made it may have closed the buffer for a flush;
+        with its rows gone that decision is re-made at the next admission."""
         self.reserved_fill = max(0, self.reserved_fill - int(n))
         if samples:
             ids = {id(s) for s in samples}
             self.buffer_samples = [s for s in self.buffer_samples if id(s) not in ids]
+        if not self.pending_backward and not self.disabled and self.ft_started:
+            self.epoch_flush_pending = False
+            self.admission_open = True
 
     def note_injection(self, next_sample_len: int | None, admitted_now: int = 0) -> None:
         """After an admission: close the buffer (flush pending) when the

@@ -695,6 +695,11 @@ class CoServingEngine:
                    f"prefill={len(out.prefill)} ft={len(out.ft)} t_in={out.t_in} t_ft={out.t_ft} "
                    f"bwd={'busy' if bwd_busy else 'idle'} pred_ms="
                    f"{'-' if pred is None else round(pred * 1e3, 3)}")
+        # Tier C: an FT-only step is abandoned between layers if a request
+        # arrives meanwhile (every rank stops at the same layer).
+        abort_check = ((lambda: self.arrival_flag)
+                       if (self.ftcfg.forward_interruptible and not self.profiling and self.ft_enabled) else None)
+        vote = (lambda f: self.comm.all_reduce_max_int(f)) if self.tp_size > 1 else None
         if self.cuda:
             with torch.cuda.stream(self.fwd_stream):
                 if uses_ft_slot and self._publish_evt is not None:
@@ -703,13 +708,19 @@ class CoServingEngine:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
                 toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
-                                              before_sample=feed)
+                                              before_sample=feed, abort_check=abort_check, vote=vote)
                 ev1.record()
         else:
             ev0 = time.perf_counter()
             toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
-                                          before_sample=feed)
+                                          before_sample=feed, abort_check=abort_check, vote=vote)
             ev1 = time.perf_counter()
+        if self.runner.last_aborted:
+            # Partial captures and KV pages of the FT rows are simply released.
+            self._rollback_ft(out)
+            self.stats["ft_aborts"] = self.stats.get("ft_aborts", 0) + 1
+            self.arrival_flag = False
+            return []
         if not out.prefill and not out.ft:
             self.stats["decode_steps"] = self.stats.get("decode_steps", 0) + 1
             self.stats["decode_enqueue_s"] = (self.stats.get("decode_enqueue_s", 0.0)
@@ -1150,10 +1161,12 @@ class CoServingEngine:
                             if has_ft and self._publish_evt is not None:
                                 self.fwd_stream.wait_event(self._publish_evt)
                             self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
-                                                         self.capture if has_ft else None)
+                                                         self.capture if has_ft else None,
+                                                         vote=self.comm.all_reduce_max_int)
                     else:
                         self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
-                                                     self.capture if has_ft else None)
+                                                     self.capture if has_ft else None,
+                                                     vote=self.comm.all_reduce_max_int)
                 elif kind == "bwd_start":
                     m = a[1]
                     if self.cuda:

@@ -14,7 +14,7 @@ import numpy as np
 import torch
 
 from .. import ops
-from ..models.decoder import CaptureBuffers, DecoderModel, ForwardBatch
+from ..models.decoder import CaptureBuffers, DecoderModel, FTAborted, ForwardBatch
 from .scheduler import SchedulerOutput
 
 
@@ -273,13 +273,39 @@ class ModelRunner:
         return (self.graphs is not None and meta["npf"] == 0 and meta["nd"] > 0
                 and DecodeGraphs.bucket(meta["nd"]) is not None)
 
-    def forward_follower(self, meta: dict, pk: "_Packer", cap) -> None:
-        """A follower rank's replay of a step: the same graph or kernels as rank 0."""
+    def abort_hook(self, should_abort, vote=None, ahead: int = 2):
+        """Per-layer pre-emption check of an FT-only forward (tier C): the host
+        never runs more than ``ahead`` layers ahead of the GPU (an event per
+        layer), so an abort lands within a couple of layers; under TP the
+        decision is a MAX vote so every rank stops at the same layer."""
+        events = []
+
+        def hook(l: int) -> bool:
+            if self.device.type == "cuda":
+                if l >= ahead:
+                    events[l - ahead].synchronize()
+                ev = torch.cuda.Event()
+                ev.record()
+                events.append(ev)
+            flag = 1 if should_abort() else 0
+            if vote is not None:
+                flag = vote(flag)
+            return bool(flag)
+        return hook
+
+    def forward_follower(self, meta: dict, pk: "_Packer", cap, vote=None) -> bool:
+        """A follower rank's replay of a step: the same graph or kernels as rank 0.
+        Returns False when the step was pre-empted (tier C, same layer as rank 0)."""
         if self.graph_eligible(meta):
             self.graphs.run(meta, pk)
-            return
+            return True
         b = self.batch_from(meta, pk)
-        self.model.forward(b, cap)
+        hook = self.abort_hook(lambda: False, vote) if meta.get("abortable") else None
+        try:
+            self.model.forward(b, cap, layer_hook=hook)
+        except FTAborted:
+            return False
+        return True
 
     def build_host(self, out: SchedulerOutput, ft_dst: int = 0) -> tuple[dict, _Packer, list]:
         bs = self.block_size
@@ -380,14 +406,17 @@ class ModelRunner:
         return b
 
     def execute(self, out: SchedulerOutput, cap: CaptureBuffers | None = None, ft_dst: int = 0,
-                on_host_plan=None, before_sample=None):
+                on_host_plan=None, before_sample=None, abort_check=None, vote=None):
         """Forward + sampling. Returns ({seq_no: token}, logits). ``on_host_plan``
         (rank 0 under TP) receives the host metadata before the forward is
         enqueued, so the other ranks can replay the same step."""
+        self.last_aborted = False
         if out.is_empty():
             return {}, None
         t0 = time.perf_counter()
         meta, pk, reqs = self.build_host(out, ft_dst)
+        # Tier C: an FT-only step can be abandoned between layers.
+        meta["abortable"] = bool(abort_check is not None and out.ft and not out.decode and not out.prefill)
         if on_host_plan is not None:
             on_host_plan(meta, pk)
         if self.graph_eligible(meta) and len(reqs) == meta["nd"]:
@@ -403,7 +432,13 @@ class ModelRunner:
             self.last_d2h_bytes = len(reqs) * 8
             return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}, self.graphs.last_logits
         b = self.batch_from(meta, pk)
-        logits = self.model.forward(b, cap if out.ft else None)
+        hook = self.abort_hook(abort_check, vote) if meta["abortable"] else None
+        try:
+            logits = self.model.forward(b, cap if out.ft else None, layer_hook=hook)
+        except FTAborted:
+            self.last_aborted = True
+            self.last_enqueue_s = time.perf_counter() - t0
+            return {}, None
         self.last_enqueue_s = time.perf_counter() - t0   # host time to enqueue the forward
         if before_sample is not None:
             before_sample()

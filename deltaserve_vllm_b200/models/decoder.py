@@ -97,6 +97,10 @@ class CaptureBuffers:
                     self.final_in) if t is not None)
 
 
+class FTAborted(Exception):
+    """Raised between layers when an FT-only forward is pre-empted (tier C)."""
+
+
 class Communicator:
     """Tensor-parallel collectives used by the forward. ``size == 1`` is a no-op."""
 
@@ -179,9 +183,11 @@ class DecoderModel:
 
     # ------------------------------------------------------------------ forward
     @torch.no_grad()
-    def forward(self, b: ForwardBatch, cap: CaptureBuffers | None = None) -> torch.Tensor:
+    def forward(self, b: ForwardBatch, cap: CaptureBuffers | None = None, layer_hook=None) -> torch.Tensor:
         """Runs all layers; returns fp32 logits [R, V] for ``b.logits_idx`` rows
-        (or the final hidden states [T, D] when ``logits_idx`` is None)."""
+        (or the final hidden states [T, D] when ``logits_idx`` is None).
+        ``layer_hook(l)`` runs on the host before layer ``l`` is enqueued; a
+        True return abandons the forward (:class:`FTAborted`)."""
         a, w = self.arch, self.w
         T, D = b.num_tokens, a.hidden
         dev, dt = w.embed.device, w.embed.dtype
@@ -203,6 +209,8 @@ class DecoderModel:
         mlp = torch.empty(T, D, dtype=dt, device=dev)
         eps = a.rms_eps
         for l, lw in enumerate(w.layers):
+            if layer_hook is not None and layer_hook(l):
+                raise FTAborted(l)
             sv = cap.layer_in[l] if cap_on else None
             if l == 0:
                 ops.rms_norm(residual, lw.in_ln, x, eps, save=sv, save_lo=lo, save_hi=hi, save_dst=dst)

@@ -96,3 +96,28 @@ def test_save_activations_off_trains_nothing_cpu():
         assert eng.trainer.step == 0
         assert eng.store.finished()            # samples were forwarded and retired
         assert eng.coord.completed_cycles >= 1
+
+
+def test_tier_c_abort_ft_only_step_cpu():
+    """An FT-only forward pre-empted between layers (tier C) releases its
+    rows (KV pages, capture reservation, claimed samples); training then
+    proceeds normally."""
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp, forward_interruptible=True, ft_only_admission_grace_ms=0)
+        orig = eng.runner.abort_hook
+        state = {"n": 0}
+
+        def patched(should_abort, vote=None, ahead=2):
+            def sa():
+                state["n"] += 1
+                return state["n"] == 2          # a request "arrives" before layer 1
+            return orig(sa, vote, ahead)
+        eng.runner.abort_hook = patched
+        eng.step()
+        assert eng.stats.get("ft_aborts") == 1
+        assert eng.coord.reserved_fill == 0 and eng.coord.fill_count == 0
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+        eng.runner.abort_hook = orig
+        eng.run_until_idle(max_steps=2000)
+        assert eng.coord.completed_cycles >= 2
+        assert eng.store.finished()
