@@ -255,6 +255,10 @@ class EngineConfig:
     # A preset name (``llama3-8b``, ``qwen3-0.6b`` ...), an HF model id whose
     # architecture is known, or a directory with an HF ``config.json``.
     model: str = "qwen3-tiny"
+    # Base weights: "auto" loads the model directory's *.safetensors when it
+    # has any and random-initialises otherwise; "safetensors" requires them;
+    # "dummy" always random-initialises (vLLM's load_format names).
+    load_format: str = "auto"
     tokenizer: str | None = None
     tokenizer_mode: str = "auto"
     trust_remote_code: bool = False

@@ -89,9 +89,7 @@ class CoServingEngine:
         self.arch = arch or resolve_arch(ecfg.model)
         self.tokenizer = tokenizer
         t0 = time.perf_counter()
-        self.weights = init_weights(self.arch, self.tp, seed=ecfg.seed, device=self.device,
-                                    dtype=self.dtype,
-                                    keep_full_head=self.ftcfg.enable_finetuning)
+        self.weights = self._load_weights(ecfg)
         # ---- LoRA slots: inference adapters + the pinned FT slot
         self.adapter_slots: dict[str, int] = {}
         self.adapter_meta: dict[str, dict] = {}
@@ -496,6 +494,24 @@ class CoServingEngine:
         return self._save_trainer(path, save_id, background=background)
 
     # ------------------------------------------------------------------ estimator state
+    def _load_weights(self, ecfg: EngineConfig):
+        """Base weights: the model directory's safetensors checkpoint (this
+        rank's shards only) or the seeded random initialisation."""
+        from ..models.loader import checkpoint_files, load_hf_weights
+        fmt = ecfg.load_format
+        if fmt not in ("auto", "safetensors", "dummy"):
+            raise ValueError(f"load_format must be auto, safetensors or dummy, got {fmt!r}")
+        files = [] if fmt == "dummy" else checkpoint_files(ecfg.model)
+        if fmt == "safetensors" and not files:
+            raise FileNotFoundError(f"load_format=safetensors but {ecfg.model!r} has no *.safetensors")
+        keep = self.ftcfg.enable_finetuning
+        if files:
+            dprint(f"loading {len(files)} safetensors file(s) from {ecfg.model} (tp rank {self.tp.rank})")
+            return load_hf_weights(self.arch, ecfg.model, self.tp, device=self.device, dtype=self.dtype,
+                                   keep_full_head=keep)
+        return init_weights(self.arch, self.tp, seed=ecfg.seed, device=self.device, dtype=self.dtype,
+                            keep_full_head=keep)
+
     def save_estimator_state(self, path: str | None = None) -> str | None:
         """Estimator coefficients plus the tracker's step samples as one JSON
         file, written atomically; with no ``path`` the configured

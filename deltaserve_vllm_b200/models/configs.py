@@ -110,7 +110,13 @@ def arch_from_hf_config(cfg: dict, name: str = "hf") -> ModelArch:
     heads = int(cfg["num_attention_heads"])
     hidden = int(cfg["hidden_size"])
     head_dim = int(cfg.get("head_dim") or hidden // heads)
-    rs = cfg.get("rope_scaling")
+    # Older configs carry ``rope_theta`` + ``rope_scaling``; newer ones one
+    # ``rope_parameters`` dict holding both (``rope_type`` "default" = none).
+    rp = cfg.get("rope_parameters") or {}
+    theta = float(cfg.get("rope_theta") or rp.get("rope_theta") or 10000.0)
+    rs = cfg.get("rope_scaling") or {k: v for k, v in rp.items() if k != "rope_theta"}
+    if rs and rs.get("rope_type", rs.get("type", "default")) == "default" and len(rs) <= 1:
+        rs = None
     if rs:
         rtype = rs.get("rope_type", rs.get("type", "default"))
         if rtype not in _SUPPORTED_ROPE:
@@ -123,7 +129,7 @@ def arch_from_hf_config(cfg: dict, name: str = "hf") -> ModelArch:
         num_heads=heads, num_kv_heads=int(cfg.get("num_key_value_heads", heads)),
         head_dim=head_dim, intermediate=int(cfg["intermediate_size"]),
         vocab=int(cfg["vocab_size"]), rms_eps=float(cfg.get("rms_norm_eps", 1e-6)),
-        rope_theta=float(cfg.get("rope_theta", 10000.0)), rope_scaling=rs or None,
+        rope_theta=theta, rope_scaling=rs or None,
         tie_embeddings=bool(cfg.get("tie_word_embeddings", False)),
         max_position=int(cfg.get("max_position_embeddings", 8192)))
 

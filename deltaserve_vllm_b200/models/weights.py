@@ -135,16 +135,24 @@ def full_layer_tensors(arch: ModelArch, i: int, seed: int, device, dtype=torch.b
     return t
 
 
-def shard_layer(arch: ModelArch, t: dict[str, torch.Tensor], tp: TPInfo) -> LayerWeights:
+def _layer_from(arch: ModelArch, get, tp: TPInfo) -> LayerWeights:
+    """One rank's layer from ``get(name, dim, start, length)``, which returns
+    the slice ``[start, start + length)`` along ``dim`` of the full HF-orientation
+    tensor ``name`` (``dim`` None: the whole tensor)."""
     q0, ql = tp.split(arch.q_size)
     k0, kl = tp.split(arch.kv_size)
     i0, il = tp.split(arch.intermediate)
-    qkv = torch.cat([t["q"][q0:q0 + ql], t["k"][k0:k0 + kl], t["v"][k0:k0 + kl]], 0).contiguous()
-    gate_up = interleave64(t["gate"][i0:i0 + il].t(), t["up"][i0:i0 + il].t()).t().contiguous()
+    qkv = torch.cat([get("q", 0, q0, ql), get("k", 0, k0, kl), get("v", 0, k0, kl)], 0).contiguous()
+    gate_up = interleave64(get("gate", 0, i0, il).t(), get("up", 0, i0, il).t()).t().contiguous()
+    norms = {n: get(n, None, 0, 0) for n in ("q_norm", "k_norm")} if arch.qk_norm else {}
     return LayerWeights(
-        qkv=qkv, o=t["o"][:, q0:q0 + ql].contiguous(), gate_up=gate_up,
-        down=t["down"][:, i0:i0 + il].contiguous(), in_ln=t["in_ln"], post_ln=t["post_ln"],
-        q_norm=t.get("q_norm"), k_norm=t.get("k_norm"))
+        qkv=qkv, o=get("o", 1, q0, ql).contiguous(), gate_up=gate_up,
+        down=get("down", 1, i0, il).contiguous(), in_ln=get("in_ln", None, 0, 0),
+        post_ln=get("post_ln", None, 0, 0), q_norm=norms.get("q_norm"), k_norm=norms.get("k_norm"))
+
+
+def shard_layer(arch: ModelArch, t: dict[str, torch.Tensor], tp: TPInfo) -> LayerWeights:
+    return _layer_from(arch, lambda n, d, s, l: t[n] if d is None else t[n].narrow(d, s, l), tp)
 
 
 def init_weights(arch: ModelArch, tp: TPInfo | None = None, seed: int = 0, device="cpu",
