@@ -429,7 +429,7 @@ class CoServingEngine:
             torch.cuda.synchronize(self.device)
 
     def _save_trainer(self, path: str, save_id: str = "", extra: dict | None = None,
-                      background: bool = False) -> str | None:
+                      background: bool = False, after=None) -> str | None:
         """PEFT save of the trained adapter, merged across TP ranks (every
         rank takes part in the gather, so the driver records it first)."""
         if self.is_driver and self.tp_size > 1:
@@ -437,7 +437,7 @@ class CoServingEngine:
             self._flush_actions()
         if self.cuda:
             torch.cuda.synchronize(self.device)
-        return self.trainer.save_adapter(path, save_id, extra, background=background)
+        return self.trainer.save_adapter(path, save_id, extra, background=background, after=after)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_ids: list[int], params: SamplingParams | None = None,
@@ -493,7 +493,6 @@ class CoServingEngine:
         self._drain_backward()
         return self._save_trainer(path, save_id, background=background)
 
-    # ------------------------------------------------------------------ estimator state
     def _load_weights(self, ecfg: EngineConfig):
         """Base weights: the model directory's safetensors checkpoint (this
         rank's shards only) or the seeded random initialisation."""
@@ -512,6 +511,7 @@ class CoServingEngine:
         return init_weights(self.arch, self.tp, seed=ecfg.seed, device=self.device, dtype=self.dtype,
                             keep_full_head=keep)
 
+    # ------------------------------------------------------------------ estimator state
     def save_estimator_state(self, path: str | None = None) -> str | None:
         """Estimator coefficients plus the tracker's step samples as one JSON
         file, written atomically; with no ``path`` the configured
@@ -881,12 +881,15 @@ class CoServingEngine:
         from ..adapters import peft_io
         st = self.trainer.step
         if cfg.adapter_save_every_backwards > 0 and st % cfg.adapter_save_every_backwards == 0:
-            self._save_trainer(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"), background=True)
-            peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last)
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"backward-{st:06d}"), background=True,
+                               after=lambda: peft_io.prune_checkpoints(cfg.adapter_save_path,
+                                                                       cfg.adapter_save_keep_last))
         if cfg.adapter_save_every_epoch and getattr(self, "_epoch_ended", False):
             ep = self.store.current_epoch if self.store else 0
-            self._save_trainer(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"), background=True)
-            peft_io.prune_checkpoints(cfg.adapter_save_path, cfg.adapter_save_keep_last, prefix="epoch-")
+            self._save_trainer(os.path.join(cfg.adapter_save_path, f"epoch-{ep:04d}"), background=True,
+                               after=lambda: peft_io.prune_checkpoints(cfg.adapter_save_path,
+                                                                       cfg.adapter_save_keep_last,
+                                                                       prefix="epoch-"))
         self._epoch_ended = False
 
     def _drain_backward(self) -> None:

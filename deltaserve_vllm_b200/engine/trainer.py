@@ -368,12 +368,14 @@ class LoraTrainer:
         return peft_io.merge_tp_shards(shards) if shards is not None else None
 
     def save_adapter(self, path: str, save_id: str = "", extra: dict | None = None,
-                     background: bool = False) -> str | None:
+                     background: bool = False, after=None) -> str | None:
         """PEFT checkpoint of the trained adapter (merged across TP ranks, on
         rank 0). The tensors are gathered to host memory here; with
         ``background`` the files are written by a writer thread, so the
         serving loop does not wait on the disk — ``trainer_state.json`` (the
-        completion marker) or ``save_error.json`` appears when it is done."""
+        completion marker) or ``save_error.json`` appears when it is done.
+        ``after`` (e.g. pruning older checkpoints) runs once the files are
+        written, on the same thread, so it sees the new directory."""
         full = self.export_full()
         if full is None:
             return None
@@ -383,6 +385,8 @@ class LoraTrainer:
         cfg = dict(self.adapter_config)
         if not background:
             peft_io.write_peft_adapter(path, full, cfg, state)
+            if after is not None:
+                after()
             return path
         if self._writer is None:
             import concurrent.futures as cf
@@ -393,6 +397,9 @@ class LoraTrainer:
                 peft_io.write_peft_adapter(path, full, cfg, state)
             except Exception as e:  # reported through the save handshake
                 peft_io.write_save_error(path, save_id, repr(e))
+                return
+            if after is not None:
+                after()
         self._pending_save = self._writer.submit(write)
         return path
 
