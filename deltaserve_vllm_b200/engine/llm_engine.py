@@ -57,6 +57,9 @@ from .scheduler import Scheduler, SchedulerOutput
 from .trainer import LoraTrainer
 
 FT_ADAPTER_NAME = "__finetune__"
+# Host-side fault injection for tests: raise in the backward after this many
+# layer steps (-1 = off); nothing is done to the GPU.
+_FAIL_BACKWARD_AT = int(os.environ.get("DSERVE_TEST_FAIL_BACKWARD", "-1"))
 
 
 @dataclass
@@ -831,6 +834,8 @@ class CoServingEngine:
         for _ in range(k):
             self._bwd_remaining -= 1
             try:
+                if _FAIL_BACKWARD_AT >= 0 and self.stats["bwd_layers"] >= _FAIL_BACKWARD_AT:
+                    raise RuntimeError("injected backward failure (DSERVE_TEST_FAIL_BACKWARD)")
                 if self.cuda:
                     with torch.cuda.stream(self.bwd_stream):
                         next(self._bwd_gen)
@@ -851,6 +856,34 @@ class CoServingEngine:
                 else:
                     self._finish_backward()
                 break
+            except Exception as e:
+                self._backward_failed(e)
+                break
+
+    def _backward_failed(self, err: Exception) -> None:
+        """A backward cycle raised (a host-side error, an allocation failure):
+        finetuning is switched off for the rest of the run (sticky), the
+        cycle's samples are dropped untrained and inference continues — the
+        reference's handling of a failed or dead backward child
+        (``deltaserve-plugin/deltaserve/coordinator.py:884-919``). Under TP
+        the ranks cannot agree on a half-run cycle, so the error propagates."""
+        if self.tp_size > 1:
+            raise err
+        dprint(f"[engine] backward cycle {self.coord.cycle} failed: {err!r}; finetuning disabled")
+        self._bwd_gen = None
+        self._bwd_result = None
+        self._bwd_done_evt = None
+        self._publish_evt = None
+        self._bwd_events.clear()
+        self._bwd_remaining = 0
+        c = self.coord
+        c.disable(f"backward failed: {err!r}")
+        c.pending_backward = False
+        c._t_trigger = None
+        c.fill_count = 0
+        c.sample_lens = []
+        c.buffer_samples = []
+        self.stats["bwd_failures"] = self.stats.get("bwd_failures", 0) + 1
 
     def _poll_backward(self) -> None:
         if self._bwd_done_evt is not None and self._bwd_done_evt.query():

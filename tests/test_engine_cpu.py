@@ -121,3 +121,30 @@ def test_tier_c_abort_ft_only_step_cpu():
         eng.run_until_idle(max_steps=2000)
         assert eng.coord.completed_cycles >= 2
         assert eng.store.finished()
+
+
+def test_backward_failure_disables_finetuning_sticky(monkeypatch):
+    """A backward cycle that raises (injected on the host) switches
+    finetuning off for the rest of the run; inference keeps serving and a
+    later start request does not re-enable it."""
+    from deltaserve_vllm_b200.engine import llm_engine
+    monkeypatch.setattr(llm_engine, "_FAIL_BACKWARD_AT", 1)
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        g = torch.Generator().manual_seed(1)
+        for i in range(4):
+            eng.add_request(f"r{i}", torch.randint(0, 1024, (30,), generator=g).tolist(),
+                            SamplingParams(max_tokens=6))
+        eng.run_until_idle(max_steps=2000)
+        assert eng.stats.get("bwd_failures") == 1
+        assert eng.coord.disabled and "backward failed" in eng.coord.disabled_reason
+        assert not eng.bwd_active and eng.trainer.step == 0
+        assert len(eng.finished) == 4 and all(len(r.output_ids) == 6 for r in eng.finished)
+        eng.start_finetuning()
+        assert eng.coord.disabled and not eng.coord.admission_open
+        eng.add_request("late", list(range(40)), SamplingParams(max_tokens=3))
+        fwd = eng.stats["ft_tokens_forwarded"]
+        eng.run_until_idle(max_steps=200)
+        assert eng.finished[-1].request_id == "late" and eng.stats["ft_tokens_forwarded"] == fwd
+        assert eng.finetuning_status()["disabled"]
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
