@@ -16,6 +16,10 @@ this engine's fused weights:
 
 * The base-weight input gradients ``dX = dY W`` are "MN-major" GEMMs on the
   tcgen05 kernel (no transposed weight copy).
+* Attention: on CUDA the fused varlen flash-style backward of
+  ``ops/csrc/attn_bwd.cu`` (scores, softmax statistics and the dS terms in
+  fp32 registers; the S / P / dS tiles never reach memory); on CPU the fp32
+  batched-matmul oracle :func:`attn_backward`.
 * Precision: GEMM operands bf16 with fp32 accumulation; residual-stream
   gradient, RMSNorm backward, attention scores/softmax and the LM head / CE in
   fp32 (the reference's precision contract).
@@ -162,15 +166,23 @@ class CycleInputs:
     attn_groups: list | None = None
 
 
-def attention_groups(starts, lens, device) -> list:
+class AttnGroups(list):
+    """Samples of equal length as (length, count, row index) groups, for the
+    batched fp32 path, plus ``tiles``: the 64-row tile table of the fused
+    attention kernels (built here, outside any CUDA-graph capture)."""
+    tiles: torch.Tensor | None = None
+
+
+def attention_groups(starts, lens, device) -> AttnGroups:
     groups: dict[int, list[int]] = {}
     for st, ln in zip(starts, lens):
         groups.setdefault(int(ln), []).append(int(st))
-    out = []
+    out = AttnGroups()
     for ln, sts in groups.items():
         idx = (torch.tensor(sts, device=device)[:, None]
                + torch.arange(ln, device=device)[None, :]).reshape(-1)
         out.append((ln, len(sts), idx))
+    out.tiles = ops.dense_attn_tiles(starts, lens, device)
     return out
 
 
@@ -282,10 +294,6 @@ class LoraBackward:
         self.scale = 1.0 / math.sqrt(self.hd)
         self._rows: dict[tuple[str, int], torch.Tensor] = {}
         self._ones_slots: dict = {}
-        if weights.embed.is_cuda:
-            # fp32 attention-backward matmuls on TF32 tensor cores (exact for
-            # the bf16-valued operands; fp32 accumulation).
-            torch.backends.cuda.matmul.allow_tf32 = True
         # Backward GEMMs launch one CTA per tile so the inference stream can
         # interleave between tiles (the backward runs at low priority).
         self.max_ctas = 1 << 30
@@ -436,8 +444,17 @@ class LoraBackward:
 
     def recompute_ctx(self, layer: int, qkv_raw: torch.Tensor, ci, positions, cos_sin) -> torch.Tensor:
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, self.w.layers[layer], cos_sin)
+        if qh.is_cuda:
+            out = torch.zeros(qh.shape[0], self.hq * self.hd, dtype=qkv_raw.dtype, device=qh.device)
+            return ops.attn_fwd_dense(qh, kh, vh, self._tiles(ci), self.scale, out)
         o = attn_forward(qh, kh, vh, ci.starts, ci.lens, self.scale, ci.attn_groups)
         return o.reshape(qh.shape[0], -1).to(qkv_raw.dtype)
+
+    def _tiles(self, ci) -> torch.Tensor:
+        g = ci.attn_groups
+        if g is None or getattr(g, "tiles", None) is None:
+            return ops.dense_attn_tiles(ci.starts, ci.lens, self.w.embed.device)
+        return g.tiles
 
     def recompute_resid_mid(self, layer: int, layer_in: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
         o = self._proj_lora(layer, "o", ctx, self.w.layers[layer].o)
@@ -492,8 +509,11 @@ class LoraBackward:
         d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz)        # [n, q_l]
         self.group_grads(layer, "o", ctx, d_mid_c, dz)
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
-        dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
-                                   self.scale, ci.attn_groups)
+        if qh.is_cuda:    # fused flash-style backward (sm_100a kernels)
+            dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale)
+        else:
+            dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
+                                       self.scale, ci.attn_groups)
         dq = rope_backward(dq, ci.cos, ci.sin)
         dk = rope_backward(dk, ci.cos, ci.sin)
         ql, kl = self.hq * self.hd, self.hkv * self.hd

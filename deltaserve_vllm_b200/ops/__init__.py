@@ -160,6 +160,50 @@ def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, sc
     return ref.paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, scale)
 
 
+# ----------------------------------------------------------------- trainer attention
+
+def dense_attn_tiles(starts, lens, device, bm: int = 64) -> torch.Tensor:
+    """int32 [T, 3] = (first row, length, tile row) of every ``bm``-row tile of
+    packed causal samples, ordered by tile row: the attention-backward kernels
+    use that order to start their heaviest CTAs first."""
+    rows = [(int(st), int(ln), t0) for t0 in range(0, max([int(x) for x in lens], default=0), bm)
+            for st, ln in zip(starts, lens) if t0 < int(ln)]
+    return torch.tensor(rows, dtype=torch.int32).reshape(-1, 3).to(device)
+
+
+def attn_bwd(q, k, v, d_o, tiles, scale):
+    """Gradients of causal varlen GQA attention over packed samples.
+
+    ``q`` [n, Hq, 128] / ``k``, ``v`` [n, Hkv, 128] (bf16 on CUDA; row strides
+    free, heads adjacent), ``d_o`` fp32 [n, Hq * 128], ``tiles`` from
+    :func:`dense_attn_tiles`. Returns fp32 ``dq`` [n, Hq, 128] and ``dk``,
+    ``dv`` [n, Hkv, 128]; rows outside every sample are zero."""
+    n, hq, hd = q.shape
+    hkv = k.shape[1]
+    dev = q.device
+    dq = torch.zeros(n, hq, hd, dtype=torch.float32, device=dev)
+    dk = torch.zeros(n, hkv, hd, dtype=torch.float32, device=dev)
+    dv = torch.zeros(n, hkv, hd, dtype=torch.float32, device=dev)
+    if q.is_cuda:
+        lse = torch.empty(hq, n, dtype=torch.float32, device=dev)
+        dd = torch.empty(hq, n, dtype=torch.float32, device=dev)
+        do_bf = torch.empty(n, hq * hd, dtype=torch.bfloat16, device=dev)
+        _native(2).attn_bwd(q, k, v, d_o.reshape(n, hq * hd), tiles, lse, dd, do_bf, dq, dk, dv, scale)
+        return dq, dk, dv
+    ref.dense_attn_bwd(q, k, v, d_o.reshape(n, hq, hd), tiles, scale, dq, dk, dv)
+    return dq, dk, dv
+
+
+def attn_fwd_dense(q, k, v, tiles, scale, out):
+    """Causal varlen GQA attention over packed samples into ``out`` [n, >= Hq*128]
+    (bf16 on CUDA); rows outside every sample are left untouched."""
+    if q.is_cuda:
+        _native().attn_fwd_dense(q, k, v, tiles, out, scale)
+        return out
+    ref.dense_attn_fwd(q, k, v, tiles, scale, out)
+    return out
+
+
 # ----------------------------------------------------------------- LoRA / misc
 
 def lora_shrink(x, A, slot_ids, Z, seg):

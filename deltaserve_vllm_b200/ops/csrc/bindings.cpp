@@ -18,7 +18,17 @@ void dsv_peer_close(int64_t addr);
 void dsv_peer_free(int64_t addr);
 void dsv_peer_zero(int64_t addr, int64_t bytes);
 int64_t dsv_read_error_gemm(bool clear);
-static int64_t dsv_read_error(bool clear) { return dsv_read_error_gemm(clear); }
+int64_t dsv_read_error_attn_bwd(bool clear);
+static int64_t dsv_read_error(bool clear) {
+  const int64_t g = dsv_read_error_gemm(clear);
+  const int64_t a = dsv_read_error_attn_bwd(clear);
+  return g != 0 ? g : a;
+}
+void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
+                  torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, torch::Tensor dq, torch::Tensor dk,
+                  torch::Tensor dv, double scale);
+void dsv_attn_fwd_dense(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles, torch::Tensor o,
+                        double scale);
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
                        int64_t num_heads, double scale);
@@ -57,6 +67,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
   m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
   m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");
+  m.def("attn_bwd", &dsv_attn_bwd, "varlen causal GQA attention backward (dQ, dK, dV)");
+  m.def("attn_fwd_dense", &dsv_attn_fwd_dense, "varlen causal GQA attention forward on packed rows");
   m.def("rms_norm", &dsv_rms_norm, "RMSNorm / fused residual add + RMSNorm (+ row capture)");
   m.def("qk_norm_rope_cache", &dsv_qk_norm_rope_cache, "q/k norm + RoPE + paged KV write");
   m.def("lora_shrink", &dsv_lora_shrink, "segmented multi-LoRA shrink");

@@ -139,6 +139,29 @@ def _ce(R, V):
     return (lambda: ops.ce_fwd_bwd(logits, tgt, loss, grad, 1.0), R * V * (4 + 2), 0)
 
 
+def _attn_bwd(n_seq, L, Hq=32, Hkv=8, torch_path=False):
+    """Trainer attention backward over n_seq packed causal samples of L tokens
+    (q/k/v strided views of one fused qkv buffer, fp32 dO). FLOPs: the five
+    causal 128-deep products of a standard flash backward (QK^T, dP, dV, dQ,
+    dK); the fused kernels also recompute QK^T and PV in their q-side pass."""
+    from ..models.lora_backward import attn_backward, attention_groups
+    n = n_seq * L
+    qkv = rnd(n, (Hq + 2 * Hkv) * 128, seed=7)
+    q = qkv[:, :Hq * 128].view(n, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(n, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].view(n, Hkv, 128)
+    d_o = rnd(n, Hq * 128, dtype=torch.float32, seed=8)
+    starts, lens = [i * L for i in range(n_seq)], [L] * n_seq
+    groups = attention_groups(starts, lens, DEV)
+    flops = 5 * n_seq * Hq * 128 * 2 * (L * (L + 1) / 2)
+    byts = 2 * qkv.numel() + 4 * d_o.numel() + 4 * n * (Hq + 2 * Hkv) * 128
+    if torch_path:
+        fn = lambda: attn_backward(q, k, v, d_o.view(n, Hq, 128), starts, lens, 1 / math.sqrt(128), groups)
+    else:
+        fn = lambda: ops.attn_bwd(q, k, v, d_o, groups.tiles, 1 / math.sqrt(128))
+    return fn, byts, flops
+
+
 def _adamw(n):
     p, g = rnd(n, dtype=torch.float32, seed=1), rnd(n, dtype=torch.float32, seed=2)
     m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
@@ -194,6 +217,8 @@ CASES = {
     "gemm_ar_decode_down": lambda: _gemm_ar(64, 4096, 14336),
     "attn_prefill_8x512": lambda: _prefill(8, 512),
     "attn_prefill_2x2048": lambda: _prefill(2, 2048),
+    "attn_bwd_8x512": lambda: _attn_bwd(8, 512),
+    "attn_bwd_torch_fp32_8x512": lambda: _attn_bwd(8, 512, torch_path=True),
     "attn_decode_64x1024": lambda: _decode(64, 1024),
     "attn_decode_16x4096": lambda: _decode(16, 4096),
     "rms_norm_add_8192x4096": lambda: _rms(8192, 4096),

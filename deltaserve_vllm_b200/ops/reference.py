@@ -245,3 +245,47 @@ def swiglu_bwd(gu, dact, dgu, act=None):
     dgu.copy_(interleave64(d_g, d_u).to(dgu.dtype))
     if act is not None:
         act.copy_((silu * u).to(act.dtype))
+
+
+# ----------------------------------------------------------------- trainer attention
+
+def _tile_samples(tiles: torch.Tensor) -> list[tuple[int, int]]:
+    return [(st, ln) for st, ln, r in tiles.cpu().tolist() if r == 0]
+
+
+def _dense_attn_probs(q, k, scale):
+    """fp32 causal softmax of one sample: q [l, Hq, d], k [l, Hkv, d] -> [Hq, l, l]."""
+    ln, hq, _ = q.shape
+    kk = k.float().repeat_interleave(hq // k.shape[1], 1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), kk) * scale
+    mask = torch.triu(torch.ones(ln, ln, dtype=torch.bool, device=q.device), 1)
+    return s.masked_fill(mask, float("-inf")).softmax(-1)
+
+
+def dense_attn_fwd(q, k, v, tiles, scale, out):
+    hq, hd = q.shape[1], q.shape[2]
+    for st, ln in _tile_samples(tiles):
+        p = _dense_attn_probs(q[st:st + ln], k[st:st + ln], scale)
+        vv = v[st:st + ln].float().repeat_interleave(hq // v.shape[1], 1)
+        o = torch.einsum("hqk,khd->qhd", p, vv).reshape(ln, hq * hd)
+        out[st:st + ln, :hq * hd] = o.to(out.dtype)
+    return out
+
+
+def dense_attn_bwd(q, k, v, d_o, tiles, scale, dq, dk, dv):
+    """fp32 gradients of causal GQA attention per packed sample (d_o [n, Hq, d])."""
+    hq, hkv, hd = q.shape[1], k.shape[1], q.shape[2]
+    G = hq // hkv
+    for st, ln in _tile_samples(tiles):
+        sl = slice(st, st + ln)
+        p = _dense_attn_probs(q[sl], k[sl], scale)                       # [Hq, l, l]
+        kk = k[sl].float().repeat_interleave(G, 1)
+        vv = v[sl].float().repeat_interleave(G, 1)
+        do = d_o[sl].float()
+        dvv = torch.einsum("hqk,qhd->khd", p, do)
+        dp = torch.einsum("qhd,khd->hqk", do, vv)
+        ds = p * (dp - (dp * p).sum(-1, keepdim=True))
+        dq[sl] = torch.einsum("hqk,khd->qhd", ds, kk) * scale
+        dkk = torch.einsum("hqk,qhd->khd", ds, q[sl].float()) * scale
+        dk[sl] = dkk.view(ln, hkv, G, hd).sum(2)
+        dv[sl] = dvv.view(ln, hkv, G, hd).sum(2)

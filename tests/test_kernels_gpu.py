@@ -162,6 +162,54 @@ def test_paged_prefill(bs, Hq, Hkv):
     torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
 
 
+def _packed_qkv(lens, Hq, Hkv, seed, pad=8):
+    """q/k/v as strided head views of one fused [n, (Hq+2Hkv)*128] bf16 buffer
+    (the trainer's layout), samples packed back to back, padding rows at the end."""
+    n = -(-sum(lens) // pad) * pad
+    qkv = rnd(n, (Hq + 2 * Hkv) * 128, seed=seed)
+    ql, kl = Hq * 128, Hkv * 128
+    q = qkv[:, :ql].view(n, Hq, 128)
+    k = qkv[:, ql:ql + kl].view(n, Hkv, 128)
+    v = qkv[:, ql + kl:].view(n, Hkv, 128)
+    starts = [sum(lens[:i]) for i in range(len(lens))]
+    return q, k, v, starts, n
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4), (32, 8)])
+def test_attn_bwd_varlen_gqa(Hq, Hkv):
+    lens = [1, 37, 64, 65, 130, 200, 513] if Hq <= 8 else [512, 512, 300, 7]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=31)
+    g = torch.Generator(device=DEV).manual_seed(32)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV)
+    scale = 1 / math.sqrt(128)
+    dq, dk, dv = ops.attn_bwd(q, k, v, d_o, tiles, scale)
+    eq = torch.zeros(n, Hq, 128)
+    ek, ev = torch.zeros(n, Hkv, 128), torch.zeros(n, Hkv, 128)
+    ref.dense_attn_bwd(q.cpu(), k.cpu(), v.cpu(), d_o.cpu().view(n, Hq, 128), tiles.cpu(), scale, eq, ek, ev)
+    for got, exp in ((dq, eq), (dk, ek), (dv, ev)):
+        got = got.cpu()
+        err = (got - exp).abs().max() / exp.abs().max()
+        assert err < 2e-2, float(err)
+    used = sum(lens)
+    assert dq[used:].abs().max() == 0 and dk[used:].abs().max() == 0
+    # deterministic: a second run is bit-identical
+    dq2, dk2, dv2 = ops.attn_bwd(q, k, v, d_o, tiles, scale)
+    assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (32, 8)])
+def test_attn_fwd_dense(Hq, Hkv):
+    lens = [3, 64, 129, 500]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=33)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV)
+    out = torch.zeros(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+    ops.attn_fwd_dense(q, k, v, tiles, 1 / math.sqrt(128), out)
+    exp = torch.zeros(n, Hq * 128)
+    ref.dense_attn_fwd(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), 1 / math.sqrt(128), exp)
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
 def test_paged_decode(G):
     Hkv, bs = 2, 64

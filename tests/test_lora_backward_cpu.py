@@ -33,3 +33,40 @@ def test_training_reduces_loss():
     trainer, res = manual_backward(arch, seqs, ad, 8, 16, lr=5e-3, steps=8, mask_prefix=0)
     losses = [r.loss for r in res]
     assert losses[-1] < losses[0] - 0.05, losses
+
+
+def test_dense_attention_reference_matches_autograd():
+    """The packed varlen attention oracle (the fused kernels' reference) and
+    the batched fp32 trainer path both equal autograd of causal GQA attention."""
+    import math
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.models.lora_backward import attn_backward
+    torch.manual_seed(0)
+    lens, Hq, Hkv, hd = [5, 17, 64, 3], 4, 2, 128
+    n = sum(lens) + 3
+    starts = [sum(lens[:i]) for i in range(len(lens))]
+    q = torch.randn(n, Hq, hd, dtype=torch.float64, requires_grad=True)
+    k = torch.randn(n, Hkv, hd, dtype=torch.float64, requires_grad=True)
+    v = torch.randn(n, Hkv, hd, dtype=torch.float64, requires_grad=True)
+    do = torch.randn(n, Hq, hd, dtype=torch.float64)
+    scale = 1 / math.sqrt(hd)
+    out = torch.zeros(n, Hq, hd, dtype=torch.float64)
+    for st, ln in zip(starts, lens):
+        sl = slice(st, st + ln)
+        kk, vv = k[sl].repeat_interleave(2, 1), v[sl].repeat_interleave(2, 1)
+        s = torch.einsum("qhd,khd->hqk", q[sl], kk) * scale
+        s = s.masked_fill(torch.triu(torch.ones(ln, ln, dtype=torch.bool), 1), float("-inf"))
+        out[sl] = torch.einsum("hqk,khd->qhd", s.softmax(-1), vv)
+    (out * do).sum().backward()
+    tiles = ops.dense_attn_tiles(starts, lens, "cpu")
+    assert tiles[:, 2].tolist() == sorted(tiles[:, 2].tolist())
+    dq, dk, dv = ops.attn_bwd(q.detach().float(), k.detach().float(), v.detach().float(),
+                              do.float().reshape(n, Hq * hd), tiles, scale)
+    for got, exp in ((dq, q.grad), (dk, k.grad), (dv, v.grad)):
+        torch.testing.assert_close(got.double(), exp, rtol=1e-4, atol=1e-5)
+    dq2, dk2, dv2 = attn_backward(q.detach().float(), k.detach().float(), v.detach().float(), do.float(),
+                                  starts, lens, scale)
+    torch.testing.assert_close(dq2.double(), q.grad, rtol=1e-4, atol=1e-5)
+    o = ops.attn_fwd_dense(q.detach().float(), k.detach().float(), v.detach().float(), tiles, scale,
+                           torch.zeros(n, Hq * hd))
+    torch.testing.assert_close(o.double().view(n, Hq, hd), out.detach(), rtol=1e-4, atol=1e-5)
