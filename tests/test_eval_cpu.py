@@ -72,3 +72,10 @@ def test_replay_report_and_top():
         assert rep["requests"]["completed"] == len(trace)
         cmp_ = report.compare(s, s)
         assert cmp_["completed"]["delta"] == 0
+
+
+def test_pure_ft_throughput_cpu():
+    from deltaserve_vllm_b200.eval import pure_ft
+    r = pure_ft.run("qwen3-tiny", seq=32, batch=2, cycles=3, warmup=1, device="cpu", rank=8)
+    assert r["cycles"] == 3 and r["ft_tokens"] == 3 * 2 * 32
+    assert r["ft_tok_s"] > 0 and r["wall_s"] > 0

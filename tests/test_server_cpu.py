@@ -9,6 +9,7 @@ import textwrap
 import time
 
 import pytest
+import torch
 from fastapi.testclient import TestClient
 
 from deltaserve_vllm_b200.adapters import peft_io
@@ -169,3 +170,25 @@ def test_shipped_config_templates_load():
         ecfg, ftcfg, rcfg, extras, host, port = launch.resolve(launch.parse(["--config", f]))
         assert ecfg.model and port > 0
         assert ftcfg.enable_finetuning
+
+
+def test_toy_adapter_builder(tmp_path):
+    """The toy-adapter CLI trains adapters with the engine itself and writes
+    PEFT dirs, their -ft twins and the topic corpus."""
+    from deltaserve_vllm_b200.adapters import peft_io, toy
+    out = str(tmp_path / "adapters")
+    assert toy.main(["--model", "qwen3-tiny", "--out", out, "--count", "2", "--rank", "8", "--alpha", "16",
+                     "--epochs", "1", "--device", "cpu"]) == 0
+    assert sorted(os.listdir(out)) == ["toy-00", "toy-00-ft", "toy-01", "toy-01-ft"]
+    t0, cfg = peft_io.read_adapter(os.path.join(out, "toy-00"))
+    t0ft, _ = peft_io.read_adapter(os.path.join(out, "toy-00-ft"))
+    t1, _ = peft_io.read_adapter(os.path.join(out, "toy-01"))
+    assert cfg["r"] == 8 and sorted(cfg["target_modules"]) == ["k_proj", "o_proj", "q_proj", "v_proj"]
+    assert all(".mlp." not in k for k in t0)
+    assert all(torch.equal(t0[k], t0ft[k]) for k in t0)
+    bkeys = [k for k in t0 if ".lora_B." in k]
+    assert any(t0[k].abs().max() > 0 for k in bkeys)            # trained away from B = 0
+    assert any(not torch.equal(t0[k], t1[k]) for k in bkeys)
+    lines = open(os.path.join(out, "toy-01", "data.txt")).read().splitlines()
+    assert len(lines) == 96 and all(line.endswith(")") for line in lines)
+    assert toy.topic_corpus(0)[0] != toy.topic_corpus(1)[0]
