@@ -39,7 +39,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import ops
-from ..ops import EPI_F32, EPI_F32_ACCUM
+from ..ops import EPI_F32, EPI_F32_ACCUM, EPI_SWIGLU_BWD
 from ..ops.reference import deinterleave64, interleave64
 from .configs import ModelArch
 from .lora import GROUP_PROJS, GROUPS, COLUMN_PARALLEL, GroupGeom, group_geoms, peft_key, shard_lora_factor
@@ -348,10 +348,16 @@ class LoraBackward:
         input gradient before the A factor."""
         return self._mm(dY, self._bfull(layer, g), b_mn=True)
 
-    def dx_gemm(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor) -> torch.Tensor:
+    def dx_gemm(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor,
+                swiglu_gu: torch.Tensor | None = None, act_out: torch.Tensor | None = None) -> torch.Tensor:
         """dX = dY . W + dZ . A in ONE GEMM: the rank-R adapter term rides as
         one extra 64-deep K block (dZ and A zero-padded to 64) instead of a
-        second pass over the fp32 dX."""
+        second pass over the fp32 dX.
+
+        With ``swiglu_gu`` (the saved interleaved gate/up of the MLP) the
+        product is d(act) and the epilogue applies the SwiGLU backward
+        instead of storing it: the result is d(gate_up) in the compute dtype
+        (and the activation into ``act_out`` when given)."""
         n = dY.shape[0]
         PR = dZ.shape[1]
         seg = -(-PR // 64) * 64
@@ -359,6 +365,10 @@ class LoraBackward:
         if not dY.is_cuda:
             out = self._mm(dY, W, b_mn=True)
             out += dZ @ A
+            if swiglu_gu is not None:
+                d_gu = torch.empty(n, swiglu_gu.shape[1], dtype=self.cdt, device=dY.device)
+                ops.swiglu_bwd(swiglu_gu, out, d_gu, act_out)
+                return d_gu
             return out
         zp = torch.zeros(n, seg, dtype=self.cdt, device=dY.device)
         zp[:, :PR] = dZ
@@ -369,6 +379,12 @@ class LoraBackward:
         if ts is None:
             ts = torch.ones(key[0], dtype=torch.int32, device=dY.device)
             self._ones_slots[key] = ts
+        if swiglu_gu is not None:
+            out = torch.empty(n, swiglu_gu.shape[1], dtype=self.cdt, device=dY.device)
+            ops.gemm(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), out, b_mn=True,
+                     epi=EPI_SWIGLU_BWD, z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas,
+                     aux=swiglu_gu, aux_out=act_out)
+            return out
         out = torch.empty(n, W.shape[1], dtype=torch.float32, device=dY.device)
         ops.gemm(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), out, b_mn=True, epi=EPI_F32,
                  z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas)
@@ -411,7 +427,11 @@ class LoraBackward:
         w = self.w
         eps = self.arch.rms_eps
         head = w.lm_head_full if w.lm_head_full is not None else w.lm_head
-        h = rmsnorm_fwd(final_in, w.final_norm, eps)
+        if final_in.is_cuda:    # the norm kernels (bf16 out, fp32 inside)
+            h = torch.empty(final_in.shape, dtype=self.cdt, device=final_in.device)
+            ops.rms_norm(final_in, w.final_norm, h, eps)
+        else:
+            h = rmsnorm_fwd(final_in, w.final_norm, eps)
         if n_valid == 0:
             return (torch.zeros((), device=final_in.device),
                     torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device))
@@ -423,7 +443,10 @@ class LoraBackward:
         del logits
         dh = self._mm(dlog, head, b_mn=True)                # [n, D]
         del dlog
-        d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
+        if final_in.is_cuda:
+            d_final = ops.rms_norm_bwd(final_in, dh, w.final_norm, eps)
+        else:
+            d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
         return loss.sum(), d_final
 
     # ------------------------------------------------------------ recompute
@@ -488,13 +511,16 @@ class LoraBackward:
         # ---- MLP -------------------------------------------------------
         dh_c = _bf(dh, cdt)
         dz = self.group_dz(layer, "down", dh_c)
-        d_act = self.dx_gemm(layer, "down", dh_c, lw.down, dz)     # [n, I_l] fp32
+        # d(act) = dh . W_down (+ adapter) with the SwiGLU backward applied in
+        # the GEMM epilogue: d(gate_up) directly, and the activation when it
+        # was not captured.
+        act_out = None
         if act is None:
-            g, u = deinterleave64(gate_up.float())
-            act = _bf(F.silu(g) * u, x.dtype)
+            act_out = torch.empty(n, gate_up.shape[1] // 2, dtype=x.dtype, device=dev)
+        d_gu = self.dx_gemm(layer, "down", dh_c, lw.down, dz, swiglu_gu=gate_up, act_out=act_out)
+        if act is None:
+            act = act_out
         self.group_grads(layer, "down", act, dh_c, dz)
-        d_gu = torch.empty(n, gate_up.shape[1], dtype=cdt, device=dev)
-        ops.swiglu_bwd(gate_up, d_act, d_gu)
         x2 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
         dz = self.group_dz(layer, "gate_up", d_gu)
@@ -509,15 +535,25 @@ class LoraBackward:
         d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz)        # [n, q_l]
         self.group_grads(layer, "o", ctx, d_mid_c, dz)
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
-        if qh.is_cuda:    # fused flash-style backward (sm_100a kernels)
-            dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale)
+        ql, kl = self.hq * self.hd, self.hkv * self.hd
+        d_qkv = torch.empty(n, ql + 2 * kl, dtype=cdt, device=dev)
+        if qh.is_cuda:
+            # Fused flash-style backward; its epilogues undo RoPE and store
+            # bf16 straight into d(qkv) (dq / dk stay fp32 for the Qwen3 q/k
+            # norm backward). Rows past the samples carry no gradient.
+            d_qkv[ci.n:].zero_()
+            mask = 4 if self.arch.qk_norm else 7
+            dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale, rope=(ci.cos, ci.sin),
+                                      dqkv=d_qkv, bf16_mask=mask)
         else:
             dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
                                        self.scale, ci.attn_groups)
-        dq = rope_backward(dq, ci.cos, ci.sin)
-        dk = rope_backward(dk, ci.cos, ci.sin)
-        ql, kl = self.hq * self.hd, self.hkv * self.hd
-        d_qkv = torch.empty(n, ql + 2 * kl, dtype=cdt, device=dev)
+            dq = rope_backward(dq, ci.cos, ci.sin)
+            dk = rope_backward(dk, ci.cos, ci.sin)
+            d_qkv[:, ql + kl:] = dv.reshape(n, kl)
+            if not self.arch.qk_norm:
+                d_qkv[:, :ql] = dq.reshape(n, ql)
+                d_qkv[:, ql:ql + kl] = dk.reshape(n, kl)
         if self.arch.qk_norm:
             q_pre = qkv_raw[:, :ql].reshape(n * self.hq, self.hd)
             k_pre = qkv_raw[:, ql:ql + kl].reshape(n * self.hkv, self.hd)
@@ -525,10 +561,6 @@ class LoraBackward:
             dkn = ops.rms_norm_bwd(k_pre, dk.reshape(n * self.hkv, self.hd), lw.k_norm, eps)
             d_qkv[:, :ql] = dqn.view(n, ql)
             d_qkv[:, ql:ql + kl] = dkn.view(n, kl)
-        else:
-            d_qkv[:, :ql] = dq.reshape(n, ql)
-            d_qkv[:, ql:ql + kl] = dk.reshape(n, kl)
-        d_qkv[:, ql + kl:] = dv.reshape(n, kl)
         x1 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(x, lw.in_ln, x1, eps)
         dz = self.group_dz(layer, "qkv", d_qkv)

@@ -16,7 +16,7 @@ import os
 import torch
 
 from . import reference as ref
-from .reference import EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM  # noqa: F401
+from .reference import EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM, EPI_SWIGLU_BWD  # noqa: F401
 
 _EXT = None
 _C_ERR: Exception | None = None
@@ -58,18 +58,22 @@ def check_device_error(clear: bool = True) -> int:
 # ----------------------------------------------------------------- GEMM
 
 def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None,
-         lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0, max_ctas=0):
+         lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0, max_ctas=0,
+         aux=None, aux_out=None):
     """``out = a @ b.T`` (``b`` is [N, K]) or ``a @ b`` (``b_mn``: ``b`` is [K, N]),
     plus the segmented LoRA expand ``z @ b2.T`` and the epilogue ``epi``:
-    bf16 / fp32 store, fp32 accumulate, or SwiGLU over 64-interleaved
-    gate/up columns. ``save`` receives raw accumulator rows [save_lo, save_hi).
+    bf16 / fp32 store, fp32 accumulate, SwiGLU over 64-interleaved gate/up
+    columns, or (``EPI_SWIGLU_BWD``, MN-major ``b``) the SwiGLU backward: the
+    product is d(act), ``aux`` the saved interleaved gate/up [M, 2N], ``out``
+    receives their gradient [M, 2N] and ``aux_out`` (optional) the activation.
+    ``save`` receives raw accumulator rows [save_lo, save_hi).
     ``max_ctas`` > number of SMs launches one CTA per tile (non-persistent)."""
     if a.is_cuda:
         _native().gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save,
-                       save_lo, save_hi, save_dst, force_bn, max_ctas)
+                       save_lo, save_hi, save_dst, force_bn, max_ctas, aux, aux_out)
         return out
     return ref.gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi,
-                    save_dst)
+                    save_dst, aux=aux, aux_out=aux_out)
 
 
 def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_splits=0, force_reducers=-1):
@@ -171,27 +175,48 @@ def dense_attn_tiles(starts, lens, device, bm: int = 64) -> torch.Tensor:
     return torch.tensor(rows, dtype=torch.int32).reshape(-1, 3).to(device)
 
 
-def attn_bwd(q, k, v, d_o, tiles, scale):
+def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0):
     """Gradients of causal varlen GQA attention over packed samples.
 
     ``q`` [n, Hq, 128] / ``k``, ``v`` [n, Hkv, 128] (bf16 on CUDA; row strides
     free, heads adjacent), ``d_o`` fp32 [n, Hq * 128], ``tiles`` from
-    :func:`dense_attn_tiles`. Returns fp32 ``dq`` [n, Hq, 128] and ``dk``,
-    ``dv`` [n, Hkv, 128]; rows outside every sample are zero."""
+    :func:`dense_attn_tiles`. ``rope = (cos, sin)`` ([n, 64] fp32) rotates dq
+    and dk back through RoPE (gradients w.r.t. the pre-RoPE q / k). Bits of
+    ``bf16_mask`` (1: dq, 2: dk, 4: dv) store those gradients as bf16 into the
+    fused ``dqkv`` [n, (Hq + 2 Hkv) * 128] (q, k, v column blocks) instead of
+    returning them. Returns (dq, dk, dv): fp32 [n, H, 128], or None for the
+    ones written into ``dqkv``; rows outside every sample are zero in the fp32
+    outputs and untouched in ``dqkv``."""
     n, hq, hd = q.shape
     hkv = k.shape[1]
     dev = q.device
-    dq = torch.zeros(n, hq, hd, dtype=torch.float32, device=dev)
-    dk = torch.zeros(n, hkv, hd, dtype=torch.float32, device=dev)
-    dv = torch.zeros(n, hkv, hd, dtype=torch.float32, device=dev)
+    if bf16_mask and dqkv is None:
+        raise ValueError("attn_bwd: bf16_mask needs dqkv")
+    outs = [None if bf16_mask & (1 << i) else torch.zeros(n, h, hd, dtype=torch.float32, device=dev)
+            for i, h in enumerate((hq, hkv, hkv))]
     if q.is_cuda:
         lse = torch.empty(hq, n, dtype=torch.float32, device=dev)
         dd = torch.empty(hq, n, dtype=torch.float32, device=dev)
         do_bf = torch.empty(n, hq * hd, dtype=torch.bfloat16, device=dev)
-        _native(2).attn_bwd(q, k, v, d_o.reshape(n, hq * hd), tiles, lse, dd, do_bf, dq, dk, dv, scale)
-        return dq, dk, dv
-    ref.dense_attn_bwd(q, k, v, d_o.reshape(n, hq, hd), tiles, scale, dq, dk, dv)
-    return dq, dk, dv
+        cos, sin = rope if rope is not None else (None, None)
+        _native(2).attn_bwd(q, k, v, d_o.reshape(n, hq * hd), tiles, lse, dd, do_bf, outs[0], outs[1],
+                            outs[2], scale, cos, sin, dqkv, bf16_mask)
+        return tuple(outs)
+    full = [torch.zeros(n, h, hd, dtype=torch.float32) for h in (hq, hkv, hkv)]
+    ref.dense_attn_bwd(q, k, v, d_o.reshape(n, hq, hd), tiles, scale, *full)
+    if rope is not None:
+        full[0] = ref.rope_bwd(full[0], *rope)
+        full[1] = ref.rope_bwd(full[1], *rope)
+    cols = (0, hq * hd, (hq + hkv) * hd)
+    samples = ref._tile_samples(tiles)
+    for i, t in enumerate(full):
+        if bf16_mask & (1 << i):
+            w = t.shape[1] * hd
+            for st, ln in samples:
+                dqkv[st:st + ln, cols[i]:cols[i] + w] = t[st:st + ln].reshape(ln, w).to(dqkv.dtype)
+        else:
+            outs[i].copy_(t.to(dev))
+    return tuple(outs)
 
 
 def attn_fwd_dense(q, k, v, tiles, scale, out):

@@ -61,7 +61,55 @@ struct AttnBwdArgs {
   float* dv;               // [n, Hkv * 128]
   __nv_bfloat16* o;        // forward-only: [n, ...] row stride o_stride
   int o_stride;
+  // Optional epilogue work: rotate dq / dk back through RoPE (cos / sin
+  // [n, 64] fp32, row stride rope_stride; nullptr = off) and store any of
+  // dq / dk / dv (bf16_mask bits 1 / 2 / 4) as bf16 straight into the fused
+  // d(qkv) rows (row stride dqkv_stride, head h of each part at its column
+  // offset + h * 128) instead of fp32 into dq / dk / dv.
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_stride;
+  __nv_bfloat16* dqkv;
+  int dqkv_stride, dq_col, dk_col, dv_col, bf16_mask;
 };
+
+// Row epilogue shared by both kernels: `acc` holds this thread's two rows
+// (h = 0: row g, h = 1: row g + 8) x columns j * 8 + 2t + {0, 1}. Scales,
+// optionally applies the inverse RoPE rotation (column c < 64 pairs with
+// c + 64, which the same thread holds in acc[j + 8]), and stores fp32 or bf16.
+__device__ __forceinline__ void store_grad_row(const AttnBwdArgs& a, const float (&acc)[16][4], int h, int grow,
+                                               float scale, bool rope, float* f32_row, __nv_bfloat16* bf_row,
+                                               int tq) {
+  float v[16][2];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    v[j][0] = acc[j][2 * h] * scale;
+    v[j][1] = acc[j][2 * h + 1] * scale;
+  }
+  if (rope) {
+    const float* cr = a.rope_cos + (size_t)grow * a.rope_stride;
+    const float* sr = a.rope_sin + (size_t)grow * a.rope_stride;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 cs = *reinterpret_cast<const float2*>(cr + j * 8 + 2 * tq);
+      const float2 sn = *reinterpret_cast<const float2*>(sr + j * 8 + 2 * tq);
+      const float x0 = v[j][0], y0 = v[j + 8][0], x1 = v[j][1], y1 = v[j + 8][1];
+      v[j][0] = x0 * cs.x + y0 * sn.x;
+      v[j + 8][0] = y0 * cs.x - x0 * sn.x;
+      v[j][1] = x1 * cs.y + y1 * sn.y;
+      v[j + 8][1] = y1 * cs.y - x1 * sn.y;
+    }
+  }
+  if (bf_row != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<uint32_t*>(bf_row + j * 8 + 2 * tq) = pack_bf16(v[j][0], v[j][1]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<float2*>(f32_row + j * 8 + 2 * tq) = make_float2(v[j][0], v[j][1]);
+  }
+}
 
 // Tile of 64 rows x 128 bf16 from global rows (row0 + r) of `src` (row stride
 // `stride`, column offset `col`) into swizzled smem; rows at or past `limit`
@@ -354,14 +402,15 @@ __global__ void __launch_bounds__(AB_THREADS) attn_bwd_q_kernel(AttnBwdArgs a) {
     __syncthreads();
   }
   cp_async_wait<0>();
+  const bool rope = a.rope_cos != nullptr;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int qi = my_row + g + h * 8;
     if (qi >= len) continue;
-    float* dst = a.dq + (size_t)(st + qi) * (a.num_heads * HD) + head * HD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      *reinterpret_cast<float2*>(dst + j * 8 + 2 * tq) = make_float2(dq[j][2 * h] * a.scale, dq[j][2 * h + 1] * a.scale);
+    const size_t grow = (size_t)(st + qi);
+    float* f32 = (a.bf16_mask & 1) ? nullptr : a.dq + grow * (a.num_heads * HD) + head * HD;
+    __nv_bfloat16* bf = (a.bf16_mask & 1) ? a.dqkv + grow * a.dqkv_stride + a.dq_col + head * HD : nullptr;
+    store_grad_row(a, dq, h, (int)grow, a.scale, rope, f32, bf, tq);
   }
 }
 
@@ -460,17 +509,19 @@ __global__ void __launch_bounds__(AB_THREADS) attn_bwd_kv_kernel(AttnBwdArgs a) 
   }
   cp_async_wait<0>();
   const int ldkv = (a.num_heads / a.group) * HD;
+  const bool rope = a.rope_cos != nullptr;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int kj = my_key + g + h * 8;
     if (kj >= len) continue;
-    float* dkr = a.dk + (size_t)(st + kj) * ldkv + kvh * HD;
-    float* dvr = a.dv + (size_t)(st + kj) * ldkv + kvh * HD;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      *reinterpret_cast<float2*>(dkr + j * 8 + 2 * tq) = make_float2(dk[j][2 * h] * a.scale, dk[j][2 * h + 1] * a.scale);
-      *reinterpret_cast<float2*>(dvr + j * 8 + 2 * tq) = make_float2(dv[j][2 * h], dv[j][2 * h + 1]);
-    }
+    const size_t grow = (size_t)(st + kj);
+    __nv_bfloat16* qkv_row = a.dqkv != nullptr ? a.dqkv + grow * a.dqkv_stride : nullptr;
+    store_grad_row(a, dk, h, (int)grow, a.scale, rope,
+                   (a.bf16_mask & 2) ? nullptr : a.dk + grow * ldkv + kvh * HD,
+                   (a.bf16_mask & 2) ? qkv_row + a.dk_col + kvh * HD : nullptr, tq);
+    store_grad_row(a, dv, h, (int)grow, 1.f, false,
+                   (a.bf16_mask & 4) ? nullptr : a.dv + grow * ldkv + kvh * HD,
+                   (a.bf16_mask & 4) ? qkv_row + a.dv_col + kvh * HD : nullptr, tq);
   }
 }
 
@@ -522,8 +573,10 @@ dsv::AttnBwdArgs make_args(const torch::Tensor& q, const torch::Tensor& k, const
 // left untouched); lse / dd [Hq, >= n] fp32 and do_bf [n, Hq*128] bf16 are
 // scratch.
 void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
-                  torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, torch::Tensor dq, torch::Tensor dk,
-                  torch::Tensor dv, double scale) {
+                  torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, c10::optional<torch::Tensor> dq,
+                  c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
+                  c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+                  c10::optional<torch::Tensor> dqkv, int64_t bf16_mask) {
   using namespace dsv;
   if (tiles.size(0) == 0) return;
   c10::cuda::CUDAGuard guard(q.device());
@@ -537,19 +590,45 @@ void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tens
                   dd.sizes() == lse.sizes(), "attn_bwd: lse / dd must be fp32 [Hq, >= n]");
   TORCH_CHECK(do_bf.scalar_type() == at::kBFloat16 && do_bf.is_contiguous() && do_bf.numel() == n * hq * HD,
               "attn_bwd: do_bf must be bf16 [n, Hq*128]");
-  for (auto* t : {&dq, &dk, &dv})
-    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->size(0) == n, "attn_bwd: fp32 outputs");
-  TORCH_CHECK(dq.numel() == n * hq * HD && dk.numel() == n * hkv * HD && dv.numel() == n * hkv * HD,
-              "attn_bwd: output shapes");
+  TORCH_CHECK(bf16_mask >= 0 && bf16_mask <= 7, "attn_bwd: bf16_mask is a 3-bit mask");
+  const int64_t want[3] = {hq, hkv, hkv};
+  const c10::optional<torch::Tensor>* outs[3] = {&dq, &dk, &dv};
+  for (int i = 0; i < 3; ++i) {
+    if (bf16_mask & (1 << i)) continue;
+    const auto& t = *outs[i];
+    TORCH_CHECK(t.has_value() && t->scalar_type() == at::kFloat && t->is_contiguous() &&
+                    t->numel() == n * want[i] * HD, "attn_bwd: fp32 output ", i, " must be [n, H, 128]");
+  }
+  if (bf16_mask != 0) {
+    TORCH_CHECK(dqkv.has_value() && dqkv->scalar_type() == at::kBFloat16 && dqkv->dim() == 2 &&
+                    dqkv->size(0) == n && dqkv->stride(1) == 1 && dqkv->stride(0) % 2 == 0 &&
+                    dqkv->size(1) >= (hq + 2 * hkv) * HD, "attn_bwd: dqkv must be bf16 [n, (Hq+2Hkv)*128]");
+    a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv->data_ptr());
+    a.dqkv_stride = (int)dqkv->stride(0);
+    a.dq_col = 0;
+    a.dk_col = (int)(hq * HD);
+    a.dv_col = (int)((hq + hkv) * HD);
+  }
+  a.bf16_mask = (int)bf16_mask;
+  if (rope_cos.has_value()) {
+    TORCH_CHECK(rope_sin.has_value() && rope_cos->scalar_type() == at::kFloat && rope_sin->scalar_type() == at::kFloat &&
+                    rope_cos->dim() == 2 && rope_cos->size(0) >= n && rope_cos->size(1) == HD / 2 &&
+                    rope_cos->stride(1) == 1 && rope_sin->sizes() == rope_cos->sizes() &&
+                    rope_sin->strides() == rope_cos->strides() && rope_cos->stride(0) % 2 == 0,
+                "attn_bwd: rope cos / sin must be fp32 [>= n, 64]");
+    a.rope_cos = rope_cos->data_ptr<float>();
+    a.rope_sin = rope_sin->data_ptr<float>();
+    a.rope_stride = (int)rope_cos->stride(0);
+  }
   a.d_o = d_o.data_ptr<float>();
   a.do_stride = (int)d_o.stride(0);
   a.stat_stride = (int)lse.size(1);
   a.lse = lse.data_ptr<float>();
   a.dd = dd.data_ptr<float>();
   a.do_bf = reinterpret_cast<__nv_bfloat16*>(do_bf.data_ptr());
-  a.dq = dq.data_ptr<float>();
-  a.dk = dk.data_ptr<float>();
-  a.dv = dv.data_ptr<float>();
+  a.dq = (bf16_mask & 1) ? nullptr : dq->data_ptr<float>();
+  a.dk = (bf16_mask & 2) ? nullptr : dk->data_ptr<float>();
+  a.dv = (bf16_mask & 4) ? nullptr : dv->data_ptr<float>();
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attn_bwd_q_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AB_Q_SMEM);

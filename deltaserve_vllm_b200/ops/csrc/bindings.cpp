@@ -4,7 +4,8 @@
 void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
-              int64_t save_dst, int64_t force_bn, int64_t max_ctas);
+              int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
+              c10::optional<torch::Tensor> aux_out);
 void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> add,
                       torch::Tensor dx, c10::optional<torch::Tensor> dx_bf, double eps);
 void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10::optional<torch::Tensor> act);
@@ -25,8 +26,10 @@ static int64_t dsv_read_error(bool clear) {
   return g != 0 ? g : a;
 }
 void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
-                  torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, torch::Tensor dq, torch::Tensor dk,
-                  torch::Tensor dv, double scale);
+                  torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, c10::optional<torch::Tensor> dq,
+                  c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
+                  c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+                  c10::optional<torch::Tensor> dqkv, int64_t bf16_mask);
 void dsv_attn_fwd_dense(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles, torch::Tensor o,
                         double scale);
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,

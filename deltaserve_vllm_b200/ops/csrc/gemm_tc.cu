@@ -32,7 +32,7 @@ namespace dsv {
 
 
 enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4,
-                      kEpiShrink = 5, kEpiBF16T = 6 };
+                      kEpiShrink = 5, kEpiBF16T = 6, kEpiSwiGLUBwd = 7 };
 
 constexpr int kMaxPeers = 8;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
@@ -76,6 +76,14 @@ struct GemmArgs {
   // Swapped operands (kEpiBF16T, decode): the LoRA slots of every tile are
   // the OR of tile_slots[0, slot_or) (the token tiles), not tile_slots[mt].
   int slot_or;
+  // kEpiSwiGLUBwd: the accumulator is d(act) [M, N]; aux holds the saved
+  // gate/up pre-activations [M, 2N] (64-column interleave), C receives their
+  // gradient [M, 2N] (same interleave), aux_out (optional) the activation
+  // silu(g) * u [M, N].
+  const __nv_bfloat16* aux;
+  int ld_aux;
+  __nv_bfloat16* aux_out;
+  int ld_aux_out;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -618,6 +626,43 @@ __global__ void __launch_bounds__(256, 1)
             for (int zc = PR + j; zc < SEG; zc += PR) zr[sl * SEG + zc] = f2bf(0.f);
           }
         }
+      } else if constexpr (EPI == kEpiSwiGLUBwd) {
+        // 32 d(act) columns at a time, all inside one 64-column block of the
+        // interleave: their gate columns start at (col / 64) * 128 + col % 64,
+        // the up columns 64 further.
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          const int gcol = (col >> 6) * 128 + (col & 63);
+          const uint4* gp = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol);
+          const uint4* up = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol + 64);
+          float dg[32], du[32], act[32];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 gq = gp[v], uq = up[v];
+            const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gq);
+            const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uq);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int i = v * 8 + e;
+              const float g = bf2f(gb[e]), u = bf2f(ub[e]);
+              const float da = __uint_as_float(r[i]);
+              const float sg = 1.f / (1.f + __expf(-g));
+              const float silu = g * sg;
+              dg[i] = da * u * sg * (1.f + g * (1.f - sg));
+              du[i] = da * silu;
+              act[i] = silu * u;
+            }
+          }
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + gcol;
+          store_row_bf16(dst, dg, 32);
+          store_row_bf16(dst + 64, du, 32);
+          if (args.aux_out != nullptr) store_row_bf16(args.aux_out + (size_t)row * args.ld_aux_out + col, act, 32);
+        }
       } else if constexpr (EPI == kEpiSwiGLU) {
         // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
 #pragma unroll 1
@@ -859,7 +904,8 @@ static int pick_bn(int M, int N, int epi, bool b_mn) {
 void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
-              int64_t save_dst, int64_t force_bn, int64_t max_ctas) {
+              int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
+              c10::optional<torch::Tensor> aux_out) {
   using namespace dsv;
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "dsv_gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm: bf16 operands");
@@ -871,6 +917,19 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   TORCH_CHECK(out.stride(-1) == 1, "dsv_gemm: output rows must be contiguous");
   if (M == 0 || N == 0) return;
   if (epi == kEpiSwiGLU) TORCH_CHECK(N % 128 == 0 && out.size(1) * 2 == N, "dsv_gemm: SwiGLU needs N % 128 == 0");
+  if (epi == kEpiSwiGLUBwd) {
+    TORCH_CHECK(b_mn && N % 64 == 0 && out.size(1) == 2 * N && aux.has_value(),
+                "dsv_gemm: SwiGLU backward needs MN-major B, N % 64 == 0, out [M, 2N] and aux");
+    TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(0) >= M && aux->size(1) == 2 * N &&
+                    aux->stride(1) == 1 && aux->stride(0) % 8 == 0 &&
+                    reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 == 0,
+                "dsv_gemm: aux must be bf16 [M, 2N] with 16-byte aligned rows");
+    TORCH_CHECK(out.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+                "dsv_gemm: SwiGLU backward output rows must be 16-byte aligned");
+    if (aux_out.has_value())
+      TORCH_CHECK(aux_out->scalar_type() == at::kBFloat16 && aux_out->size(0) >= M && aux_out->size(1) == N &&
+                      aux_out->stride(1) == 1, "dsv_gemm: aux_out must be bf16 [M, N]");
+  }
   const bool f32_out = (epi == kEpiF32 || epi == kEpiF32Accum);
   TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "dsv_gemm: output dtype");
   TORCH_CHECK(K > 0, "dsv_gemm: empty reduction");
@@ -987,6 +1046,14 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     args.num_slots = (int)(zt.size(1) / lora_seg);
     args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
   }
+  if (epi == kEpiSwiGLUBwd) {
+    args.aux = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr());
+    args.ld_aux = (int)aux->stride(0);
+    if (aux_out.has_value()) {
+      args.aux_out = reinterpret_cast<__nv_bfloat16*>(aux_out->data_ptr());
+      args.ld_aux_out = (int)aux_out->stride(0);
+    }
+  }
   if (save.has_value()) {
     TORCH_CHECK(save->scalar_type() == at::kBFloat16 && save->stride(1) == 1, "dsv_gemm: save buffer");
     args.save = reinterpret_cast<__nv_bfloat16*>(save->data_ptr());
@@ -1000,6 +1067,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     if (epi == kEpiBF16) dispatch_bn<true, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32) dispatch_bn<true, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32Accum) dispatch_bn<true, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiSwiGLUBwd) dispatch_bn<true, kEpiSwiGLUBwd>(bn, ta, tb, tz, tb2, args, s);
     else TORCH_CHECK(false, "dsv_gemm: unsupported epilogue for MN-major B");
   } else {
     if (epi == kEpiBF16) dispatch_bn<false, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);

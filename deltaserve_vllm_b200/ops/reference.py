@@ -13,6 +13,7 @@ import torch
 import torch.nn.functional as F
 
 EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_F32_ACCUM = 0, 1, 2, 3
+EPI_SWIGLU_BWD = 7  # MN-major only: SwiGLU backward over saved interleaved gate/up
 
 
 def deinterleave64(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -30,7 +31,7 @@ def interleave64(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
 
 
 def gemm(a, b, out, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0,
-         save=None, save_lo=0, save_hi=0, save_dst=0):
+         save=None, save_lo=0, save_hi=0, save_dst=0, aux=None, aux_out=None):
     acc = a.float() @ (b.float() if b_mn else b.float().t())
     if lora_seg and z is not None:  # b_mn: b2 is [S*SEG, N] like b; else [N, S*SEG]
         acc = acc + z[: a.shape[0]].float() @ (b2.float() if b_mn else b2.float().t())
@@ -39,6 +40,8 @@ def gemm(a, b, out, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None, 
     if epi == EPI_SWIGLU:
         g, u = deinterleave64(acc)
         out.copy_((F.silu(g) * u).to(out.dtype))
+    elif epi == EPI_SWIGLU_BWD:
+        swiglu_bwd(aux[: a.shape[0]], acc, out, aux_out)
     elif epi == EPI_F32_ACCUM:
         out.add_(acc)
     else:
@@ -289,3 +292,11 @@ def dense_attn_bwd(q, k, v, d_o, tiles, scale, dq, dk, dv):
         dkk = torch.einsum("hqk,qhd->khd", ds, q[sl].float()) * scale
         dk[sl] = dkk.view(ln, hkv, G, hd).sum(2)
         dv[sl] = dvv.view(ln, hkv, G, hd).sum(2)
+
+
+def rope_bwd(g: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Transpose of the NeoX rotate-half RoPE on g [n, H, d] (cos / sin [n, d/2])."""
+    h = g.shape[-1] // 2
+    g1, g2 = g[..., :h], g[..., h:]
+    c, s = cos[:, None, :].float(), sin[:, None, :].float()
+    return torch.cat([g1 * c + g2 * s, g2 * c - g1 * s], dim=-1)

@@ -198,6 +198,62 @@ def test_attn_bwd_varlen_gqa(Hq, Hkv):
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
 
 
+@pytest.mark.parametrize("mask", [7, 4])
+def test_attn_bwd_rope_epilogue_into_dqkv(mask):
+    """RoPE backward + bf16 stores into the fused d(qkv) rows (the trainer's
+    call) == the fp32 kernel outputs rotated back by the reference."""
+    Hq, Hkv = 8, 2
+    lens = [5, 64, 130, 77]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=35)
+    g = torch.Generator(device=DEV).manual_seed(36)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV)
+    pos = torch.cat([torch.arange(ln) for ln in lens] + [torch.zeros(n - sum(lens), dtype=torch.long)]).to(DEV)
+    from deltaserve_vllm_b200.models.rope import cos_sin
+    cos, sin = cos_sin(pos, 128, 500000.0)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV)
+    scale = 1 / math.sqrt(128)
+    dq0, dk0, dv0 = ops.attn_bwd(q, k, v, d_o, tiles, scale)
+    dqkv = torch.full((n, (Hq + 2 * Hkv) * 128), 7.0, dtype=torch.bfloat16, device=DEV)
+    dq, dk, dv = ops.attn_bwd(q, k, v, d_o, tiles, scale, rope=(cos, sin), dqkv=dqkv, bf16_mask=mask)
+    eq, ek = ref.rope_bwd(dq0.cpu(), cos.cpu(), sin.cpu()), ref.rope_bwd(dk0.cpu(), cos.cpu(), sin.cpu())
+    used = sum(lens)
+    ql, kl = Hq * 128, Hkv * 128
+    torch.testing.assert_close(dqkv[:used, ql + kl:].float().cpu(), dv0[:used].reshape(used, kl).cpu(),
+                               rtol=1e-2, atol=1e-2)
+    if mask == 7:
+        assert dq is None and dk is None and dv is None
+        torch.testing.assert_close(dqkv[:used, :ql].float().cpu(), eq[:used].reshape(used, ql), rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(dqkv[:used, ql:ql + kl].float().cpu(), ek[:used].reshape(used, kl),
+                                   rtol=1e-2, atol=1e-2)
+    else:
+        torch.testing.assert_close(dq.cpu(), eq, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(dk.cpu(), ek, rtol=1e-5, atol=1e-5)
+        assert (dqkv[:, :ql + kl] == 7.0).all()          # untouched
+    assert (dqkv[used:] == 7.0).all()                       # rows past the samples untouched
+
+
+def test_gemm_swiglu_bwd_epilogue():
+    """d(act) GEMM (MN-major, with the LoRA K block) whose epilogue applies the
+    SwiGLU backward == fp32 product then the SwiGLU backward reference."""
+    M, K, I = 300, 512, 640
+    a = rnd(M, K, seed=40)
+    w = rnd(K, I, scale=0.05, seed=41)
+    gu = rnd(M, 2 * I, seed=42)
+    z = rnd(M, 64, seed=43)
+    b2 = rnd(64, I, scale=0.05, seed=44)
+    ts = torch.ones((M + 127) // 128, dtype=torch.int32, device=DEV)
+    out = torch.empty(M, 2 * I, dtype=torch.bfloat16, device=DEV)
+    act = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(a, w, out, b_mn=True, epi=ops.EPI_SWIGLU_BWD, z=z, b2=b2, tile_slots=ts, lora_seg=64,
+             aux=gu, aux_out=act)
+    exp = torch.empty(M, 2 * I)
+    eact = torch.empty(M, I)
+    ref.gemm(a.cpu(), w.cpu(), exp, True, ops.EPI_SWIGLU_BWD, z.cpu(), b2.cpu(), ts.cpu(), 64,
+             aux=gu.cpu(), aux_out=eact)
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(act.float().cpu(), eact, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("Hq,Hkv", [(8, 2), (32, 8)])
 def test_attn_fwd_dense(Hq, Hkv):
     lens = [3, 64, 129, 500]

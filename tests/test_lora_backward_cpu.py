@@ -70,3 +70,27 @@ def test_dense_attention_reference_matches_autograd():
     o = ops.attn_fwd_dense(q.detach().float(), k.detach().float(), v.detach().float(), tiles, scale,
                            torch.zeros(n, Hq * hd))
     torch.testing.assert_close(o.double().view(n, Hq, hd), out.detach(), rtol=1e-4, atol=1e-5)
+
+
+def test_attn_bwd_wrapper_rope_and_dqkv_cpu():
+    """The CPU path of ops.attn_bwd with RoPE and bf16 d(qkv) outputs equals
+    the plain fp32 outputs rotated back, written into the fused rows."""
+    import math
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.models.rope import cos_sin, rope_backward
+    torch.manual_seed(1)
+    lens, Hq, Hkv, hd = [9, 30], 4, 2, 128
+    n = 40
+    starts = [0, 9]
+    q, k, v = torch.randn(n, Hq, hd), torch.randn(n, Hkv, hd), torch.randn(n, Hkv, hd)
+    d_o = torch.randn(n, Hq * hd)
+    tiles = ops.dense_attn_tiles(starts, lens, "cpu")
+    cos, sin = cos_sin(torch.arange(n), hd, 10000.0)
+    dq, dk, dv = ops.attn_bwd(q, k, v, d_o, tiles, 1 / math.sqrt(hd))
+    dqkv = torch.full((n, (Hq + 2 * Hkv) * hd), 5.0)
+    out = ops.attn_bwd(q, k, v, d_o, tiles, 1 / math.sqrt(hd), rope=(cos, sin), dqkv=dqkv, bf16_mask=6)
+    torch.testing.assert_close(out[0], rope_backward(dq, cos, sin))
+    assert out[1] is None and out[2] is None
+    torch.testing.assert_close(dqkv[:39, Hq * hd:(Hq + Hkv) * hd], rope_backward(dk, cos, sin)[:39].reshape(39, -1))
+    torch.testing.assert_close(dqkv[:39, (Hq + Hkv) * hd:], dv[:39].reshape(39, -1))
+    assert (dqkv[39:] == 5.0).all() and (dqkv[:, :Hq * hd] == 5.0).all()
