@@ -219,7 +219,119 @@ void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::T
 namespace dsv {
 
 // dx = rmsnorm_backward(x, dy) [+ add]; fp32 out, optional bf16 copy.
-// One CTA per row; x bf16, dy fp32 or bf16 (dy_bf16 != nullptr), w bf16.
+// x bf16 (row stride sx), dy / add / dx fp32 [T, D], w bf16 [D].
+// d/dx of x * inv * w = inv * (g - xhat * mean(g * xhat)), g = dy * w.
+//
+// Wide rows: one CTA of 256 threads per row, NCH chunks of 8 consecutive
+// elements per thread held in registers between the reduction and the store
+// (16-byte loads and stores).
+template <int NCH>
+__global__ void __launch_bounds__(256) rms_norm_bwd_vec_kernel(const __nv_bfloat16* __restrict__ x, int sx,
+                                                               const float* __restrict__ dy,
+                                                               const __nv_bfloat16* __restrict__ w,
+                                                               const float* __restrict__ add, float* dx,
+                                                               __nv_bfloat16* dx_bf, int D, float eps) {
+  __shared__ float2 red[8];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + (size_t)row * sx;
+  const float* dyr = dy + (size_t)row * D;
+  float xv[NCH][8], gv[NCH][8];
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int i = (threadIdx.x + k * 256) * 8;
+    if (i < D) {
+      const uint4 xq = *reinterpret_cast<const uint4*>(xr + i);
+      const uint4 wq = *reinterpret_cast<const uint4*>(w + i);
+      const float4 d0 = *reinterpret_cast<const float4*>(dyr + i);
+      const float4 d1 = *reinterpret_cast<const float4*>(dyr + i + 4);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xq);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wq);
+      const float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        xv[k][e] = bf2f(xb[e]);
+        gv[k][e] = d[e] * bf2f(wb[e]);
+        ss += xv[k][e] * xv[k][e];
+        dot += gv[k][e] * xv[k][e];
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(ss, dot);
+  __syncthreads();
+  float2 t = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    t.x += red[i].x;
+    t.y += red[i].y;
+  }
+  const float inv = rsqrtf(t.x / D + eps);
+  const float c = t.y * inv * inv / D;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int i = (threadIdx.x + k * 256) * 8;
+    if (i >= D) continue;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = inv * (gv[k][e] - xv[k][e] * c);
+    if (add != nullptr) {
+      const float4 a0 = *reinterpret_cast<const float4*>(add + (size_t)row * D + i);
+      const float4 a1 = *reinterpret_cast<const float4*>(add + (size_t)row * D + i + 4);
+      v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+      v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+    }
+    float4* o = reinterpret_cast<float4*>(dx + (size_t)row * D + i);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (dx_bf != nullptr) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+        pk[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(dx_bf + (size_t)row * D + i) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+}
+
+// Narrow rows (per-head q/k norms, D <= 256): one warp per row, D / 32
+// consecutive elements per lane.
+template <int PER>
+__global__ void __launch_bounds__(256) rms_norm_bwd_warp_kernel(const __nv_bfloat16* __restrict__ x, int sx,
+                                                                const float* __restrict__ dy,
+                                                                const __nv_bfloat16* __restrict__ w,
+                                                                const float* __restrict__ add, float* dx,
+                                                                __nv_bfloat16* dx_bf, int T, int D, float eps) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int lane = threadIdx.x & 31;
+  const int i0 = lane * PER;
+  float xv[PER], gv[PER];
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    xv[e] = bf2f(x[(size_t)row * sx + i0 + e]);
+    gv[e] = dy[(size_t)row * D + i0 + e] * bf2f(w[i0 + e]);
+    ss += xv[e] * xv[e];
+    dot += gv[e] * xv[e];
+  }
+  ss = warp_sum(ss);
+  dot = warp_sum(dot);
+  const float inv = rsqrtf(ss / D + eps);
+  const float c = dot * inv * inv / D;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    float v = inv * (gv[e] - xv[e] * c);
+    if (add != nullptr) v += add[(size_t)row * D + i0 + e];
+    dx[(size_t)row * D + i0 + e] = v;
+    if (dx_bf != nullptr) dx_bf[(size_t)row * D + i0 + e] = f2bf(v);
+  }
+}
+
+// General fallback (any D): one CTA per row, scalar loads.
 __global__ void rms_norm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int sx, const float* __restrict__ dy,
                                     const __nv_bfloat16* __restrict__ w, const float* __restrict__ add,
                                     float* dx, __nv_bfloat16* dx_bf, int D, float eps) {
@@ -248,8 +360,7 @@ __global__ void rms_norm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int sx,
   ss = bsum(ss);
   dot = bsum(dot);
   const float inv = rsqrtf(ss / D + eps);
-  // d/dx of x*inv*w : inv * (g - xhat * mean(g * xhat)), g = dy*w, xhat = x*inv
-  const float c = dot * inv * inv / D;  // = mean(g*xhat) * inv / ... folded
+  const float c = dot * inv * inv / D;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     const float xv = bf2f(xr[i]);
     float v = inv * (dyr[i] * bf2f(w[i]) - xv * c);
@@ -261,22 +372,48 @@ __global__ void rms_norm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int sx,
 
 // SwiGLU backward over 64-interleaved gate/up: from the saved pre-activation
 // gu (bf16) and d_act (fp32) produce d_gu (bf16, same interleave) and the
-// activation silu(g)*u (bf16, the down projection's input).
+// activation silu(g)*u (bf16, the down projection's input). One thread per 8
+// consecutive d_act columns (inside one 64-column block): 16-byte loads and
+// stores throughout.
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, int sgu, const float* __restrict__ dact,
-                                  __nv_bfloat16* dgu, __nv_bfloat16* act, int I, int64_t total) {
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+                                  __nv_bfloat16* dgu, __nv_bfloat16* act, int I, int64_t total8) {
+  const int per_row = I / 8;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total8;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = idx / I;
-    const int j = (int)(idx % I);
+    const int64_t row = idx / per_row;
+    const int j = (int)(idx % per_row) * 8;
     const int col_g = (j / 64) * 128 + (j % 64);
-    const float g = bf2f(gu[row * sgu + col_g]);
-    const float u = bf2f(gu[row * sgu + col_g + 64]);
-    const float sg = 1.f / (1.f + __expf(-g));
-    const float silu = g * sg;
-    const float da = dact[row * I + j];
-    dgu[row * (2 * (int64_t)I) + col_g] = f2bf(da * u * sg * (1.f + g * (1.f - sg)));
-    dgu[row * (2 * (int64_t)I) + col_g + 64] = f2bf(da * silu);
-    if (act != nullptr) act[row * I + j] = f2bf(silu * u);
+    const uint4 gq = *reinterpret_cast<const uint4*>(gu + row * sgu + col_g);
+    const uint4 uq = *reinterpret_cast<const uint4*>(gu + row * sgu + col_g + 64);
+    const float4 d0 = *reinterpret_cast<const float4*>(dact + row * I + j);
+    const float4 d1 = *reinterpret_cast<const float4*>(dact + row * I + j + 4);
+    const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gq);
+    const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uq);
+    const float da[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    uint32_t og[4], ou[4], oa[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float rg[2], ru[2], ra[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const float g = bf2f(gb[e + t]), u = bf2f(ub[e + t]);
+        const float sg = 1.f / (1.f + __expf(-g));
+        const float silu = g * sg;
+        rg[t] = da[e + t] * u * sg * (1.f + g * (1.f - sg));
+        ru[t] = da[e + t] * silu;
+        ra[t] = silu * u;
+      }
+      __nv_bfloat162 hg = __floats2bfloat162_rn(rg[0], rg[1]);
+      __nv_bfloat162 hu = __floats2bfloat162_rn(ru[0], ru[1]);
+      __nv_bfloat162 ha = __floats2bfloat162_rn(ra[0], ra[1]);
+      og[e / 2] = *reinterpret_cast<uint32_t*>(&hg);
+      ou[e / 2] = *reinterpret_cast<uint32_t*>(&hu);
+      oa[e / 2] = *reinterpret_cast<uint32_t*>(&ha);
+    }
+    __nv_bfloat16* drow = dgu + row * (2 * (int64_t)I);
+    *reinterpret_cast<uint4*>(drow + col_g) = make_uint4(og[0], og[1], og[2], og[3]);
+    *reinterpret_cast<uint4*>(drow + col_g + 64) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+    if (act != nullptr) *reinterpret_cast<uint4*>(act + row * I + j) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
   }
 }
 
@@ -288,12 +425,39 @@ void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::o
   if (T == 0) return;
   TORCH_CHECK(dy.scalar_type() == at::kFloat && dx.scalar_type() == at::kFloat && dy.is_contiguous() &&
                   dx.is_contiguous(), "rms_norm_bwd: fp32 contiguous dy/dx");
+  if (add.has_value())
+    TORCH_CHECK(add->scalar_type() == at::kFloat && add->is_contiguous() && add->numel() == (int64_t)T * D,
+                "rms_norm_bwd: add must be fp32 [T, D]");
+  if (dx_bf.has_value())
+    TORCH_CHECK(dx_bf->scalar_type() == at::kBFloat16 && dx_bf->is_contiguous() && dx_bf->numel() == (int64_t)T * D,
+                "rms_norm_bwd: bf16 copy must be contiguous [T, D]");
   c10::cuda::CUDAGuard guard(x.device());
-  dsv::rms_norm_bwd_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0), dy.data_ptr<float>(),
-      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), add.has_value() ? add->data_ptr<float>() : nullptr,
-      dx.data_ptr<float>(), dx_bf.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf->data_ptr()) : nullptr, D,
-      (float)eps);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  const auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  const float* ap = add.has_value() ? add->data_ptr<float>() : nullptr;
+  auto* bp = dx_bf.has_value() ? reinterpret_cast<__nv_bfloat16*>(dx_bf->data_ptr()) : nullptr;
+  const int sx = (int)x.stride(0);
+  auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool vec_ok = D % 8 == 0 && sx % 8 == 0 && al16(xp) && al16(wp) && al16(dy.data_ptr()) &&
+                      al16(dx.data_ptr()) && (ap == nullptr || al16(ap)) && (bp == nullptr || al16(bp));
+  if (vec_ok && D >= 512 && D <= 8192) {
+    const int nch = (D + 2047) / 2048;
+    if (nch == 1) dsv::rms_norm_bwd_vec_kernel<1><<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+    else if (nch == 2) dsv::rms_norm_bwd_vec_kernel<2><<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+    else if (nch == 3) dsv::rms_norm_bwd_vec_kernel<3><<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+    else dsv::rms_norm_bwd_vec_kernel<4><<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+  } else if (D % 32 == 0 && D <= 256) {
+    const int per = D / 32;
+    const int blocks = (T + 7) / 8;
+    if (per == 1) dsv::rms_norm_bwd_warp_kernel<1><<<blocks, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, T, D, (float)eps);
+    else if (per == 2) dsv::rms_norm_bwd_warp_kernel<2><<<blocks, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, T, D, (float)eps);
+    else if (per == 4) dsv::rms_norm_bwd_warp_kernel<4><<<blocks, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, T, D, (float)eps);
+    else if (per == 8) dsv::rms_norm_bwd_warp_kernel<8><<<blocks, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, T, D, (float)eps);
+    else dsv::rms_norm_bwd_kernel<<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+  } else {
+    dsv::rms_norm_bwd_kernel<<<T, 256, 0, st>>>(xp, sx, dy.data_ptr<float>(), wp, ap, dx.data_ptr<float>(), bp, D, (float)eps);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -302,9 +466,16 @@ void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10
   const int I = (int)dact.size(1);
   if (T == 0) return;
   TORCH_CHECK(I % 64 == 0 && gu.size(1) == 2 * I && dact.is_contiguous() && dgu.is_contiguous(), "swiglu_bwd");
+  TORCH_CHECK(gu.stride(1) == 1 && gu.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(gu.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(dact.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(dgu.data_ptr()) % 16 == 0,
+              "swiglu_bwd: 16-byte aligned rows");
+  if (act.has_value())
+    TORCH_CHECK(act->is_contiguous() && reinterpret_cast<uintptr_t>(act->data_ptr()) % 16 == 0,
+                "swiglu_bwd: act must be contiguous and 16-byte aligned");
   c10::cuda::CUDAGuard guard(gu.device());
-  const int64_t total = T * I;
-  const int blocks = (int)std::min<int64_t>(8192, (total + 255) / 256);
+  const int64_t total = T * I / 8;
+  const int blocks = (int)std::min<int64_t>(148 * 16, (total + 255) / 256);
   dsv::swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), (int)gu.stride(0), dact.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()),

@@ -162,6 +162,40 @@ def _attn_bwd(n_seq, L, Hq=32, Hkv=8, torch_path=False):
     return fn, byts, flops
 
 
+def _dx_gemm(M, K, N, swiglu: bool):
+    """The backward's MN-major dX GEMM (dY [M, K] . W [K, N]); with ``swiglu``
+    the epilogue applies the SwiGLU backward over a saved gate/up [M, 2N]."""
+    a = rnd(M, K, seed=11)
+    b = rnd(K, N, scale=0.02, seed=12)
+    flops = 2 * M * N * K
+    if swiglu:
+        gu = rnd(M, 2 * N, seed=13)
+        out = torch.empty(M, 2 * N, dtype=torch.bfloat16, device=DEV)
+        byts = 2 * (M * K + K * N) + 2 * 2 * M * 2 * N
+        return (lambda: ops.gemm(a, b, out, b_mn=True, epi=ops.EPI_SWIGLU_BWD, aux=gu), byts, flops)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    byts = 2 * (M * K + K * N) + 4 * M * N
+    return (lambda: ops.gemm(a, b, out, b_mn=True, epi=ops.EPI_F32), byts, flops)
+
+
+def _swiglu_bwd(T, I):
+    gu = rnd(T, 2 * I, seed=14)
+    dact = rnd(T, I, dtype=torch.float32, seed=15)
+    dgu = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=DEV)
+    return (lambda: ops.swiglu_bwd(gu, dact, dgu), T * I * (2 * 2 + 4 + 2 * 2), 0)
+
+
+def _rms_bwd(T, D):
+    x = rnd(T, D, seed=16)
+    w = rnd(D, seed=17)
+    dy = rnd(T, D, dtype=torch.float32, seed=18)
+    add = rnd(T, D, dtype=torch.float32, seed=19)
+    out = torch.empty(T, D, device=DEV)
+    obf = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    return (lambda: ops.rms_norm_bwd(x, dy, w, 1e-5, add=add, out=out, out_bf16=obf),
+            T * D * (2 + 4 + 4 + 4 + 2), 0)
+
+
 def _adamw(n):
     p, g = rnd(n, dtype=torch.float32, seed=1), rnd(n, dtype=torch.float32, seed=2)
     m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
@@ -222,6 +256,13 @@ CASES = {
     "attn_decode_64x1024": lambda: _decode(64, 1024),
     "attn_decode_16x4096": lambda: _decode(16, 4096),
     "rms_norm_add_8192x4096": lambda: _rms(8192, 4096),
+    "rms_norm_bwd_4096x4096": lambda: _rms_bwd(4096, 4096),
+    "rms_norm_bwd_qknorm_131072x128": lambda: _rms_bwd(131072, 128),
+    # backward dX of the down projection (Llama-3-8B, 4096 FT tokens): plain
+    # fp32 store, and with the SwiGLU backward fused in the epilogue
+    "gemm_dx_down_f32": lambda: _dx_gemm(4096, 4096, 14336, False),
+    "gemm_dx_down_swiglu_bwd": lambda: _dx_gemm(4096, 4096, 14336, True),
+    "swiglu_bwd_4096x14336": lambda: _swiglu_bwd(4096, 14336),
     "lora_shrink_4096x4096_r16x3": lambda: _shrink(4096, 4096, 48),
     "rope_kvwrite_4096": lambda: _rope(4096),
     "ce_fwd_bwd_512x128256": lambda: _ce(512, 128256),

@@ -379,8 +379,9 @@ def test_gemm_splitk_swiglu_lora_save(M):
     torch.testing.assert_close(save[:M - 1].float(), acc[1:M], rtol=2e-2, atol=3e-2)
 
 
-def test_rms_norm_bwd_and_swiglu_bwd():
-    T, D = 50, 4096
+@pytest.mark.parametrize("T,D", [(50, 4096), (9, 5120), (7, 1024), (33, 8192), (301, 128), (5, 96), (3, 200)])
+def test_rms_norm_bwd_shapes(T, D):
+    """Vector (one CTA per row), warp-per-row (q/k norms) and scalar paths."""
     x = rnd(T, D, seed=37)
     dy = rnd(T, D, dtype=torch.float32, seed=38)
     w = rnd(D, scale=0.1, seed=39) + 1
@@ -390,6 +391,13 @@ def test_rms_norm_bwd_and_swiglu_bwd():
     exp = ref.rms_norm_bwd(x.cpu(), dy.cpu(), w.cpu(), 1e-5, add.cpu())
     torch.testing.assert_close(out.cpu(), exp, rtol=1e-4, atol=1e-4)
     torch.testing.assert_close(bf.float().cpu(), exp, rtol=1e-2, atol=1e-2)
+    out2 = ops.rms_norm_bwd(x, dy, w, 1e-5)
+    torch.testing.assert_close(out2.cpu(), ref.rms_norm_bwd(x.cpu(), dy.cpu(), w.cpu(), 1e-5, None),
+                               rtol=1e-4, atol=1e-4)
+
+
+def test_rms_norm_bwd_and_swiglu_bwd():
+    T = 50
     I = 1792
     gu = rnd(T, 2 * I, seed=41)
     dact = rnd(T, I, dtype=torch.float32, seed=42)
