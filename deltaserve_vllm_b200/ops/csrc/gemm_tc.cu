@@ -995,14 +995,18 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
   if (b_mn && bn < 64) bn = 64;
   if (epi == kEpiSwiGLU && bn < 128) bn = 128;
-  // Split-K for skinny problems (decode: one M tile) that would leave most SMs
-  // idle: each split streams a slice of K, fp32 partials are reduced after.
+  // Split-K for problems with too few output tiles to fill the GPU (decode:
+  // one M tile; the trainer's rank-sized LoRA products: one skinny side):
+  // each split streams a slice of K, fp32 partials are reduced after in a
+  // fixed order (deterministic). Not with a real grid cap or the SwiGLU
+  // backward epilogue (its product is never materialised).
   int splits = 1;
   {
     const int kbs = (K + BK - 1) / BK;
     const int m_t = (M + BM - 1) / BM;
-    if (!b_mn && m_t == 1 && max_ctas == 0) {
-      if (force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
+    const bool uncapped = max_ctas == 0 || max_ctas >= num_sms();
+    if (!b_mn && m_t == 1 && max_ctas == 0 && force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
+    if (uncapped && epi != kEpiSwiGLUBwd) {
       const int tiles = m_t * ((N + bn - 1) / bn);
       if (tiles < num_sms() / 2 && kbs >= 8) {
         splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));

@@ -48,6 +48,30 @@ def test_gemm_mn_major_f32(M, N, K):
     torch.testing.assert_close(acc, 1 + a.float() @ w.float(), rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("M,N,K,b_mn", [(48, 4096, 4096, True), (48, 28672, 4096, True), (4096, 48, 4096, True),
+                                        (4096, 48, 14336, False), (16, 1024, 8192, True), (2048, 64, 2048, False)])
+@pytest.mark.parametrize("epi", [1, 3, 0])
+def test_gemm_skinny_splitk(M, N, K, b_mn, epi):
+    """The trainer's rank-sized LoRA products (one side <= 64): split-K with a
+    deterministic fp32 reduction, for MN-major and K-major B, with the grid
+    uncapped as the backward launches it."""
+    a = rnd(M, K, seed=50)
+    b = rnd(K, N, scale=0.05, seed=51) if b_mn else rnd(N, K, scale=0.05, seed=51)
+    exp = a.float() @ (b.float() if b_mn else b.float().t())
+    if epi == 0:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    else:
+        out = torch.full((M, N), 0.5 if epi == 3 else 0.0, device=DEV)
+    ops.gemm(a, b, out, b_mn=b_mn, epi=epi, max_ctas=1 << 30)
+    if epi == 3:
+        exp = exp + 0.5
+    torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+    out2 = out.clone() if epi != 3 else None
+    if out2 is not None:
+        ops.gemm(a, b, out2, b_mn=b_mn, epi=epi, max_ctas=1 << 30)
+        assert torch.equal(out, out2)
+
+
 @pytest.mark.parametrize("M", [5, 130, 600])
 def test_gemm_swiglu_save(M):
     K, I = 512, 768
