@@ -23,6 +23,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -391,6 +392,70 @@ __device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, 
   }
 }
 
+// Epilogue of one tile row for the plain store kinds (bf16 / fp32 /
+// fp32-accumulate, or SwiGLU over 64-interleaved gate/up columns), plus the
+// optional raw-row capture: this thread's TMEM lane `t_row` holds output row
+// `row`, columns n0 .. n0 + BN. Shared by the 1-CTA and 2-CTA kernels.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_rows(const GemmArgs& args, uint32_t t_row, int row, bool row_ok, int n0,
+                                              bool do_save) {
+  if constexpr (EPI == kEpiSwiGLU) {
+    // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 128) {
+#pragma unroll 1
+      for (int h = 0; h < 64; h += 32) {
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(t_row + c + h, g);
+        tmem_ld_32x32b_x32(t_row + c + 64 + h, u);
+        tmem_ld_wait();
+        float o[32], gf[32], uf[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          gf[i] = __uint_as_float(g[i]);
+          uf[i] = __uint_as_float(u[i]);
+          float sg = gf[i] / (1.0f + __expf(-gf[i]));
+          o[i] = sg * uf[i];
+        }
+        const int gcol = n0 + c;  // first gate column of this 128 block
+        if (row_ok && gcol < args.N) {
+          const int ocol = gcol / 2 + h;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + ocol;
+          store_row_bf16(dst, o, min(32, args.N / 2 - ocol));
+          if (do_save) {
+            __nv_bfloat16* sv = args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save;
+            store_row_bf16(sv + gcol + h, gf, min(32, args.N - (gcol + h)));
+            store_row_bf16(sv + gcol + 64 + h, uf, min(32, args.N - (gcol + 64 + h)));
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      const int col = n0 + c;
+      if (row_ok && col < args.N) {
+        const int nv = min(32, args.N - col);
+        if constexpr (EPI == kEpiBF16) {
+          store_row_bf16(reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col, v, nv);
+        } else {
+          store_row_f32(reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col, v, nv,
+                        EPI == kEpiF32Accum);
+        }
+        if (do_save) {
+          store_row_bf16(args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save + col, v, nv);
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(256, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -663,60 +728,8 @@ __global__ void __launch_bounds__(256, 1)
           store_row_bf16(dst + 64, du, 32);
           if (args.aux_out != nullptr) store_row_bf16(args.aux_out + (size_t)row * args.ld_aux_out + col, act, 32);
         }
-      } else if constexpr (EPI == kEpiSwiGLU) {
-        // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 128) {
-#pragma unroll 1
-          for (int h = 0; h < 64; h += 32) {
-            uint32_t g[32], u[32];
-            tmem_ld_32x32b_x32(t_row + c + h, g);
-            tmem_ld_32x32b_x32(t_row + c + 64 + h, u);
-            tmem_ld_wait();
-            float o[32], gf[32], uf[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              gf[i] = __uint_as_float(g[i]);
-              uf[i] = __uint_as_float(u[i]);
-              float sg = gf[i] / (1.0f + __expf(-gf[i]));
-              o[i] = sg * uf[i];
-            }
-            const int gcol = n0 + c;  // first gate column of this 128 block
-            if (row_ok && gcol < args.N) {
-              const int ocol = gcol / 2 + h;
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + ocol;
-              store_row_bf16(dst, o, min(32, args.N / 2 - ocol));
-              if (do_save) {
-                __nv_bfloat16* sv = args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save;
-                store_row_bf16(sv + gcol + h, gf, min(32, args.N - (gcol + h)));
-                store_row_bf16(sv + gcol + 64 + h, uf, min(32, args.N - (gcol + 64 + h)));
-              }
-            }
-          }
-        }
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c, r);
-          tmem_ld_wait();
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          const int col = n0 + c;
-          if (row_ok && col < args.N) {
-            const int nv = min(32, args.N - col);
-            if constexpr (EPI == kEpiBF16) {
-              store_row_bf16(reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col, v, nv);
-            } else {
-              store_row_f32(reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col, v, nv,
-                            EPI == kEpiF32Accum);
-            }
-            if (do_save) {
-              store_row_bf16(args.save + (size_t)(row - args.save_lo + args.save_dst) * args.ld_save + col, v, nv);
-            }
-          }
-        }
+        epilogue_rows<BN, EPI>(args, t_row, row, row_ok, n0, do_save);
       }
       tc_fence_before();
       __syncwarp();
@@ -732,6 +745,221 @@ __global__ void __launch_bounds__(256, 1)
     // broadcast the owned tiles themselves once their own tiles are pushed.
     if (args.peer.reducers == 0) peer_reducer<BN>(args, num_m_tiles, num_n_tiles, cta0, ncta, smem);
   }
+}
+
+// ---------------------------------------------------------------- CTA-pair GEMM
+// Same pipeline as gemm_tc_kernel, on a cluster of two CTAs sharing one
+// 256 x BN tile through the pair MMA (tcgen05 cta_group::2): CTA r stages
+// rows [r*128, r*128+128) of the A tile and columns [r*BN/2, (r+1)*BN/2) of
+// the B tile; the even CTA's MMA thread issues the M=256 MMAs, each CTA's
+// TMEM receives its own 128 accumulator rows and its epilogue stores them.
+// Per SM, shared-memory traffic per MMA drops from A+B to A+B/2, which is
+// what limits the single-CTA 128 x 256 tile.
+//
+// Barriers: the even CTA's full[s] counts the bytes of both CTAs' TMA loads
+// (each load signals it through its shared::cluster address); the MMA
+// commit releases empty[s] in both CTAs and signals both CTAs' accf[a];
+// both CTAs' epilogue warps arrive on the even CTA's acce[a] (count 8).
+// Every wait is bounded; every thread reaches the final cluster barrier.
+template <int BN, bool B_MN>
+struct GemmCfgPair {
+  static constexpr int A_BYTES = BM * BK * 2;          // this CTA's 128 rows
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // this CTA's BN/2 columns
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN >= 256) ? 6 : 8;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmB2,
+                        GemmArgs args) {
+  static_assert(EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiF32Accum || EPI == kEpiSwiGLU,
+                "pair GEMM: plain store epilogues only");
+  using Cfg = GemmCfgPair<BN, B_MN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accf_bar = empty_bar + STAGES;  // [2]
+  uint64_t* acce_bar = accf_bar + 2;        // [2] (used in the even CTA)
+  uint64_t* drain_bar = acce_bar + 2;       // [1]
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();  // 0 = MMA-issuing CTA
+  const int num_m128 = (args.M + BM - 1) / BM;
+  const int num_m_tiles = (args.M + 2 * BM - 1) / (2 * BM);
+  const int num_n_tiles = (args.N + BN - 1) / BN;
+  const int num_tiles = num_m_tiles * num_n_tiles;
+  const int kb_main = (args.K + BK - 1) / BK;
+  const int kb_per_slot = args.lora_seg / BK;
+  const int pair0 = blockIdx.x / 2, npairs = gridDim.x / 2;
+  // LoRA slots of a 256-row tile: both of its 128-row halves.
+  auto tile_slots_of = [&](int mt) -> uint32_t {
+    if (args.lora_seg <= 0) return 0u;
+    uint32_t m = args.tile_slots[2 * mt];
+    if (2 * mt + 1 < num_m128) m |= args.tile_slots[2 * mt + 1];
+    return m;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 8);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init_cluster();
+  }
+  if (warp == 2) tmem_alloc_pair(tmem_base_smem, Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (args.lora_seg > 0) {
+      tma_prefetch_desc(&tmZ);
+      tma_prefetch_desc(&tmB2);
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int fills[STAGES];
+    for (int s = 0; s < STAGES; ++s) fills[s] = 0;
+    for (int t = pair0; t < num_tiles && ok; t += npairs) {
+      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
+      const int m0 = mt * 2 * BM + (int)rank * BM;
+      const int nb0 = nt * BN + (int)rank * (BN / 2);
+      const uint32_t slots = tile_slots_of(mt);
+      const int n_lora = __popc(slots) * kb_per_slot;
+      for (int j = 0; j < kb_main + n_lora; ++j) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
+        uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
+        uint8_t* sB = sA + Cfg::A_BYTES;
+        if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+        const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+        if (j < kb_main) {
+          const int k0 = j * BK;
+          tma_load_2d_pair(sA, &tmA, bar, k0, m0);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(sB + c * (64 * BK * 2), &tmB, bar, nb0 + c * 64, k0);
+          } else {
+            tma_load_2d_pair(sB, &tmB, bar, k0, nb0);
+          }
+        } else {
+          int lb = j - kb_main;
+          int which = lb / kb_per_slot, sub = lb % kb_per_slot;
+          uint32_t m = slots;
+          for (int i = 0; i < which; ++i) m &= m - 1;
+          const int slot = __ffs(m) - 1;
+          const int k0 = slot * args.lora_seg + sub * BK;
+          tma_load_2d_pair(sA, &tmZ, bar, k0, m0);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 128; ++c) tma_load_2d_pair(sB + c * (64 * BK * 2), &tmB2, bar, nb0 + c * 64, k0);
+          } else {
+            tma_load_2d_pair(sB, &tmB2, bar, k0, nb0);
+          }
+        }
+        fills[stage]++;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // Drain (even CTA): its full barriers count both CTAs' copies, so once
+    // they completed no copy of either CTA is in flight.
+    if (rank == 0) {
+      for (int s = 0; s < STAGES; ++s) {
+        if (fills[s] == 0) continue;
+        uint32_t par = (uint32_t)((fills[s] - 1) & 1);
+        uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[s], par)) {
+          if (globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitFull); break; }
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN, false, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int t = pair0; t < num_tiles && ok; t += npairs, ++iter) {
+      const int mt = t % num_m_tiles;
+      const int n_kb = kb_main + __popc(tile_slots_of(mt)) * kb_per_slot;
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, kErrWaitAccEmpty)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < n_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, kErrWaitFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+        const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t da = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+          const uint64_t db = B_MN ? smem_desc(b_addr + k * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B)
+                                   : smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B);
+          tc_mma_f16_pair(d_tmem, da, db, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        issued = true;
+        tc_commit_pair_mc(&empty_bar[stage], (uint16_t)0x3);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      tc_commit_pair_mc(&accf_bar[acc], (uint16_t)0x3);
+    }
+    // Every pair MMA issued here has finished before either CTA frees TMEM.
+    if (issued) {
+      tc_commit_pair_mc(drain_bar, (uint16_t)0x1);
+      uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitAccFull); break; }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp - 4;
+    const uint32_t acce_leader0 = mapa_shared(smem_u32(&acce_bar[0]), 0);
+    int iter = 0;
+    for (int t = pair0; t < num_tiles; t += npairs, ++iter) {
+      const int mt = t % num_m_tiles, nt = t / num_m_tiles;
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      const bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
+      if (!acc_ok) break;
+      tc_fence_after();
+      const int row = mt * 2 * BM + (int)rank * BM + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      const bool do_save = args.save != nullptr && row_ok && row >= args.save_lo && row < args.save_hi;
+      epilogue_rows<BN, EPI>(args, t_row, row, row_ok, nt * BN, do_save);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still uses it
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
 }
 
 // Split-K epilogue: sum the fp32 partials of every split and apply the
@@ -878,6 +1106,38 @@ static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap
   const int grid = std::min(tiles, args.max_ctas > 0 ? args.max_ctas : num_sms());
   kern<<<grid, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// CTA-pair launch (BN = 256): clusters of two CTAs, one 256 x 256 tile per
+// pair at a time; persistent unless the grid cap asks for one tile per pair.
+template <bool B_MN, int EPI>
+static void launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
+                        const GemmArgs& args, cudaStream_t stream) {
+  using Cfg = GemmCfgPair<256, B_MN>;
+  auto kern = gemm_tc_pair_kernel<256, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    attr_set = true;
+  }
+  const int tiles = ((args.M + 2 * BM - 1) / (2 * BM)) * ((args.N + 255) / 256);
+  const int pairs = std::min(tiles, args.max_ctas > 0 ? std::max(1, args.max_ctas / 2) : num_sms() / 2);
+  kern<<<2 * pairs, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Pair tiles pay off once there are enough of them to occupy the GPU.
+static bool use_pair(int M, int N, int epi, bool b_mn, int bn, int splits, int64_t force_bn, int64_t max_ctas) {
+  static int mode = -1;  // DSV_GEMM_PAIR=0 disables the pair kernel (1-CTA tiles everywhere)
+  if (mode < 0) {
+    const char* e = std::getenv("DSV_GEMM_PAIR");
+    mode = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  if (mode == 0 || splits != 1 || bn != 256 || force_bn != 0) return false;
+  if (!(epi == kEpiBF16 || epi == kEpiF32 || epi == kEpiF32Accum || (epi == kEpiSwiGLU && !b_mn))) return false;
+  if (max_ctas > 0 && max_ctas < num_sms()) return false;
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  return M >= 256 && tiles >= num_sms() / 2;
 }
 
 template <bool B_MN, int EPI>
@@ -1028,9 +1288,11 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   args.C = out.data_ptr();
   args.ldc = (int)out.stride(0);
   args.max_ctas = (int)max_ctas;
+  const bool pair = use_pair(M, N, (int)epi, b_mn, bn, splits, force_bn, max_ctas);
+  const int b_box = pair ? bn / 2 : bn;  // a pair CTA stages half of the B tile
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), BM);
   CUtensorMap tb = b_mn ? make_tmap_bf16(b.data_ptr(), K, N, b.stride(0), BK)
-                        : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
+                        : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), b_box);
   CUtensorMap tz = ta, tb2 = tb;
   if (lora_seg > 0) {
     TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "dsv_gemm: LoRA operands missing");
@@ -1045,7 +1307,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     TORCH_CHECK(tile_slots->scalar_type() == at::kInt && tile_slots->numel() >= (M + BM - 1) / BM, "dsv_gemm: tile_slots");
     tz = make_tmap_bf16(zt.data_ptr(), M, zt.size(1), zt.stride(0), BM);
     tb2 = b_mn ? make_tmap_bf16(bt.data_ptr(), bt.size(0), N, bt.stride(0), BK)
-               : make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), bn);
+               : make_tmap_bf16(bt.data_ptr(), N, bt.size(1), bt.stride(0), b_box);
     args.lora_seg = (int)lora_seg;
     args.num_slots = (int)(zt.size(1) / lora_seg);
     args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
@@ -1067,6 +1329,19 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     args.save_dst = (int)save_dst;
   }
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  if (pair) {
+    if (b_mn) {
+      if (epi == kEpiBF16) launch_pair<true, kEpiBF16>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiF32) launch_pair<true, kEpiF32>(ta, tb, tz, tb2, args, s);
+      else launch_pair<true, kEpiF32Accum>(ta, tb, tz, tb2, args, s);
+    } else {
+      if (epi == kEpiBF16) launch_pair<false, kEpiBF16>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiF32) launch_pair<false, kEpiF32>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiF32Accum) launch_pair<false, kEpiF32Accum>(ta, tb, tz, tb2, args, s);
+      else launch_pair<false, kEpiSwiGLU>(ta, tb, tz, tb2, args, s);
+    }
+    return;
+  }
   if (b_mn) {
     if (epi == kEpiBF16) dispatch_bn<true, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32) dispatch_bn<true, kEpiF32>(bn, ta, tb, tz, tb2, args, s);

@@ -72,6 +72,76 @@ def test_gemm_skinny_splitk(M, N, K, b_mn, epi):
         assert torch.equal(out, out2)
 
 
+# ---------------------------------------------------------------- CTA-pair GEMM
+# Shapes with >= 74 tiles of 256 x 256 take the pair (cta_group::2) kernel;
+# ragged M / N exercise rows and columns past the end in either CTA.
+@pytest.mark.parametrize("M,N,K", [(2000, 4000, 512), (4096, 4096, 1024), (2304, 8192, 256)])
+@pytest.mark.parametrize("max_ctas", [0, 1 << 30])
+def test_gemm_pair_kmajor_bf16(M, N, K, max_ctas):
+    a, b = rnd(M, K, seed=60), rnd(N, K, scale=0.05, seed=61)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(a, b, out, max_ctas=max_ctas)
+    torch.testing.assert_close(out.float(), a.float() @ b.float().t(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("epi", [1, 3])
+def test_gemm_pair_mn_major_f32(epi):
+    M, N, K = 2304, 4096, 1024
+    a, w = rnd(M, K, seed=62), rnd(K, N, scale=0.05, seed=63)
+    out = torch.full((M, N), 0.25, device=DEV)
+    ops.gemm(a, w, out, b_mn=True, epi=epi, max_ctas=1 << 30)
+    exp = a.float() @ w.float() + (0.25 if epi == 3 else 0.0)
+    torch.testing.assert_close(out, exp, rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_pair_swiglu_save():
+    M, K, I = 2048, 512, 4096
+    x, w = rnd(M, K, seed=64), rnd(2 * I, K, scale=0.05, seed=65)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    save = torch.zeros(M, 2 * I, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, epi=ops.EPI_SWIGLU, save=save, save_lo=100, save_hi=1900, save_dst=0)
+    acc = x.float() @ w.float().t()
+    g, u = ref.deinterleave64(acc)
+    torch.testing.assert_close(out.float(), torch.nn.functional.silu(g) * u, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(save[:1800].float(), acc[100:1900], rtol=2e-2, atol=2e-2)
+    assert save[1800:].abs().sum() == 0
+
+
+def test_gemm_pair_lora_expand_mixed_slots():
+    """LoRA K-blocks: the two 128-row halves of a pair tile carry different
+    slots; the pair loads the union."""
+    M, N, K, slots, seg = 2048, 4096, 512, 4, 64
+    x, w = rnd(M, K, seed=66), rnd(N, K, scale=0.05, seed=67)
+    Z = rnd(M, slots * seg, scale=0.5, seed=68)
+    B2 = rnd(N, slots * seg, scale=0.05, seed=69)
+    nt = M // 128
+    mask = torch.tensor([1 << (t % slots) for t in range(nt)], dtype=torch.int32)
+    rows_slot = torch.repeat_interleave(torch.tensor([t % slots for t in range(nt)]), 128)
+    Zm = Z.float().cpu().clone()
+    for s in range(slots):   # a row's Z is zero outside its own slot segment
+        Zm[rows_slot != s, s * seg:(s + 1) * seg] = 0
+    Zm = Zm.to(DEV).to(torch.bfloat16)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, z=Zm, b2=B2, tile_slots=mask.to(DEV), lora_seg=seg)
+    exp = x.float() @ w.float().t() + Zm.float() @ B2.float().t()
+    torch.testing.assert_close(out.float(), exp, rtol=2e-2, atol=3e-2)
+
+
+def test_gemm_pair_mn_major_lora_block():
+    """The backward's dX GEMM: MN-major B plus one 64-deep adapter K-block."""
+    M, Kred, N, PR = 2048, 4096, 4096, 48
+    dy, W = rnd(M, Kred, seed=70), rnd(Kred, N, scale=0.02, seed=71)
+    zp = torch.zeros(M, 64, dtype=torch.bfloat16, device=DEV)
+    zp[:, :PR] = rnd(M, PR, seed=72)
+    ap = torch.zeros(64, N, dtype=torch.bfloat16, device=DEV)
+    ap[:PR] = rnd(PR, N, scale=0.05, seed=73)
+    ts = torch.ones(M // 128, dtype=torch.int32, device=DEV)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(dy, W, out, b_mn=True, epi=ops.EPI_F32, z=zp, b2=ap, tile_slots=ts, lora_seg=64, max_ctas=1 << 30)
+    exp = dy.float() @ W.float() + zp.float() @ ap.float()
+    torch.testing.assert_close(out, exp, rtol=1e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("M", [5, 130, 600])
 def test_gemm_swiglu_save(M):
     K, I = 512, 768
