@@ -787,7 +787,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   uint64_t* accf_bar = empty_bar + STAGES;  // [2]
   uint64_t* acce_bar = accf_bar + 2;        // [2] (used in the even CTA)
   uint64_t* drain_bar = acce_bar + 2;       // [1]
-  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* exit_bar = drain_bar + 1;       // [1] the peer CTA is done with the pair
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(exit_bar + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -817,11 +818,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       mbar_init(&acce_bar[a], 8);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(exit_bar, 1);
     fence_mbarrier_init_cluster();
   }
+  // Both CTAs' barriers are initialised before any remote arrive; nothing
+  // that can block precedes this barrier.
+  cluster_sync_all();
   if (warp == 2) tmem_alloc_pair(tmem_base_smem, Cfg::TMEM_COLS);
   tc_fence_before();
-  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_smem;
 
@@ -955,9 +960,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       if (lane == 0) mbar_arrive_cluster(acce_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
     }
   }
+  // Exit handshake (bounded): each CTA tells its peer it is done with the
+  // pair (its MMAs drained / its TMEM reads and copies finished) and waits
+  // for the peer's word before freeing TMEM and leaving.
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still uses it
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(mapa_shared(smem_u32(exit_bar), rank ^ 1u));
+    uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(exit_bar, 0)) {
+      if (globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitPeer); break; }
+    }
+  }
+  __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
 }
