@@ -59,7 +59,9 @@ def parse():
     p.add_argument("--tbt-slo", type=float, default=0.06)
     p.add_argument("--profile-repeats", type=int, default=1)
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"])
+    p.add_argument("--tp-comm", default="fused", choices=["nccl", "fused"],
+                   help="row-parallel all-reduce: fused GEMM+all-reduce kernel over NVLink peer memory "
+                        "(falls back to NCCL if its start-up self-test fails) or plain NCCL")
     p.add_argument("--run-ahead", type=int, default=6, help="backward layers queued ahead of the GPU")
     p.add_argument("--phase", default="both", choices=["prefill", "both"],
                    help="coserving_admission_phase (both: FT may ride decode-only steps too)")
