@@ -148,3 +148,26 @@ def test_backward_failure_disables_finetuning_sticky(monkeypatch):
         assert eng.finished[-1].request_id == "late" and eng.stats["ft_tokens_forwarded"] == fwd
         assert eng.finetuning_status()["disabled"]
         assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+
+
+def test_lora_slot_limit_with_pinned_ft_slot():
+    """max_loras counts the pinned finetuning slot: with max_loras=3 two
+    inference adapters fit, a third is refused, and requests of every loaded
+    adapter are co-batched with FT rows (the reference's scheduler edge case
+    ``tests/test_ft_lora_limit.py``: FT rows must not be starved by the slot
+    limit)."""
+    import pytest
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)                  # loads "toy" (max_loras=3: toy + FT + one more)
+        eng.load_inference_adapter("second", rank=8, alpha=16, seed=3)
+        with pytest.raises(RuntimeError, match="no free LoRA slot"):
+            eng.load_inference_adapter("third", rank=8, alpha=16, seed=4)
+        g = torch.Generator().manual_seed(5)
+        for i, ad in enumerate(["toy", "second", None, "toy"]):
+            eng.add_request(f"r{i}", torch.randint(0, 1024, (25,), generator=g).tolist(),
+                            SamplingParams(max_tokens=4), adapter=ad)
+        eng.run_until_idle(max_steps=2000)
+        assert len(eng.finished) == 4
+        assert eng.stats["ft_tokens_forwarded"] > 0 and eng.coord.completed_cycles >= 1
+        eng.unload_inference_adapter("second")
+        eng.load_inference_adapter("third", rank=8, alpha=16, seed=4)   # the freed slot is reusable
