@@ -22,6 +22,7 @@ request arrival, run-ahead bound) — the reference's pause contract
 from __future__ import annotations
 
 import math
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -89,6 +90,12 @@ class LoraTrainer:
         self._seen_shapes: set = set()
         self._sq_rep = torch.zeros(L, dtype=torch.float32, device=dev)
         self._sq_shard = torch.zeros(L, dtype=torch.float32, device=dev)
+        # DSERVE_TP_DIAG=N: for the first N cycles, recompute every captured
+        # activation from the layer input and log its largest deviation from
+        # the captured copy (forward capture vs backward recompute; the
+        # reference's remat-vs-captured check). Runs eagerly, graphs off.
+        self.diag_cycles = int(os.environ.get("DSERVE_TP_DIAG", "0") or 0)
+        self.diag_log: list[dict] = []
 
     # ------------------------------------------------------------ adapter state
     def load_adapter(self, tensors: dict[str, torch.Tensor], rank: int, alpha: float) -> None:
@@ -172,12 +179,31 @@ class LoraTrainer:
             saved["ctx"] = self.bwd.recompute_ctx(l, saved["qkv"], ci, pos, self.cos_sin)
         if saved["resid_mid"] is None:
             saved["resid_mid"] = self.bwd.recompute_resid_mid(l, saved["layer_in"], saved["ctx"])
+        if self.diag_cycles > 0 and self.step < self.diag_cycles:
+            self._diag_layer(l, saved, ci, pos)
         dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin)
         if self.comm is not None and self.comm.size > 1 and (l % BUCKET_LAYERS == 0):
             # Layers [l, l + BUCKET_LAYERS) are done: one all-reduce of their
             # replicated factor gradients.
             self.comm.all_reduce(m.rep_block(m.grads, l, min(L, l + BUCKET_LAYERS)))
         return dh
+
+    @torch.no_grad()
+    def _diag_layer(self, l, saved, ci, pos) -> None:
+        """Largest relative deviation of each recomputed activation from its
+        captured copy over the cycle's rows (logged and kept in diag_log)."""
+        n = ci.n
+        rec = {"cycle": self.step, "layer": l}
+        qkv = self.bwd.recompute_qkv_raw(l, saved["layer_in"])
+        ctx = self.bwd.recompute_ctx(l, saved["qkv"], ci, pos, self.cos_sin)
+        mid = self.bwd.recompute_resid_mid(l, saved["layer_in"], saved["ctx"])
+        for name, got in (("qkv", qkv), ("ctx", ctx), ("resid_mid", mid)):
+            ref = saved[name][:n].float()
+            d = (got[:n].float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6)
+            rec[name] = float(d)
+        self.diag_log.append(rec)
+        dprint(f"[diag] cycle {self.step} layer {l}: recompute vs captured rel max "
+               f"qkv {rec['qkv']:.2e} ctx {rec['ctx']:.2e} resid_mid {rec['resid_mid']:.2e}")
 
     def _graph_set(self, cap, ci, n_valid):
         """Per-batch-shape CUDA graphs: one for the head, one per layer, all in
@@ -189,7 +215,7 @@ class LoraTrainer:
         gs = self._graphs.get(key)
         if gs is not None:
             return gs
-        if not self.use_graphs or len(self._graphs) >= self.max_graph_shapes:
+        if not self.use_graphs or len(self._graphs) >= self.max_graph_shapes or self.diag_cycles > 0:
             return None
         if key not in self._seen_shapes:
             # First cycle of a shape runs eagerly (creates library handles and

@@ -171,3 +171,16 @@ def test_lora_slot_limit_with_pinned_ft_slot():
         assert eng.stats["ft_tokens_forwarded"] > 0 and eng.coord.completed_cycles >= 1
         eng.unload_inference_adapter("second")
         eng.load_inference_adapter("third", rank=8, alpha=16, seed=4)   # the freed slot is reusable
+
+
+def test_tp_diag_recompute_matches_capture(monkeypatch):
+    """DSERVE_TP_DIAG: the backward's recompute of every captured activation
+    agrees with what the serving forward captured."""
+    monkeypatch.setenv("DSERVE_TP_DIAG", "2")
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        eng.run_until_idle(max_steps=2000)
+        log = eng.trainer.diag_log
+        assert len(log) == 2 * eng.arch.num_layers
+        for rec in log:
+            assert rec["qkv"] < 1e-4 and rec["ctx"] < 1e-4 and rec["resid_mid"] < 1e-4, rec
