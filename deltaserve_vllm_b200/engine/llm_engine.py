@@ -27,13 +27,11 @@ Step (rank 0):
 from __future__ import annotations
 
 import json
-import math
-import sys
 import threading
 import os
 import time
 from collections import deque
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 import torch
@@ -52,7 +50,7 @@ from .ft.tbt_window import TbtWindow
 from .ft_job import FinetuneJobSpec, FtJobManager
 from .kv_cache import KVCache
 from .model_runner import ModelRunner
-from .request import Request, SamplingParams, Status
+from .request import Request, SamplingParams
 from .scheduler import Scheduler, SchedulerOutput
 from .trainer import LoraTrainer
 

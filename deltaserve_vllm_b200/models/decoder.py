@@ -22,14 +22,14 @@ gate_up GEMM with SwiGLU epilogue (+LoRA) -> down GEMM (+LoRA) -> all-reduce.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 
 from .. import ops
 from ..ops import EPI_BF16, EPI_F32, EPI_SWIGLU
 from .configs import ModelArch
-from .lora import GROUPS, LoraServeBuffers
+from .lora import LoraServeBuffers
 from .weights import ModelWeights
 
 

@@ -40,10 +40,10 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..ops import EPI_F32, EPI_F32_ACCUM, EPI_SWIGLU_BWD
-from ..ops.reference import deinterleave64, interleave64
+from ..ops.reference import interleave64
 from .configs import ModelArch
-from .lora import GROUP_PROJS, GROUPS, COLUMN_PARALLEL, GroupGeom, group_geoms, peft_key, shard_lora_factor
-from .rope import apply_rope, rope_backward
+from .lora import GROUP_PROJS, GROUPS, GroupGeom, group_geoms, peft_key, shard_lora_factor
+from .rope import rope_backward
 from .weights import ModelWeights, TPInfo
 
 REPLICATED = {"qkv": "A", "gate_up": "A", "o": "B", "down": "B"}

@@ -10,7 +10,6 @@ silent fallback.
 
 from __future__ import annotations
 
-import math
 import os
 
 import torch

@@ -7,7 +7,6 @@ kernel so that CPU runs of the engine and GPU runs agree up to bf16 rounding.
 
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.nn.functional as F
