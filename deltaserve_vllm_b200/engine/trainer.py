@@ -69,7 +69,7 @@ class LoraTrainer:
         dev = weights.embed.device
         R = served.R if served is not None else rank
         self.masters = LoraMasters(self.arch, weights.tp, R, dev)
-        self.bwd = LoraBackward(weights, self.masters, self.scaling, comm)
+        self.bwd = LoraBackward(weights, self.masters, self.scaling, comm, served=served, ft_slot=ft_slot)
         self.adapter_config = adapter_config or peft_io.default_adapter_config(
             rank, alpha, self.targets or ("q", "k", "v", "o", "gate", "up", "down"))
         self.cos_sin = cos_sin_table

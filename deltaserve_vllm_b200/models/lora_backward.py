@@ -39,7 +39,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import ops
-from ..ops import EPI_F32, EPI_F32_ACCUM, EPI_SWIGLU_BWD
+from ..ops import EPI_BF16, EPI_F32, EPI_F32_ACCUM, EPI_SWIGLU_BWD
 from ..ops.reference import interleave64
 from .configs import ModelArch
 from .lora import GROUP_PROJS, GROUPS, GroupGeom, group_geoms, peft_key, shard_lora_factor
@@ -290,8 +290,14 @@ class LoraBackward:
     head / layer backward steps. Works on CPU (fp32 oracle ops) and CUDA."""
 
     def __init__(self, weights: ModelWeights, masters: LoraMasters, scaling: float, comm=None,
-                 cdt=torch.bfloat16):
+                 cdt=torch.bfloat16, served=None, ft_slot: int = -1):
         self.w, self.m, self.s = weights, masters, scaling
+        # The served copy of the trained adapter (its slot of the serving LoRA
+        # buffers, republished after every optimizer step): A [P*R, K] and the
+        # scaled, scattered expand factor in the compute dtype, read in place
+        # instead of being rebuilt from the fp32 masters for every group.
+        self.served = served if (served is not None and ft_slot >= 0) else None
+        self.ft_slot = ft_slot
         self.arch = weights.arch
         self.comm = comm
         self.cdt = cdt if weights.embed.is_cuda else torch.float32
@@ -308,8 +314,12 @@ class LoraBackward:
 
     # ------------------------------------------------------------ GEMM helpers
     def _mm(self, a, b, b_mn, epi=EPI_F32, out=None):
-        a = _bf(a, self.cdt).contiguous()
-        b = _bf(b, self.cdt).contiguous()
+        a = _bf(a, self.cdt)
+        b = _bf(b, self.cdt)
+        if a.stride(-1) != 1:
+            a = a.contiguous()
+        if b.stride(-1) != 1:
+            b = b.contiguous()
         if out is None:
             n = b.shape[1] if b_mn else b.shape[0]
             out = torch.empty(a.shape[0], n, dtype=torch.float32, device=a.device)
@@ -351,10 +361,33 @@ class LoraBackward:
         tensor as a writable view [R, N/128, 64]."""
         return t.view(t.shape[0], gg.N // 128, 2, 64)[:, :, p]
 
+    def slot_A(self, layer: int, g: str) -> torch.Tensor:
+        """The trained A factor [P*R, K] in the compute dtype."""
+        if self.served is not None:
+            return self.served.A[layer][g][self.ft_slot]
+        return _bf(self.m.p(layer, g, "A"), self.cdt)
+
+    def slot_B(self, layer: int, g: str) -> torch.Tensor:
+        """The scaled, scattered expand factor [N, P*R] in the compute dtype
+        (a strided view of the served slot when there is one)."""
+        if self.served is not None:
+            sv = self.served
+            c0 = self.ft_slot * sv.seg[g]
+            return sv.B2[layer][g][:, c0:c0 + self.geom[g].P * self.m.R]
+        return self._bfull(layer, g)
+
     def group_dz(self, layer: int, g: str, dY: torch.Tensor) -> torch.Tensor:
-        """dZ = dY . B_full (fp32 [n, P*R]): the adapter's share of the
-        input gradient before the A factor."""
-        return self._mm(dY, self._bfull(layer, g), b_mn=True)
+        """dZ = dY . B_full, the adapter's share of the input gradient before
+        the A factor, in the compute dtype and zero-padded to a 64-column
+        segment: [n, seg] (columns P*R.. are zero) — the extra K-block of the
+        fused dX GEMM and the left operand of the A gradient."""
+        n = dY.shape[0]
+        PR = self.geom[g].P * self.m.R
+        seg = -(-PR // 64) * 64
+        zp = torch.zeros(n, seg, dtype=self.cdt, device=dY.device)
+        self._mm(dY, self.slot_B(layer, g), b_mn=True, epi=EPI_BF16 if self.cdt == torch.bfloat16 else EPI_F32,
+                 out=zp[:, :PR])
+        return zp
 
     def dx_gemm(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor,
                 swiglu_gu: torch.Tensor | None = None, act_out: torch.Tensor | None = None) -> torch.Tensor:
@@ -367,21 +400,17 @@ class LoraBackward:
         instead of storing it: the result is d(gate_up) in the compute dtype
         (and the activation into ``act_out`` when given)."""
         n = dY.shape[0]
-        PR = dZ.shape[1]
-        seg = -(-PR // 64) * 64
-        A = self.m.p(layer, g, "A")
+        zp = dZ                       # [n, seg] from group_dz (zero-padded columns)
+        seg = zp.shape[1]
+        ap = self.slot_A(layer, g)    # [P*R, K]: rows seg.. of the K-block read as zero
         if not dY.is_cuda:
             out = self._mm(dY, W, b_mn=True)
-            out += dZ @ A
+            out += zp[:, :ap.shape[0]].float() @ ap.float()
             if swiglu_gu is not None:
                 d_gu = torch.empty(n, swiglu_gu.shape[1], dtype=self.cdt, device=dY.device)
                 ops.swiglu_bwd(swiglu_gu, out, d_gu, act_out)
                 return d_gu
             return out
-        zp = torch.zeros(n, seg, dtype=self.cdt, device=dY.device)
-        zp[:, :PR] = dZ
-        ap = torch.zeros(seg, A.shape[1], dtype=self.cdt, device=dY.device)
-        ap[:PR] = A
         key = (-(-n // 128), dY.device)
         ts = self._ones_slots.get(key)
         if ts is None:
@@ -399,22 +428,29 @@ class LoraBackward:
         return out
 
     def group_grads(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor, dZ: torch.Tensor) -> None:
-        """Factor gradients of one group into the trainer's grad buffer."""
+        """Factor gradients of one group into the trainer's grad buffer:
+        dA = dZ^T X and dB^T = s Z^T dY with Z^T = A X^T computed directly
+        (no transposed copies of Z)."""
         gg = self.geom[g]
         R = self.m.R
-        A = _bf(self.m.p(layer, g, "A"), self.cdt)
-        Z = self._mm(X, A, b_mn=False)                       # [n, PR]
+        PR = gg.P * R
+        A = self.slot_A(layer, g)
+        n = X.shape[0]
+        epi_c = EPI_BF16 if self.cdt == torch.bfloat16 else EPI_F32
+        ZT = torch.empty(PR, n, dtype=self.cdt, device=X.device)
+        self._mm(A, X, b_mn=False, epi=epi_c, out=ZT)        # Z^T [PR, n]
+        dZT = dZ[:, :PR].t().contiguous()                   # [PR, n]
         gA = self.m.g(layer, g, "A")
-        self._mm(dZ.t(), X, b_mn=True, out=gA)               # [PR, K]
-        gBfT = self._mm(Z.t(), dY, b_mn=True) * self.s       # [PR, N]
+        self._mm(dZT, X, b_mn=True, out=gA)                 # [PR, K]
+        gBfT = self._mm(ZT, dY, b_mn=True)                  # [PR, N] (unscaled)
         gBt = self.m.g(layer, g, "Bt")
         for p in range(gg.P):
             src = gBfT[p * R:(p + 1) * R]
             if gg.interleave:
-                self._cols3(gBt, gg, p).copy_(self._cols3(src, gg, p))
+                torch.mul(self._cols3(src, gg, p), self.s, out=self._cols3(gBt, gg, p))
             else:
                 b0, b1 = self._bounds(gg, p)
-                gBt[:, b0:b1].copy_(src[:, b0:b1])
+                torch.mul(src[:, b0:b1], self.s, out=gBt[:, b0:b1])
 
     def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
                        dX: torch.Tensor) -> None:
@@ -422,8 +458,8 @@ class LoraBackward:
         (fp32) and writes the factor gradients (the layer backward uses the
         fused :meth:`dx_gemm` instead)."""
         dZ = self.group_dz(layer, g, dY)
-        A = _bf(self.m.p(layer, g, "A"), self.cdt)
-        self._mm(dZ, A, b_mn=True, epi=EPI_F32_ACCUM, out=dX)
+        A = self.slot_A(layer, g)
+        self._mm(dZ[:, :A.shape[0]], A, b_mn=True, epi=EPI_F32_ACCUM, out=dX)
         self.group_grads(layer, g, X, dY, dZ)
 
     # ------------------------------------------------------------ head
@@ -462,9 +498,8 @@ class LoraBackward:
         """fp32 ``X @ W^T`` plus the trained adapter's term for group ``g``
         (the forward's projection, for activations that were not captured)."""
         y = self._mm(X, W, b_mn=False)
-        A = _bf(self.m.p(layer, g, "A"), self.cdt)
-        Z = self._mm(X, A, b_mn=False)
-        self._mm(Z, self._bfull(layer, g), b_mn=False, epi=EPI_F32_ACCUM, out=y)
+        Z = self._mm(X, self.slot_A(layer, g), b_mn=False)
+        self._mm(Z, self.slot_B(layer, g), b_mn=False, epi=EPI_F32_ACCUM, out=y)
         return y
 
     def recompute_qkv_raw(self, layer: int, layer_in: torch.Tensor) -> torch.Tensor:

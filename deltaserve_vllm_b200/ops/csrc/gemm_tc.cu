@@ -1314,8 +1314,8 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     TORCH_CHECK(lora_seg % 64 == 0, "dsv_gemm: lora_seg must be a multiple of 64");
     auto& zt = *z;
     auto& bt = *b2;
-    if (b_mn) {  // B2 is [S*SEG, N] (same orientation as B)
-      TORCH_CHECK(zt.size(0) >= M && bt.size(1) == N && zt.size(1) == bt.size(0), "dsv_gemm: LoRA shapes");
+    if (b_mn) {  // B2 is [S*SEG, N] (same orientation as B); rows past its end read as zero
+      TORCH_CHECK(zt.size(0) >= M && bt.size(1) == N && zt.size(1) >= bt.size(0), "dsv_gemm: LoRA shapes");
     } else {     // B2 is [N, S*SEG]
       TORCH_CHECK(zt.size(0) >= M && bt.size(0) == N && zt.size(1) == bt.size(1), "dsv_gemm: LoRA shapes");
     }

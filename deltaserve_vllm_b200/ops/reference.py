@@ -32,8 +32,11 @@ def interleave64(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
 def gemm(a, b, out, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0,
          save=None, save_lo=0, save_hi=0, save_dst=0, aux=None, aux_out=None):
     acc = a.float() @ (b.float() if b_mn else b.float().t())
-    if lora_seg and z is not None:  # b_mn: b2 is [S*SEG, N] like b; else [N, S*SEG]
-        acc = acc + z[: a.shape[0]].float() @ (b2.float() if b_mn else b2.float().t())
+    if lora_seg and z is not None:  # b_mn: b2 is [S*SEG, N] like b (rows past its end are zero); else [N, S*SEG]
+        if b_mn:
+            acc = acc + z[: a.shape[0], : b2.shape[0]].float() @ b2.float()
+        else:
+            acc = acc + z[: a.shape[0]].float() @ b2.float().t()
     if save is not None and save_hi > save_lo:
         save[save_dst: save_dst + save_hi - save_lo] = acc[save_lo:save_hi].to(save.dtype)
     if epi == EPI_SWIGLU:

@@ -48,6 +48,23 @@ def test_gemm_mn_major_f32(M, N, K):
     torch.testing.assert_close(acc, 1 + a.float() @ w.float(), rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("M", [300, 2048])
+def test_gemm_mn_major_lora_block_unpadded_b2(M):
+    """dX = dY . W + dZ . A with A given unpadded ([P*R, N], fewer rows than the
+    64-deep K-block): rows past A's end read as zero (dZ's padding columns are
+    zero too)."""
+    Kred, N, PR = 1024, 2048, 48
+    dy, W = rnd(M, Kred, seed=80), rnd(Kred, N, scale=0.02, seed=81)
+    zp = torch.zeros(M, 64, dtype=torch.bfloat16, device=DEV)
+    zp[:, :PR] = rnd(M, PR, seed=82)
+    A = rnd(PR, N, scale=0.05, seed=83)
+    ts = torch.ones((M + 127) // 128, dtype=torch.int32, device=DEV)
+    out = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(dy, W, out, b_mn=True, epi=ops.EPI_F32, z=zp, b2=A, tile_slots=ts, lora_seg=64, max_ctas=1 << 30)
+    exp = dy.float() @ W.float() + zp[:, :PR].float() @ A.float()
+    torch.testing.assert_close(out, exp, rtol=1e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("M,N,K,b_mn", [(48, 4096, 4096, True), (48, 28672, 4096, True), (4096, 48, 4096, True),
                                         (4096, 48, 14336, False), (16, 1024, 8192, True), (2048, 64, 2048, False)])
 @pytest.mark.parametrize("epi", [1, 3, 0])
