@@ -12,6 +12,9 @@ activation-capture buffers (``gpu_memory_utilization`` of the total).
 
 from __future__ import annotations
 
+import hashlib
+from collections import OrderedDict
+
 import torch
 
 
@@ -43,6 +46,95 @@ class BlockAllocator:
 
 def blocks_needed(num_tokens: int, block_size: int) -> int:
     return -(-num_tokens // block_size)
+
+
+def block_hash(parent: bytes, tokens, extra: tuple = ()) -> bytes:
+    """Hash of a full page given its parent page's hash, its token ids and the
+    identity of whatever else shaped its KV (the LoRA slot and its version)."""
+    h = hashlib.blake2b(digest_size=16)
+    h.update(parent)
+    h.update(repr(tuple(extra)).encode())
+    h.update(b",".join(str(int(t)).encode() for t in tokens))
+    return h.digest()
+
+
+class PrefixCachingAllocator(BlockAllocator):
+    """Page allocator with automatic prefix caching (vLLM's semantics): every
+    full page of a request is registered under a chained hash of its tokens
+    (and the LoRA slot version that produced its K/V); a later request whose
+    prompt starts with the same pages reuses them instead of recomputing.
+    Pages are reference counted; a released page that holds a registered
+    prefix stays cached (evictable, least recently used first) until its id
+    is needed for a new allocation."""
+
+    def __init__(self, num_blocks: int):
+        super().__init__(num_blocks)
+        self.ref = [0] * num_blocks
+        self.hash_of: dict[int, bytes] = {}     # page -> registered hash
+        self.page_of: dict[bytes, int] = {}     # hash -> page
+        self.evictable: OrderedDict[int, None] = OrderedDict()  # cached pages with ref 0, LRU first
+        self.hits = 0
+        self.queries = 0
+
+    @property
+    def num_free(self) -> int:
+        return len(self._free) + len(self.evictable)
+
+    def _evict(self, page: int) -> None:
+        del self.evictable[page]
+        h = self.hash_of.pop(page)
+        if self.page_of.get(h) == page:
+            del self.page_of[h]
+
+    def allocate(self, n: int) -> list[int]:
+        if n > self.num_free:
+            raise MemoryError(f"KV cache out of pages: need {n}, have {self.num_free}")
+        take = min(n, len(self._free))
+        out = super().allocate(take)
+        while len(out) < n:                      # reuse the least recently used cached pages
+            page = next(iter(self.evictable))
+            self._evict(page)
+            out.append(page)
+        for p in out:
+            self.ref[p] = 1
+        return out
+
+    def free(self, ids: list[int]) -> None:
+        plain = []
+        for p in ids:
+            self.ref[p] -= 1
+            if self.ref[p] > 0:
+                continue
+            if p in self.hash_of:
+                self.evictable[p] = None         # most recently used at the end
+            else:
+                plain.append(p)
+        super().free(plain)
+
+    def lookup(self, hashes: list[bytes]) -> list[int]:
+        """Pages holding the longest cached run of ``hashes`` (each gets a
+        reference)."""
+        out = []
+        self.queries += len(hashes)
+        for h in hashes:
+            p = self.page_of.get(h)
+            if p is None:
+                break
+            if self.ref[p] == 0:
+                del self.evictable[p]
+            self.ref[p] += 1
+            out.append(p)
+        self.hits += len(out)
+        return out
+
+    def register(self, page: int, h: bytes) -> None:
+        """Record that ``page`` (full) holds the prefix hashed ``h``."""
+        if page in self.hash_of:
+            return
+        if h in self.page_of:                    # the same prefix already lives elsewhere
+            return
+        self.hash_of[page] = h
+        self.page_of[h] = page
 
 
 class KVCache:

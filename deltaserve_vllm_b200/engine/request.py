@@ -65,11 +65,18 @@ class Request:
 
     @property
     def in_prefill(self) -> bool:
-        return self.num_computed < self.num_prompt
+        """True while more than the newest token lacks KV: a fresh prompt, a
+        chunked prompt, or a request pre-empted by recompute (which must
+        recompute its prompt AND the tokens it already produced before
+        decoding continues)."""
+        pending = self.num_tokens - self.num_computed
+        return pending > 1 or (not self.output_ids and pending > 0)
 
     @property
     def remaining_prefill(self) -> int:
-        return max(0, self.num_prompt - self.num_computed)
+        """Tokens the prefill still has to process (the last one's logits give
+        the next token)."""
+        return self.num_tokens - self.num_computed if self.in_prefill else 0
 
     def finished(self) -> bool:
         return self.status in (Status.FINISHED, Status.ABORTED)
