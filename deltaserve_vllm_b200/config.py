@@ -274,6 +274,8 @@ class EngineConfig:
     max_num_seqs: int = 256
     max_num_batched_tokens: int = 8192
     enable_chunked_prefill: bool = True
+    # Automatic prefix caching of full KV pages (chained token hashes keyed by
+    # the LoRA slot version; finetuning rows never share pages).
     enable_prefix_caching: bool = False
     enforce_eager: bool = False
     enable_lora: bool = True

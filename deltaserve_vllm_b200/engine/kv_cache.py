@@ -127,6 +127,9 @@ class PrefixCachingAllocator(BlockAllocator):
         self.hits += len(out)
         return out
 
+    def usage(self) -> float:
+        return 1.0 - self.num_free / max(1, self.num_blocks)
+
     def register(self, page: int, h: bytes) -> None:
         """Record that ``page`` (full) holds the prefix hashed ``h``."""
         if page in self.hash_of:
@@ -139,13 +142,13 @@ class PrefixCachingAllocator(BlockAllocator):
 
 class KVCache:
     def __init__(self, num_layers: int, num_blocks: int, num_kv_heads_local: int, block_size: int,
-                 head_dim: int, device, dtype=torch.bfloat16):
+                 head_dim: int, device, dtype=torch.bfloat16, prefix_caching: bool = False):
         self.block_size = block_size
         self.num_blocks = num_blocks
         shape = (num_blocks, num_kv_heads_local, block_size, head_dim)
         self.k = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
         self.v = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
-        self.allocator = BlockAllocator(num_blocks)
+        self.allocator = PrefixCachingAllocator(num_blocks) if prefix_caching else BlockAllocator(num_blocks)
 
     @staticmethod
     def bytes_per_block(num_layers: int, num_kv_heads_local: int, block_size: int, head_dim: int,

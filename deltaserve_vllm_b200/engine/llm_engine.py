@@ -125,7 +125,7 @@ class CoServingEngine:
                    if self.cuda else 148)
         self.scheduler = Scheduler(self.kv.allocator, ecfg.block_size, ecfg.max_num_seqs,
                                    ecfg.max_num_batched_tokens, ecfg.max_model_len,
-                                   ecfg.enable_chunked_prefill)
+                                   ecfg.enable_chunked_prefill, cache_key=self._cache_key)
         self.runner = ModelRunner(self.model, ecfg.block_size, self.device, num_sms,
                                   max_model_len=ecfg.max_model_len, decode_graphs=not ecfg.enforce_eager)
         # Backward collectives use their own communicator: forward and backward
@@ -225,7 +225,18 @@ class CoServingEngine:
         if nb < 2:
             raise MemoryError("no room for the KV cache")
         return KVCache(self.arch.num_layers, nb, hkv, e.block_size, self.arch.head_dim, self.device,
-                       self.dtype)
+                       self.dtype, prefix_caching=e.enable_prefix_caching)
+
+    def _cache_key(self, req: Request):
+        """What besides the tokens shaped a request's K/V, for prefix caching:
+        its LoRA slot and the slot's load version. Requests on the adapter
+        being trained never share pages (its weights change every cycle)."""
+        slot = req.lora_slot
+        if slot < 0:
+            return (-1, 0)
+        if slot == self.ft_slot:
+            return None
+        return (slot, self.lora.version[slot] if self.lora is not None else 0)
 
     def _init_finetuning(self, ft_adapter) -> None:
         from ..adapters import peft_io

@@ -50,6 +50,11 @@ class Request:
     seq_no: int = field(default_factory=lambda: next(_counter))
     # Route decision headers, filled by adapter routing.
     trace: dict = field(default_factory=dict)
+    # Prefix caching: hashes of the request's full pages (chained), how many
+    # of its pages are registered, and prompt tokens served from the cache.
+    block_hashes: list = field(default_factory=list)
+    num_registered: int = 0
+    num_cached_tokens: int = 0
 
     @property
     def all_ids(self) -> list[int]:

@@ -22,7 +22,7 @@ import time
 from collections import deque
 from dataclasses import dataclass, field
 
-from .kv_cache import BlockAllocator, blocks_needed
+from .kv_cache import BlockAllocator, PrefixCachingAllocator, block_hash, blocks_needed
 from .request import Request, Status
 
 
@@ -80,8 +80,15 @@ class SchedulerOutput:
 class Scheduler:
     def __init__(self, allocator: BlockAllocator, block_size: int, max_num_seqs: int = 256,
                  max_num_batched_tokens: int = 8192, max_model_len: int = 4096,
-                 enable_chunked_prefill: bool = True):
+                 enable_chunked_prefill: bool = True, cache_key=None):
         self.alloc = allocator
+        # Automatic prefix caching when the allocator supports it: a waiting
+        # request starts after the longest run of cached full pages of its
+        # tokens. ``cache_key(req)`` identifies what else shaped the K/V (its
+        # LoRA slot and version); None = the request neither uses nor feeds
+        # the cache (finetuning rows, the adapter being trained).
+        self.caching = isinstance(allocator, PrefixCachingAllocator)
+        self.cache_key = cache_key or (lambda req: ())
         self.block_size = block_size
         self.max_num_seqs = max_num_seqs
         self.max_num_batched_tokens = max_num_batched_tokens
@@ -131,6 +138,66 @@ class Scheduler:
         req.block_ids.extend(self.alloc.allocate(need))
         return True
 
+    # ------------------------------------------------------------ prefix cache
+    def _key(self, req: Request):
+        if not self.caching or req.is_ft:
+            return None
+        return self.cache_key(req)
+
+    def _hashes(self, req: Request, key, n_pages: int) -> list:
+        bs = self.block_size
+        ids = req.all_ids
+        hs = req.block_hashes
+        while len(hs) < n_pages:
+            j = len(hs)
+            hs.append(block_hash(hs[-1] if hs else b"", ids[j * bs:(j + 1) * bs], key))
+        return hs
+
+    def _attach_prefix(self, req: Request) -> None:
+        """Reuse cached pages for the request's leading full pages (at least
+        one token is always left to compute: its logits give the next token)."""
+        key = self._key(req)
+        if key is None or req.num_computed or req.block_ids:
+            return
+        req.block_hashes, req.num_registered = [], 0
+        n_pages = (req.num_tokens - 1) // self.block_size
+        if n_pages <= 0:
+            return
+        pages = self.alloc.lookup(self._hashes(req, key, n_pages))
+        if pages:
+            req.block_ids = pages
+            req.num_registered = len(pages)
+            req.num_computed = len(pages) * self.block_size
+            req.num_cached_tokens = req.num_computed
+
+    def _detach_prefix(self, req: Request) -> None:
+        """Give back cached pages of a request that could not be admitted."""
+        if req.block_ids:
+            self.alloc.free(req.block_ids)
+            req.block_ids = []
+        req.num_computed = 0
+        req.num_registered = 0
+        req.num_cached_tokens = 0
+
+    def _register(self, req: Request) -> None:
+        """Publish the request's newly completed full pages to the cache."""
+        key = self._key(req)
+        if key is None:
+            return
+        full = min(req.num_computed // self.block_size, len(req.block_ids))
+        if full <= req.num_registered:
+            return
+        hs = self._hashes(req, key, full)
+        for j in range(req.num_registered, full):
+            self.alloc.register(req.block_ids[j], hs[j])
+        req.num_registered = full
+
+    def cache_stats(self) -> dict:
+        if not self.caching:
+            return {"enabled": False}
+        return {"enabled": True, "queried_pages": self.alloc.queries, "hit_pages": self.alloc.hits,
+                "cached_pages": len(self.alloc.hash_of), "evictable_pages": len(self.alloc.evictable)}
+
     def _preempt_one(self, out: SchedulerOutput, protect: Request) -> bool:
         for victim in reversed(self.running):
             if victim is protect:
@@ -138,6 +205,7 @@ class Scheduler:
             self.running.remove(victim)
             self._free(victim)
             victim.num_computed = 0
+            victim.num_registered = 0
             victim.status = Status.WAITING
             self.waiting.appendleft(victim)
             out.preempted.append(victim)
@@ -175,12 +243,18 @@ class Scheduler:
         # 2b. waiting requests
         while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
             req = self.waiting[0]
+            if self.caching:
+                self._attach_prefix(req)
             n = req.remaining_prefill
             if n > budget:
                 if not self.chunked:
+                    if self.caching:
+                        self._detach_prefix(req)
                     break
                 n = budget
             if not self._ensure_blocks(req, req.num_computed + n):
+                if self.caching:
+                    self._detach_prefix(req)
                 break
             self.waiting.popleft()
             req.status = Status.RUNNING
@@ -222,6 +296,8 @@ class Scheduler:
         for s in out.decode + out.prefill:
             r = s.req
             r.num_computed += s.num_new
+            if self.caching:
+                self._register(r)
             if not s.sample:
                 continue
             tok = sampled.get(r.seq_no)

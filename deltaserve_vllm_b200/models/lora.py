@@ -134,8 +134,12 @@ class LoraServeBuffers:
             self.A.append(a)
             self.B2.append(b)
         self.slot_rank = [0] * slots
+        # Bumped whenever a slot's weights are replaced: cached K/V computed
+        # with an older version of the slot is never reused.
+        self.version = [0] * slots
 
     def clear_slot(self, slot: int) -> None:
+        self.version[slot] += 1
         for i in range(self.arch.num_layers):
             for g in GROUPS:
                 self.A[i][g][slot].zero_()
@@ -148,7 +152,7 @@ class LoraServeBuffers:
         """Write a full PEFT adapter (all layers) into ``slot``, sharding for TP."""
         if rank > self.R:
             raise ValueError(f"adapter rank {rank} > max_lora_rank {self.R}")
-        self.clear_slot(slot)
+        self.clear_slot(slot)           # (bumps the version)
         scale = alpha / rank
         for i in range(self.arch.num_layers):
             for g in GROUPS:

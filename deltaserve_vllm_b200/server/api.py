@@ -231,6 +231,10 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         return {"saved": True, "path": path}
 
     # ------------------------------------------------------------ telemetry
+    @app.get("/prefix_cache")
+    async def prefix_cache():
+        return await et.call(lambda e: dict(e.scheduler.cache_stats(), kv_usage=e.kv.allocator.usage()))
+
     @app.get("/system_metrics")
     async def system_metrics():
         m = getattr(engine, "metrics", None)

@@ -184,3 +184,39 @@ def test_tp_diag_recompute_matches_capture(monkeypatch):
         assert len(log) == 2 * eng.arch.num_layers
         for rec in log:
             assert rec["qkv"] < 1e-4 and rec["ctx"] < 1e-4 and rec["resid_mid"] < 1e-4, rec
+
+
+def test_prefix_caching_engine_adapters_versions_and_ft():
+    """Engine with prefix caching and co-served finetuning: pages are shared
+    only between requests of the same adapter version, requests on the
+    adapter being trained and FT rows never use or feed the cache."""
+    with tempfile.TemporaryDirectory() as tmp:
+        ecfg = EngineConfig(model="qwen3-tiny", device="cpu", max_model_len=512, block_size=16,
+                            max_num_batched_tokens=256, max_loras=3, max_lora_rank=8,
+                            enable_prefix_caching=True)
+        fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=96, learning_rate=1e-3)
+        store = FinetuningStore.synthetic(1024, 12, 16, 40, seed=0, max_saved_finetuning_tokens=96)
+        eng = CoServingEngine(ecfg, fcfg, ft_store=store)
+        eng.load_inference_adapter("toy", rank=8, alpha=16)
+        prefix = list(range(100, 180))                           # 5 full pages
+        sched = eng.scheduler
+
+        def run(rid, adapter, tail):
+            eng.add_request(rid, prefix + tail, SamplingParams(max_tokens=3), adapter=adapter)
+            eng.run_until_idle(max_steps=500)
+            return next(r for r in eng.finished if r.request_id == rid)
+
+        assert run("a0", None, [1, 2]).num_cached_tokens == 0
+        assert run("a1", None, [3]).num_cached_tokens == 80        # same (base) prefix
+        assert run("b0", "toy", [4]).num_cached_tokens == 0        # other adapter: other K/V
+        assert run("b1", "toy", [5]).num_cached_tokens == 80
+        eng.unload_inference_adapter("toy")
+        eng.load_inference_adapter("toy", rank=8, alpha=16, seed=77)   # new weights, same slot
+        assert run("b2", "toy", [6]).num_cached_tokens == 0
+        assert run("f0", FT_ADAPTER_NAME, [7]).num_cached_tokens == 0
+        assert run("f1", FT_ADAPTER_NAME, [8]).num_cached_tokens == 0  # never shared
+        assert eng.coord.completed_cycles >= 1                     # FT rows ran alongside
+        ft_reqs = [r for r in eng.finished if r.is_ft]
+        assert all(r.num_cached_tokens == 0 for r in ft_reqs)
+        assert sched.cache_stats()["hit_pages"] >= 10
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks

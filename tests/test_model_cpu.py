@@ -65,29 +65,35 @@ def test_paged_forward_matches_dense(arch_name, with_lora):
     assert kv.allocator.num_free == kv.allocator.num_blocks
 
 
-def _serve(num_blocks, prompts, max_tokens, block_size=16):
-    """Greedy outputs of a batch served with ``num_blocks`` KV pages."""
+def _serve(num_blocks, prompts, max_tokens, block_size=16, caching=False, waves=1, budget=64):
+    """Greedy outputs of ``prompts`` served with ``num_blocks`` KV pages; with
+    ``waves`` > 1 the prompts arrive in that many groups, each after the
+    previous one finished (so later groups can hit pages cached by earlier ones)."""
     arch = PRESETS["qwen3-tiny"]
     # large init: the greedy continuations vary token to token (a small-init
     # random model repeats one token, which would hide ordering mistakes)
     w = init_weights(arch, seed=3, dtype=torch.float32, std=0.3)
-    kv = KVCache(arch.num_layers, num_blocks, arch.num_kv_heads, block_size, arch.head_dim, "cpu", torch.float32)
+    kv = KVCache(arch.num_layers, num_blocks, arch.num_kv_heads, block_size, arch.head_dim, "cpu", torch.float32,
+                 prefix_caching=caching)
     model = DecoderModel(w, kv.k, kv.v, None)
-    sched = Scheduler(kv.allocator, block_size, max_num_batched_tokens=64, max_model_len=256)
+    sched = Scheduler(kv.allocator, block_size, max_num_batched_tokens=budget, max_model_len=256)
     runner = ModelRunner(model, block_size, "cpu")
     reqs = [Request(f"r{i}", p, SamplingParams(max_tokens=max_tokens)) for i, p in enumerate(prompts)]
-    for r in reqs:
-        sched.add(r)
     preempted = 0
-    for _ in range(2000):
-        out = sched.schedule()
-        preempted += len(out.preempted)
-        if out.is_empty():
-            break
-        toks, _ = runner.execute(out)
-        sched.update(out, toks)
+    per = -(-len(reqs) // waves)
+    for w0 in range(0, len(reqs), per):
+        for r in reqs[w0:w0 + per]:
+            sched.add(r)
+        for _ in range(2000):
+            out = sched.schedule()
+            preempted += len(out.preempted)
+            if out.is_empty():
+                break
+            toks, _ = runner.execute(out)
+            sched.update(out, toks)
     assert all(r.finished() for r in reqs)
     assert kv.allocator.num_free == kv.allocator.num_blocks
+    _serve.last = (sched, reqs)
     return [list(r.output_ids) for r in reqs], preempted
 
 
@@ -101,3 +107,37 @@ def test_preemption_by_recompute_keeps_outputs():
     assert p0 == 0 and p1 > 0
     assert all(len(set(o)) > 5 for o in ref)       # non-degenerate continuations
     assert got == ref
+
+
+
+def test_prefix_caching_reuses_pages_and_matches_uncached():
+    """Automatic prefix caching: prompts sharing a system prefix (and exact
+    repeats) reuse cached full pages; outputs equal the uncached run; a tiny
+    cache evicts and still matches."""
+    g = torch.Generator().manual_seed(11)
+    system = torch.randint(0, 1024, (70,), generator=g).tolist()
+    prompts = [system + torch.randint(0, 1024, (5 + i,), generator=g).tolist() for i in range(4)]
+    prompts += [prompts[0], prompts[2][:40]]          # an exact repeat, a strict prefix
+    ref, _ = _serve(256, prompts, 12, waves=3)
+    got, _ = _serve(256, prompts, 12, caching=True, waves=3)
+    assert got == ref
+    sched, reqs = _serve.last
+    st = sched.cache_stats()
+    assert st["hit_pages"] > 0
+    # the first wave computes the shared system prompt; later waves reuse its
+    # 4 full pages (64 of 70 tokens); the exact repeat reuses every page but
+    # the one holding its last token; the 40-token prefix reuses 2 pages
+    assert reqs[2].num_cached_tokens == 64 and reqs[3].num_cached_tokens == 64
+    assert reqs[4].num_cached_tokens == ((len(prompts[0]) - 1) // 16) * 16
+    assert reqs[5].num_cached_tokens == 32
+    tight, _ = _serve(24, prompts, 12, caching=True, waves=3)
+    assert tight == ref
+
+
+def test_prefix_caching_with_preemption():
+    g = torch.Generator().manual_seed(12)
+    base = torch.randint(0, 1024, (40,), generator=g).tolist()
+    prompts = [base + torch.randint(0, 1024, (3 * i + 1,), generator=g).tolist() for i in range(5)]
+    ref, _ = _serve(256, prompts, 40)
+    got, pre = _serve(16, prompts, 40, caching=True)
+    assert pre > 0 and got == ref

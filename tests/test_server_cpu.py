@@ -61,6 +61,8 @@ def test_api_completions_and_finetuning_control():
             r = c.post("/v1/completions", json={"prompt": [5, 6, 7, 8], "max_tokens": 3, "model": "toy"})
             assert r.status_code == 200 and len(r.json()["choices"][0]["token_ids"]) == 3
             assert c.post("/v1/completions", json={"prompt": "x", "model": "nope"}).status_code == 404
+            pc = c.get("/prefix_cache").json()
+            assert pc["enabled"] is False and 0.0 <= pc["kv_usage"] <= 1.0
             assert c.post("/v1/completions", json={"max_tokens": 3}).status_code == 400
             # streaming: every token arrives, then [DONE]
             with c.stream("POST", "/v1/completions",
