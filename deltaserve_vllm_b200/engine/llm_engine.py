@@ -227,6 +227,21 @@ class CoServingEngine:
         return KVCache(self.arch.num_layers, nb, hkv, e.block_size, self.arch.head_dim, self.device,
                        self.dtype, prefix_caching=e.enable_prefix_caching)
 
+    def _check_stop_strings(self, out, now: float) -> list:
+        """Requests whose decoded output now contains one of their stop strings."""
+        ended = []
+        for s in out.decode + out.prefill:
+            r = s.req
+            if not r.params.stop or r.finished() or not s.sample or not r.output_ids:
+                continue
+            text = self.tokenizer.decode(r.output_ids)
+            hit = next((st for st in r.params.stop if st and st in text), None)
+            if hit is not None:
+                r.stop_reason = hit
+                self.scheduler.finish(r, now)
+                ended.append(r)
+        return ended
+
     def _cache_key(self, req: Request):
         """What besides the tokens shaped a request's K/V, for prefix caching:
         its LoRA slot and the slot's load version. Requests on the adapter
@@ -758,6 +773,8 @@ class CoServingEngine:
         self._pending_timing.append(StepRecord(feats, ev0, ev1, pred, "step"))
         now = time.perf_counter()
         done = self.scheduler.update(out, toks, now)
+        if self.tokenizer is not None:
+            done.extend(self._check_stop_strings(out, now))
         self.stats["steps"] += 1
         if self.tbt_window is not None:
             self.tbt_window.step_done(now, out.b_d, bool(self.scheduler.running))

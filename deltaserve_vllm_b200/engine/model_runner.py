@@ -271,6 +271,7 @@ class ModelRunner:
 
     def graph_eligible(self, meta: dict) -> bool:
         return (self.graphs is not None and meta["npf"] == 0 and meta["nd"] > 0
+                and not meta.get("full_sampler", False)
                 and DecodeGraphs.bucket(meta["nd"]) is not None)
 
     def abort_hook(self, should_abort, vote=None, ahead: int = 2):
@@ -371,7 +372,8 @@ class ModelRunner:
                 mask[t] = m if m < (1 << 31) else m - (1 << 32)
             pk.add("tile_slots", mask)
         pk.add("logits_idx", sample_rows)
-        meta = {"nd": nd, "maxb": maxb, "splits": splits, "kps": kps, "npf": len(pf),
+        meta = {"full_sampler": any(r.params.needs_full_sampler for r in sample_reqs),
+                "nd": nd, "maxb": maxb, "splits": splits, "kps": kps, "npf": len(pf),
                 "use_lora": use_lora, "T": T, "ft_rows": sum(s.num_new for s in out.ft),
                 "ft_dst": ft_dst}
         return meta, pk, sample_reqs
@@ -453,9 +455,21 @@ class ModelRunner:
         sd = torch.tensor([(r.params.seed if r.params.seed is not None else r.seq_no) * 1000003
                            + len(r.output_ids) for r in reqs], dtype=torch.int64)
         toks = torch.empty(R, dtype=torch.int64, device=logits.device)
-        ops.sample(logits, t.to(logits.device, non_blocking=True), sd.to(logits.device, non_blocking=True),
-                   toks)
+        dev = logits.device
+        topk = topp = lps = None
+        if any(r.params.needs_full_sampler for r in reqs):
+            topk = torch.tensor([r.params.top_k for r in reqs], dtype=torch.int32).to(dev, non_blocking=True)
+            topp = torch.tensor([r.params.top_p for r in reqs], dtype=torch.float32).to(dev, non_blocking=True)
+            if any(r.params.logprobs for r in reqs):
+                lps = torch.empty(R, dtype=torch.float32, device=dev)
+            self.last_h2d_bytes += R * 8
+        ops.sample(logits, t.to(dev, non_blocking=True), sd.to(dev, non_blocking=True), toks, topk, topp, lps)
         host = toks.cpu()
         self.last_h2d_bytes += R * 12
         self.last_d2h_bytes = R * 8
+        if lps is not None:
+            for r, v in zip(reqs, lps.cpu().tolist()):
+                if r.params.logprobs:
+                    r.output_logprobs.append(float(v))
+            self.last_d2h_bytes += R * 4
         return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}

@@ -22,6 +22,14 @@ class SamplingParams:
     seed: int | None = None
     ignore_eos: bool = True
     stop_token_ids: tuple[int, ...] = ()
+    top_k: int = 0                   # 0 = off
+    top_p: float = 1.0               # 1 = off
+    logprobs: bool = False           # record the chosen token's log-probability
+    stop: tuple[str, ...] = ()       # stop strings (checked on the decoded output)
+
+    @property
+    def needs_full_sampler(self) -> bool:
+        return self.top_k > 0 or self.top_p < 1.0 or self.logprobs
 
 
 _counter = itertools.count()
@@ -41,6 +49,8 @@ class Request:
     # -- runtime state --------------------------------------------------
     status: Status = Status.WAITING
     output_ids: list[int] = field(default_factory=list)
+    output_logprobs: list[float] = field(default_factory=list)
+    stop_reason: str | None = None   # the stop string that ended the request
     num_computed: int = 0            # tokens whose KV is in the cache
     block_ids: list[int] = field(default_factory=list)
     lora_slot: int = -1

@@ -263,6 +263,17 @@ class Scheduler:
             budget -= n
         return out
 
+    def finish(self, req: Request, now: float | None = None) -> None:
+        """End a running request early (a stop string matched)."""
+        if req in self.running:
+            self.running.remove(req)
+        req.status = Status.FINISHED
+        req.finish_time = time.perf_counter() if now is None else now
+        if self.caching:
+            self._register(req)
+        self._free(req)
+        self.finished.append(req)
+
     def add_ft(self, out: SchedulerOutput, reqs: list[Request]) -> list[Request]:
         """Append whole FT samples to ``out``; returns the ones that did not fit
         (token budget or pages) so the caller can release them."""

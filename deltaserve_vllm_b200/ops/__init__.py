@@ -296,9 +296,15 @@ def swiglu_bwd(gu, dact, dgu, act=None):
     ref.swiglu_bwd(gu, dact, dgu, act)
 
 
-def sample(logits, temps, seeds, out):
+def sample(logits, temps, seeds, out, top_k=None, top_p=None, logprobs=None):
+    """One token per row of fp32 ``logits``: greedy where ``temps`` <= 0, else
+    Gumbel-max at the row's temperature (counter-based noise from ``seeds``),
+    optionally restricted to the ``top_k`` largest logits (int32 per row, 0 =
+    off) and then to the top-``top_p`` probability mass (fp32 per row, 1 =
+    off). ``logprobs`` (fp32 per row) receives the chosen token's raw
+    log-softmax."""
     if logits.is_cuda:
-        _native().sample(logits, temps, seeds, out)
+        _native().sample(logits, temps, seeds, out, top_k, top_p, logprobs)
         return out
-    ref.sample(logits, temps, seeds, out)
+    ref.sample(logits, temps, seeds, out, top_k, top_p, logprobs)
     return out

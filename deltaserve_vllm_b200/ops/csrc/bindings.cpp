@@ -54,7 +54,9 @@ void dsv_adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor 
                double b2, double eps, double wd, int64_t step);
 void dsv_lora_publish(torch::Tensor A_src, torch::Tensor A_dst, torch::Tensor Bt_src, torch::Tensor B2_dst,
                       int64_t col0, int64_t b1, int64_t b2, bool interleave64, double scale);
-void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out);
+void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out,
+                c10::optional<torch::Tensor> topk, c10::optional<torch::Tensor> topp,
+                c10::optional<torch::Tensor> logprobs);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &dsv_gemm, "tcgen05 GEMM with fused epilogues / LoRA expand");

@@ -292,24 +292,115 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
-// One CTA per row: greedy (temperature <= 0) or Gumbel-max sampling at the
-// row's temperature.
+// Block-wide sum (1024 threads) through a 32-entry shared scratch; every
+// thread gets the total.
+template <typename T>
+__device__ __forceinline__ T block_sum_1024(T v, T* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+  __syncthreads();
+  T t = 0;
+  for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += red[w];
+  return t;
+}
+
+// One CTA (1024 threads) per row: greedy (temperature <= 0) or Gumbel-max
+// sampling at the row's temperature, optionally restricted to the top-k
+// tokens and then to the smallest top set whose renormalised probability
+// reaches top-p (thresholds found by bisection on the scaled logits, one
+// pass over the row per step). Optionally the chosen token's log-probability
+// under the raw logits (log_softmax) is written to logprob_out.
 __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, const float* __restrict__ temps,
-                              const int64_t* __restrict__ seeds, int64_t* out, int V) {
+                              const int64_t* __restrict__ seeds, int64_t* out, int V,
+                              const int* __restrict__ topk, const float* __restrict__ topp,
+                              float* __restrict__ logprob_out) {
   __shared__ float bv[32];
   __shared__ int bi[32];
+  __shared__ float redf[32];
+  __shared__ int redi[32];
   const int r = blockIdx.x;
   const float* lr = logits + (size_t)r * sl;
   const float t = temps[r];
   const uint64_t seed = (uint64_t)seeds[r];
+  const int k = topk != nullptr ? topk[r] : 0;
+  const float p = topp != nullptr ? topp[r] : 1.f;
+  const float inv_t = t > 0.f ? 1.f / t : 1.f;
+  // Row max / min of the (scaled) logits: the bisection range and the softmax shift.
+  float zmax, zmin;
+  {
+    float m = -INFINITY, n = INFINITY;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float z = lr[i] * inv_t;
+      m = fmaxf(m, z);
+      n = fminf(n, z);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      n = fminf(n, __shfl_xor_sync(0xffffffffu, n, o));
+    }
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) {
+      bv[threadIdx.x / 32] = m;
+      redf[threadIdx.x / 32] = n;
+    }
+    __syncthreads();
+    m = -INFINITY;
+    n = INFINITY;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) {
+      m = fmaxf(m, bv[w]);
+      n = fminf(n, redf[w]);
+    }
+    zmax = m;
+    zmin = n;
+  }
+  float thr = -INFINITY;  // keep tokens whose scaled logit >= thr
+  if (t > 0.f && ((k > 0 && k < V) || p < 1.f)) {
+    if (k > 0 && k < V) {
+      float lo = zmin, hi = zmax;  // invariant: count(z >= lo) >= k
+      for (int it = 0; it < 40; ++it) {
+        const float mid = 0.5f * (lo + hi);
+        int c = 0;
+        for (int i = threadIdx.x; i < V; i += blockDim.x) c += (lr[i] * inv_t >= mid);
+        c = block_sum_1024(c, redi);
+        if (c >= k) lo = mid;
+        else hi = mid;
+      }
+      thr = lo;
+    }
+    if (p < 1.f) {
+      float zsum = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float z = lr[i] * inv_t;
+        if (z >= thr) zsum += __expf(z - zmax);
+      }
+      zsum = block_sum_1024(zsum, redf);
+      float lo = fmaxf(thr, zmin), hi = zmax;  // invariant: mass(z >= lo) >= p
+      for (int it = 0; it < 40; ++it) {
+        const float mid = 0.5f * (lo + hi);
+        float m = 0.f;
+        for (int i = threadIdx.x; i < V; i += blockDim.x) {
+          const float z = lr[i] * inv_t;
+          if (z >= mid && z >= thr) m += __expf(z - zmax);
+        }
+        m = block_sum_1024(m, redf);
+        if (m >= p * zsum) lo = mid;
+        else hi = mid;
+      }
+      thr = fmaxf(thr, lo);
+    }
+  }
   float best = -INFINITY;
   int arg = 0;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     float v = lr[i];
     if (t > 0.f) {
+      if (v * inv_t < thr) continue;
       const uint64_t h = mix64(seed * 0x100000001B3ull + (uint64_t)i);
       const float u = ((h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
-      v = v / t - __logf(-__logf(u));
+      v = v * inv_t - __logf(-__logf(u));
     }
     if (v > best) {
       best = v;
@@ -324,6 +415,7 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
       arg = oi;
     }
   }
+  __syncthreads();
   if (threadIdx.x % 32 == 0) {
     bv[threadIdx.x / 32] = best;
     bi[threadIdx.x / 32] = arg;
@@ -336,6 +428,24 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
         arg = bi[w];
       }
     out[r] = arg;
+    bi[0] = arg;
+  }
+  if (logprob_out != nullptr) {
+    __syncthreads();
+    const int chosen = bi[0];
+    float mraw = -INFINITY;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) mraw = fmaxf(mraw, lr[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mraw = fmaxf(mraw, __shfl_xor_sync(0xffffffffu, mraw, o));
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) bv[threadIdx.x / 32] = mraw;
+    __syncthreads();
+    mraw = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) mraw = fmaxf(mraw, bv[w]);
+    float se = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) se += __expf(lr[i] - mraw);
+    se = block_sum_1024(se, redf);
+    if (threadIdx.x == 0) logprob_out[r] = lr[chosen] - mraw - __logf(se);
   }
 }
 
@@ -441,12 +551,22 @@ void dsv_lora_publish(torch::Tensor A_src, torch::Tensor A_dst, torch::Tensor Bt
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out) {
+void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, torch::Tensor out,
+                c10::optional<torch::Tensor> topk, c10::optional<torch::Tensor> topp,
+                c10::optional<torch::Tensor> logprobs) {
   const int R = (int)logits.size(0);
   if (R == 0) return;
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "sample: fp32 logits rows");
+  if (topk.has_value())
+    TORCH_CHECK(topk->scalar_type() == at::kInt && topk->numel() >= R, "sample: top_k must be int32 [R]");
+  if (topp.has_value())
+    TORCH_CHECK(topp->scalar_type() == at::kFloat && topp->numel() >= R, "sample: top_p must be fp32 [R]");
+  if (logprobs.has_value())
+    TORCH_CHECK(logprobs->scalar_type() == at::kFloat && logprobs->numel() >= R, "sample: logprobs fp32 [R]");
   c10::cuda::CUDAGuard guard(logits.device());
   dsv::sample_kernel<<<R, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), logits.stride(0), temps.data_ptr<float>(), seeds.data_ptr<int64_t>(),
-      out.data_ptr<int64_t>(), (int)logits.size(1));
+      out.data_ptr<int64_t>(), (int)logits.size(1), topk.has_value() ? topk->data_ptr<int>() : nullptr,
+      topp.has_value() ? topp->data_ptr<float>() : nullptr, logprobs.has_value() ? logprobs->data_ptr<float>() : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

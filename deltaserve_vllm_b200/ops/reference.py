@@ -211,19 +211,42 @@ def lora_publish(A_src, A_dst, Bt_src, B2_dst, col0, b1, b2, interleave, scale):
     B2_dst[n[:, None], cols] = vals
 
 
-def sample(logits, temps, seeds, out):
-    # The CPU path is greedy-only for temperature <= 0 and uses torch's RNG
+def sample_keep_mask(z: torch.Tensor, k: int, p: float) -> torch.Tensor:
+    """Tokens kept by top-k then top-p on scaled logits ``z`` (one row)."""
+    keep = torch.ones_like(z, dtype=torch.bool)
+    if 0 < k < z.numel():
+        keep &= z >= torch.topk(z, k).values[-1]
+    if p < 1.0:
+        zs = torch.where(keep, z, torch.full_like(z, float("-inf")))
+        order = torch.argsort(zs, descending=True)
+        probs = torch.softmax(zs[order], -1)
+        cum = torch.cumsum(probs, -1)
+        n_keep = int((cum < p).sum()) + 1               # up to and including the token crossing p
+        thr = zs[order[min(n_keep, z.numel()) - 1]]
+        keep &= z >= thr
+    return keep
+
+
+def sample(logits, temps, seeds, out, top_k=None, top_p=None, logprobs=None):
+    # The CPU path is greedy for temperature <= 0 and uses torch's RNG
     # otherwise (the GPU kernel uses a counter-based hash per row).
     lf = logits.float()
-    greedy = lf.argmax(-1)
-    res = greedy.clone()
+    res = lf.argmax(-1)
     for r in range(lf.shape[0]):
         t = float(temps[r])
         if t > 0:
             gen = torch.Generator().manual_seed(int(seeds[r]))
             u = torch.rand(lf.shape[1], generator=gen).clamp(1e-7, 1 - 1e-7)
-            res[r] = (lf[r] / t - torch.log(-torch.log(u))).argmax()
+            z = lf[r] / t
+            k = int(top_k[r]) if top_k is not None else 0
+            p = float(top_p[r]) if top_p is not None else 1.0
+            g = z - torch.log(-torch.log(u))
+            g = torch.where(sample_keep_mask(z, k, p), g, torch.full_like(g, float("-inf")))
+            res[r] = g.argmax()
     out.copy_(res)
+    if logprobs is not None:
+        lp = torch.log_softmax(lf, -1).gather(1, res.view(-1, 1)).view(-1)
+        logprobs.copy_(lp)
 
 
 def rms_norm_bwd(x, dy, w, eps, add=None, out=None, out_bf16=None):

@@ -62,7 +62,50 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     if tok is None:
         from ..utils.tokenizer import ByteTokenizer
         tok = ByteTokenizer(engine.arch.vocab)
+    if engine.tokenizer is None:
+        engine.tokenizer = tok        # stop strings are matched on decoded text
     route_name = engine.rcfg.route_model_name if engine.router is not None else None
+
+    def _choice(index: int, r) -> dict:
+        text = tok.decode(r.output_ids)
+        if r.stop_reason:
+            text = text[:text.find(r.stop_reason)] if r.stop_reason in text else text
+        c = {"index": index, "text": text, "token_ids": r.output_ids, "finish_reason": _finish_reason(r)}
+        if r.params.logprobs:
+            c["logprobs"] = {"tokens": [tok.decode([t]) for t in r.output_ids],
+                             "token_logprobs": list(r.output_logprobs[:len(r.output_ids)])}
+        return c
+
+    async def _completions_n(body, ids, params, n, model):
+        """``n`` independent completions of one prompt (seeds seed, seed+1, ...)."""
+        import dataclasses as _dc
+        model_adapter = None if model == model_name else model
+        if model_adapter is not None and model_adapter not in engine.adapter_slots:
+            return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
+        base_seed = params.seed if params.seed is not None else int(uuid.uuid4().int % (1 << 31))
+        rids, waits = [], []
+        for i in range(n):
+            rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+            p = _dc.replace(params, seed=base_seed + i)
+            waits.append(et.register(rid, False))
+            rids.append(rid)
+            try:
+                await et.call(lambda e, rid=rid, p=p: e.add_request(rid, ids, p, model_adapter))
+            except Exception as e:
+                for x in rids:
+                    et.unregister(x)
+                return JSONResponse(status_code=400, content={"error": str(e)})
+        et.notify_arrival()
+        try:
+            reqs = [await w.done for w in waits]
+        finally:
+            for x in rids:
+                et.unregister(x)
+        ntok = sum(len(r.output_ids) for r in reqs)
+        return JSONResponse(content={
+            "id": rids[0], "object": "text_completion", "created": int(time.time()), "model": model,
+            "choices": [_choice(i, r) for i, r in enumerate(reqs)],
+            "usage": {"prompt_tokens": len(ids), "completion_tokens": ntok, "total_tokens": len(ids) * n + ntok}})
 
     async def body_of(req: Request) -> dict:
         try:
@@ -102,10 +145,27 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         if not ids:
             return JSONResponse(status_code=400, content={"error": "empty prompt"})
         model = body.get("model") or model_name
-        params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
-                                temperature=float(body.get("temperature", 0.0) or 0.0),
-                                seed=body.get("seed"), ignore_eos=bool(body.get("ignore_eos", False)),
-                                stop_token_ids=tuple(body.get("stop_token_ids") or ()))
+        stop = body.get("stop") or ()
+        if isinstance(stop, str):
+            stop = (stop,)
+        try:
+            n_choices = int(body.get("n", 1) or 1)
+            params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
+                                    temperature=float(body.get("temperature", 0.0) or 0.0),
+                                    seed=body.get("seed"), ignore_eos=bool(body.get("ignore_eos", False)),
+                                    stop_token_ids=tuple(body.get("stop_token_ids") or ()),
+                                    top_k=max(0, int(body.get("top_k", 0) or 0)),
+                                    top_p=float(body.get("top_p", 1.0) if body.get("top_p") is not None else 1.0),
+                                    logprobs=body.get("logprobs") is not None,
+                                    stop=tuple(str(x) for x in stop))
+        except (TypeError, ValueError) as e:
+            return JSONResponse(status_code=400, content={"error": f"bad sampling parameter: {e}"})
+        if not 0.0 < params.top_p <= 1.0:
+            return JSONResponse(status_code=400, content={"error": "top_p must be in (0, 1]"})
+        if n_choices > 1:
+            if bool(body.get("stream", False)):
+                return JSONResponse(status_code=400, content={"error": "n > 1 is not supported with stream"})
+            return await _completions_n(body, ids, params, n_choices, model)
         rid = f"cmpl-{uuid.uuid4().hex[:24]}"
         stream = bool(body.get("stream", False))
         router = engine.router
@@ -163,8 +223,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         finally:
             et.unregister(rid)
         out = {"id": rid, "object": "text_completion", "created": created, "model": model,
-               "choices": [{"index": 0, "text": tok.decode(r.output_ids), "token_ids": r.output_ids,
-                            "finish_reason": _finish_reason(r)}],
+               "choices": [_choice(0, r)],
                "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),
                          "total_tokens": r.num_prompt + len(r.output_ids)},
                "metrics": {"ttft_s": r.ttft(), "tbt_mean_s": (sum(r.tbts()) / len(r.tbts()))
@@ -360,4 +419,6 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
 def _finish_reason(r) -> str:
     if r.status.name == "ABORTED":
         return "abort"
+    if getattr(r, "stop_reason", None):
+        return "stop"
     return "length" if len(r.output_ids) >= r.params.max_tokens else "stop"

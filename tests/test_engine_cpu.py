@@ -220,3 +220,28 @@ def test_prefix_caching_engine_adapters_versions_and_ft():
         assert all(r.num_cached_tokens == 0 for r in ft_reqs)
         assert sched.cache_stats()["hit_pages"] >= 10
         assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+
+
+def test_stop_strings_end_requests():
+    class LetterTok:
+        def encode(self, text, add_special_tokens=False):
+            return [ord(c) % 1024 for c in text]
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(65 + int(i) % 26) for i in ids)
+
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp, start_on_launch=False)
+        eng.tokenizer = LetterTok()
+        eng.add_request("full", [5, 6, 7, 8], SamplingParams(max_tokens=10))
+        eng.run_until_idle(max_steps=200)
+        full = eng.finished[-1]
+        text = eng.tokenizer.decode(full.output_ids)
+        stop = text[3:5]
+        eng.add_request("cut", [5, 6, 7, 8], SamplingParams(max_tokens=10, stop=(stop,)))
+        eng.run_until_idle(max_steps=200)
+        cut = eng.finished[-1]
+        assert cut.stop_reason == stop
+        k = text.find(stop)
+        assert cut.output_ids == full.output_ids[:k + len(stop)]   # ended on the token completing the match
+        assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks

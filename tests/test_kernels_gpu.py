@@ -458,6 +458,33 @@ def test_sample_greedy():
     assert ((out >= 0) & (out < 30000)).all()
 
 
+def test_sample_topk_topp_logprobs():
+    """Top-k / top-p restricted sampling: every sampled token lies in the kept
+    set of the reference rules; top_k = 1 is the argmax; the log-probability
+    is the chosen token's raw log-softmax."""
+    R, V = 48, 32000
+    logits = rnd(R, V, scale=3.0, dtype=torch.float32, seed=90)
+    g = torch.Generator().manual_seed(91)
+    topk = torch.randint(0, 60, (R,), generator=g).to(torch.int32)
+    topk[:4] = 1
+    topp = (torch.rand(R, generator=g) * 0.9 + 0.1)
+    topp[4:8] = 1.0
+    temps = torch.rand(R, generator=g) * 1.5 + 0.3
+    out = torch.empty(R, dtype=torch.int64, device=DEV)
+    lps = torch.empty(R, device=DEV)
+    for trial in range(3):
+        seeds = torch.arange(R, device=DEV) * 7919 + trial
+        ops.sample(logits, temps.to(DEV), seeds, out, top_k=topk.to(DEV), top_p=topp.to(DEV), logprobs=lps)
+        lc, oc = logits.cpu(), out.cpu()
+        for r in range(R):
+            z = lc[r] / float(temps[r])
+            keep = ref.sample_keep_mask(z, int(topk[r]), min(1.0, float(topp[r]) + 1e-4))
+            assert keep[oc[r]], (r, int(topk[r]), float(topp[r]))
+        assert torch.equal(oc[:4], lc[:4].argmax(-1))
+        exp_lp = torch.log_softmax(lc, -1).gather(1, oc.view(-1, 1)).view(-1)
+        torch.testing.assert_close(lps.cpu(), exp_lp, rtol=1e-4, atol=1e-4)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 6144, 4096), (64, 4096, 14336), (100, 1024, 2048)])
 def test_gemm_splitk_decode_shapes(M, N, K):
     a, b = rnd(M, K, seed=31), rnd(N, K, scale=0.05, seed=32)

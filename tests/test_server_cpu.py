@@ -194,3 +194,34 @@ def test_toy_adapter_builder(tmp_path):
     lines = open(os.path.join(out, "toy-01", "data.txt")).read().splitlines()
     assert len(lines) == 96 and all(line.endswith(")") for line in lines)
     assert toy.topic_corpus(0)[0] != toy.topic_corpus(1)[0]
+
+
+
+def test_api_sampling_options_stop_n_logprobs():
+    """OpenAI sampling options: top_k / top_p (kept-set sampling), logprobs of
+    the chosen tokens, stop strings (output cut before the match), n > 1."""
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        app = create_app(eng)
+        with TestClient(app) as c:
+            r = c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 6, "temperature": 1.0,
+                                                "top_k": 1, "seed": 3, "logprobs": 0}).json()
+            g = c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 6}).json()
+            # top_k = 1 leaves only the argmax: equal to greedy whatever the noise
+            assert r["choices"][0]["token_ids"] == g["choices"][0]["token_ids"]
+            lps = r["choices"][0]["logprobs"]["token_logprobs"]
+            assert len(lps) == 6 and all(x <= 0.0 for x in lps)
+            many = c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 5, "temperature": 1.5,
+                                                   "top_p": 0.9, "n": 3, "seed": 7}).json()
+            assert [ch["index"] for ch in many["choices"]] == [0, 1, 2]
+            assert many["usage"]["completion_tokens"] == 15
+            # stop string: the text of the greedy continuation, from its second token on
+            full = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 8}).json()["choices"][0]
+            ids = full["token_ids"]
+            stop_text = eng.tokenizer.decode(ids[2:4])
+            if stop_text:
+                st = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 8,
+                                                     "stop": [stop_text]}).json()["choices"][0]
+                assert st["finish_reason"] == "stop"
+                assert stop_text not in st["text"] and len(st["token_ids"]) <= 4
+            assert c.post("/v1/completions", json={"prompt": "x", "top_p": 0}).status_code == 400
