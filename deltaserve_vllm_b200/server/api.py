@@ -66,17 +66,24 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         engine.tokenizer = tok        # stop strings are matched on decoded text
     route_name = engine.rcfg.route_model_name if engine.router is not None else None
 
-    def _choice(index: int, r) -> dict:
+    def _choice(index: int, r, chat: bool = False) -> dict:
         text = tok.decode(r.output_ids)
         if r.stop_reason:
             text = text[:text.find(r.stop_reason)] if r.stop_reason in text else text
+        if chat:
+            c = {"index": index, "message": {"role": "assistant", "content": text},
+                 "finish_reason": _finish_reason(r)}
+            if r.params.logprobs:
+                c["logprobs"] = {"content": [{"token": tok.decode([t]), "logprob": lp}
+                                             for t, lp in zip(r.output_ids, r.output_logprobs)]}
+            return c
         c = {"index": index, "text": text, "token_ids": r.output_ids, "finish_reason": _finish_reason(r)}
         if r.params.logprobs:
             c["logprobs"] = {"tokens": [tok.decode([t]) for t in r.output_ids],
                              "token_logprobs": list(r.output_logprobs[:len(r.output_ids)])}
         return c
 
-    async def _completions_n(body, ids, params, n, model):
+    async def _completions_n(body, ids, params, n, model, chat=False):
         """``n`` independent completions of one prompt (seeds seed, seed+1, ...)."""
         import dataclasses as _dc
         model_adapter = None if model == model_name else model
@@ -103,8 +110,9 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                 et.unregister(x)
         ntok = sum(len(r.output_ids) for r in reqs)
         return JSONResponse(content={
-            "id": rids[0], "object": "text_completion", "created": int(time.time()), "model": model,
-            "choices": [_choice(i, r) for i, r in enumerate(reqs)],
+            "id": rids[0], "object": "chat.completion" if chat else "text_completion",
+            "created": int(time.time()), "model": model,
+            "choices": [_choice(i, r, chat) for i, r in enumerate(reqs)],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": ntok, "total_tokens": len(ids) * n + ntok}})
 
     async def body_of(req: Request) -> dict:
@@ -128,46 +136,56 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         return {"object": "list", "data": [{"id": n, "object": "model", "owned_by": "deltaserve"}
                                            for n in names]}
 
-    @app.post("/v1/completions")
-    async def completions(req: Request):
-        body = await body_of(req)
-        prompt = body.get("prompt")
-        if prompt is None:
-            return JSONResponse(status_code=400, content={"error": "prompt is required"})
-        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
-            ids = [int(t) for t in prompt]
-        elif isinstance(prompt, list):
-            if len(prompt) != 1:
-                return JSONResponse(status_code=400, content={"error": "one prompt per request"})
-            ids = tok.encode(str(prompt[0]))
-        else:
-            ids = tok.encode(str(prompt))
-        if not ids:
-            return JSONResponse(status_code=400, content={"error": "empty prompt"})
-        model = body.get("model") or model_name
+    def _parse_params(body: dict):
+        """SamplingParams and n of an OpenAI request body (or an error response)."""
         stop = body.get("stop") or ()
         if isinstance(stop, str):
             stop = (stop,)
         try:
             n_choices = int(body.get("n", 1) or 1)
-            params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
+            max_tokens = body.get("max_tokens", body.get("max_completion_tokens", 16))
+            params = SamplingParams(max_tokens=int(max_tokens if max_tokens is not None else 16),
                                     temperature=float(body.get("temperature", 0.0) or 0.0),
                                     seed=body.get("seed"), ignore_eos=bool(body.get("ignore_eos", False)),
                                     stop_token_ids=tuple(body.get("stop_token_ids") or ()),
                                     top_k=max(0, int(body.get("top_k", 0) or 0)),
                                     top_p=float(body.get("top_p", 1.0) if body.get("top_p") is not None else 1.0),
-                                    logprobs=body.get("logprobs") is not None,
+                                    logprobs=bool(body.get("logprobs") is not None and body.get("logprobs") is not False),
                                     stop=tuple(str(x) for x in stop))
         except (TypeError, ValueError) as e:
-            return JSONResponse(status_code=400, content={"error": f"bad sampling parameter: {e}"})
+            return None, 0, JSONResponse(status_code=400, content={"error": f"bad sampling parameter: {e}"})
         if not 0.0 < params.top_p <= 1.0:
-            return JSONResponse(status_code=400, content={"error": "top_p must be in (0, 1]"})
-        if n_choices > 1:
-            if bool(body.get("stream", False)):
-                return JSONResponse(status_code=400, content={"error": "n > 1 is not supported with stream"})
-            return await _completions_n(body, ids, params, n_choices, model)
-        rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+            return None, 0, JSONResponse(status_code=400, content={"error": "top_p must be in (0, 1]"})
+        if n_choices < 1:
+            return None, 0, JSONResponse(status_code=400, content={"error": "n must be >= 1"})
+        return params, n_choices, None
+
+    def _chat_prompt(messages) -> list[int]:
+        """Token ids of a chat: the tokenizer's chat template when it has one,
+        else a plain role-tagged transcript ending with the assistant turn."""
+        apply = getattr(tok, "apply_chat_template", None)
+        if apply is not None:
+            try:
+                out = apply(messages, add_generation_prompt=True, tokenize=True)
+                if isinstance(out, dict):
+                    out = out.get("input_ids")
+                return [int(t) for t in out]
+            except Exception:
+                pass
+        text = "".join(f"<|{m.get('role', 'user')}|>\n{m.get('content', '')}\n" for m in messages)
+        return tok.encode(text + "<|assistant|>\n")
+
+    async def _generate(body: dict, ids: list[int], chat: bool):
+        params, n_choices, err = _parse_params(body)
+        if err is not None:
+            return err
+        model = body.get("model") or model_name
         stream = bool(body.get("stream", False))
+        if n_choices > 1:
+            if stream:
+                return JSONResponse(status_code=400, content={"error": "n > 1 is not supported with stream"})
+            return await _completions_n(body, ids, params, n_choices, model, chat)
+        rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:24]}"
         router = engine.router
         headers = {}
         routed = named_pool = False
@@ -200,20 +218,31 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             et.unregister(rid)
             return JSONResponse(status_code=400, content={"error": str(e)})
         created = int(time.time())
+        obj = "chat.completion" if chat else "text_completion"
         if stream:
             async def gen():
                 try:
+                    first = True
                     while True:
                         toks = await w.tokens.get()
                         if toks is None:
                             break
-                        chunk = {"id": rid, "object": "text_completion", "created": created,
-                                 "model": model, "choices": [{"index": 0, "text": tok.decode(toks),
-                                                              "token_ids": toks, "finish_reason": None}]}
+                        if chat:
+                            delta = {"content": tok.decode(toks)}
+                            if first:
+                                delta["role"] = "assistant"
+                            ch = {"index": 0, "delta": delta, "finish_reason": None}
+                        else:
+                            ch = {"index": 0, "text": tok.decode(toks), "token_ids": toks, "finish_reason": None}
+                        first = False
+                        chunk = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
+                                 "model": model, "choices": [ch]}
                         yield f"data: {json.dumps(chunk)}\n\n"
                     r = await w.done
-                    fin = {"id": rid, "object": "text_completion", "created": created, "model": model,
-                           "choices": [{"index": 0, "text": "", "finish_reason": _finish_reason(r)}]}
+                    last = ({"index": 0, "delta": {}, "finish_reason": _finish_reason(r)} if chat else
+                            {"index": 0, "text": "", "finish_reason": _finish_reason(r)})
+                    fin = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
+                           "model": model, "choices": [last]}
                     yield f"data: {json.dumps(fin)}\n\ndata: [DONE]\n\n"
                 finally:
                     et.unregister(rid)
@@ -222,13 +251,42 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             r = await w.done
         finally:
             et.unregister(rid)
-        out = {"id": rid, "object": "text_completion", "created": created, "model": model,
-               "choices": [_choice(0, r)],
+        out = {"id": rid, "object": obj, "created": created, "model": model,
+               "choices": [_choice(0, r, chat)],
                "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),
                          "total_tokens": r.num_prompt + len(r.output_ids)},
                "metrics": {"ttft_s": r.ttft(), "tbt_mean_s": (sum(r.tbts()) / len(r.tbts()))
                            if r.tbts() else None}}
         return JSONResponse(content=out, headers=headers)
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await body_of(req)
+        prompt = body.get("prompt")
+        if prompt is None:
+            return JSONResponse(status_code=400, content={"error": "prompt is required"})
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            ids = [int(t) for t in prompt]
+        elif isinstance(prompt, list):
+            if len(prompt) != 1:
+                return JSONResponse(status_code=400, content={"error": "one prompt per request"})
+            ids = tok.encode(str(prompt[0]))
+        else:
+            ids = tok.encode(str(prompt))
+        if not ids:
+            return JSONResponse(status_code=400, content={"error": "empty prompt"})
+        return await _generate(body, ids, chat=False)
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(req: Request):
+        body = await body_of(req)
+        messages = body.get("messages")
+        if not isinstance(messages, list) or not messages:
+            return JSONResponse(status_code=400, content={"error": "messages is required"})
+        ids = _chat_prompt(messages)
+        if not ids:
+            return JSONResponse(status_code=400, content={"error": "empty prompt"})
+        return await _generate(body, ids, chat=True)
 
     # ------------------------------------------------------------ finetuning
     @app.post("/start_finetuning")

@@ -225,3 +225,29 @@ def test_api_sampling_options_stop_n_logprobs():
                 assert st["finish_reason"] == "stop"
                 assert stop_text not in st["text"] and len(st["token_ids"]) <= 4
             assert c.post("/v1/completions", json={"prompt": "x", "top_p": 0}).status_code == 400
+
+
+def test_api_chat_completions():
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = make_engine(tmp)
+        app = create_app(eng)
+        with TestClient(app) as c:
+            msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+            r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 4})
+            assert r.status_code == 200, r.text
+            out = r.json()
+            assert out["object"] == "chat.completion"
+            assert out["choices"][0]["message"]["role"] == "assistant"
+            assert out["usage"]["completion_tokens"] == 4
+            with c.stream("POST", "/v1/chat/completions",
+                          json={"messages": msgs, "max_tokens": 3, "stream": True}) as s:
+                lines = [ln for ln in s.iter_lines() if ln.startswith("data: ")]
+            assert lines[-1] == "data: [DONE]"
+            chunks = [json.loads(ln[6:]) for ln in lines[:-1]]
+            assert chunks[0]["object"] == "chat.completion.chunk"
+            assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+            assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+            two = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "n": 2,
+                                                       "temperature": 1.0, "logprobs": True}).json()
+            assert len(two["choices"]) == 2 and len(two["choices"][1]["logprobs"]["content"]) == 2
+            assert c.post("/v1/chat/completions", json={"max_tokens": 2}).status_code == 400
