@@ -61,6 +61,9 @@ PRESETS: dict[str, ModelArch] = {
                             rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True),
     "llama3-tiny": ModelArch("llama3-tiny", "llama", 2, 256, 4, 2, 64, 512, 1024,
                              rms_eps=1e-5, rope_theta=5e5),
+    # Tiny GQA model whose heads split over 4 tensor-parallel ranks (CPU rank tests).
+    "llama3-tiny-kv4": ModelArch("llama3-tiny-kv4", "llama", 2, 256, 8, 4, 32, 1024, 1024,
+                                 rms_eps=1e-5, rope_theta=5e5),
     # Small head_dim-128 models for GPU tests of the full engine path.
     "qwen3-test": ModelArch("qwen3-test", "qwen3", 2, 512, 4, 2, 128, 1024, 4096,
                             rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True),

@@ -8,6 +8,7 @@ import socket
 import tempfile
 from datetime import timedelta
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -21,7 +22,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, model="qwen3-tiny"):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world, timeout=timedelta(seconds=60))
     from deltaserve_vllm_b200.config import EngineConfig, FinetuneConfig
@@ -30,7 +31,7 @@ def _worker(rank, world, port, outdir):
     from deltaserve_vllm_b200.engine.request import SamplingParams
     from deltaserve_vllm_b200.parallel.comm import TPComm
     comm = TPComm()
-    ecfg = EngineConfig(model="qwen3-tiny", device="cpu", tensor_parallel_size=world, max_model_len=512,
+    ecfg = EngineConfig(model=model, device="cpu", tensor_parallel_size=world, max_model_len=512,
                         block_size=16, max_num_batched_tokens=256, max_loras=2, max_lora_rank=8)
     fcfg = FinetuneConfig(enable_finetuning=True, max_saved_finetuning_tokens=96, learning_rate=1e-3)
     store = FinetuningStore.synthetic(1024, 10, 16, 40, seed=0, max_saved_finetuning_tokens=96)
@@ -65,19 +66,20 @@ def _worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-def test_tp2_engine_protocol_gloo():
+@pytest.mark.parametrize("model,world", [("qwen3-tiny", 2), ("llama3-tiny-kv4", 4)])
+def test_tp_engine_protocol_gloo(model, world):
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_worker, args=(world, _port(), d, model), nprocs=world, join=True, start_method="spawn")
         r = torch.load(os.path.join(d, "res.pt"))
         assert r["cycles"] >= 2
         assert all(l == l for l in r["losses"])
         assert r["outs"] == [4] * 5
-        assert len(r["regions"]) == 2
+        assert len(r["regions"]) == world
         assert r["t0"] == [3]
         from deltaserve_vllm_b200.adapters import peft_io
         tensors, cfg = peft_io.read_adapter(r["ck"])
         from deltaserve_vllm_b200.models.configs import resolve_arch
-        arch = resolve_arch("qwen3-tiny")
+        arch = resolve_arch(model)
         assert len(tensors) == 2 * 7 * arch.num_layers
         q_b = [v for k, v in tensors.items() if "q_proj.lora_B" in k][0]
         assert q_b.shape[0] == arch.num_heads * arch.head_dim      # merged across ranks

@@ -51,14 +51,14 @@ def _worker(rank, world, port, name, outdir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name", ["qwen3-tiny", "llama3-tiny"])
-def test_tp2_gloo_matches_autograd_and_peft_roundtrip(name):
+@pytest.mark.parametrize("name,world", [("qwen3-tiny", 2), ("llama3-tiny", 2), ("llama3-tiny-kv4", 4)])
+def test_tp_gloo_matches_autograd_and_peft_roundtrip(name, world):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     from lora_harness import autograd_reference, config1_data
     arch = PRESETS[name]
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(2, _port(), name, d), nprocs=2, join=True,
+        mp.start_processes(_worker, args=(world, _port(), name, d), nprocs=world, join=True,
                            start_method="spawn")
         r0 = torch.load(os.path.join(d, "r0.pt"))
         ad = random_adapter(arch, 8, seed=7, b_std=0.01)
