@@ -137,6 +137,13 @@ class CoServingEngine:
             self.bwd_comm = TPComm(dist.new_group(list(range(comm.size))), comm.cpu_group)
         self._actions: list = []
         self._actions_lock = threading.Lock()
+        # Step plans reach the follower ranks through shared memory (a memory
+        # copy per step); DSERVE_TP_PLAN_CHANNEL=gloo sends them through the
+        # process group instead.
+        self.plan_chan = None
+        if comm is not None and comm.size > 1 and os.environ.get("DSERVE_TP_PLAN_CHANNEL", "shm") == "shm":
+            from ..parallel.shm_channel import ShmChannel
+            self.plan_chan = ShmChannel(comm)
         self.estimator = MergedExecutionEstimator()
         self.estimator.set_margin(self.ftcfg.admission_margin, self.ftcfg.admission_margin_k)
         set_ft_mixed_split(self.ftcfg.graph_ft_batches)
@@ -1093,7 +1100,10 @@ class CoServingEngine:
             with self._actions_lock:
                 acts, self._actions = self._actions, []
             if acts:
-                self.comm.broadcast_object(acts)
+                if self.plan_chan is not None:
+                    self.plan_chan.send(acts)
+                else:
+                    self.comm.broadcast_object(acts)
 
     def _plan_hook(self, has_ft: bool):
         if self.tp_size == 1:
@@ -1122,6 +1132,9 @@ class CoServingEngine:
             self.peer_ws = None
             if self.comm is not None:
                 self.comm.peer_ws = None
+        if self.plan_chan is not None:
+            self.plan_chan.close()
+            self.plan_chan = None
 
     def _mark_local(self, name: str) -> None:
         """Synchronise every stream of this GPU, then stamp wall time and a CUDA
@@ -1188,7 +1201,7 @@ class CoServingEngine:
         """Follower-rank loop: replay rank 0's actions until it stops."""
         assert not self.is_driver
         while True:
-            actions = self.comm.broadcast_object(None)
+            actions = self.plan_chan.recv() if self.plan_chan is not None else self.comm.broadcast_object(None)
             for a in actions:
                 kind = a[0]
                 if kind == "stop":

@@ -1,0 +1,157 @@
+"""One-to-many message channel for the step plans of tensor-parallel ranks on
+one node, through POSIX shared memory.
+
+Rank 0 pickles each batch of actions into a single shared slot and bumps a
+sequence number; every follower spins (then naps) on the sequence number,
+copies the payload out and acknowledges it. Rank 0 waits for every
+acknowledgement of the previous message before it overwrites the slot, so
+followers are never more than one message behind. A payload larger than the
+slot travels through the fallback broadcast (the process group) instead, with
+a marker in the slot. All waits are bounded: a wait raises when the process
+it waits for has exited (every rank records its pid in the header; the
+waiter checks it about every 50 ms once it has started to nap) or after
+``timeout_s``, as a missing rank would make the process-group collectives
+fail.
+
+This replaces a gloo/TCP ``broadcast_object_list`` per engine step (two
+collectives, tens to hundreds of microseconds) with a memory copy; it plays
+the role of the reference's shared-memory signals between processes on one box
+(``deltaserve-plugin/deltaserve/coordinator.py:64-115``).
+"""
+
+from __future__ import annotations
+
+import mmap
+import os
+import pickle
+import time
+import uuid
+
+import numpy as np
+
+_HDR = 8            # int64 words: [seq, length, via_fallback, ...], then per rank an ack word, then a pid word
+_MAX_RANKS = 64
+_PID = _HDR + _MAX_RANKS
+_SHM_DIR = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
+
+
+class ShmChannel:
+    def __init__(self, comm, capacity: int = 8 << 20, timeout_s: float = 600.0, name: str | None = None):
+        """Collective: every rank of ``comm`` constructs it (rank 0 creates the
+        segment and shares its name through ``comm``)."""
+        self.comm = comm
+        self.rank, self.size = comm.rank, comm.size
+        if self.size > _MAX_RANKS:
+            raise ValueError("too many ranks for the shared-memory channel")
+        self.timeout_s = timeout_s
+        self.header_bytes = (_HDR + 2 * _MAX_RANKS) * 8
+        size = self.header_bytes + capacity
+        if self.rank == 0:
+            name = name or f"dsv_tp_{os.getpid()}_{uuid.uuid4().hex[:12]}"
+            fd = os.open(os.path.join(_SHM_DIR, name), os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
+            os.ftruncate(fd, size)
+        name = comm.broadcast_object(name if self.rank == 0 else None)
+        if self.rank != 0:
+            fd = os.open(os.path.join(_SHM_DIR, name), os.O_RDWR)
+        self.buf = mmap.mmap(fd, size)
+        os.close(fd)
+        self.path = os.path.join(_SHM_DIR, name)
+        self.name = name
+        self.capacity = capacity
+        self.words = np.ndarray((_HDR + 2 * _MAX_RANKS,), dtype=np.int64, buffer=self.buf)
+        if self.rank == 0:
+            self.words[:] = 0
+        comm.broadcast_object(None)      # header zeroed before anyone writes its pid
+        self.words[_PID + self.rank] = os.getpid()
+        self.seq = 0
+        comm.broadcast_object(None)      # every rank attached before the first message
+        if self.rank == 0:
+            # Every rank holds a mapping now: drop the name so nothing is left
+            # behind in /dev/shm however the processes end.
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+
+    def _gone(self, ranks) -> int | None:
+        """The first of ``ranks`` whose process has exited, else None."""
+        for r in ranks:
+            pid = int(self.words[_PID + r])
+            if pid <= 0:
+                continue
+            try:
+                os.kill(pid, 0)
+            except ProcessLookupError:
+                return r
+            except PermissionError:
+                continue
+            try:                     # an exited child that nobody has reaped yet
+                with open(f"/proc/{pid}/stat", "rb") as f:
+                    state = f.read().rsplit(b")", 1)[1].split()[0]
+                if state in (b"Z", b"X"):
+                    return r
+            except (OSError, IndexError):
+                pass
+        return None
+
+    def _wait(self, ready, ranks, spin: int, what: str) -> None:
+        t0 = time.perf_counter()
+        last_check = t0
+        spins = 0
+        while not ready():
+            spins += 1
+            if spins > spin:
+                time.sleep(50e-6 if spins < 100 * spin else 1e-3)
+                now = time.perf_counter()
+                if now - last_check > 0.05:
+                    last_check = now
+                    dead = self._gone(ranks)
+                    if dead is not None:
+                        raise RuntimeError(f"shm channel: rank {dead} exited ({what})")
+                    if now - t0 > self.timeout_s:
+                        raise TimeoutError(f"shm channel: timed out ({what})")
+
+    # ------------------------------------------------------------ rank 0
+    def send(self, obj) -> None:
+        assert self.rank == 0
+        w = self.words
+        # the previous message has been read by every follower
+        if self.seq > 0:
+            seq, n = self.seq, self.size
+            self._wait(lambda: int(w[_HDR + 1:_HDR + n].min()) >= seq, range(1, n), 200,
+                       "a follower stopped reading step plans")
+        data = pickle.dumps(obj, protocol=pickle.HIGHEST_PROTOCOL)
+        if len(data) <= self.capacity:
+            self.buf[self.header_bytes:self.header_bytes + len(data)] = data
+            w[1] = len(data)
+            w[2] = 0
+            self.seq += 1
+            w[0] = self.seq                  # published last
+        else:
+            w[1] = 0
+            w[2] = 1
+            self.seq += 1
+            w[0] = self.seq
+            self.comm.broadcast_object(obj)
+
+    # ------------------------------------------------------------ followers
+    def recv(self):
+        assert self.rank != 0
+        w = self.words
+        want = self.seq + 1
+        self._wait(lambda: int(w[0]) >= want, (0,), 2000, "waiting for a step plan from rank 0")
+        self.seq = want
+        if int(w[2]):
+            w[_HDR + self.rank] = self.seq
+            return self.comm.broadcast_object(None)
+        n = int(w[1])
+        data = bytes(self.buf[self.header_bytes:self.header_bytes + n])
+        w[_HDR + self.rank] = self.seq       # acknowledged: rank 0 may overwrite the slot
+        return pickle.loads(data)
+
+    def close(self) -> None:
+        try:
+            self.words = None
+            self.buf.close()
+        except Exception:
+            pass
