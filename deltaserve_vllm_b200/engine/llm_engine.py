@@ -142,8 +142,11 @@ class CoServingEngine:
         # process group instead.
         self.plan_chan = None
         if comm is not None and comm.size > 1 and os.environ.get("DSERVE_TP_PLAN_CHANNEL", "shm") == "shm":
-            from ..parallel.shm_channel import ShmChannel
-            self.plan_chan = ShmChannel(comm)
+            from ..parallel.shm_channel import ChannelUnavailable, ShmChannel
+            try:
+                self.plan_chan = ShmChannel(comm)
+            except ChannelUnavailable as e:
+                dprint(f"[tp] {e}; step plans go through the process group")
         self.estimator = MergedExecutionEstimator()
         self.estimator.set_margin(self.ftcfg.admission_margin, self.ftcfg.admission_margin_k)
         set_ft_mixed_split(self.ftcfg.graph_ft_batches)

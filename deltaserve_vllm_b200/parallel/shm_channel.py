@@ -35,10 +35,15 @@ _PID = _HDR + _MAX_RANKS
 _SHM_DIR = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
 
 
+class ChannelUnavailable(RuntimeError):
+    """Raised on every rank when any rank could not set up the segment."""
+
+
 class ShmChannel:
     def __init__(self, comm, capacity: int = 8 << 20, timeout_s: float = 600.0, name: str | None = None):
         """Collective: every rank of ``comm`` constructs it (rank 0 creates the
-        segment and shares its name through ``comm``)."""
+        segment and shares its name through ``comm``). Raises
+        ``ChannelUnavailable`` on every rank if any rank failed to map it."""
         self.comm = comm
         self.rank, self.size = comm.rank, comm.size
         if self.size > _MAX_RANKS:
@@ -46,16 +51,35 @@ class ShmChannel:
         self.timeout_s = timeout_s
         self.header_bytes = (_HDR + 2 * _MAX_RANKS) * 8
         size = self.header_bytes + capacity
+        err = None
+        self.buf = None
         if self.rank == 0:
             name = name or f"dsv_tp_{os.getpid()}_{uuid.uuid4().hex[:12]}"
-            fd = os.open(os.path.join(_SHM_DIR, name), os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
-            os.ftruncate(fd, size)
-        name = comm.broadcast_object(name if self.rank == 0 else None)
+            try:
+                fd = os.open(os.path.join(_SHM_DIR, name), os.O_CREAT | os.O_EXCL | os.O_RDWR, 0o600)
+                os.ftruncate(fd, size)
+                self.buf = mmap.mmap(fd, size)
+                os.close(fd)
+            except OSError as e:
+                err = e
+        self.path = os.path.join(_SHM_DIR, comm.broadcast_object(name if self.rank == 0 else None))
         if self.rank != 0:
-            fd = os.open(os.path.join(_SHM_DIR, name), os.O_RDWR)
-        self.buf = mmap.mmap(fd, size)
-        os.close(fd)
-        self.path = os.path.join(_SHM_DIR, name)
+            try:
+                fd = os.open(self.path, os.O_RDWR)
+                self.buf = mmap.mmap(fd, size)
+                os.close(fd)
+            except OSError as e:
+                err = e
+        # every rank learns whether any rank failed, so all of them take the same path
+        if comm.all_reduce_max_int(1 if err is not None else 0):
+            if self.rank == 0:
+                try:
+                    os.unlink(self.path)
+                except OSError:
+                    pass
+            if self.buf is not None:
+                self.buf.close()
+            raise ChannelUnavailable(f"shared-memory channel unavailable: {err!r}")
         self.name = name
         self.capacity = capacity
         self.words = np.ndarray((_HDR + 2 * _MAX_RANKS,), dtype=np.int64, buffer=self.buf)

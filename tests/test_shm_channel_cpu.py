@@ -88,3 +88,34 @@ def test_shm_channel_detects_exited_rank():
         assert not alive
         res = open(os.path.join(d, "r0")).read()
         assert res.startswith("raised:") and "rank 1 exited" in res, res
+
+
+def _fallback_worker(rank, world, port, outdir):
+    import deltaserve_vllm_b200.parallel.shm_channel as sc
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        if rank == 1:
+            sc._SHM_DIR = os.path.join(outdir, "missing")   # this rank cannot open the segment
+        comm = TPComm()
+        try:
+            sc.ShmChannel(comm, capacity=4096, timeout_s=60)
+            res = "built"
+        except sc.ChannelUnavailable:
+            res = "unavailable"
+        # the process group is still in step on every rank
+        res += f" {comm.all_reduce_max_int(rank)}"
+        with open(os.path.join(outdir, f"r{rank}"), "w") as f:
+            f.write(res)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shm_channel_setup_failure_is_agreed():
+    world = 3
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_fallback_worker, args=(world, _port(), d), nprocs=world, join=True,
+                           start_method="spawn")
+        for r in range(world):
+            assert open(os.path.join(d, f"r{r}")).read() == f"unavailable {world - 1}"
+        if os.path.isdir("/dev/shm"):                   # rank 0 removed its segment
+            assert not [f for f in os.listdir("/dev/shm") if f.startswith("dsv_tp_")]
