@@ -752,7 +752,7 @@ class CoServingEngine:
         # arrives meanwhile (every rank stops at the same layer).
         abort_check = ((lambda: self.arrival_flag)
                        if (self.ftcfg.forward_interruptible and not self.profiling and self.ft_enabled) else None)
-        vote = (lambda f: self.comm.all_reduce_max_int(f)) if self.tp_size > 1 else None
+        vote = self._abort_vote() if self.tp_size > 1 else None
         if self.cuda:
             with torch.cuda.stream(self.fwd_stream):
                 if uses_ft_slot and self._publish_evt is not None:
@@ -1093,6 +1093,14 @@ class CoServingEngine:
     def tp_size(self) -> int:
         return self.comm.size if self.comm is not None else 1
 
+    def _abort_vote(self):
+        """The per-layer pre-emption vote of an interruptible forward (MAX over
+        ranks): through the shared-memory channel (one store and a spin per
+        layer), else an all-reduce on the process group."""
+        if self.plan_chan is not None:
+            return self.plan_chan.all_max
+        return self.comm.all_reduce_max_int
+
     def _record(self, action) -> None:
         if self.tp_size > 1 and self.is_driver:
             with self._actions_lock:
@@ -1256,11 +1264,11 @@ class CoServingEngine:
                                 self.fwd_stream.wait_event(self._publish_evt)
                             self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
                                                          self.capture if has_ft else None,
-                                                         vote=self.comm.all_reduce_max_int)
+                                                         vote=self._abort_vote())
                     else:
                         self.runner.forward_follower(meta, _Packer.thaw(arr, spans),
                                                      self.capture if has_ft else None,
-                                                     vote=self.comm.all_reduce_max_int)
+                                                     vote=self._abort_vote())
                 elif kind == "bwd_start":
                     m = a[1]
                     if self.cuda:

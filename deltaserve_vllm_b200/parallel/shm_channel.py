@@ -24,14 +24,17 @@ from __future__ import annotations
 import mmap
 import os
 import pickle
+import platform
 import time
 import uuid
 
 import numpy as np
 
-_HDR = 8            # int64 words: [seq, length, via_fallback, ...], then per rank an ack word, then a pid word
-_MAX_RANKS = 64
+_HDR = 8            # int64 words: [seq, length, via_fallback, ...], then per rank a message ack
+_MAX_RANKS = 64     # word, a pid word and two vote words (one per parity)
 _PID = _HDR + _MAX_RANKS
+_VOTE = _HDR + 2 * _MAX_RANKS
+_WORDS = _HDR + 4 * _MAX_RANKS
 _SHM_DIR = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
 
 
@@ -48,8 +51,13 @@ class ShmChannel:
         self.rank, self.size = comm.rank, comm.size
         if self.size > _MAX_RANKS:
             raise ValueError("too many ranks for the shared-memory channel")
+        if platform.machine() not in ("x86_64", "AMD64"):
+            # The payload-then-sequence publication relies on x86-64's total
+            # store order; elsewhere the process group carries the plans (every
+            # rank of one node takes this branch alike).
+            raise ChannelUnavailable(f"shared-memory channel needs x86-64 store ordering, not {platform.machine()}")
         self.timeout_s = timeout_s
-        self.header_bytes = (_HDR + 2 * _MAX_RANKS) * 8
+        self.header_bytes = _WORDS * 8
         size = self.header_bytes + capacity
         err = None
         self.buf = None
@@ -82,12 +90,13 @@ class ShmChannel:
             raise ChannelUnavailable(f"shared-memory channel unavailable: {err!r}")
         self.name = name
         self.capacity = capacity
-        self.words = np.ndarray((_HDR + 2 * _MAX_RANKS,), dtype=np.int64, buffer=self.buf)
+        self.words = np.ndarray((_WORDS,), dtype=np.int64, buffer=self.buf)
         if self.rank == 0:
             self.words[:] = 0
         comm.broadcast_object(None)      # header zeroed before anyone writes its pid
         self.words[_PID + self.rank] = os.getpid()
         self.seq = 0
+        self.vseq = 0                    # votes taken
         comm.broadcast_object(None)      # every rank attached before the first message
         if self.rank == 0:
             # Every rank holds a mapping now: drop the name so nothing is left
@@ -172,6 +181,25 @@ class ShmChannel:
         data = bytes(self.buf[self.header_bytes:self.header_bytes + n])
         w[_HDR + self.rank] = self.seq       # acknowledged: rank 0 may overwrite the slot
         return pickle.loads(data)
+
+    # ------------------------------------------------------------ host votes
+    def all_max(self, flag: int) -> int:
+        """Collective: the MAX of every rank's ``flag`` (0 or 1), the per-layer
+        abort vote of an interruptible forward. Vote ``k`` of a rank is one
+        store of ``2k + flag`` into its word of parity ``k & 1``; a rank reads
+        the others' words of that parity once each shows vote ``k``. A rank
+        can be at most one vote ahead of the slowest, so a word is never
+        overwritten before every rank has read it."""
+        w = self.words
+        self.vseq += 1
+        k = self.vseq
+        base = _VOTE + (k & 1) * _MAX_RANKS
+        w[base + self.rank] = 2 * k + (1 if flag else 0)
+        n = self.size
+        others = [r for r in range(n) if r != self.rank]
+        self._wait(lambda: int((w[base:base + n] >> 1).min()) >= k, others, 2000,
+                   "waiting for the other ranks' votes")
+        return int((w[base:base + n] & 1).max())
 
     def close(self) -> None:
         try:

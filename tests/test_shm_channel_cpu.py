@@ -1,6 +1,7 @@
 """The shared-memory step-plan channel between TP ranks (gloo ranks on CPU):
 messages arrive in order on every follower, payloads larger than the slot
-travel through the process-group fallback, and a wait ends with an error
+travel through the process-group fallback, the per-layer MAX vote agrees
+with the process group's, and a wait ends with an error
 (not a hang) when the peer process has exited."""
 import os
 import socket
@@ -35,10 +36,17 @@ def _order_worker(rank, world, port, outdir):
                 ch.send(m)
             else:
                 got.append(ch.recv())
+        # votes: MAX over ranks, every rank sees the same sequence
+        import random
+        rng = random.Random(rank)
+        flags = [1 if rng.random() < 0.1 else 0 for _ in range(300)]
+        votes = [ch.all_max(f) for f in flags]
+        all_flags = comm.all_gather_object(flags)
+        votes_ok = votes == [max(col) for col in zip(*all_flags)]
         # the process group still works in step with the channel
         total = comm.all_reduce_max_int(rank)
         if rank != 0:
-            ok = got == msgs and total == world - 1
+            ok = got == msgs and total == world - 1 and votes_ok
             with open(os.path.join(outdir, f"r{rank}"), "w") as f:
                 f.write("ok" if ok else "bad")
         ch.close()
