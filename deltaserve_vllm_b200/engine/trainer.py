@@ -6,7 +6,8 @@ One backward *cycle* trains on the activations of one filled capture buffer:
 2. layers L-1 .. 0: hand-written layer backward (``models/lora_backward.py``);
    under TP the replicated factor gradients of every 8 layers are summed with
    one all-reduce of a contiguous slab (the reference buckets the same way,
-   ``bwd_services/common/tp.py:186-236``);
+   ``bwd_services/common/tp.py:186-236``), issued from a side stream while the
+   next layer's backward runs;
 3. per-layer gradient clipping to norm 1.0 (rank-symmetric under TP), AdamW on
    the flat fp32 masters (two launches), StepLR decay per epoch;
 4. publish: bf16 ``A`` and ``B * alpha/r`` written straight into the served
@@ -181,11 +182,17 @@ class LoraTrainer:
             saved["resid_mid"] = self.bwd.recompute_resid_mid(l, saved["layer_in"], saved["ctx"])
         if self.diag_cycles > 0 and self.step < self.diag_cycles:
             self._diag_layer(l, saved, ci, pos)
+        tp = self.comm is not None and self.comm.size > 1
+        h = None
+        if tp and (l + 1) % BUCKET_LAYERS == 0 and l + 1 < L:
+            # Layers [l + 1, l + 1 + BUCKET_LAYERS) finished with the previous
+            # step: one all-reduce of their replicated factor gradients, which
+            # overlaps this layer's backward (it writes only layer l's).
+            h = self.bwd.reduce_begin(m.rep_block(m.grads, l + 1, min(L, l + 1 + BUCKET_LAYERS)))
         dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin)
-        if self.comm is not None and self.comm.size > 1 and (l % BUCKET_LAYERS == 0):
-            # Layers [l, l + BUCKET_LAYERS) are done: one all-reduce of their
-            # replicated factor gradients.
-            self.comm.all_reduce(m.rep_block(m.grads, l, min(L, l + BUCKET_LAYERS)))
+        self.bwd.reduce_end(h, dh.device)
+        if tp and l == 0:
+            self.comm.all_reduce(m.rep_block(m.grads, 0, min(L, BUCKET_LAYERS)))
         return dh
 
     @torch.no_grad()

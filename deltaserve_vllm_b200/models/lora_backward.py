@@ -26,8 +26,10 @@ this engine's fused weights:
 
 Tensor parallelism: ``comm.all_reduce`` sums the per-rank partials of the two
 residual-stream gradients per layer (after the MLP and after the qkv input
-gradient); replicated factor gradients (column-parallel ``A``, row-parallel
-``B``) are summed by the trainer in buckets.
+gradient), each issued from a side stream while the factor-gradient GEMMs of
+the same half-layer run; replicated factor gradients (column-parallel ``A``,
+row-parallel ``B``) are summed by the trainer in buckets, overlapped with the
+next layer's backward.
 """
 
 from __future__ import annotations
@@ -311,6 +313,33 @@ class LoraBackward:
         # Backward GEMMs launch one CTA per tile so the inference stream can
         # interleave between tiles (the backward runs at low priority).
         self.max_ctas = 1 << 30
+        self._comm_streams: dict = {}
+
+    # ------------------------------------------------------------ TP sums
+    def reduce_begin(self, t: torch.Tensor):
+        """Start the sum of ``t`` over the TP ranks. On CUDA the all-reduce is
+        issued from a side stream forked off the current one, so the kernels
+        enqueued next (work that does not read ``t``) overlap it; inside a
+        CUDA-graph capture this is a fork that :meth:`reduce_end` joins. The
+        collectives keep one issue order on every rank."""
+        if self.comm is None or self.comm.size == 1:
+            return None
+        if not t.is_cuda:
+            self.comm.all_reduce(t)
+            return None
+        cs = self._comm_streams.get(t.device)
+        if cs is None:
+            cs = self._comm_streams[t.device] = torch.cuda.Stream(t.device)
+        cs.wait_stream(torch.cuda.current_stream(t.device))
+        with torch.cuda.stream(cs):
+            self.comm.all_reduce(t)
+        return cs
+
+    @staticmethod
+    def reduce_end(handle, device) -> None:
+        """Order the current stream after a :meth:`reduce_begin`."""
+        if handle is not None:
+            torch.cuda.current_stream(device).wait_stream(handle)
 
     # ------------------------------------------------------------ GEMM helpers
     def _mm(self, a, b, b_mn, epi=EPI_F32, out=None):
@@ -567,20 +596,22 @@ class LoraBackward:
             ops.swiglu_bwd(gate_up, d_act, d_gu, act_out)
         if act is None:
             act = act_out
-        self.group_grads(layer, "down", act, dh_c, dz)
+        dz_down = dz
         x2 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
         dz = self.group_dz(layer, "gate_up", d_gu)
         d_x2 = self.dx_gemm(layer, "gate_up", d_gu, lw.gate_up, dz)  # [n, D]
+        # The TP sum of d_x2 runs while the factor gradients (which do not
+        # read it) are computed.
+        h = self.reduce_begin(d_x2)
+        self.group_grads(layer, "down", act, dh_c, dz_down)
         self.group_grads(layer, "gate_up", x2, d_gu, dz)
-        if self.comm is not None:
-            self.comm.all_reduce(d_x2)
+        self.reduce_end(h, dev)
         d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
         d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
         # ---- attention ---------------------------------------------------
-        dz = self.group_dz(layer, "o", d_mid_c)
-        d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz)        # [n, q_l]
-        self.group_grads(layer, "o", ctx, d_mid_c, dz)
+        dz_o = self.group_dz(layer, "o", d_mid_c)
+        d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o)      # [n, q_l]
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
         ql, kl = self.hq * self.hd, self.hkv * self.hd
         d_qkv = torch.empty(n, ql + 2 * kl, dtype=cdt, device=dev)
@@ -612,7 +643,8 @@ class LoraBackward:
         ops.rms_norm(x, lw.in_ln, x1, eps)
         dz = self.group_dz(layer, "qkv", d_qkv)
         d_x1 = self.dx_gemm(layer, "qkv", d_qkv, lw.qkv, dz)       # [n, D]
+        h = self.reduce_begin(d_x1)
+        self.group_grads(layer, "o", ctx, d_mid_c, dz_o)
         self.group_grads(layer, "qkv", x1, d_qkv, dz)
-        if self.comm is not None:
-            self.comm.all_reduce(d_x1)
+        self.reduce_end(h, dev)
         return ops.rms_norm_bwd(x, d_x1, lw.in_ln, eps, add=d_mid)
