@@ -31,7 +31,7 @@ import time
 import uuid
 
 from fastapi import FastAPI, Request
-from fastapi.responses import JSONResponse, StreamingResponse
+from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
 
 from ..adapters.routing.router import DISABLED, RouteDecision, extract_text
 from ..engine.request import SamplingParams
@@ -65,6 +65,10 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     if engine.tokenizer is None:
         engine.tokenizer = tok        # stop strings are matched on decoded text
     route_name = engine.rcfg.route_model_name if engine.router is not None else None
+    from .prom import ServingStats
+    serving_stats = ServingStats()
+    engine.request_listeners.append(serving_stats.on_request)
+    app.state.serving_stats = serving_stats
 
     def _choice(index: int, r, chat: bool = False) -> dict:
         text = tok.decode(r.output_ids)
@@ -460,6 +464,75 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         except Exception as ex:
             return JSONResponse(status_code=400, content={"error": str(ex)})
         return {"name": name, "removed": True, "result": res}
+
+    # ------------------------------------------------------------ vLLM-compatible extras
+    @app.get("/metrics")
+    async def metrics():
+        from .prom import render
+        return PlainTextResponse(render(serving_stats, engine, model_name),
+                                 media_type="text/plain; version=0.0.4; charset=utf-8")
+
+    @app.get("/version")
+    async def version():
+        from .. import __version__
+        return {"version": __version__}
+
+    @app.get("/ping")
+    @app.post("/ping")
+    async def ping():
+        return Response(status_code=200 if (et.alive and et.error is None) else 503)
+
+    @app.post("/tokenize")
+    async def tokenize(req: Request):
+        body = await body_of(req)
+        if body.get("messages") is not None:
+            ids = _chat_prompt(body["messages"])
+        elif isinstance(body.get("prompt"), str):
+            ids = tok.encode(body["prompt"])
+        else:
+            return JSONResponse(status_code=400, content={"error": "JSON body with 'prompt' or 'messages' required"})
+        return {"count": len(ids), "max_model_len": engine.ecfg.max_model_len, "tokens": ids}
+
+    @app.post("/detokenize")
+    async def detokenize(req: Request):
+        body = await body_of(req)
+        ids = body.get("tokens")
+        if not isinstance(ids, list):
+            return JSONResponse(status_code=400, content={"error": "JSON body with 'tokens' required"})
+        try:
+            return {"prompt": tok.decode([int(t) for t in ids])}
+        except (TypeError, ValueError) as ex:
+            return JSONResponse(status_code=400, content={"error": str(ex)})
+
+    @app.post("/v1/load_lora_adapter")
+    async def load_lora_adapter(req: Request):
+        """vLLM's runtime LoRA loading: ``{"lora_name", "lora_path"}``; the
+        adapter then serves requests whose ``model`` is its name."""
+        body = await body_of(req)
+        name, path = body.get("lora_name"), body.get("lora_path")
+        if not name or not path:
+            return PlainTextResponse("'lora_name' and 'lora_path' are required", status_code=400)
+        if name in engine.adapter_slots:
+            return PlainTextResponse(f"The lora adapter '{name}' has already been loaded.", status_code=400)
+        try:
+            await et.call(lambda e: e.load_inference_adapter(name, path=path))
+        except Exception as ex:
+            return PlainTextResponse(f"Failed to load LoRA adapter '{name}': {ex}", status_code=400)
+        return PlainTextResponse(f"Success: LoRA adapter '{name}' added successfully.")
+
+    @app.post("/v1/unload_lora_adapter")
+    async def unload_lora_adapter(req: Request):
+        body = await body_of(req)
+        name = body.get("lora_name")
+        if not name:
+            return PlainTextResponse("'lora_name' is required", status_code=400)
+        if name not in engine.adapter_slots or name.startswith("__"):
+            return PlainTextResponse(f"The lora adapter '{name}' cannot be found.", status_code=404)
+        try:
+            await et.call(lambda e: e.unload_inference_adapter(name))
+        except Exception as ex:
+            return PlainTextResponse(f"Failed to unload LoRA adapter '{name}': {ex}", status_code=400)
+        return PlainTextResponse(f"Success: LoRA adapter '{name}' removed successfully.")
 
     # ------------------------------------------------------------ lifecycle
     @app.post("/shutdown")

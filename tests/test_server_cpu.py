@@ -251,3 +251,56 @@ def test_api_chat_completions():
                                                        "temperature": 1.0, "logprobs": True}).json()
             assert len(two["choices"]) == 2 and len(two["choices"][1]["logprobs"]["content"]) == 2
             assert c.post("/v1/chat/completions", json={"max_tokens": 2}).status_code == 400
+
+
+def test_api_vllm_compatible_extras(tmp_path):
+    """The routes a client of vLLM's OpenAI server also uses: /metrics
+    (Prometheus text), /tokenize and /detokenize, /version, /ping, and runtime
+    LoRA loading (/v1/load_lora_adapter, /v1/unload_lora_adapter)."""
+    from deltaserve_vllm_b200.models.configs import resolve_arch
+    from deltaserve_vllm_b200.models.lora import LORA_PROJS, random_adapter
+    eng = make_engine(str(tmp_path))
+    arch = resolve_arch("qwen3-tiny")
+    adir = str(tmp_path / "extra_ad")
+    peft_io.write_peft_adapter(adir, random_adapter(arch, 8, seed=5),
+                               peft_io.default_adapter_config(8, 16.0, LORA_PROJS), {"save_id": "x"})
+    with TestClient(create_app(eng)) as c:
+        assert c.get("/ping").status_code == 200
+        assert c.get("/version").json()["version"]
+        t = c.post("/tokenize", json={"prompt": "hello"}).json()
+        assert t["count"] == 5 and t["max_model_len"] == 512
+        assert c.post("/detokenize", json={"tokens": t["tokens"]}).json()["prompt"] == "hello"
+        assert c.post("/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()["count"] > 2
+        assert c.post("/tokenize", json={}).status_code == 400
+        # runtime LoRA loading
+        r = c.post("/v1/load_lora_adapter", json={"lora_name": "extra", "lora_path": adir})
+        assert r.status_code == 200 and "Success" in r.text, r.text
+        assert c.post("/v1/load_lora_adapter", json={"lora_name": "extra", "lora_path": adir}).status_code == 400
+        assert "extra" in [m["id"] for m in c.get("/v1/models").json()["data"]]
+        r = c.post("/v1/completions", json={"model": "extra", "prompt": "abc", "max_tokens": 3})
+        assert r.status_code == 200 and r.json()["usage"]["completion_tokens"] == 3
+        r = c.post("/v1/completions", json={"prompt": "abcd", "max_tokens": 2})
+        assert r.status_code == 200
+        r = c.post("/v1/unload_lora_adapter", json={"lora_name": "extra"})
+        assert r.status_code == 200 and "removed" in r.text
+        assert c.post("/v1/unload_lora_adapter", json={"lora_name": "extra"}).status_code == 404
+        assert c.post("/v1/completions", json={"model": "extra", "prompt": "a", "max_tokens": 1}).status_code == 404
+        # Prometheus exposition
+        m = c.get("/metrics")
+        assert m.status_code == 200 and m.headers["content-type"].startswith("text/plain")
+        lines = m.text.splitlines()
+        val = {ln.split(" ")[0]: float(ln.split(" ")[1]) for ln in lines if ln and not ln.startswith("#")}
+        lab = '{model_name="qwen3-tiny"}'
+        assert val["dserve:prompt_tokens_total" + lab] == 7
+        assert val["dserve:generation_tokens_total" + lab] == 5
+        assert val["dserve:time_to_first_token_seconds_count"] == 2
+        assert val['dserve:time_to_first_token_seconds_bucket{le="+Inf"}'] == 2
+        assert val["dserve:time_per_output_token_seconds_count"] == 3      # (3-1) + (2-1) gaps
+        assert val["dserve:num_requests_running" + lab] == 0
+        assert 0.0 <= val["dserve:kv_cache_usage_perc" + lab] <= 1.0
+        assert "dserve:ft_tokens_trained_total" + lab in val
+        # every sample line belongs to a declared family
+        declared = {ln.split(" ")[2] for ln in lines if ln.startswith("# TYPE")}
+        for name in val:
+            base = name.split("{")[0]
+            assert any(base == d or base.startswith(d + "_") for d in declared), name
