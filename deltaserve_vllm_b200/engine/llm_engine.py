@@ -69,6 +69,24 @@ class StepRecord:
     kind: str
 
 
+def _generation_eos_ids(model: str) -> tuple[int, ...]:
+    """``eos_token_id`` of a model directory's ``generation_config.json`` (an
+    int or a list), else ()."""
+    path = os.path.join(model, "generation_config.json") if model and os.path.isdir(model) else None
+    if path is None or not os.path.isfile(path):
+        return ()
+    try:
+        with open(path) as f:
+            e = json.load(f).get("eos_token_id")
+    except (OSError, ValueError):
+        return ()
+    if isinstance(e, int):
+        return (e,)
+    if isinstance(e, list):
+        return tuple(int(x) for x in e if isinstance(x, int))
+    return ()
+
+
 class CoServingEngine:
     def __init__(self, ecfg: EngineConfig, ftcfg: FinetuneConfig | None = None,
                  rcfg: AdapterRoutingConfig | None = None, comm=None,
@@ -91,6 +109,7 @@ class CoServingEngine:
         self.tokenizer = tokenizer
         t0 = time.perf_counter()
         self.weights = self._load_weights(ecfg)
+        self._gen_eos = _generation_eos_ids(ecfg.model)
         # ---- LoRA slots: inference adapters + the pinned FT slot
         self.adapter_slots: dict[str, int] = {}
         self.adapter_meta: dict[str, dict] = {}
@@ -782,7 +801,7 @@ class CoServingEngine:
         self.stats["d2h_bytes"] += self.runner.last_d2h_bytes
         self._pending_timing.append(StepRecord(feats, ev0, ev1, pred, "step"))
         now = time.perf_counter()
-        done = self.scheduler.update(out, toks, now)
+        done = self.scheduler.update(out, toks, now, eos_id=self.eos_ids())
         if self.tokenizer is not None:
             done.extend(self._check_stop_strings(out, now))
         self.stats["steps"] += 1
@@ -1092,6 +1111,23 @@ class CoServingEngine:
     @property
     def tp_size(self) -> int:
         return self.comm.size if self.comm is not None else 1
+
+    def eos_ids(self) -> tuple[int, ...]:
+        """End-of-sequence token ids: the tokenizer's ``eos_token_id`` plus the
+        checkpoint's ``generation_config.json`` ids (Llama-3 instruct models
+        end turns with a second id). A request stops on any of them unless
+        its ``ignore_eos`` is set."""
+        tok = self.tokenizer
+        key = id(tok)
+        if getattr(self, "_eos_key", None) != key:
+            ids = set(self._gen_eos)
+            e = getattr(tok, "eos_token_id", None) if tok is not None else None
+            if isinstance(e, int):
+                ids.add(e)
+            elif isinstance(e, (list, tuple)):
+                ids.update(int(x) for x in e)
+            self._eos_cache, self._eos_key = tuple(sorted(ids)), key
+        return self._eos_cache
 
     def _abort_vote(self):
         """The per-layer pre-emption vote of an interruptible forward (MAX over

@@ -299,10 +299,11 @@ class Scheduler:
         return reqs
 
     def update(self, out: SchedulerOutput, sampled: dict[int, int], now: float | None = None,
-               eos_id: int | None = None) -> list[Request]:
+               eos_id=None) -> list[Request]:
         """Apply a finished step: advance computed counts, append sampled tokens,
         retire finished requests. ``sampled`` maps Request.seq_no -> token."""
         now = time.perf_counter() if now is None else now
+        eos = (() if eos_id is None else (eos_id,) if isinstance(eos_id, int) else tuple(eos_id))
         done: list[Request] = []
         for s in out.decode + out.prefill:
             r = s.req
@@ -320,7 +321,7 @@ class Scheduler:
             else:
                 r.token_times.append(now)
             stop = (len(r.output_ids) >= r.params.max_tokens
-                    or (not r.params.ignore_eos and eos_id is not None and tok == eos_id)
+                    or (not r.params.ignore_eos and tok in eos)
                     or tok in r.params.stop_token_ids
                     or r.num_tokens >= self.max_model_len)
             if stop:

@@ -245,3 +245,41 @@ def test_stop_strings_end_requests():
         k = text.find(stop)
         assert cut.output_ids == full.output_ids[:k + len(stop)]   # ended on the token completing the match
         assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+
+
+def test_eos_ends_requests_unless_ignored(tmp_path):
+    """A request stops on the tokenizer's end-of-sequence id (or one listed in
+    the model directory's generation_config.json) unless ignore_eos is set."""
+    import json as _json
+    from deltaserve_vllm_b200.engine.llm_engine import _generation_eos_ids
+
+    class Tok:
+        eos_token_id = None
+
+    eng = make_engine(str(tmp_path), start_on_launch=False)
+    eng.tokenizer = Tok()
+    eng.add_request("full", [5, 6, 7, 8], SamplingParams(max_tokens=8, ignore_eos=True))
+    eng.run_until_idle(max_steps=200)
+    full = eng.finished[-1].output_ids
+    assert len(full) == 8
+    k = 3
+    eos = full[k]
+    first = full.index(eos)
+    tok2 = Tok()
+    tok2.eos_token_id = eos
+    eng.tokenizer = tok2
+    eng.add_request("eos", [5, 6, 7, 8], SamplingParams(max_tokens=8, ignore_eos=False))
+    eng.add_request("ign", [5, 6, 7, 8], SamplingParams(max_tokens=8, ignore_eos=True))
+    eng.run_until_idle(max_steps=200)
+    got = {r.request_id: r.output_ids for r in eng.finished[-2:]}
+    assert got["eos"] == full[:first + 1]                  # the EOS token is the last output
+    assert got["ign"] == full
+    assert eng.kv.allocator.num_free == eng.kv.allocator.num_blocks
+    # generation_config.json: an int or a list
+    d = tmp_path / "m"
+    d.mkdir()
+    (d / "generation_config.json").write_text(_json.dumps({"eos_token_id": [128001, 128009]}))
+    assert _generation_eos_ids(str(d)) == (128001, 128009)
+    (d / "generation_config.json").write_text(_json.dumps({"eos_token_id": 7}))
+    assert _generation_eos_ids(str(d)) == (7,)
+    assert _generation_eos_ids("qwen3-tiny") == ()
