@@ -261,7 +261,8 @@ class CoServingEngine:
         ended = []
         for s in out.decode + out.prefill:
             r = s.req
-            if not r.params.stop or r.finished() or not s.sample or not r.output_ids:
+            if (not r.params.stop or r.finished() or not s.sample or not r.output_ids
+                    or len(r.output_ids) < r.params.min_tokens):
                 continue
             text = self.tokenizer.decode(r.output_ids)
             hit = next((st for st in r.params.stop if st and st in text), None)
@@ -771,6 +772,7 @@ class CoServingEngine:
         # arrives meanwhile (every rank stops at the same layer).
         abort_check = ((lambda: self.arrival_flag)
                        if (self.ftcfg.forward_interruptible and not self.profiling and self.ft_enabled) else None)
+        self.runner.eos_ids = self.eos_ids()
         vote = self._abort_vote() if self.tp_size > 1 else None
         if self.cuda:
             with torch.cuda.stream(self.fwd_stream):

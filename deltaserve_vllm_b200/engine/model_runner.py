@@ -115,6 +115,7 @@ class DecodeGraphs:
         self.graphs: dict[tuple[int, bool], dict] = {}
         self.pool = None
         self.replays = 0
+        self.eos_ids: tuple[int, ...] = ()   # set by the engine (min_tokens masks them)
         self._host: torch.Tensor | None = None
         self._host_f: torch.Tensor | None = None
         self._evt = None
@@ -457,6 +458,9 @@ class ModelRunner:
         toks = torch.empty(R, dtype=torch.int64, device=logits.device)
         dev = logits.device
         topk = topp = lps = None
+        if any(r.params.has_penalties for r in reqs):
+            from .penalties import apply_penalties
+            self.last_h2d_bytes += apply_penalties(logits, reqs, self.eos_ids)
         if any(r.params.needs_full_sampler for r in reqs):
             topk = torch.tensor([r.params.top_k for r in reqs], dtype=torch.int32).to(dev, non_blocking=True)
             topp = torch.tensor([r.params.top_p for r in reqs], dtype=torch.float32).to(dev, non_blocking=True)

@@ -26,10 +26,20 @@ class SamplingParams:
     top_p: float = 1.0               # 1 = off
     logprobs: bool = False           # record the chosen token's log-probability
     stop: tuple[str, ...] = ()       # stop strings (checked on the decoded output)
+    presence_penalty: float = 0.0
+    frequency_penalty: float = 0.0
+    repetition_penalty: float = 1.0  # 1 = off
+    min_tokens: int = 0              # no EOS / stop token / stop string before this many
+    logit_bias: tuple[tuple[int, float], ...] = ()
+
+    @property
+    def has_penalties(self) -> bool:
+        return bool(self.presence_penalty or self.frequency_penalty or self.repetition_penalty != 1.0
+                    or self.min_tokens > 0 or self.logit_bias)
 
     @property
     def needs_full_sampler(self) -> bool:
-        return self.top_k > 0 or self.top_p < 1.0 or self.logprobs
+        return self.top_k > 0 or self.top_p < 1.0 or self.logprobs or self.has_penalties
 
 
 _counter = itertools.count()

@@ -155,9 +155,23 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                                     top_k=max(0, int(body.get("top_k", 0) or 0)),
                                     top_p=float(body.get("top_p", 1.0) if body.get("top_p") is not None else 1.0),
                                     logprobs=bool(body.get("logprobs") is not None and body.get("logprobs") is not False),
-                                    stop=tuple(str(x) for x in stop))
-        except (TypeError, ValueError) as e:
+                                    stop=tuple(str(x) for x in stop),
+                                    presence_penalty=float(body.get("presence_penalty") or 0.0),
+                                    frequency_penalty=float(body.get("frequency_penalty") or 0.0),
+                                    repetition_penalty=float(1.0 if body.get("repetition_penalty") is None
+                                                             else body["repetition_penalty"]),
+                                    min_tokens=int(body.get("min_tokens") or 0),
+                                    logit_bias=tuple(sorted((int(k), max(-100.0, min(100.0, float(v))))
+                                                            for k, v in (body.get("logit_bias") or {}).items())))
+        except (TypeError, ValueError, AttributeError) as e:
             return None, 0, JSONResponse(status_code=400, content={"error": f"bad sampling parameter: {e}"})
+        if not (-2.0 <= params.presence_penalty <= 2.0 and -2.0 <= params.frequency_penalty <= 2.0):
+            return None, 0, JSONResponse(status_code=400,
+                                         content={"error": "presence_penalty / frequency_penalty must be in [-2, 2]"})
+        if params.repetition_penalty <= 0.0:
+            return None, 0, JSONResponse(status_code=400, content={"error": "repetition_penalty must be > 0"})
+        if not 0 <= params.min_tokens <= params.max_tokens:
+            return None, 0, JSONResponse(status_code=400, content={"error": "min_tokens must be in [0, max_tokens]"})
         if not 0.0 < params.top_p <= 1.0:
             return None, 0, JSONResponse(status_code=400, content={"error": "top_p must be in (0, 1]"})
         if n_choices < 1:
