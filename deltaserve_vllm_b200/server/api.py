@@ -70,10 +70,12 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     engine.request_listeners.append(serving_stats.on_request)
     app.state.serving_stats = serving_stats
 
-    def _choice(index: int, r, chat: bool = False) -> dict:
+    def _choice(index: int, r, chat: bool = False, echo: bool = False) -> dict:
         text = tok.decode(r.output_ids)
         if r.stop_reason:
             text = text[:text.find(r.stop_reason)] if r.stop_reason in text else text
+        if echo:
+            text = tok.decode(r.prompt_ids) + text
         if chat:
             c = {"index": index, "message": {"role": "assistant", "content": text},
                  "finish_reason": _finish_reason(r)}
@@ -87,25 +89,27 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                              "token_logprobs": list(r.output_logprobs[:len(r.output_ids)])}
         return c
 
-    async def _completions_n(body, ids, params, n, model, chat=False):
-        """``n`` independent completions of one prompt (seeds seed, seed+1, ...)."""
+    async def _completions_n(body, prompts, params, n, model, chat=False, echo=False):
+        """``n`` independent completions of each prompt of a batch (seeds seed,
+        seed+1, ...); choice ``p * n + i`` is completion ``i`` of prompt ``p``."""
         import dataclasses as _dc
         model_adapter = None if model == model_name else model
         if model_adapter is not None and model_adapter not in engine.adapter_slots:
             return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
         base_seed = params.seed if params.seed is not None else int(uuid.uuid4().int % (1 << 31))
         rids, waits = [], []
-        for i in range(n):
-            rid = f"cmpl-{uuid.uuid4().hex[:24]}"
-            p = _dc.replace(params, seed=base_seed + i)
-            waits.append(et.register(rid, False))
-            rids.append(rid)
-            try:
-                await et.call(lambda e, rid=rid, p=p: e.add_request(rid, ids, p, model_adapter))
-            except Exception as e:
-                for x in rids:
-                    et.unregister(x)
-                return JSONResponse(status_code=400, content={"error": str(e)})
+        for k, ids in enumerate(prompts):
+            for i in range(n):
+                rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+                p = _dc.replace(params, seed=base_seed + k * n + i)
+                waits.append(et.register(rid, False))
+                rids.append(rid)
+                try:
+                    await et.call(lambda e, rid=rid, p=p, ids=ids: e.add_request(rid, ids, p, model_adapter))
+                except Exception as e:
+                    for x in rids:
+                        et.unregister(x)
+                    return JSONResponse(status_code=400, content={"error": str(e)})
         et.notify_arrival()
         try:
             reqs = [await w.done for w in waits]
@@ -113,11 +117,12 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             for x in rids:
                 et.unregister(x)
         ntok = sum(len(r.output_ids) for r in reqs)
+        nprompt = sum(len(ids) for ids in prompts)
         return JSONResponse(content={
             "id": rids[0], "object": "chat.completion" if chat else "text_completion",
             "created": int(time.time()), "model": model,
-            "choices": [_choice(i, r, chat) for i, r in enumerate(reqs)],
-            "usage": {"prompt_tokens": len(ids), "completion_tokens": ntok, "total_tokens": len(ids) * n + ntok}})
+            "choices": [_choice(i, r, chat, echo) for i, r in enumerate(reqs)],
+            "usage": {"prompt_tokens": nprompt, "completion_tokens": ntok, "total_tokens": nprompt + ntok}})
 
     async def body_of(req: Request) -> dict:
         try:
@@ -193,16 +198,20 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         text = "".join(f"<|{m.get('role', 'user')}|>\n{m.get('content', '')}\n" for m in messages)
         return tok.encode(text + "<|assistant|>\n")
 
-    async def _generate(body: dict, ids: list[int], chat: bool):
+    async def _generate(body: dict, prompts: list[list[int]], chat: bool):
         params, n_choices, err = _parse_params(body)
         if err is not None:
             return err
         model = body.get("model") or model_name
         stream = bool(body.get("stream", False))
-        if n_choices > 1:
+        echo = bool(body.get("echo", False)) and not chat
+        include_usage = bool((body.get("stream_options") or {}).get("include_usage", False))
+        if n_choices > 1 or len(prompts) > 1:
             if stream:
-                return JSONResponse(status_code=400, content={"error": "n > 1 is not supported with stream"})
-            return await _completions_n(body, ids, params, n_choices, model, chat)
+                return JSONResponse(status_code=400,
+                                    content={"error": "n > 1 and prompt batches are not supported with stream"})
+            return await _completions_n(body, prompts, params, n_choices, model, chat, echo)
+        ids = prompts[0]
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:24]}"
         router = engine.router
         headers = {}
@@ -241,6 +250,9 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             async def gen():
                 try:
                     first = True
+                    if echo:
+                        ch = {"index": 0, "text": tok.decode(ids), "token_ids": [], "finish_reason": None}
+                        yield f"data: {json.dumps({'id': rid, 'object': obj, 'created': created, 'model': model, 'choices': [ch]})}\n\n"
                     while True:
                         toks = await w.tokens.get()
                         if toks is None:
@@ -261,7 +273,14 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                             {"index": 0, "text": "", "finish_reason": _finish_reason(r)})
                     fin = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
                            "model": model, "choices": [last]}
-                    yield f"data: {json.dumps(fin)}\n\ndata: [DONE]\n\n"
+                    yield f"data: {json.dumps(fin)}\n\n"
+                    if include_usage:
+                        use = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
+                               "model": model, "choices": [],
+                               "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),
+                                         "total_tokens": r.num_prompt + len(r.output_ids)}}
+                        yield f"data: {json.dumps(use)}\n\n"
+                    yield "data: [DONE]\n\n"
                 finally:
                     et.unregister(rid)
             return StreamingResponse(gen(), media_type="text/event-stream", headers=headers)
@@ -270,7 +289,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         finally:
             et.unregister(rid)
         out = {"id": rid, "object": obj, "created": created, "model": model,
-               "choices": [_choice(0, r, chat)],
+               "choices": [_choice(0, r, chat, echo)],
                "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),
                          "total_tokens": r.num_prompt + len(r.output_ids)},
                "metrics": {"ttft_s": r.ttft(), "tbt_mean_s": (sum(r.tbts()) / len(r.tbts()))
@@ -283,17 +302,19 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         prompt = body.get("prompt")
         if prompt is None:
             return JSONResponse(status_code=400, content={"error": "prompt is required"})
-        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
-            ids = [int(t) for t in prompt]
-        elif isinstance(prompt, list):
-            if len(prompt) != 1:
-                return JSONResponse(status_code=400, content={"error": "one prompt per request"})
-            ids = tok.encode(str(prompt[0]))
-        else:
-            ids = tok.encode(str(prompt))
-        if not ids:
+        # a string, a token-id list, or a batch of either
+        try:
+            if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+                prompts = [[int(t) for t in prompt]]
+            elif isinstance(prompt, list):
+                prompts = [[int(t) for t in p] if isinstance(p, list) else tok.encode(str(p)) for p in prompt]
+            else:
+                prompts = [tok.encode(str(prompt))]
+        except (TypeError, ValueError) as ex:
+            return JSONResponse(status_code=400, content={"error": f"bad prompt: {ex}"})
+        if not prompts or any(not p for p in prompts):
             return JSONResponse(status_code=400, content={"error": "empty prompt"})
-        return await _generate(body, ids, chat=False)
+        return await _generate(body, prompts, chat=False)
 
     @app.post("/v1/chat/completions")
     async def chat_completions(req: Request):
@@ -304,7 +325,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         ids = _chat_prompt(messages)
         if not ids:
             return JSONResponse(status_code=400, content={"error": "empty prompt"})
-        return await _generate(body, ids, chat=True)
+        return await _generate(body, [ids], chat=True)
 
     # ------------------------------------------------------------ finetuning
     @app.post("/start_finetuning")

@@ -304,3 +304,40 @@ def test_api_vllm_compatible_extras(tmp_path):
         for name in val:
             base = name.split("{")[0]
             assert any(base == d or base.startswith(d + "_") for d in declared), name
+
+
+def test_api_prompt_batches_echo_and_stream_usage(tmp_path):
+    """A completions request with a batch of prompts gives n choices per
+    prompt in prompt order (each equal to the prompt run alone with the same
+    seed), ``echo`` prefixes the prompt text, and
+    ``stream_options.include_usage`` adds a usage chunk before [DONE]."""
+    eng = make_engine(str(tmp_path))
+    with TestClient(create_app(eng)) as c:
+        single = {}
+        for p in ("abc", "hello"):
+            r = c.post("/v1/completions", json={"prompt": p, "max_tokens": 4})
+            single[p] = r.json()["choices"][0]["token_ids"]
+        r = c.post("/v1/completions", json={"prompt": ["abc", "hello"], "max_tokens": 4})
+        assert r.status_code == 200, r.text
+        out = r.json()
+        assert [ch["index"] for ch in out["choices"]] == [0, 1]
+        assert out["choices"][0]["token_ids"] == single["abc"]           # greedy: seed-independent
+        assert out["choices"][1]["token_ids"] == single["hello"]
+        assert out["usage"] == {"prompt_tokens": 8, "completion_tokens": 8, "total_tokens": 16}
+        r = c.post("/v1/completions", json={"prompt": [[10, 11, 12], [13, 14]], "max_tokens": 2, "n": 2,
+                                            "temperature": 1.0, "seed": 3})
+        assert r.status_code == 200 and len(r.json()["choices"]) == 4
+        assert r.json()["usage"]["prompt_tokens"] == 5
+        # echo
+        r = c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4, "echo": True})
+        assert r.json()["choices"][0]["text"].startswith("abc")
+        assert r.json()["choices"][0]["token_ids"] == single["abc"]
+        # streamed usage
+        with c.stream("POST", "/v1/completions", json={"prompt": "abc", "max_tokens": 3, "stream": True,
+                                                       "stream_options": {"include_usage": True}}) as s:
+            events = [ln[6:] for ln in s.iter_lines() if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]"
+        usage = json.loads(events[-2])
+        assert usage["choices"] == [] and usage["usage"]["completion_tokens"] == 3
+        assert c.post("/v1/completions", json={"prompt": ["a", "b"], "stream": True}).status_code == 400
+        assert c.post("/v1/completions", json={"prompt": ["a", ""]}).status_code == 400
