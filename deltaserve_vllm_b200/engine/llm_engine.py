@@ -518,6 +518,9 @@ class CoServingEngine:
 
     def abort_request(self, request_id: str) -> bool:
         r = self.scheduler.abort(request_id)
+        if r is not None:
+            self.requests.pop(request_id, None)
+            r.finish_time = time.perf_counter()
         return r is not None
 
     def has_unfinished(self) -> bool:

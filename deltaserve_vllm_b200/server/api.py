@@ -89,6 +89,14 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                              "token_logprobs": list(r.output_logprobs[:len(r.output_ids)])}
         return c
 
+    def _release(rid: str, w) -> None:
+        """Forget a request's waiter; a request still running (the client went
+        away: a cancelled handler or a closed stream) is aborted, so it stops
+        taking batch slots and KV pages."""
+        et.unregister(rid)
+        if not w.done.done():
+            et.submit(lambda e: e.abort_request(rid))
+
     async def _completions_n(body, prompts, params, n, model, chat=False, echo=False):
         """``n`` independent completions of each prompt of a batch (seeds seed,
         seed+1, ...); choice ``p * n + i`` is completion ``i`` of prompt ``p``."""
@@ -114,8 +122,8 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         try:
             reqs = [await w.done for w in waits]
         finally:
-            for x in rids:
-                et.unregister(x)
+            for x, w in zip(rids, waits):
+                _release(x, w)
         ntok = sum(len(r.output_ids) for r in reqs)
         nprompt = sum(len(ids) for ids in prompts)
         return JSONResponse(content={
@@ -282,12 +290,12 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                         yield f"data: {json.dumps(use)}\n\n"
                     yield "data: [DONE]\n\n"
                 finally:
-                    et.unregister(rid)
+                    _release(rid, w)
             return StreamingResponse(gen(), media_type="text/event-stream", headers=headers)
         try:
             r = await w.done
         finally:
-            et.unregister(rid)
+            _release(rid, w)
         out = {"id": rid, "object": obj, "created": created, "model": model,
                "choices": [_choice(0, r, chat, echo)],
                "usage": {"prompt_tokens": r.num_prompt, "completion_tokens": len(r.output_ids),

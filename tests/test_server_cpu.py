@@ -341,3 +341,44 @@ def test_api_prompt_batches_echo_and_stream_usage(tmp_path):
         assert usage["choices"] == [] and usage["usage"]["completion_tokens"] == 3
         assert c.post("/v1/completions", json={"prompt": ["a", "b"], "stream": True}).status_code == 400
         assert c.post("/v1/completions", json={"prompt": ["a", ""]}).status_code == 400
+
+
+def test_api_client_disconnect_aborts_request(tmp_path):
+    """A streaming client that goes away mid-generation has its request
+    aborted: it leaves the batch and its KV pages are freed, instead of
+    generating to max_tokens for nobody. Runs a real HTTP server (the test
+    client buffers whole responses) and drops the socket after the first
+    event."""
+    import socket
+    import threading
+    import uvicorn
+    eng = make_engine(str(tmp_path))
+    app = create_app(eng)
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    srv = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    try:
+        assert _wait(lambda: srv.started, 30)
+        body = json.dumps({"prompt": "abc", "max_tokens": 400, "stream": True, "ignore_eos": True}).encode()
+        conn = socket.create_connection(("127.0.0.1", port), timeout=30)
+        conn.sendall(b"POST /v1/completions HTTP/1.1\r\nHost: x\r\nContent-Type: application/json\r\n"
+                     + f"Content-Length: {len(body)}\r\n\r\n".encode() + body)
+        buf = b""
+        while b"data: " not in buf:
+            chunk = conn.recv(4096)
+            assert chunk, buf
+            buf += chunk
+        live = [r for r in list(eng.requests.values()) if not r.is_ft]
+        assert len(live) == 1
+        req = live[0]
+        conn.close()
+        assert _wait(lambda: req.status.name == "ABORTED", 30), (req.status, len(req.output_ids))
+        assert len(req.output_ids) < 400
+        assert req.request_id not in eng.requests
+        assert _wait(lambda: all(r.is_ft for r in list(eng.scheduler.running) + list(eng.scheduler.waiting)), 30)
+    finally:
+        srv.should_exit = True
+        th.join(30)
