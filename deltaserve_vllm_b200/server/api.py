@@ -57,6 +57,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     app.state.engine_thread = et
     app.state.engine = engine
     app.state.server = None        # a uvicorn.Server, set by the launcher for /shutdown
+    app.state.started_at = time.time()
     model_name = served_model_name or engine.ecfg.served_model_name or engine.ecfg.model
     tok = tokenizer or engine.tokenizer
     if tok is None:
@@ -141,7 +142,8 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
     # ------------------------------------------------------------ inference
     @app.get("/health")
     async def health():
-        return {"ok": et.alive and et.error is None, "error": et.error}
+        ok = et.alive and et.error is None
+        return JSONResponse(status_code=200 if ok else 503, content={"ok": ok, "error": et.error})
 
     @app.get("/v1/models")
     async def models():
@@ -150,8 +152,12 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             names += [n for n in engine.router.pool.names() if n not in names]
         if route_name:
             names.append(route_name)
-        return {"object": "list", "data": [{"id": n, "object": "model", "owned_by": "deltaserve"}
-                                           for n in names]}
+        created = int(app.state.started_at)
+        ml = engine.ecfg.max_model_len
+        # adapters name the base model as their parent (as vLLM lists LoRA modules)
+        return {"object": "list", "data": [
+            {"id": n, "object": "model", "created": created, "owned_by": "deltaserve", "root": model_name,
+             "parent": None if n == model_name else model_name, "max_model_len": ml} for n in names]}
 
     def _parse_params(body: dict):
         """SamplingParams and n of an OpenAI request body (or an error response)."""

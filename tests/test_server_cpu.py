@@ -49,8 +49,12 @@ def test_api_completions_and_finetuning_control():
         app = create_app(eng)
         with TestClient(app) as c:
             assert c.get("/health").json()["ok"]
-            names = [m["id"] for m in c.get("/v1/models").json()["data"]]
+            data = c.get("/v1/models").json()["data"]
+            names = [m["id"] for m in data]
             assert "qwen3-tiny" in names and "toy" in names
+            by = {m["id"]: m for m in data}
+            assert by["toy"]["parent"] == "qwen3-tiny" and by["qwen3-tiny"]["parent"] is None
+            assert by["toy"]["max_model_len"] == 512
             r = c.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 4})
             assert r.status_code == 200, r.text
             out = r.json()
