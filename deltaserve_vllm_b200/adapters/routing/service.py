@@ -154,6 +154,18 @@ class AdapterRouter:
     def has_pending(self) -> bool:
         return bool(self.pending or self.held)
 
+    def cancel(self, rid: str) -> bool:
+        """Drop a request still waiting for its route decision or for its
+        adapter's slot (its client went away)."""
+        for q in (self.pending, self.held):
+            for item in list(q):
+                if item[0] == rid:
+                    q.remove(item)
+                    if q is self.pending and not item[-1].done():
+                        item[-1].cancel()
+                    return True
+        return False
+
     def _in_use(self) -> set[str]:
         return {r.adapter for r in self.eng.requests.values() if r.adapter}
 

@@ -517,6 +517,8 @@ class CoServingEngine:
         return r
 
     def abort_request(self, request_id: str) -> bool:
+        if self.router is not None and self.router.cancel(request_id):
+            return True
         r = self.scheduler.abort(request_id)
         if r is not None:
             self.requests.pop(request_id, None)

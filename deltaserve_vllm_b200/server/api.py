@@ -255,6 +255,9 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                     headers = decision.headers()
             else:
                 await et.call(lambda e: e.add_request(rid, ids, params, adapter))
+        except asyncio.CancelledError:       # the client went away before the route decision
+            _release(rid, w)
+            raise
         except Exception as e:
             et.unregister(rid)
             return JSONResponse(status_code=400, content={"error": str(e)})

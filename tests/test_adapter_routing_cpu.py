@@ -382,3 +382,16 @@ def test_job_switch_with_indexing_and_admission_stages():
             r = c.post("/v1/completions", json={"model": "auto", "prompt": "the striker scored a goal",
                                                 "max_tokens": 2})
             assert r.headers["x-deltaserve-adapter"] == "sports-ft"
+
+
+def test_router_cancel_drops_pending_request(tmp_path):
+    """Aborting a routed request that still waits for its decision removes it
+    from the router's queue (its future is cancelled; nothing is scheduled)."""
+    from deltaserve_vllm_b200.engine.request import SamplingParams
+    eng = _routing_engine(str(tmp_path), slots=2)
+    fut = eng.router.submit("gone", [5, 6, 7], SamplingParams(max_tokens=4), text="bake bread")
+    keep = eng.router.submit("kept", [5, 6, 7], SamplingParams(max_tokens=4), text="bond yields")
+    assert eng.abort_request("gone")
+    assert fut.cancelled() and not keep.done()
+    assert [p[0] for p in eng.router.pending] == ["kept"]
+    assert not eng.abort_request("gone")
