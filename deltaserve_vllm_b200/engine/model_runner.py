@@ -476,4 +476,15 @@ class ModelRunner:
                 if r.params.logprobs:
                     r.output_logprobs.append(float(v))
             self.last_d2h_bytes += R * 4
+        k = max((r.params.top_logprobs for r in reqs if r.params.logprobs), default=0)
+        if k > 0:
+            # the k most likely tokens of each position under the model's
+            # distribution (log-softmax of the logits)
+            vals, idx = torch.log_softmax(logits[:R].float(), dim=-1).topk(k, dim=-1)
+            vals, idx = vals.cpu().tolist(), idx.cpu().tolist()
+            self.last_d2h_bytes += R * k * 12
+            for r, v, i in zip(reqs, vals, idx):
+                if r.params.logprobs and r.params.top_logprobs > 0:
+                    n = r.params.top_logprobs
+                    r.output_top_logprobs.append(list(zip(i[:n], v[:n])))
         return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}

@@ -25,6 +25,7 @@ class SamplingParams:
     top_k: int = 0                   # 0 = off
     top_p: float = 1.0               # 1 = off
     logprobs: bool = False           # record the chosen token's log-probability
+    top_logprobs: int = 0            # and this many most likely alternatives per position
     stop: tuple[str, ...] = ()       # stop strings (checked on the decoded output)
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
@@ -60,6 +61,7 @@ class Request:
     status: Status = Status.WAITING
     output_ids: list[int] = field(default_factory=list)
     output_logprobs: list[float] = field(default_factory=list)
+    output_top_logprobs: list[list[tuple[int, float]]] = field(default_factory=list)
     stop_reason: str | None = None   # the stop string that ended the request
     num_computed: int = 0            # tokens whose KV is in the cache
     block_ids: list[int] = field(default_factory=list)

@@ -81,13 +81,20 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             c = {"index": index, "message": {"role": "assistant", "content": text},
                  "finish_reason": _finish_reason(r)}
             if r.params.logprobs:
-                c["logprobs"] = {"content": [{"token": tok.decode([t]), "logprob": lp}
-                                             for t, lp in zip(r.output_ids, r.output_logprobs)]}
+                tops = r.output_top_logprobs
+                c["logprobs"] = {"content": [
+                    {"token": tok.decode([t]), "logprob": lp,
+                     **({"top_logprobs": [{"token": tok.decode([a]), "logprob": b} for a, b in tops[j]]}
+                        if j < len(tops) else {})}
+                    for j, (t, lp) in enumerate(zip(r.output_ids, r.output_logprobs))]}
             return c
         c = {"index": index, "text": text, "token_ids": r.output_ids, "finish_reason": _finish_reason(r)}
         if r.params.logprobs:
             c["logprobs"] = {"tokens": [tok.decode([t]) for t in r.output_ids],
                              "token_logprobs": list(r.output_logprobs[:len(r.output_ids)])}
+            if r.params.top_logprobs > 0:
+                c["logprobs"]["top_logprobs"] = [{tok.decode([a]): b for a, b in pos}
+                                                 for pos in r.output_top_logprobs[:len(r.output_ids)]]
         return c
 
     def _release(rid: str, w) -> None:
@@ -159,6 +166,17 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
             {"id": n, "object": "model", "created": created, "owned_by": "deltaserve", "root": model_name,
              "parent": None if n == model_name else model_name, "max_model_len": ml} for n in names]}
 
+    def _top_logprobs(body: dict) -> int:
+        """Alternatives per position: ``top_logprobs`` (chat) or an integer
+        ``logprobs`` (completions); at most 20."""
+        k = body.get("top_logprobs")
+        if k is None and not isinstance(body.get("logprobs"), bool):
+            k = body.get("logprobs")
+        k = int(k or 0)
+        if not 0 <= k <= 20:
+            raise ValueError("top_logprobs / logprobs must be in [0, 20]")
+        return k
+
     def _parse_params(body: dict):
         """SamplingParams and n of an OpenAI request body (or an error response)."""
         stop = body.get("stop") or ()
@@ -174,6 +192,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
                                     top_k=max(0, int(body.get("top_k", 0) or 0)),
                                     top_p=float(body.get("top_p", 1.0) if body.get("top_p") is not None else 1.0),
                                     logprobs=bool(body.get("logprobs") is not None and body.get("logprobs") is not False),
+                                    top_logprobs=_top_logprobs(body),
                                     stop=tuple(str(x) for x in stop),
                                     presence_penalty=float(body.get("presence_penalty") or 0.0),
                                     frequency_penalty=float(body.get("frequency_penalty") or 0.0),

@@ -386,3 +386,23 @@ def test_api_client_disconnect_aborts_request(tmp_path):
     finally:
         srv.should_exit = True
         th.join(30)
+
+
+def test_api_top_logprobs(tmp_path):
+    """logprobs=k (completions) / top_logprobs=k (chat) return the k most
+    likely tokens of every position; under greedy decoding the chosen token
+    is the first of them."""
+    eng = make_engine(str(tmp_path))
+    with TestClient(create_app(eng)) as c:
+        out = c.post("/v1/completions", json={"prompt": "abc", "max_tokens": 3, "logprobs": 3}).json()
+        lp = out["choices"][0]["logprobs"]
+        assert len(lp["top_logprobs"]) == 3 and all(len(d) <= 3 for d in lp["top_logprobs"])
+        for pos, tokstr in zip(lp["top_logprobs"], lp["tokens"]):
+            best = max(pos.values())
+            assert pos.get(tokstr) is not None and abs(pos[tokstr] - best) < 1e-4
+            assert all(v <= 0.0 for v in pos.values())
+        ch = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                  "max_tokens": 2, "logprobs": True, "top_logprobs": 2}).json()
+        content = ch["choices"][0]["logprobs"]["content"]
+        assert len(content) == 2 and all(len(x["top_logprobs"]) == 2 for x in content)
+        assert c.post("/v1/completions", json={"prompt": "a", "logprobs": 21}).status_code == 400
