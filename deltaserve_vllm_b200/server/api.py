@@ -105,6 +105,84 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         if not w.done.done():
             et.submit(lambda e: e.abort_request(rid))
 
+    async def _stream_many(prompts, params, n, model, chat, echo, include_usage):
+        """Streamed ``n`` completions of each prompt of a batch: one event
+        stream whose chunks carry the choice index (``p * n + i``), tokens in
+        the order they are generated, a finish chunk per choice."""
+        import dataclasses as _dc
+        model_adapter = None if model == model_name else model
+        if model_adapter is not None and model_adapter not in engine.adapter_slots:
+            return JSONResponse(status_code=404, content={"error": f"unknown model {model!r}"})
+        base_seed = params.seed if params.seed is not None else int(uuid.uuid4().int % (1 << 31))
+        rids, waits = [], []
+        for k, ids in enumerate(prompts):
+            for i in range(n):
+                rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:24]}"
+                p = _dc.replace(params, seed=base_seed + k * n + i)
+                waits.append(et.register(rid, True))
+                rids.append(rid)
+                try:
+                    await et.call(lambda e, rid=rid, p=p, ids=ids: e.add_request(rid, ids, p, model_adapter))
+                except Exception as ex:
+                    for x, w in zip(rids, waits):
+                        _release(x, w)
+                    return JSONResponse(status_code=400, content={"error": str(ex)})
+        et.notify_arrival()
+        created = int(time.time())
+        obj = ("chat.completion" if chat else "text_completion") + (".chunk" if chat else "")
+        sid = rids[0]
+
+        def event(choice):
+            return f"data: {json.dumps({'id': sid, 'object': obj, 'created': created, 'model': model, 'choices': [choice]})}\n\n"
+
+        async def gen():
+            merged: asyncio.Queue = asyncio.Queue()
+
+            async def pump(idx, w):
+                while True:
+                    toks = await w.tokens.get()
+                    await merged.put((idx, toks))
+                    if toks is None:
+                        return
+            tasks = [asyncio.create_task(pump(j, w)) for j, w in enumerate(waits)]
+            try:
+                if echo:
+                    for j in range(len(waits)):
+                        yield event({"index": j, "text": tok.decode(prompts[j // n]), "token_ids": [],
+                                     "finish_reason": None})
+                started, left = set(), len(waits)
+                while left:
+                    j, toks = await merged.get()
+                    if toks is None:
+                        r = await waits[j].done
+                        left -= 1
+                        yield event({"index": j, "delta": {}, "finish_reason": _finish_reason(r)} if chat else
+                                    {"index": j, "text": "", "finish_reason": _finish_reason(r)})
+                        continue
+                    if chat:
+                        delta = {"content": tok.decode(toks)}
+                        if j not in started:
+                            delta["role"] = "assistant"
+                        ch = {"index": j, "delta": delta, "finish_reason": None}
+                    else:
+                        ch = {"index": j, "text": tok.decode(toks), "token_ids": toks, "finish_reason": None}
+                    started.add(j)
+                    yield event(ch)
+                if include_usage:
+                    reqs = [w.done.result() for w in waits]
+                    npr = sum(len(ids) for ids in prompts)
+                    ntok = sum(len(r.output_ids) for r in reqs)
+                    use = {"id": sid, "object": obj, "created": created, "model": model, "choices": [],
+                           "usage": {"prompt_tokens": npr, "completion_tokens": ntok, "total_tokens": npr + ntok}}
+                    yield f"data: {json.dumps(use)}\n\n"
+                yield "data: [DONE]\n\n"
+            finally:
+                for t in tasks:
+                    t.cancel()
+                for x, w in zip(rids, waits):
+                    _release(x, w)
+        return StreamingResponse(gen(), media_type="text/event-stream")
+
     async def _completions_n(body, prompts, params, n, model, chat=False, echo=False):
         """``n`` independent completions of each prompt of a batch (seeds seed,
         seed+1, ...); choice ``p * n + i`` is completion ``i`` of prompt ``p``."""
@@ -241,8 +319,7 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         include_usage = bool((body.get("stream_options") or {}).get("include_usage", False))
         if n_choices > 1 or len(prompts) > 1:
             if stream:
-                return JSONResponse(status_code=400,
-                                    content={"error": "n > 1 and prompt batches are not supported with stream"})
+                return await _stream_many(prompts, params, n_choices, model, chat, echo, include_usage)
             return await _completions_n(body, prompts, params, n_choices, model, chat, echo)
         ids = prompts[0]
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:24]}"

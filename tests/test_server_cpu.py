@@ -343,7 +343,21 @@ def test_api_prompt_batches_echo_and_stream_usage(tmp_path):
         assert events[-1] == "[DONE]"
         usage = json.loads(events[-2])
         assert usage["choices"] == [] and usage["usage"]["completion_tokens"] == 3
-        assert c.post("/v1/completions", json={"prompt": ["a", "b"], "stream": True}).status_code == 400
+        # streamed batch x n: per-choice token streams equal the non-streamed choices
+        body = {"prompt": ["abc", "hello"], "max_tokens": 3, "n": 2, "temperature": 1.0, "seed": 9}
+        want = [ch["token_ids"] for ch in c.post("/v1/completions", json=body).json()["choices"]]
+        with c.stream("POST", "/v1/completions", json=dict(body, stream=True,
+                                                           stream_options={"include_usage": True})) as s:
+            events = [ln[6:] for ln in s.iter_lines() if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]"
+        got, fins = {}, {}
+        for e in events[:-2]:
+            ch = json.loads(e)["choices"][0]
+            got.setdefault(ch["index"], []).extend(ch.get("token_ids", []))
+            if ch["finish_reason"]:
+                fins[ch["index"]] = ch["finish_reason"]
+        assert [got[j] for j in range(4)] == want and sorted(fins) == [0, 1, 2, 3]
+        assert json.loads(events[-2])["usage"]["completion_tokens"] == 12
         assert c.post("/v1/completions", json={"prompt": ["a", ""]}).status_code == 400
 
 
