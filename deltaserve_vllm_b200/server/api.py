@@ -313,6 +313,13 @@ def create_app(engine, served_model_name: str | None = None, tokenizer=None) -> 
         params, n_choices, err = _parse_params(body)
         if err is not None:
             return err
+        if chat and body.get("max_tokens") is None and body.get("max_completion_tokens") is None:
+            # chat with no limit: up to the end of the context (as vLLM)
+            import dataclasses as _dc
+            room = engine.ecfg.max_model_len - max(len(p) for p in prompts)
+            if room < 1:
+                return JSONResponse(status_code=400, content={"error": "the prompt fills the context"})
+            params = _dc.replace(params, max_tokens=room)
         model = body.get("model") or model_name
         stream = bool(body.get("stream", False))
         echo = bool(body.get("echo", False)) and not chat

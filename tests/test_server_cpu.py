@@ -420,3 +420,15 @@ def test_api_top_logprobs(tmp_path):
         content = ch["choices"][0]["logprobs"]["content"]
         assert len(content) == 2 and all(len(x["top_logprobs"]) == 2 for x in content)
         assert c.post("/v1/completions", json={"prompt": "a", "logprobs": 21}).status_code == 400
+
+
+def test_api_chat_without_max_tokens_runs_to_context_end(tmp_path):
+    """A chat request with no max_tokens may generate until the context
+    (max_model_len) is full, as in vLLM; completions keep OpenAI's 16."""
+    eng = make_engine(str(tmp_path))
+    with TestClient(create_app(eng)) as c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                 "ignore_eos": True}).json()
+        assert r["usage"]["prompt_tokens"] + r["usage"]["completion_tokens"] == 512
+        r = c.post("/v1/completions", json={"prompt": "hi", "ignore_eos": True}).json()
+        assert r["usage"]["completion_tokens"] == 16
