@@ -523,6 +523,8 @@ class CoServingEngine:
         if r is not None:
             self.requests.pop(request_id, None)
             r.finish_time = time.perf_counter()
+            for cb in self.request_listeners:
+                cb("abort", r)
         return r is not None
 
     def has_unfinished(self) -> bool:

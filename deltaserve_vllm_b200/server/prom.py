@@ -73,10 +73,10 @@ class ServingStats:
         self.e2e = _Histogram(E2E_BUCKETS)
 
     def on_request(self, kind: str, req) -> None:
-        if kind != "finish" or getattr(req, "is_ft", False):
+        if kind not in ("finish", "abort") or getattr(req, "is_ft", False):
             return
         from .api import _finish_reason
-        reason = _finish_reason(req)
+        reason = "abort" if kind == "abort" else _finish_reason(req)
         ttft = req.ttft()
         tbts = req.tbts()
         with self.lock:

@@ -397,6 +397,7 @@ def test_api_client_disconnect_aborts_request(tmp_path):
         assert len(req.output_ids) < 400
         assert req.request_id not in eng.requests
         assert _wait(lambda: all(r.is_ft for r in list(eng.scheduler.running) + list(eng.scheduler.waiting)), 30)
+        assert app.state.serving_stats.finished.get("abort") == 1     # /metrics counts the abort
     finally:
         srv.should_exit = True
         th.join(30)
