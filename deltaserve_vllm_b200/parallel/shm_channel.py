@@ -7,11 +7,11 @@ copies the payload out and acknowledges it. Rank 0 waits for every
 acknowledgement of the previous message before it overwrites the slot, so
 followers are never more than one message behind. A payload larger than the
 slot travels through the fallback broadcast (the process group) instead, with
-a marker in the slot. All waits are bounded: a wait raises when the process
-it waits for has exited (every rank records its pid in the header; the
-waiter checks it about every 50 ms once it has started to nap) or after
-``timeout_s``, as a missing rank would make the process-group collectives
-fail.
+a marker in the slot. Every wait raises when the process it waits for has
+exited (every rank records its pid in the header; the waiter checks it about
+every 50 ms once it has started to nap). Waits on acknowledgements and votes
+also end after ``timeout_s``; a follower's wait for the next plan has no time
+limit by default (``recv_timeout_s``), since an idle server sends none.
 
 This replaces a gloo/TCP ``broadcast_object_list`` per engine step (two
 collectives, tens to hundreds of microseconds) with a memory copy; it plays
@@ -35,6 +35,7 @@ _MAX_RANKS = 64     # word, a pid word and two vote words (one per parity)
 _PID = _HDR + _MAX_RANKS
 _VOTE = _HDR + 2 * _MAX_RANKS
 _WORDS = _HDR + 4 * _MAX_RANKS
+_DEFAULT = object()
 _SHM_DIR = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
 
 
@@ -43,7 +44,8 @@ class ChannelUnavailable(RuntimeError):
 
 
 class ShmChannel:
-    def __init__(self, comm, capacity: int = 8 << 20, timeout_s: float = 600.0, name: str | None = None):
+    def __init__(self, comm, capacity: int = 8 << 20, timeout_s: float = 600.0, name: str | None = None,
+                 recv_timeout_s: float | None = None):
         """Collective: every rank of ``comm`` constructs it (rank 0 creates the
         segment and shares its name through ``comm``). Raises
         ``ChannelUnavailable`` on every rank if any rank failed to map it."""
@@ -57,6 +59,9 @@ class ShmChannel:
             # rank of one node takes this branch alike).
             raise ChannelUnavailable(f"shared-memory channel needs x86-64 store ordering, not {platform.machine()}")
         self.timeout_s = timeout_s
+        # A follower waits for the next plan as long as rank 0 lives (an idle
+        # server sends none); the pid check ends the wait if rank 0 exits.
+        self.recv_timeout_s = recv_timeout_s
         self.header_bytes = _WORDS * 8
         size = self.header_bytes + capacity
         err = None
@@ -127,7 +132,8 @@ class ShmChannel:
                 pass
         return None
 
-    def _wait(self, ready, ranks, spin: int, what: str) -> None:
+    def _wait(self, ready, ranks, spin: int, what: str, timeout_s=_DEFAULT) -> None:
+        limit = self.timeout_s if timeout_s is _DEFAULT else timeout_s
         t0 = time.perf_counter()
         last_check = t0
         spins = 0
@@ -141,7 +147,7 @@ class ShmChannel:
                     dead = self._gone(ranks)
                     if dead is not None:
                         raise RuntimeError(f"shm channel: rank {dead} exited ({what})")
-                    if now - t0 > self.timeout_s:
+                    if limit is not None and now - t0 > limit:
                         raise TimeoutError(f"shm channel: timed out ({what})")
 
     # ------------------------------------------------------------ rank 0
@@ -172,7 +178,8 @@ class ShmChannel:
         assert self.rank != 0
         w = self.words
         want = self.seq + 1
-        self._wait(lambda: int(w[0]) >= want, (0,), 2000, "waiting for a step plan from rank 0")
+        self._wait(lambda: int(w[0]) >= want, (0,), 2000, "waiting for a step plan from rank 0",
+                   self.recv_timeout_s)
         self.seq = want
         if int(w[2]):
             w[_HDR + self.rank] = self.seq

@@ -127,3 +127,25 @@ def test_shm_channel_setup_failure_is_agreed():
             assert open(os.path.join(d, f"r{r}")).read() == f"unavailable {world - 1}"
         if os.path.isdir("/dev/shm"):                   # rank 0 removed its segment
             assert not [f for f in os.listdir("/dev/shm") if f.startswith("dsv_tp_")]
+
+
+def _idle_worker(rank, world, port, outdir):
+    import time
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        ch = ShmChannel(TPComm(), capacity=4096, timeout_s=0.5)
+        if rank == 0:
+            time.sleep(2.0)                  # an idle server: no plan for longer than timeout_s
+            ch.send(["late"])
+        else:
+            with open(os.path.join(outdir, "r1"), "w") as f:
+                f.write(repr(ch.recv()))
+        ch.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shm_channel_follower_waits_through_idle_periods():
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_idle_worker, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        assert open(os.path.join(d, "r1")).read() == "['late']"
