@@ -2,21 +2,31 @@
 """Headline benchmark: co-served finetuning tokens/s at >= 99 % SLO attainment,
 with p99 TTFT / TBT, Llama-3-8B architecture (random init, bf16) at TP=N.
 
-Trace: Poisson arrivals at 8 req/s per GPU; prompt lengths
-lognormal (median 512, clipped to 32..4096); output lengths uniform 32..256;
-uniform-random token ids; every inference request uses an r=16 inference LoRA.
-Finetuning stream: uniform-random 512-token sequences, 8 per backward cycle,
-AdamW, trainable r=16 / alpha=32 LoRA on all seven projections. SLOs: TTFT
-500 ms, TBT 60 ms.
+Trace (the Llama-3-8B co-serving configuration): Poisson arrivals at 8 req/s
+per GPU; prompt lengths lognormal (median 512, clipped to 32..4096); output
+lengths uniform 32..256; uniform-random token ids; every inference request
+uses an r=16 inference LoRA. Finetuning stream: uniform-random 512-token
+sequences, 8 per backward cycle, AdamW, trainable r=16 / alpha=32 LoRA on all
+seven projections. SLOs: TTFT 500 ms, TBT 60 ms.
 
-Timing: W warm-up engine steps, then EXACTLY K steps bracketed by a device-wide
+A bench *step* is one second of serving (``--step-s``): every engine
+iteration that runs while one second of the arrival trace is served. The
+metric is a rate over a trace, so the window has to hold many requests and
+many backward cycles to mean anything (at 8 req/s per GPU a 20-step window
+holds about 160 x N requests).
+
+Timing: W warm-up steps, then EXACTLY K steps bracketed by a device-wide
 synchronize + stamp on every rank (the stamps travel in the rank-0 step plan,
 so every rank stamps at the same point); device time of the region is the
 max over ranks. ``value`` = FT tokens forwarded-and-captured for training in
 the region / region seconds (each captured token is trained in the next
-backward cycle). The e2e number is the same count over the wall clock of the
-region measured around the public ``CoServingEngine.step()`` calls, which
-copy every step's inputs host->device (pinned) and read sampled tokens back.
+backward cycle; the tokens whose backward finished inside the region are
+reported next to it as ``ft_tokens_trained``). ``valid_slo`` is true only
+when attainment is >= 99 % over at least 100 requests and at least 3
+backward cycles completed inside the region. The e2e number is the same
+count over the wall clock of the region measured around the public
+``CoServingEngine.step()`` calls, which copy every step's inputs
+host->device (pinned) and read sampled tokens back.
 
 ``--impl reference`` runs the reference plugin (vLLM + DeltaServe) when it can
 run here, else prints an ``unavailable`` line.
@@ -40,15 +50,16 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric/config
+BASELINE_VALUE = None  # the reference publishes no number for this metric on this config
 METRIC = "co-served FT tokens/s at ≥99% SLO attainment; p99 TTFT & TBT (Llama-3-8B TP8)"
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=600)
-    p.add_argument("--warmup", type=int, default=40)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--step-s", type=float, default=1.0, help="seconds of serving per bench step")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--model", default="llama3-8b")
     p.add_argument("--rate-per-gpu", type=float, default=8.0)
@@ -146,14 +157,16 @@ def reference_arm(args) -> None:
 
 def _exit_watchdog(seconds: float = 90.0) -> None:
     """The result line is out: if tearing down (graphs, peer mappings, process
-    group) takes longer than ``seconds``, dump every thread's stack and exit."""
+    group) takes longer than ``seconds``, dump every thread's stack and exit
+    with status 3, so a teardown hang shows up as a failed run."""
     import faulthandler
     import threading
 
     def fire():
+        sys.stderr.write(f"bench: teardown still running after {seconds:.0f} s; exiting with status 3\n")
         faulthandler.dump_traceback(all_threads=True)
         sys.stderr.flush()
-        os._exit(0)
+        os._exit(3)
     t = threading.Timer(seconds, fire)
     t.daemon = True
     t.start()
@@ -229,29 +242,41 @@ def main():
             ti += 1
 
     verbose = os.environ.get("DSV_BENCH_VERBOSE") == "1"
+
+    def bench_step() -> int:
+        """Serve ``--step-s`` seconds of the trace; returns engine iterations."""
+        t_end = time.perf_counter() + args.step_s
+        k = 0
+        while time.perf_counter() < t_end:
+            ingest()
+            eng.step()
+            k += 1
+        return k
+
     for i in range(args.warmup):
-        ingest()
-        eng.step()
+        k = bench_step()
         if verbose:
-            dprint(f"warmup step {i}: {eng.coord.status()['cycle']} cycles, bwd_active={eng.bwd_active}")
+            dprint(f"warmup step {i}: {k} iterations, {eng.coord.status()['cycle']} cycles, "
+                   f"bwd_active={eng.bwd_active}")
     eng.synchronize()
     stats0 = dict(eng.stats)
     l0 = ops.LAUNCHES[0]
-    n_req0 = ti
+    cyc0 = len(eng.coord.history)
+    trk0 = len(eng.tracker.durations)
+    iters = 0
     gpu_idx = os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(args.gpus)))
     with ClockSampler(gpu_idx) as clocks:
         eng.mark("t0")
         w0 = time.perf_counter()
         for _ in range(args.steps):
-            ingest()
-            eng.step()
+            iters += bench_step()
         w1 = time.perf_counter()
         eng.mark("t1")
     regions = eng.gather_region("t0", "t1")
     launches = ops.LAUNCHES[0] - l0
     dev_ms = max(r[0] for r in regions)
     wall_ms = (w1 - w0) * 1e3
-    st = {k: eng.stats[k] - stats0[k] for k in stats0}
+    st = {k: eng.stats.get(k, 0) - stats0.get(k, 0) for k in eng.stats}
     # requests that arrived inside the timed region
     t_lo, t_hi = w0, w1
     reqs = [r for r in list(eng.finished) + list(eng.requests.values())
@@ -276,12 +301,31 @@ def main():
     cs = clocks.summary()
     # Decode-only steps: host time to enqueue the forward vs its GPU time
     # (launch-bound when the first is larger).
-    dec_gpu = [d for f, d in zip(eng.tracker.features, eng.tracker.durations)
-               if f.t_in == 0 and f.t_ft == 0 and f.b_d > 0]
-    n_dec = eng.stats.get("decode_steps", 0)
-    dec_info = {"host_enqueue_ms": round(1e3 * eng.stats.get("decode_enqueue_s", 0.0) / max(1, n_dec), 3),
+    eng._drain_timing(block=True)
+    feats = eng.tracker.features[trk0:]
+    durs = eng.tracker.durations[trk0:]
+    dec_gpu = [d for f, d in zip(feats, durs) if f.t_in == 0 and f.t_ft == 0 and f.b_d > 0]
+    n_dec = st.get("decode_steps", 0)
+    dec_info = {"host_enqueue_ms": round(1e3 * st.get("decode_enqueue_s", 0.0) / max(1, n_dec), 3),
                 "gpu_ms": round(1e3 * float(np.mean(dec_gpu)), 3) if dec_gpu else None,
                 "steps": n_dec}
+    # Engine iterations of the region by kind: count and mean GPU time.
+    kinds: dict = {}
+    for f, d in zip(feats, durs):
+        k = ("ft_only" if f.t_ft > 0 and f.t_in == 0 and f.b_d == 0 else
+             "mixed_ft" if f.t_ft > 0 else "prefill" if f.t_in > 0 else "decode")
+        kinds.setdefault(k, []).append(d)
+    step_kinds = {k: {"n": len(v), "gpu_ms_mean": round(1e3 * float(np.mean(v)), 3),
+                      "gpu_ms_sum": round(1e3 * float(np.sum(v)), 1)} for k, v in kinds.items()}
+    # Backward cycles completed in the region: fill (admission reopened ->
+    # buffer full) and backward (trigger -> trained and published) wall time.
+    hist = eng.coord.history[cyc0:]
+    cyc = {"completed": len(hist),
+           "bwd_gpu_ms_mean": round(float(np.mean([h["gpu_ms"] for h in hist])), 2) if hist else None,
+           "bwd_wall_ms_mean": round(float(np.mean([h["wall_ms"] for h in hist])), 2) if hist else None,
+           "fill_wall_ms_mean": (round(float(np.mean([h["fill_ms"] for h in hist if h.get("fill_ms")])), 2)
+                                 if any(h.get("fill_ms") for h in hist) else None)}
+    enough = len(reqs) >= 100 and len(hist) >= 3
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "FT tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -290,20 +334,26 @@ def main():
         "dtype": "bf16", "data": "synthetic (random-init weights, uniform-random token ids)",
         "config": {"model": args.model, "global_batch": args.ft_batch, "seq_len": args.ft_seq,
                    "parallelism": f"tp{args.gpus}", "rate_req_s": rate,
+                   "step": f"{args.step_s:g} s of serving (all engine iterations in it)",
                    "prompts": "lognormal(median 512, sigma 0.8) clip 32..4096",
                    "outputs": "uniform 32..256", "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
                    "l2": "inputs larger than L2 (16 GB of weights stream every step)",
                    "tp_comm": args.tp_comm, "admission_phase": args.phase,
                    "run_ahead_layers": args.run_ahead},
+        "fused_ar_active": eng.peer_ws is not None,
         "slo_attainment": attain, "p99_ttft_ms": (percentile(ttfts, 99) or 0) * 1e3 if ttfts else None,
         "p99_tbt_ms": (percentile(tbts, 99) or 0) * 1e3 if tbts else None,
         "p50_ttft_ms": (percentile(ttfts, 50) or 0) * 1e3 if ttfts else None,
         "requests_in_region": len(reqs), "ft_tokens": st["ft_tokens_forwarded"],
-        "ft_tokens_trained": st["ft_tokens_trained"], "backward_cycles_total": eng.coord.completed_cycles,
-        "last_loss": eng.coord.last_loss, "valid_slo": (attain is not None and attain >= 0.99),
+        "ft_tokens_trained": st["ft_tokens_trained"],
+        "ft_tokens_trained_per_s": round(st["ft_tokens_trained"] / (dev_ms / 1e3), 2),
+        "backward_cycles_total": eng.coord.completed_cycles, "backward_cycles": cyc,
+        "engine_iterations": iters, "iteration_kinds": step_kinds,
+        "last_loss": eng.coord.last_loss,
+        "valid_slo": bool(attain is not None and attain >= 0.99 and enough),
         "e2e": {"value": round(e2e, 2), "unit": "FT tokens/s (wall clock, public step() API)",
-                "h2d_bytes_per_step": int(st["h2d_bytes"] / max(1, st["steps"])),
-                "d2h_bytes_per_step": int(st["d2h_bytes"] / max(1, st["steps"]))},
+                "h2d_bytes_per_step": int(st["h2d_bytes"] / max(1, args.steps)),
+                "d2h_bytes_per_step": int(st["d2h_bytes"] / max(1, args.steps))},
         "gpu_launches": int(launches), "clocks": cs, "device_ms_per_rank": [round(r[0], 2) for r in regions],
         "decode_steps": dec_info,
     }

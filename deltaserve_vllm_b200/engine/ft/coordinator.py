@@ -64,6 +64,10 @@ class FinetuneCoordinator:
         self.total_trained_tokens = 0
         self.last_loss: float | None = None
         self._t_trigger: float | None = None
+        # When the buffer last became free to fill (the previous cycle's end):
+        # the fill time of a cycle is the gap from there to its trigger.
+        self._t_free: float | None = None
+        self._fill_ms: float | None = None
         self._warned = False
         self.stuck_warn_s, self.stuck_disable_s = stuck_warn_s, stuck_disable_s
         self.rps = RpsTracker()
@@ -156,6 +160,7 @@ class FinetuneCoordinator:
         self.epoch_flush_pending = False
         self.cycle += 1
         self._t_trigger = time.monotonic()
+        self._fill_ms = (self._t_trigger - self._t_free) * 1e3 if self._t_free is not None else None
         self._warned = False
         return True
 
@@ -169,7 +174,9 @@ class FinetuneCoordinator:
         self.last_loss = loss
         rec = {"time": time.time(), "cycle": self.cycle, "epoch": self.current_epoch if epoch is None else epoch,
                "batch_tokens": int(n), "loss": float(loss), "gpu_ms": float(gpu_ms),
-               "wall_ms": float(wall_ms), "total_tokens": self.total_trained_tokens}
+               "wall_ms": float(wall_ms), "total_tokens": self.total_trained_tokens,
+               "fill_ms": self._fill_ms}
+        self._t_free = time.monotonic()
         self.history.append(rec)
         self._log(rec)
         self.fill_count = 0

@@ -1177,6 +1177,14 @@ class CoServingEngine:
         or its teardown waits forever. Safe to call on every rank."""
         if self.cuda:
             torch.cuda.synchronize(self.device)
+        # A cycle cut short by shutdown is a suspended generator whose frame
+        # holds the captured backward graphs (NCCL collectives inside): close
+        # it first, or releasing the trainer's graph table frees nothing and
+        # the process-group teardown waits on those graphs for good.
+        if self._bwd_gen is not None:
+            self._bwd_gen.close()
+            self._bwd_gen = None
+        self._bwd_result = None
         if self.trainer is not None:
             self.trainer.release_graphs()
         if self.runner.graphs is not None:

@@ -191,8 +191,10 @@ class LoraTrainer:
             h = self.bwd.reduce_begin(m.rep_block(m.grads, l + 1, min(L, l + 1 + BUCKET_LAYERS)))
         dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin)
         self.bwd.reduce_end(h, dh.device)
+        self.bwd._mark("wait_bucket")
         if tp and l == 0:
             self.comm.all_reduce(m.rep_block(m.grads, 0, min(L, BUCKET_LAYERS)))
+            self.bwd._mark("bucket_allreduce_last")
         return dh
 
     @torch.no_grad()
@@ -250,19 +252,27 @@ class LoraTrainer:
                 self._cap_stream = torch.cuda.Stream(dev)
             self._cap_stream.wait_stream(stream)
             stream = self._cap_stream
+        # Kernels of this package inside each graph: a replay launches them
+        # again, so the launch count (bench accounting) adds them per replay.
+        gs["kernels"] = {}
         g = torch.cuda.CUDAGraph()
+        k0 = ops.LAUNCHES[0]
         with torch.cuda.graph(g, pool=self._pool, stream=stream):
             loss, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], sci.labels, n_valid)
             gs["loss"].copy_(loss)
             gs["dh"].copy_(dh)
         gs["head"] = g
+        gs["kernels"]["head"] = ops.LAUNCHES[0] - k0
         gs["layers"] = {}
         for l in range(self.arch.num_layers - 1, -1, -1):
             g = torch.cuda.CUDAGraph()
+            k0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, pool=self._pool, stream=stream):
                 dh = self._layer_step(cap, sci, l, gs["dh"])
                 gs["dh"].copy_(dh)
             gs["layers"][l] = g
+            gs["kernels"][l] = ops.LAUNCHES[0] - k0
+        ops.LAUNCHES[0] -= sum(gs["kernels"].values())     # capture launches nothing
         self._graphs[key] = gs
         return gs
 
@@ -302,10 +312,12 @@ class LoraTrainer:
             gs["cos"].copy_(ci.cos)
             gs["sin"].copy_(ci.sin)
             gs["head"].replay()
+            ops.LAUNCHES[0] += gs["kernels"]["head"]
             loss_sum = gs["loss"]
             yield "head"
             for l in range(L - 1, -1, -1):
                 gs["layers"][l].replay()
+                ops.LAUNCHES[0] += gs["kernels"][l]
                 yield l
         else:
             loss_sum, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels, n_valid)
@@ -314,7 +326,9 @@ class LoraTrainer:
                 dh = self._layer_step(cap, ci, l, dh)
                 yield l
         self._optimizer_step(epoch)
+        self.bwd._mark("optimizer")
         self.publish()
+        self.bwd._mark("publish")
         if ev1 is not None:
             ev1.record()
         res = CycleResult(0.0, n, n_valid, 0.0, 0.0, self.step)

@@ -56,7 +56,7 @@ class ModelArch:
 
 
 PRESETS: dict[str, ModelArch] = {
-    # the CPU/gloo plumbing model.
+    # The CPU/gloo plumbing model (tiny Qwen3-style decoder, fp32 checks).
     "qwen3-tiny": ModelArch("qwen3-tiny", "qwen3", 2, 256, 4, 2, 64, 512, 1024,
                             rms_eps=1e-6, rope_theta=1e6, tie_embeddings=True),
     "llama3-tiny": ModelArch("llama3-tiny", "llama", 2, 256, 4, 2, 64, 512, 1024,

@@ -314,6 +314,14 @@ class LoraBackward:
         # interleave between tiles (the backward runs at low priority).
         self.max_ctas = 1 << 30
         self._comm_streams: dict = {}
+        # Optional per-phase CUDA-event recorder (``engine.bwd_profile``):
+        # ``mark(name)`` closes the phase that ends here on the current stream,
+        # ``comm(name, ev0, ev1)`` brackets a collective on its side stream.
+        self.timer = None
+
+    def _mark(self, name: str) -> None:
+        if self.timer is not None:
+            self.timer.mark(name)
 
     # ------------------------------------------------------------ TP sums
     def reduce_begin(self, t: torch.Tensor):
@@ -332,7 +340,14 @@ class LoraBackward:
             cs = self._comm_streams[t.device] = torch.cuda.Stream(t.device)
         cs.wait_stream(torch.cuda.current_stream(t.device))
         with torch.cuda.stream(cs):
-            self.comm.all_reduce(t)
+            if self.timer is not None:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                self.comm.all_reduce(t)
+                ev1.record()
+                self.timer.comm(f"allreduce_{tuple(t.shape)}_{str(t.dtype)[6:]}", ev0, ev1)
+            else:
+                self.comm.all_reduce(t)
         return cs
 
     @staticmethod
@@ -508,18 +523,23 @@ class LoraBackward:
         if n_valid == 0:
             return (torch.zeros((), device=final_in.device),
                     torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device))
+        self._mark("head_norm")
         logits = torch.empty(h.shape[0], head.shape[0], dtype=torch.float32, device=h.device)
         ops.gemm(_bf(h, self.cdt).contiguous(), _bf(head, self.cdt), logits, epi=EPI_F32)
+        self._mark("head_logits")
         loss = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
         dlog = torch.empty(h.shape[0], head.shape[0], dtype=self.cdt, device=h.device)
         ops.ce_fwd_bwd(logits, labels, loss, dlog, 1.0 / n_valid)
         del logits
+        self._mark("head_ce")
         dh = self._mm(dlog, head, b_mn=True)                # [n, D]
         del dlog
+        self._mark("head_dh")
         if final_in.is_cuda:
             d_final = ops.rms_norm_bwd(final_in, dh, w.final_norm, eps)
         else:
             d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
+        self._mark("head_norm")
         return loss.sum(), d_final
 
     # ------------------------------------------------------------ recompute
@@ -601,17 +621,22 @@ class LoraBackward:
         ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
         dz = self.group_dz(layer, "gate_up", d_gu)
         d_x2 = self.dx_gemm(layer, "gate_up", d_gu, lw.gate_up, dz)  # [n, D]
+        self._mark("mlp_dx")
         # The TP sum of d_x2 runs while the factor gradients (which do not
         # read it) are computed.
         h = self.reduce_begin(d_x2)
         self.group_grads(layer, "down", act, dh_c, dz_down)
         self.group_grads(layer, "gate_up", x2, d_gu, dz)
+        self._mark("mlp_factor_grads")
         self.reduce_end(h, dev)
+        self._mark("wait_reduce_mid")
         d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
         d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
+        self._mark("norm_bwd_mid")
         # ---- attention ---------------------------------------------------
         dz_o = self.group_dz(layer, "o", d_mid_c)
         d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o)      # [n, q_l]
+        self._mark("o_dx")
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
         ql, kl = self.hq * self.hd, self.hkv * self.hd
         d_qkv = torch.empty(n, ql + 2 * kl, dtype=cdt, device=dev)
@@ -639,12 +664,18 @@ class LoraBackward:
             dkn = ops.rms_norm_bwd(k_pre, dk.reshape(n * self.hkv, self.hd), lw.k_norm, eps)
             d_qkv[:, :ql] = dqn.view(n, ql)
             d_qkv[:, ql:ql + kl] = dkn.view(n, kl)
+        self._mark("attention")
         x1 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(x, lw.in_ln, x1, eps)
         dz = self.group_dz(layer, "qkv", d_qkv)
         d_x1 = self.dx_gemm(layer, "qkv", d_qkv, lw.qkv, dz)       # [n, D]
+        self._mark("qkv_dx")
         h = self.reduce_begin(d_x1)
         self.group_grads(layer, "o", ctx, d_mid_c, dz_o)
         self.group_grads(layer, "qkv", x1, d_qkv, dz)
+        self._mark("attn_factor_grads")
         self.reduce_end(h, dev)
-        return ops.rms_norm_bwd(x, d_x1, lw.in_ln, eps, add=d_mid)
+        self._mark("wait_reduce_x")
+        out = ops.rms_norm_bwd(x, d_x1, lw.in_ln, eps, add=d_mid)
+        self._mark("norm_bwd_x")
+        return out

@@ -547,6 +547,9 @@ namespace dsv {
 // name as an address: it looks the device address up with cudaGetSymbolAddress.
 static __device__ __align__(256) float g_noalloc_scratch[DSV_NOALLOC_SCRATCH_FLOATS];
 constexpr int kMaxDevices = 64;
+// Per-device cache of the array's device address. Written without a lock:
+// threads making their first call on one device at the same time each look
+// the address up and store the same value.
 static float* g_noalloc_ptr[kMaxDevices] = {nullptr};
 }  // namespace dsv
 
@@ -557,7 +560,7 @@ extern "C" int dsv_paged_decode_noalloc(const void* q, int q_stride, const void*
   using namespace dsv;
   if (batch == 0) return DSV_NOALLOC_OK;
   if (!q || !k_cache || !v_cache || !block_tables || !ctx_lens || !out || batch < 0 || num_kv_heads <= 0 ||
-      num_heads % num_kv_heads != 0 || splits < 1 || keys_per_split <= 0 || keys_per_split % DC_KEYS != 0 ||
+      num_heads % num_kv_heads != 0 || splits < 1 || keys_per_split < 0 || keys_per_split % DC_KEYS != 0 ||
       block_size <= 0)
     return DSV_NOALLOC_EINVAL;
   const int G = num_heads / num_kv_heads;
@@ -593,13 +596,22 @@ extern "C" int dsv_paged_decode_noalloc(const void* q, int q_stride, const void*
   a.splits = splits;
   a.keys_per_split = keys_per_split;
   a.scale_log2 = scale * 1.4426950408889634f;
+  // An error already pending on this thread belongs to an earlier, unrelated
+  // call: leave it in place for its owner and launch nothing.
+  if (cudaPeekAtLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
   if (cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DC_SMEM) != cudaSuccess)
     return DSV_NOALLOC_ECUDA;
   paged_decode_kernel<<<dim3(batch, num_kv_heads, (unsigned)splits), DC_THREADS, DC_SMEM, stream>>>(a);
-  if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+  if (cudaPeekAtLastError() != cudaSuccess) {
+    (void)cudaGetLastError();  // this launch's own error: consumed and reported
+    return DSV_NOALLOC_ECUDA;
+  }
   if (splits > 1) {
     decode_combine_kernel<<<dim3(batch, (unsigned)num_heads), HD, 0, stream>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return DSV_NOALLOC_ECUDA;
+    if (cudaPeekAtLastError() != cudaSuccess) {
+      (void)cudaGetLastError();
+      return DSV_NOALLOC_ECUDA;
+    }
   }
   return DSV_NOALLOC_OK;
 }

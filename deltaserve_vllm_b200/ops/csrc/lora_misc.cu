@@ -334,7 +334,9 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
       const float z = lr[i] * inv_t;
       m = fmaxf(m, z);
-      n = fminf(n, z);
+      // Masked tokens (-inf, e.g. EOS under min_tokens) stay out of the
+      // bisection range: a -inf lower bound would never move.
+      if (z > -INFINITY) n = fminf(n, z);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -354,7 +356,7 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
       n = fminf(n, redf[w]);
     }
     zmax = m;
-    zmin = n;
+    zmin = fminf(n, m);  // every token masked: an empty range at zmax
   }
   float thr = -INFINITY;  // keep tokens whose scaled logit >= thr
   if (t > 0.f && ((k > 0 && k < V) || p < 1.f)) {
@@ -399,8 +401,10 @@ __global__ void sample_kernel(const float* __restrict__ logits, int64_t sl, cons
     if (t > 0.f) {
       if (v * inv_t < thr) continue;
       const uint64_t h = mix64(seed * 0x100000001B3ull + (uint64_t)i);
-      const float u = ((h >> 40) + 0.5f) * (1.0f / 16777216.0f);  // (0, 1)
-      v = v * inv_t - __logf(-__logf(u));
+      // 23 random bits: (k + 0.5) / 2^23 is exact in fp32 and strictly inside
+      // (0, 1), so -log(-log(u)) is finite for every token.
+      const float u = ((float)(h >> 41) + 0.5f) * (1.0f / 8388608.0f);
+      v = v * inv_t - logf(-logf(u));
     }
     if (v > best) {
       best = v;

@@ -24,6 +24,11 @@
 //   (different streams, or different host threads) race on it. Serialise them
 //   on one stream. Nothing in the array has to start at zero: each call writes
 //   every partial result it later reads.
+// * keys_per_split: a multiple of 64 keys per split, or 0 to let each sequence
+//   split its own context evenly over `splits` (as dsv_paged_decode does).
+// * Errors: DSV_NOALLOC_ECUDA is returned without launching when a CUDA error
+//   from an earlier call is already pending on the thread (it is left in place
+//   for its owner); a failed launch of this call is consumed and reported.
 // * Inputs and outputs are caller-owned device pointers with the layouts of
 //   dsv_paged_decode: q [batch, q_stride] bf16 (head h at h*128), caches
 //   [num_blocks, num_kv_heads, block_size, 128] bf16, block_tables
@@ -37,7 +42,7 @@
 
 enum {
   DSV_NOALLOC_OK = 0,
-  DSV_NOALLOC_EINVAL = 1,    // bad argument (null pointer, group size, split size)
+  DSV_NOALLOC_EINVAL = 1,    // bad argument (null pointer, group size, split size < 0 or not a multiple of 64)
   DSV_NOALLOC_ETOOBIG = 2,   // batch * heads * splits exceeds the scratch array
   DSV_NOALLOC_ECUDA = 3,     // a CUDA call failed (device lookup, symbol address, launch)
 };

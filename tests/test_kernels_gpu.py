@@ -630,3 +630,45 @@ def test_gemm_mn_major_with_lora_block(M, N, K):
     ops.gemm(a, b, out, b_mn=True, epi=ops.EPI_F32, z=z, b2=b2, tile_slots=ts, lora_seg=64, max_ctas=1 << 30)
     exp = a.float() @ b.float() + z.float() @ b2.float()
     torch.testing.assert_close(out, exp, rtol=2e-2, atol=3e-2)
+
+
+def test_sample_gumbel_never_picks_a_negligible_token():
+    """One dominant logit over a 128k vocabulary: with every other token 30
+    nats below it, no sample over ~10k seeds may land elsewhere (the Gumbel
+    noise is finite for every token)."""
+    R, V = 64, 128256
+    logits = torch.full((R, V), -30.0, dtype=torch.float32, device=DEV)
+    hot = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(3)).to(DEV)
+    logits[torch.arange(R, device=DEV), hot] = 0.0
+    out = torch.empty(R, dtype=torch.int64, device=DEV)
+    temps = torch.ones(R, device=DEV)
+    misses = 0
+    for trial in range(160):
+        seeds = torch.arange(R, device=DEV) * 104729 + trial * 7
+        ops.sample(logits, temps, seeds, out)
+        misses += int((out != hot).sum())
+    assert misses == 0, misses
+
+
+def test_sample_topk_topp_with_masked_tokens():
+    """Top-k / top-p still apply when some logits are -inf (tokens masked by
+    min_tokens or logit_bias): the kept set matches the reference rules."""
+    R, V = 24, 32000
+    logits = rnd(R, V, scale=3.0, dtype=torch.float32, seed=93)
+    g = torch.Generator().manual_seed(94)
+    masked = torch.randint(0, V, (R, 40), generator=g)
+    logits[torch.arange(R)[:, None].to(DEV), masked.to(DEV)] = float("-inf")
+    topk = torch.randint(1, 30, (R,), generator=g).to(torch.int32)
+    topp = torch.rand(R, generator=g) * 0.8 + 0.1
+    topp[:6] = 1.0          # top-k alone
+    topk[6:12] = 0          # top-p alone
+    temps = torch.rand(R, generator=g) * 1.5 + 0.3
+    out = torch.empty(R, dtype=torch.int64, device=DEV)
+    for trial in range(4):
+        seeds = torch.arange(R, device=DEV) * 31 + trial
+        ops.sample(logits, temps.to(DEV), seeds, out, top_k=topk.to(DEV), top_p=topp.to(DEV))
+        lc, oc = logits.cpu(), out.cpu()
+        for r in range(R):
+            z = lc[r] / float(temps[r])
+            keep = ref.sample_keep_mask(z, int(topk[r]), min(1.0, float(topp[r]) + 1e-4))
+            assert keep[oc[r]] and torch.isfinite(lc[r, oc[r]]), (r, int(topk[r]), float(topp[r]))

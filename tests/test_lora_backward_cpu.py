@@ -1,4 +1,4 @@
-"""BASELINE config 1 (tp=1 part): the hand-written LoRA backward over the
+"""TP=1 part of the CPU plumbing check: the hand-written LoRA backward over the
 captured activations == torch autograd, fp32, tiny Qwen3-style and Llama-style
 models, LoRA r=8 alpha=16 on all 7 projections, first 16 label positions masked."""
 import pytest

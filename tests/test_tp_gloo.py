@@ -1,4 +1,4 @@
-"""CPU/gloo TP=2 plumbing check. Two ranks run the sharded
+"""CPU/gloo TP=2 plumbing check of the tiny Qwen3-style decoder. Two ranks run the sharded
 serving forward (with its all-reduces) + the hand-written backward (per-layer
 residual all-reduces, bucketed replicated-factor all-reduce, rank-symmetric
 clip). The TP-merged gradients and loss equal torch autograd on the unsharded

@@ -45,13 +45,17 @@ def _case(seed, lens, Hq, Hkv, bs=64):
     return q, kc, vc, bt.cuda(), torch.tensor(lens, dtype=torch.int32, device="cuda")
 
 
-@pytest.mark.parametrize("Hq,Hkv,lens", [(32, 8, [1, 600, 2049, 77]), (16, 8, [300, 5, 1024])])
-def test_noalloc_decode_matches_regular_entry_point(Hq, Hkv, lens):
+@pytest.mark.parametrize("Hq,Hkv,lens,even", [(32, 8, [1, 600, 2049, 77], False), (16, 8, [300, 5, 1024], False),
+                                               (32, 8, [1, 600, 2049, 77], True)])
+def test_noalloc_decode_matches_regular_entry_point(Hq, Hkv, lens, even):
+    """``even``: keys_per_split 0, each sequence splits its own context."""
     fn = _lib()
     scale = 1 / math.sqrt(128)
     for call, seed in enumerate((1, 2)):  # two calls in a row share the scratch array
         q, kc, vc, bt, ctx = _case(seed + 10 * Hq, lens, Hq, Hkv)
         splits, kps = ops.decode_splits(len(lens), Hkv, max(lens))
+        if even:
+            kps = 0
         exp = torch.zeros(len(lens), Hq * 128, dtype=torch.bfloat16, device="cuda")
         po = torch.empty(len(lens) * Hq * splits * 128, device="cuda")
         pml = torch.empty(len(lens) * Hq * splits * 2, device="cuda")
