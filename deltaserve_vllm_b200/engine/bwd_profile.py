@@ -111,6 +111,8 @@ def main() -> None:
     ap.add_argument("--seq-len", type=int, default=512)
     ap.add_argument("--rank", type=int, default=16, help="LoRA rank of the trained adapter")
     ap.add_argument("--cycles", type=int, default=3)
+    ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
+                    help="residual-gradient reductions over peer memory (fused) or NCCL all-reduces")
     ap.add_argument("--out", default="")
     args = ap.parse_args()
 
@@ -147,6 +149,11 @@ def main() -> None:
                                                                     arch.rope_theta, arch.rope_scaling, device=dev))
     trainer.init_random(1)
     trainer.publish()
+    tpws = None
+    if comm is not None and args.tp_comm == "fused":
+        from ..parallel.peer import BwdPeerWorkspace
+        tpws = BwdPeerWorkspace(comm, n + 8, arch.hidden)
+        trainer.bwd.tpws = tpws
     lens = [args.seq_len] * args.seqs
     starts = [i * args.seq_len for i in range(args.seqs)]
     rank0 = tp.rank == 0
@@ -210,7 +217,8 @@ def main() -> None:
         coll["bucket_bytes"] = bucket.numel() * 4
         coll["resid_bytes_fp32"] = f32.numel() * 4
         coll["nccl_max_ctas"] = os.environ.get("NCCL_MAX_CTAS")
-    rec = {"tp": tp.size, "model": args.model, "rows": n, "seqs": args.seqs, "seq_len": args.seq_len,
+    rec = {"tp": tp.size, "tp_comm": args.tp_comm if comm is not None else None, "model": args.model,
+           "rows": n, "seqs": args.seqs, "seq_len": args.seq_len,
            "lora_rank": args.rank,
            "graph_cycle_ms": sum(gms) / len(gms), "graph_cycle_ms_runs": gms,
            "eager_cycle_ms": sum(eager_ms) / len(eager_ms),
@@ -226,6 +234,9 @@ def main() -> None:
             with open(args.out, "w") as f:
                 json.dump(rec, f, indent=1)
     trainer.release_graphs()
+    if tpws is not None:
+        trainer.bwd.tpws = None
+        tpws.close()
     if comm is not None:
         comm.barrier()
         dist.destroy_process_group()

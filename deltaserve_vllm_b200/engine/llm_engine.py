@@ -181,6 +181,17 @@ class CoServingEngine:
             self.adapter_slots[FT_ADAPTER_NAME] = self.ft_slot
             self.runner.ft_slot = self.ft_slot
             self._init_finetuning(ft_adapter)
+        # ---- the backward's residual-gradient reductions over peer memory
+        self.bwd_ws = None
+        if (self.cuda and comm is not None and comm.size > 1 and ecfg.tp_comm == "fused"
+                and self.trainer is not None and self.capture is not None):
+            from ..parallel.peer import BwdPeerWorkspace
+            self.bwd_ws = BwdPeerWorkspace(comm, cap_tokens + 8, self.arch.hidden)
+            if self._self_test_bwd(comm):
+                self.trainer.bwd.tpws = self.bwd_ws
+            else:
+                self.bwd_ws.close()
+                self.bwd_ws = None
         # Every rank builds with the same constructor adapters; later loads
         # are made by the driver and replayed by the followers.
         self._replicate = False
@@ -348,6 +359,37 @@ class CoServingEngine:
         ok = -comm.all_reduce_max_int(-ok)
         if not ok:
             dprint("[tp] fused GEMM + all-reduce failed its self-test: using GEMM + NCCL")
+        return bool(ok)
+
+    def _self_test_bwd(self, comm) -> bool:
+        """Check the backward's push + reduce over peer memory against a GEMM
+        and an NCCL all-reduce before training with it (the decision is the
+        MIN over ranks; a failure keeps the NCCL path for the whole run)."""
+        import torch.distributed as dist
+        ok = 1
+        try:
+            g = torch.Generator(device=self.device).manual_seed(4321 + comm.rank)
+            D = self.arch.hidden
+            for M in (8, 300):
+                a = torch.randn(M, 192, generator=g, device=self.device).to(self.dtype)
+                b = (torch.randn(192, D, generator=g, device=self.device) * 0.05).to(self.dtype)
+                out = torch.zeros(M, D, dtype=torch.float32, device=self.device)
+                ops.gemm_push(a, b, self.bwd_ws)
+                got = ops.tp_reduce_rows(self.bwd_ws, M, 0, out).float().clone()
+                ref = a.float() @ b.float()
+                dist.all_reduce(ref, group=comm.group)
+                err = float((got - ref).abs().max()) / max(1e-6, float(ref.abs().max()))
+                if not err < 2e-2:
+                    ok = 0
+            torch.cuda.synchronize(self.device)
+            if ops.check_device_error() != 0:
+                ok = 0
+        except Exception as e:  # a failing launch must not take serving down
+            dprint(f"[tp] backward peer reduction self-test raised {e!r}")
+            ok = 0
+        ok = -comm.all_reduce_max_int(-ok)
+        if not ok:
+            dprint("[tp] backward peer reduction failed its self-test: using NCCL all-reduces")
         return bool(ok)
 
     def weight_hash(self) -> float:
@@ -567,7 +609,9 @@ class CoServingEngine:
         files = [] if fmt == "dummy" else checkpoint_files(ecfg.model)
         if fmt == "safetensors" and not files:
             raise FileNotFoundError(f"load_format=safetensors but {ecfg.model!r} has no *.safetensors")
-        keep = self.ftcfg.enable_finetuning
+        # The finetuning head works on the serving head's vocabulary shard:
+        # no full copy of the LM head is kept.
+        keep = False
         if files:
             dprint(f"loading {len(files)} safetensors file(s) from {ecfg.model} (tp rank {self.tp.rank})")
             return load_hf_weights(self.arch, ecfg.model, self.tp, device=self.device, dtype=self.dtype,
@@ -867,8 +911,8 @@ class CoServingEngine:
         self._bwd_events.clear()
         self._record(("bwd_start", dict(self._bwd_meta)))
         self._bwd_gen = gen
-        # head + one step per layer + the optimizer/publish step
-        self._bwd_remaining = self.arch.num_layers + 2
+        # head pieces + one step per layer + the optimizer/publish step
+        self._bwd_remaining = self.trainer.num_steps()
 
     @property
     def bwd_active(self) -> bool:
@@ -1196,6 +1240,11 @@ class CoServingEngine:
             self.peer_ws = None
             if self.comm is not None:
                 self.comm.peer_ws = None
+        if self.bwd_ws is not None:
+            if self.trainer is not None:
+                self.trainer.bwd.tpws = None
+            self.bwd_ws.close()
+            self.bwd_ws = None
         if self.plan_chan is not None:
             self.plan_chan.close()
             self.plan_chan = None

@@ -2,7 +2,8 @@
 
 One backward *cycle* trains on the activations of one filled capture buffer:
 
-1. head backward (final norm + LM head + CE, fp32 logits);
+1. head backward (final norm + vocabulary-parallel LM head + cross-entropy,
+   statistics then gradient per vocabulary chunk, no logits stored);
 2. layers L-1 .. 0: hand-written layer backward (``models/lora_backward.py``);
    under TP the replicated factor gradients of every 8 layers are summed with
    one all-reduce of a contiguous slab (the reference buckets the same way,
@@ -39,6 +40,11 @@ from ..models.weights import ModelWeights
 
 BUCKET_LAYERS = 8
 CLIP_NORM = 1.0
+
+
+def _copy_unless_same(dst: torch.Tensor, src: torch.Tensor) -> None:
+    if src.data_ptr() != dst.data_ptr():
+        dst.copy_(src)
 
 
 @dataclass
@@ -189,7 +195,8 @@ class LoraTrainer:
             # step: one all-reduce of their replicated factor gradients, which
             # overlaps this layer's backward (it writes only layer l's).
             h = self.bwd.reduce_begin(m.rep_block(m.grads, l + 1, min(L, l + 1 + BUCKET_LAYERS)))
-        dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin)
+        # The first layer's input gradient feeds nothing that is trained.
+        dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin, need_input_grad=l > 0)
         self.bwd.reduce_end(h, dh.device)
         self.bwd._mark("wait_bucket")
         if tp and l == 0:
@@ -232,9 +239,12 @@ class LoraTrainer:
             self._seen_shapes.add(key)
             return None
         dev = self.masters.params.device
+        # The residual gradient passes between graphs in a static buffer; the
+        # fused TP path keeps it in its own persistent buffer already.
+        dh_buf = (self.bwd._resid32(ci.n_pad, dev)[1] if self.bwd.tpws is not None else
+                  torch.empty(ci.n_pad, self.arch.hidden, dtype=torch.float32, device=dev))
         gs = {"labels": torch.empty(ci.n_pad, dtype=torch.long, device=dev),
-              "cos": torch.empty_like(ci.cos), "sin": torch.empty_like(ci.sin),
-              "dh": torch.empty(ci.n_pad, self.arch.hidden, dtype=torch.float32, device=dev),
+              "cos": torch.empty_like(ci.cos), "sin": torch.empty_like(ci.sin), "dh": dh_buf,
               "loss": torch.zeros((), dtype=torch.float32, device=dev), "n_valid": n_valid}
         gs["labels"].copy_(ci.labels)
         gs["cos"].copy_(ci.cos)
@@ -255,26 +265,42 @@ class LoraTrainer:
         # Kernels of this package inside each graph: a replay launches them
         # again, so the launch count (bench accounting) adds them per replay.
         gs["kernels"] = {}
-        g = torch.cuda.CUDAGraph()
-        k0 = ops.LAUNCHES[0]
-        with torch.cuda.graph(g, pool=self._pool, stream=stream):
-            loss, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], sci.labels, n_valid)
-            gs["loss"].copy_(loss)
-            gs["dh"].copy_(dh)
-        gs["head"] = g
-        gs["kernels"]["head"] = ops.LAUNCHES[0] - k0
+        # The head in pieces (statistics, then each vocabulary chunk): one
+        # graph per piece, each a pause boundary.
+        gs["head"] = []
+        head = self.bwd.head_steps(cap.final_in[:ci.n_pad], sci.labels, n_valid)
+        done = False
+        while not done:
+            g = torch.cuda.CUDAGraph()
+            k0 = ops.LAUNCHES[0]
+            with torch.cuda.graph(g, pool=self._pool, stream=stream):
+                try:
+                    next(head)
+                except StopIteration:
+                    done = True
+                    loss, dh = self.bwd._head_out
+                    gs["loss"].copy_(loss)
+                    _copy_unless_same(gs["dh"], dh)
+            gs["kernels"][("head", len(gs["head"]))] = ops.LAUNCHES[0] - k0
+            gs["head"].append(g)
         gs["layers"] = {}
         for l in range(self.arch.num_layers - 1, -1, -1):
             g = torch.cuda.CUDAGraph()
             k0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, pool=self._pool, stream=stream):
                 dh = self._layer_step(cap, sci, l, gs["dh"])
-                gs["dh"].copy_(dh)
+                _copy_unless_same(gs["dh"], dh)
             gs["layers"][l] = g
             gs["kernels"][l] = ops.LAUNCHES[0] - k0
         ops.LAUNCHES[0] -= sum(gs["kernels"].values())     # capture launches nothing
         self._graphs[key] = gs
         return gs
+
+    def num_steps(self) -> int:
+        """``next`` calls of one :meth:`cycle` until it returns: the head's
+        pieces (statistics + one per vocabulary chunk), every layer, then the
+        optimizer step."""
+        return len(self.bwd.head_chunks()) + 1 + self.arch.num_layers + 1
 
     def release_graphs(self) -> None:
         """Drop every captured graph (and its memory pool)."""
@@ -306,21 +332,25 @@ class LoraTrainer:
         m.grads.zero_()
         n_valid = self.n_valid(lens)
         L = self.arch.num_layers
+        self.bwd.prepare(ci.n_pad, dev)
         gs = self._graph_set(cap, ci, n_valid) if dev.type == "cuda" else None
         if gs is not None:
             gs["labels"].copy_(ci.labels)
             gs["cos"].copy_(ci.cos)
             gs["sin"].copy_(ci.sin)
-            gs["head"].replay()
-            ops.LAUNCHES[0] += gs["kernels"]["head"]
+            for i, g in enumerate(gs["head"]):
+                g.replay()
+                ops.LAUNCHES[0] += gs["kernels"][("head", i)]
+                yield "head"
             loss_sum = gs["loss"]
-            yield "head"
             for l in range(L - 1, -1, -1):
                 gs["layers"][l].replay()
                 ops.LAUNCHES[0] += gs["kernels"][l]
                 yield l
         else:
-            loss_sum, dh = self.bwd.head_backward(cap.final_in[:ci.n_pad], ci.labels, n_valid)
+            for _ in self.bwd.head_steps(cap.final_in[:ci.n_pad], ci.labels, n_valid):
+                yield "head"
+            loss_sum, dh = self.bwd._head_out
             yield "head"
             for l in range(L - 1, -1, -1):
                 dh = self._layer_step(cap, ci, l, dh)

@@ -24,12 +24,17 @@ this engine's fused weights:
   gradient, RMSNorm backward, attention scores/softmax and the LM head / CE in
   fp32 (the reference's precision contract).
 
-Tensor parallelism: ``comm.all_reduce`` sums the per-rank partials of the two
-residual-stream gradients per layer (after the MLP and after the qkv input
-gradient), each issued from a side stream while the factor-gradient GEMMs of
-the same half-layer run; replicated factor gradients (column-parallel ``A``,
-row-parallel ``B``) are summed by the trainer in buckets, overlapped with the
-next layer's backward.
+Tensor parallelism: the two residual-stream gradients per layer (after the MLP
+and after the qkv input gradient) are per-rank partials. On GPUs with the
+peer workspace (:attr:`LoraBackward.tpws`) each dX GEMM pushes its bf16 partial
+rows to their owner rank, which sums them, applies the RMSNorm backward for
+its rows and all-gathers the bf16 result over NVLink (``ops/csrc/tp_bwd.cu``);
+otherwise ``comm.all_reduce`` sums them from a side stream. Either way the
+factor-gradient GEMMs of the same half-layer run meanwhile. The LM head is
+vocabulary-parallel: each rank computes the cross-entropy statistics and
+gradient of its vocabulary slice only. Replicated factor gradients
+(column-parallel ``A``, row-parallel ``B``) are summed by the trainer in
+buckets, overlapped with the next layer's backward.
 """
 
 from __future__ import annotations
@@ -314,6 +319,19 @@ class LoraBackward:
         # interleave between tiles (the backward runs at low priority).
         self.max_ctas = 1 << 30
         self._comm_streams: dict = {}
+        # The head's gradient pass takes the vocabulary slice in chunks of
+        # this many columns (a bf16 [n, chunk] gradient block at a time).
+        self.vocab_chunk = 16384
+        self._head_bufs: dict = {}
+        self._head_out = None
+        # Fused TP path (``parallel.peer.BwdPeerWorkspace``, set by the
+        # engine): residual-gradient reductions over peer memory instead of
+        # NCCL all-reduces. ``resid_bf16`` is then the current residual
+        # gradient's bf16 rows (every row, gathered); the fp32 rows live in
+        # ``_resid32`` (owned rows only).
+        self.tpws = None
+        self.resid_bf16 = None
+        self._r32: dict = {}
         # Optional per-phase CUDA-event recorder (``engine.bwd_profile``):
         # ``mark(name)`` closes the phase that ends here on the current stream,
         # ``comm(name, ev0, ev1)`` brackets a collective on its side stream.
@@ -471,6 +489,30 @@ class LoraBackward:
                  z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas)
         return out
 
+    def prepare(self, n: int, device) -> None:
+        """Allocate the per-shape scratch of a cycle of ``n`` rows (called
+        before any CUDA-graph capture, so no scratch lives in a graph pool)."""
+        if self.w.embed.is_cuda:
+            self._head_scratch(n, device)
+            if self.tpws is not None:
+                self._resid32(n, device)
+
+    def _tile_ones(self, n: int, device) -> torch.Tensor:
+        key = (-(-n // 128), device)
+        ts = self._ones_slots.get(key)
+        if ts is None:
+            ts = torch.ones(key[0], dtype=torch.int32, device=device)
+            self._ones_slots[key] = ts
+        return ts
+
+    def push_dx(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor) -> None:
+        """The fused TP form of :meth:`dx_gemm`: ``dY . W + dZ . A`` in one
+        GEMM whose epilogue pushes each 128-row block's bf16 partial to the
+        block's owner rank (completed by ``ops.tp_reduce_rows``)."""
+        ap = self.slot_A(layer, g)
+        ops.gemm_push(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), self.tpws, z=dZ, b2=ap,
+                      tile_slots=self._tile_ones(dY.shape[0], dY.device), lora_seg=dZ.shape[1])
+
     def group_grads(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor, dZ: torch.Tensor) -> None:
         """Factor gradients of one group into the trainer's grad buffer:
         dA = dZ^T X and dB^T = s Z^T dY with Z^T = A X^T computed directly
@@ -507,40 +549,131 @@ class LoraBackward:
         self.group_grads(layer, g, X, dY, dZ)
 
     # ------------------------------------------------------------ head
+    def head_chunks(self) -> list[tuple[int, int]]:
+        """Column ranges of this rank's vocabulary slice that the head's
+        gradient pass takes one at a time (bounds the bf16 gradient block)."""
+        V = self.w.lm_head.shape[0]
+        return [(c, min(V, c + self.vocab_chunk)) for c in range(0, V, self.vocab_chunk)]
+
+    def _head_scratch(self, n: int, device) -> dict:
+        key = (n, str(device))
+        st = self._head_bufs.get(key)
+        if st is None:
+            V, D = self.w.lm_head.shape
+            ch = min(V, self.vocab_chunk)
+            world = self.comm.size if self.comm is not None else 1
+            f32 = dict(dtype=torch.float32, device=device)
+            st = {"stats": torch.empty(n, 2 * (-(-V // 64)), **f32), "tgt": torch.empty(n, **f32),
+                  "part": torch.empty(n, 3, **f32), "parts": torch.empty(world, n, 3, **f32),
+                  "lse": torch.empty(n, **f32), "loss": torch.empty(n, **f32),
+                  "dlog": torch.empty(n, ch, dtype=self.cdt, device=device), "dh": torch.empty(n, D, **f32)}
+            self._head_bufs = {key: st}
+        return st
+
     def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor,
                       n_valid: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """Final RMSNorm + LM head + CE. Returns (summed loss as a 0-d device
-        tensor, d final_in fp32); the loss is the sum over the ``n_valid``
-        labelled rows and the gradient is already divided by ``n_valid``."""
+        """Final RMSNorm + LM head + cross-entropy on this rank's slice of the
+        vocabulary (the serving head's shard: rows ``[rank * V_l, (rank + 1) * V_l)``).
+
+        1. statistics pass: one GEMM whose epilogue keeps, per row and tile,
+           the max logit and the sum of exponentials (and the label's logit),
+           merged per row; under TP the ranks' (max, sum, label logit) rows are
+           gathered (one small collective) into the row's log-sum-exp;
+        2. gradient pass, per vocabulary chunk: the GEMM recomputes the
+           logits and its epilogue writes ``(softmax - onehot) / n_valid`` in
+           bf16; ``dh += dlog_chunk @ W_chunk`` (fp32);
+        3. ``dh`` is this rank's partial over its slice: summed over the
+           ranks, then the final-norm backward.
+
+        No [n, V] logit tensor exists at any point (the reference's head,
+        ``bwd_services/common/head.py:31-100``, materialises fp32 logits).
+        Returns (summed loss as a 0-d device tensor, d final_in fp32); the
+        loss is the sum over the ``n_valid`` labelled rows and the gradient is
+        already divided by ``n_valid``. Under the fused TP path the returned
+        gradient holds this rank's owned rows (the rest lives in
+        :attr:`resid_bf16`)."""
+        for _ in self.head_steps(final_in, labels, n_valid):
+            pass
+        return self._head_out
+
+    def head_steps(self, final_in: torch.Tensor, labels: torch.Tensor, n_valid: int):
+        """:meth:`head_backward` as a generator that yields between its
+        pieces (statistics, then every vocabulary chunk): the trainer's pause
+        boundaries inside the head. The result is left in ``_head_out``."""
         w = self.w
         eps = self.arch.rms_eps
-        head = w.lm_head_full if w.lm_head_full is not None else w.lm_head
+        head = w.lm_head
+        dev = final_in.device
+        n, D = final_in.shape
+        world = self.comm.size if self.comm is not None else 1
+        v0 = (self.comm.rank if self.comm is not None else 0) * head.shape[0]
         if final_in.is_cuda:    # the norm kernels (bf16 out, fp32 inside)
-            h = torch.empty(final_in.shape, dtype=self.cdt, device=final_in.device)
+            h = torch.empty(final_in.shape, dtype=self.cdt, device=dev)
             ops.rms_norm(final_in, w.final_norm, h, eps)
         else:
             h = rmsnorm_fwd(final_in, w.final_norm, eps)
         if n_valid == 0:
-            return (torch.zeros((), device=final_in.device),
-                    torch.zeros(final_in.shape, dtype=torch.float32, device=final_in.device))
+            self._head_out = (torch.zeros((), device=dev), torch.zeros(n, D, dtype=torch.float32, device=dev))
+            self.resid_bf16 = None
+            return
+        h = _bf(h, self.cdt).contiguous()
+        headc = _bf(head, self.cdt)
+        st = self._head_scratch(n, dev)
         self._mark("head_norm")
-        logits = torch.empty(h.shape[0], head.shape[0], dtype=torch.float32, device=h.device)
-        ops.gemm(_bf(h, self.cdt).contiguous(), _bf(head, self.cdt), logits, epi=EPI_F32)
-        self._mark("head_logits")
-        loss = torch.empty(h.shape[0], dtype=torch.float32, device=h.device)
-        dlog = torch.empty(h.shape[0], head.shape[0], dtype=self.cdt, device=h.device)
-        ops.ce_fwd_bwd(logits, labels, loss, dlog, 1.0 / n_valid)
-        del logits
-        self._mark("head_ce")
-        dh = self._mm(dlog, head, b_mn=True)                # [n, D]
-        del dlog
-        self._mark("head_dh")
-        if final_in.is_cuda:
-            d_final = ops.rms_norm_bwd(final_in, dh, w.final_norm, eps)
+        st["tgt"].zero_()
+        tiles = ops.ce_stats(h, headc, labels, v0, st["stats"], st["tgt"])
+        ops.ce_merge(st["stats"], tiles, st["tgt"], st["part"])
+        if world > 1:
+            self.comm.all_gather_into(st["parts"], st["part"])
+            parts = st["parts"]
         else:
-            d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
+            parts = st["part"].view(1, n, 3)
+        ops.ce_finalize(parts, labels, st["lse"], st["loss"])
+        self._mark("head_stats")
+        yield "head_stats"
+        chunks = self.head_chunks()
+        fused = self.tpws is not None and final_in.is_cuda
+        dh = st["dh"]
+        for i, (c0, c1) in enumerate(chunks):
+            dlog = st["dlog"][:, :c1 - c0]
+            ops.ce_grad(h, headc[c0:c1], labels, v0 + c0, st["lse"], 1.0 / n_valid, dlog)
+            last = i == len(chunks) - 1
+            if fused and last:
+                # The last chunk's product goes straight to the row owners
+                # (with the earlier chunks' fp32 sum added), then the owner
+                # applies the final-norm backward and all-gathers the rows.
+                ops.gemm_push(dlog, headc[c0:c1], self.tpws, add=dh if i > 0 else None)
+            else:
+                ops.gemm(dlog, headc[c0:c1], dh, b_mn=True, epi=EPI_F32 if i == 0 else EPI_F32_ACCUM)
+            self._mark("head_grad")
+            if not last:
+                yield "head_chunk"
+        loss = st["loss"].sum()
+        if fused:
+            r32 = self._resid32(n, dev)[1]
+            self.resid_bf16 = ops.tp_reduce_rows(self.tpws, n, 1, r32, x=final_in, w=w.final_norm, eps=eps)
+            d_final = r32
+        else:
+            if world > 1:
+                self.comm.all_reduce(dh)
+            if final_in.is_cuda:
+                d_final = ops.rms_norm_bwd(final_in, dh, w.final_norm, eps)
+            else:
+                d_final = rmsnorm_bwd(final_in, dh, w.final_norm, eps)
+            self.resid_bf16 = None
         self._mark("head_norm")
-        return loss.sum(), d_final
+        self._head_out = (loss, d_final)
+
+    def _resid32(self, n: int, device) -> list[torch.Tensor]:
+        """The fused TP path's two fp32 residual-gradient buffers [n, D]
+        (only this rank's owned rows are ever written or read)."""
+        key = (n, str(device))
+        r = self._r32.get(key)
+        if r is None:
+            D = self.arch.hidden
+            r = [torch.zeros(n, D, dtype=torch.float32, device=device) for _ in range(2)]
+            self._r32 = {key: r}
+        return r
 
     # ------------------------------------------------------------ recompute
     def _proj_lora(self, layer: int, g: str, X: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
@@ -589,9 +722,23 @@ class LoraBackward:
                 t[:, ql + kl:].view(n, self.hkv, self.hd))
 
     def layer_backward(self, layer: int, dh: torch.Tensor, saved: dict, ci: CycleInputs,
-                       positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+                       positions: torch.Tensor, cos_sin: torch.Tensor,
+                       need_input_grad: bool = True) -> torch.Tensor:
         """dh: fp32 [n, D] gradient w.r.t. the layer output. Returns the gradient
-        w.r.t. the layer input (fp32); this layer's factor gradients are written."""
+        w.r.t. the layer input (fp32); this layer's factor gradients are written.
+        With ``need_input_grad`` False (the first layer: nothing below it is
+        trained) the input gradient is not computed and ``dh`` comes back.
+
+        Under TP the two residual-stream gradients (after the MLP and after
+        the qkv input gradient) are per-rank partials. With the fused path
+        (:attr:`tpws`) each dX GEMM pushes its bf16 partial rows to their
+        owner rank, the owner sums them and applies the RMSNorm backward
+        (plus the residual gradient) for its rows, and the bf16 rows are
+        all-gathered — the reference's ``reduce_partial`` all-reduces
+        (``bwd_services/llama3.py:178-180, 210-211``) as GEMM ->
+        reduce-scatter -> norm -> all-gather over NVLink; the factor-gradient
+        GEMMs run while the partials travel. Otherwise ``comm.all_reduce``
+        sums them on a side stream."""
         w = self.w
         lw = w.layers[layer]
         eps = self.arch.rms_eps
@@ -600,8 +747,9 @@ class LoraBackward:
         n, D = x.shape
         dev = x.device
         cdt = self.cdt
+        fused = self.tpws is not None and x.is_cuda
         # ---- MLP -------------------------------------------------------
-        dh_c = _bf(dh, cdt)
+        dh_c = self.resid_bf16 if fused else _bf(dh, cdt)
         dz = self.group_dz(layer, "down", dh_c)
         # d(act) = dh . W_down (+ adapter), then the SwiGLU backward gives
         # d(gate_up) (and the activation when it was not captured).
@@ -620,19 +768,30 @@ class LoraBackward:
         x2 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(resid_mid, lw.post_ln, x2, eps)
         dz = self.group_dz(layer, "gate_up", d_gu)
-        d_x2 = self.dx_gemm(layer, "gate_up", d_gu, lw.gate_up, dz)  # [n, D]
-        self._mark("mlp_dx")
-        # The TP sum of d_x2 runs while the factor gradients (which do not
-        # read it) are computed.
-        h = self.reduce_begin(d_x2)
-        self.group_grads(layer, "down", act, dh_c, dz_down)
-        self.group_grads(layer, "gate_up", x2, d_gu, dz)
-        self._mark("mlp_factor_grads")
-        self.reduce_end(h, dev)
-        self._mark("wait_reduce_mid")
-        d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
-        d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
-        self._mark("norm_bwd_mid")
+        if fused:
+            self.push_dx(layer, "gate_up", d_gu, lw.gate_up, dz)
+            self._mark("mlp_dx")
+            self.group_grads(layer, "down", act, dh_c, dz_down)
+            self.group_grads(layer, "gate_up", x2, d_gu, dz)
+            self._mark("mlp_factor_grads")
+            r32 = self._resid32(n, dev)
+            d_mid_c = ops.tp_reduce_rows(self.tpws, n, 0, r32[0], x=resid_mid, w=lw.post_ln, eps=eps, add=dh)
+            d_mid = r32[0]
+            self._mark("reduce_norm_mid")
+        else:
+            d_x2 = self.dx_gemm(layer, "gate_up", d_gu, lw.gate_up, dz)  # [n, D]
+            self._mark("mlp_dx")
+            # The TP sum of d_x2 runs while the factor gradients (which do not
+            # read it) are computed.
+            h = self.reduce_begin(d_x2)
+            self.group_grads(layer, "down", act, dh_c, dz_down)
+            self.group_grads(layer, "gate_up", x2, d_gu, dz)
+            self._mark("mlp_factor_grads")
+            self.reduce_end(h, dev)
+            self._mark("wait_reduce_mid")
+            d_mid_c = torch.empty(n, D, dtype=cdt, device=dev)
+            d_mid = ops.rms_norm_bwd(resid_mid, d_x2, lw.post_ln, eps, add=dh, out_bf16=d_mid_c)
+            self._mark("norm_bwd_mid")
         # ---- attention ---------------------------------------------------
         dz_o = self.group_dz(layer, "o", d_mid_c)
         d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o)      # [n, q_l]
@@ -668,6 +827,21 @@ class LoraBackward:
         x1 = torch.empty(n, D, dtype=x.dtype, device=dev)
         ops.rms_norm(x, lw.in_ln, x1, eps)
         dz = self.group_dz(layer, "qkv", d_qkv)
+        if not need_input_grad:
+            self.group_grads(layer, "o", ctx, d_mid_c, dz_o)
+            self.group_grads(layer, "qkv", x1, d_qkv, dz)
+            self._mark("attn_factor_grads")
+            return dh
+        if fused:
+            self.push_dx(layer, "qkv", d_qkv, lw.qkv, dz)
+            self._mark("qkv_dx")
+            self.group_grads(layer, "o", ctx, d_mid_c, dz_o)
+            self.group_grads(layer, "qkv", x1, d_qkv, dz)
+            self._mark("attn_factor_grads")
+            r32 = self._resid32(n, dev)
+            self.resid_bf16 = ops.tp_reduce_rows(self.tpws, n, 1, r32[1], x=x, w=lw.in_ln, eps=eps, add=d_mid)
+            self._mark("reduce_norm_x")
+            return r32[1]
         d_x1 = self.dx_gemm(layer, "qkv", d_qkv, lw.qkv, dz)       # [n, D]
         self._mark("qkv_dx")
         h = self.reduce_begin(d_x1)

@@ -308,3 +308,71 @@ def sample(logits, temps, seeds, out, top_k=None, top_p=None, logprobs=None):
         return out
     ref.sample(logits, temps, seeds, out, top_k, top_p, logprobs)
     return out
+
+
+# ----------------------------------------------------------------- LM head + CE (vocabulary slices)
+
+def ce_stats(h, w, labels, v0, stats, tgt) -> int:
+    """Softmax statistics of ``logits = h @ w.T`` (``w``: vocabulary rows
+    ``[v0, v0 + N)``) without storing the logits: per row and N tile
+    (max, sum exp(logit - max)) into ``stats`` (fp32 [M, >= 2 * ceil(N / 64)],
+    float pairs) and the label's logit into ``tgt`` (rows whose label is
+    outside the slice keep their value). Returns the tiles per row."""
+    if h.is_cuda:
+        return int(_native().gemm_ce_stats(h, w, labels, int(v0), stats, tgt))
+    return ref.ce_stats(h, w, labels, int(v0), stats, tgt)
+
+
+def ce_merge(stats, n_tiles, tgt, part):
+    """part [M, 3] = (max, sum exp, label logit) of this vocabulary slice."""
+    if part.is_cuda:
+        _native().ce_merge(stats, int(n_tiles), tgt, part)
+        return part
+    return ref.ce_merge(stats, int(n_tiles), tgt, part)
+
+
+def ce_finalize(parts, labels, lse, loss):
+    """Across slices (``parts`` [slices, M, 3]): log-sum-exp per row and the
+    loss ``lse - logit[label]`` (0 on rows without a label)."""
+    if parts.is_cuda:
+        _native().ce_finalize(parts, labels, lse, loss)
+        return lse, loss
+    return ref.ce_finalize(parts, labels, lse, loss)
+
+
+def ce_grad(h, w, labels, v0, lse, scale, dlog):
+    """bf16 ``dlog = (softmax - onehot) * scale`` for ``logits = h @ w.T``
+    (``w``: vocabulary rows ``[v0, v0 + N)``), recomputed from ``lse``; zero
+    rows where the label is -1."""
+    if h.is_cuda:
+        _native().gemm_ce_grad(h, w, labels, int(v0), lse, float(scale), dlog)
+        return dlog
+    return ref.ce_grad(h, w, labels, int(v0), lse, float(scale), dlog)
+
+
+# ----------------------------------------------------------------- tensor-parallel backward over peer memory
+
+def gemm_push(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, add=None):
+    """``a @ b`` (``b`` MN-major [K, N]) plus the LoRA term, pushed as bf16
+    partial rows to each 128-row block's owner rank in ``ws`` (a
+    :class:`~..parallel.peer.BwdPeerWorkspace`); ``add`` (fp32 [M, N]) is
+    added first. Nothing waits here: :func:`tp_reduce_rows` completes it."""
+    _native().gemm_push(a, b, z, b2, tile_slots, lora_seg, ws.push_table, ws.rank, ws.world, ws.blocks_cap,
+                        ws.ld, add)
+
+
+def tp_reduce_rows(ws, M, buf, out, *, x=None, w=None, eps=0.0, add=None):
+    """Finish a push: wait for this rank's owned row blocks, sum them, apply
+    the RMSNorm backward of ``x`` / ``w`` (when given) plus ``add``, write the
+    fp32 rows into ``out`` (owned rows only) and the bf16 rows into gather
+    buffer ``buf`` (0 or 1) of every rank, then wait for the other ranks'
+    rows. Returns this rank's gather buffer [M, N] (every row)."""
+    ext = _native(3)
+    D = ws.ld
+    n_blocks = -(-M // 128)
+    n_owned = -(-(n_blocks - ws.rank) // ws.world)
+    ext.wait_counts(ws.cnt_addr, n_owned, ws.world * D, 0, 0, 0)
+    ext.reduce_norm_bcast(ws.recv_addr, ws.rank, ws.world, ws.blocks_cap, D, M, D, x, w, float(eps), add, out,
+                          ws.gather_tables[buf])
+    ext.wait_counts(ws.gcnt_addr, n_blocks, 0, M, ws.world, ws.rank)
+    return ws.gather_view(buf, M)

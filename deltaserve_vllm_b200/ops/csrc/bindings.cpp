@@ -18,12 +18,28 @@ int64_t dsv_peer_open(const std::string& handle);
 void dsv_peer_close(int64_t addr);
 void dsv_peer_free(int64_t addr);
 void dsv_peer_zero(int64_t addr, int64_t bytes);
+torch::Tensor dsv_peer_view(int64_t addr, std::vector<int64_t> shape, c10::ScalarType dtype, int64_t device);
+int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor stats,
+                          torch::Tensor tgt);
+void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor lse,
+                      double scale, torch::Tensor dlog);
+void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
+                   c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, torch::Tensor table, int64_t rank,
+                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add);
+void dsv_wait_counts(int64_t cnt, int64_t n, int64_t per_block, int64_t rows, int64_t skip_mod, int64_t skip_rem);
+void dsv_reduce_norm_bcast(int64_t recv, int64_t rank, int64_t world, int64_t blocks_cap, int64_t ld, int64_t M,
+                           int64_t D, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> w, double eps,
+                           c10::optional<torch::Tensor> add, torch::Tensor out, torch::Tensor table);
+void dsv_ce_merge(torch::Tensor stats, int64_t n_tiles, torch::Tensor tgt, torch::Tensor part);
+void dsv_ce_finalize(torch::Tensor parts, torch::Tensor labels, torch::Tensor lse, torch::Tensor loss);
 int64_t dsv_read_error_gemm(bool clear);
 int64_t dsv_read_error_attn_bwd(bool clear);
+int64_t dsv_read_error_tp_bwd(bool clear);
 static int64_t dsv_read_error(bool clear) {
   const int64_t g = dsv_read_error_gemm(clear);
   const int64_t a = dsv_read_error_attn_bwd(clear);
-  return g != 0 ? g : a;
+  const int64_t t = dsv_read_error_tp_bwd(clear);
+  return g != 0 ? g : (a != 0 ? a : t);
 }
 void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
                   torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, c10::optional<torch::Tensor> dq,
@@ -61,6 +77,13 @@ void dsv_sample(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &dsv_gemm, "tcgen05 GEMM with fused epilogues / LoRA expand");
   m.def("gemm_ar", &dsv_gemm_ar, "tcgen05 GEMM fused with an all-reduce over peer memory");
+  m.def("gemm_ce_stats", &dsv_gemm_ce_stats, "LM-head GEMM whose epilogue keeps only softmax statistics");
+  m.def("gemm_ce_grad", &dsv_gemm_ce_grad, "LM-head GEMM whose epilogue writes the cross-entropy gradient");
+  m.def("gemm_push", &dsv_gemm_push, "MN-major GEMM pushing bf16 partial rows to their owner rank");
+  m.def("wait_counts", &dsv_wait_counts, "one-CTA bounded wait on this rank's arrival counters");
+  m.def("reduce_norm_bcast", &dsv_reduce_norm_bcast, "owned-row reduce + RMSNorm backward + P2P all-gather");
+  m.def("ce_merge", &dsv_ce_merge, "merge per-tile softmax statistics of one vocabulary slice");
+  m.def("ce_finalize", &dsv_ce_finalize, "log-sum-exp and loss over the ranks' vocabulary slices");
   m.def("peer_alloc", [](int64_t bytes) {
     auto r = dsv_peer_alloc(bytes);
     return std::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));
@@ -69,6 +92,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_close", &dsv_peer_close, "unmap a peer block");
   m.def("peer_free", &dsv_peer_free, "free this rank's block");
   m.def("peer_zero", &dsv_peer_zero, "zero a range of this rank's block");
+  m.def("peer_view", &dsv_peer_view, "tensor over a range of a peer workspace block");
   m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
   m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
   m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");

@@ -33,7 +33,8 @@ namespace dsv {
 
 
 enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4,
-                      kEpiShrink = 5, kEpiBF16T = 6, kEpiSwiGLUBwd = 7 };
+                      kEpiShrink = 5, kEpiBF16T = 6, kEpiSwiGLUBwd = 7, kEpiCEStats = 8, kEpiCEGrad = 9,
+                      kEpiPushRows = 10 };
 
 constexpr int kMaxPeers = 8;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
@@ -54,6 +55,21 @@ struct PeerArgs {
   __nv_bfloat16* out[kMaxPeers];
   uint32_t* rflag[kMaxPeers];
   uint32_t* fflag[kMaxPeers];
+};
+
+// Row push to the row owner (kEpiPushRows, the tensor-parallel backward's
+// "GEMM -> reduce-scatter"): 128-row block mt belongs to rank mt % world; the
+// bf16 partial of a tile goes into the owner's receive rows
+//   recv[owner][((rank * blocks_cap) + mt / world) * 128 + r][ld]
+// (P2P stores), then one thread adds the tile's column count to the owner's
+// arrival counter cnt[owner][mt / world] with release semantics. Nothing
+// here waits: the owner's wait kernel counts world * N columns per block.
+struct PushArgs {
+  int rank, world, blocks_cap, ld;
+  const float* add;       // optional fp32 [M, ld] added to the accumulator before the push
+  int ld_add;
+  __nv_bfloat16* recv[kMaxPeers];
+  uint32_t* cnt[kMaxPeers];
 };
 
 struct GemmArgs {
@@ -85,6 +101,22 @@ struct GemmArgs {
   int ld_aux;
   __nv_bfloat16* aux_out;
   int ld_aux_out;
+  // LM head + cross-entropy (B is this rank's slice of the vocabulary, K-major):
+  // kEpiCEStats writes, per row and N tile, the tile's max logit and
+  // sum(exp(logit - max)) to ce_stats[row * n_tiles + tile], and the logit of
+  // the row's label to ce_tgt[row] when the label falls in the tile;
+  // kEpiCEGrad writes (softmax - onehot) * ce_scale in bf16 to C (zero on
+  // rows without a label), from the row's log-sum-exp ce_lse[row].
+  // Labels are global token ids (-1 = none); column n of this GEMM is token
+  // ce_v0 + n.
+  const int64_t* ce_labels;
+  int64_t ce_v0;
+  float2* ce_stats;
+  int ce_ld;              // row pitch of ce_stats (float2 elements)
+  float* ce_tgt;
+  const float* ce_lse;
+  float ce_scale;
+  PushArgs push;          // kEpiPushRows only
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -392,6 +424,72 @@ __device__ __forceinline__ void peer_reducer(const GemmArgs& args, int m_tiles, 
   }
 }
 
+// Row push (kEpiPushRows): the 128 x BN tile's bf16 partial goes to the row
+// block's owner rank (P2P stores through the warp's staging area, as in
+// push_rows_32x32, with the receive rows `ld` elements apart), then one
+// thread publishes the tile's column count on the owner's block counter.
+// Every epilogue warp of the CTA calls this for every tile (also after a
+// failed accumulator wait, with the TMEM reads skipped), so the four warps
+// always meet at the named barrier.
+__device__ __forceinline__ void push_rows_pitch(uint4* stg, const float* v, __nv_bfloat16* tile_base, int ld, int q,
+                                                int lane, int c, int rows_valid) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    pk[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    stg[lane * 4 + (k ^ (lane & 3))] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2), ch = lane & 3;
+    const uint4 val = stg[r * 4 + (ch ^ (r & 3))];
+    if (q * 32 + r < rows_valid)
+      *reinterpret_cast<uint4*>(tile_base + (size_t)(q * 32 + r) * ld + c + ch * 8) = val;
+  }
+  __syncwarp();
+}
+
+template <int BN>
+__device__ __forceinline__ void push_rows_tile(const GemmArgs& args, uint32_t t_row, int mt128, int n0, int q,
+                                               int lane, bool acc_ok, uint4* stg) {
+  const PushArgs& P = args.push;
+  const int owner = mt128 % P.world, local = mt128 / P.world;
+  const int rows_valid = min(BM, args.M - mt128 * BM);   // <= 0: a pair CTA past the last row
+  const int row = mt128 * BM + q * 32 + lane;
+  __nv_bfloat16* base = P.recv[owner] + (size_t)(P.rank * P.blocks_cap + local) * BM * P.ld + n0;
+#pragma unroll 1
+  for (int c = 0; c < BN && acc_ok && rows_valid > 0; c += 32) {
+    if (n0 + c >= args.N) break;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c, r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    if (P.add != nullptr && row < args.M) {
+      const float4* a4 = reinterpret_cast<const float4*>(P.add + (size_t)row * P.ld_add + n0 + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 f = a4[i];
+        v[4 * i] += f.x;
+        v[4 * i + 1] += f.y;
+        v[4 * i + 2] += f.z;
+        v[4 * i + 3] += f.w;
+      }
+    }
+    push_rows_pitch(stg, v, base, P.ld, q, lane, c, rows_valid);
+  }
+  named_bar_sync(1, 128);
+  if (q == 0 && lane == 0 && acc_ok && rows_valid > 0) {
+    __threadfence_system();
+    red_release_sys_add(P.cnt[owner] + local, (uint32_t)min(BN, args.N - n0));
+  }
+}
+
 // Epilogue of one tile row for the plain store kinds (bf16 / fp32 /
 // fp32-accumulate, or SwiGLU over 64-interleaved gate/up columns), plus the
 // optional raw-row capture: this thread's TMEM lane `t_row` holds output row
@@ -429,6 +527,77 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, uint32_t t_r
           }
         }
       }
+    }
+  } else if constexpr (EPI == kEpiCEStats) {
+    // Online max / sum-exp over this tile's columns (32 at a time), and the
+    // label's logit when the label falls in the tile.
+    int lab = -1;
+    if (row_ok) {
+      const int64_t g = args.ce_labels[row];
+      const int64_t L = g - args.ce_v0;
+      if (g >= 0 && L >= n0 && L < n0 + BN && L < args.N) lab = (int)(L - n0);
+    }
+    float m = -INFINITY, ssum = 0.f, tv = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      const int nv = min(32, args.N - (n0 + c));   // the same for every lane
+      if (nv <= 0) continue;
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) cm = fmaxf(cm, __uint_as_float(r[i]));
+      const float mn = fmaxf(m, cm);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) acc += __expf(__uint_as_float(r[i]) - mn);
+      ssum = ssum * __expf(m - mn) + acc;
+      m = mn;
+      if (lab >= c && lab < c + 32) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i == lab - c) tv = __uint_as_float(r[i]);
+      }
+    }
+    if (row_ok) {
+      args.ce_stats[(size_t)row * args.ce_ld + n0 / BN] = make_float2(m, ssum);
+      if (lab >= 0) args.ce_tgt[row] = tv;
+    }
+  } else if constexpr (EPI == kEpiCEGrad) {
+    // d(loss)/d(logit) = (softmax - onehot) / n_valid, recomputed from the
+    // row's log-sum-exp; rows without a label get zeros.
+    int lab = -1;
+    float lse = 0.f, sc = 0.f;
+    if (row_ok) {
+      const int64_t g = args.ce_labels[row];
+      if (g >= 0) {
+        sc = args.ce_scale;
+        lse = args.ce_lse[row];
+        const int64_t L = g - args.ce_v0;
+        if (L >= 0 && L < args.N) lab = (int)L;
+      }
+    }
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      const int col = n0 + c;
+      if (!row_ok || col >= args.N) continue;
+      float v[32];
+      if (sc != 0.f) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          v[i] = (__expf(__uint_as_float(r[i]) - lse) - (col + i == lab ? 1.f : 0.f)) * sc;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col, v,
+                     min(32, args.N - col));
     }
   } else {
 #pragma unroll 1
@@ -629,7 +798,7 @@ __global__ void __launch_bounds__(256, 1)
       bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
       // The fused all-reduce's epilogue warps meet at named barriers: they keep
       // iterating after a failed wait (TMEM reads skipped) so they always meet.
-      if (EPI != kEpiPeerAR && !acc_ok) break;
+      if (EPI != kEpiPeerAR && EPI != kEpiPushRows && !acc_ok) break;
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
@@ -640,6 +809,8 @@ __global__ void __launch_bounds__(256, 1)
         // the four epilogue warps always meet at their named barriers.
         peer_push_tile<BN>(args, tl, t_row, row, row_ok && acc_ok, acc_ok, q, lane, num_m_tiles,
                            staging + q * 128);
+      } else if constexpr (EPI == kEpiPushRows) {
+        push_rows_tile<BN>(args, t_row, tl.mt, n0, q, lane, acc_ok, staging + q * 128);
       } else if (args.k_splits > 1) {
         // Split-K: raw fp32 partial sums; the reduce kernel applies the epilogue.
 #pragma unroll 1
@@ -768,7 +939,8 @@ struct GemmCfgPair {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 6 : 8;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGING = 4 * 2048;  // push epilogue: 2 KB per epilogue warp
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + STAGING;
 };
 
 template <int BN, bool B_MN, int EPI>
@@ -776,8 +948,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmB2,
                         GemmArgs args) {
-  static_assert(EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiF32Accum || EPI == kEpiSwiGLU,
-                "pair GEMM: plain store epilogues only");
+  static_assert(EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiF32Accum || EPI == kEpiSwiGLU ||
+                    EPI == kEpiCEStats || EPI == kEpiCEGrad || EPI == kEpiPushRows,
+                "pair GEMM: row-wise epilogues only");
   using Cfg = GemmCfgPair<BN, B_MN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -789,6 +962,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   uint64_t* drain_bar = acce_bar + 2;       // [1]
   uint64_t* exit_bar = drain_bar + 1;       // [1] the peer CTA is done with the pair
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(exit_bar + 1);
+  uint4* staging = reinterpret_cast<uint4*>(smem + STAGES * Cfg::STAGE_BYTES + 256);  // [4 warps][2 KB]
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -948,13 +1122,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
       const bool acc_ok = __all_sync(0xffffffffu, mbar_wait(&accf_bar[acc], acc_phase, kErrWaitAccFull));
-      if (!acc_ok) break;
+      if (EPI != kEpiPushRows && !acc_ok) break;
       tc_fence_after();
       const int row = mt * 2 * BM + (int)rank * BM + q * 32 + lane;
       const bool row_ok = row < args.M;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       const bool do_save = args.save != nullptr && row_ok && row >= args.save_lo && row < args.save_hi;
-      epilogue_rows<BN, EPI>(args, t_row, row, row_ok, nt * BN, do_save);
+      if constexpr (EPI == kEpiPushRows) {
+        // This CTA's 128 rows are one row block of the push.
+        push_rows_tile<BN>(args, t_row, mt * 2 + (int)rank, nt * BN, q, lane, acc_ok, staging + q * 128);
+      } else {
+        epilogue_rows<BN, EPI>(args, t_row, row, row_ok, nt * BN, do_save);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acce_leader0 + (uint32_t)(acc * sizeof(uint64_t)));
@@ -1149,7 +1328,9 @@ static bool use_pair(int M, int N, int epi, bool b_mn, int bn, int splits, int64
     mode = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   if (mode == 0 || splits != 1 || bn != 256 || force_bn != 0) return false;
-  if (!(epi == kEpiBF16 || epi == kEpiF32 || epi == kEpiF32Accum || (epi == kEpiSwiGLU && !b_mn))) return false;
+  if (!(epi == kEpiBF16 || epi == kEpiF32 || epi == kEpiF32Accum || (epi == kEpiSwiGLU && !b_mn) ||
+        ((epi == kEpiCEStats || epi == kEpiCEGrad) && !b_mn) || (epi == kEpiPushRows && b_mn)))
+    return false;
   if (max_ctas > 0 && max_ctas < num_sms()) return false;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
   return M >= 256 && tiles >= num_sms() / 2;
@@ -1174,14 +1355,17 @@ static int pick_bn(int M, int N, int epi, bool b_mn) {
 
 }  // namespace dsv
 
-// out = a @ b^T (b_mn=false, b is [N, K]) or a @ b (b_mn=true, b is [K_red, N]);
-// optional LoRA expand z @ b2^T over the slots listed per M tile.
-void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
-              c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
-              int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
-              int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
-              c10::optional<torch::Tensor> aux_out) {
+// `extra` (the CE and row-push entry points) carries the fields of those
+// epilogues; the plain entry point passes nullptr.
+static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
+                          c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
+                          c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, c10::optional<torch::Tensor> save,
+                          int64_t save_lo, int64_t save_hi, int64_t save_dst, int64_t force_bn, int64_t max_ctas,
+                          c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out,
+                          const dsv::GemmArgs* extra) {
   using namespace dsv;
+  const bool special = epi == kEpiCEStats || epi == kEpiCEGrad || epi == kEpiPushRows;
+  TORCH_CHECK(special == (extra != nullptr), "dsv_gemm: epilogue needs its own entry point");
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "dsv_gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "dsv_gemm: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "dsv_gemm: row-major 2-D operands");
@@ -1190,7 +1374,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   const int N = b_mn ? (int)b.size(1) : (int)b.size(0);
   TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "dsv_gemm: reduction length mismatch");
   TORCH_CHECK(out.stride(-1) == 1, "dsv_gemm: output rows must be contiguous");
-  if (M == 0 || N == 0) return;
+  if (M == 0 || N == 0) return 64;
   if (epi == kEpiSwiGLU) TORCH_CHECK(N % 128 == 0 && out.size(1) * 2 == N, "dsv_gemm: SwiGLU needs N % 128 == 0");
   if (epi == kEpiSwiGLUBwd) {
     TORCH_CHECK(b_mn && N % 64 == 0 && out.size(1) == 2 * N && aux.has_value(),
@@ -1205,8 +1389,9 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
       TORCH_CHECK(aux_out->scalar_type() == at::kBFloat16 && aux_out->size(0) >= M && aux_out->size(1) == N &&
                       aux_out->stride(1) == 1, "dsv_gemm: aux_out must be bf16 [M, N]");
   }
-  const bool f32_out = (epi == kEpiF32 || epi == kEpiF32Accum);
-  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "dsv_gemm: output dtype");
+  const bool f32_out = (epi == kEpiF32 || epi == kEpiF32Accum || epi == kEpiCEStats);
+  if (epi != kEpiPushRows)  // the push writes peer buffers, not `out`
+    TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "dsv_gemm: output dtype");
   TORCH_CHECK(K > 0, "dsv_gemm: empty reduction");
   c10::cuda::CUDAGuard guard(a.device());
   // Decode-sized batches (one M tile, plain bf16 store, no row capture): swap
@@ -1265,7 +1450,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
                                                    args.ldc, nullptr, 0, 0, 0, 0);
       C10_CUDA_KERNEL_LAUNCH_CHECK();
     }
-    return;
+    return bnt;
   }
   int bn = force_bn > 0 ? (int)force_bn : pick_bn(M, N, (int)epi, b_mn);
   if (b_mn && bn < 64) bn = 64;
@@ -1281,7 +1466,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     const int m_t = (M + BM - 1) / BM;
     const bool uncapped = max_ctas == 0 || max_ctas >= num_sms();
     if (!b_mn && m_t == 1 && max_ctas == 0 && force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
-    if (uncapped && epi != kEpiSwiGLUBwd) {
+    if (uncapped && epi != kEpiSwiGLUBwd && !special) {
       const int tiles = m_t * ((N + bn - 1) / bn);
       if (tiles < num_sms() / 2 && kbs >= 8) {
         splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
@@ -1303,6 +1488,16 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
   args.C = out.data_ptr();
   args.ldc = (int)out.stride(0);
   args.max_ctas = (int)max_ctas;
+  if (extra != nullptr) {
+    args.ce_labels = extra->ce_labels;
+    args.ce_v0 = extra->ce_v0;
+    args.ce_stats = extra->ce_stats;
+    args.ce_ld = extra->ce_ld;
+    args.ce_tgt = extra->ce_tgt;
+    args.ce_lse = extra->ce_lse;
+    args.ce_scale = extra->ce_scale;
+    args.push = extra->push;
+  }
   const bool pair = use_pair(M, N, (int)epi, b_mn, bn, splits, force_bn, max_ctas);
   const int b_box = pair ? bn / 2 : bn;  // a pair CTA stages half of the B tile
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), BM);
@@ -1348,26 +1543,33 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
     if (b_mn) {
       if (epi == kEpiBF16) launch_pair<true, kEpiBF16>(ta, tb, tz, tb2, args, s);
       else if (epi == kEpiF32) launch_pair<true, kEpiF32>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiPushRows) launch_pair<true, kEpiPushRows>(ta, tb, tz, tb2, args, s);
       else launch_pair<true, kEpiF32Accum>(ta, tb, tz, tb2, args, s);
     } else {
       if (epi == kEpiBF16) launch_pair<false, kEpiBF16>(ta, tb, tz, tb2, args, s);
       else if (epi == kEpiF32) launch_pair<false, kEpiF32>(ta, tb, tz, tb2, args, s);
       else if (epi == kEpiF32Accum) launch_pair<false, kEpiF32Accum>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiCEStats) launch_pair<false, kEpiCEStats>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiCEGrad) launch_pair<false, kEpiCEGrad>(ta, tb, tz, tb2, args, s);
       else launch_pair<false, kEpiSwiGLU>(ta, tb, tz, tb2, args, s);
     }
-    return;
+    return 256;
   }
   if (b_mn) {
     if (epi == kEpiBF16) dispatch_bn<true, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32) dispatch_bn<true, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32Accum) dispatch_bn<true, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiSwiGLUBwd) dispatch_bn<true, kEpiSwiGLUBwd>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiPushRows) dispatch_bn<true, kEpiPushRows>(bn, ta, tb, tz, tb2, args, s);
     else TORCH_CHECK(false, "dsv_gemm: unsupported epilogue for MN-major B");
   } else {
     if (epi == kEpiBF16) dispatch_bn<false, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32) dispatch_bn<false, kEpiF32>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiF32Accum) dispatch_bn<false, kEpiF32Accum>(bn, ta, tb, tz, tb2, args, s);
     else if (epi == kEpiSwiGLU) dispatch_bn<false, kEpiSwiGLU>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiCEStats) dispatch_bn<false, kEpiCEStats>(bn, ta, tb, tz, tb2, args, s);
+    else if (epi == kEpiCEGrad) dispatch_bn<false, kEpiCEGrad>(bn, ta, tb, tz, tb2, args, s);
+    else TORCH_CHECK(false, "dsv_gemm: unsupported epilogue for K-major B");
   }
   if (splits > 1) {
     const int64_t work = (epi == kEpiSwiGLU) ? (int64_t)M * (N / 2) : (int64_t)M * N;
@@ -1377,6 +1579,103 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
                                                 args.save_dst);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+  return bn;
+}
+
+// out = a @ b^T (b_mn=false, b is [N, K]) or a @ b (b_mn=true, b is [K_red, N]);
+// optional LoRA expand z @ b2^T over the slots listed per M tile.
+void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, int64_t epi,
+              c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
+              int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
+              int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
+              c10::optional<torch::Tensor> aux_out) {
+  dsv_gemm_impl(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi, save_dst, force_bn,
+                max_ctas, aux, aux_out, nullptr);
+}
+
+// LM-head statistics for cross-entropy without storing logits: for
+// logits = h @ w^T (w = rows [v0, v0 + N) of the vocabulary, [N, K]), writes
+// per row and N tile the tile's (max, sum exp(logit - max)) into `stats`
+// (fp32 [M, >= 2 * ceil(N / 64)], read as float2 pairs) and the label's logit
+// into tgt[row] when the label lies in this slice (other rows untouched).
+// Returns the number of N tiles written per row.
+int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor stats,
+                          torch::Tensor tgt) {
+  using namespace dsv;
+  const int M = (int)h.size(0), N = (int)w.size(0);
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() >= M,
+              "ce_stats: labels must be int64 [>= M]");
+  TORCH_CHECK(stats.scalar_type() == at::kFloat && stats.dim() == 2 && stats.size(0) >= M && stats.stride(1) == 1 &&
+                  stats.size(1) >= 2 * ((N + 63) / 64) && stats.stride(0) % 2 == 0,
+              "ce_stats: stats must be fp32 [M, >= 2 * ceil(N / 64)]");
+  TORCH_CHECK(tgt.scalar_type() == at::kFloat && tgt.is_contiguous() && tgt.numel() >= M, "ce_stats: tgt fp32 [M]");
+  GemmArgs ex{};
+  ex.ce_labels = labels.data_ptr<int64_t>();
+  ex.ce_v0 = v0;
+  ex.ce_stats = reinterpret_cast<float2*>(stats.data_ptr<float>());
+  ex.ce_ld = (int)(stats.stride(0) / 2);
+  ex.ce_tgt = tgt.data_ptr<float>();
+  const int bn = dsv_gemm_impl(h, w, stats, false, kEpiCEStats, c10::nullopt, c10::nullopt, c10::nullopt, 0,
+                               c10::nullopt, 0, 0, 0, 0, 0, c10::nullopt, c10::nullopt, &ex);
+  return (N + bn - 1) / bn;
+}
+
+// Cross-entropy gradient rows from recomputed logits: dlog = (softmax - onehot)
+// * scale in bf16 for logits = h @ w^T, w = rows [v0, v0 + N) of the
+// vocabulary; lse [M] is each row's log-sum-exp over the whole vocabulary;
+// rows whose label is -1 get zeros.
+void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor lse,
+                      double scale, torch::Tensor dlog) {
+  using namespace dsv;
+  const int M = (int)h.size(0);
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() >= M,
+              "ce_grad: labels must be int64 [>= M]");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() >= M, "ce_grad: lse fp32 [M]");
+  TORCH_CHECK(dlog.scalar_type() == at::kBFloat16 && dlog.size(0) >= M && dlog.size(1) == w.size(0),
+              "ce_grad: dlog must be bf16 [M, N]");
+  GemmArgs ex{};
+  ex.ce_labels = labels.data_ptr<int64_t>();
+  ex.ce_v0 = v0;
+  ex.ce_lse = lse.data_ptr<float>();
+  ex.ce_scale = (float)scale;
+  dsv_gemm_impl(h, w, dlog, false, kEpiCEGrad, c10::nullopt, c10::nullopt, c10::nullopt, 0, c10::nullopt, 0, 0, 0,
+                0, 0, c10::nullopt, c10::nullopt, &ex);
+}
+
+// a @ b (MN-major b, [K, N]) (+ the LoRA term z @ b2) pushed to the row
+// owners as bf16 partials (see PushArgs): `table` is an int64 CPU tensor
+// [2, world] of device addresses (receive rows and block counters of every
+// rank); `add` (optional fp32 [M, >= N]) is added before the push.
+void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
+                   c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, torch::Tensor table, int64_t rank,
+                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add) {
+  using namespace dsv;
+  const int M = (int)a.size(0), N = (int)b.size(1);
+  TORCH_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "gemm_push: rank/world");
+  TORCH_CHECK(table.device().is_cpu() && table.scalar_type() == at::kLong && table.size(0) == 2 &&
+                  table.size(1) == world, "gemm_push: table must be int64 [2, world] on the CPU");
+  TORCH_CHECK(N % 32 == 0 && ld >= N && ld % 8 == 0, "gemm_push: N % 32 == 0 and a 16-byte row pitch >= N");
+  TORCH_CHECK(((M + BM - 1) / BM + world - 1) / world <= blocks_cap, "gemm_push: too many rows for the workspace");
+  GemmArgs ex{};
+  PushArgs& P = ex.push;
+  P.rank = (int)rank;
+  P.world = (int)world;
+  P.blocks_cap = (int)blocks_cap;
+  P.ld = (int)ld;
+  if (add.has_value()) {
+    TORCH_CHECK(add->scalar_type() == at::kFloat && add->size(0) >= M && add->size(1) >= N && add->stride(1) == 1 &&
+                    add->stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(add->data_ptr()) % 16 == 0,
+                "gemm_push: add must be fp32 [M, >= N] with 16-byte aligned rows");
+    P.add = add->data_ptr<float>();
+    P.ld_add = (int)add->stride(0);
+  }
+  auto* tab = table.data_ptr<int64_t>();
+  for (int r = 0; r < world; ++r) {
+    P.recv[r] = reinterpret_cast<__nv_bfloat16*>(tab[r]);
+    P.cnt[r] = reinterpret_cast<uint32_t*>(tab[world + r]);
+  }
+  dsv_gemm_impl(a, b, a, true, kEpiPushRows, z, b2, tile_slots, lora_seg, c10::nullopt, 0, 0, 0, 0, 0, c10::nullopt,
+                c10::nullopt, &ex);
 }
 
 // Multi-LoRA shrink on the tensor cores: Z[T, slots*seg] from x[T, K] and the

@@ -45,3 +45,10 @@ void dsv_peer_free(int64_t addr) { C10_CUDA_CHECK(cudaFree(reinterpret_cast<void
 void dsv_peer_zero(int64_t addr, int64_t bytes) {
   C10_CUDA_CHECK(cudaMemset(reinterpret_cast<void*>(addr), 0, (size_t)bytes));
 }
+
+// A tensor over `addr` on `device` (memory owned by a peer workspace block,
+// never freed through PyTorch).
+torch::Tensor dsv_peer_view(int64_t addr, std::vector<int64_t> shape, c10::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, (int)device);
+  return torch::from_blob(reinterpret_cast<void*>(addr), shape, opts);
+}

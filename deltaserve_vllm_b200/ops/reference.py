@@ -325,3 +325,52 @@ def rope_bwd(g: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Ten
     g1, g2 = g[..., :h], g[..., h:]
     c, s = cos[:, None, :].float(), sin[:, None, :].float()
     return torch.cat([g1 * c + g2 * s, g2 * c - g1 * s], dim=-1)
+
+
+# ----------------------------------------------------------------- LM head + CE on vocabulary slices
+# fp32 restatements of ops.ce_stats / ce_merge / ce_finalize / ce_grad (one
+# statistics pair per row instead of per tile: n_tiles = 1).
+
+def ce_stats(h, w, labels, v0, stats, tgt):
+    logits = h.float() @ w.float().t()
+    m = logits.max(-1).values
+    s = torch.exp(logits - m[:, None]).sum(-1)
+    M = h.shape[0]
+    stats[:M, 0] = m
+    stats[:M, 1] = s
+    lab = labels[:M] - v0
+    inside = (labels[:M] >= 0) & (lab >= 0) & (lab < w.shape[0])
+    rows = torch.nonzero(inside).view(-1)
+    tgt[rows] = logits[rows, lab[rows]]
+    return 1
+
+
+def ce_merge(stats, n_tiles, tgt, part):
+    M = part.shape[0]
+    part[:, 0] = stats[:M, 0]
+    part[:, 1] = stats[:M, 1]
+    part[:, 2] = tgt[:M]
+    return part
+
+
+def ce_finalize(parts, labels, lse, loss):
+    m = parts[:, :, 0].max(0).values
+    s = (parts[:, :, 1] * torch.exp(parts[:, :, 0] - m[None])).sum(0)
+    lse.copy_(m + torch.log(s))
+    M = parts.shape[1]
+    loss.copy_(torch.where(labels[:M] >= 0, lse - parts[:, :, 2].sum(0), torch.zeros_like(lse)))
+    return lse, loss
+
+
+def ce_grad(h, w, labels, v0, lse, scale, dlog):
+    logits = h.float() @ w.float().t()
+    g = torch.exp(logits - lse[:, None])
+    M = h.shape[0]
+    lab = labels[:M] - v0
+    inside = (labels[:M] >= 0) & (lab >= 0) & (lab < w.shape[0])
+    rows = torch.nonzero(inside).view(-1)
+    g[rows, lab[rows]] -= 1.0
+    g = g * scale
+    g[labels[:M] < 0] = 0.0
+    dlog.copy_(g.to(dlog.dtype))
+    return dlog

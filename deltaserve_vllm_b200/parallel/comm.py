@@ -42,11 +42,22 @@ class TPComm:
         self.num_collectives += 1
         return torch.cat(parts, dim=1)
 
+    def all_gather_into(self, out: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """``out`` [size, *t.shape] = every rank's ``t`` (rank-major)."""
+        if self.size == 1:
+            out[0].copy_(t)
+            return out
+        flat = out.view((self.size * t.shape[0],) + tuple(t.shape[1:]))   # gloo wants rank-major rows
+        dist.all_gather_into_tensor(flat, t.contiguous(), group=self.group)
+        self.num_collectives += 1
+        return out
+
     def all_gather_rows(self, t: torch.Tensor) -> torch.Tensor:
         if self.size == 1:
             return t
         out = torch.empty((self.size * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        flat = out.view((self.size * t.shape[0],) + tuple(t.shape[1:]))   # gloo wants rank-major rows
+        dist.all_gather_into_tensor(flat, t.contiguous(), group=self.group)
         self.num_collectives += 1
         return out
 

@@ -99,3 +99,95 @@ class PeerWorkspace:
                 self._ext.peer_close(p)
         self._ext.peer_free(self.base)
         self.base = None
+
+
+class BwdPeerWorkspace:
+    """Peer-mapped buffers of the tensor-parallel backward's residual-gradient
+    reductions (``ops.gemm_push`` + ``ops.tp_reduce_rows``): the dX GEMM
+    pushes each 128-row block's bf16 partial to the block's owner
+    (block ``mt`` -> rank ``mt % world``), the owner sums, applies the RMSNorm
+    backward and writes the bf16 rows into every rank's gather buffer.
+
+    One cudaMalloc'd block per rank, opened by every peer (CUDA IPC, plain P2P
+    mappings, no multicast object), holding:
+
+    * ``recv``  — ``[world][blocks_cap][128][ld]`` bf16 partial rows pushed to
+      this rank (``blocks_cap`` = owned row blocks at ``max_rows``);
+    * ``gather`` x 2 — ``[max_rows][ld]`` bf16 reduced rows (two, so the
+      result of one reduction is still readable while the next is gathered);
+    * ``cnt``   — per owned block, columns arrived (reset by this rank);
+    * ``gcnt``  — per row block, rows arrived from its owner (reset by this rank).
+    """
+
+    def __init__(self, comm, max_rows: int, ld: int):
+        from .. import ops
+        ext = ops.native_ext()
+        if ext is None:
+            raise RuntimeError("the tensor-parallel backward workspace needs the CUDA extension")
+        if ld % 32:
+            raise ValueError("the row width must be a multiple of 32")
+        self.comm = comm
+        self.world = comm.size
+        self.rank = comm.rank
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        self.ld = ld
+        self.m_blocks = math.ceil(max_rows / TILE)
+        self.max_rows = self.m_blocks * TILE
+        self.blocks_cap = math.ceil(self.m_blocks / self.world)
+        sizes = [self.world * self.blocks_cap * TILE * ld * 2,   # recv
+                 self.max_rows * ld * 2,                          # gather 0
+                 self.max_rows * ld * 2,                          # gather 1
+                 self.blocks_cap * 4,                             # cnt
+                 self.m_blocks * 4]                               # gcnt
+        self.offsets = []
+        off = 0
+        for sz in sizes:
+            self.offsets.append(off)
+            off += _align(sz)
+        self.bytes = off
+        self._ext = ext
+        self.base, handle = ext.peer_alloc(self.bytes)
+        handles = comm.all_gather_object(handle)
+        self.ptrs = [self.base if r == self.rank else ext.peer_open(h) for r, h in enumerate(handles)]
+        at = lambda k: [p + self.offsets[k] for p in self.ptrs]
+        self.push_table = torch.tensor([at(0), at(3)], dtype=torch.int64)
+        self.gather_tables = [torch.tensor([at(1), at(4)], dtype=torch.int64),
+                              torch.tensor([at(2), at(4)], dtype=torch.int64)]
+        self.recv_addr = self.base + self.offsets[0]
+        self.cnt_addr = self.base + self.offsets[3]
+        self.gcnt_addr = self.base + self.offsets[4]
+        self._views = {}
+        comm.barrier()        # every rank mapped every block before first use
+
+    def gather_view(self, buf: int, rows: int) -> torch.Tensor:
+        """This rank's gather buffer ``buf`` as a bf16 [rows, ld] tensor."""
+        key = (buf, rows)
+        t = self._views.get(key)
+        if t is None:
+            full = self._views.get((buf, None))
+            if full is None:
+                full = _from_ptr(self.base + self.offsets[1 + buf], (self.max_rows, self.ld),
+                                 torch.bfloat16, torch.cuda.current_device())
+                self._views[(buf, None)] = full
+            t = full[:rows]
+            self._views[key] = t
+        return t
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        self.comm.barrier()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.peer_close(p)
+        self._ext.peer_free(self.base)
+        self.base = None
+        self._views.clear()
+
+
+def _from_ptr(addr: int, shape, dtype, device) -> torch.Tensor:
+    """A tensor over ``addr`` (memory owned by the workspace, not by PyTorch)."""
+    from .. import ops
+    return ops.native_ext().peer_view(int(addr), list(shape), dtype, int(device))

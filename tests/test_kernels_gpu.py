@@ -672,3 +672,84 @@ def test_sample_topk_topp_with_masked_tokens():
             z = lc[r] / float(temps[r])
             keep = ref.sample_keep_mask(z, int(topk[r]), min(1.0, float(topp[r]) + 1e-4))
             assert keep[oc[r]] and torch.isfinite(lc[r, oc[r]]), (r, int(topk[r]), float(topp[r]))
+
+
+def _ce_ref(h, W, labels, n_valid):
+    logits = h.float() @ W.float().t()
+    lse = torch.logsumexp(logits, -1)
+    lab = labels.clamp_min(0)
+    loss = torch.where(labels >= 0, lse - logits.gather(1, lab[:, None]).view(-1), torch.zeros_like(lse))
+    g = torch.softmax(logits, -1)
+    g[torch.arange(h.shape[0], device=h.device), lab] -= 1.0
+    g = torch.where((labels >= 0)[:, None], g / n_valid, torch.zeros_like(g))
+    return lse, loss, g
+
+
+@pytest.mark.parametrize("n,V,D", [(300, 5000, 512), (128, 16032, 1024)])
+def test_ce_head_stats_and_grad_vs_fp32(n, V, D):
+    """Vocabulary-slice cross-entropy: the statistics GEMM + merge + finalize
+    give the fp32 log-sum-exp and loss, the gradient GEMM gives
+    (softmax - onehot) / n_valid; with the vocabulary split in two slices (two
+    ranks' shards on one GPU) the merged statistics are the same."""
+    h = rnd(n, D, seed=61)
+    W = rnd(V, D, scale=0.3, seed=62)
+    labels = torch.randint(0, V, (n,), generator=torch.Generator().manual_seed(63)).to(DEV)
+    labels[::7] = -1
+    n_valid = int((labels >= 0).sum())
+    lse_r, loss_r, g_r = _ce_ref(h, W, labels, n_valid)
+    for split in (V, V // 2 + 13):
+        slices = [(0, split), (split, V)] if split < V else [(0, V)]
+        parts = torch.empty(len(slices), n, 3, device=DEV)
+        for i, (a, b) in enumerate(slices):
+            stats = torch.empty(n, 2 * (-(-(b - a) // 64)), device=DEV)
+            tgt = torch.zeros(n, device=DEV)
+            t = ops.ce_stats(h, W[a:b], labels, a, stats, tgt)
+            ops.ce_merge(stats, t, tgt, parts[i])
+        lse = torch.empty(n, device=DEV)
+        loss = torch.empty(n, device=DEV)
+        ops.ce_finalize(parts, labels, lse, loss)
+        torch.testing.assert_close(lse, lse_r, rtol=1e-5, atol=2e-4)
+        torch.testing.assert_close(loss, loss_r, rtol=1e-4, atol=2e-4)
+    for c0, c1 in ((0, 1999), (1999, V)):
+        dlog = torch.empty(n, c1 - c0, dtype=torch.bfloat16, device=DEV)
+        ops.ce_grad(h, W[c0:c1], labels, c0, lse, 1.0 / n_valid, dlog)
+        torch.testing.assert_close(dlog.float(), g_r[:, c0:c1], rtol=2e-2, atol=1e-6)
+    assert ops.check_device_error() == 0
+
+
+class _OneRank:
+    size, rank = 1, 0
+
+    def all_gather_object(self, obj):
+        return [obj]
+
+    def barrier(self):
+        pass
+
+
+@pytest.mark.parametrize("M,K,D", [(300, 192, 512), (1000, 640, 4096)])
+def test_push_reduce_norm_one_rank(M, K, D):
+    """The backward's row push + owner reduce + RMSNorm backward on one rank:
+    the gathered bf16 rows and the fp32 rows equal
+    rmsnorm_bwd(x, a @ b + add_push) + add_norm."""
+    from deltaserve_vllm_b200.parallel.peer import BwdPeerWorkspace
+    ws = BwdPeerWorkspace(_OneRank(), M + 8, D)
+    try:
+        a, b = rnd(M, K, seed=71), rnd(K, D, scale=0.05, seed=72)
+        x, w = rnd(M, D, seed=73), rnd(D, scale=0.2, seed=74) + 1.0
+        add_push = rnd(M, D, dtype=torch.float32, seed=75)
+        add_norm = rnd(M, D, dtype=torch.float32, seed=76)
+        for it in range(2):                      # twice: the counters reset themselves
+            out = torch.zeros(M, D, device=DEV)
+            ops.gemm_push(a, b, ws, add=add_push)
+            got = ops.tp_reduce_rows(ws, M, it % 2, out, x=x, w=w, eps=1e-5, add=add_norm)
+            torch.cuda.synchronize()
+            dy = (a.float() @ b.float() + add_push).bfloat16().float()   # the partial travels in bf16
+            exp = ref.rms_norm_bwd(x.float().cpu(), dy.cpu(), w.float().cpu(), 1e-5, add=add_norm.cpu()).to(DEV)
+            # dy crosses the wire in bf16: a last-bit rounding difference of
+            # the fp32 sum (tensor-core vs torch summation order) is allowed.
+            torch.testing.assert_close(out, exp, rtol=1e-2, atol=1e-2)
+            torch.testing.assert_close(got.float(), exp, rtol=1e-2, atol=1e-2)
+        assert ops.check_device_error() == 0
+    finally:
+        ws.close()

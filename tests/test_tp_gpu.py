@@ -59,9 +59,10 @@ def test_tp2_backward_matches_tp1_on_gpu():
         a, b = torch.load(os.path.join(d, "tp2.pt")), torch.load(os.path.join(d, "tp1.pt"))
         assert abs(a["loss"] - b["loss"]) < 0.01 * abs(b["loss"])
         for k, g in b["grads"].items():
-            x, y = a["grads"][k].flatten().double(), g.flatten().double()
-            cos = float(x @ y / (x.norm() * y.norm() + 1e-30))
-            assert cos > 0.99, (k, cos)
+            x, y = a["grads"][k].double(), g.double()
+            rel_l2 = float((x - y).norm() / (y.norm() + 1e-30))
+            rel_max = float((x - y).abs().max() / (y.abs().max() + 1e-30))
+            assert rel_l2 < 0.05 and rel_max < 0.08, (k, rel_l2, rel_max)
 
 
 def _run_gemm_ar(rank, world, port, outdir):
@@ -100,3 +101,62 @@ def test_fused_gemm_allreduce_tp2():
             res = torch.load(os.path.join(d, f"ar{r}.pt"))
             assert res["code"] == 0
             assert max(res["errs"]) < 2e-2, res["errs"]
+
+
+def _run_fused_vs_nccl(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.adapters.peft_io import merge_tp_shards
+    from deltaserve_vllm_b200.models.configs import PRESETS
+    from deltaserve_vllm_b200.models.lora import random_adapter
+    from deltaserve_vllm_b200.models.weights import TPInfo
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from test_trainer_gpu import run as run_trainer
+    arch = PRESETS["llama3-8b-2l"]
+    g = torch.Generator().manual_seed(7)
+    seqs = [torch.randint(0, arch.vocab, (n,), generator=g).tolist() for n in (512, 200, 333, 130)]
+    ad = random_adapter(arch, 16, seed=3, b_std=0.02)
+    comm = TPComm(None, dist.new_group(backend="gloo"))
+    out = {}
+    for mode in ("nccl", "fused"):
+        tr, res = run_trainer(arch, seqs, ad, "cuda", torch.bfloat16, tp=TPInfo(rank, world), comm=comm,
+                              fused_tp=mode == "fused")
+        shards = comm.gather_objects(tr.masters.export_peft(16, grads=True))
+        if rank == 0:
+            out[mode] = {"loss": res[0].loss, "grads": merge_tp_shards(shards)}
+        if tr.bwd.tpws is not None:
+            tr.bwd.tpws.close()
+            tr.bwd.tpws = None
+    torch.cuda.synchronize()
+    out["code"] = ops.check_device_error()
+    if rank == 0:
+        torch.save(out, os.path.join(outdir, "fused_vs_nccl.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_tp_backward_matches_nccl(world):
+    """The tensor-parallel backward with its residual-gradient reductions
+    fused over peer memory (dX GEMM pushes bf16 partial rows to the row
+    owner, owner reduce + RMSNorm backward + all-gather) gives the same loss
+    and, elementwise, the same LoRA gradients as the NCCL all-reduce path
+    on the same ranks (Llama-3-8B layer geometry, 2 layers)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run_fused_vs_nccl, args=(world, _port(), d), nprocs=world, join=True,
+                           start_method="spawn")
+        r = torch.load(os.path.join(d, "fused_vs_nccl.pt"))
+        assert r["code"] == 0
+        a, b = r["fused"], r["nccl"]
+        assert abs(a["loss"] - b["loss"]) < 1e-3 * abs(b["loss"])
+        for k, y in b["grads"].items():
+            x = a["grads"][k].float()
+            y = y.float()
+            scale = float(y.abs().max()) + 1e-12
+            assert float((x - y).abs().max()) < 3e-2 * scale, (k, float((x - y).abs().max()) / scale)
+            assert float((x - y).norm()) < 1e-2 * (float(y.norm()) + 1e-12), k

@@ -17,7 +17,10 @@ from deltaserve_vllm_b200.models.weights import init_weights
 pytestmark = pytest.mark.gpu
 
 
-def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None):
+def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None, fused_tp=False):
+    """Forward the FT rows through the serving model (capturing activations)
+    and run ``steps`` backward cycles. ``fused_tp``: the residual-gradient
+    reductions over peer memory (the caller closes ``tr.bwd.tpws``)."""
     from deltaserve_vllm_b200.models.weights import TPInfo
     tp = tp or TPInfo()
     w = init_weights(arch, tp=tp, seed=5, device="cpu", dtype=torch.float32).to(device, dtype)
@@ -29,6 +32,9 @@ def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None):
     tr = LoraTrainer(w, served, 1, 16, 32, lr=lr, mask_prefix=16, cos_sin_table=model.cos_sin, comm=comm)
     tr.load_adapter(ad, 16, 32)
     tr.publish()
+    if fused_tp:
+        from deltaserve_vllm_b200.parallel.peer import BwdPeerWorkspace
+        tr.bwd.tpws = BwdPeerWorkspace(comm, n + 8, arch.hidden)
     runner = ModelRunner(model, 64, device, ft_slot=1)
     sched = Scheduler(kv.allocator, 64, max_num_batched_tokens=8192, max_model_len=4096)
     res = []
@@ -60,8 +66,14 @@ def test_gpu_backward_matches_cpu_oracle(name):
     assert abs(gres[0].loss - cres[0].loss) < 0.02 * abs(cres[0].loss)
     gg = gt.masters.export_peft(16, grads=True)
     cg = ct.masters.export_peft(16, grads=True)
+    # Elementwise per tensor (bf16 operands against the fp32 oracle; measured
+    # worst: 2.6 % relative L2, 3.5 % of the tensor's max): a wrong scale on a
+    # projection's slice or a missing row block moves either far more.
     for k in cg:
-        assert cos(gg[k], cg[k]) > 0.98, k
+        x, y = gg[k].double(), cg[k].double()
+        rel_l2 = float((x - y).norm() / (y.norm() + 1e-30))
+        rel_max = float((x - y).abs().max() / (y.abs().max() + 1e-30))
+        assert rel_l2 < 0.05 and rel_max < 0.08, (k, rel_l2, rel_max)
 
 
 def test_gpu_training_reduces_loss():
