@@ -260,6 +260,7 @@ def main():
                    f"bwd_active={eng.bwd_active}")
     eng.synchronize()
     stats0 = dict(eng.stats)
+    host0 = dict(eng.host_s)
     l0 = ops.LAUNCHES[0]
     cyc0 = len(eng.coord.history)
     trk0 = len(eng.tracker.durations)
@@ -349,6 +350,12 @@ def main():
         "ft_tokens_trained_per_s": round(st["ft_tokens_trained"] / (dev_ms / 1e3), 2),
         "backward_cycles_total": eng.coord.completed_cycles, "backward_cycles": cyc,
         "engine_iterations": iters, "iteration_kinds": step_kinds,
+        "host_ms_per_iteration": {k: round(1e3 * (v - host0.get(k, 0.0)) / max(1, iters), 3)
+                                  for k, v in sorted(eng.host_s.items())},
+        # followers (ranks 1..N-1), whole run: seconds waiting for / replaying step plans
+        "follower_host_s_max": ({k: round(max(f.get(k, 0.0) for f in eng.follower_host_s), 2)
+                                 for k in ("follower_wait_plan", "follower_replay")}
+                                if getattr(eng, "follower_host_s", None) else None),
         "last_loss": eng.coord.last_loss,
         "valid_slo": bool(attain is not None and attain >= 0.99 and enough),
         "e2e": {"value": round(e2e, 2), "unit": "FT tokens/s (wall clock, public step() API)",

@@ -124,7 +124,7 @@ def main() -> None:
     from ..models.lora import LoraServeBuffers
     from ..ops.reference import rope_cos_sin_table
     from ..models.weights import TPInfo, init_weights
-    from ..parallel.comm import TPComm, init_tp
+    from ..parallel.comm import init_tp, new_backward_group
     from .trainer import BUCKET_LAYERS, LoraTrainer
 
     if not torch.cuda.is_available() or not ops.native_available():
@@ -134,8 +134,7 @@ def main() -> None:
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     dev = torch.device("cuda", torch.cuda.current_device())
     tp = TPInfo(comm.rank, comm.size) if comm is not None else TPInfo()
-    bwd_comm = (TPComm(dist.new_group(list(range(comm.size))), comm.cpu_group)
-                if comm is not None else None)
+    bwd_comm = new_backward_group(comm) if comm is not None else None
     arch = resolve_arch(args.model)
     t0 = time.perf_counter()
     w = init_weights(arch, tp, seed=0, device=dev, dtype=torch.bfloat16, keep_full_head=True)
@@ -216,7 +215,8 @@ def main() -> None:
         coll["allreduce_bucket_ms"] = _time_collective(lambda: bwd_comm.all_reduce(bucket), 10)
         coll["bucket_bytes"] = bucket.numel() * 4
         coll["resid_bytes_fp32"] = f32.numel() * 4
-        coll["nccl_max_ctas"] = os.environ.get("NCCL_MAX_CTAS")
+        from ..parallel.comm import BWD_NCCL_MAX_CTAS
+        coll["bwd_nccl_max_ctas"] = BWD_NCCL_MAX_CTAS
     rec = {"tp": tp.size, "tp_comm": args.tp_comm if comm is not None else None, "model": args.model,
            "rows": n, "seqs": args.seqs, "seq_len": args.seq_len,
            "lora_rank": args.rank,

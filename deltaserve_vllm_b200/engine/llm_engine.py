@@ -153,7 +153,8 @@ class CoServingEngine:
         if comm is not None and comm.size > 1:
             import torch.distributed as dist
             from ..parallel.comm import TPComm
-            self.bwd_comm = TPComm(dist.new_group(list(range(comm.size))), comm.cpu_group)
+            from ..parallel.comm import new_backward_group
+            self.bwd_comm = new_backward_group(comm)
         self._actions: list = []
         self._actions_lock = threading.Lock()
         # Step plans reach the follower ranks through shared memory (a memory
@@ -220,6 +221,8 @@ class CoServingEngine:
         self.step_no = 0
         self.profiling = False
         self.last_admit = None
+        # Host seconds per step phase (rank 0), for the bench's breakdown.
+        self.host_s: dict[str, float] = {}
         self.stats = {"ft_tokens_forwarded": 0, "ft_tokens_trained": 0, "steps": 0,
                       "bwd_layers": 0, "h2d_bytes": 0, "d2h_bytes": 0}
         self.arrival_flag = False
@@ -725,6 +728,12 @@ class CoServingEngine:
             if self.tracker.check_refit():
                 self.estimator.data_fit(self.tracker)
 
+    def _host(self, phase: str, t0: float) -> float:
+        """Accumulate host seconds of a step phase since ``t0``; returns now."""
+        t = time.perf_counter()
+        self.host_s[phase] = self.host_s.get(phase, 0.0) + (t - t0)
+        return t
+
     def step(self) -> list[Request]:
         """One engine step (rank 0). Returns requests that finished."""
         now = time.perf_counter()
@@ -742,7 +751,9 @@ class CoServingEngine:
             self.jobs.tick(self)
             if self.coord.try_flush():
                 self._start_backward()
+        t_h = self._host("housekeeping", now)
         out = self.scheduler.schedule()
+        t_h = self._host("schedule", t_h)
         if self.ftcfg.print_scheduler_add and out.prefill:
             dprint(f"[sched] step {self.step_no}: prefill {[s.num_new for s in out.prefill]} "
                    f"decode {len(out.decode)}")
@@ -780,9 +791,11 @@ class CoServingEngine:
                     time.sleep(0.0002)
                 if self.arrival_flag:
                     self._rollback_ft(out)
+        t_h = self._host("admission", t_h)
         if out.is_empty():
             self._advance_backward(idle=not self.has_unfinished())
             self._flush_actions()
+            self._host("backward_feed", t_h)
             return []
         return self._run(out, ft_dst, bwd_busy)
 
@@ -825,6 +838,7 @@ class CoServingEngine:
                        if (self.ftcfg.forward_interruptible and not self.profiling and self.ft_enabled) else None)
         self.runner.eos_ids = self.eos_ids()
         vote = self._abort_vote() if self.tp_size > 1 else None
+        t_h = time.perf_counter()
         if self.cuda:
             with torch.cuda.stream(self.fwd_stream):
                 if uses_ft_slot and self._publish_evt is not None:
@@ -840,6 +854,10 @@ class CoServingEngine:
             toks, _ = self.runner.execute(out, self.capture, ft_dst, self._plan_hook(bool(out.ft)),
                                           before_sample=feed, abort_check=abort_check, vote=vote)
             ev1 = time.perf_counter()
+        t_h = self._host("execute", t_h)
+        for name, v in zip(("exec_pack_plan", "exec_enqueue", "exec_backward_feed", "exec_sample_wait"),
+                           self.runner.last_phases):
+            self.host_s[name] = self.host_s.get(name, 0.0) + v
         if self.runner.last_aborted:
             # Partial captures and KV pages of the FT rows are simply released.
             self._rollback_ft(out)
@@ -873,9 +891,11 @@ class CoServingEngine:
                 cb("finish", r)
         self.finished.extend(done)
         self.arrival_flag = False
+        t_h = self._host("update", t_h)
         pause = has_inf_prefill and (self.ftcfg.pause_on_arrival or self.ftcfg.pause_until_prefill_done
                                      or self.ftcfg.pause_prefill_always)
         self._advance_backward(idle=False, paused=(pause and bool(self.scheduler.waiting)) or big_step)
+        self._host("backward_feed", t_h)
         if self.ftcfg.validate_estimator:
             self._drain_timing(block=True)      # synchronous: every prediction checked at once
         if self.ftcfg.print_engine_batch_done:
@@ -1285,6 +1305,8 @@ class CoServingEngine:
         self._flush_actions()
         self.marks["__region__"] = mine
         res = self.comm.gather_objects(self.marks)
+        # The followers' host seconds (waiting for step plans / replaying them).
+        self.follower_host_s = [r.get("__host__", {}) for r in res[1:]]
         return [mine] + [r["__region__"] for r in res[1:]]
 
     def shutdown(self) -> None:
@@ -1313,8 +1335,10 @@ class CoServingEngine:
     def follow(self) -> None:
         """Follower-rank loop: replay rank 0's actions until it stops."""
         assert not self.is_driver
+        t_h = time.perf_counter()
         while True:
             actions = self.plan_chan.recv() if self.plan_chan is not None else self.comm.broadcast_object(None)
+            t_h = self._host("follower_wait_plan", t_h)
             for a in actions:
                 kind = a[0]
                 if kind == "stop":
@@ -1328,6 +1352,7 @@ class CoServingEngine:
                     continue
                 if kind == "gather":
                     self.marks["__region__"] = self.region_ms(a[1], a[2])
+                    self.marks["__host__"] = dict(self.host_s)
                     self.comm.gather_objects(self.marks)
                     continue
                 if kind == "save":
@@ -1393,6 +1418,7 @@ class CoServingEngine:
                             ev.record(self.bwd_stream)
                             self._publish_evt = ev
                         self.trainer.losses.append(0.0)
+            t_h = self._host("follower_replay", t_h)
 
     def _drain_backward_follower(self) -> None:
         if self.cuda:

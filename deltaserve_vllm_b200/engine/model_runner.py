@@ -414,6 +414,7 @@ class ModelRunner:
         (rank 0 under TP) receives the host metadata before the forward is
         enqueued, so the other ranks can replay the same step."""
         self.last_aborted = False
+        self.last_phases = (0.0, 0.0, 0.0, 0.0)
         if out.is_empty():
             return {}, None
         t0 = time.perf_counter()
@@ -422,18 +423,26 @@ class ModelRunner:
         meta["abortable"] = bool(abort_check is not None and out.ft and not out.decode and not out.prefill)
         if on_host_plan is not None:
             on_host_plan(meta, pk)
+        t1 = time.perf_counter()
+        # Host seconds of this call: (pack + plan send, enqueue, backward feed,
+        # sampling incl. the wait for the GPU).
+        self.last_phases = (t1 - t0, 0.0, 0.0, 0.0)
         if self.graph_eligible(meta) and len(reqs) == meta["nd"]:
             temps = np.array([r.params.temperature for r in reqs], dtype=np.float32)
             seeds = np.array([(r.params.seed if r.params.seed is not None else r.seq_no) * 1000003
                               + len(r.output_ids) for r in reqs], dtype=np.int64)
             toks, nbytes = self.graphs.run(meta, pk, temps, seeds)
             self.last_h2d_bytes = nbytes
-            self.last_enqueue_s = time.perf_counter() - t0
+            t2 = time.perf_counter()
+            self.last_enqueue_s = t2 - t0
             if before_sample is not None:
                 before_sample()
+            t3 = time.perf_counter()
             host = toks[:len(reqs)].cpu()
             self.last_d2h_bytes = len(reqs) * 8
-            return {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}, self.graphs.last_logits
+            res = {r.seq_no: int(v) for r, v in zip(reqs, host.tolist())}
+            self.last_phases = (t1 - t0, t2 - t1, t3 - t2, time.perf_counter() - t3)
+            return res, self.graphs.last_logits
         b = self.batch_from(meta, pk)
         hook = self.abort_hook(abort_check, vote) if meta["abortable"] else None
         try:
@@ -442,10 +451,14 @@ class ModelRunner:
             self.last_aborted = True
             self.last_enqueue_s = time.perf_counter() - t0
             return {}, None
-        self.last_enqueue_s = time.perf_counter() - t0   # host time to enqueue the forward
+        t2 = time.perf_counter()
+        self.last_enqueue_s = t2 - t0   # host time to enqueue the forward
         if before_sample is not None:
             before_sample()
-        return self.sample(logits, reqs), logits
+        t3 = time.perf_counter()
+        res = self.sample(logits, reqs)
+        self.last_phases = (t1 - t0, t2 - t1, t3 - t2, time.perf_counter() - t3)
+        return res, logits
 
     def sample(self, logits, reqs) -> dict:
         if not reqs:

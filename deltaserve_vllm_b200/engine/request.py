@@ -46,8 +46,11 @@ class SamplingParams:
 _counter = itertools.count()
 
 
-@dataclass
+@dataclass(eq=False)
 class Request:
+    """One inference or finetuning request. Compared by identity: the
+    scheduler's queues test membership on every step, and a field-by-field
+    comparison (prompt token lists included) made that O(fields) per test."""
     request_id: str
     prompt_ids: list[int]
     params: SamplingParams = field(default_factory=SamplingParams)

@@ -219,13 +219,15 @@ class Scheduler:
         out = SchedulerOutput()
         budget = self.max_num_batched_tokens
         # 1. decode for running requests that finished their prompt
+        gone: set[int] = set()     # ids of requests pre-empted during this loop
         for req in list(self.running):
-            if req.in_prefill or req not in self.running:
+            if req.in_prefill or id(req) in gone:
                 continue
             while not self._ensure_blocks(req, req.num_computed + 1):
                 if not self._preempt_one(out, req):
                     break
-            if req not in self.running:
+                gone.add(id(out.preempted[-1]))
+            if id(req) in gone:
                 continue
             if blocks_needed(req.num_computed + 1, self.block_size) > len(req.block_ids):
                 continue  # could not get a page even after pre-emption

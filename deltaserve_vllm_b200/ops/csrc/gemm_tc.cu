@@ -37,7 +37,7 @@ enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 
                       kEpiPushRows = 10 };
 
 constexpr int kMaxPeers = 8;
-constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (>= NCCL_MAX_CTAS)
+constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (backward NCCL cap + its waits)
 
 // Fused all-reduce over peer memory (kEpiPeerAR). Every rank holds one
 // workspace, mapped into every other rank's address space:

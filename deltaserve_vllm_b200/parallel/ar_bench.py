@@ -4,8 +4,9 @@
         --master-port 29600 -m deltaserve_vllm_b200.parallel.ar_bench [--iters 20]
 
 Shapes are Llama-3-8B's row-parallel projections at this TP degree
-(o: K = 4096/tp, down: K = 14336/tp, N = 4096) for a decode step (M = 64) and
-a prefill step (M = 4096). Each variant is timed with CUDA events over
+(o: K = 4096/tp, down: K = 14336/tp, N = 4096) for a decode step (M = 64) up
+to prefill steps (M = 4096, 8192), then the backward's residual-gradient
+reductions (see ``_backward_cases``). Each variant is timed with CUDA events over
 ``iters`` launches after warm-up; the max over ranks is reported. The
 roofline of the fused path is the slower of its FLOPs at the measured bf16
 peak and the bytes each rank must send over NVLink at 770 GB/s per direction
@@ -53,13 +54,14 @@ def main(argv=None) -> None:
     comm = init_tp()
     tp, rank = comm.size, comm.rank
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
-    ws = PeerWorkspace(comm, 4096, 4096)
+    ws = PeerWorkspace(comm, 8192, 4096)
     peak = _peaks()
     g = torch.Generator(device="cuda").manual_seed(rank)
     for name, M, K in [("o_decode", 64, 4096 // tp), ("down_decode", 64, 14336 // tp),
                        ("o_m256", 256, 4096 // tp), ("o_m1024", 1024, 4096 // tp),
                        ("down_m1024", 1024, 14336 // tp), ("o_m2048", 2048, 4096 // tp),
-                       ("o_prefill", 4096, 4096 // tp), ("down_prefill", 4096, 14336 // tp)]:
+                       ("o_prefill", 4096, 4096 // tp), ("down_prefill", 4096, 14336 // tp),
+                       ("o_m8192", 8192, 4096 // tp), ("down_m8192", 8192, 14336 // tp)]:
         N = 4096
         a = torch.randn(M, K, generator=g, device="cuda").bfloat16()
         b = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
@@ -96,9 +98,56 @@ def main(argv=None) -> None:
                               "speedup_vs_nccl": round(t_base / t_fused, 3),
                               "roofline_ms": round(bound_ms, 4), "frac_roofline": round(bound_ms / t_fused, 3),
                               "max_rel_err": round(err, 5), "peaks": peak["src"]}), flush=True)
+    _backward_cases(comm, args.iters, peak, g)
     assert ops.check_device_error() == 0
     ws.close()
     dist.destroy_process_group()
+
+
+def _backward_cases(comm, iters: int, peak: dict, g) -> None:
+    """The backward's residual-gradient reduction at Llama-3-8B shapes (4096
+    FT rows): dX GEMM (MN-major) + row push + owner reduce + RMSNorm backward
+    + all-gather over peer memory, against GEMM (fp32 out) + NCCL fp32
+    all-reduce + RMSNorm backward, and against GEMM + NCCL bf16 all-reduce.
+    Roofline: the slower of the GEMM at peak and the push + gather bytes
+    ((tp-1)/tp of the bf16 rows each way) at 770 GB/s."""
+    from .peer import BwdPeerWorkspace
+    tp, rank = comm.size, comm.rank
+    M, D = 4096, 4096
+    bws = BwdPeerWorkspace(comm, M, D)
+    x = torch.randn(M, D, generator=g, device="cuda").bfloat16()
+    wn = (torch.randn(D, generator=g, device="cuda") * 0.1 + 1).bfloat16()
+    add = torch.randn(M, D, generator=g, device="cuda")
+    out32 = torch.empty(M, D, device="cuda")
+    for name, K in [("bwd_gate_up_dx", 2 * 14336 // tp), ("bwd_qkv_dx", 6144 // tp)]:
+        a = torch.randn(M, K, generator=g, device="cuda").bfloat16()
+        b = (torch.randn(K, D, generator=g, device="cuda") * 0.02).bfloat16()
+        y32 = torch.empty(M, D, device="cuda")
+        y16 = torch.empty(M, D, dtype=torch.bfloat16, device="cuda")
+
+        def fused():
+            ops.gemm_push(a, b, bws)
+            ops.tp_reduce_rows(bws, M, 0, out32, x=x, w=wn, eps=1e-5, add=add)
+
+        def nccl_f32():
+            ops.gemm(a, b, y32, b_mn=True, epi=ops.EPI_F32)
+            dist.all_reduce(y32)
+            ops.rms_norm_bwd(x, y32, wn, 1e-5, add=add, out=out32)
+
+        def nccl_bf16():
+            ops.gemm(a, b, y16, b_mn=True, epi=ops.EPI_BF16)
+            dist.all_reduce(y16)
+
+        t_f, t_n32, t_n16 = _time(fused, iters), _time(nccl_f32, iters), _time(nccl_bf16, iters)
+        flops = 2 * M * D * K
+        nvl = 2 * (tp - 1) / tp * M * D * 2
+        bound = max(flops / (peak["bf16_tflops"] * 1e9), nvl / (NVLINK_GBS * 1e6))
+        if rank == 0:
+            print(json.dumps({"case": name, "tp": tp, "M": M, "N": D, "K": K, "fused_ms": round(t_f, 4),
+                              "gemm_nccl_f32_norm_ms": round(t_n32, 4), "gemm_nccl_bf16_ms": round(t_n16, 4),
+                              "speedup_vs_nccl_f32": round(t_n32 / t_f, 3), "roofline_ms": round(bound, 4),
+                              "frac_roofline": round(bound / t_f, 3), "peaks": peak["src"]}), flush=True)
+    bws.close()
 
 
 if __name__ == "__main__":

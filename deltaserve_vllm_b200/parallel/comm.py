@@ -95,6 +95,40 @@ class TPComm:
             dist.barrier(group=self.cpu_group or self.group)
 
 
+# SM budget of the collectives that can run at the same time on one GPU. Every
+# kernel that waits on other ranks must be able to be resident together with
+# the others, or two ranks could each hold the SMs the other's partner needs:
+#   forward stream: the fused GEMM + all-reduce (at most SMs - 20 CTAs) or an
+#     NCCL collective of the default group (at most FWD_NCCL_MAX_CTAS), never
+#     both at once (one stream);
+#   backward stream: NCCL collectives of the backward's own group (at most
+#     BWD_NCCL_MAX_CTAS) and the one-CTA waits of its peer-memory reductions.
+# 128 + 16 + 1 and 64 + 16 + 1 both fit in 148 SMs. The forward's group also
+# runs on a high-priority NCCL stream, ahead of the backward's kernels.
+FWD_NCCL_MAX_CTAS = int(os.environ.get("DSV_FWD_NCCL_CTAS", "64"))
+BWD_NCCL_MAX_CTAS = 16
+
+
+def nccl_options(max_ctas: int, high_priority: bool):
+    """ProcessGroupNCCL options with a CTA cap and stream priority."""
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = high_priority
+    opts.config.max_ctas = int(max_ctas)
+    return opts
+
+
+def new_backward_group(comm: "TPComm") -> "TPComm":
+    """The backward's own communicator (its collectives run on another
+    stream than the forward's and must never share an NCCL queue), capped at
+    BWD_NCCL_MAX_CTAS CTAs on a normal-priority stream."""
+    ranks = list(range(comm.size))
+    if dist.get_backend() == "nccl":
+        g = dist.new_group(ranks, pg_options=nccl_options(BWD_NCCL_MAX_CTAS, high_priority=False))
+    else:
+        g = dist.new_group(ranks)
+    return TPComm(g, comm.cpu_group)
+
+
 def init_tp(backend: str | None = None, timeout_s: float = 120.0) -> TPComm:
     """Initialise the default process group from the torchrun environment."""
     ws = int(os.environ.get("WORLD_SIZE", "1"))
@@ -103,15 +137,13 @@ def init_tp(backend: str | None = None, timeout_s: float = 120.0) -> TPComm:
     if not dist.is_initialized():
         if backend is None:
             backend = "nccl" if torch.cuda.is_available() else "gloo"
-        # NCCL kernels may occupy at most this many SMs: the fused GEMM +
-        # all-reduce grid leaves that many free, so both can always be resident.
-        os.environ.setdefault("NCCL_MAX_CTAS", "16")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         kw = {}
         if backend == "nccl":
             local = int(os.environ.get("LOCAL_RANK", os.environ.get("RANK", "0")))
             torch.cuda.set_device(local)
             kw["device_id"] = torch.device("cuda", local)
+            kw["pg_options"] = nccl_options(FWD_NCCL_MAX_CTAS, high_priority=True)
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
     cpu_group = dist.new_group(backend="gloo") if backend == "nccl" else None
     return TPComm(None, cpu_group)

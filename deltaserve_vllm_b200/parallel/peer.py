@@ -72,7 +72,11 @@ class PeerWorkspace:
                                   dtype=torch.int64)
         self.tile_cnt = self.base + self.offsets[4]
         self.calls = 0
-        self.fused_max_rows = int(os.environ.get("DSV_FUSED_AR_MAX_ROWS", "2048"))
+        # At TP=2 GEMM + NCCL wins above 2048 rows (measured); at 4+ ranks
+        # the fused kernel takes every size (NCCL's ring costs grow with the
+        # rank count, the fused one-shot exchange does not).
+        default_max = 2048 if self.world <= 2 else self.max_rows
+        self.fused_max_rows = int(os.environ.get("DSV_FUSED_AR_MAX_ROWS", str(default_max)))
         if comm is not None and self.world > 1:
             comm.barrier()        # every rank mapped every block before first use
 
@@ -83,7 +87,7 @@ class PeerWorkspace:
         """Whether the fused kernel should take this call: measured at TP=2 it
         beats GEMM + NCCL from 256 to 2048 rows (1.2-1.5x) and at 4096 rows
         for o_proj, not for down_proj at 4096 rows; calls above
-        ``fused_max_rows`` go to NCCL's bandwidth-optimised rings."""
+        ``fused_max_rows`` go to NCCL."""
         return self.fits(rows, n_cols) and rows <= self.fused_max_rows
 
     def close(self) -> None:
