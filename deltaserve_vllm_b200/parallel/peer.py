@@ -72,10 +72,10 @@ class PeerWorkspace:
                                   dtype=torch.int64)
         self.tile_cnt = self.base + self.offsets[4]
         self.calls = 0
-        # At TP=2 GEMM + NCCL wins above 2048 rows (measured); at 4+ ranks
-        # the fused kernel takes every size (NCCL's ring costs grow with the
-        # rank count, the fused one-shot exchange does not).
-        default_max = 2048 if self.world <= 2 else self.max_rows
+        # Measured (ar_bench, Llama-3-8B o / down shapes): at TP=2 GEMM + NCCL
+        # wins above 2048 rows; at TP=4 the fused kernel wins up to 4096 rows
+        # (1.03-1.33x) and NCCL at 8192 rows (0.82-0.91x).
+        default_max = 2048 if self.world <= 2 else 4096
         self.fused_max_rows = int(os.environ.get("DSV_FUSED_AR_MAX_ROWS", str(default_max)))
         if comm is not None and self.world > 1:
             comm.barrier()        # every rank mapped every block before first use
