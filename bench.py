@@ -263,7 +263,7 @@ def main():
     host0 = dict(eng.host_s)
     l0 = ops.LAUNCHES[0]
     cyc0 = len(eng.coord.history)
-    trk0 = len(eng.tracker.durations)
+    trk0 = eng.tracker.appended
     iters = 0
     gpu_idx = os.environ.get("CUDA_VISIBLE_DEVICES", ",".join(str(i) for i in range(args.gpus)))
     with ClockSampler(gpu_idx) as clocks:
@@ -303,8 +303,9 @@ def main():
     # Decode-only steps: host time to enqueue the forward vs its GPU time
     # (launch-bound when the first is larger).
     eng._drain_timing(block=True)
-    feats = eng.tracker.features[trk0:]
-    durs = eng.tracker.durations[trk0:]
+    n_new = min(eng.tracker.appended - trk0, eng.tracker.size())
+    feats = eng.tracker.features[-n_new:] if n_new else []
+    durs = eng.tracker.durations[-n_new:].tolist() if n_new else []
     dec_gpu = [d for f, d in zip(feats, durs) if f.t_in == 0 and f.t_ft == 0 and f.b_d > 0]
     n_dec = st.get("decode_steps", 0)
     dec_info = {"host_enqueue_ms": round(1e3 * st.get("decode_enqueue_s", 0.0) / max(1, n_dec), 3),

@@ -106,7 +106,7 @@ class FinetuneAdmission:
                 if base >= tbt:
                     res.code = "S"
                     return res
-                if use_avg and self.tbt_window.average_with(now, feats.b_d, base) >= cfg.avg_tbt_slo:
+                if use_avg and self.tbt_window.mean_with(now, feats.b_d, base) >= cfg.avg_tbt_slo:
                     res.code = "S"
                     return res
             if ttft_deadline is not None and ttft_deadline - now - base <= 0:
@@ -160,12 +160,12 @@ class FinetuneAdmission:
                                b_d=feats.b_d, k=feats.k, prefill_lens=lens + [cand.input_len],
                                bwd=bwd_in_flight)
             if est.is_ready:
-                t_with = est.predict(hyp, regime=hyp.regime()) + extra_s
+                t_with = est.predict(hyp, regime=est.regime_of(hyp)) + extra_s
                 if feats.b_d > 0:
                     if t_with > tbt:
                         stop = "S"
                         break
-                    if use_avg and self.tbt_window.average_with(now, feats.b_d, t_with) > cfg.avg_tbt_slo:
+                    if use_avg and self.tbt_window.mean_with(now, feats.b_d, t_with) > cfg.avg_tbt_slo:
                         stop = "S"
                         break
                 if ttft_deadline is not None and ttft_deadline - now - t_with <= 0:

@@ -45,18 +45,6 @@ REGIME_DECODE_BWD = "decode_bwd"
 REGIME_FT_MIXED = "ft_mixed"
 REGIMES = (REGIME_INF_PREFILL, REGIME_EAGER, REGIME_DECODE_ONLY, REGIME_DECODE_BWD, REGIME_FT_MIXED)
 
-_FT_MIXED_SPLIT = False
-
-
-def set_ft_mixed_split(enabled: bool) -> None:
-    global _FT_MIXED_SPLIT
-    _FT_MIXED_SPLIT = bool(enabled)
-
-
-def ft_mixed_split() -> bool:
-    return _FT_MIXED_SPLIT
-
-
 @dataclass
 class StepFeatures:
     t_in: float = 0.0
@@ -67,9 +55,12 @@ class StepFeatures:
     prefill_lens: Sequence[int] | None = None
     bwd: bool = False
     load_s: float = 0.0
+    s_sum: float | None = None      # sum of squared prefill lengths when known without the lengths
 
     @property
     def s(self) -> float:
+        if self.s_sum is not None:
+            return float(self.s_sum)
         if self.prefill_lens:
             return float(sum(int(n) * int(n) for n in self.prefill_lens))
         if self.p > 0:
@@ -83,20 +74,23 @@ class StepFeatures:
     def row(self) -> list[float]:
         return [self.s, float(self.t_in), float(self.t_ft), float(self.b_d), float(self.k), 1.0]
 
-    def regime(self) -> str:
-        if self.t_ft > 0:
-            if _FT_MIXED_SPLIT and (self.t_in > self.t_ft or self.b_d > 0):
-                return REGIME_FT_MIXED
-            return REGIME_EAGER
-        if self.t_in > 0:
-            return REGIME_INF_PREFILL
-        if self.bwd:
-            return REGIME_DECODE_BWD
-        return REGIME_DECODE_ONLY
+    def regime(self, split_mixed: bool = False) -> str:
+        """The regime of this step. ``split_mixed`` (the ``graph_ft_batches``
+        switch, an attribute of the estimator) gives FT rows that share a step
+        with inference work their own regime."""
+        return _regime(self.t_in, self.t_ft, self.b_d, self.bwd, split_mixed)
 
     @property
     def contended(self) -> bool:
         return self.bwd and self.t_in > 0
+
+
+def _regime(t_in, t_ft, b_d, bwd, split_mixed: bool) -> str:
+    if t_ft > 0:
+        return REGIME_FT_MIXED if split_mixed and (t_in > t_ft or b_d > 0) else REGIME_EAGER
+    if t_in > 0:
+        return REGIME_INF_PREFILL
+    return REGIME_DECODE_BWD if bwd else REGIME_DECODE_ONLY
 
 
 @dataclass
@@ -118,80 +112,132 @@ class StepParams:
                 + self.epsilon * f.k + self.c)
 
 
-class StepExecutionTracker:
-    """Rolling record of served steps: features, measured and predicted time."""
+class StepLog:
+    """The served steps the estimator learns from: a ring of ``capacity``
+    records in numpy columns (features, measured and predicted seconds,
+    graph flag, wall time). Appending overwrites the oldest record once the
+    ring is full; fits read the columns directly (no per-step objects)."""
 
-    def __init__(self, max_steps: int = 10240):
-        self.max_steps = max_steps
-        self.features: list[StepFeatures] = []
-        self.durations: list[float] = []
-        self.predicted: list[float | None] = []
-        self.was_graph: list[bool | None] = []
-        self.timestamps: list[float] = []
-        self._last_refit_size = 0
+    _F = ("t_in", "p", "t_ft", "b_d", "k", "s", "bwd")   # feature columns
 
+    def __init__(self, capacity: int = 10240):
+        self.capacity = int(capacity)
+        self._col = {c: np.zeros(self.capacity) for c in self._F}
+        self._dur = np.zeros(self.capacity)
+        self._pred = np.full(self.capacity, np.nan)     # nan = no prediction was made
+        self._graph = np.full(self.capacity, -1, dtype=np.int8)   # -1 unknown, 0 eager, 1 graph
+        self._wall = np.zeros(self.capacity)
+        self.appended = 0          # records ever appended (the write position is appended % capacity)
+        self._refit_at = 0         # `appended` when the last refit was signalled
+
+    # ------------------------------------------------------------ records
     def add(self, features: StepFeatures, duration: float, predicted: float | None = None,
             was_graph: bool | None = None) -> None:
-        self.features.append(features)
-        self.durations.append(float(duration))
-        self.predicted.append(predicted)
-        self.was_graph.append(was_graph)
-        self.timestamps.append(time.time())
-        if len(self.durations) > self.max_steps:
-            for lst in (self.features, self.durations, self.predicted, self.was_graph, self.timestamps):
-                del lst[0]
+        i = self.appended % self.capacity
+        f = features
+        for c, v in zip(self._F, (f.t_in, f.p, f.t_ft, f.b_d, f.k, f.s, float(bool(f.bwd)))):
+            self._col[c][i] = v
+        self._dur[i] = duration
+        self._pred[i] = np.nan if predicted is None else predicted
+        self._graph[i] = -1 if was_graph is None else int(bool(was_graph))
+        self._wall[i] = time.time()
+        self.appended += 1
 
     def size(self) -> int:
-        return len(self.durations)
+        return min(self.appended, self.capacity)
 
-    def check_refit(self) -> bool:
+    __len__ = size
+
+    def _order(self) -> np.ndarray:
+        """Ring slots in chronological order."""
         n = self.size()
-        if n > 0 and n % REFIT_EVERY == 0 and n > self._last_refit_size:
-            self._last_refit_size = n
+        if self.appended <= self.capacity:
+            return np.arange(n)
+        return (np.arange(n) + self.appended) % self.capacity
+
+    def column(self, name: str) -> np.ndarray:
+        """One column in chronological order (copy): a feature name,
+        ``duration``, ``predicted`` (nan where none) or ``wall``."""
+        src = {"duration": self._dur, "predicted": self._pred, "wall": self._wall}.get(name)
+        return (self._col[name] if src is None else src)[self._order()]
+
+    def feature(self, i: int) -> StepFeatures:
+        j = self._order()[i]
+        c = self._col
+        return StepFeatures(t_in=float(c["t_in"][j]), p=int(c["p"][j]), t_ft=float(c["t_ft"][j]),
+                            b_d=int(c["b_d"][j]), k=float(c["k"][j]), bwd=bool(c["bwd"][j]),
+                            s_sum=float(c["s"][j]))
+
+    @property
+    def features(self) -> list[StepFeatures]:
+        return [self.feature(i) for i in range(self.size())]
+
+    @property
+    def durations(self) -> np.ndarray:
+        return self.column("duration")
+
+    def set_predicted(self, i: int, value: float | None) -> None:
+        self._pred[self._order()[i]] = np.nan if value is None else value
+
+    def truncate(self, n: int) -> None:
+        """Forget every record after the first ``n`` (used before the ring
+        has ever wrapped: the launch-time profiling steps)."""
+        if not 0 <= n <= self.size() or self.appended > self.capacity:
+            raise ValueError("truncate: only before the ring wraps, to a length it has")
+        self.appended = n
+        self._refit_at = min(self._refit_at, n)
+
+    def due_for_refit(self) -> bool:
+        """True once per REFIT_EVERY appended records."""
+        mark = self.appended - self.appended % REFIT_EVERY
+        if mark > self._refit_at:
+            self._refit_at = mark
             return True
         return False
 
+    # ------------------------------------------------------------ state / export
     def export_state(self) -> dict:
-        return {"max_steps": self.max_steps, "last_refit_size": self._last_refit_size,
-                "samples": [[f.t_in, f.p, f.t_ft, f.b_d, f.k,
-                             list(f.prefill_lens) if f.prefill_lens is not None else None,
-                             bool(f.bwd), d, wg]
-                            for f, d, wg in zip(self.features, self.durations, self.was_graph)]}
+        cols = {c: self.column(c).tolist() for c in self._F}
+        cols["duration"] = self.column("duration").tolist()
+        cols["graph"] = self._graph[self._order()].astype(int).tolist()
+        return {"format": "columns", "capacity": self.capacity, "refit_at": self._refit_at,
+                "appended": self.appended, "cols": cols}
 
     def import_state(self, state: dict) -> None:
-        self.features, self.durations, self.predicted, self.was_graph, self.timestamps = [], [], [], [], []
-        now = time.time()
-        for t_in, p, t_ft, b_d, k, lens, bwd, dur, wg in state["samples"]:
-            self.features.append(StepFeatures(t_in=t_in, p=p, t_ft=t_ft, b_d=b_d, k=k,
-                                              prefill_lens=lens, bwd=bwd))
-            self.durations.append(float(dur))
-            self.predicted.append(None)
-            self.was_graph.append(wg)
-            self.timestamps.append(now)
-        while len(self.durations) > self.max_steps:
-            for lst in (self.features, self.durations, self.predicted, self.was_graph, self.timestamps):
-                del lst[0]
-        self._last_refit_size = min(int(state.get("last_refit_size", 0)), self.size())
+        self.__init__(self.capacity)
+        if "cols" in state:
+            cols = state["cols"]
+            n = len(cols["duration"])
+            for i in range(n):
+                f = StepFeatures(t_in=cols["t_in"][i], p=int(cols["p"][i]), t_ft=cols["t_ft"][i],
+                                 b_d=int(cols["b_d"][i]), k=cols["k"][i], bwd=bool(cols["bwd"][i]),
+                                 s_sum=cols["s"][i])
+                g = cols["graph"][i]
+                self.add(f, cols["duration"][i], None, None if g < 0 else bool(g))
+        else:   # the row-list format of earlier files: one list per step
+            for t_in, p, t_ft, b_d, k, lens, bwd, dur, wg in state.get("samples", []):
+                self.add(StepFeatures(t_in=t_in, p=p, t_ft=t_ft, b_d=b_d, k=k, prefill_lens=lens, bwd=bwd),
+                         dur, None, wg)
+        self._refit_at = min(int(state.get("refit_at", state.get("last_refit_size", 0))), self.appended)
 
-    def write_prediction_stats_csv(self, path: str | None) -> None:
+    def write_prediction_stats_csv(self, path: str | None, split_mixed: bool = False) -> None:
+        """One row per step that had a prediction: features, regime, measured
+        and predicted seconds."""
         if path is None:
             return
         if os.path.dirname(path):
             os.makedirs(os.path.dirname(path), exist_ok=True)
         cols = ["timestamp", "step_index", "regime", "was_graph", "t_in", "p", "t_ft", "b_d", "k",
                 "s", "execution_duration", "predicted_duration"]
+        pred, dur, wall = self.column("predicted"), self.column("duration"), self.column("wall")
+        graph = self._graph[self._order()]
         with open(path, "w", newline="") as fh:
-            w = csv.DictWriter(fh, fieldnames=cols)
-            w.writeheader()
-            for i in range(self.size()):
-                if self.predicted[i] is None:
-                    continue
-                f = self.features[i]
-                w.writerow({"timestamp": self.timestamps[i], "step_index": i, "regime": f.regime(),
-                            "was_graph": self.was_graph[i], "t_in": f.t_in, "p": f.p, "t_ft": f.t_ft,
-                            "b_d": f.b_d, "k": f.k, "s": f.s,
-                            "execution_duration": self.durations[i],
-                            "predicted_duration": self.predicted[i]})
+            w = csv.writer(fh)
+            w.writerow(cols)
+            for i in np.flatnonzero(~np.isnan(pred)):
+                f = self.feature(int(i))
+                w.writerow([wall[i], int(i), f.regime(split_mixed), None if graph[i] < 0 else bool(graph[i]),
+                            f.t_in, f.p, f.t_ft, f.b_d, f.k, f.s, dur[i], pred[i]])
 
 
 _COLS = {
@@ -213,6 +259,12 @@ class MergedExecutionEstimator:
         self._rel_rmse: dict[str, float | None] = {r: None for r in REGIMES}
         self.margin_mode = "legacy"
         self.margin_k = 1.5
+        # graph_ft_batches: FT rows that share a step with inference work are
+        # their own regime (ft_mixed) instead of the eager one.
+        self.split_mixed = False
+
+    def regime_of(self, f: StepFeatures) -> str:
+        return f.regime(self.split_mixed)
 
     def set_margin(self, mode: str = "legacy", k: float = 1.5) -> None:
         if mode not in self.MARGIN_MODES:
@@ -233,24 +285,33 @@ class MergedExecutionEstimator:
     def is_ready(self) -> bool:
         return any(p.is_fitted for p in self._params.values())
 
+    # ------------------------------------------------------------ state
     def export_state(self) -> dict:
-        return {"ft_mixed_split": ft_mixed_split(),
-                "params": {r: {n: getattr(p, n) for n in _NAMES} for r, p in self._params.items()},
-                "rmse": dict(self._rmse), "rel_rmse": dict(self._rel_rmse)}
+        """Per regime: the six coefficients (alpha .. c, None when unfitted)
+        and the fit's RMSE / relative RMSE."""
+        return {"split_mixed": self.split_mixed,
+                "regimes": {r: {"coef": [getattr(self._params[r], n) for n in _NAMES],
+                                "rmse": self._rmse[r], "rel_rmse": self._rel_rmse[r]} for r in REGIMES}}
 
     def import_state(self, state: dict) -> None:
-        for r, coefs in (state.get("params") or {}).items():
-            if r in self._params:
-                self._params[r] = StepParams(**coefs)
-                self._rmse[r] = (state.get("rmse") or {}).get(r)
-                self._rel_rmse[r] = (state.get("rel_rmse") or {}).get(r)
+        regimes = state.get("regimes")
+        if regimes is None:   # files written with per-name coefficient dicts
+            regimes = {r: {"coef": [c.get(n) for n in _NAMES],
+                           "rmse": (state.get("rmse") or {}).get(r),
+                           "rel_rmse": (state.get("rel_rmse") or {}).get(r)}
+                       for r, c in (state.get("params") or {}).items()}
+        for r, ent in regimes.items():
+            if r not in self._params:
+                continue
+            self._params[r] = StepParams(*ent["coef"])
+            self._rmse[r], self._rel_rmse[r] = ent.get("rmse"), ent.get("rel_rmse")
 
     @property
     def fit_rmse(self) -> float | None:
-        for r in (REGIME_EAGER, REGIME_INF_PREFILL, REGIME_DECODE_ONLY):
-            if self._rmse[r] is not None:
-                return self._rmse[r]
-        return None
+        """RMSE of the most informative fitted regime (FT steps first)."""
+        fitted = [self._rmse[r] for r in (REGIME_EAGER, REGIME_INF_PREFILL, REGIME_DECODE_ONLY)
+                  if self._rmse[r] is not None]
+        return fitted[0] if fitted else None
 
     def rmse(self, regime: str) -> float | None:
         return self._rmse[regime]
@@ -262,7 +323,7 @@ class MergedExecutionEstimator:
         return self._params[regime]
 
     def _select(self, f: StepFeatures, regime: str | None = None):
-        regime = regime or f.regime()
+        regime = regime or self.regime_of(f)
         p = self._params[regime]
         if p.is_fitted:
             return regime, p
@@ -288,34 +349,32 @@ class MergedExecutionEstimator:
             pred = self._with_margin(pred, r)
         return max(0.0, float(pred))
 
-    def data_fit(self, tracker: StepExecutionTracker) -> dict[str, StepParams]:
-        buckets: dict[str, tuple[list, list]] = {r: ([], []) for r in REGIMES}
-        contended = 0
-        for f, dur in zip(tracker.features, tracker.durations):
-            if f.contended:
-                contended += 1
-                continue
-            r = f.regime()
-            row = f.row()
-            buckets[r][0].append([row[i] for i in _COLS[r]])
-            buckets[r][1].append(dur)
-        msg = [f"excluded {contended} contended prefill"] if contended else []
+    def data_fit(self, log: StepLog) -> dict[str, StepParams]:
+        """Least squares per regime over the log's columns (prefill steps
+        taken while a backward was in flight are left out: contended)."""
+        c = {n: log.column(n) for n in StepLog._F}
+        dur = log.column("duration")
+        design = np.stack([c["s"], c["t_in"], c["t_ft"], c["b_d"], c["k"], np.ones_like(dur)], axis=1)
+        bwd = c["bwd"] > 0
+        contended = bwd & (c["t_in"] > 0)
+        labels = np.array([_regime(a, b, d, e, self.split_mixed)
+                           for a, b, d, e in zip(c["t_in"], c["t_ft"], c["b_d"], bwd)], dtype=object)
+        msg = [f"excluded {int(contended.sum())} contended prefill"] if contended.any() else []
         for r in REGIMES:
-            X, y = buckets[r]
-            if len(y) < MIN_FIT_SAMPLES:
+            sel = (labels == r) & ~contended
+            if int(sel.sum()) < MIN_FIT_SAMPLES:
                 continue
-            A, b = np.asarray(X, float), np.asarray(y, float)
-            coef, *_ = np.linalg.lstsq(A, b, rcond=None)
-            vals = [0.0] * 6
-            for c, i in zip(coef, _COLS[r]):
-                vals[i] = float(c)
-            self._params[r] = StepParams(*vals)
-            pred = A @ coef
-            self._rmse[r] = float(np.sqrt(np.mean((pred - b) ** 2)))
-            pos = b > 1e-6
-            self._rel_rmse[r] = (float(np.sqrt(np.mean(((pred[pos] - b[pos]) / b[pos]) ** 2)))
-                                 if pos.any() else None)
-            msg.append(f"{r}={len(y)}(rmse={self._rmse[r]:.5f})")
+            cols = list(_COLS[r])
+            A, y = design[sel][:, cols], dur[sel]
+            coef = np.linalg.lstsq(A, y, rcond=None)[0]
+            full = np.zeros(6)
+            full[cols] = coef
+            self._params[r] = StepParams(*map(float, full))
+            err = A @ coef - y
+            self._rmse[r] = float(np.sqrt(np.mean(err ** 2)))
+            pos = y > 1e-6
+            self._rel_rmse[r] = float(np.sqrt(np.mean((err[pos] / y[pos]) ** 2))) if pos.any() else None
+            msg.append(f"{r}={int(sel.sum())}(rmse={self._rmse[r]:.5f})")
         if msg:
             dprint("[estimator] fit: " + ", ".join(msg))
         return self._params

@@ -44,9 +44,9 @@ from ..models.lora import LoraServeBuffers, random_adapter
 from ..models.weights import TPInfo, init_weights
 from .ft.admission import FinetuneAdmission
 from .ft.coordinator import FinetuneCoordinator
-from .ft.estimator import MergedExecutionEstimator, StepExecutionTracker, StepFeatures, set_ft_mixed_split
+from .ft.estimator import MergedExecutionEstimator, StepFeatures, StepLog
 from .ft.store import FinetuningStore
-from .ft.tbt_window import TbtWindow
+from .ft.tbt_window import DecodeGapWindow
 from .ft_job import FinetuneJobSpec, FtJobManager
 from .kv_cache import KVCache
 from .model_runner import ModelRunner
@@ -169,9 +169,9 @@ class CoServingEngine:
                 dprint(f"[tp] {e}; step plans go through the process group")
         self.estimator = MergedExecutionEstimator()
         self.estimator.set_margin(self.ftcfg.admission_margin, self.ftcfg.admission_margin_k)
-        set_ft_mixed_split(self.ftcfg.graph_ft_batches)
-        self.tracker = StepExecutionTracker()
-        self.tbt_window = TbtWindow(self.ftcfg.avg_tbt_window_s) if self.ftcfg.avg_tbt_window_s > 0 else None
+        self.estimator.split_mixed = bool(self.ftcfg.graph_ft_batches)
+        self.tracker = StepLog()
+        self.tbt_window = DecodeGapWindow(self.ftcfg.avg_tbt_window_s) if self.ftcfg.avg_tbt_window_s > 0 else None
         self.coord = FinetuneCoordinator(cap_tokens, ft_started=self.ftcfg.start_on_launch,
                                          bwd_log_path=self.ftcfg.bwd_log_path)
         self.jobs = FtJobManager()
@@ -725,7 +725,7 @@ class CoServingEngine:
             self.tracker.add(rec.features, dur, rec.predicted)
             for cb in self.step_listeners:
                 cb(rec, dur)
-            if self.tracker.check_refit():
+            if self.tracker.due_for_refit():
                 self.estimator.data_fit(self.tracker)
 
     def _host(self, phase: str, t0: float) -> float:
@@ -877,7 +877,7 @@ class CoServingEngine:
             done.extend(self._check_stop_strings(out, now))
         self.stats["steps"] += 1
         if self.tbt_window is not None:
-            self.tbt_window.step_done(now, out.b_d, bool(self.scheduler.running))
+            self.tbt_window.note_step(now, out.b_d, bool(self.scheduler.running))
         if out.ft and (self.profiling or not record_capture):
             pass  # profiling FT rows: captured at offset 0, never trained
         elif out.ft:
@@ -1131,10 +1131,10 @@ class CoServingEngine:
             self._forced_ft = None
 
     def _profile_shape(self, sh, record: bool) -> None:
-        rng = np.random.default_rng(len(self.tracker.durations) + 17)
+        rng = np.random.default_rng(self.tracker.size() + 17)
         V = self.arch.vocab
         mk = lambda n: rng.integers(0, V, size=int(n)).tolist()
-        n0 = len(self.tracker.durations)
+        n0 = self.tracker.size()
         ids = []
         for i, n in enumerate(sh.inf_lens):
             rid = f"__prof__{self.step_no}_{i}"
@@ -1160,8 +1160,7 @@ class CoServingEngine:
             self._forced_ft_step()
         self.synchronize()
         if not record:
-            del self.tracker.features[n0:], self.tracker.durations[n0:], self.tracker.predicted[n0:]
-            del self.tracker.was_graph[n0:], self.tracker.timestamps[n0:]
+            self.tracker.truncate(n0)
         self.finished = [r for r in self.finished if not r.request_id.startswith("__prof")]
 
     def _bwd_call(self, fn, *args):
@@ -1321,7 +1320,7 @@ class CoServingEngine:
             path = self.ftcfg.batch_prediction_stats_path or (
                 self.ftcfg.estimator_validation_path if self.ftcfg.validate_estimator else None)
             if path:
-                self.tracker.write_prediction_stats_csv(path)
+                self.tracker.write_prediction_stats_csv(path, self.estimator.split_mixed)
         self.stop_telemetry()
         if self.trainer is not None:
             self.trainer.wait_saves()

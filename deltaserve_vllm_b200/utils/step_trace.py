@@ -67,7 +67,7 @@ def attach_step_trace(engine, path: str) -> StepTraceWriter:
     def on_step(rec, dur):
         f = rec.features
         adm = engine.last_admit
-        w.put_row(kind=rec.kind, t_done=time.time(), regime=f.regime(),
+        w.put_row(kind=rec.kind, t_done=time.time(), regime=est.regime_of(f),
                   regime_used=est.select_regime(f), t_in=f.t_in, p=f.p, t_ft=f.t_ft, b_d=f.b_d, k=f.k,
                   s=f.s, pred_raw=est.predict(f, apply_margin=False) if est.is_ready else None,
                   pred=rec.predicted, actual=dur, admit_code=adm.code if adm else None,

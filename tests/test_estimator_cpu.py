@@ -18,7 +18,7 @@ from deltaserve_vllm_b200.engine.ft import estimator as est_mod
 from deltaserve_vllm_b200.engine.ft.estimator import (MIN_FIT_SAMPLES, REFIT_EVERY, REGIME_DECODE_BWD,
                                                       REGIME_DECODE_ONLY, REGIME_EAGER, REGIME_FT_MIXED,
                                                       REGIME_INF_PREFILL, MergedExecutionEstimator,
-                                                      StepExecutionTracker, StepFeatures)
+                                                      StepFeatures, StepLog)
 from deltaserve_vllm_b200.engine.profiling import ProfilingShapeGenerator
 from deltaserve_vllm_b200.utils.step_trace import COLUMNS, StepTraceWriter, attach_step_trace
 
@@ -57,17 +57,23 @@ def _sample(rng, regime: str) -> StepFeatures:
 
 @pytest.fixture
 def split_on():
-    est_mod.set_ft_mixed_split(True)
-    yield
-    est_mod.set_ft_mixed_split(False)
+    """The FT-mixed regime split (graph_ft_batches) for the samples and the
+    estimators this test makes."""
+    return True
 
 
-def _tracker(rng, per_regime: int, regimes=tuple(TRUE)) -> StepExecutionTracker:
-    tr = StepExecutionTracker()
+def _est(split: bool = False) -> MergedExecutionEstimator:
+    e = MergedExecutionEstimator()
+    e.split_mixed = split
+    return e
+
+
+def _tracker(rng, per_regime: int, regimes=tuple(TRUE)) -> StepLog:
+    tr = StepLog()
     for r in regimes:
         for _ in range(per_regime):
             f = _sample(rng, r)
-            assert f.regime() == r
+            assert f.regime(True) == r
             tr.add(f, _t(f, r))
     return tr
 
@@ -75,7 +81,7 @@ def _tracker(rng, per_regime: int, regimes=tuple(TRUE)) -> StepExecutionTracker:
 def test_fit_recovers_known_coefficients_per_regime(split_on):
     rng = np.random.default_rng(0)
     tr = _tracker(rng, 64)
-    est = MergedExecutionEstimator()
+    est = _est(split_on)
     assert not est.is_ready and est.predict(StepFeatures(b_d=4, k=512.0)) == 0.0
     est.data_fit(tr)
     assert est.is_ready
@@ -100,7 +106,7 @@ def test_fit_recovers_known_coefficients_per_regime(split_on):
 
 def test_contended_prefill_excluded_and_min_samples():
     rng = np.random.default_rng(2)
-    tr = StepExecutionTracker()
+    tr = StepLog()
     for _ in range(32):                 # prefill while a backward runs: recorded, never fitted
         f = _sample(rng, REGIME_INF_PREFILL)
         f.bwd = True
@@ -138,24 +144,30 @@ def test_regime_routing_fallbacks():
 
 
 def test_refit_cadence_and_tracker_window():
-    tr = StepExecutionTracker(max_steps=3 * REFIT_EVERY)
+    tr = StepLog(capacity=REFIT_EVERY)
     f = StepFeatures(b_d=1, k=64.0)
     fired = []
-    for i in range(1, 2 * REFIT_EVERY + 3):
+    for i in range(1, 3 * REFIT_EVERY + 3):
         tr.add(f, 0.01)
-        if tr.check_refit():
+        if tr.due_for_refit():
             fired.append(i)
-        assert not tr.check_refit()      # at most once per size
-    assert fired == [REFIT_EVERY, 2 * REFIT_EVERY]
-    small = StepExecutionTracker(max_steps=10)
+        assert not tr.due_for_refit()      # at most once per REFIT_EVERY records
+    # the cadence keeps going after the ring is full
+    assert fired == [REFIT_EVERY, 2 * REFIT_EVERY, 3 * REFIT_EVERY]
+    small = StepLog(capacity=10)
     for i in range(25):
         small.add(StepFeatures(b_d=i + 1, k=1.0), float(i))
-    assert small.size() == 10 and small.durations[0] == 15.0
+    assert small.size() == 10 and small.durations[0] == 15.0 and small.feature(0).b_d == 16
+    grow = StepLog(capacity=10)
+    for i in range(6):
+        grow.add(StepFeatures(b_d=1, k=1.0), float(i))
+    grow.truncate(4)
+    assert grow.size() == 4 and list(grow.durations) == [0.0, 1.0, 2.0, 3.0]
 
 
 def test_margin_modes():
     rng = np.random.default_rng(4)
-    tr = StepExecutionTracker()
+    tr = StepLog()
     for _ in range(64):
         f = _sample(rng, REGIME_DECODE_ONLY)
         tr.add(f, _t(f, REGIME_DECODE_ONLY) * (1.0 + 0.05 * rng.standard_normal()))
@@ -177,21 +189,22 @@ def test_margin_modes():
 def test_estimator_and_tracker_state_round_trip(tmp_path, split_on):
     rng = np.random.default_rng(5)
     tr = _tracker(rng, 16)
-    est = MergedExecutionEstimator()
+    est = _est(split_on)
     est.data_fit(tr)
-    est2, tr2 = MergedExecutionEstimator(), StepExecutionTracker()
+    est2, tr2 = _est(split_on), StepLog()
     est2.import_state(est.export_state())
     tr2.import_state(tr.export_state())
     assert tr2.size() == tr.size()
+    assert np.array_equal(tr2.column("s"), tr.column("s"))
     for f in tr.features[::7]:
         assert est2.predict(f) == est.predict(f)
     # predictions are only written for steps that had one
     for i, f in enumerate(tr.features[:5]):
-        tr.predicted[i] = est.predict(f)
+        tr.set_predicted(i, est.predict(f))
     path = tmp_path / "pred" / "stats.csv"
-    tr.write_prediction_stats_csv(str(path))
+    tr.write_prediction_stats_csv(str(path), split_mixed=True)
     rows = list(csv.DictReader(open(path)))
-    assert len(rows) == 5 and rows[0]["regime"] == tr.features[0].regime()
+    assert len(rows) == 5 and rows[0]["regime"] == tr.features[0].regime(True)
 
 
 def test_profiling_shapes_cover_every_regime(split_on):

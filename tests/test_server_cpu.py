@@ -117,7 +117,7 @@ def test_api_completions_and_finetuning_control():
         assert lines[0].startswith("seq,kind") and len(lines) > 2
         with open(os.path.join(tmp, "est.json")) as f:
             st = json.load(f)
-        assert st["version"] == 1 and st["tracker"]["samples"]
+        assert st["version"] == 1 and st["tracker"]["cols"]["duration"]
 
 
 def test_estimator_state_round_trip():
@@ -131,8 +131,8 @@ def test_estimator_state_round_trip():
             saved = json.load(f)
         eng2 = make_engine(tmp, estimator_state_load_path=path, profile_num_repeats=1)
         eng2.profile_execution_model(shapes=[], repeats=1)
-        assert eng2.tracker.size() == len(saved["tracker"]["samples"])
-        assert eng2.estimator.export_state()["params"] == saved["estimator"]["params"]
+        assert eng2.tracker.size() == len(saved["tracker"]["cols"]["duration"])
+        assert eng2.estimator.export_state()["regimes"] == saved["estimator"]["regimes"]
         # a missing file is a warning, not an error
         assert not eng2.load_estimator_state(os.path.join(tmp, "missing.json"))
 
