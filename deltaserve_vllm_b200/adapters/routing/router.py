@@ -18,7 +18,7 @@ import json
 import time
 from dataclasses import dataclass
 
-from .decision import RoutingModel
+from .decision import PoolGeometry
 from .index import CentroidIndex
 
 ROUTED, FALLBACK = "routed", "fallback"
@@ -103,7 +103,7 @@ class Router:
         self.decision_log = decision_log
         self.tier_of = tier_of or (lambda name: "")
         self.index = CentroidIndex()
-        self.model = RoutingModel(self.index, *self._args)
+        self.model = PoolGeometry(self.index, *self._args)
         self.routed: dict[str, int] = {}
         self.requests = 0
 
@@ -113,17 +113,17 @@ class Router:
         snap = CentroidIndex(index.encoder, index.prefix, index.max_tokens)
         snap.names, snap.matrix = list(index.names), index.matrix.copy()
         snap.refs = dict(index.refs)
-        self.index, self.model = snap, RoutingModel(snap, *self._args)
+        self.index, self.model = snap, PoolGeometry(snap, *self._args)
 
     def _prefer(self, name: str):
         return (self.tier_of(name) == "gpu", self.routed.get(name, 0))
 
-    def _decide(self, model: RoutingModel, emb) -> RouteDecision:
+    def _decide(self, model: PoolGeometry, emb) -> RouteDecision:
         c = model.decide(emb, prefer=self._prefer, raw_floor=self.raw_floor)
-        reason = "" if c.adapter else (LOW_CONFIDENCE if c.low_confidence else BELOW_THRESHOLD)
+        reason = "" if c.adapter else (LOW_CONFIDENCE if c.below_gate else BELOW_THRESHOLD)
         if c.adapter:
             self.routed[c.adapter] = self.routed.get(c.adapter, 0) + 1
-        d = RouteDecision(c.adapter, c.score, reason, c.confidence, tuple(c.candidates))
+        d = RouteDecision(c.adapter, c.raw_cosine, reason, c.confidence, tuple(c.shortlist))
         if self.decision_log:
             try:
                 with open(self.decision_log, "a") as f:

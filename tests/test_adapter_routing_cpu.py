@@ -11,7 +11,7 @@ import tempfile
 import numpy as np
 import pytest
 
-from deltaserve_vllm_b200.adapters.routing.decision import CENTRED, RAW, UNGATED, RoutingModel, admission_report
+from deltaserve_vllm_b200.adapters.routing.decision import CENTRED, RAW, UNGATED, PoolGeometry, admission_report
 from deltaserve_vllm_b200.adapters.routing.encoder import HashingEncoder
 from deltaserve_vllm_b200.adapters.routing.index import CentroidIndex, Indexer, fingerprint, l2_normalize, select_samples
 from deltaserve_vllm_b200.adapters.routing.pool import ACTIVE, CPU, DISK, GPU, RETIRED, AdapterPool, PoolFull, read_registry
@@ -76,29 +76,29 @@ def test_select_samples_and_fingerprint():
 def test_decision_centred_routes_and_gates():
     centres, samples = _clusters()
     idx = _index(samples)
-    m = RoutingModel(idx, keep_percent=90, close_band=0.0, min_pool=4)
+    m = PoolGeometry(idx, keep_percent=90, close_band=0.0, min_pool=4)
     assert m.mode == CENTRED and m.threshold is not None
     # typical requests (near a cluster's centre) route to their adapter
     hits = sum(m.decide(samples[n][-8:].mean(0)).adapter == n for n in samples)
     assert hits == len(samples)
     # the top candidate is right for individual samples even when gated
-    assert sum(m.decide(samples[n][-1]).candidates[0] == n for n in samples) == len(samples)
+    assert sum(m.decide(samples[n][-1]).shortlist[0] == n for n in samples) == len(samples)
     # a request unlike every adapter falls back with low confidence
     far = -centres.mean(0)
     c = m.decide(far)
-    assert c.adapter is None and c.low_confidence
+    assert c.adapter is None and c.below_gate
     # keep_percent 100 disables the gate
-    assert RoutingModel(idx, keep_percent=100).threshold is None
+    assert PoolGeometry(idx, keep_percent=100).threshold is None
 
 
 def test_decision_small_pool_raw_and_ungated():
     _, samples = _clusters(n_adapters=2)
     idx = _index(samples)
-    assert RoutingModel(idx, min_pool=4).mode == RAW
+    assert PoolGeometry(idx, min_pool=4).mode == RAW
     bare = CentroidIndex()
     for n, S in samples.items():
         bare.add(n, S.mean(0))
-    m = RoutingModel(bare)
+    m = PoolGeometry(bare)
     assert m.mode == UNGATED and m.decide(samples["a1"][0]).adapter == "a1"
 
 
@@ -107,7 +107,7 @@ def test_decision_close_band_prefers():
     base = l2_normalize(np.ones(8))
     idx.add("x", base)
     idx.add("y", base + 1e-4)
-    m = RoutingModel(idx, close_band=0.5, min_pool=99)
+    m = PoolGeometry(idx, close_band=0.5, min_pool=99)
     assert m.decide(base, prefer=lambda n: n == "y").adapter in ("x", "y")
 
 
