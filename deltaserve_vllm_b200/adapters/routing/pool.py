@@ -51,24 +51,35 @@ def decayed(score: float, dt: float, half_life: float) -> float:
 
 
 class PoolFull(Exception):
-    pass
+    """The active set has no room for another adapter."""
+
+
+# Where an adapter's weights can be, coldest first; a move walks this order
+# one hop at a time, calling the backend verb of each hop.
+_TIERS = (DISK, CPU, GPU)
+_HOP_UP = {DISK: "load", CPU: "activate"}          # tier -> verb to the next warmer tier
+_HOP_DOWN = {GPU: "deactivate", CPU: "unload"}     # tier -> verb to the next colder tier
 
 
 @dataclass
 class PoolEntry:
+    """One adapter of the pool: identity, placement and usage.
+
+    ``usage`` is a frequency with exponential decay: every hit adds 1 to the
+    value decayed to the hit's time (``usage_at``)."""
     name: str
     path: str
     job: str | None = None
+    uid: int = 0                  # stable id (never reused, survives restarts)
     tier: str = DISK
     level: str = ACTIVE
     pinned: bool = False
-    uid: int = 0                  # stable id (never reused, survives restarts)
     admitted_at: float = 0.0
-    hits: int = 0
-    score: float = 0.0
-    score_at: float = 0.0
     centroid: object = None
     refs: object = None
+    hits: int = 0
+    usage: float = 0.0
+    usage_at: float = 0.0
 
     @property
     def enabled(self) -> bool:
@@ -138,6 +149,9 @@ class AdapterPool:
         for fn in self.listeners:
             fn(self)
 
+    def _full_message(self) -> str:
+        return f"no room in the active set: {len(self.active_names())} of {self.capacity} adapters are active"
+
     def _publish(self) -> None:
         if self.directory and not self._hold_save:
             self.save(self.directory)
@@ -151,21 +165,23 @@ class AdapterPool:
         if name in self.entries:
             raise ValueError(f"adapter '{name}' is already in the pool")
         if level == ACTIVE and len(self.active_names()) >= self.capacity:
-            raise PoolFull(f"adapter pool is full ({self.capacity} active)")
-        uid = uid if uid is not None else self._next_uid
+            raise PoolFull(self._full_message())
+        if uid is None:
+            uid = self._next_uid
         self._next_uid = max(self._next_uid, uid + 1)
         now = self.clock()
-        e = PoolEntry(name, path, job, DISK, level, pinned, uid, now, 0, 0.0, now, centroid, refs)
+        e = PoolEntry(name=name, path=path, job=job, uid=uid, level=level, pinned=pinned, admitted_at=now,
+                      centroid=centroid, refs=refs, usage_at=now)
         self.entries[name] = e
         try:
             if level == ACTIVE:
                 if load:
-                    self._to_cpu(e)
+                    self._move(e, CPU)
                 if centroid is not None:
                     self.index.add(name, centroid, refs=refs)
                     self._index_changed()
                 if load and prewarm and self.count(GPU) < self.gpu_slots:
-                    self._to_gpu(e)
+                    self._move(e, GPU)
         except Exception:
             self.entries.pop(name, None)
             if self.index.remove(name):
@@ -179,7 +195,7 @@ class AdapterPool:
     @_locked
     def remove(self, name: str) -> None:
         e = self.get(name)
-        self._to_disk(e)
+        self._move(e, DISK)
         if self.index.remove(name):
             self._index_changed()
         del self.entries[name]
@@ -189,31 +205,21 @@ class AdapterPool:
     def count(self, tier: str) -> int:
         return sum(1 for e in self.entries.values() if e.tier == tier)
 
-    def _to_cpu(self, e: PoolEntry) -> None:
-        if e.tier == DISK:
-            self.backend.load(e)
-        elif e.tier == GPU:
-            self.backend.deactivate(e)
-        e.tier = CPU
-
-    def _to_gpu(self, e: PoolEntry) -> None:
-        if e.tier == DISK:
-            self._to_cpu(e)
-        if e.tier != GPU:
-            self.backend.activate(e)
-            e.tier = GPU
-
-    def _to_disk(self, e: PoolEntry) -> None:
-        if e.tier == GPU:
-            self.backend.deactivate(e)
-            e.tier = CPU
-        if e.tier == CPU:
-            self.backend.unload(e)
-            e.tier = DISK
+    def _move(self, e: PoolEntry, target: str) -> None:
+        """Bring ``e``'s weights to ``target``, one tier at a time (the backend
+        sees load / activate going warmer, deactivate / unload going colder).
+        The entry's tier follows every hop that succeeded."""
+        want = _TIERS.index(target)
+        while _TIERS.index(e.tier) != want:
+            here = _TIERS.index(e.tier)
+            warmer = want > here
+            getattr(self.backend, (_HOP_UP if warmer else _HOP_DOWN)[e.tier])(e)
+            e.tier = _TIERS[here + (1 if warmer else -1)]
 
     def score_of(self, e: PoolEntry, now: float | None = None) -> float:
+        """Decayed usage of ``e`` at ``now``."""
         now = self.clock() if now is None else now
-        return decayed(e.score, now - e.score_at, self.half_life_s)
+        return decayed(e.usage, now - e.usage_at, self.half_life_s)
 
     def protected_names(self, now: float | None = None) -> set[str]:
         now = self.clock() if now is None else now
@@ -231,34 +237,29 @@ class AdapterPool:
 
     @_locked
     def ensure_gpu(self, name: str, in_use=()) -> bool:
-        """Give ``name`` a GPU slot, evicting by frequency if needed; False
-        when every slot is in use or protected (the adapter is at least
-        brought to the CPU tier)."""
+        """Give ``name`` a GPU slot, freeing the least-used unprotected slot
+        when all are taken; False when no slot can be freed (the adapter then
+        at least reaches the CPU tier)."""
         e = self.get(name)
-        if e.tier == GPU:
-            return True
-        if self.count(GPU) >= self.gpu_slots:
+        if e.tier != GPU and self.count(GPU) >= self.gpu_slots:
             victim = self.choose_victim(in_use, exclude=name)
             if victim is None:
-                if e.tier == DISK:
-                    self._to_cpu(e)
+                self._move(e, max(e.tier, CPU, key=_TIERS.index))
                 return False
-            self._to_cpu(self.entries[victim])
+            self._move(self.entries[victim], CPU)
             self.evictions += 1
-        self._to_gpu(e)
+        self._move(e, GPU)
         return True
 
     @_locked
     def note_hit(self, name: str, in_use=(), place: bool = True) -> PoolEntry:
-        """A request uses ``name`` (routed or named): bump its decayed score;
-        with ``place``, try to give it a GPU slot now."""
+        """A request uses ``name`` (routed or named): one more unit of decayed
+        usage; with ``place``, try to give it a GPU slot now."""
         e = self.get(name)
         now = self.clock()
-        e.score = self.score_of(e, now) + 1.0
-        e.score_at = now
+        e.usage, e.usage_at = self.score_of(e, now) + 1.0, now
         e.hits += 1
-        if e.tier == DISK:
-            self.cold_loads += 1
+        self.cold_loads += e.tier == DISK
         if place:
             self.ensure_gpu(name, in_use)
         return e
@@ -304,7 +305,7 @@ class AdapterPool:
         victim = None
         if rep["level"] == ACTIVE and not was_active and len(self.active_names()) >= self.capacity:
             if self.when_full == REJECT:
-                raise PoolFull(f"adapter pool is full ({self.capacity} active)")
+                raise PoolFull(self._full_message())
             if self.when_full == RETIRE_LEAST_USED:
                 victim = self._retire_victim(exclude=name)
             if victim is None:
@@ -320,7 +321,7 @@ class AdapterPool:
                               level=rep["level"], pinned=pinned)
             else:
                 if path != old.path:          # a new version: new weights, new id
-                    self._to_disk(old)
+                    self._move(old, DISK)
                     old.path, old.uid = path, self._next_uid
                     self._next_uid += 1
                 old.centroid, old.refs, old.job = centroid, refs, job or old.job
@@ -343,7 +344,7 @@ class AdapterPool:
     @_locked
     def offload(self, name: str) -> PoolEntry:
         e = self.get(name)
-        self._to_disk(e)
+        self._move(e, DISK)
         self._publish()
         return e
 
@@ -353,7 +354,7 @@ class AdapterPool:
         e.level = RETIRED
         if self.index.remove(name):
             self._index_changed()
-        self._to_disk(e)
+        self._move(e, DISK)
         self._publish()
         return e
 
@@ -405,53 +406,59 @@ class AdapterPool:
                                                                   key=lambda e: e.name)]}
 
     # ------------------------------------------------------------ persistence
+    def _registry(self) -> dict:
+        """The registry document: pool version, next id, the routable index
+        file of this version, one record per adapter."""
+        now = self.clock()
+        recs = []
+        for e in self.entries.values():
+            rec = self.describe(e, now)
+            rec["offloaded"] = e.tier == DISK
+            recs.append(rec)
+        return {"version": self.version, "next_uid": self._next_uid,
+                "routable": f"routable-{self.version}.npz", "adapters": recs}
+
     @_locked
     def save(self, directory: str) -> None:
-        """Routable index to a new versioned file, then the registry swapped
-        in by one rename (readers see the old pool or the new one)."""
+        """Write the routable index (a new versioned file whenever it changed)
+        and then the registry, replaced in one rename: a reader sees either
+        the previous pool or this one. Index files two versions old go."""
         os.makedirs(directory, exist_ok=True)
-        if self._dirty or not self.version:
+        if self._dirty or self.version == 0:
             self.version += 1
             self.index.save(os.path.join(directory, f"routable-{self.version}.npz"))
             self._dirty = False
-        now = self.clock()
-        reg = {"version": self.version, "next_uid": self._next_uid,
-               "routable": f"routable-{self.version}.npz",
-               "adapters": [{**self.describe(e, now), "offloaded": e.tier == DISK}
-                            for e in self.entries.values()]}
-        tmp = os.path.join(directory, REGISTRY_FILE + ".tmp")
-        with open(tmp, "w") as f:
-            json.dump(reg, f, indent=1)
-        os.replace(tmp, os.path.join(directory, REGISTRY_FILE))
-        for fn in os.listdir(directory):
-            m = _ROUTABLE.fullmatch(fn)
-            if m and int(m.group(1)) < self.version - 1:
-                try:
-                    os.unlink(os.path.join(directory, fn))
-                except OSError:
-                    pass
+        _write_json_atomic(os.path.join(directory, REGISTRY_FILE), self._registry())
+        stale = [f for f in os.listdir(directory)
+                 if (m := _ROUTABLE.fullmatch(f)) and int(m.group(1)) < self.version - 1]
+        for f in stale:
+            try:
+                os.unlink(os.path.join(directory, f))
+            except OSError:
+                pass
 
     @_locked
     def restore(self, directory: str, centroids: CentroidIndex | None = None) -> int:
-        """Re-register a saved registry's adapters with their levels, pins and
-        ids; centroids come from ``centroids`` (else the routable file)."""
+        """Bring back a saved pool: every adapter with its level, pin and id,
+        loaded unless it was offloaded; centroids from ``centroids`` or the
+        registry's routable index file. Returns the number of adapters."""
         reg = read_registry(directory)
         if reg is None:
             return 0
-        if centroids is None and reg.get("routable"):
-            p = os.path.join(directory, reg["routable"])
-            centroids = CentroidIndex.load(p) if os.path.exists(p) else None
+        if centroids is None:
+            f = os.path.join(directory, reg.get("routable") or "")
+            centroids = CentroidIndex.load(f) if reg.get("routable") and os.path.exists(f) else None
         self._hold_save += 1
         try:
             self.version = max(self.version, int(reg.get("version", 0)))
-            for a in reg["adapters"]:
-                c = r = None
-                if centroids is not None and a["name"] in centroids:
-                    c, r = centroids.centroid_of(a["name"]), centroids.refs.get(a["name"])
-                off = bool(a.get("offloaded"))
-                self.register(a["name"], a["path"], c, r, a.get("job"), load=not off, prewarm=not off,
-                              level=a.get("level", ACTIVE), pinned=bool(a.get("pinned")),
-                              uid=a.get("uid"))
+            for rec in reg["adapters"]:
+                known = centroids is not None and rec["name"] in centroids
+                cold = bool(rec.get("offloaded"))
+                self.register(rec["name"], rec["path"],
+                              centroids.centroid_of(rec["name"]) if known else None,
+                              centroids.refs.get(rec["name"]) if known else None,
+                              rec.get("job"), load=not cold, prewarm=not cold, level=rec.get("level", ACTIVE),
+                              pinned=bool(rec.get("pinned")), uid=rec.get("uid"))
             self._next_uid = max(self._next_uid, int(reg.get("next_uid", 0)))
         finally:
             self._hold_save -= 1
@@ -460,10 +467,20 @@ class AdapterPool:
         return len(reg["adapters"])
 
 
+def _write_json_atomic(path: str, obj) -> None:
+    """``obj`` as JSON at ``path``, replacing the old file in one rename."""
+    tmp = f"{path}.tmp"
+    with open(tmp, "w") as f:
+        json.dump(obj, f, indent=1)
+    os.replace(tmp, path)
+
+
 def read_registry(directory: str) -> dict | None:
+    """The registry of a pool directory (None when absent or unreadable)."""
     try:
         with open(os.path.join(directory, REGISTRY_FILE)) as f:
             reg = json.load(f)
     except (OSError, ValueError):
         return None
-    return reg if isinstance(reg, dict) and isinstance(reg.get("adapters"), list) else None
+    ok = isinstance(reg, dict) and isinstance(reg.get("adapters"), list)
+    return reg if ok else None
