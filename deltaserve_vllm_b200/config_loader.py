@@ -136,44 +136,52 @@ def load_yaml_config(path: str | Path, verbose: bool = False) -> dict[str, Any]:
     return raw
 
 
-def finetune_kwargs(config: dict[str, Any]) -> dict[str, Any]:
-    """Flat :class:`FinetuneConfig` kwargs from the finetune sections and ``ft_job``."""
-    out: dict[str, Any] = {}
-    for section in LEGACY_SECTIONS:
-        if config.get(section):
-            dprint(f"[config] note: section '{section}' is the old layout "
-                   f"(now finetune_param + finetune_features); loaded as is")
+def _finetune_settings(config: dict[str, Any]):
+    """Every finetune setting of a loaded YAML as ``(where, field, value)``:
+    the keys of the finetune sections (legacy one included), then the
+    ``ft_job`` keys that stand for a flat field."""
     for section in ALL_FINETUNE_SECTIONS:
         for key, value in (config.get(section) or {}).items():
-            if key in RETIRED_KEYS:
-                dprint(f"[config] WARNING: '{section}.{key}' is ignored "
-                       f"({RETIRED_KEYS[key]}); remove it")
-                continue
-            home = SECTION_OF.get(key)
-            if home is not None and home != section and section not in LEGACY_SECTIONS:
-                dprint(f"[config] WARNING: '{section}.{key}' belongs in section "
-                       f"'{home}' (loaded anyway)")
-            if key in out:
-                raise ValueError(f"finetune key '{key}' appears in two sections")
-            out[key] = value
+            yield section, key, value
+    for key, value in (config.get(FT_JOB_SECTION) or {}).items():
+        if key in JOB_FLAT_KEYS:
+            yield f"{FT_JOB_SECTION}.{key}", JOB_FLAT_KEYS[key], value
+
+
+def finetune_kwargs(config: dict[str, Any]) -> dict[str, Any]:
+    """Flat :class:`FinetuneConfig` kwargs from the finetune sections and
+    ``ft_job``, checked against the dataclass: a field set from two places is
+    an error, a retired key is dropped with a warning, a key outside its
+    usual section is accepted with a warning, and ``ft_job``'s metadata keys
+    land in ``ft_job``."""
+    import dataclasses
+    known = {f.name for f in dataclasses.fields(FinetuneConfig)}
+    for section in LEGACY_SECTIONS:
+        if config.get(section):
+            dprint(f"[config] section '{section}' uses the single-section layout; its keys are read as they are")
+    values: dict[str, Any] = {}
+    source: dict[str, str] = {}
+    for where, field_name, value in _finetune_settings(config):
+        if field_name in RETIRED_KEYS:
+            dprint(f"[config] WARNING: {where}.{field_name} has no effect any more "
+                   f"({RETIRED_KEYS[field_name]}) and is dropped")
+            continue
+        home = SECTION_OF.get(field_name)
+        if where in FINETUNE_SECTIONS and home is not None and home != where:
+            dprint(f"[config] WARNING: {where}.{field_name} is normally under '{home}'; accepted")
+        if field_name in values:
+            raise ValueError(f"finetune setting '{field_name}' is given twice ({source[field_name]} and {where})")
+        if field_name not in known:
+            raise ValueError(f"{where}.{field_name} is not a finetune setting")
+        values[field_name], source[field_name] = value, where
     job = config.get(FT_JOB_SECTION)
     if job:
-        meta: dict[str, Any] = {}
-        for key, value in job.items():
-            if key in JOB_FLAT_KEYS:
-                flat = JOB_FLAT_KEYS[key]
-                if flat in out:
-                    raise ValueError(f"'{FT_JOB_SECTION}.{key}' and "
-                                     f"'{SECTION_OF.get(flat)}.{flat}' set the "
-                                     f"same thing; keep one")
-                out[flat] = value
-            elif key in JOB_META_KEYS:
-                meta[key] = value
-            else:
-                raise ValueError(f"unknown '{FT_JOB_SECTION}' key '{key}'; known: "
-                                 f"{sorted((*JOB_META_KEYS, *JOB_FLAT_KEYS))}")
-        out["ft_job"] = meta
-    return out
+        extra = sorted(k for k in job if k not in JOB_FLAT_KEYS and k not in JOB_META_KEYS)
+        if extra:
+            raise ValueError(f"{FT_JOB_SECTION}: unsupported key(s) {extra}; allowed: "
+                             f"{sorted((*JOB_META_KEYS, *JOB_FLAT_KEYS))}")
+        values["ft_job"] = {k: v for k, v in job.items() if k in JOB_META_KEYS}
+    return values
 
 
 def finetune_value(config: dict[str, Any], key: str, default: Any = None) -> Any:
