@@ -54,20 +54,36 @@ BASELINE_VALUE = None  # the reference publishes no number for this metric on th
 METRIC = "co-served FT tokens/s at ≥99% SLO attainment; p99 TTFT & TBT (Llama-3-8B TP8)"
 
 
+# Workload presets (``--config``): model, trace, finetuning stream, SLOs, LoRA
+# rank. ``llama3-8b`` is the headline configuration; the others run the same
+# harness on the other model families of the benchmark plan.
+CONFIGS = {
+    "llama3-8b": dict(model="llama3-8b", rate_per_gpu=8.0, prompt_median=512, prompt_min=32,
+                      prompt_max=4096, out_min=32, out_max=256, ft_min=512, ft_max=512, ft_batch=8,
+                      ttft_slo=0.5, tbt_slo=0.06, lora_rank=16, max_model_len=4096 + 512),
+    # Qwen3-0.6B on one GPU: 20 req/s, prompts median 256 (16..2048), outputs
+    # 16..256, FT sequences of 128..512 tokens, SLOs 200 ms / 50 ms.
+    "qwen3-0.6b": dict(model="qwen3-0.6b", rate_per_gpu=20.0, prompt_median=256, prompt_min=16,
+                       prompt_max=2048, out_min=16, out_max=256, ft_min=128, ft_max=512, ft_batch=8,
+                       ttft_slo=0.2, tbt_slo=0.05, lora_rank=16, max_model_len=2048 + 256),
+    # Qwen3-14B at TP=2/4/8, LoRA r=32, the Llama-3-8B trace shapes.
+    "qwen3-14b": dict(model="qwen3-14b", rate_per_gpu=8.0, prompt_median=512, prompt_min=32,
+                      prompt_max=4096, out_min=32, out_max=256, ft_min=512, ft_max=512, ft_batch=8,
+                      ttft_slo=0.5, tbt_slo=0.06, lora_rank=32, max_model_len=4096 + 512),
+}
+
+
 def parse():
     p = argparse.ArgumentParser()
+    p.add_argument("--config", default="llama3-8b", choices=sorted(CONFIGS),
+                   help="workload preset (model, trace, FT stream, SLOs, LoRA rank)")
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--step-s", type=float, default=1.0, help="seconds of serving per bench step")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--model", default="llama3-8b")
-    p.add_argument("--rate-per-gpu", type=float, default=8.0)
-    p.add_argument("--ft-seq", type=int, default=512)
-    p.add_argument("--ft-batch", type=int, default=8)
+    p.add_argument("--rate-per-gpu", type=float, default=None, help="override the preset's arrival rate")
     p.add_argument("--max-batched-tokens", type=int, default=8192)
-    p.add_argument("--ttft-slo", type=float, default=0.5)
-    p.add_argument("--tbt-slo", type=float, default=0.06)
     p.add_argument("--profile-repeats", type=int, default=1)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--tp-comm", default="fused", choices=["nccl", "fused"],
@@ -76,7 +92,12 @@ def parse():
     p.add_argument("--run-ahead", type=int, default=6, help="backward layers queued ahead of the GPU")
     p.add_argument("--phase", default="both", choices=["prefill", "both"],
                    help="coserving_admission_phase (both: FT may ride decode-only steps too)")
-    return p.parse_args()
+    a = p.parse_args()
+    for k, v in CONFIGS[a.config].items():
+        if getattr(a, k, None) is None:
+            setattr(a, k, v)
+    a.ft_seq = a.ft_max
+    return a
 
 
 class ClockSampler:
@@ -121,13 +142,16 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def make_trace(rate: float, duration_s: float, vocab: int, seed: int):
+def make_trace(rate: float, duration_s: float, vocab: int, seed: int, args):
+    """Poisson arrivals; lognormal prompt lengths (sigma 0.8) clipped to the
+    preset's range; uniform output lengths; uniform-random token ids."""
     rng = np.random.default_rng(seed)
     t, out = 0.0, []
     while t < duration_s:
         t += rng.exponential(1.0 / rate)
-        plen = int(np.clip(np.round(rng.lognormal(np.log(512), 0.8)), 32, 4096))
-        olen = int(rng.integers(32, 257))
+        plen = int(np.clip(np.round(rng.lognormal(np.log(args.prompt_median), 0.8)), args.prompt_min,
+                           args.prompt_max))
+        olen = int(rng.integers(args.out_min, args.out_max + 1))
         out.append((t, rng.integers(0, vocab, size=plen).tolist(), olen))
     return out
 
@@ -201,9 +225,9 @@ def main():
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     arch = resolve_arch(args.model)
     cap = args.ft_seq * args.ft_batch
-    ecfg = EngineConfig(model=args.model, tensor_parallel_size=args.gpus, max_model_len=4096 + 512,
+    ecfg = EngineConfig(model=args.model, tensor_parallel_size=args.gpus, max_model_len=args.max_model_len,
                         block_size=64, max_num_seqs=256, max_num_batched_tokens=args.max_batched_tokens,
-                        max_loras=2, max_lora_rank=16, gpu_memory_utilization=0.85, seed=args.seed,
+                        max_loras=2, max_lora_rank=args.lora_rank, gpu_memory_utilization=0.85, seed=args.seed,
                         tp_comm=args.tp_comm)
     fcfg = FinetuneConfig(enable_finetuning=True, backward_cuda_graph=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
                           num_epochs=1000, ttft_slo=args.ttft_slo, max_tbt_slo=args.tbt_slo,
@@ -211,12 +235,12 @@ def main():
                           pause_on_arrival=True, backward_run_ahead_boundaries=args.run_ahead,
                           coserving_admission_phase=args.phase,
                           profile_num_repeats=args.profile_repeats)
-    store = FinetuningStore.synthetic(arch.vocab, 512, args.ft_seq, args.ft_seq, seed=args.seed + 7,
+    store = FinetuningStore.synthetic(arch.vocab, 512, args.ft_min, args.ft_max, seed=args.seed + 7,
                                       max_saved_finetuning_tokens=cap, total_epochs=1000)
     t0 = time.perf_counter()
     eng = CoServingEngine(ecfg, fcfg, comm=comm, arch=arch, ft_store=store)
     if rank == 0:   # replayed on the other ranks
-        eng.load_inference_adapter("inf", rank=16, alpha=32, seed=11)
+        eng.load_inference_adapter("inf", rank=args.lora_rank, alpha=2 * args.lora_rank, seed=11)
     if rank != 0:
         eng.follow()
         _exit_watchdog()
@@ -228,7 +252,7 @@ def main():
     eng.profile_execution_model(repeats=args.profile_repeats)
     dprint(f"profiling done at {time.perf_counter() - t0:.1f}s; estimator ready={eng.estimator.is_ready}")
     rate = args.rate_per_gpu * args.gpus
-    trace = make_trace(rate, 3600.0, arch.vocab, args.seed)
+    trace = make_trace(rate, 3600.0, arch.vocab, args.seed, args)
     ti = 0
     clock0 = time.perf_counter()
 
@@ -329,16 +353,21 @@ def main():
                                  if any(h.get("fill_ms") for h in hist) else None)}
     enough = len(reqs) >= 100 and len(hist) >= 3
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "FT tokens/s",
+        "metric": (METRIC if args.config == "llama3-8b" else
+                   f"co-served FT tokens/s at ≥99% SLO attainment; p99 TTFT & TBT ({args.model})"),
+        "value": round(value, 2), "unit": "FT tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": (round(value / BASELINE_VALUE, 3) if BASELINE_VALUE else None),
         "dtype": "bf16", "data": "synthetic (random-init weights, uniform-random token ids)",
         "config": {"model": args.model, "global_batch": args.ft_batch, "seq_len": args.ft_seq,
-                   "parallelism": f"tp{args.gpus}", "rate_req_s": rate,
+                   "parallelism": f"tp{args.gpus}", "rate_req_s": rate, "preset": args.config,
                    "step": f"{args.step_s:g} s of serving (all engine iterations in it)",
-                   "prompts": "lognormal(median 512, sigma 0.8) clip 32..4096",
-                   "outputs": "uniform 32..256", "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
+                   "prompts": f"lognormal(median {args.prompt_median}, sigma 0.8) clip "
+                              f"{args.prompt_min}..{args.prompt_max}",
+                   "outputs": f"uniform {args.out_min}..{args.out_max}",
+                   "ft_seq": f"uniform {args.ft_min}..{args.ft_max}", "lora_rank": args.lora_rank,
+                   "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
                    "l2": "inputs larger than L2 (16 GB of weights stream every step)",
                    "tp_comm": args.tp_comm, "admission_phase": args.phase,
                    "run_ahead_layers": args.run_ahead},

@@ -40,6 +40,7 @@ buckets, overlapped with the next layer's backward.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -319,6 +320,12 @@ class LoraBackward:
         # interleave between tiles (the backward runs at low priority).
         self.max_ctas = 1 << 30
         self._comm_streams: dict = {}
+        # Side-stream collective debugging (read once): DSERVE_BWD_COMM_SYNC=1
+        # joins every side-stream all-reduce right after it is issued;
+        # DSERVE_BWD_COMM_DELAY=<GPU cycles> spins the side stream before each
+        # one, turning a missing reduce_end into a deterministic stale read.
+        self.comm_sync = os.environ.get("DSERVE_BWD_COMM_SYNC", "0") == "1"
+        self.comm_delay_cycles = int(os.environ.get("DSERVE_BWD_COMM_DELAY", "0") or 0)
         # The head's gradient pass takes the vocabulary slice in chunks of
         # this many columns (a bf16 [n, chunk] gradient block at a time).
         self.vocab_chunk = 16384
@@ -358,6 +365,10 @@ class LoraBackward:
             cs = self._comm_streams[t.device] = torch.cuda.Stream(t.device)
         cs.wait_stream(torch.cuda.current_stream(t.device))
         with torch.cuda.stream(cs):
+            if self.comm_delay_cycles > 0:
+                # Race exposure: the collective starts late, so a consumer that
+                # reads ``t`` without reduce_end reads stale data every time.
+                torch.cuda._sleep(self.comm_delay_cycles)
             if self.timer is not None:
                 ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 ev0.record()
@@ -366,6 +377,9 @@ class LoraBackward:
                 self.timer.comm(f"allreduce_{tuple(t.shape)}_{str(t.dtype)[6:]}", ev0, ev1)
             else:
                 self.comm.all_reduce(t)
+        if self.comm_sync:
+            # Debug: join right away (the asynchronous path must match this).
+            torch.cuda.current_stream(t.device).wait_stream(cs)
         return cs
 
     @staticmethod

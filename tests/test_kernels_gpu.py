@@ -753,3 +753,39 @@ def test_push_reduce_norm_one_rank(M, K, D):
         assert ops.check_device_error() == 0
     finally:
         ws.close()
+
+
+class _DoubleComm:
+    """Stand-in for a 2-rank communicator whose all-reduce doubles in place."""
+    size, rank = 2, 0
+
+    def all_reduce(self, t):
+        t.mul_(2.0)
+        return t
+
+
+def test_bwd_comm_delay_exposes_a_missing_wait(monkeypatch):
+    """DSERVE_BWD_COMM_DELAY spins the backward's side stream before each
+    collective: a reader that skips reduce_end sees the old values every
+    time, one that joins sees the reduced ones; DSERVE_BWD_COMM_SYNC joins
+    at once."""
+    from deltaserve_vllm_b200.models.configs import PRESETS
+    from deltaserve_vllm_b200.models.lora_backward import LoraBackward, LoraMasters
+    from deltaserve_vllm_b200.models.weights import init_weights
+    arch = PRESETS["llama3-test"]
+    w = init_weights(arch, seed=1, device=DEV)
+    m = LoraMasters(arch, w.tp, 16, DEV)
+    for env, joined in (({"DSERVE_BWD_COMM_DELAY": str(int(2e8))}, False), ({"DSERVE_BWD_COMM_SYNC": "1"}, True)):
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        bwd = LoraBackward(w, m, 2.0, comm=_DoubleComm())
+        t = torch.ones(1 << 20, device=DEV)
+        h = bwd.reduce_begin(t)
+        early = t.clone()                      # no reduce_end: races the side stream
+        LoraBackward.reduce_end(h, t.device)
+        late = t.clone()
+        torch.cuda.synchronize()
+        assert float(late.min()) == 2.0
+        assert float(early.max()) == (2.0 if joined else 1.0)
+        for k in env:
+            monkeypatch.delenv(k)
