@@ -528,29 +528,27 @@ class LoraBackward:
                       tile_slots=self._tile_ones(dY.shape[0], dY.device), lora_seg=dZ.shape[1])
 
     def group_grads(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor, dZ: torch.Tensor) -> None:
-        """Factor gradients of one group into the trainer's grad buffer:
-        dA = dZ^T X and dB^T = s Z^T dY with Z^T = A X^T computed directly
-        (no transposed copies of Z)."""
+        """Factor gradients of one group into the trainer's grad buffer, three
+        GEMMs over the token dimension:
+
+        * ``Z = X A^T`` [n, P*R];
+        * ``dA = dZ^T X`` — written transposed by the GEMM (token-major
+          operands, no transposed copies);
+        * ``dB_p^T = s Z_p^T dY`` for every projection p at once: output
+          feature m keeps its own projection's R columns, scaled."""
         gg = self.geom[g]
         R = self.m.R
         PR = gg.P * R
         A = self.slot_A(layer, g)
         n = X.shape[0]
-        epi_c = EPI_BF16 if self.cdt == torch.bfloat16 else EPI_F32
-        ZT = torch.empty(PR, n, dtype=self.cdt, device=X.device)
-        self._mm(A, X, b_mn=False, epi=epi_c, out=ZT)        # Z^T [PR, n]
-        dZT = dZ[:, :PR].t().contiguous()                   # [PR, n]
-        gA = self.m.g(layer, g, "A")
-        self._mm(dZT, X, b_mn=True, out=gA)                 # [PR, K]
-        gBfT = self._mm(ZT, dY, b_mn=True)                  # [PR, N] (unscaled)
-        gBt = self.m.g(layer, g, "Bt")
-        for p in range(gg.P):
-            src = gBfT[p * R:(p + 1) * R]
-            if gg.interleave:
-                torch.mul(self._cols3(src, gg, p), self.s, out=self._cols3(gBt, gg, p))
-            else:
-                b0, b1 = self._bounds(gg, p)
-                torch.mul(src[:, b0:b1], self.s, out=gBt[:, b0:b1])
+        Z = torch.empty(n, PR, dtype=self.cdt, device=X.device)
+        self._mm(X, A, b_mn=False, epi=EPI_BF16 if self.cdt == torch.bfloat16 else EPI_F32, out=Z)
+        Xc, dYc = _bf(X, self.cdt), _bf(dY, self.cdt)
+        ops.gemm_wgrad(Xc if Xc.stride(-1) == 1 else Xc.contiguous(), dZ, self.m.g(layer, g, "A"),
+                       kind="t", n_valid=PR)
+        b1, b2 = (gg.b1, gg.b2) if gg.P == 3 else (gg.N, gg.N)
+        ops.gemm_wgrad(dYc if dYc.stride(-1) == 1 else dYc.contiguous(), Z, self.m.g(layer, g, "Bt"),
+                       kind="bt", n_valid=PR, R=R, b1=b1, b2=b2, interleave=gg.interleave, scale=self.s)
 
     def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
                        dX: torch.Tensor) -> None:

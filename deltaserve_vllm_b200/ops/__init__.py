@@ -376,3 +376,17 @@ def tp_reduce_rows(ws, M, buf, out, *, x=None, w=None, eps=0.0, add=None):
                           ws.gather_tables[buf])
     ext.wait_counts(ws.gcnt_addr, n_blocks, 0, M, ws.world, ws.rank)
     return ws.gather_view(buf, M)
+
+
+def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, scale=1.0):
+    """LoRA factor-gradient GEMM reducing over the token dimension (``a``
+    [T, M], ``b`` [T, >= n_valid] bf16, both token-major). ``kind="t"``:
+    ``out[N, M] = b^T a`` (fp32) for the first ``n_valid`` columns of ``b``;
+    ``kind="bt"``: ``out[j, m] = scale * (a^T b)[m, p(m) * R + j]`` with the
+    projection p(m) of output feature m (bounds ``b1`` / ``b2`` or 64-column
+    interleave) — every projection's B gradient of a group in one pass."""
+    k = {"t": 0, "bt": 1}[kind]
+    if a.is_cuda:
+        _native().gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))
+        return out
+    return ref.gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))

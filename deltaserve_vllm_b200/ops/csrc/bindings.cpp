@@ -26,6 +26,8 @@ void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, in
 void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
                    c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, torch::Tensor table, int64_t rank,
                    int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add);
+void dsv_gemm_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t kind, int64_t n_valid, int64_t R,
+                    int64_t b1, int64_t b2, bool interleave, double scale);
 void dsv_wait_counts(int64_t cnt, int64_t n, int64_t per_block, int64_t rows, int64_t skip_mod, int64_t skip_rem);
 void dsv_reduce_norm_bcast(int64_t recv, int64_t rank, int64_t world, int64_t blocks_cap, int64_t ld, int64_t M,
                            int64_t D, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> w, double eps,
@@ -80,6 +82,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ce_stats", &dsv_gemm_ce_stats, "LM-head GEMM whose epilogue keeps only softmax statistics");
   m.def("gemm_ce_grad", &dsv_gemm_ce_grad, "LM-head GEMM whose epilogue writes the cross-entropy gradient");
   m.def("gemm_push", &dsv_gemm_push, "MN-major GEMM pushing bf16 partial rows to their owner rank");
+  m.def("gemm_wgrad", &dsv_gemm_wgrad, "LoRA factor-gradient GEMM over the token dimension");
   m.def("wait_counts", &dsv_wait_counts, "one-CTA bounded wait on this rank's arrival counters");
   m.def("reduce_norm_bcast", &dsv_reduce_norm_bcast, "owned-row reduce + RMSNorm backward + P2P all-gather");
   m.def("ce_merge", &dsv_ce_merge, "merge per-tile softmax statistics of one vocabulary slice");

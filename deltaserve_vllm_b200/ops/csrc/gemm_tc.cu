@@ -34,7 +34,13 @@ namespace dsv {
 
 enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2, kEpiF32Accum = 3, kEpiPeerAR = 4,
                       kEpiShrink = 5, kEpiBF16T = 6, kEpiSwiGLUBwd = 7, kEpiCEStats = 8, kEpiCEGrad = 9,
-                      kEpiPushRows = 10 };
+                      kEpiPushRows = 10, kEpiF32T = 11, kEpiLoraBt = 12 };
+
+// Weight-gradient GEMMs of the LoRA factors (kEpiF32T, kEpiLoraBt) reduce over
+// the token dimension: both operands are token-major ([tokens, M] and
+// [tokens, N] row-major), so A is read MN-major like B.
+template <int EPI>
+constexpr bool a_mn_major() { return EPI == kEpiF32T || EPI == kEpiLoraBt; }
 
 constexpr int kMaxPeers = 8;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (backward NCCL cap + its waits)
@@ -117,6 +123,13 @@ struct GemmArgs {
   const float* ce_lse;
   float ce_scale;
   PushArgs push;          // kEpiPushRows only
+  // kEpiF32T: C is [N, M] fp32 (the transposed product; columns >= N skipped).
+  // kEpiLoraBt: the product is [M = output features, N = P * R]; row m keeps
+  // only the R columns of its own projection p(m) (p = 0 below bt_b1, 1 below
+  // bt_b2, else 2; or alternating 64-column blocks when bt_interleave) and
+  // stores them scaled by bt_scale into C[j, m] (C is [R, M] fp32).
+  int bt_r, bt_b1, bt_b2, bt_interleave;
+  float bt_scale;
 };
 
 // Work unit = (M tile, N tile, K split); M fastest, then N, then split.
@@ -528,6 +541,37 @@ __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, uint32_t t_r
         }
       }
     }
+  } else if constexpr (EPI == kEpiF32T) {
+    float* Cf = reinterpret_cast<float*>(args.C);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) {
+        const int col = n0 + c + i;
+        if (col < args.N) Cf[(size_t)col * args.ldc + row] = __uint_as_float(r[i]);
+      }
+    }
+  } else if constexpr (EPI == kEpiLoraBt) {
+    float* Cf = reinterpret_cast<float*>(args.C);
+    const int R = args.bt_r;
+    const int p = args.bt_interleave ? ((row >> 6) & 1) : (row < args.bt_b1 ? 0 : (row < args.bt_b2 ? 1 : 2));
+    const int lo = p * R;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) {
+        const int j = n0 + c + i - lo;
+        if (j >= 0 && j < R) Cf[(size_t)j * args.ldc + row] = args.bt_scale * __uint_as_float(r[i]);
+      }
+    }
   } else if constexpr (EPI == kEpiCEStats) {
     // Online max / sum-exp over this tile's columns (32 at a time), and the
     // label's logit when the label falls in the tile.
@@ -703,7 +747,12 @@ __global__ void __launch_bounds__(256, 1)
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
         if (j < tl.n_main) {
           const int k0 = (tl.kb_lo + j) * BK;
-          tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+          if constexpr (a_mn_major<EPI>()) {
+#pragma unroll
+            for (int jj = 0; jj < BM / 64; ++jj) tma_load_2d(sA + jj * (64 * BK * 2), &tmA, &full_bar[stage], m0 + jj * 64, k0);
+          } else {
+            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+          }
           if constexpr (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * (64 * BK * 2), &tmB, &full_bar[stage], n0 + j * 64, k0);
@@ -743,7 +792,7 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, B_MN);
+    constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, a_mn_major<EPI>(), B_MN);
     int stage = 0;
     uint32_t phase = 0;
     int iter = 0;
@@ -764,7 +813,8 @@ __global__ void __launch_bounds__(256, 1)
         const bool lora_blk = kb >= tl.n_main;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t da = smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+          const uint64_t da = a_mn_major<EPI>() ? smem_desc(a_addr + k * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B)
+                                                : smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
           uint64_t db;
           (void)lora_blk;
           if (B_MN) {
@@ -1676,6 +1726,57 @@ void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor
   }
   dsv_gemm_impl(a, b, a, true, kEpiPushRows, z, b2, tile_slots, lora_seg, c10::nullopt, 0, 0, 0, 0, 0, c10::nullopt,
                 c10::nullopt, &ex);
+}
+
+// LoRA factor gradients, reducing over the token dimension (both operands
+// token-major, read MN-major): a [T, M], b [T, N] bf16.
+//   kind 0 (kEpiF32T):   out [N, M] fp32 = (a^T b)^T = b^T a   (dA = dZ^T X from a = X, b = dZ);
+//   kind 1 (kEpiLoraBt): out [R, M] fp32, out[j, m] = scale * (a^T b)[m, p(m) * R + j]
+//                        (dB of every projection of a group from a = dY, b = Z).
+// n_valid bounds the columns of b that are used (the rest may be padding).
+void dsv_gemm_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t kind, int64_t n_valid, int64_t R,
+                    int64_t b1, int64_t b2, bool interleave, double scale) {
+  using namespace dsv;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_wgrad: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kFloat,
+              "gemm_wgrad: bf16 operands, fp32 output");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1,
+              "gemm_wgrad: row-major 2-D tensors");
+  const int T = (int)a.size(0), M = (int)a.size(1), N = (int)n_valid;
+  TORCH_CHECK(b.size(0) == T && N >= 1 && N <= b.size(1) && N <= 256, "gemm_wgrad: b must be [T, >= n_valid <= 256]");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_wgrad: 16-byte row pitch");
+  if (kind == 0) {
+    TORCH_CHECK(out.size(0) >= N && out.size(1) >= M, "gemm_wgrad: out must be [N, M]");
+  } else {
+    TORCH_CHECK(out.size(0) >= R && out.size(1) >= M && R >= 1, "gemm_wgrad: out must be [R, M]");
+  }
+  if (T == 0 || M == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = T;
+  args.k_splits = 1;
+  args.C = out.data_ptr();
+  args.ldc = (int)out.stride(0);
+  args.bt_r = (int)R;
+  args.bt_b1 = (int)b1;
+  args.bt_b2 = (int)b2;
+  args.bt_interleave = interleave ? 1 : 0;
+  args.bt_scale = (float)scale;
+  const int bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), T, M, a.stride(0), BK);
+  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), T, b.size(1), b.stride(0), BK);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (kind == 0) {
+    if (bn == 64) launch<64, true, kEpiF32T>(ta, tb, ta, tb, args, st);
+    else if (bn == 128) launch<128, true, kEpiF32T>(ta, tb, ta, tb, args, st);
+    else launch<256, true, kEpiF32T>(ta, tb, ta, tb, args, st);
+  } else {
+    if (bn == 64) launch<64, true, kEpiLoraBt>(ta, tb, ta, tb, args, st);
+    else if (bn == 128) launch<128, true, kEpiLoraBt>(ta, tb, ta, tb, args, st);
+    else launch<256, true, kEpiLoraBt>(ta, tb, ta, tb, args, st);
+  }
 }
 
 // Multi-LoRA shrink on the tensor cores: Z[T, slots*seg] from x[T, K] and the

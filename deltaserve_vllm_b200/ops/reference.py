@@ -374,3 +374,16 @@ def ce_grad(h, w, labels, v0, lse, scale, dlog):
     g[labels[:M] < 0] = 0.0
     dlog.copy_(g.to(dlog.dtype))
     return dlog
+
+
+def gemm_wgrad(a, b, out, kind, n_valid, R, b1, b2, interleave, scale):
+    prod = a.float().t() @ b[:, :n_valid].float()          # [M, n_valid]
+    M = a.shape[1]
+    if kind == 0:
+        out[:n_valid, :M] = prod.t()
+        return out
+    m = torch.arange(M)
+    p = ((m // 64) % 2) if interleave else torch.where(m < b1, 0, torch.where(m < b2, 1, 2))
+    cols = p[:, None] * R + torch.arange(R)[None, :]        # [M, R]
+    out[:R, :M] = (scale * prod.gather(1, cols.to(prod.device))).t()
+    return out

@@ -789,3 +789,25 @@ def test_bwd_comm_delay_exposes_a_missing_wait(monkeypatch):
         assert float(early.max()) == (2.0 if joined else 1.0)
         for k in env:
             monkeypatch.delenv(k)
+
+
+@pytest.mark.parametrize("T,M,PR,R,mode", [(4096, 4096, 48, 16, "qkv"), (1000, 3584, 32, 16, "gate_up"),
+                                          (777, 512, 16, 16, "o"), (2048, 1792, 192, 64, "qkv")])
+def test_gemm_wgrad_vs_fp32(T, M, PR, R, mode):
+    """LoRA factor-gradient GEMMs over the token dimension: dA^T written
+    transposed, and every projection's scaled dB^T scattered by output
+    feature, against fp32 references."""
+    a = rnd(T, M, seed=81)
+    b = rnd(T, PR, seed=82)
+    out = torch.zeros(PR, M, device=DEV)
+    ops.gemm_wgrad(a, b, out, kind="t", n_valid=PR)
+    prod = a.float().t() @ b.float()                       # [M, PR]
+    torch.testing.assert_close(out, prod.t(), rtol=1e-3, atol=1e-2)
+    interleave = mode == "gate_up"
+    b1, b2 = (M // 2, 3 * M // 4) if mode == "qkv" else (M, M)
+    bt = torch.zeros(R, M, device=DEV)
+    ops.gemm_wgrad(a, b, bt, kind="bt", n_valid=PR, R=R, b1=b1, b2=b2, interleave=interleave, scale=0.5)
+    exp = torch.zeros(R, M)
+    ref.gemm_wgrad(a.cpu(), b.cpu(), exp, 1, PR, R, b1, b2, interleave, 0.5)
+    torch.testing.assert_close(bt.cpu(), exp, rtol=1e-3, atol=1e-2)
+    assert ops.check_device_error() == 0
