@@ -90,6 +90,10 @@ def parse():
                    help="row-parallel all-reduce: fused GEMM+all-reduce kernel over NVLink peer memory "
                         "(falls back to NCCL if its start-up self-test fails) or plain NCCL")
     p.add_argument("--run-ahead", type=int, default=6, help="backward layers queued ahead of the GPU")
+    p.add_argument("--bwd-sm-pct", type=int, default=0,
+                   help="backward_mps_percentage: cap the backward GEMMs at this share of the SMs (0 = no cap)")
+    p.add_argument("--pause", default="arrival", choices=["arrival", "off"],
+                   help="pause_on_arrival: stop feeding the backward while an inference prefill is pending")
     p.add_argument("--phase", default="both", choices=["prefill", "both"],
                    help="coserving_admission_phase (both: FT may ride decode-only steps too)")
     a = p.parse_args()
@@ -232,7 +236,8 @@ def main():
     fcfg = FinetuneConfig(enable_finetuning=True, backward_cuda_graph=True, max_saved_finetuning_tokens=cap, learning_rate=1e-4,
                           num_epochs=1000, ttft_slo=args.ttft_slo, max_tbt_slo=args.tbt_slo,
                           avg_tbt_slo=args.tbt_slo, admission_margin="relative", admission_margin_k=1.5,
-                          pause_on_arrival=True, backward_run_ahead_boundaries=args.run_ahead,
+                          pause_on_arrival=args.pause == "arrival", backward_mps_percentage=args.bwd_sm_pct,
+                          backward_run_ahead_boundaries=args.run_ahead,
                           coserving_admission_phase=args.phase,
                           profile_num_repeats=args.profile_repeats)
     store = FinetuningStore.synthetic(arch.vocab, 512, args.ft_min, args.ft_max, seed=args.seed + 7,
@@ -369,7 +374,8 @@ def main():
                    "ft_seq": f"uniform {args.ft_min}..{args.ft_max}", "lora_rank": args.lora_rank,
                    "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
                    "l2": "inputs larger than L2 (16 GB of weights stream every step)",
-                   "tp_comm": args.tp_comm, "admission_phase": args.phase,
+                   "tp_comm": args.tp_comm, "admission_phase": args.phase, "pause": args.pause,
+                   "bwd_sm_pct": args.bwd_sm_pct,
                    "run_ahead_layers": args.run_ahead},
         "fused_ar_active": eng.peer_ws is not None,
         "slo_attainment": attain, "p99_ttft_ms": (percentile(ttfts, 99) or 0) * 1e3 if ttfts else None,

@@ -241,9 +241,11 @@ class CoServingEngine:
             self.start_telemetry(self.ftcfg.metrics_dir)
         if self.ftcfg.print_weight_hash:
             dprint(f"[weights] rank {self.tp.rank} hash {self.weight_hash():.6e}")
-        if self.ftcfg.backward_mps_percentage:
-            dprint("[config] backward_mps_percentage is ignored: the backward runs on a "
-                   "low-priority stream of this process (no MPS)")
+        if self.ftcfg.backward_mps_percentage and self.trainer is not None and self.cuda:
+            # The backward is a low-priority stream of this process, not an MPS
+            # client: its share of the GPU becomes a cap on its GEMM grids.
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            self.trainer.bwd.set_sm_share(float(self.ftcfg.backward_mps_percentage), sms)
 
     # ------------------------------------------------------------------ setup
     def _alloc_kv(self) -> KVCache:

@@ -317,7 +317,9 @@ class LoraBackward:
         self._rows: dict[tuple[str, int], torch.Tensor] = {}
         self._ones_slots: dict = {}
         # Backward GEMMs launch one CTA per tile so the inference stream can
-        # interleave between tiles (the backward runs at low priority).
+        # interleave between tiles (the backward runs at low priority); with
+        # an SM share (:meth:`set_sm_share`) they run persistent grids of that
+        # many CTAs instead, leaving the rest of the GPU to the forward.
         self.max_ctas = 1 << 30
         self._comm_streams: dict = {}
         # Side-stream collective debugging (read once): DSERVE_BWD_COMM_SYNC=1
@@ -343,6 +345,15 @@ class LoraBackward:
         # ``mark(name)`` closes the phase that ends here on the current stream,
         # ``comm(name, ev0, ev1)`` brackets a collective on its side stream.
         self.timer = None
+
+    def set_sm_share(self, percent: float, num_sms: int) -> None:
+        """Cap every backward GEMM at ``percent`` of the GPU's SMs (the
+        reference's ``backward_mps_percentage``, which gives its backward
+        process that share of the GPU through MPS); 0 or >= 100 = no cap."""
+        if percent <= 0 or percent >= 100:
+            self.max_ctas = 1 << 30
+        else:
+            self.max_ctas = max(8, int(round(num_sms * percent / 100.0)))
 
     def _mark(self, name: str) -> None:
         if self.timer is not None:
@@ -525,7 +536,8 @@ class LoraBackward:
         block's owner rank (completed by ``ops.tp_reduce_rows``)."""
         ap = self.slot_A(layer, g)
         ops.gemm_push(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), self.tpws, z=dZ, b2=ap,
-                      tile_slots=self._tile_ones(dY.shape[0], dY.device), lora_seg=dZ.shape[1])
+                      tile_slots=self._tile_ones(dY.shape[0], dY.device), lora_seg=dZ.shape[1],
+                      max_ctas=self.max_ctas)
 
     def group_grads(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor, dZ: torch.Tensor) -> None:
         """Factor gradients of one group into the trainer's grad buffer, three
@@ -545,10 +557,11 @@ class LoraBackward:
         self._mm(X, A, b_mn=False, epi=EPI_BF16 if self.cdt == torch.bfloat16 else EPI_F32, out=Z)
         Xc, dYc = _bf(X, self.cdt), _bf(dY, self.cdt)
         ops.gemm_wgrad(Xc if Xc.stride(-1) == 1 else Xc.contiguous(), dZ, self.m.g(layer, g, "A"),
-                       kind="t", n_valid=PR)
+                       kind="t", n_valid=PR, max_ctas=self.max_ctas)
         b1, b2 = (gg.b1, gg.b2) if gg.P == 3 else (gg.N, gg.N)
         ops.gemm_wgrad(dYc if dYc.stride(-1) == 1 else dYc.contiguous(), Z, self.m.g(layer, g, "Bt"),
-                       kind="bt", n_valid=PR, R=R, b1=b1, b2=b2, interleave=gg.interleave, scale=self.s)
+                       kind="bt", n_valid=PR, R=R, b1=b1, b2=b2, interleave=gg.interleave, scale=self.s,
+                       max_ctas=self.max_ctas)
 
     def group_backward(self, layer: int, g: str, X: torch.Tensor, dY: torch.Tensor,
                        dX: torch.Tensor) -> None:
@@ -633,7 +646,7 @@ class LoraBackward:
         st = self._head_scratch(n, dev)
         self._mark("head_norm")
         st["tgt"].zero_()
-        tiles = ops.ce_stats(h, headc, labels, v0, st["stats"], st["tgt"])
+        tiles = ops.ce_stats(h, headc, labels, v0, st["stats"], st["tgt"], max_ctas=self.max_ctas)
         ops.ce_merge(st["stats"], tiles, st["tgt"], st["part"])
         if world > 1:
             self.comm.all_gather_into(st["parts"], st["part"])
@@ -648,15 +661,16 @@ class LoraBackward:
         dh = st["dh"]
         for i, (c0, c1) in enumerate(chunks):
             dlog = st["dlog"][:, :c1 - c0]
-            ops.ce_grad(h, headc[c0:c1], labels, v0 + c0, st["lse"], 1.0 / n_valid, dlog)
+            ops.ce_grad(h, headc[c0:c1], labels, v0 + c0, st["lse"], 1.0 / n_valid, dlog, max_ctas=self.max_ctas)
             last = i == len(chunks) - 1
             if fused and last:
                 # The last chunk's product goes straight to the row owners
                 # (with the earlier chunks' fp32 sum added), then the owner
                 # applies the final-norm backward and all-gathers the rows.
-                ops.gemm_push(dlog, headc[c0:c1], self.tpws, add=dh if i > 0 else None)
+                ops.gemm_push(dlog, headc[c0:c1], self.tpws, add=dh if i > 0 else None, max_ctas=self.max_ctas)
             else:
-                ops.gemm(dlog, headc[c0:c1], dh, b_mn=True, epi=EPI_F32 if i == 0 else EPI_F32_ACCUM)
+                ops.gemm(dlog, headc[c0:c1], dh, b_mn=True, epi=EPI_F32 if i == 0 else EPI_F32_ACCUM,
+                         max_ctas=self.max_ctas)
             self._mark("head_grad")
             if not last:
                 yield "head_chunk"

@@ -312,14 +312,14 @@ def sample(logits, temps, seeds, out, top_k=None, top_p=None, logprobs=None):
 
 # ----------------------------------------------------------------- LM head + CE (vocabulary slices)
 
-def ce_stats(h, w, labels, v0, stats, tgt) -> int:
+def ce_stats(h, w, labels, v0, stats, tgt, max_ctas=0) -> int:
     """Softmax statistics of ``logits = h @ w.T`` (``w``: vocabulary rows
     ``[v0, v0 + N)``) without storing the logits: per row and N tile
     (max, sum exp(logit - max)) into ``stats`` (fp32 [M, >= 2 * ceil(N / 64)],
     float pairs) and the label's logit into ``tgt`` (rows whose label is
     outside the slice keep their value). Returns the tiles per row."""
     if h.is_cuda:
-        return int(_native().gemm_ce_stats(h, w, labels, int(v0), stats, tgt))
+        return int(_native().gemm_ce_stats(h, w, labels, int(v0), stats, tgt, int(max_ctas)))
     return ref.ce_stats(h, w, labels, int(v0), stats, tgt)
 
 
@@ -340,25 +340,25 @@ def ce_finalize(parts, labels, lse, loss):
     return ref.ce_finalize(parts, labels, lse, loss)
 
 
-def ce_grad(h, w, labels, v0, lse, scale, dlog):
+def ce_grad(h, w, labels, v0, lse, scale, dlog, max_ctas=0):
     """bf16 ``dlog = (softmax - onehot) * scale`` for ``logits = h @ w.T``
     (``w``: vocabulary rows ``[v0, v0 + N)``), recomputed from ``lse``; zero
     rows where the label is -1."""
     if h.is_cuda:
-        _native().gemm_ce_grad(h, w, labels, int(v0), lse, float(scale), dlog)
+        _native().gemm_ce_grad(h, w, labels, int(v0), lse, float(scale), dlog, int(max_ctas))
         return dlog
     return ref.ce_grad(h, w, labels, int(v0), lse, float(scale), dlog)
 
 
 # ----------------------------------------------------------------- tensor-parallel backward over peer memory
 
-def gemm_push(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, add=None):
+def gemm_push(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, add=None, max_ctas=0):
     """``a @ b`` (``b`` MN-major [K, N]) plus the LoRA term, pushed as bf16
     partial rows to each 128-row block's owner rank in ``ws`` (a
     :class:`~..parallel.peer.BwdPeerWorkspace`); ``add`` (fp32 [M, N]) is
     added first. Nothing waits here: :func:`tp_reduce_rows` completes it."""
     _native().gemm_push(a, b, z, b2, tile_slots, lora_seg, ws.push_table, ws.rank, ws.world, ws.blocks_cap,
-                        ws.ld, add)
+                        ws.ld, add, int(max_ctas))
 
 
 def tp_reduce_rows(ws, M, buf, out, *, x=None, w=None, eps=0.0, add=None):
@@ -378,7 +378,7 @@ def tp_reduce_rows(ws, M, buf, out, *, x=None, w=None, eps=0.0, add=None):
     return ws.gather_view(buf, M)
 
 
-def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, scale=1.0):
+def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, scale=1.0, max_ctas=0):
     """LoRA factor-gradient GEMM reducing over the token dimension (``a``
     [T, M], ``b`` [T, >= n_valid] bf16, both token-major). ``kind="t"``:
     ``out[N, M] = b^T a`` (fp32) for the first ``n_valid`` columns of ``b``;
@@ -387,6 +387,7 @@ def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, s
     interleave) — every projection's B gradient of a group in one pass."""
     k = {"t": 0, "bt": 1}[kind]
     if a.is_cuda:
-        _native().gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))
+        _native().gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale),
+                             int(max_ctas))
         return out
     return ref.gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))

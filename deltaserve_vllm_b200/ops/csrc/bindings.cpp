@@ -20,14 +20,15 @@ void dsv_peer_free(int64_t addr);
 void dsv_peer_zero(int64_t addr, int64_t bytes);
 torch::Tensor dsv_peer_view(int64_t addr, std::vector<int64_t> shape, c10::ScalarType dtype, int64_t device);
 int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor stats,
-                          torch::Tensor tgt);
+                          torch::Tensor tgt, int64_t max_ctas);
 void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor lse,
-                      double scale, torch::Tensor dlog);
+                      double scale, torch::Tensor dlog, int64_t max_ctas);
 void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
                    c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, torch::Tensor table, int64_t rank,
-                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add);
+                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add,
+                   int64_t max_ctas);
 void dsv_gemm_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t kind, int64_t n_valid, int64_t R,
-                    int64_t b1, int64_t b2, bool interleave, double scale);
+                    int64_t b1, int64_t b2, bool interleave, double scale, int64_t max_ctas);
 void dsv_wait_counts(int64_t cnt, int64_t n, int64_t per_block, int64_t rows, int64_t skip_mod, int64_t skip_rem);
 void dsv_reduce_norm_bcast(int64_t recv, int64_t rank, int64_t world, int64_t blocks_cap, int64_t ld, int64_t M,
                            int64_t D, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> w, double eps,

@@ -1650,7 +1650,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
 // into tgt[row] when the label lies in this slice (other rows untouched).
 // Returns the number of N tiles written per row.
 int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor stats,
-                          torch::Tensor tgt) {
+                          torch::Tensor tgt, int64_t max_ctas) {
   using namespace dsv;
   const int M = (int)h.size(0), N = (int)w.size(0);
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() >= M,
@@ -1666,7 +1666,7 @@ int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels
   ex.ce_ld = (int)(stats.stride(0) / 2);
   ex.ce_tgt = tgt.data_ptr<float>();
   const int bn = dsv_gemm_impl(h, w, stats, false, kEpiCEStats, c10::nullopt, c10::nullopt, c10::nullopt, 0,
-                               c10::nullopt, 0, 0, 0, 0, 0, c10::nullopt, c10::nullopt, &ex);
+                               c10::nullopt, 0, 0, 0, 0, max_ctas, c10::nullopt, c10::nullopt, &ex);
   return (N + bn - 1) / bn;
 }
 
@@ -1675,7 +1675,7 @@ int64_t dsv_gemm_ce_stats(torch::Tensor h, torch::Tensor w, torch::Tensor labels
 // vocabulary; lse [M] is each row's log-sum-exp over the whole vocabulary;
 // rows whose label is -1 get zeros.
 void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, int64_t v0, torch::Tensor lse,
-                      double scale, torch::Tensor dlog) {
+                      double scale, torch::Tensor dlog, int64_t max_ctas) {
   using namespace dsv;
   const int M = (int)h.size(0);
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() >= M,
@@ -1689,7 +1689,7 @@ void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, in
   ex.ce_lse = lse.data_ptr<float>();
   ex.ce_scale = (float)scale;
   dsv_gemm_impl(h, w, dlog, false, kEpiCEGrad, c10::nullopt, c10::nullopt, c10::nullopt, 0, c10::nullopt, 0, 0, 0,
-                0, 0, c10::nullopt, c10::nullopt, &ex);
+                0, max_ctas, c10::nullopt, c10::nullopt, &ex);
 }
 
 // a @ b (MN-major b, [K, N]) (+ the LoRA term z @ b2) pushed to the row
@@ -1698,7 +1698,8 @@ void dsv_gemm_ce_grad(torch::Tensor h, torch::Tensor w, torch::Tensor labels, in
 // rank); `add` (optional fp32 [M, >= N]) is added before the push.
 void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
                    c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, torch::Tensor table, int64_t rank,
-                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add) {
+                   int64_t world, int64_t blocks_cap, int64_t ld, c10::optional<torch::Tensor> add,
+                   int64_t max_ctas) {
   using namespace dsv;
   const int M = (int)a.size(0), N = (int)b.size(1);
   TORCH_CHECK(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world, "gemm_push: rank/world");
@@ -1724,8 +1725,8 @@ void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor
     P.recv[r] = reinterpret_cast<__nv_bfloat16*>(tab[r]);
     P.cnt[r] = reinterpret_cast<uint32_t*>(tab[world + r]);
   }
-  dsv_gemm_impl(a, b, a, true, kEpiPushRows, z, b2, tile_slots, lora_seg, c10::nullopt, 0, 0, 0, 0, 0, c10::nullopt,
-                c10::nullopt, &ex);
+  dsv_gemm_impl(a, b, a, true, kEpiPushRows, z, b2, tile_slots, lora_seg, c10::nullopt, 0, 0, 0, 0, max_ctas,
+                c10::nullopt, c10::nullopt, &ex);
 }
 
 // LoRA factor gradients, reducing over the token dimension (both operands
@@ -1735,7 +1736,7 @@ void dsv_gemm_push(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor
 //                        (dB of every projection of a group from a = dY, b = Z).
 // n_valid bounds the columns of b that are used (the rest may be padding).
 void dsv_gemm_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t kind, int64_t n_valid, int64_t R,
-                    int64_t b1, int64_t b2, bool interleave, double scale) {
+                    int64_t b1, int64_t b2, bool interleave, double scale, int64_t max_ctas) {
   using namespace dsv;
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_wgrad: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kFloat,
@@ -1764,6 +1765,7 @@ void dsv_gemm_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t
   args.bt_b2 = (int)b2;
   args.bt_interleave = interleave ? 1 : 0;
   args.bt_scale = (float)scale;
+  args.max_ctas = (int)max_ctas;
   const int bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), T, M, a.stride(0), BK);
   CUtensorMap tb = make_tmap_bf16(b.data_ptr(), T, b.size(1), b.stride(0), BK);
