@@ -332,7 +332,7 @@ class LoraTrainer:
         m.grads.zero_()
         n_valid = self.n_valid(lens)
         L = self.arch.num_layers
-        self.bwd.prepare(ci.n_pad, dev)
+        self.bwd.prepare(ci.n_pad, dev, max_rows=cap.layer_in.shape[1])
         gs = self._graph_set(cap, ci, n_valid) if dev.type == "cuda" else None
         if gs is not None:
             gs["labels"].copy_(ci.labels)

@@ -331,7 +331,8 @@ class LoraBackward:
         # The head's gradient pass takes the vocabulary slice in chunks of
         # this many columns (a bf16 [n, chunk] gradient block at a time).
         self.vocab_chunk = 16384
-        self._head_bufs: dict = {}
+        self.scratch_rows = 0          # rows of the cycle scratch (set by prepare)
+        self._head_bufs: dict | None = None
         self._head_out = None
         # Fused TP path (``parallel.peer.BwdPeerWorkspace``, set by the
         # engine): residual-gradient reductions over peer memory instead of
@@ -340,7 +341,7 @@ class LoraBackward:
         # ``_resid32`` (owned rows only).
         self.tpws = None
         self.resid_bf16 = None
-        self._r32: dict = {}
+        self._r32: list | None = None
         # Optional per-phase CUDA-event recorder (``engine.bwd_profile``):
         # ``mark(name)`` closes the phase that ends here on the current stream,
         # ``comm(name, ev0, ev1)`` brackets a collective on its side stream.
@@ -514,9 +515,11 @@ class LoraBackward:
                  z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas)
         return out
 
-    def prepare(self, n: int, device) -> None:
-        """Allocate the per-shape scratch of a cycle of ``n`` rows (called
-        before any CUDA-graph capture, so no scratch lives in a graph pool)."""
+    def prepare(self, n: int, device, max_rows: int = 0) -> None:
+        """Allocate the cycle scratch (once, for ``max_rows`` rows: the capture
+        buffer's size) before any CUDA-graph capture, so no scratch lives in a
+        graph pool and every shape's graphs see the same buffers."""
+        self.scratch_rows = max(self.scratch_rows, int(max_rows))
         if self.w.embed.is_cuda:
             self._head_scratch(n, device)
             if self.tpws is not None:
@@ -581,19 +584,27 @@ class LoraBackward:
         return [(c, min(V, c + self.vocab_chunk)) for c in range(0, V, self.vocab_chunk)]
 
     def _head_scratch(self, n: int, device) -> dict:
-        key = (n, str(device))
-        st = self._head_bufs.get(key)
-        if st is None:
+        """The head's scratch for ``n`` rows: views of buffers allocated once
+        for :attr:`scratch_rows` rows. Captured CUDA graphs keep the buffers'
+        addresses, so they are never reallocated while the trainer lives."""
+        if self._head_bufs is None or n > self._head_bufs["rows"]:
+            # (the trainer prepares the capture capacity before capturing any
+            # graph, so only callers without graphs ever grow the scratch)
+            rows = max(n, self.scratch_rows)
             V, D = self.w.lm_head.shape
             ch = min(V, self.vocab_chunk)
             world = self.comm.size if self.comm is not None else 1
             f32 = dict(dtype=torch.float32, device=device)
-            st = {"stats": torch.empty(n, 2 * (-(-V // 64)), **f32), "tgt": torch.empty(n, **f32),
-                  "part": torch.empty(n, 3, **f32), "parts": torch.empty(world, n, 3, **f32),
-                  "lse": torch.empty(n, **f32), "loss": torch.empty(n, **f32),
-                  "dlog": torch.empty(n, ch, dtype=self.cdt, device=device), "dh": torch.empty(n, D, **f32)}
-            self._head_bufs = {key: st}
-        return st
+            self._head_bufs = {"rows": rows, "world": world,
+                               "stats": torch.empty(rows, 2 * (-(-V // 64)), **f32), "tgt": torch.empty(rows, **f32),
+                               "part": torch.empty(rows, 3, **f32), "parts": torch.empty(world * rows * 3, **f32),
+                               "lse": torch.empty(rows, **f32), "loss": torch.empty(rows, **f32),
+                               "dlog": torch.empty(rows, ch, dtype=self.cdt, device=device),
+                               "dh": torch.empty(rows, D, **f32)}
+        b = self._head_bufs
+        return {"stats": b["stats"][:n], "tgt": b["tgt"][:n], "part": b["part"][:n],
+                "parts": b["parts"][:b["world"] * n * 3].view(b["world"], n, 3),
+                "lse": b["lse"][:n], "loss": b["loss"][:n], "dlog": b["dlog"][:n], "dh": b["dh"][:n]}
 
     def head_backward(self, final_in: torch.Tensor, labels: torch.Tensor,
                       n_valid: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -692,14 +703,12 @@ class LoraBackward:
 
     def _resid32(self, n: int, device) -> list[torch.Tensor]:
         """The fused TP path's two fp32 residual-gradient buffers [n, D]
-        (only this rank's owned rows are ever written or read)."""
-        key = (n, str(device))
-        r = self._r32.get(key)
-        if r is None:
-            D = self.arch.hidden
-            r = [torch.zeros(n, D, dtype=torch.float32, device=device) for _ in range(2)]
-            self._r32 = {key: r}
-        return r
+        (only this rank's owned rows are ever written or read): views of two
+        buffers allocated once for :attr:`scratch_rows` rows."""
+        if self._r32 is None or n > self._r32[0].shape[0]:
+            rows = max(n, self.scratch_rows)
+            self._r32 = [torch.zeros(rows, self.arch.hidden, dtype=torch.float32, device=device) for _ in range(2)]
+        return [t[:n] for t in self._r32]
 
     # ------------------------------------------------------------ recompute
     def _proj_lora(self, layer: int, g: str, X: torch.Tensor, W: torch.Tensor) -> torch.Tensor:

@@ -748,8 +748,8 @@ def test_push_reduce_norm_one_rank(M, K, D):
             exp = ref.rms_norm_bwd(x.float().cpu(), dy.cpu(), w.float().cpu(), 1e-5, add=add_norm.cpu()).to(DEV)
             # dy crosses the wire in bf16: a last-bit rounding difference of
             # the fp32 sum (tensor-core vs torch summation order) is allowed.
-            torch.testing.assert_close(out, exp, rtol=1e-2, atol=1e-2)
-            torch.testing.assert_close(got.float(), exp, rtol=1e-2, atol=1e-2)
+            torch.testing.assert_close(out, exp, rtol=2e-2, atol=3e-2)
+            torch.testing.assert_close(got.float(), exp, rtol=2e-2, atol=3e-2)
         assert ops.check_device_error() == 0
     finally:
         ws.close()

@@ -83,3 +83,55 @@ def test_gpu_training_reduces_loss():
     ad = random_adapter(arch, 16, seed=3, b_std=0.0)
     tr, res = run(arch, seqs, ad, "cuda", torch.bfloat16, steps=10, lr=2e-3)
     assert res[-1].loss < res[0].loss - 0.05, [r.loss for r in res]
+
+
+def test_graph_replay_after_a_shape_change_matches_eager():
+    """Cycles of two batch shapes alternate (A, B, A, B, A): shape A's graphs
+    are captured on its second cycle and replayed on the third, after shape B
+    ran in between; with lr = 0 the replayed cycle's gradients equal an eager
+    cycle's (the cycle scratch is shared by every shape's graphs, so a replay
+    never touches memory freed by another shape)."""
+    arch = PRESETS["qwen3-test"]
+    g = torch.Generator().manual_seed(9)
+    shapes = {"A": [torch.randint(0, arch.vocab, (n,), generator=g).tolist() for n in (130, 64, 200)],
+              "B": [torch.randint(0, arch.vocab, (n,), generator=g).tolist() for n in (300, 33)]}
+    ad = random_adapter(arch, 16, seed=4, b_std=0.02)
+    dev, dt = "cuda", torch.bfloat16
+    w = init_weights(arch, seed=5, device="cpu", dtype=torch.float32).to(dev, dt)
+    kv = KVCache(arch.num_layers, 64, arch.num_kv_heads, 64, 128, dev, dt)
+    served = LoraServeBuffers(arch, w.tp, slots=2, max_rank=16, device=dev, dtype=dt)
+    model = DecoderModel(w, kv.k, kv.v, served, None)
+    cap = CaptureBuffers.allocate(w, 512, dev, dt)
+    runner = ModelRunner(model, 64, dev, ft_slot=1)
+    sched = Scheduler(kv.allocator, 64, max_num_batched_tokens=8192, max_model_len=4096)
+
+    def trainer():
+        tr = LoraTrainer(w, served, 1, 16, 32, lr=0.0, mask_prefix=0, cos_sin_table=model.cos_sin)
+        tr.load_adapter(ad, 16, 32)
+        tr.publish()
+        return tr
+
+    def cycle(tr, name):
+        seqs = shapes[name]
+        out = SchedulerOutput()
+        reqs = [Request(f"{name}{i}", s, SamplingParams(max_tokens=1), is_ft=True) for i, s in enumerate(seqs)]
+        assert not sched.add_ft(out, reqs)
+        runner.execute(out, cap, 0)
+        sched.update(out, {})
+        lens = [len(s) for s in seqs]
+        starts = [sum(lens[:i]) for i in range(len(lens))]
+        return tr.run_cycle(cap, sum(lens), starts, lens)
+
+    tr = trainer()
+    for name in ("A", "B", "A", "B", "A"):
+        res = cycle(tr, name)
+    assert len(tr._graphs) == 2
+    graphed = tr.masters.export_peft(16, grads=True)
+    eager_tr = trainer()
+    eager_tr.use_graphs = False
+    res_e = cycle(eager_tr, "A")
+    eager = eager_tr.masters.export_peft(16, grads=True)
+    assert ops.check_device_error() == 0
+    assert abs(res.loss - res_e.loss) < 1e-4 * abs(res_e.loss)
+    for k, y in eager.items():
+        torch.testing.assert_close(graphed[k], y, rtol=1e-3, atol=1e-6)
