@@ -391,3 +391,45 @@ def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, s
                              int(max_ctas))
         return out
     return ref.gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))
+
+
+# ----------------------------------------------------------------- fused optimizer of the replicated factors
+
+def push_slices(g, lo, hi, ws):
+    """Send elements [lo, hi) of the replicated gradient block ``g`` to their
+    slice owners (``ws``: :class:`~..parallel.peer.OptPeerWorkspace`)."""
+    _native().push_slices(g, int(lo), int(hi), ws.slice, ws.rank, ws.world, ws.push_table)
+
+
+def fused_replicated_adamw(ws, params, grads, exp_avg, exp_avg_sq, seg_len, shard_sumsq, *, max_norm, lr, wd,
+                           step, b1=0.9, b2=0.999, eps=1e-8, coef=None, total=None, sq=None):
+    """Finish the replicated block's optimizer step once every rank pushed all
+    of its gradients: sum the owned slice, exchange per-layer sums of squares
+    (plus ``shard_sumsq``, this rank's unreplicated part), AdamW with
+    per-layer clipping on the owned slice, updated values to every rank, then
+    wait for the other owners' slices and copy them in. Returns the per-layer
+    squared norms (for the unreplicated part's own AdamW)."""
+    ext = _native(7)
+    L = ws.layers
+    ext.wait_counts(ws.cnt_push, 1, ws.world * ws.len, 0, 0, 0)
+    sq = sq if sq is not None else torch.zeros(L, dtype=torch.float32, device=params.device)
+    sq.zero_()
+    ext.reduce_slice_sumsq(ws.recv_addr, ws.world, ws.slice, ws.first, ws.len, seg_len, grads, sq)
+    ext.exchange_rows(sq, shard_sumsq, ws.rank, ws.world, ws.row_table)
+    ext.wait_counts(ws.cnt_rows, 1, ws.world, 0, 0, 0)
+    coef = coef if coef is not None else torch.empty(L, dtype=torch.float32, device=params.device)
+    total = total if total is not None else torch.empty(L, dtype=torch.float32, device=params.device)
+    ext.clip_coef(ws.rows, float(max_norm), coef, total)
+    ext.adamw_slice_bcast(params, grads, exp_avg, exp_avg_sq, ws.first, ws.len, seg_len, coef, lr, b1, b2, eps,
+                          wd, int(step), ws.rank, ws.world, ws.param_table)
+    return total
+
+
+def fused_replicated_finish(ws, params):
+    """Wait for the other owners' updated slices and copy them into ``params``."""
+    _native().wait_counts(ws.cnt_param, 1, ws.total - ws.len, 0, 0, 0)
+    if ws.first > 0:
+        params[:ws.first].copy_(ws.pstage[:ws.first])
+    end = ws.first + ws.len
+    if end < ws.total:
+        params[end:ws.total].copy_(ws.pstage[end:ws.total])

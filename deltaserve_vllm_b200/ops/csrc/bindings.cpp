@@ -33,6 +33,16 @@ void dsv_wait_counts(int64_t cnt, int64_t n, int64_t per_block, int64_t rows, in
 void dsv_reduce_norm_bcast(int64_t recv, int64_t rank, int64_t world, int64_t blocks_cap, int64_t ld, int64_t M,
                            int64_t D, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> w, double eps,
                            c10::optional<torch::Tensor> add, torch::Tensor out, torch::Tensor table);
+void dsv_push_slices(torch::Tensor g, int64_t lo, int64_t hi, int64_t slice, int64_t rank, int64_t world,
+                     torch::Tensor table);
+void dsv_reduce_slice_sumsq(int64_t recv, int64_t world, int64_t slice, int64_t first, int64_t len, int64_t seg_len,
+                            torch::Tensor g, torch::Tensor sq);
+void dsv_exchange_rows(torch::Tensor a, c10::optional<torch::Tensor> b, int64_t rank, int64_t world,
+                       torch::Tensor table);
+void dsv_clip_coef(torch::Tensor rows, double max_norm, torch::Tensor coef, torch::Tensor total);
+void dsv_adamw_slice_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, int64_t first,
+                           int64_t len, int64_t seg_len, torch::Tensor coef, double lr, double b1, double b2,
+                           double eps, double wd, int64_t step, int64_t rank, int64_t world, torch::Tensor table);
 void dsv_ce_merge(torch::Tensor stats, int64_t n_tiles, torch::Tensor tgt, torch::Tensor part);
 void dsv_ce_finalize(torch::Tensor parts, torch::Tensor labels, torch::Tensor lse, torch::Tensor loss);
 int64_t dsv_read_error_gemm(bool clear);
@@ -86,6 +96,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &dsv_gemm_wgrad, "LoRA factor-gradient GEMM over the token dimension");
   m.def("wait_counts", &dsv_wait_counts, "one-CTA bounded wait on this rank's arrival counters");
   m.def("reduce_norm_bcast", &dsv_reduce_norm_bcast, "owned-row reduce + RMSNorm backward + P2P all-gather");
+  m.def("push_slices", &dsv_push_slices, "push fp32 partials to their slice owners over peer memory");
+  m.def("reduce_slice_sumsq", &dsv_reduce_slice_sumsq, "sum an owned slice over the ranks + per-layer sum of squares");
+  m.def("exchange_rows", &dsv_exchange_rows, "write a small row into every rank's table");
+  m.def("clip_coef", &dsv_clip_coef, "per-layer clip coefficients from the ranks' sums of squares");
+  m.def("adamw_slice_bcast", &dsv_adamw_slice_bcast, "AdamW on an owned slice, updated values to every rank");
   m.def("ce_merge", &dsv_ce_merge, "merge per-tile softmax statistics of one vocabulary slice");
   m.def("ce_finalize", &dsv_ce_finalize, "log-sum-exp and loss over the ranks' vocabulary slices");
   m.def("peer_alloc", [](int64_t bytes) {
