@@ -1246,6 +1246,8 @@ class CoServingEngine:
         """Release GPU resources that hold communicator state. CUDA graphs with
         captured NCCL collectives must be destroyed before the process group,
         or its teardown waits forever. Safe to call on every rank."""
+        if self.router is not None:
+            self.router.stop()              # indexing thread and encoder processes
         if self.cuda:
             torch.cuda.synchronize(self.device)
         # A cycle cut short by shutdown is a suspended generator whose frame
