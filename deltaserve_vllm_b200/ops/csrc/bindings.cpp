@@ -48,12 +48,20 @@ void dsv_ce_finalize(torch::Tensor parts, torch::Tensor labels, torch::Tensor ls
 int64_t dsv_read_error_gemm(bool clear);
 int64_t dsv_read_error_attn_bwd(bool clear);
 int64_t dsv_read_error_tp_bwd(bool clear);
+int64_t dsv_read_error_attn_tc(bool clear);
+int64_t dsv_read_error_attn_bwd_tc(bool clear);
 static int64_t dsv_read_error(bool clear) {
-  const int64_t g = dsv_read_error_gemm(clear);
-  const int64_t a = dsv_read_error_attn_bwd(clear);
-  const int64_t t = dsv_read_error_tp_bwd(clear);
-  return g != 0 ? g : (a != 0 ? a : t);
+  const int64_t codes[5] = {dsv_read_error_gemm(clear), dsv_read_error_attn_bwd(clear), dsv_read_error_tp_bwd(clear),
+                            dsv_read_error_attn_tc(clear), dsv_read_error_attn_bwd_tc(clear)};
+  for (int64_t c : codes)
+    if (c != 0) return c;
+  return 0;
 }
+void dsv_attn_bwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor d_o,
+                     torch::Tensor tiles, torch::Tensor lse, torch::Tensor dd, c10::optional<torch::Tensor> dq,
+                     c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
+                     c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+                     c10::optional<torch::Tensor> dqkv, int64_t bf16_mask);
 void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
                   torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, c10::optional<torch::Tensor> dq,
                   c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
@@ -63,7 +71,13 @@ void dsv_attn_fwd_dense(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch
                         double scale);
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
-                       int64_t num_heads, double scale);
+                       int64_t num_heads, double scale, int64_t tile_rows);
+void dsv_paged_prefill_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                          torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
+                          int64_t num_heads, double scale);
+void dsv_attn_fwd_dense_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles, torch::Tensor out,
+                           int64_t num_heads, int64_t num_kv_heads, double scale, c10::optional<torch::Tensor> lse,
+                           c10::optional<torch::Tensor> d_o, c10::optional<torch::Tensor> dd);
 void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
                       int64_t num_heads, double scale, int64_t splits, int64_t keys_per_split);
@@ -113,7 +127,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_zero", &dsv_peer_zero, "zero a range of this rank's block");
   m.def("peer_view", &dsv_peer_view, "tensor over a range of a peer workspace block");
   m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
-  m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
+  m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill), warp-level MMA");
+  m.def("paged_prefill_tc", &dsv_paged_prefill_tc, "paged varlen causal attention (prefill), tcgen05 + TMA");
+  m.def("attn_bwd_tc", &dsv_attn_bwd_tc,
+        "varlen causal GQA attention backward, tcgen05 + TMA (dQ pass, then dK / dV pass)");
+  m.def("attn_fwd_dense_tc", &dsv_attn_fwd_dense_tc,
+        "varlen causal GQA attention forward on packed rows, tcgen05 + TMA (optional lse / rowsum(dO*O))");
   m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");
   m.def("attn_bwd", &dsv_attn_bwd, "varlen causal GQA attention backward (dQ, dK, dV)");
   m.def("attn_fwd_dense", &dsv_attn_fwd_dense, "varlen causal GQA attention forward on packed rows");

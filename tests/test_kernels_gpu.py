@@ -259,18 +259,37 @@ def _paged_setup(lens, qlens, Hq, Hkv, bs, seed=0):
         torch.tensor(lens, dtype=torch.int32, device=DEV), q
 
 
-@pytest.mark.parametrize("bs", [16, 64])
+@pytest.mark.parametrize("bs", [16, 64, 128, 256, 48])
 @pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4)])
 def test_paged_prefill(bs, Hq, Hkv):
-    lens = [1, 63, 64, 65, 200, 513]
-    qlens = [1, 63, 10, 65, 200, 100]
+    """Block sizes that tile 128 keys run the tcgen05 kernel, 48 the warp-level one."""
+    lens = [1, 63, 64, 65, 200, 513, 1100]
+    qlens = [1, 63, 10, 65, 200, 100, 700]
     kc, vc, bt, cu, ctx, q = _paged_setup(lens, qlens, Hq, Hkv, bs)
+    assert ops.prefill_uses_tc(bs) == (bs != 48)
     tiles = torch.tensor(ops.prefill_tiles(cu.tolist()), dtype=torch.int32, device=DEV)
     out = torch.zeros(q.shape[0], Hq * 128, dtype=torch.bfloat16, device=DEV)
     ops.paged_prefill(q, kc, vc, bt, cu, ctx, tiles, out, Hq, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
     exp = torch.zeros_like(out, dtype=torch.float32).cpu()
     ref.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), cu.cpu(), ctx.cpu(), exp, Hq, 1 / math.sqrt(128))
     torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+def test_paged_prefill_tc_matches_warp_kernel():
+    """Both prefill kernels on one batch (64-key pages): same outputs to bf16 rounding."""
+    lens, qlens = [300, 1024, 77], [300, 512, 77]
+    kc, vc, bt, cu, ctx, q = _paged_setup(lens, qlens, 32, 8, 64)
+    tiles = torch.tensor(ops.prefill_tiles(cu.tolist()), dtype=torch.int32, device=DEV)
+    a = torch.zeros(q.shape[0], 32 * 128, dtype=torch.bfloat16, device=DEV)
+    b = torch.zeros_like(a)
+    nat = ops._native()
+    nat.paged_prefill_tc(q, kc, vc, bt, cu, ctx, tiles, a, 32, 1 / math.sqrt(128))
+    nat.paged_prefill(q, kc, vc, bt, cu, ctx, tiles, b, 32, 1 / math.sqrt(128), ops.PREFILL_TILE)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    torch.testing.assert_close(a.float(), b.float(), rtol=1.6e-2, atol=1.6e-2)
 
 
 def _packed_qkv(lens, Hq, Hkv, seed, pad=8):
@@ -375,6 +394,31 @@ def test_attn_fwd_dense(Hq, Hkv):
     exp = torch.zeros(n, Hq * 128)
     ref.dense_attn_fwd(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), 1 / math.sqrt(128), exp)
     torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (32, 8)])
+def test_attn_fwd_dense_tc_with_stats(Hq, Hkv):
+    """tcgen05 dense forward: O, base-2 row log-sum-exp and rowsum(dO * O) against fp32."""
+    lens = [3, 64, 129, 500, 1000]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=35)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV, bm=128)
+    g = torch.Generator(device=DEV).manual_seed(36)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV)
+    out = torch.zeros(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+    lse = torch.zeros(Hq, n, device=DEV)
+    dd = torch.zeros(Hq, n, device=DEV)
+    scale = 1 / math.sqrt(128)
+    ops.attn_fwd_dense(q, k, v, None, scale, out, tiles128=tiles, lse=lse, d_o=d_o, dd=dd)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    exp = torch.zeros(n, Hq * 128)
+    else_, edd = torch.zeros(Hq, n), torch.zeros(Hq, n)
+    ref.dense_attn_fwd(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), scale, exp)
+    ref.dense_attn_stats(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), scale, else_, d_o.cpu(), edd)
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(lse.cpu(), else_, rtol=1e-3, atol=2e-3)
+    # dd sums 128 products of O (bf16-level error) and dO ~ N(0, 1)
+    torch.testing.assert_close(dd.cpu(), edd, rtol=2e-2, atol=5e-2)
 
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
