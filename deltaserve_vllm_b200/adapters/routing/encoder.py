@@ -88,6 +88,57 @@ class SentenceEncoder:
     def unload(self) -> None:
         self._tok = self._model = None
 
+    # ------------------------------------------------ sharing with a child process
+    def shared_state(self) -> tuple[dict, dict]:
+        """(model config, every parameter and buffer by name): what a child
+        process needs to run this encoder on the SAME tensors. Sent over a
+        ``torch.multiprocessing`` pipe, CUDA tensors travel as IPC handles
+        (the child maps this process's device memory) and CPU tensors move
+        to shared memory; the caller keeps this encoder loaded for as long as
+        the child uses them."""
+        self.load()
+        state = {n: p.detach() for n, p in self._model.named_parameters()}
+        state.update({n: b for n, b in self._model.named_buffers()})
+        return self._model.config.to_dict(), state
+
+    @classmethod
+    def from_shared(cls, path: str, prefix: str, max_tokens: int, device: str, config: dict,
+                    state: dict) -> "SentenceEncoder":
+        """An encoder whose module is built around ``state``'s tensors (from
+        :meth:`shared_state` of another process): the architecture comes from
+        ``config`` on the meta device, so no weight is allocated or read here;
+        the tokenizer is read from ``path``."""
+        import torch
+        from transformers import AutoConfig, AutoModel, AutoTokenizer
+        enc = cls(path, prefix, max_tokens, device)
+        enc._tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+        with torch.device("meta"):
+            model = AutoModel.from_config(AutoConfig.for_model(**config))
+        named = dict(model.named_parameters())
+        named.update(dict(model.named_buffers()))
+        missing = sorted(set(named) - set(state))
+        if missing:
+            raise RuntimeError(f"shared encoder state lacks {missing[:4]}")
+        for name, t in state.items():
+            owner, _, leaf = name.rpartition(".")
+            mod = model.get_submodule(owner) if owner else model
+            if leaf in mod._parameters:
+                mod._parameters[leaf] = torch.nn.Parameter(t, requires_grad=False)
+            elif leaf in mod._buffers:
+                mod._buffers[leaf] = t
+        enc._model = model.eval()
+        return enc
+
+    def layers(self):
+        """The encoder's layer stack (its longest ``ModuleList``), or []."""
+        import torch
+        self.load()
+        best = []
+        for m in self._model.modules():
+            if isinstance(m, torch.nn.ModuleList) and len(m) > len(best):
+                best = m
+        return list(best)
+
     def encode(self, texts: list[str], batch_size: int = 16) -> np.ndarray:
         import torch
         self.load()

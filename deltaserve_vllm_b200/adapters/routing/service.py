@@ -25,7 +25,7 @@ from ... import dprint
 from .. import peft_io
 from .encoder import SentenceEncoder, encoder_identity, make_encoder
 from .index import CentroidIndex
-from .indexing import index_dir, start_indexing, store_centroid
+from .indexing import index_dir, make_indexing_service, prepare_indexing, store_centroid
 from .pool import GPU, AdapterPool
 from .router import NO_TEXT, RouteDecision, Router
 
@@ -62,9 +62,12 @@ class AdapterRouter:
         self.eng, self.cfg = engine, cfg
         dev = str(engine.device) if getattr(engine, "cuda", False) else "cpu"
         self.encoder = make_encoder(cfg, dev)
-        # Indexing runs on a host thread; an HF encoder gets its own CPU copy.
+        # Indexing encodes in processes of its own (started with the first
+        # job): a CPU copy of the encoder, and a GPU process on the route
+        # encoder's own weights while the engine is idle.
         self.index_encoder = (make_encoder(cfg, "cpu") if isinstance(self.encoder, SentenceEncoder)
                               else self.encoder)
+        self.indexer_service = None
         self.enc_id = encoder_identity(self.encoder)
         self.dir = index_dir(cfg)
         used = set(engine.adapter_slots.values())
@@ -85,7 +88,8 @@ class AdapterRouter:
         self.pool.listeners.append(lambda p: self.router.set_index(p.index))
         self.pending: deque = deque()   # (rid, ids, params, text, adapter, arrival, future)
         self.held: deque = deque()      # (rid, ids, params, adapter, arrival)
-        self.indexing: dict[str, tuple] = {}     # name -> (runner, path, fingerprint)
+        self.indexing: dict[str, tuple] = {}     # name -> (job, path, fingerprint)
+        engine.request_listeners.append(self._on_request)
         self.stats = {"routed": 0, "fallback": 0, "held": 0, "encode_calls": 0, "encode_ms": 0.0}
         for a in cfg.adapters or []:
             self.add(a.get("name") or os.path.basename(os.path.normpath(a["path"])), a["path"],
@@ -112,21 +116,38 @@ class AdapterRouter:
         return {"name": name, "level": self.pool.entries[name].level, "indexed": False}
 
     def start_indexing(self, name: str, path: str, data_path: str) -> dict:
-        runner, hit, fp = start_indexing(self.cfg, self.index_encoder, self.enc_id, name, data_path,
-                                         busy=self.eng.has_unfinished)
+        job, hit = self.index_job(name, data_path)
         if hit is not None:
             return self.pool.admit(name, path, hit[0], hit[1], load=True)
-        self.indexing[name] = (runner, path, fp)
-        return {"name": name, "indexing": runner.describe()}
+        self.indexing[name] = (job, path, job.fp)
+        return {"name": name, "indexing": job.describe()}
+
+    def index_job(self, name: str, data_path: str):
+        """(indexing job, None) or (None, cached (centroid, refs)); the job
+        carries its fingerprint as ``job.fp``."""
+        ix, hit, fp = prepare_indexing(self.cfg, self.enc_id, name, data_path)
+        if hit is not None:
+            return None, hit
+        if self.indexer_service is None:
+            self.indexer_service = make_indexing_service(self.cfg, self.index_encoder, self.encoder)
+            if self.eng.has_unfinished():
+                self.indexer_service.placement.note_inference()
+        job = self.indexer_service.submit(name, ix)
+        job.fp = fp
+        return job, None
+
+    def _on_request(self, what: str, _req) -> None:
+        if what == "add" and self.indexer_service is not None:
+            self.indexer_service.placement.note_inference()
 
     def _poll_indexing(self) -> None:
-        for name, (runner, path, fp) in list(self.indexing.items()):
-            if runner.error:
-                dprint(f"[indexing] {name} failed: {runner.error}")
+        for name, (job, path, fp) in list(self.indexing.items()):
+            if job.error:
+                dprint(f"[indexing] {name} failed: {job.error}")
                 del self.indexing[name]
-            elif runner.done:
+            elif job.done:
                 del self.indexing[name]
-                c, r = runner.indexer.centroid(), runner.indexer.references()
+                c, r = job.indexer.centroid(), job.indexer.references()
                 store_centroid(self.dir, name, fp, c, r, self.enc_id, self.cfg.encoder_query_prefix,
                                self.cfg.encoder_max_tokens)
                 if name in self.pool:
@@ -146,6 +167,8 @@ class AdapterRouter:
         a request naming a pool adapter. The future resolves with the
         :class:`RouteDecision` at the next encode step."""
         fut: cf.Future = cf.Future()
+        if self.indexer_service is not None:
+            self.indexer_service.placement.note_inference()
         self.pending.append((rid, list(ids), params, text, adapter,
                              arrival if arrival is not None else time.perf_counter(), fut))
         self.eng.arrival_flag = True
@@ -174,6 +197,8 @@ class AdapterRouter:
 
     def tick(self) -> None:
         """The encode step plus slot placement; runs on the engine thread."""
+        if self.indexer_service is not None and (self.pending or self.held or self.eng.scheduler.has_unfinished()):
+            self.indexer_service.placement.note_inference()
         if self.indexing:
             self._poll_indexing()
         if self.pending:
@@ -217,11 +242,15 @@ class AdapterRouter:
     def status(self) -> dict:
         return {"pool": self.pool.status(), "model": self.router.model.describe(),
                 "pending": len(self.pending), "held": len(self.held), "stats": dict(self.stats),
-                "indexing": {n: r.describe() for n, (r, _, _) in self.indexing.items()}}
+                "indexing": {n: j.describe() for n, (j, _, _) in self.indexing.items()},
+                "indexer": self.indexer_service.describe() if self.indexer_service is not None else None}
 
     def stop(self) -> None:
-        for runner, _, _ in self.indexing.values():
-            runner.stop()
+        for job, _, _ in self.indexing.values():
+            job.stop()
+        if self.indexer_service is not None:
+            self.indexer_service.stop()
+            self.indexer_service = None
 
 
 NO_TEXT_DECISION = RouteDecision(None, None, NO_TEXT)

@@ -31,22 +31,20 @@ class IndexingStage(Stage):
             raise RuntimeError("adapter routing is not running")
         if not job.spec.data_path:
             raise RuntimeError("the job has no dataset to index")
-        from .indexing import start_indexing
-        runner, hit, fp = start_indexing(router.cfg, router.index_encoder, router.enc_id, job.spec.name,
-                                         job.spec.data_path, busy=ctx.has_unfinished)
-        job.data["indexing"] = (router, runner, hit, fp)
+        ijob, hit = router.index_job(job.spec.name, job.spec.data_path)
+        job.data["indexing"] = (router, ijob, hit)
 
     def poll(self, job, ctx) -> bool:
-        router, runner, hit, fp = job.data["indexing"]
+        router, ijob, hit = job.data["indexing"]
         if hit is not None:
             job.data["centroid"] = hit
             return True
-        if runner.error:
-            raise RuntimeError(runner.error)
-        if not runner.done:
+        if ijob.error:
+            raise RuntimeError(ijob.error)
+        if not ijob.done:
             return False
-        c, r = runner.indexer.centroid(), runner.indexer.references()
-        store_centroid(router.dir, job.spec.name, fp, c, r, router.enc_id,
+        c, r = ijob.indexer.centroid(), ijob.indexer.references()
+        store_centroid(router.dir, job.spec.name, ijob.fp, c, r, router.enc_id,
                        router.cfg.encoder_query_prefix, router.cfg.encoder_max_tokens)
         job.data["centroid"] = (c, r)
         return True

@@ -202,6 +202,7 @@ class AdapterRoutingConfig:
     indexing_cpu_max_threads: int = 8
     indexing_cpu_busy_threads: int = 2
     indexing_cpus: str | None = None
+    indexing_process: bool = True
     indexing_on_gpu: bool = True
     indexing_gpu_chunk_samples: int = 8
     indexing_gpu_after_quiet_s: float = 3.0
@@ -216,11 +217,11 @@ class AdapterRoutingConfig:
         for name in ("encoder_max_tokens", "max_active_adapters",
                      "route_encode_max_tokens", "indexing_max_samples",
                      "indexing_chunk_samples", "indexing_cpu_max_threads",
-                     "indexing_cpu_busy_threads", "indexing_gpu_chunk_samples",
+                     "indexing_gpu_chunk_samples",
                      "route_min_pool"):
             if int(getattr(self, name)) < 1:
                 raise ValueError(f"adapter_routing.{name} must be >= 1")
-        for name in ("indexing_gpu_after_quiet_s", "pool_protected_slots",
+        for name in ("indexing_gpu_after_quiet_s", "pool_protected_slots", "indexing_cpu_busy_threads",
                      "pool_hit_half_life_s", "route_close_band",
                      "route_confidence_slack", "retire_grace_s",
                      "route_reference_samples"):

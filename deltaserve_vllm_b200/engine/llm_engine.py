@@ -184,12 +184,18 @@ class CoServingEngine:
             self._init_finetuning(ft_adapter)
         # ---- the backward's residual-gradient reductions over peer memory
         self.bwd_ws = None
+        self.opt_ws = None
         if (self.cuda and comm is not None and comm.size > 1 and ecfg.tp_comm == "fused"
                 and self.trainer is not None and self.capture is not None):
             from ..parallel.peer import BwdPeerWorkspace
             self.bwd_ws = BwdPeerWorkspace(comm, cap_tokens + 8, self.arch.hidden)
             if self._self_test_bwd(comm):
                 self.trainer.bwd.tpws = self.bwd_ws
+                # ... and the replicated factors' optimizer over peer memory
+                from ..parallel.peer import OptPeerWorkspace
+                m = self.trainer.masters
+                self.opt_ws = OptPeerWorkspace(comm, m.rep_total, self.arch.num_layers)
+                self.trainer.optws = self.opt_ws
             else:
                 self.bwd_ws.close()
                 self.bwd_ws = None
@@ -1240,6 +1246,8 @@ class CoServingEngine:
         """Release GPU resources that hold communicator state. CUDA graphs with
         captured NCCL collectives must be destroyed before the process group,
         or its teardown waits forever. Safe to call on every rank."""
+        if self.router is not None:
+            self.router.stop()              # indexing thread and encoder processes
         if self.cuda:
             torch.cuda.synchronize(self.device)
         # A cycle cut short by shutdown is a suspended generator whose frame
@@ -1266,6 +1274,11 @@ class CoServingEngine:
                 self.trainer.bwd.tpws = None
             self.bwd_ws.close()
             self.bwd_ws = None
+        if self.opt_ws is not None:
+            if self.trainer is not None:
+                self.trainer.optws = None
+            self.opt_ws.close()
+            self.opt_ws = None
         if self.plan_chan is not None:
             self.plan_chan.close()
             self.plan_chan = None

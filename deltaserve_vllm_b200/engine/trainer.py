@@ -5,12 +5,14 @@ One backward *cycle* trains on the activations of one filled capture buffer:
 1. head backward (final norm + vocabulary-parallel LM head + cross-entropy,
    statistics then gradient per vocabulary chunk, no logits stored);
 2. layers L-1 .. 0: hand-written layer backward (``models/lora_backward.py``);
-   under TP the replicated factor gradients of every 8 layers are summed with
-   one all-reduce of a contiguous slab (the reference buckets the same way,
-   ``bwd_services/common/tp.py:186-236``), issued from a side stream while the
-   next layer's backward runs;
-3. per-layer gradient clipping to norm 1.0 (rank-symmetric under TP), AdamW on
-   the flat fp32 masters (two launches), StepLR decay per epoch;
+   under TP the replicated factor gradients of every 8 layers (a contiguous
+   slab; the reference buckets the same way, ``bwd_services/common/tp.py:186-236``)
+   are pushed to their slice owners over peer memory while the next layer's
+   backward runs (or, on the NCCL path, all-reduced from a side stream);
+3. per-layer gradient clipping to norm 1.0 (rank-symmetric under TP) and
+   AdamW on the flat fp32 masters; on the fused path each owner sums, clips
+   and updates its slice of the replicated factors and sends the new values
+   to every rank (``ops.fused_replicated_adamw``); StepLR decay per epoch;
 4. publish: bf16 ``A`` and ``B * alpha/r`` written straight into the served
    LoRA slot (``ops.lora_publish``), so inference uses the new weights from the
    next step.
@@ -97,6 +99,11 @@ class LoraTrainer:
         self._seen_shapes: set = set()
         self._sq_rep = torch.zeros(L, dtype=torch.float32, device=dev)
         self._sq_shard = torch.zeros(L, dtype=torch.float32, device=dev)
+        # Fused optimizer of the TP-replicated factors over peer memory
+        # (``parallel.peer.OptPeerWorkspace``, set by the engine).
+        self.optws = None
+        self._opt_coef = torch.zeros(L, dtype=torch.float32, device=dev)
+        self._opt_total = torch.zeros(L, dtype=torch.float32, device=dev)
         # DSERVE_TP_DIAG=N: for the first N cycles, recompute every captured
         # activation from the layer input and log its largest deviation from
         # the captured copy (forward capture vs backward recompute; the
@@ -192,15 +199,23 @@ class LoraTrainer:
         h = None
         if tp and (l + 1) % BUCKET_LAYERS == 0 and l + 1 < L:
             # Layers [l + 1, l + 1 + BUCKET_LAYERS) finished with the previous
-            # step: one all-reduce of their replicated factor gradients, which
+            # step: their replicated factor gradients go to their slice owners
+            # (fused optimizer) or into one all-reduce on a side stream, which
             # overlaps this layer's backward (it writes only layer l's).
-            h = self.bwd.reduce_begin(m.rep_block(m.grads, l + 1, min(L, l + 1 + BUCKET_LAYERS)))
+            if self.optws is not None:
+                ops.push_slices(m.rep_block(m.grads), (l + 1) * m.rep_per_layer,
+                                min(L, l + 1 + BUCKET_LAYERS) * m.rep_per_layer, self.optws)
+            else:
+                h = self.bwd.reduce_begin(m.rep_block(m.grads, l + 1, min(L, l + 1 + BUCKET_LAYERS)))
         # The first layer's input gradient feeds nothing that is trained.
         dh = self.bwd.layer_backward(l, dh, saved, ci, pos, self.cos_sin, need_input_grad=l > 0)
         self.bwd.reduce_end(h, dh.device)
         self.bwd._mark("wait_bucket")
         if tp and l == 0:
-            self.comm.all_reduce(m.rep_block(m.grads, 0, min(L, BUCKET_LAYERS)))
+            if self.optws is not None:
+                ops.push_slices(m.rep_block(m.grads), 0, min(L, BUCKET_LAYERS) * m.rep_per_layer, self.optws)
+            else:
+                self.comm.all_reduce(m.rep_block(m.grads, 0, min(L, BUCKET_LAYERS)))
             self.bwd._mark("bucket_allreduce_last")
         return dh
 
@@ -425,6 +440,22 @@ class LoraTrainer:
             self.epoch = epoch
         lr = self.lr * (self.gamma ** self.epoch)
         self.step += 1
+        if self.optws is not None:
+            # Fused path: the replicated block's slices were pushed to their
+            # owners during the backward; each owner sums its slice, the
+            # ranks swap per-layer squared norms (replicated slice + own
+            # shard), the owner runs AdamW on its slice and sends the new
+            # values to every rank; the shard runs AdamW locally.
+            ops.seg_sumsq(m.shard_block(m.grads), m.shard_per_layer, self._sq_shard)
+            total = ops.fused_replicated_adamw(
+                self.optws, m.rep_block(m.params), m.rep_block(m.grads), m.rep_block(m.exp_avg),
+                m.rep_block(m.exp_avg_sq), m.rep_per_layer, self._sq_shard, max_norm=CLIP_NORM, lr=lr, wd=self.wd,
+                step=self.step, coef=self._opt_coef, total=self._opt_total, sq=self._sq_rep)
+            ops.adamw(m.shard_block(m.params), m.shard_block(m.grads), m.shard_block(m.exp_avg),
+                      m.shard_block(m.exp_avg_sq), seg_len=m.shard_per_layer, seg_sumsq_t=total,
+                      max_norm=CLIP_NORM, grad_scale=1.0, lr=lr, wd=self.wd, step=self.step)
+            ops.fused_replicated_finish(self.optws, m.rep_block(m.params))
+            return
         ops.seg_sumsq(m.rep_block(m.grads), m.rep_per_layer, self._sq_rep)
         ops.seg_sumsq(m.shard_block(m.grads), m.shard_per_layer, self._sq_shard)
         if self.comm is not None and self.comm.size > 1:

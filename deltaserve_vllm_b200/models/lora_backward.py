@@ -176,9 +176,11 @@ class CycleInputs:
 
 class AttnGroups(list):
     """Samples of equal length as (length, count, row index) groups, for the
-    batched fp32 path, plus ``tiles``: the 64-row tile table of the fused
-    attention kernels (built here, outside any CUDA-graph capture)."""
+    batched fp32 path, plus the tile tables of the fused attention kernels
+    (built here, outside any CUDA-graph capture): ``tiles`` (64-row, the
+    warp-level kernels) and ``tiles128`` (the tcgen05 kernels)."""
     tiles: torch.Tensor | None = None
+    tiles128: torch.Tensor | None = None
 
 
 def attention_groups(starts, lens, device) -> AttnGroups:
@@ -191,6 +193,7 @@ def attention_groups(starts, lens, device) -> AttnGroups:
                + torch.arange(ln, device=device)[None, :]).reshape(-1)
         out.append((ln, len(sts), idx))
     out.tiles = ops.dense_attn_tiles(starts, lens, device)
+    out.tiles128 = ops.dense_attn_tiles(starts, lens, device, bm=128)
     return out
 
 
@@ -332,6 +335,7 @@ class LoraBackward:
         # this many columns (a bf16 [n, chunk] gradient block at a time).
         self.vocab_chunk = 16384
         self.scratch_rows = 0          # rows of the cycle scratch (set by prepare)
+        self._astats = None            # tcgen05 attention (lse, dd) scratch
         self._head_bufs: dict | None = None
         self._head_out = None
         # Fused TP path (``parallel.peer.BwdPeerWorkspace``, set by the
@@ -478,7 +482,8 @@ class LoraBackward:
         return zp
 
     def dx_gemm(self, layer: int, g: str, dY: torch.Tensor, W: torch.Tensor, dZ: torch.Tensor,
-                swiglu_gu: torch.Tensor | None = None, act_out: torch.Tensor | None = None) -> torch.Tensor:
+                swiglu_gu: torch.Tensor | None = None, act_out: torch.Tensor | None = None,
+                bf16_out: bool = False) -> torch.Tensor:
         """dX = dY . W + dZ . A in ONE GEMM: the rank-R adapter term rides as
         one extra 64-deep K block (dZ and A zero-padded to 64) instead of a
         second pass over the fp32 dX.
@@ -510,9 +515,10 @@ class LoraBackward:
                      epi=EPI_SWIGLU_BWD, z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas,
                      aux=swiglu_gu, aux_out=act_out)
             return out
-        out = torch.empty(n, W.shape[1], dtype=torch.float32, device=dY.device)
-        ops.gemm(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), out, b_mn=True, epi=EPI_F32,
-                 z=zp, b2=ap, tile_slots=ts, lora_seg=seg, max_ctas=self.max_ctas)
+        out = torch.empty(n, W.shape[1], dtype=torch.bfloat16 if bf16_out else torch.float32, device=dY.device)
+        ops.gemm(_bf(dY, self.cdt).contiguous(), _bf(W, self.cdt).contiguous(), out, b_mn=True,
+                 epi=EPI_BF16 if bf16_out else EPI_F32, z=zp, b2=ap, tile_slots=ts, lora_seg=seg,
+                 max_ctas=self.max_ctas)
         return out
 
     def prepare(self, n: int, device, max_rows: int = 0) -> None:
@@ -522,6 +528,8 @@ class LoraBackward:
         self.scratch_rows = max(self.scratch_rows, int(max_rows))
         if self.w.embed.is_cuda:
             self._head_scratch(n, device)
+            if ops.ATTN_TC:
+                self.attn_stats(n, device)
             if self.tpws is not None:
                 self._resid32(n, device)
 
@@ -710,6 +718,17 @@ class LoraBackward:
             self._r32 = [torch.zeros(rows, self.arch.hidden, dtype=torch.float32, device=device) for _ in range(2)]
         return [t[:n] for t in self._r32]
 
+    def attn_stats(self, n: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """(lse, dd) fp32 [Hq, rows] scratch of the tcgen05 attention: the
+        forward's row log-sum-exp and the backward's rowsum(dO * O), indexed
+        by packed row (allocated once for :attr:`scratch_rows` rows, so every
+        captured graph sees the same buffers)."""
+        if self._astats is None or n > self._astats[0].shape[1]:
+            rows = max(n, self.scratch_rows)
+            self._astats = (torch.zeros(self.hq, rows, dtype=torch.float32, device=device),
+                            torch.zeros(self.hq, rows, dtype=torch.float32, device=device))
+        return self._astats
+
     # ------------------------------------------------------------ recompute
     def _proj_lora(self, layer: int, g: str, X: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
         """fp32 ``X @ W^T`` plus the trained adapter's term for group ``g``
@@ -725,11 +744,17 @@ class LoraBackward:
         ops.rms_norm(layer_in, lw.in_ln, x1, self.arch.rms_eps)
         return self._proj_lora(layer, "qkv", x1, lw.qkv).to(layer_in.dtype)
 
-    def recompute_ctx(self, layer: int, qkv_raw: torch.Tensor, ci, positions, cos_sin) -> torch.Tensor:
+    def recompute_ctx(self, layer: int, qkv_raw: torch.Tensor, ci, positions, cos_sin,
+                      lse: torch.Tensor | None = None) -> torch.Tensor:
+        """The attention output of the layer; with ``lse`` (and the tcgen05
+        kernels) also its base-2 row log-sum-exp, which the attention
+        backward then reuses instead of recomputing the forward."""
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, self.w.layers[layer], cos_sin)
         if qh.is_cuda:
             out = torch.zeros(qh.shape[0], self.hq * self.hd, dtype=qkv_raw.dtype, device=qh.device)
-            return ops.attn_fwd_dense(qh, kh, vh, self._tiles(ci), self.scale, out)
+            t128 = self._tiles128(ci) if ops.ATTN_TC else None
+            return ops.attn_fwd_dense(qh, kh, vh, self._tiles(ci), self.scale, out, tiles128=t128,
+                                      lse=lse if t128 is not None else None)
         o = attn_forward(qh, kh, vh, ci.starts, ci.lens, self.scale, ci.attn_groups)
         return o.reshape(qh.shape[0], -1).to(qkv_raw.dtype)
 
@@ -738,6 +763,12 @@ class LoraBackward:
         if g is None or getattr(g, "tiles", None) is None:
             return ops.dense_attn_tiles(ci.starts, ci.lens, self.w.embed.device)
         return g.tiles
+
+    def _tiles128(self, ci) -> torch.Tensor:
+        g = ci.attn_groups
+        if g is None or getattr(g, "tiles128", None) is None:
+            return ops.dense_attn_tiles(ci.starts, ci.lens, self.w.embed.device, bm=128)
+        return g.tiles128
 
     def recompute_resid_mid(self, layer: int, layer_in: torch.Tensor, ctx: torch.Tensor) -> torch.Tensor:
         o = self._proj_lora(layer, "o", ctx, self.w.layers[layer].o)
@@ -829,7 +860,8 @@ class LoraBackward:
             self._mark("norm_bwd_mid")
         # ---- attention ---------------------------------------------------
         dz_o = self.group_dz(layer, "o", d_mid_c)
-        d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o)      # [n, q_l]
+        tc_attn = ops.ATTN_TC and x.is_cuda
+        d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o, bf16_out=tc_attn)      # [n, q_l]
         self._mark("o_dx")
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)
         ql, kl = self.hq * self.hd, self.hkv * self.hd
@@ -840,8 +872,15 @@ class LoraBackward:
             # norm backward). Rows past the samples carry no gradient.
             d_qkv[ci.n:].zero_()
             mask = 4 if self.arch.qk_norm else 7
-            dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale, rope=(ci.cos, ci.sin),
-                                      dqkv=d_qkv, bf16_mask=mask)
+            if tc_attn:
+                lse, dd = self.attn_stats(n, dev)
+                have_lse = saved.get("lse") is not None
+                dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale, rope=(ci.cos, ci.sin),
+                                          dqkv=d_qkv, bf16_mask=mask, o=ctx if have_lse else None,
+                                          lse=lse if have_lse else None, tiles128=self._tiles128(ci), dd=dd)
+            else:
+                dq, dk, dv = ops.attn_bwd(qh, kh, vh, d_ctx, self._tiles(ci), self.scale, rope=(ci.cos, ci.sin),
+                                          dqkv=d_qkv, bf16_mask=mask)
         else:
             dq, dk, dv = attn_backward(qh, kh, vh, d_ctx.view(n, self.hq, self.hd), ci.starts, ci.lens,
                                        self.scale, ci.attn_groups)

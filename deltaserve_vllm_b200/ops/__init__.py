@@ -126,21 +126,40 @@ def qk_norm_rope_cache(qkv, positions, cos_sin, q_norm, k_norm, eps, num_heads, 
 
 # ----------------------------------------------------------------- attention
 
-def prefill_tiles(cu_q: list[int], bm: int = 64) -> list[tuple[int, int]]:
-    """(sequence, first query) of every 64-query tile of a varlen batch."""
+PREFILL_TILE = 128      # queries per prefill tile (the tcgen05 kernel's M)
+ATTN_TC = os.environ.get("DSV_ATTN_TC", "1") != "0"
+
+
+def prefill_tiles(cu_q: list[int], bm: int = PREFILL_TILE) -> list[tuple[int, int]]:
+    """(sequence, first query) of every ``bm``-query tile of a varlen batch,
+    later queries first: under the causal mask they see the most keys, so
+    the longest CTAs start first."""
     out = []
     for s in range(len(cu_q) - 1):
         n = cu_q[s + 1] - cu_q[s]
         for q0 in range(0, n, bm):
             out.append((s, q0))
+    out.sort(key=lambda t: -t[1])
     return out
+
+
+def prefill_uses_tc(block_size: int) -> bool:
+    """The tcgen05 prefill kernel loads 128-key tiles as whole page boxes:
+    the page size must divide 128 or be a multiple of it."""
+    return ATTN_TC and (128 % block_size == 0 or block_size % 128 == 0) and block_size % 8 == 0
 
 
 def paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, out, num_heads,
                   scale):
+    """Causal varlen attention of the new queries over their paged context;
+    ``tile_info`` from :func:`prefill_tiles` (128-query tiles)."""
     if q.is_cuda:
-        _native().paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, out,
-                                num_heads, scale)
+        if prefill_uses_tc(k_cache.shape[2]):
+            _native().paged_prefill_tc(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info,
+                                       out, num_heads, scale)
+        else:
+            _native().paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, tile_info, out,
+                                    num_heads, scale, PREFILL_TILE)
         return out
     return ref.paged_prefill(q, k_cache, v_cache, block_tables, cu_q, ctx_lens, out, num_heads, scale)
 
@@ -174,18 +193,25 @@ def dense_attn_tiles(starts, lens, device, bm: int = 64) -> torch.Tensor:
     return torch.tensor(rows, dtype=torch.int32).reshape(-1, 3).to(device)
 
 
-def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0):
+def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0, o=None, lse=None,
+             tiles128=None, dd=None):
     """Gradients of causal varlen GQA attention over packed samples.
 
     ``q`` [n, Hq, 128] / ``k``, ``v`` [n, Hkv, 128] (bf16 on CUDA; row strides
-    free, heads adjacent), ``d_o`` fp32 [n, Hq * 128], ``tiles`` from
+    free, heads adjacent), ``d_o`` [n, Hq * 128], ``tiles`` from
     :func:`dense_attn_tiles`. ``rope = (cos, sin)`` ([n, 64] fp32) rotates dq
     and dk back through RoPE (gradients w.r.t. the pre-RoPE q / k). Bits of
     ``bf16_mask`` (1: dq, 2: dk, 4: dv) store those gradients as bf16 into the
     fused ``dqkv`` [n, (Hq + 2 Hkv) * 128] (q, k, v column blocks) instead of
     returning them. Returns (dq, dk, dv): fp32 [n, H, 128], or None for the
     ones written into ``dqkv``; rows outside every sample are zero in the fp32
-    outputs and untouched in ``dqkv``."""
+    outputs and untouched in ``dqkv``.
+
+    With ``tiles128`` (128-row tiles) the tcgen05 kernels run on CUDA. They
+    take the forward output ``o`` [n, Hq*128] bf16 and its base-2 row
+    log-sum-exp ``lse`` [Hq, >= n] (from :func:`attn_fwd_dense`); without
+    them the tcgen05 forward recomputes both first. ``dd`` is optional
+    scratch shaped like ``lse``."""
     n, hq, hd = q.shape
     hkv = k.shape[1]
     dev = q.device
@@ -193,12 +219,25 @@ def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0):
         raise ValueError("attn_bwd: bf16_mask needs dqkv")
     outs = [None if bf16_mask & (1 << i) else torch.zeros(n, h, hd, dtype=torch.float32, device=dev)
             for i, h in enumerate((hq, hkv, hkv))]
+    cos, sin = rope if rope is not None else (None, None)
+    if q.is_cuda and ATTN_TC and tiles128 is not None:
+        g = d_o.reshape(n, hq * hd)
+        if g.dtype != torch.bfloat16:
+            g = g.to(torch.bfloat16)
+        if o is None or lse is None:
+            o = torch.empty(n, hq * hd, dtype=torch.bfloat16, device=dev)
+            lse = torch.empty(hq, n, dtype=torch.float32, device=dev)
+            _native().attn_fwd_dense_tc(q, k, v, tiles128, o, hq, hkv, scale, lse, None, None)
+        if dd is None:
+            dd = torch.empty_like(lse)
+        _native(2).attn_bwd_tc(q, k, v, o, g, tiles128, lse, dd, outs[0], outs[1], outs[2], scale, cos, sin,
+                               dqkv, bf16_mask)
+        return tuple(outs)
     if q.is_cuda:
         lse = torch.empty(hq, n, dtype=torch.float32, device=dev)
         dd = torch.empty(hq, n, dtype=torch.float32, device=dev)
         do_bf = torch.empty(n, hq * hd, dtype=torch.bfloat16, device=dev)
-        cos, sin = rope if rope is not None else (None, None)
-        _native(2).attn_bwd(q, k, v, d_o.reshape(n, hq * hd), tiles, lse, dd, do_bf, outs[0], outs[1],
+        _native(2).attn_bwd(q, k, v, d_o.reshape(n, hq * hd).float(), tiles, lse, dd, do_bf, outs[0], outs[1],
                             outs[2], scale, cos, sin, dqkv, bf16_mask)
         return tuple(outs)
     full = [torch.zeros(n, h, hd, dtype=torch.float32) for h in (hq, hkv, hkv)]
@@ -218,13 +257,24 @@ def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0):
     return tuple(outs)
 
 
-def attn_fwd_dense(q, k, v, tiles, scale, out):
+def attn_fwd_dense(q, k, v, tiles, scale, out, tiles128=None, lse=None, d_o=None, dd=None):
     """Causal varlen GQA attention over packed samples into ``out`` [n, >= Hq*128]
-    (bf16 on CUDA); rows outside every sample are left untouched."""
+    (bf16 on CUDA); rows outside every sample are left untouched.
+
+    With ``tiles128`` (:func:`dense_attn_tiles` with ``bm=128``) the tcgen05
+    kernel runs, and can also write the base-2 row log-sum-exp into ``lse``
+    and rowsum(dO * O) into ``dd`` (fp32 [Hq, >= n]; ``d_o`` fp32 [n, Hq*128])."""
     if q.is_cuda:
-        _native().attn_fwd_dense(q, k, v, tiles, out, scale)
+        if ATTN_TC and tiles128 is not None:
+            _native().attn_fwd_dense_tc(q, k, v, tiles128, out, q.shape[1], k.shape[1], scale, lse, d_o, dd)
+        else:
+            if lse is not None or dd is not None:
+                raise ValueError("attn_fwd_dense: statistics need the tcgen05 kernel (tiles128)")
+            _native().attn_fwd_dense(q, k, v, tiles, out, scale)
         return out
-    ref.dense_attn_fwd(q, k, v, tiles, scale, out)
+    ref.dense_attn_fwd(q, k, v, tiles if tiles is not None else tiles128, scale, out)
+    if lse is not None or dd is not None:
+        ref.dense_attn_stats(q, k, v, tiles if tiles is not None else tiles128, scale, lse, d_o, dd)
     return out
 
 
@@ -391,3 +441,45 @@ def gemm_wgrad(a, b, out, *, kind, n_valid, R=0, b1=0, b2=0, interleave=False, s
                              int(max_ctas))
         return out
     return ref.gemm_wgrad(a, b, out, k, int(n_valid), int(R), int(b1), int(b2), bool(interleave), float(scale))
+
+
+# ----------------------------------------------------------------- fused optimizer of the replicated factors
+
+def push_slices(g, lo, hi, ws):
+    """Send elements [lo, hi) of the replicated gradient block ``g`` to their
+    slice owners (``ws``: :class:`~..parallel.peer.OptPeerWorkspace`)."""
+    _native().push_slices(g, int(lo), int(hi), ws.slice, ws.rank, ws.world, ws.push_table)
+
+
+def fused_replicated_adamw(ws, params, grads, exp_avg, exp_avg_sq, seg_len, shard_sumsq, *, max_norm, lr, wd,
+                           step, b1=0.9, b2=0.999, eps=1e-8, coef=None, total=None, sq=None):
+    """Finish the replicated block's optimizer step once every rank pushed all
+    of its gradients: sum the owned slice, exchange per-layer sums of squares
+    (plus ``shard_sumsq``, this rank's unreplicated part), AdamW with
+    per-layer clipping on the owned slice, updated values to every rank, then
+    wait for the other owners' slices and copy them in. Returns the per-layer
+    squared norms (for the unreplicated part's own AdamW)."""
+    ext = _native(7)
+    L = ws.layers
+    ext.wait_counts(ws.cnt_push, 1, ws.world * ws.len, 0, 0, 0)
+    sq = sq if sq is not None else torch.zeros(L, dtype=torch.float32, device=params.device)
+    sq.zero_()
+    ext.reduce_slice_sumsq(ws.recv_addr, ws.world, ws.slice, ws.first, ws.len, seg_len, grads, sq)
+    ext.exchange_rows(sq, shard_sumsq, ws.rank, ws.world, ws.row_table)
+    ext.wait_counts(ws.cnt_rows, 1, ws.world, 0, 0, 0)
+    coef = coef if coef is not None else torch.empty(L, dtype=torch.float32, device=params.device)
+    total = total if total is not None else torch.empty(L, dtype=torch.float32, device=params.device)
+    ext.clip_coef(ws.rows, float(max_norm), coef, total)
+    ext.adamw_slice_bcast(params, grads, exp_avg, exp_avg_sq, ws.first, ws.len, seg_len, coef, lr, b1, b2, eps,
+                          wd, int(step), ws.rank, ws.world, ws.param_table)
+    return total
+
+
+def fused_replicated_finish(ws, params):
+    """Wait for the other owners' updated slices and copy them into ``params``."""
+    _native().wait_counts(ws.cnt_param, 1, ws.total - ws.len, 0, 0, 0)
+    if ws.first > 0:
+        params[:ws.first].copy_(ws.pstage[:ws.first])
+    end = ws.first + ws.len
+    if end < ws.total:
+        params[end:ws.total].copy_(ws.pstage[end:ws.total])

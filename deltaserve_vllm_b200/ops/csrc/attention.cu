@@ -6,7 +6,8 @@
 // from block_tables[seq, :]. Query i of a sequence with q_len new tokens and
 // total context ctx sits at position ctx - q_len + i and sees keys <= that.
 //
-// Prefill: one CTA = 64 queries x 1 head, 4 warps x 16 rows, K/V tiles of 64
+// Prefill (the warp-level fallback of the tcgen05 kernel in attn_tc.cu, for
+// page sizes that do not tile 128 keys): one CTA = 64 queries x 1 head, 4 warps x 16 rows, K/V tiles of 64
 // keys double-buffered through cp.async into XOR-swizzled shared memory,
 // QK^T and PV on the warp-level tensor-core path (m16n8k16), online softmax
 // in fp32 registers.
@@ -53,9 +54,12 @@ __global__ void __launch_bounds__(PF_THREADS) paged_prefill_kernel(PrefillArgs a
   const int head = blockIdx.y;
   const int kvh = head / a.group;
   const int seq = a.tile_info[2 * tile];
-  const int qt0 = a.tile_info[2 * tile + 1];  // first query index within the sequence
+  // first query index within the sequence: tiles list 128-query spans, each
+  // covered by gridDim.z CTAs of 64 queries
+  const int qt0 = a.tile_info[2 * tile + 1] + (int)blockIdx.z * PF_BM;
   const int q_begin = a.cu_q[seq];
   const int q_len = a.cu_q[seq + 1] - q_begin;
+  if (qt0 >= q_len) return;
   const int ctx = a.ctx_lens[seq];
   const int pos0 = ctx - q_len;  // position of query 0
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -452,9 +456,10 @@ __global__ void decode_combine_kernel(DecodeArgs a) {
 
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
-                       int64_t num_heads, double scale) {
+                       int64_t num_heads, double scale, int64_t tile_rows) {
   using namespace dsv;
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16, "prefill: bf16");
+  TORCH_CHECK(tile_rows > 0 && tile_rows % PF_BM == 0, "prefill: tile_rows must be a multiple of 64");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == HD, "prefill: cache [blocks, Hkv, BS, 128]");
   TORCH_CHECK(q.stride(-1) == 1 && out.stride(-1) == 1, "prefill: contiguous rows");
   const int num_tiles = (int)tile_info.size(0);
@@ -482,7 +487,7 @@ void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
     cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr = true;
   }
-  dim3 grid(num_tiles, (unsigned)num_heads);
+  dim3 grid(num_tiles, (unsigned)num_heads, (unsigned)(tile_rows / PF_BM));
   paged_prefill_kernel<<<grid, PF_THREADS, smem, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

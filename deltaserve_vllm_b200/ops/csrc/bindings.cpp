@@ -33,17 +33,35 @@ void dsv_wait_counts(int64_t cnt, int64_t n, int64_t per_block, int64_t rows, in
 void dsv_reduce_norm_bcast(int64_t recv, int64_t rank, int64_t world, int64_t blocks_cap, int64_t ld, int64_t M,
                            int64_t D, c10::optional<torch::Tensor> x, c10::optional<torch::Tensor> w, double eps,
                            c10::optional<torch::Tensor> add, torch::Tensor out, torch::Tensor table);
+void dsv_push_slices(torch::Tensor g, int64_t lo, int64_t hi, int64_t slice, int64_t rank, int64_t world,
+                     torch::Tensor table);
+void dsv_reduce_slice_sumsq(int64_t recv, int64_t world, int64_t slice, int64_t first, int64_t len, int64_t seg_len,
+                            torch::Tensor g, torch::Tensor sq);
+void dsv_exchange_rows(torch::Tensor a, c10::optional<torch::Tensor> b, int64_t rank, int64_t world,
+                       torch::Tensor table);
+void dsv_clip_coef(torch::Tensor rows, double max_norm, torch::Tensor coef, torch::Tensor total);
+void dsv_adamw_slice_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, int64_t first,
+                           int64_t len, int64_t seg_len, torch::Tensor coef, double lr, double b1, double b2,
+                           double eps, double wd, int64_t step, int64_t rank, int64_t world, torch::Tensor table);
 void dsv_ce_merge(torch::Tensor stats, int64_t n_tiles, torch::Tensor tgt, torch::Tensor part);
 void dsv_ce_finalize(torch::Tensor parts, torch::Tensor labels, torch::Tensor lse, torch::Tensor loss);
 int64_t dsv_read_error_gemm(bool clear);
 int64_t dsv_read_error_attn_bwd(bool clear);
 int64_t dsv_read_error_tp_bwd(bool clear);
+int64_t dsv_read_error_attn_tc(bool clear);
+int64_t dsv_read_error_attn_bwd_tc(bool clear);
 static int64_t dsv_read_error(bool clear) {
-  const int64_t g = dsv_read_error_gemm(clear);
-  const int64_t a = dsv_read_error_attn_bwd(clear);
-  const int64_t t = dsv_read_error_tp_bwd(clear);
-  return g != 0 ? g : (a != 0 ? a : t);
+  const int64_t codes[5] = {dsv_read_error_gemm(clear), dsv_read_error_attn_bwd(clear), dsv_read_error_tp_bwd(clear),
+                            dsv_read_error_attn_tc(clear), dsv_read_error_attn_bwd_tc(clear)};
+  for (int64_t c : codes)
+    if (c != 0) return c;
+  return 0;
 }
+void dsv_attn_bwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor d_o,
+                     torch::Tensor tiles, torch::Tensor lse, torch::Tensor dd, c10::optional<torch::Tensor> dq,
+                     c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
+                     c10::optional<torch::Tensor> rope_cos, c10::optional<torch::Tensor> rope_sin,
+                     c10::optional<torch::Tensor> dqkv, int64_t bf16_mask);
 void dsv_attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor d_o, torch::Tensor tiles,
                   torch::Tensor lse, torch::Tensor dd, torch::Tensor do_bf, c10::optional<torch::Tensor> dq,
                   c10::optional<torch::Tensor> dk, c10::optional<torch::Tensor> dv, double scale,
@@ -53,7 +71,13 @@ void dsv_attn_fwd_dense(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch
                         double scale);
 void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
-                       int64_t num_heads, double scale);
+                       int64_t num_heads, double scale, int64_t tile_rows);
+void dsv_paged_prefill_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                          torch::Tensor cu_q, torch::Tensor ctx_lens, torch::Tensor tile_info, torch::Tensor out,
+                          int64_t num_heads, double scale);
+void dsv_attn_fwd_dense_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles, torch::Tensor out,
+                           int64_t num_heads, int64_t num_kv_heads, double scale, c10::optional<torch::Tensor> lse,
+                           c10::optional<torch::Tensor> d_o, c10::optional<torch::Tensor> dd);
 void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
                       int64_t num_heads, double scale, int64_t splits, int64_t keys_per_split);
@@ -86,6 +110,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_wgrad", &dsv_gemm_wgrad, "LoRA factor-gradient GEMM over the token dimension");
   m.def("wait_counts", &dsv_wait_counts, "one-CTA bounded wait on this rank's arrival counters");
   m.def("reduce_norm_bcast", &dsv_reduce_norm_bcast, "owned-row reduce + RMSNorm backward + P2P all-gather");
+  m.def("push_slices", &dsv_push_slices, "push fp32 partials to their slice owners over peer memory");
+  m.def("reduce_slice_sumsq", &dsv_reduce_slice_sumsq, "sum an owned slice over the ranks + per-layer sum of squares");
+  m.def("exchange_rows", &dsv_exchange_rows, "write a small row into every rank's table");
+  m.def("clip_coef", &dsv_clip_coef, "per-layer clip coefficients from the ranks' sums of squares");
+  m.def("adamw_slice_bcast", &dsv_adamw_slice_bcast, "AdamW on an owned slice, updated values to every rank");
   m.def("ce_merge", &dsv_ce_merge, "merge per-tile softmax statistics of one vocabulary slice");
   m.def("ce_finalize", &dsv_ce_finalize, "log-sum-exp and loss over the ranks' vocabulary slices");
   m.def("peer_alloc", [](int64_t bytes) {
@@ -98,7 +127,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_zero", &dsv_peer_zero, "zero a range of this rank's block");
   m.def("peer_view", &dsv_peer_view, "tensor over a range of a peer workspace block");
   m.def("read_error", &dsv_read_error, "read (and optionally clear) the device error word");
-  m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill)");
+  m.def("paged_prefill", &dsv_paged_prefill, "paged varlen causal attention (prefill), warp-level MMA");
+  m.def("paged_prefill_tc", &dsv_paged_prefill_tc, "paged varlen causal attention (prefill), tcgen05 + TMA");
+  m.def("attn_bwd_tc", &dsv_attn_bwd_tc,
+        "varlen causal GQA attention backward, tcgen05 + TMA (dQ pass, then dK / dV pass)");
+  m.def("attn_fwd_dense_tc", &dsv_attn_fwd_dense_tc,
+        "varlen causal GQA attention forward on packed rows, tcgen05 + TMA (optional lse / rowsum(dO*O))");
   m.def("paged_decode", &dsv_paged_decode, "paged split-KV GQA decode attention");
   m.def("attn_bwd", &dsv_attn_bwd, "varlen causal GQA attention backward (dQ, dK, dV)");
   m.def("attn_fwd_dense", &dsv_attn_fwd_dense, "varlen causal GQA attention forward on packed rows");

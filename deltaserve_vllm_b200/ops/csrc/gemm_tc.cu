@@ -28,6 +28,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "tmap.h"
 
 namespace dsv {
 
@@ -1296,7 +1297,7 @@ struct TmKeyHash {
 // `ld` elements; box = 64 columns (128 bytes, 128-byte swizzle) x box_rows.
 // Maps are cached by (pointer, shape, box): weights and the engine's
 // persistent activation buffers are encoded once.
-static CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+CUtensorMap make_tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
   static std::unordered_map<TmKey, CUtensorMap, TmKeyHash> cache;
   static std::mutex mu;
   TmKey key{reinterpret_cast<uint64_t>(ptr), rows, cols, ld, box_rows};

@@ -320,3 +320,241 @@ void dsv_ce_finalize(torch::Tensor parts, torch::Tensor labels, torch::Tensor ls
 }
 
 DSV_ERROR_ACCESSOR(dsv_read_error_tp_bwd)
+
+// ================================================================ fused optimizer
+// Replicated LoRA factors (column-parallel A, row-parallel B) hold the same
+// values on every rank but each rank's gradient is a partial. Instead of an
+// all-reduce of the gradients followed by AdamW on every rank, each rank owns
+// a contiguous slice of the replicated block:
+//   1. push_slices_kernel (during the backward, per finished bucket of layers):
+//      the rank's partial gradient of every element goes to the element's
+//      owner (recv[owner][rank][i - owner's first element], P2P stores); the
+//      owner's counter grows by the elements stored (release);
+//   2. wait_counts_kernel: every rank's elements of the owned slice arrived;
+//   3. reduce_slice_sumsq_kernel: the owned slice is summed over the ranks
+//      (into this rank's gradient buffer) and its per-layer sums of squares
+//      accumulated;
+//   4. exchange_rows_kernel + wait: every rank's per-layer sums of squares
+//      (replicated slice + own shard) are written into every rank's table, so
+//      each rank has the same per-layer gradient norm for clipping;
+//   5. adamw_slice_bcast_kernel: AdamW with per-layer clipping on the owned
+//      slice, the updated parameters stored into every rank's parameter
+//      staging buffer (P2P) with the element count added to its counter;
+//   6. wait: the other owners' slices arrived; they are copied into the
+//      parameters (local), and the per-rank shard runs the plain AdamW.
+// Only the one-CTA waits wait; reuse across cycles is ordered as in the
+// residual reductions (a rank pushes cycle k+1 only after its step 6 of k).
+
+namespace dsv {
+
+struct SliceTable {
+  float* recv[kTpMaxPeers];
+  uint32_t* cnt[kTpMaxPeers];
+};
+
+// Elements [lo, hi) of the replicated block: element e goes to owner e / slice.
+// One CTA stores a chunk of `chunk` elements (split where it crosses an
+// owner's slice boundary) and bumps each owner's count by what it stored.
+__global__ void push_slices_kernel(const float* __restrict__ g, int64_t lo, int64_t hi, int64_t slice, int rank,
+                                   int64_t chunk, SliceTable t) {
+  const int64_t c0 = lo + (int64_t)blockIdx.x * chunk;
+  const int64_t cend = min(hi, c0 + chunk);
+  for (int64_t a = c0; a < cend;) {
+    const int owner = (int)(a / slice);
+    const int64_t b = min(cend, (int64_t)(owner + 1) * slice);
+    float* dst = t.recv[owner] + (int64_t)rank * slice - (int64_t)owner * slice;
+    for (int64_t e = a + threadIdx.x; e < b; e += blockDim.x) dst[e] = g[e];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      red_release_sys_add(t.cnt[owner], (uint32_t)(b - a));
+    }
+    a = b;
+  }
+}
+
+// Owned slice of the replicated block, cut at layer boundaries into pieces:
+// piece q covers block elements [lo[q], hi[q]) of layer seg[q]. CTA (x, q)
+// sums a chunk of piece q over the ranks' partials (recv row s holds rank s's
+// values for the slice starting at `first`), writes the sums into g and adds
+// the chunk's sum of squares to sq[seg[q]] (one atomic per CTA).
+constexpr int kMaxPieces = 64;
+struct SlicePieces {
+  int64_t lo[kMaxPieces], hi[kMaxPieces];
+  int seg[kMaxPieces];
+};
+
+__global__ void reduce_slice_sumsq_kernel(const float* __restrict__ recv, int world, int64_t slice, int64_t first,
+                                          int64_t chunk, SlicePieces pc, float* __restrict__ g, float* sq) {
+  __shared__ float red[8];
+  const int q = blockIdx.y;
+  const int64_t c0 = pc.lo[q] + (int64_t)blockIdx.x * chunk;
+  if (c0 >= pc.hi[q]) return;                   // uniform per CTA
+  const int64_t c1 = min(pc.hi[q], c0 + chunk);
+  float acc = 0.f;
+  for (int64_t e = c0 + threadIdx.x; e < c1; e += blockDim.x) {
+    const int64_t i = e - first;
+    float v = 0.f;
+    for (int s = 0; s < world; ++s) v += __ldcg(recv + (int64_t)s * slice + i);
+    g[e] = v;
+    acc += v * v;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    atomicAdd(sq + pc.seg[q], t);
+  }
+}
+
+// One CTA: row[l] = a[l] (+ b[l]) written into every rank's table at row
+// `rank` (table[d] + rank * n), then each rank's counter + 1.
+__global__ void exchange_rows_kernel(const float* __restrict__ a, const float* __restrict__ b, int n, int rank,
+                                     int world, SliceTable t) {
+  for (int d = 0; d < world; ++d) {
+    float* dst = t.recv[d] + (int64_t)rank * n;
+    for (int l = threadIdx.x; l < n; l += blockDim.x) dst[l] = a[l] + (b != nullptr ? b[l] : 0.f);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    red_release_sys_add(t.cnt[threadIdx.x], 1u);
+  }
+}
+
+// AdamW on the owned slice [first, first + len) with per-layer clipping from
+// coef[layer]; the updated parameters go into every rank's staging buffer at
+// the same offset (P2P), then each rank's counter grows by the chunk.
+__global__ void adamw_slice_bcast_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                                         float* __restrict__ v, int64_t first, int64_t len, int64_t seg_len,
+                                         const float* __restrict__ coef, float lr, float b1, float b2, float eps,
+                                         float wd, float bc1, float bc2, int rank, int world, int64_t chunk,
+                                         SliceTable t) {
+  const int64_t c0 = (int64_t)blockIdx.x * chunk;
+  if (c0 >= len) return;
+  const int64_t c1 = min(len, c0 + chunk);
+  for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+    const int64_t e = first + i;
+    const float gi = g[e] * coef[e / seg_len];
+    float pi = p[e];
+    pi -= lr * wd * pi;
+    const float mi = b1 * m[e] + (1.f - b1) * gi;
+    const float vi = b2 * v[e] + (1.f - b2) * gi * gi;
+    m[e] = mi;
+    v[e] = vi;
+    pi -= lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+    p[e] = pi;
+    for (int d = 0; d < world; ++d) {
+      const int dr = (rank + d) % world;
+      if (dr != rank) t.recv[dr][e] = pi;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < world && threadIdx.x != rank) {
+    __threadfence_system();
+    red_release_sys_add(t.cnt[threadIdx.x], (uint32_t)(c1 - c0));
+  }
+}
+
+// coef[l] = min(1, max_norm / (sqrt(sum over ranks of rows[r][l]) + 1e-6)).
+__global__ void clip_coef_kernel(const float* __restrict__ rows, int world, int n, float max_norm, float* coef,
+                                 float* total) {
+  for (int l = blockIdx.x * blockDim.x + threadIdx.x; l < n; l += gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < world; ++r) s += rows[(int64_t)r * n + l];
+    total[l] = s;
+    coef[l] = max_norm > 0.f ? fminf(1.f, max_norm / (sqrtf(s) + 1e-6f)) : 1.f;
+  }
+}
+
+static SliceTable slice_table(torch::Tensor table, int world) {
+  TORCH_CHECK(table.device().is_cpu() && table.scalar_type() == at::kLong && table.size(0) == 2 &&
+                  table.size(1) == world, "slice table must be int64 [2, world] on the CPU");
+  SliceTable t{};
+  auto* p = table.data_ptr<int64_t>();
+  for (int r = 0; r < world; ++r) {
+    t.recv[r] = reinterpret_cast<float*>(p[r]);
+    t.cnt[r] = reinterpret_cast<uint32_t*>(p[world + r]);
+  }
+  return t;
+}
+
+}  // namespace dsv
+
+void dsv_push_slices(torch::Tensor g, int64_t lo, int64_t hi, int64_t slice, int64_t rank, int64_t world,
+                     torch::Tensor table) {
+  using namespace dsv;
+  if (hi <= lo) return;
+  TORCH_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && hi <= g.numel(), "push_slices: fp32 block");
+  c10::cuda::CUDAGuard guard(g.device());
+  const int64_t chunk = 8192;
+  const int64_t blocks = (hi - lo + chunk - 1) / chunk;
+  push_slices_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      g.data_ptr<float>(), lo, hi, slice, (int)rank, chunk, slice_table(table, (int)world));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_reduce_slice_sumsq(int64_t recv, int64_t world, int64_t slice, int64_t first, int64_t len, int64_t seg_len,
+                            torch::Tensor g, torch::Tensor sq) {
+  using namespace dsv;
+  if (len <= 0) return;
+  SlicePieces pc{};
+  int n = 0;
+  for (int64_t a = first; a < first + len;) {
+    const int64_t seg = a / seg_len;
+    const int64_t b = std::min(first + len, (seg + 1) * seg_len);
+    TORCH_CHECK(n < kMaxPieces, "reduce_slice_sumsq: the slice spans too many layers");
+    pc.lo[n] = a;
+    pc.hi[n] = b;
+    pc.seg[n] = (int)seg;
+    ++n;
+    a = b;
+  }
+  int64_t longest = 0;
+  for (int q = 0; q < n; ++q) longest = std::max(longest, pc.hi[q] - pc.lo[q]);
+  const int64_t chunk = 8192;
+  c10::cuda::CUDAGuard guard(g.device());
+  reduce_slice_sumsq_kernel<<<dim3((unsigned)((longest + chunk - 1) / chunk), (unsigned)n), 256, 0,
+                              at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const float*>(recv), (int)world,
+                                                                  slice, first, chunk, pc, g.data_ptr<float>(),
+                                                                  sq.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_exchange_rows(torch::Tensor a, c10::optional<torch::Tensor> b, int64_t rank, int64_t world,
+                       torch::Tensor table) {
+  using namespace dsv;
+  c10::cuda::CUDAGuard guard(a.device());
+  exchange_rows_kernel<<<1, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      a.data_ptr<float>(), b.has_value() ? b->data_ptr<float>() : nullptr, (int)a.numel(), (int)rank, (int)world,
+      slice_table(table, (int)world));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_clip_coef(torch::Tensor rows, double max_norm, torch::Tensor coef, torch::Tensor total) {
+  using namespace dsv;
+  c10::cuda::CUDAGuard guard(rows.device());
+  const int world = (int)rows.size(0), n = (int)rows.size(1);
+  clip_coef_kernel<<<(n + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      rows.data_ptr<float>(), world, n, (float)max_norm, coef.data_ptr<float>(), total.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_adamw_slice_bcast(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, int64_t first,
+                           int64_t len, int64_t seg_len, torch::Tensor coef, double lr, double b1, double b2,
+                           double eps, double wd, int64_t step, int64_t rank, int64_t world, torch::Tensor table) {
+  using namespace dsv;
+  if (len <= 0) return;
+  c10::cuda::CUDAGuard guard(p.device());
+  const float bc1 = 1.f - (float)std::pow(b1, (double)step);
+  const float bc2 = 1.f - (float)std::pow(b2, (double)step);
+  const int64_t chunk = 8192;
+  const int64_t blocks = (len + chunk - 1) / chunk;
+  adamw_slice_bcast_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), first, len, seg_len,
+      coef.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, bc1, bc2, (int)rank,
+      (int)world, chunk, slice_table(table, (int)world));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -8,6 +8,8 @@ kernel so that CPU runs of the engine and GPU runs agree up to bf16 rounding.
 from __future__ import annotations
 
 
+import math
+
 import torch
 import torch.nn.functional as F
 
@@ -298,6 +300,26 @@ def dense_attn_fwd(q, k, v, tiles, scale, out):
         o = torch.einsum("hqk,khd->qhd", p, vv).reshape(ln, hq * hd)
         out[st:st + ln, :hq * hd] = o.to(out.dtype)
     return out
+
+
+def dense_attn_stats(q, k, v, tiles, scale, lse, d_o, dd):
+    """Per packed row and query head: the base-2 log-sum-exp of the scaled
+    causal scores (``lse`` [Hq, >= n]) and rowsum(dO * O) (``dd``, from
+    ``d_o`` [n, Hq * 128]); either may be None."""
+    hq, hd = q.shape[1], q.shape[2]
+    for st, ln in _tile_samples(tiles):
+        qq = q[st:st + ln].float()
+        kk = k[st:st + ln].float().repeat_interleave(hq // k.shape[1], 1)
+        s = torch.einsum("qhd,khd->hqk", qq, kk) * scale
+        mask = torch.triu(torch.ones(ln, ln, dtype=torch.bool, device=q.device), 1)
+        s = s.masked_fill(mask, float("-inf"))
+        if lse is not None:
+            lse[:hq, st:st + ln] = (torch.logsumexp(s, -1) / math.log(2.0)).to(lse.dtype)
+        if dd is not None:
+            vv = v[st:st + ln].float().repeat_interleave(hq // v.shape[1], 1)
+            o = torch.einsum("hqk,khd->qhd", s.softmax(-1), vv)
+            g = d_o[st:st + ln].float().reshape(ln, hq, hd)
+            dd[:hq, st:st + ln] = (o * g).sum(-1).t().to(dd.dtype)
 
 
 def dense_attn_bwd(q, k, v, d_o, tiles, scale, dq, dk, dv):

@@ -195,3 +195,63 @@ def _from_ptr(addr: int, shape, dtype, device) -> torch.Tensor:
     """A tensor over ``addr`` (memory owned by the workspace, not by PyTorch)."""
     from .. import ops
     return ops.native_ext().peer_view(int(addr), list(shape), dtype, int(device))
+
+
+class OptPeerWorkspace:
+    """Peer-mapped buffers of the fused optimizer for the TP-replicated LoRA
+    factors (``ops.push_slices`` ... ``ops.adamw_slice_bcast``): rank ``r``
+    owns elements ``[r * slice, (r + 1) * slice)`` of the replicated block,
+    receives every rank's partial gradients of them, sums them, runs AdamW
+    with per-layer clipping on them and sends the updated values to every
+    rank. One IPC-exported block per rank (plain P2P mappings) holding:
+
+    * ``recv``   — ``[world][slice]`` fp32 partial gradients pushed to this rank;
+    * ``pstage`` — ``[total]`` fp32 updated parameters from the other owners;
+    * ``rows``   — ``[world][layers]`` fp32 per-layer sums of squares of every rank;
+    * three counters (gradient elements, rows, parameter elements arrived).
+    """
+
+    def __init__(self, comm, total: int, layers: int):
+        from .. import ops
+        ext = ops.native_ext()
+        if ext is None:
+            raise RuntimeError("the fused optimizer workspace needs the CUDA extension")
+        self.comm = comm
+        self.world, self.rank = comm.size, comm.rank
+        self.total, self.layers = int(total), int(layers)
+        self.slice = -(-self.total // self.world)
+        self.slice = -(-self.slice // 64) * 64
+        self.first = self.rank * self.slice
+        self.len = max(0, min(self.slice, self.total - self.first))
+        sizes = [self.world * self.slice * 4, self.total * 4, self.world * self.layers * 4, 4, 4, 4]
+        self.offsets, off = [], 0
+        for sz in sizes:
+            self.offsets.append(off)
+            off += _align(sz)
+        self._ext = ext
+        self.base, handle = ext.peer_alloc(off)
+        handles = comm.all_gather_object(handle)
+        self.ptrs = [self.base if r == self.rank else ext.peer_open(h) for r, h in enumerate(handles)]
+        at = lambda k: [p + self.offsets[k] for p in self.ptrs]
+        self.push_table = torch.tensor([at(0), at(3)], dtype=torch.int64)
+        self.param_table = torch.tensor([at(1), at(5)], dtype=torch.int64)
+        self.row_table = torch.tensor([at(2), at(4)], dtype=torch.int64)
+        self.recv_addr = self.base + self.offsets[0]
+        self.cnt_push = self.base + self.offsets[3]
+        self.cnt_rows = self.base + self.offsets[4]
+        self.cnt_param = self.base + self.offsets[5]
+        dev = torch.cuda.current_device()
+        self.pstage = _from_ptr(self.base + self.offsets[1], (self.total,), torch.float32, dev)
+        self.rows = _from_ptr(self.base + self.offsets[2], (self.world, self.layers), torch.float32, dev)
+        comm.barrier()
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        self.comm.barrier()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.peer_close(p)
+        self._ext.peer_free(self.base)
+        self.base = None

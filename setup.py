@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("deltaserve_vllm_b200", "ops", "csrc")
 SOURCES = [os.path.join(CSRC, f) for f in (
     "bindings.cpp", "gemm_tc.cu", "attention.cu", "norm_rope.cu", "lora_misc.cu", "peer.cu", "attn_bwd.cu",
-    "tp_bwd.cu")]
+    "tp_bwd.cu", "attn_tc.cu", "attn_bwd_tc.cu")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -259,18 +259,37 @@ def _paged_setup(lens, qlens, Hq, Hkv, bs, seed=0):
         torch.tensor(lens, dtype=torch.int32, device=DEV), q
 
 
-@pytest.mark.parametrize("bs", [16, 64])
+@pytest.mark.parametrize("bs", [16, 64, 128, 256, 48])
 @pytest.mark.parametrize("Hq,Hkv", [(8, 2), (4, 4)])
 def test_paged_prefill(bs, Hq, Hkv):
-    lens = [1, 63, 64, 65, 200, 513]
-    qlens = [1, 63, 10, 65, 200, 100]
+    """Block sizes that tile 128 keys run the tcgen05 kernel, 48 the warp-level one."""
+    lens = [1, 63, 64, 65, 200, 513, 1100]
+    qlens = [1, 63, 10, 65, 200, 100, 700]
     kc, vc, bt, cu, ctx, q = _paged_setup(lens, qlens, Hq, Hkv, bs)
+    assert ops.prefill_uses_tc(bs) == (bs != 48)
     tiles = torch.tensor(ops.prefill_tiles(cu.tolist()), dtype=torch.int32, device=DEV)
     out = torch.zeros(q.shape[0], Hq * 128, dtype=torch.bfloat16, device=DEV)
     ops.paged_prefill(q, kc, vc, bt, cu, ctx, tiles, out, Hq, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
     exp = torch.zeros_like(out, dtype=torch.float32).cpu()
     ref.paged_prefill(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), cu.cpu(), ctx.cpu(), exp, Hq, 1 / math.sqrt(128))
     torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+def test_paged_prefill_tc_matches_warp_kernel():
+    """Both prefill kernels on one batch (64-key pages): same outputs to bf16 rounding."""
+    lens, qlens = [300, 1024, 77], [300, 512, 77]
+    kc, vc, bt, cu, ctx, q = _paged_setup(lens, qlens, 32, 8, 64)
+    tiles = torch.tensor(ops.prefill_tiles(cu.tolist()), dtype=torch.int32, device=DEV)
+    a = torch.zeros(q.shape[0], 32 * 128, dtype=torch.bfloat16, device=DEV)
+    b = torch.zeros_like(a)
+    nat = ops._native()
+    nat.paged_prefill_tc(q, kc, vc, bt, cu, ctx, tiles, a, 32, 1 / math.sqrt(128))
+    nat.paged_prefill(q, kc, vc, bt, cu, ctx, tiles, b, 32, 1 / math.sqrt(128), ops.PREFILL_TILE)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    torch.testing.assert_close(a.float(), b.float(), rtol=1.6e-2, atol=1.6e-2)
 
 
 def _packed_qkv(lens, Hq, Hkv, seed, pad=8):
@@ -343,6 +362,67 @@ def test_attn_bwd_rope_epilogue_into_dqkv(mask):
     assert (dqkv[used:] == 7.0).all()                       # rows past the samples untouched
 
 
+@pytest.mark.parametrize("Hq,Hkv,lse_from_fwd", [(8, 2, True), (4, 4, False), (32, 8, True)])
+def test_attn_bwd_tc_varlen_gqa(Hq, Hkv, lse_from_fwd):
+    """tcgen05 attention backward (dQ pass + dK/dV pass) against the fp32
+    reference, elementwise; the forward's statistics either come from the
+    tcgen05 forward (the trainer's path) or are recomputed inside attn_bwd."""
+    lens = [1, 37, 64, 65, 130, 200, 513] if Hq <= 8 else [512, 512, 300, 7]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=41)
+    g = torch.Generator(device=DEV).manual_seed(42)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV).to(torch.bfloat16)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV)
+    t128 = ops.dense_attn_tiles(starts, lens, DEV, bm=128)
+    scale = 1 / math.sqrt(128)
+    o = lse = None
+    if lse_from_fwd:
+        o = torch.zeros(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+        lse = torch.zeros(Hq, n, device=DEV)
+        ops.attn_fwd_dense(q, k, v, tiles, scale, o, tiles128=t128, lse=lse)
+    dq, dk, dv = ops.attn_bwd(q, k, v, d_o, tiles, scale, o=o, lse=lse, tiles128=t128)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    eq = torch.zeros(n, Hq, 128)
+    ek, ev = torch.zeros(n, Hkv, 128), torch.zeros(n, Hkv, 128)
+    ref.dense_attn_bwd(q.cpu(), k.cpu(), v.cpu(), d_o.float().cpu().view(n, Hq, 128), tiles.cpu(), scale, eq, ek, ev)
+    used = sum(lens)
+    for got, exp in ((dq, eq), (dk, ek), (dv, ev)):
+        got = got.cpu()[:used]
+        exp = exp[:used]
+        tol = 2e-2 * exp.abs().max()
+        assert (got - exp).abs().max() < tol, float((got - exp).abs().max() / exp.abs().max())
+        rel = (got - exp).norm() / exp.norm()
+        assert rel < 1e-2, float(rel)
+    assert dq[used:].abs().max() == 0 and dk[used:].abs().max() == 0
+    dq2, dk2, dv2 = ops.attn_bwd(q, k, v, d_o, tiles, scale, o=o, lse=lse, tiles128=t128)
+    assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)   # deterministic
+
+
+def test_attn_bwd_tc_rope_epilogue_matches_warp_kernels():
+    """The trainer's call (RoPE backward, bf16 stores into d(qkv)) on both
+    backward implementations: same values to bf16 rounding."""
+    Hq, Hkv = 8, 2
+    lens = [5, 64, 130, 77, 300]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=45)
+    g = torch.Generator(device=DEV).manual_seed(46)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV).to(torch.bfloat16)
+    pos = torch.cat([torch.arange(ln) for ln in lens] + [torch.zeros(n - sum(lens), dtype=torch.long)]).to(DEV)
+    from deltaserve_vllm_b200.models.rope import cos_sin
+    cos, sin = cos_sin(pos, 128, 500000.0)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV)
+    t128 = ops.dense_attn_tiles(starts, lens, DEV, bm=128)
+    scale = 1 / math.sqrt(128)
+    a = torch.full((n, (Hq + 2 * Hkv) * 128), 7.0, dtype=torch.bfloat16, device=DEV)
+    b = a.clone()
+    ops.attn_bwd(q, k, v, d_o.float(), tiles, scale, rope=(cos, sin), dqkv=a, bf16_mask=7)
+    ops.attn_bwd(q, k, v, d_o, tiles, scale, rope=(cos, sin), dqkv=b, bf16_mask=7, tiles128=t128)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    used = sum(lens)
+    torch.testing.assert_close(b[:used].float(), a[:used].float(), rtol=3e-2, atol=3e-2)
+    assert (b[used:] == 7.0).all()
+
+
 def test_gemm_swiglu_bwd_epilogue():
     """d(act) GEMM (MN-major, with the LoRA K block) whose epilogue applies the
     SwiGLU backward == fp32 product then the SwiGLU backward reference."""
@@ -375,6 +455,31 @@ def test_attn_fwd_dense(Hq, Hkv):
     exp = torch.zeros(n, Hq * 128)
     ref.dense_attn_fwd(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), 1 / math.sqrt(128), exp)
     torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2), (32, 8)])
+def test_attn_fwd_dense_tc_with_stats(Hq, Hkv):
+    """tcgen05 dense forward: O, base-2 row log-sum-exp and rowsum(dO * O) against fp32."""
+    lens = [3, 64, 129, 500, 1000]
+    q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=35)
+    tiles = ops.dense_attn_tiles(starts, lens, DEV, bm=128)
+    g = torch.Generator(device=DEV).manual_seed(36)
+    d_o = torch.randn(n, Hq * 128, generator=g, device=DEV)
+    out = torch.zeros(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+    lse = torch.zeros(Hq, n, device=DEV)
+    dd = torch.zeros(Hq, n, device=DEV)
+    scale = 1 / math.sqrt(128)
+    ops.attn_fwd_dense(q, k, v, None, scale, out, tiles128=tiles, lse=lse, d_o=d_o, dd=dd)
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    exp = torch.zeros(n, Hq * 128)
+    else_, edd = torch.zeros(Hq, n), torch.zeros(Hq, n)
+    ref.dense_attn_fwd(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), scale, exp)
+    ref.dense_attn_stats(q.cpu(), k.cpu(), v.cpu(), tiles.cpu(), scale, else_, d_o.cpu(), edd)
+    torch.testing.assert_close(out.float().cpu(), exp, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(lse.cpu(), else_, rtol=1e-3, atol=2e-3)
+    # dd sums 128 products of O (bf16-level error) and dO ~ N(0, 1)
+    torch.testing.assert_close(dd.cpu(), edd, rtol=2e-2, atol=5e-2)
 
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8])

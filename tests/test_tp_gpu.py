@@ -123,14 +123,25 @@ def _run_fused_vs_nccl(rank, world, port, outdir):
     comm = TPComm(None, dist.new_group(backend="gloo"))
     out = {}
     for mode in ("nccl", "fused"):
+        # lr = 0: the gradients are compared. The unreplicated factors' ones
+        # (column-parallel B, row-parallel A) are final on every rank on both
+        # paths; the replicated ones end up summed only in each slice owner on
+        # the fused path (their optimizer has its own test below).
         tr, res = run_trainer(arch, seqs, ad, "cuda", torch.bfloat16, tp=TPInfo(rank, world), comm=comm,
                               fused_tp=mode == "fused")
         shards = comm.gather_objects(tr.masters.export_peft(16, grads=True))
         if rank == 0:
-            out[mode] = {"loss": res[0].loss, "grads": merge_tp_shards(shards)}
+            full = merge_tp_shards(shards)
+            out[mode] = {"loss": res[0].loss,
+                         "grads": {k: v for k, v in full.items()
+                                   if any(f".{p}_proj.lora_B" in k for p in ("q", "k", "v", "gate", "up"))
+                                   or any(f".{p}_proj.lora_A" in k for p in ("o", "down"))}}
         if tr.bwd.tpws is not None:
             tr.bwd.tpws.close()
             tr.bwd.tpws = None
+        if tr.optws is not None:
+            tr.optws.close()
+            tr.optws = None
     torch.cuda.synchronize()
     out["code"] = ops.check_device_error()
     if rank == 0:
@@ -154,9 +165,78 @@ def test_fused_tp_backward_matches_nccl(world):
         assert r["code"] == 0
         a, b = r["fused"], r["nccl"]
         assert abs(a["loss"] - b["loss"]) < 1e-3 * abs(b["loss"])
+        assert b["grads"]
         for k, y in b["grads"].items():
             x = a["grads"][k].float()
             y = y.float()
             scale = float(y.abs().max()) + 1e-12
             assert float((x - y).abs().max()) < 3e-2 * scale, (k, float((x - y).abs().max()) / scale)
             assert float((x - y).norm()) < 1e-2 * (float(y.norm()) + 1e-12), k
+
+
+def _run_fused_optimizer(rank, world, port, outdir):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from deltaserve_vllm_b200.parallel.peer import OptPeerWorkspace
+    comm = TPComm(None, dist.new_group(backend="gloo"))
+    L, seg = 5, 3000 + 17                    # layers x elements per layer (odd sizes on purpose)
+    T = L * seg
+    ws = OptPeerWorkspace(comm, T, L)
+    g0 = torch.Generator().manual_seed(0)
+    p0 = torch.randn(T, generator=g0)
+    m0 = torch.randn(T, generator=g0) * 0.01
+    v0 = torch.rand(T, generator=g0) * 0.01
+    gr = torch.Generator().manual_seed(100 + rank)
+    g_in = (torch.randn(T, generator=gr) * 0.3).cuda()
+    g = torch.empty_like(g_in)
+    shard_sq = (torch.rand(L, generator=gr) * 2.0).cuda()
+    p, m, v = p0.cuda(), m0.cuda(), v0.cuda()
+    for step in (1, 2):                     # twice: the counters and buffers reset themselves
+        g.copy_(g_in)                       # (the owner's slice of g is overwritten by the sum)
+        ops.push_slices(g, 3 * seg, T, ws)
+        ops.push_slices(g, 0, 3 * seg, ws)
+        total = ops.fused_replicated_adamw(ws, p, g, m, v, seg, shard_sq, max_norm=1.0, lr=1e-2, wd=0.01, step=step)
+        ops.fused_replicated_finish(ws, p)
+    torch.cuda.synchronize()
+    gs = comm.all_gather_object(g_in.cpu())
+    sqs = comm.all_gather_object(shard_sq.cpu())
+    ps = comm.all_gather_object(p.cpu())
+    code = ops.check_device_error()
+    ws.close()
+    if rank == 0:
+        torch.save({"gs": gs, "sqs": sqs, "ps": ps, "total": total.cpu(), "p0": p0, "m0": m0, "v0": v0,
+                    "code": code, "L": L, "seg": seg}, os.path.join(outdir, "opt.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_replicated_optimizer(world):
+    """The replicated factors' optimizer over peer memory: after two steps
+    every rank holds the same parameters, equal to AdamW with per-layer
+    clipping applied on the host to the sum of the ranks' gradients (the
+    per-layer norms including every rank's shard part)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run_fused_optimizer, args=(world, _port(), d), nprocs=world, join=True,
+                           start_method="spawn")
+        r = torch.load(os.path.join(d, "opt.pt"))
+        assert r["code"] == 0
+        L, seg = r["L"], r["seg"]
+        # every step pushes the rank's same gradients (the test does not rerun a backward)
+        G = sum(r["gs"])
+        sq = (G.view(L, seg) ** 2).sum(1) + sum(r["sqs"])
+        coef = torch.clamp(1.0 / (sq.sqrt() + 1e-6), max=1.0).repeat_interleave(seg)
+        p, m, v = r["p0"].clone(), r["m0"].clone(), r["v0"].clone()
+        for step in (1, 2):
+            gi = G * coef
+            p = p - 1e-2 * 0.01 * p
+            m = 0.9 * m + 0.1 * gi
+            v = 0.999 * v + 0.001 * gi * gi
+            p = p - 1e-2 * (m / (1 - 0.9 ** step)) / ((v / (1 - 0.999 ** step)).sqrt() + 1e-8)
+        torch.testing.assert_close(r["total"], sq, rtol=1e-4, atol=1e-4)
+        for got in r["ps"]:
+            torch.testing.assert_close(got, p, rtol=1e-4, atol=1e-5)

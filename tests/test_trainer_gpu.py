@@ -20,7 +20,8 @@ pytestmark = pytest.mark.gpu
 def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None, fused_tp=False):
     """Forward the FT rows through the serving model (capturing activations)
     and run ``steps`` backward cycles. ``fused_tp``: the residual-gradient
-    reductions over peer memory (the caller closes ``tr.bwd.tpws``)."""
+    reductions and the replicated factors' optimizer over peer memory (the
+    caller closes ``tr.bwd.tpws`` and ``tr.optws``)."""
     from deltaserve_vllm_b200.models.weights import TPInfo
     tp = tp or TPInfo()
     w = init_weights(arch, tp=tp, seed=5, device="cpu", dtype=torch.float32).to(device, dtype)
@@ -33,8 +34,9 @@ def run(arch, seqs, ad, device, dtype, steps=1, lr=0.0, tp=None, comm=None, fuse
     tr.load_adapter(ad, 16, 32)
     tr.publish()
     if fused_tp:
-        from deltaserve_vllm_b200.parallel.peer import BwdPeerWorkspace
+        from deltaserve_vllm_b200.parallel.peer import BwdPeerWorkspace, OptPeerWorkspace
         tr.bwd.tpws = BwdPeerWorkspace(comm, n + 8, arch.hidden)
+        tr.optws = OptPeerWorkspace(comm, tr.masters.rep_total, arch.num_layers)
     runner = ModelRunner(model, 64, device, ft_slot=1)
     sched = Scheduler(kv.allocator, 64, max_num_batched_tokens=8192, max_model_len=4096)
     res = []
