@@ -79,13 +79,19 @@ def _paged(lens, qlens, Hq=32, Hkv=8, bs=64, seed=0):
     return kc, vc, bt.to(DEV), cu, torch.tensor(lens, dtype=torch.int32, device=DEV), q
 
 
-def _prefill(n_seq, L, Hq=32, Hkv=8):
+def _prefill(n_seq, L, Hq=32, Hkv=8, warp_kernel=False):
+    """Paged causal prefill of n_seq x L new tokens: the tcgen05 kernel, or
+    (``warp_kernel``) the warp-level mma.sync kernel on the same tiles."""
     kc, vc, bt, cu, ctx, q = _paged([L] * n_seq, [L] * n_seq, Hq, Hkv)
     tiles = torch.tensor(ops.prefill_tiles(cu), dtype=torch.int32, device=DEV)
     cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
     out = torch.empty(q.shape[0], Hq * 128, dtype=torch.bfloat16, device=DEV)
     flops = n_seq * Hq * 128 * 4 * (L * (L + 1) / 2)
     byts = 2 * (2 * q.numel() + 2 * n_seq * L * Hkv * 128)
+    if warp_kernel:
+        nat = ops._native()
+        return (lambda: nat.paged_prefill(q, kc, vc, bt, cu_t, ctx, tiles, out, Hq, 1 / math.sqrt(128),
+                                          ops.PREFILL_TILE), byts, flops)
     return (lambda: ops.paged_prefill(q, kc, vc, bt, cu_t, ctx, tiles, out, Hq, 1 / math.sqrt(128)),
             byts, flops)
 
@@ -139,7 +145,25 @@ def _ce(R, V):
     return (lambda: ops.ce_fwd_bwd(logits, tgt, loss, grad, 1.0), R * V * (4 + 2), 0)
 
 
-def _attn_bwd(n_seq, L, Hq=32, Hkv=8, torch_path=False):
+def _attn_fwd_dense_tc(n_seq, L, Hq=32, Hkv=8):
+    """The trainer's attention recompute on the tcgen05 kernel: O plus the
+    row log-sum-exp the backward reuses."""
+    from ..models.lora_backward import attention_groups
+    n = n_seq * L
+    qkv = rnd(n, (Hq + 2 * Hkv) * 128, seed=7)
+    q = qkv[:, :Hq * 128].view(n, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(n, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].view(n, Hkv, 128)
+    groups = attention_groups([i * L for i in range(n_seq)], [L] * n_seq, DEV)
+    out = torch.empty(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+    lse = torch.empty(Hq, n, device=DEV)
+    flops = n_seq * Hq * 128 * 4 * (L * (L + 1) / 2)
+    byts = 2 * qkv.numel() + 2 * out.numel() + 4 * lse.numel()
+    return (lambda: ops.attn_fwd_dense(q, k, v, groups.tiles, 1 / math.sqrt(128), out, tiles128=groups.tiles128,
+                                       lse=lse), byts, flops)
+
+
+def _attn_bwd(n_seq, L, Hq=32, Hkv=8, torch_path=False, tc=False):
     """Trainer attention backward over n_seq packed causal samples of L tokens
     (q/k/v strided views of one fused qkv buffer, fp32 dO). FLOPs: the five
     causal 128-deep products of a standard flash backward (QK^T, dP, dV, dQ,
@@ -157,6 +181,16 @@ def _attn_bwd(n_seq, L, Hq=32, Hkv=8, torch_path=False):
     byts = 2 * qkv.numel() + 4 * d_o.numel() + 4 * n * (Hq + 2 * Hkv) * 128
     if torch_path:
         fn = lambda: attn_backward(q, k, v, d_o.view(n, Hq, 128), starts, lens, 1 / math.sqrt(128), groups)
+    elif tc:
+        # The trainer's call: bf16 dO, and O / lse from the recompute forward.
+        g = d_o.to(torch.bfloat16)
+        o = torch.empty(n, Hq * 128, dtype=torch.bfloat16, device=DEV)
+        lse = torch.empty(Hq, n, device=DEV)
+        dd = torch.empty_like(lse)
+        ops.attn_fwd_dense(q, k, v, groups.tiles, 1 / math.sqrt(128), o, tiles128=groups.tiles128, lse=lse)
+        byts = 2 * qkv.numel() + 2 * 2 * d_o.numel() + 4 * n * (Hq + 2 * Hkv) * 128
+        fn = lambda: ops.attn_bwd(q, k, v, g, groups.tiles, 1 / math.sqrt(128), o=o, lse=lse,
+                                  tiles128=groups.tiles128, dd=dd)
     else:
         fn = lambda: ops.attn_bwd(q, k, v, d_o, groups.tiles, 1 / math.sqrt(128))
     return fn, byts, flops
@@ -251,6 +285,10 @@ CASES = {
     "gemm_ar_decode_down": lambda: _gemm_ar(64, 4096, 14336),
     "attn_prefill_8x512": lambda: _prefill(8, 512),
     "attn_prefill_2x2048": lambda: _prefill(2, 2048),
+    "attn_prefill_warp_8x512": lambda: _prefill(8, 512, warp_kernel=True),
+    "attn_prefill_warp_2x2048": lambda: _prefill(2, 2048, warp_kernel=True),
+    "attn_fwd_dense_tc_8x512": lambda: _attn_fwd_dense_tc(8, 512),
+    "attn_bwd_tc_8x512": lambda: _attn_bwd(8, 512, tc=True),
     "attn_bwd_8x512": lambda: _attn_bwd(8, 512),
     "attn_bwd_torch_fp32_8x512": lambda: _attn_bwd(8, 512, torch_path=True),
     "attn_decode_64x1024": lambda: _decode(64, 1024),
