@@ -248,7 +248,7 @@ TOPICS = {
 }
 
 
-def _routing_engine(tmp, slots=2):
+def _routing_engine(tmp, slots=2, encoder=None):
     import torch
     from deltaserve_vllm_b200.adapters import peft_io
     from deltaserve_vllm_b200.adapters.routing import AdapterRouter
@@ -271,7 +271,8 @@ def _routing_engine(tmp, slots=2):
                         max_num_batched_tokens=256, max_loras=slots, max_lora_rank=8)
     rcfg = AdapterRoutingConfig(enable_adapter_routing=True, index_path=os.path.join(tmp, "index"),
                                 adapters=entries, route_min_pool=2, route_keep_percent=100.0,
-                                route_reference_samples=8, indexing_chunk_samples=4)
+                                route_reference_samples=8, indexing_chunk_samples=4,
+                                **({"encoder": encoder, "encoder_query_prefix": "query: "} if encoder else {}))
     eng = CoServingEngine(ecfg, FinetuneConfig(enable_finetuning=False), rcfg,
                           tokenizer=ByteTokenizer(arch.vocab))
     eng.router = AdapterRouter(eng, rcfg)
@@ -395,3 +396,39 @@ def test_router_cancel_drops_pending_request(tmp_path):
     assert fut.cancelled() and not keep.done()
     assert [p[0] for p in eng.router.pending] == ["kept"]
     assert not eng.abort_request("gone")
+
+
+def test_routing_with_a_sentence_encoder_directory():
+    """The Hugging Face encoder path end to end on CPU: a local encoder
+    directory (a random 2-layer BERT whose vocabulary covers the topics)
+    selects SentenceEncoder; indexing runs it in the CPU encoder process;
+    a request carrying one of a topic's own samples routes to that topic."""
+    import time
+    import torch
+    from transformers import BertConfig, BertModel, BertTokenizerFast
+    from deltaserve_vllm_b200.adapters.routing.encoder import SentenceEncoder
+    with tempfile.TemporaryDirectory() as tmp:
+        enc_dir = os.path.join(tmp, "encoder")
+        words = ["[PAD]", "[UNK]", "[CLS]", "[SEP]", "[MASK]", "query", ":"]
+        for texts in TOPICS.values():
+            for t in texts:
+                words += [w for w in t.split() if w not in words]
+        BertTokenizerFast(vocab={w: i for i, w in enumerate(words)}).save_pretrained(enc_dir)
+        torch.manual_seed(0)
+        BertModel(BertConfig(vocab_size=len(words), hidden_size=64, num_hidden_layers=2, num_attention_heads=2,
+                             intermediate_size=128, max_position_embeddings=64)).save_pretrained(enc_dir)
+        eng = _routing_engine(tmp, slots=2, encoder=enc_dir)
+        assert isinstance(eng.router.encoder, SentenceEncoder)
+        t0 = time.time()
+        while eng.router.indexing and time.time() - t0 < 120:
+            eng.router.tick()
+            time.sleep(0.02)
+        assert sorted(eng.router.pool.routable_names()) == sorted(TOPICS)
+        svc = eng.router.indexer_service.describe()
+        assert svc["executors"]["cpu"]["running"] and svc["executors"]["cpu"]["priority"] in ("SCHED_IDLE", "nice 19")
+        hits = 0
+        for name, texts in TOPICS.items():
+            d = eng.router.router.route_many([texts[0]])[0]
+            hits += d.adapter == name
+        assert hits >= 3, hits
+        eng.close()
