@@ -112,8 +112,9 @@ def _install_grant_checks(encoder, grant: IndexGrant) -> int:
     return len(layers)
 
 
-def _child_main(conn, encoder, device: str, shared, grant, cpus, low_priority: bool) -> None:
-    """The indexing process: build the encoder, then answer
+def _child_main(conn, encoder, device: str, shared: bool, grant, cpus, low_priority: bool) -> None:
+    """The indexing process: build the encoder (with ``shared``, around the
+    tensors that arrive as the pipe's first message), then answer
     ``("encode", seq, texts, threads)`` with ``("ok", seq, embeddings)``,
     ``("preempted", seq)`` or ``("error", seq, message)`` until ``("stop",)``
     or until the serving process goes away (the pipe closes)."""
@@ -121,11 +122,12 @@ def _child_main(conn, encoder, device: str, shared, grant, cpus, low_priority: b
         prio = lower_priority() if low_priority else "unchanged"
         if cpus:
             os.sched_setaffinity(0, cpus)
-        if shared is not None:
+        if shared:
             from .encoder import SentenceEncoder
-            config, state = shared
+            _, config, state = conn.recv()
             encoder = SentenceEncoder.from_shared(encoder.path, encoder.prefix, encoder.max_tokens,
                                                   device, config, state)
+            del state
         else:
             if hasattr(encoder, "device"):
                 encoder.device = device
@@ -136,6 +138,21 @@ def _child_main(conn, encoder, device: str, shared, grant, cpus, low_priority: b
         conn.send(("error", 0, f"{type(e).__name__}: {e}"))
         return
     conn.send(("ready", os.getpid(), {"priority": prio, "layers_checked": checked, "device": device}))
+    try:
+        _serve(conn, encoder, grant)
+    finally:
+        # Drop every reference to tensors received from the parent before the
+        # process ends (they live only in this frame and the encoder), so the
+        # parent's CUDA IPC bookkeeping sees them released.
+        encoder = None
+        import gc
+        gc.collect()
+        if shared and str(device).startswith("cuda"):
+            import torch
+            torch.cuda.synchronize()
+
+
+def _serve(conn, encoder, grant) -> None:
     threads_now = 0
     while True:
         try:
@@ -202,11 +219,13 @@ class EncoderProcess:
         ctx = tmp.get_context("spawn")
         parent, child = ctx.Pipe()
         self._proc = ctx.Process(target=_child_main, name=f"dsv-indexer-{self.name}", daemon=True,
-                                 args=(child, self.encoder, self.device, self.shared, self.grant,
+                                 args=(child, self.encoder, self.device, self.shared is not None, self.grant,
                                        self.cpus, self.low_priority))
         self._proc.start()
         child.close()
         self._conn = parent
+        if self.shared is not None:
+            parent.send(("state", *self.shared))
         if not parent.poll(self.start_timeout_s):
             self.stop()
             raise RuntimeError(f"the {self.name} indexing process did not come up")
@@ -293,6 +312,9 @@ class EncoderProcess:
                 proc.join(timeout=3.0)
         if conn is not None:
             conn.close()
+        if proc is not None and str(self.device).startswith("cuda"):
+            import torch
+            torch.cuda.ipc_collect()       # release the tensors the child held
 
     def describe(self) -> dict:
         return {"name": self.name, "device": self.device, "running": self.ready, **self.info}

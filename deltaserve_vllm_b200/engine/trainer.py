@@ -190,7 +190,11 @@ class LoraTrainer:
         if saved["qkv"] is None:
             saved["qkv"] = self.bwd.recompute_qkv_raw(l, saved["layer_in"])
         if saved["ctx"] is None:
-            saved["ctx"] = self.bwd.recompute_ctx(l, saved["qkv"], ci, pos, self.cos_sin)
+            # The tcgen05 recompute also leaves the row log-sum-exp, which the
+            # attention backward reuses instead of running the forward again.
+            lse = self.bwd.attn_stats(ci.n_pad, saved["qkv"].device)[0] if self.bwd.tc_attention(saved["qkv"]) else None
+            saved["ctx"] = self.bwd.recompute_ctx(l, saved["qkv"], ci, pos, self.cos_sin, lse=lse)
+            saved["lse"] = lse
         if saved["resid_mid"] is None:
             saved["resid_mid"] = self.bwd.recompute_resid_mid(l, saved["layer_in"], saved["ctx"])
         if self.diag_cycles > 0 and self.step < self.diag_cycles:

@@ -718,6 +718,11 @@ class LoraBackward:
             self._r32 = [torch.zeros(rows, self.arch.hidden, dtype=torch.float32, device=device) for _ in range(2)]
         return [t[:n] for t in self._r32]
 
+    @staticmethod
+    def tc_attention(t: torch.Tensor) -> bool:
+        """Whether the attention of tensors like ``t`` runs on the tcgen05 kernels."""
+        return ops.ATTN_TC and t.is_cuda
+
     def attn_stats(self, n: int, device) -> tuple[torch.Tensor, torch.Tensor]:
         """(lse, dd) fp32 [Hq, rows] scratch of the tcgen05 attention: the
         forward's row log-sum-exp and the backward's rowsum(dO * O), indexed
@@ -860,7 +865,7 @@ class LoraBackward:
             self._mark("norm_bwd_mid")
         # ---- attention ---------------------------------------------------
         dz_o = self.group_dz(layer, "o", d_mid_c)
-        tc_attn = ops.ATTN_TC and x.is_cuda
+        tc_attn = self.tc_attention(x)
         d_ctx = self.dx_gemm(layer, "o", d_mid_c, lw.o, dz_o, bf16_out=tc_attn)      # [n, q_l]
         self._mark("o_dx")
         qh, kh, vh = self.recompute_qkv(qkv_raw, positions, lw, cos_sin)

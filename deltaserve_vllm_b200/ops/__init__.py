@@ -226,7 +226,7 @@ def attn_bwd(q, k, v, d_o, tiles, scale, *, rope=None, dqkv=None, bf16_mask=0, o
             g = g.to(torch.bfloat16)
         if o is None or lse is None:
             o = torch.empty(n, hq * hd, dtype=torch.bfloat16, device=dev)
-            lse = torch.empty(hq, n, dtype=torch.float32, device=dev)
+            lse = torch.empty_like(dd) if dd is not None else torch.empty(hq, n, dtype=torch.float32, device=dev)
             _native().attn_fwd_dense_tc(q, k, v, tiles128, o, hq, hkv, scale, lse, None, None)
         if dd is None:
             dd = torch.empty_like(lse)
