@@ -289,6 +289,11 @@ CASES = {
     "attn_prefill_warp_2x2048": lambda: _prefill(2, 2048, warp_kernel=True),
     "attn_fwd_dense_tc_8x512": lambda: _attn_fwd_dense_tc(8, 512),
     "attn_bwd_tc_8x512": lambda: _attn_bwd(8, 512, tc=True),
+    # one TP = 8 rank's share of the same attention: 4 query heads, 1 KV head
+    "attn_prefill_8x512_tp8": lambda: _prefill(8, 512, Hq=4, Hkv=1),
+    "attn_fwd_dense_tc_8x512_tp8": lambda: _attn_fwd_dense_tc(8, 512, Hq=4, Hkv=1),
+    "attn_bwd_tc_8x512_tp8": lambda: _attn_bwd(8, 512, Hq=4, Hkv=1, tc=True),
+    "attn_bwd_8x512_tp8": lambda: _attn_bwd(8, 512, Hq=4, Hkv=1),
     "attn_bwd_8x512": lambda: _attn_bwd(8, 512),
     "attn_bwd_torch_fp32_8x512": lambda: _attn_bwd(8, 512, torch_path=True),
     "attn_decode_64x1024": lambda: _decode(64, 1024),
