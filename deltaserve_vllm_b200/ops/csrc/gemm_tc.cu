@@ -1372,6 +1372,29 @@ static void launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtens
 }
 
 // Pair tiles pay off once there are enough of them to occupy the GPU.
+// Split-K factor for a GEMM of `tiles` output tiles and `kbs` K-blocks on
+// `sms` persistent CTAs. The (tile, split) units are dealt round-robin, so
+// the kernel lasts about ceil(units / sms) units of (kbs / splits) K-blocks;
+// each split beyond the first adds a little fp32 partial traffic (weighted
+// 4 % per split here). Every split keeps at least 4 K-blocks and none is empty.
+static int balanced_splits(int tiles, int kbs, int sms, int max_splits) {
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= max_splits; ++s) {
+    if (s > 1 && kbs / s < 4) break;
+    const int per = (kbs + s - 1) / s;
+    const int sp = (kbs + per - 1) / per;
+    const int64_t units = (int64_t)tiles * sp;
+    const int64_t rounds = (units + sms - 1) / sms;
+    const double cost = (double)rounds * per * (1.0 + 0.04 * (sp - 1));
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
+  return best;
+}
+
 static bool use_pair(int M, int N, int epi, bool b_mn, int bn, int splits, int64_t force_bn, int64_t max_ctas) {
   static int mode = -1;  // DSV_GEMM_PAIR=0 disables the pair kernel (1-CTA tiles everywhere)
   if (mode < 0) {
@@ -1454,12 +1477,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
     const int bnt = M <= 64 ? 64 : 128;
     const int tiles = (N + BM - 1) / BM;
     const int kbs = (K + BK - 1) / BK;
-    int splits = 1;
-    if (tiles < num_sms() && kbs >= 8) {
-      splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
-      const int per = (kbs + splits - 1) / splits;
-      splits = (kbs + per - 1) / per;
-    }
+    const int splits = kbs >= 8 ? balanced_splits(tiles, kbs, num_sms(), 16) : 1;
     GemmArgs args{};
     args.M = N;
     args.N = M;
@@ -1519,7 +1537,10 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
     if (!b_mn && m_t == 1 && max_ctas == 0 && force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
     if (uncapped && epi != kEpiSwiGLUBwd && !special) {
       const int tiles = m_t * ((N + bn - 1) / bn);
-      if (tiles < num_sms() / 2 && kbs >= 8) {
+      if (m_t == 1 && kbs >= 8) {
+        // one M tile (decode): balance the units over the persistent CTAs
+        splits = balanced_splits(tiles, kbs, num_sms(), 16);
+      } else if (tiles < num_sms() / 2 && kbs >= 8) {
         splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
         const int per = (kbs + splits - 1) / splits;
         splits = (kbs + per - 1) / per;  // no empty split

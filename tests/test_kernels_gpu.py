@@ -622,6 +622,18 @@ def test_gemm_splitk_swiglu_lora_save(M):
     torch.testing.assert_close(save[:M - 1].float(), acc[1:M], rtol=2e-2, atol=3e-2)
 
 
+def test_gemm_decode_gateup_full_width_swiglu():
+    """The decode gate_up at Llama-3-8B width (224 output tiles: split so the
+    (tile, split) units fill the persistent CTAs evenly; SwiGLU applied by the
+    split reduction) against fp32."""
+    M, K, I = 16, 4096, 14336
+    x, w = rnd(M, K, seed=51), rnd(2 * I, K, scale=0.02, seed=52)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out, epi=ops.EPI_SWIGLU)
+    g, u = ref.deinterleave64(x.float() @ w.float().t())
+    torch.testing.assert_close(out.float(), torch.nn.functional.silu(g) * u, rtol=3e-2, atol=3e-2)
+
+
 @pytest.mark.parametrize("T,D", [(50, 4096), (9, 5120), (7, 1024), (33, 8192), (301, 128), (5, 96), (3, 200)])
 def test_rms_norm_bwd_shapes(T, D):
     """Vector (one CTA per row), warp-per-row (q/k norms) and scalar paths."""
