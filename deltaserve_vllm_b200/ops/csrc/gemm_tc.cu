@@ -511,7 +511,44 @@ __device__ __forceinline__ void push_rows_tile(const GemmArgs& args, uint32_t t_
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_rows(const GemmArgs& args, uint32_t t_row, int row, bool row_ok, int n0,
                                               bool do_save) {
-  if constexpr (EPI == kEpiSwiGLU) {
+  if constexpr (EPI == kEpiSwiGLUBwd) {
+    // 32 d(act) columns at a time, all inside one 64-column block of the
+    // interleave: their gate columns start at (col / 64) * 128 + col % 64,
+    // the up columns 64 further.
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c, r);
+      tmem_ld_wait();
+      const int col = n0 + c;
+      if (!row_ok || col >= args.N) continue;
+      const int gcol = (col >> 6) * 128 + (col & 63);
+      const uint4* gp = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol);
+      const uint4* up = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol + 64);
+      float dg[32], du[32], act[32];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 gq = gp[v], uq = up[v];
+        const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gq);
+        const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uq);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = v * 8 + e;
+          const float g = bf2f(gb[e]), u = bf2f(ub[e]);
+          const float da = __uint_as_float(r[i]);
+          const float sg = 1.f / (1.f + __expf(-g));
+          const float silu = g * sg;
+          dg[i] = da * u * sg * (1.f + g * (1.f - sg));
+          du[i] = da * silu;
+          act[i] = silu * u;
+        }
+      }
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + gcol;
+      store_row_bf16(dst, dg, 32);
+      store_row_bf16(dst + 64, du, 32);
+      if (args.aux_out != nullptr) store_row_bf16(args.aux_out + (size_t)row * args.ld_aux_out + col, act, 32);
+    }
+  } else if constexpr (EPI == kEpiSwiGLU) {
     // Columns come interleaved in blocks of 64: [gate(64) | up(64)] per 128.
 #pragma unroll 1
     for (int c = 0; c < BN; c += 128) {
@@ -913,43 +950,6 @@ __global__ void __launch_bounds__(256, 1)
             for (int zc = PR + j; zc < SEG; zc += PR) zr[sl * SEG + zc] = f2bf(0.f);
           }
         }
-      } else if constexpr (EPI == kEpiSwiGLUBwd) {
-        // 32 d(act) columns at a time, all inside one 64-column block of the
-        // interleave: their gate columns start at (col / 64) * 128 + col % 64,
-        // the up columns 64 further.
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + c, r);
-          tmem_ld_wait();
-          const int col = n0 + c;
-          if (!row_ok || col >= args.N) continue;
-          const int gcol = (col >> 6) * 128 + (col & 63);
-          const uint4* gp = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol);
-          const uint4* up = reinterpret_cast<const uint4*>(args.aux + (size_t)row * args.ld_aux + gcol + 64);
-          float dg[32], du[32], act[32];
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint4 gq = gp[v], uq = up[v];
-            const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gq);
-            const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uq);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int i = v * 8 + e;
-              const float g = bf2f(gb[e]), u = bf2f(ub[e]);
-              const float da = __uint_as_float(r[i]);
-              const float sg = 1.f / (1.f + __expf(-g));
-              const float silu = g * sg;
-              dg[i] = da * u * sg * (1.f + g * (1.f - sg));
-              du[i] = da * silu;
-              act[i] = silu * u;
-            }
-          }
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + gcol;
-          store_row_bf16(dst, dg, 32);
-          store_row_bf16(dst + 64, du, 32);
-          if (args.aux_out != nullptr) store_row_bf16(args.aux_out + (size_t)row * args.ld_aux_out + col, act, 32);
-        }
       } else {
         epilogue_rows<BN, EPI>(args, t_row, row, row_ok, n0, do_save);
       }
@@ -1000,7 +1000,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                         const __grid_constant__ CUtensorMap tmZ, const __grid_constant__ CUtensorMap tmB2,
                         GemmArgs args) {
   static_assert(EPI == kEpiBF16 || EPI == kEpiF32 || EPI == kEpiF32Accum || EPI == kEpiSwiGLU ||
-                    EPI == kEpiCEStats || EPI == kEpiCEGrad || EPI == kEpiPushRows,
+                    EPI == kEpiCEStats || EPI == kEpiCEGrad || EPI == kEpiPushRows || EPI == kEpiSwiGLUBwd,
                 "pair GEMM: row-wise epilogues only");
   using Cfg = GemmCfgPair<BN, B_MN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -1403,7 +1403,7 @@ static bool use_pair(int M, int N, int epi, bool b_mn, int bn, int splits, int64
   }
   if (mode == 0 || splits != 1 || bn != 256 || force_bn != 0) return false;
   if (!(epi == kEpiBF16 || epi == kEpiF32 || epi == kEpiF32Accum || (epi == kEpiSwiGLU && !b_mn) ||
-        ((epi == kEpiCEStats || epi == kEpiCEGrad) && !b_mn) || (epi == kEpiPushRows && b_mn)))
+        ((epi == kEpiCEStats || epi == kEpiCEGrad) && !b_mn) || ((epi == kEpiPushRows || epi == kEpiSwiGLUBwd) && b_mn)))
     return false;
   if (max_ctas > 0 && max_ctas < num_sms()) return false;
   const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
@@ -1537,10 +1537,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
     if (!b_mn && m_t == 1 && max_ctas == 0 && force_bn == 0 && bn == 64 && epi != kEpiSwiGLU) bn = 128;
     if (uncapped && epi != kEpiSwiGLUBwd && !special) {
       const int tiles = m_t * ((N + bn - 1) / bn);
-      if (m_t == 1 && kbs >= 8) {
-        // one M tile (decode): balance the units over the persistent CTAs
-        splits = balanced_splits(tiles, kbs, num_sms(), 16);
-      } else if (tiles < num_sms() / 2 && kbs >= 8) {
+      if (tiles < num_sms() / 2 && kbs >= 8) {
         splits = std::max(1, std::min({num_sms() / tiles, kbs / 4, 16}));
         const int per = (kbs + splits - 1) / splits;
         splits = (kbs + per - 1) / per;  // no empty split
@@ -1616,6 +1613,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
       if (epi == kEpiBF16) launch_pair<true, kEpiBF16>(ta, tb, tz, tb2, args, s);
       else if (epi == kEpiF32) launch_pair<true, kEpiF32>(ta, tb, tz, tb2, args, s);
       else if (epi == kEpiPushRows) launch_pair<true, kEpiPushRows>(ta, tb, tz, tb2, args, s);
+      else if (epi == kEpiSwiGLUBwd) launch_pair<true, kEpiSwiGLUBwd>(ta, tb, tz, tb2, args, s);
       else launch_pair<true, kEpiF32Accum>(ta, tb, tz, tb2, args, s);
     } else {
       if (epi == kEpiBF16) launch_pair<false, kEpiBF16>(ta, tb, tz, tb2, args, s);

@@ -124,44 +124,71 @@ __global__ void __launch_bounds__(SHR_THREADS) lora_shrink_kernel(const __nv_bfl
   }
 }
 
-// Small-batch shrink (decode): one warp per (row, output column) pair does the
-// whole K-long dot product with 16-byte loads of the x row and the A row (both
-// L2-resident), so a 16-row step still spreads over T*P*R warps. The warp of
-// output 0 also writes the row's zero columns.
+// Small-batch shrink (decode): one CTA per (row, block of 8 output columns).
+// Its 8 warps split the K range; each warp loads its slice of the x row once
+// per 256 elements and the 8 A rows of the block alongside it (9 independent
+// 16-byte loads in flight per lane), keeping 8 running dot products; the 8
+// warps' partials meet in shared memory and warp 0 writes the 8 outputs. The
+// CTA of block 0 also writes the row's zero columns. (One warp per output with
+// the whole K serial was latency-bound: ~16 us per call at decode sizes.)
+constexpr int SHV_OUT = 8;
 __global__ void __launch_bounds__(256) lora_shrink_gemv_kernel(const __nv_bfloat16* __restrict__ x, int sx,
                                                                const __nv_bfloat16* __restrict__ A,
                                                                const int* __restrict__ slot_ids, __nv_bfloat16* Z,
                                                                int sz, int T, int K, int PR, int SEG, int slots) {
+  __shared__ float part[8][SHV_OUT];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int pair = blockIdx.x * 8 + warp;
-  if (pair >= T * PR) return;
-  const int row = pair / PR, o = pair % PR;
+  const int row = blockIdx.x;
+  const int o0 = blockIdx.y * SHV_OUT;
   const int s = slot_ids[row];
-  if (o == 0) {
+  if (blockIdx.y == 0) {
     const int W = slots * SEG;
-    for (int c = lane; c < W; c += 32) {
+    for (int c = threadIdx.x; c < W; c += blockDim.x) {
       if (s >= 0 && c >= s * SEG && c < s * SEG + PR) continue;
       Z[(size_t)row * sz + c] = f2bf(0.f);
     }
   }
   if (s < 0) return;
+  // K range of this warp: whole 256-element steps, split as evenly as possible.
+  const int steps = (K + 255) / 256;
+  const int per = (steps + 7) / 8;
+  const int k_lo = warp * per * 256, k_hi = min(K, (warp + 1) * per * 256);
   const __nv_bfloat16* xr = x + (size_t)row * sx;
-  const __nv_bfloat16* ar = A + ((size_t)s * PR + o) * K;
-  float d = 0.f;
-  for (int k = lane * 8; k < K; k += 256) {
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
-    const uint4 av = *reinterpret_cast<const uint4*>(ar + k);
-    const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
-    const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&av);
+  const __nv_bfloat16* ab = A + ((size_t)s * PR + o0) * K;
+  const int n_out = min(SHV_OUT, PR - o0);
+  float d[SHV_OUT];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 xf = __bfloat1622float2(xh[e]);
-      const float2 af = __bfloat1622float2(ah[e]);
-      d += xf.x * af.x + xf.y * af.y;
+  for (int j = 0; j < SHV_OUT; ++j) d[j] = 0.f;
+  for (int k = k_lo + lane * 8; k < k_hi; k += 256) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+    uint4 av[SHV_OUT];
+#pragma unroll
+    for (int j = 0; j < SHV_OUT; ++j)
+      av[j] = j < n_out ? *reinterpret_cast<const uint4*>(ab + (size_t)j * K + k) : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+    for (int j = 0; j < SHV_OUT; ++j) {
+      const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&av[j]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 xf = __bfloat1622float2(xh[e]);
+        const float2 af = __bfloat1622float2(ah[e]);
+        d[j] += xf.x * af.x + xf.y * af.y;
+      }
     }
   }
-  d = warp_sum(d);
-  if (lane == 0) Z[(size_t)row * sz + s * SEG + o] = f2bf(d);
+#pragma unroll
+  for (int j = 0; j < SHV_OUT; ++j) {
+    const float v = warp_sum(d[j]);
+    if (lane == 0) part[warp][j] = v;
+  }
+  __syncthreads();
+  if (warp == 0 && lane < n_out) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += part[w][lane];
+    Z[(size_t)row * sz + s * SEG + o0 + lane] = f2bf(v);
+  }
 }
 
 // Vocab-parallel embedding: ids outside [v0, v0 + Vl) give zero rows (the TP
@@ -467,8 +494,8 @@ void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, t
   TORCH_CHECK(A.size(2) == K && K % 8 == 0 && PR <= SHR_MAXPR && PR <= seg, "lora_shrink: shapes");
   TORCH_CHECK(Z.size(1) == slots * seg && Z.size(0) >= T, "lora_shrink: Z shape");
   c10::cuda::CUDAGuard guard(x.device());
-  if (T * PR <= 64 * 192 && x.stride(0) % 8 == 0) {
-    const int blocks = (T * PR + 7) / 8;
+  if (T * PR <= 64 * 192 && x.stride(0) % 8 == 0 && (uintptr_t)x.data_ptr() % 16 == 0 && A.is_contiguous()) {
+    const dim3 blocks((unsigned)T, (unsigned)((PR + SHV_OUT - 1) / SHV_OUT));
     lora_shrink_gemv_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),

@@ -177,6 +177,22 @@ def test_gemm_swiglu_save(M):
     assert save[:7].abs().sum() == 0
 
 
+@pytest.mark.parametrize("T,K,P,R,slots", [(1, 4096, 3, 16, 2), (16, 4096, 3, 16, 2), (16, 14336, 1, 16, 2),
+                                             (64, 4096, 2, 16, 4), (13, 1000, 3, 8, 3), (40, 4096, 1, 64, 2)])
+def test_lora_shrink_decode_sizes(T, K, P, R, slots):
+    """The decode shrink (K split over a CTA's warps): every row's own slot
+    segment against fp32, the other slots' columns and the padding zero."""
+    seg = -(-P * R // 64) * 64
+    x = rnd(T, K, seed=61)
+    A = rnd(slots, P * R, K, scale=0.05, seed=62)
+    sid = torch.randint(-1, slots, (T,), device=DEV, dtype=torch.int32, generator=torch.Generator(device=DEV).manual_seed(63))
+    Z = torch.full((T, slots * seg), 9.0, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, sid, Z, seg)
+    Zr = torch.empty_like(Z).cpu()
+    ref.lora_shrink(x.cpu().float(), A.cpu().float(), sid.cpu(), Zr, seg)
+    torch.testing.assert_close(Z.float().cpu(), Zr.float(), rtol=2e-2, atol=2e-2)
+
+
 def test_gemm_lora_expand_segmented():
     M, N, K, slots, P, R = 300, 384, 256, 4, 3, 16
     seg = 64
@@ -423,10 +439,11 @@ def test_attn_bwd_tc_rope_epilogue_matches_warp_kernels():
     assert (b[used:] == 7.0).all()
 
 
-def test_gemm_swiglu_bwd_epilogue():
+@pytest.mark.parametrize("M,K,I", [(300, 512, 640), (2048, 1024, 4608)])
+def test_gemm_swiglu_bwd_epilogue(M, K, I):
     """d(act) GEMM (MN-major, with the LoRA K block) whose epilogue applies the
-    SwiGLU backward == fp32 product then the SwiGLU backward reference."""
-    M, K, I = 300, 512, 640
+    SwiGLU backward == fp32 product then the SwiGLU backward reference (the
+    second shape has enough 256 x 256 tiles for the CTA-pair kernel)."""
     a = rnd(M, K, seed=40)
     w = rnd(K, I, scale=0.05, seed=41)
     gu = rnd(M, 2 * I, seed=42)
@@ -623,9 +640,8 @@ def test_gemm_splitk_swiglu_lora_save(M):
 
 
 def test_gemm_decode_gateup_full_width_swiglu():
-    """The decode gate_up at Llama-3-8B width (224 output tiles: split so the
-    (tile, split) units fill the persistent CTAs evenly; SwiGLU applied by the
-    split reduction) against fp32."""
+    """The decode gate_up at Llama-3-8B width (224 output tiles of one M tile)
+    against fp32."""
     M, K, I = 16, 4096, 14336
     x, w = rnd(M, K, seed=51), rnd(2 * I, K, scale=0.02, seed=52)
     out = torch.empty(M, I, dtype=torch.bfloat16, device=DEV)
