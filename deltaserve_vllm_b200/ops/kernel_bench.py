@@ -307,6 +307,8 @@ CASES = {
     "gemm_dx_down_swiglu_bwd": lambda: _dx_gemm(4096, 4096, 14336, True),
     "swiglu_bwd_4096x14336": lambda: _swiglu_bwd(4096, 14336),
     "lora_shrink_4096x4096_r16x3": lambda: _shrink(4096, 4096, 48),
+    "lora_shrink_decode_16x4096_r16x3": lambda: _shrink(16, 4096, 48),
+    "lora_shrink_decode_16x14336_r16": lambda: _shrink(16, 14336, 16),
     "rope_kvwrite_4096": lambda: _rope(4096),
     "ce_fwd_bwd_512x128256": lambda: _ce(512, 128256),
     "adamw_64M": lambda: _adamw(64 << 20),
