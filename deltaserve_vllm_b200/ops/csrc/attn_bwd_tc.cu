@@ -319,17 +319,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       tc_fence_after();
       const int lim = min(qi + 1, len) - j * 64;  // keys [j*64, j*64 + lim) are visible to this row
       uint8_t* ds_tile = sDS + b * AT_C128;
+      uint32_t x[2][32], y[2][32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t x[32], y[32];
-        tmem_ld_32x32b_x32(t_lane + b * 64 + c * 32, x);
-        tmem_ld_32x32b_x32(t_lane + 128 + b * 64 + c * 32, y);
-        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_lane + b * 64 + c * 32, x[c]);
+        tmem_ld_32x32b_x32(t_lane + 128 + b * 64 + c * 32, y[c]);
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         float ds[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float p = (c * 32 + i < lim) ? fast_exp2(__uint_as_float(x[i]) * a.scale_log2 - lse_r) : 0.f;
-          ds[i] = p * (__uint_as_float(y[i]) - d_r);
+          const float p = (c * 32 + i < lim) ? fast_exp2(fmaf(__uint_as_float(x[c][i]), a.scale_log2, -lse_r)) : 0.f;
+          ds[i] = p * (__uint_as_float(y[c][i]) - d_r);
         }
         store_row_units(ds_tile, r, c * 4, ds);
       }
@@ -525,19 +528,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       const int q0 = k0 + (it % nq) * 64;
       const int first = kpos - q0;              // queries q0 + i with i >= first see this key
       const float* sl = stats + st * 128;
+      uint32_t x[2][32], y[2][32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t x[32], y[32];
-        tmem_ld_32x32b_x32(t_lane + st * 64 + c * 32, x);
-        tmem_ld_32x32b_x32(t_lane + 128 + st * 64 + c * 32, y);
-        tmem_ld_wait();
+        tmem_ld_32x32b_x32(t_lane + st * 64 + c * 32, x[c]);
+        tmem_ld_32x32b_x32(t_lane + 128 + st * 64 + c * 32, y[c]);
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         float p[32], ds[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int qq = c * 32 + i;
-          const float pv = qq >= first ? fast_exp2(__uint_as_float(x[i]) * a.scale_log2 - sl[qq]) : 0.f;
+          const float pv = qq >= first ? fast_exp2(fmaf(__uint_as_float(x[c][i]), a.scale_log2, -sl[qq])) : 0.f;
           p[i] = pv;
-          ds[i] = pv * (__uint_as_float(y[i]) - sl[64 + qq]);
+          ds[i] = pv * (__uint_as_float(y[c][i]) - sl[64 + qq]);
         }
         store_row_units(sPt + st * AT_C128, r, c * 4, p);
         store_row_units(sDSt + st * AT_C128, r, c * 4, ds);

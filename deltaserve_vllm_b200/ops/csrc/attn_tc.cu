@@ -270,38 +270,53 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       const int st = j & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (uint32_t)(j >> 1) & 1u, kErrFaS))) { ok = false; break; }
       tc_fence_after();
+      // All four 32-column loads in flight before one wait; scores stay raw
+      // (the scale is folded into the exponent's FMA below).
       float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_lane + st * 128 + c * 32, v);
+      {
+        uint32_t v0[32], v1[32], v2[32], v3[32];
+        tmem_ld_32x32b_x32(t_lane + st * 128 + 0, v0);
+        tmem_ld_32x32b_x32(t_lane + st * 128 + 32, v1);
+        tmem_ld_32x32b_x32(t_lane + st * 128 + 64, v2);
+        tmem_ld_32x32b_x32(t_lane + st * 128 + 96, v3);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(v[i]) * a.scale_log2;
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(v0[i]);
+          s[32 + i] = __uint_as_float(v1[i]);
+          s[64 + i] = __uint_as_float(v2[i]);
+          s[96 + i] = __uint_as_float(v3[i]);
+        }
       }
       tc_fence_before();
       mbar_arrive(&s_empty[st]);
       const int key0 = j * FA_ROWS;
       const int lim = min(qpos + 1, kv_end) - key0;        // keys [key0, key0 + lim) are visible
-      float mx = m;
       if (lim < FA_ROWS) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 128; ++i)
           if (i >= lim) s[i] = -INFINITY;
-          mx = fmaxf(mx, s[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, s[i]);
       }
+      // Row max and sum as 8 independent chains (a single 128-long chain of
+      // dependent max / add instructions dominated the loop).
+      float red[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) red[c] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) red[i & 7] = fmaxf(red[i & 7], s[i]);
+      const float tile_max = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
+                                   fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+      const float mx = fmaxf(m, tile_max * a.scale_log2);  // running max, base-2 scaled domain
       const float corr = (m == -INFINITY) ? 0.f : fast_exp2(m - mx);
       const float mref = (mx == -INFINITY) ? 0.f : mx;
-      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) red[c] = 0.f;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        s[i] = fast_exp2(s[i] - mref);
-        sum += s[i];
+        s[i] = fast_exp2(fmaf(s[i], a.scale_log2, -mref));
+        red[i & 7] += s[i];
       }
+      const float sum = ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
       l = l * corr + sum;
       m = mx;
       if (j > 0) {
@@ -320,13 +335,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
       if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_lane + FA_O_COL + c * 32, v);
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(t_lane + FA_O_COL + c * 32, v0);
+          tmem_ld_32x32b_x32(t_lane + FA_O_COL + (c + 1) * 32, v1);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * corr);
-          tmem_st_32x32b_x32(t_lane + FA_O_COL + c * 32, v);
+          for (int i = 0; i < 32; ++i) {
+            v0[i] = __float_as_uint(__uint_as_float(v0[i]) * corr);
+            v1[i] = __float_as_uint(__uint_as_float(v1[i]) * corr);
+          }
+          tmem_st_32x32b_x32(t_lane + FA_O_COL + c * 32, v0);
+          tmem_st_32x32b_x32(t_lane + FA_O_COL + (c + 1) * 32, v1);
         }
         tmem_st_wait();
       }
