@@ -22,6 +22,7 @@ gate_up GEMM with SwiGLU epilogue (+LoRA) -> down GEMM (+LoRA) -> all-reduce.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -31,6 +32,10 @@ from ..ops import EPI_BF16, EPI_F32, EPI_SWIGLU
 from .configs import ModelArch
 from .lora import LoraServeBuffers
 from .weights import ModelWeights
+
+# Launch each LoRA GEMM to overlap the shrink kernel right before it (its base
+# K blocks stream while the shrink runs); DSV_OVERLAP_SHRINK=0 serialises them.
+OVERLAP_SHRINK = os.environ.get("DSV_OVERLAP_SHRINK", "1") != "0"
 
 
 @dataclass
@@ -140,7 +145,8 @@ class DecoderModel:
             seg = self.lora.seg[group]
             z = torch.empty(x.shape[0], A.shape[0] * seg, dtype=x.dtype, device=x.device)
             ops.lora_shrink(x, A, b.slot_ids, z, seg)
-            kw = dict(z=z, b2=self.lora.B2[layer][group], tile_slots=b.tile_slots, lora_seg=seg)
+            kw = dict(z=z, b2=self.lora.B2[layer][group], tile_slots=b.tile_slots, lora_seg=seg,
+                      after_shrink=OVERLAP_SHRINK)
         return ops.gemm(x, w, out, epi=epi, save=save, save_lo=save_lo, save_hi=save_hi,
                         save_dst=save_dst, **kw)
 

@@ -58,7 +58,7 @@ def check_device_error(clear: bool = True) -> int:
 
 def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=None,
          lora_seg=0, save=None, save_lo=0, save_hi=0, save_dst=0, force_bn=0, max_ctas=0,
-         aux=None, aux_out=None):
+         aux=None, aux_out=None, after_shrink=False):
     """``out = a @ b.T`` (``b`` is [N, K]) or ``a @ b`` (``b_mn``: ``b`` is [K, N]),
     plus the segmented LoRA expand ``z @ b2.T`` and the epilogue ``epi``:
     bf16 / fp32 store, fp32 accumulate, SwiGLU over 64-interleaved gate/up
@@ -66,10 +66,16 @@ def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=Non
     product is d(act), ``aux`` the saved interleaved gate/up [M, 2N], ``out``
     receives their gradient [M, 2N] and ``aux_out`` (optional) the activation.
     ``save`` receives raw accumulator rows [save_lo, save_hi).
-    ``max_ctas`` > number of SMs launches one CTA per tile (non-persistent)."""
+    ``max_ctas`` > number of SMs launches one CTA per tile (non-persistent).
+    ``after_shrink``: the kernel right before this call in the stream is the
+    :func:`lora_shrink` that wrote ``z`` (and nothing this GEMM reads came from
+    a later-pending kernel): the GEMM is then launched to overlap it, streaming
+    its base K blocks while the shrink runs and waiting for it only before the
+    LoRA blocks (programmatic dependent launch)."""
     if a.is_cuda:
         _native().gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save,
-                       save_lo, save_hi, save_dst, force_bn, max_ctas, aux, aux_out)
+                       save_lo, save_hi, save_dst, force_bn, max_ctas, aux, aux_out,
+                       bool(after_shrink and z is not None))
         return out
     return ref.gemm(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi,
                     save_dst, aux=aux, aux_out=aux_out)

@@ -5,7 +5,7 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
               int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
-              c10::optional<torch::Tensor> aux_out);
+              c10::optional<torch::Tensor> aux_out, bool overlap_prev);
 void dsv_rms_norm_bwd(torch::Tensor x, torch::Tensor dy, torch::Tensor w, c10::optional<torch::Tensor> add,
                       torch::Tensor dx, c10::optional<torch::Tensor> dx_bf, double eps);
 void dsv_swiglu_bwd(torch::Tensor gu, torch::Tensor dact, torch::Tensor dgu, c10::optional<torch::Tensor> act);

@@ -186,6 +186,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A grid launched with programmatic stream serialization may start before the
+// grid ahead of it in the stream ends; griddep_wait() blocks the calling thread
+// until that grid has completed and its memory is visible. A grid that calls
+// griddep_launch_dependents() lets such a dependent be scheduled right away.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- CTA pairs
 // Pair MMA (tcgen05 cta_group::2) on a cluster of two CTAs: each CTA stages
 // half of A (its 128 rows) and half of B (its BN/2 columns); the even CTA

@@ -90,6 +90,10 @@ struct GemmArgs {
   int ld_save, save_lo, save_hi, save_dst;
   int max_ctas;           // host only: grid cap (0 = one CTA per SM, persistent)
   int k_splits;           // > 1: split-K, fp32 partials to `partial`, reduced by a second kernel
+  // Launched right after the LoRA shrink that writes Z, allowed to start before it
+  // ends: the producer waits for it (griddep_wait) before its first LoRA block, or
+  // at the end when none of its tiles has one (the grid never outlives the shrink).
+  int wait_prev;
   float* partial;         // [k_splits, M, N]
   PeerArgs peer;          // kEpiPeerAR only
   // kEpiShrink: B is the stacked LoRA A [slots * pr, K]; output column
@@ -773,12 +777,17 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     int fills[STAGES > 0 ? STAGES : 1];
     for (int s = 0; s < STAGES; ++s) fills[s] = 0;
+    bool dep_done = args.wait_prev == 0;
     for (int t = cta0; t < num_tiles && ok; t += ncta) {
       const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
       const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const uint32_t slots = tl.slots;
       const int n_lora = __popc(slots) * kb_per_slot;
       for (int j = 0; j < tl.n_main + n_lora; ++j) {
+        if (j == tl.n_main && !dep_done) {
+          griddep_wait();
+          dep_done = true;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
         uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
         uint8_t* sB = sA + Cfg::A_BYTES;
@@ -819,6 +828,7 @@ __global__ void __launch_bounds__(256, 1)
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
+    if (!dep_done) griddep_wait();
     // Drain: every copy this thread issued has landed before the CTA can exit.
     for (int s = 0; s < STAGES; ++s) {
       if (fills[s] == 0) continue;
@@ -1068,6 +1078,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     bool ok = true;
     int fills[STAGES];
     for (int s = 0; s < STAGES; ++s) fills[s] = 0;
+    bool dep_done = args.wait_prev == 0;
     for (int t = pair0; t < num_tiles && ok; t += npairs) {
       const int mt = t % num_m_tiles, nt = t / num_m_tiles;
       const int m0 = mt * 2 * BM + (int)rank * BM;
@@ -1075,6 +1086,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const uint32_t slots = tile_slots_of(mt);
       const int n_lora = __popc(slots) * kb_per_slot;
       for (int j = 0; j < kb_main + n_lora; ++j) {
+        if (j == kb_main && !dep_done) {
+          griddep_wait();
+          dep_done = true;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
         uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
         uint8_t* sB = sA + Cfg::A_BYTES;
@@ -1108,6 +1123,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
+    if (!dep_done) griddep_wait();
     // Drain (even CTA): its full barriers count both CTAs' copies, so once
     // they completed no copy of either CTA is in flight.
     if (rank == 0) {
@@ -1333,6 +1349,26 @@ static int num_sms() {
   return n;
 }
 
+// Launch with programmatic stream serialization (the kernel may start while
+// the previous grid in the stream still runs; it calls griddep_wait first
+// where it reads that grid's output).
+template <typename Kern>
+static void launch_overlapping(Kern kern, dim3 grid, int smem, cudaStream_t stream, const CUtensorMap& a,
+                               const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
+                               const GemmArgs& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, a, b, z, b2, args) == cudaSuccess, "dsv gemm: overlapping launch failed");
+}
+
 template <int BN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& z, const CUtensorMap& b2,
                    const GemmArgs& args, cudaStream_t stream) {
@@ -1349,7 +1385,11 @@ static void launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap
   // after one tile so a higher-priority stream can interleave at tile
   // granularity (used for the low-priority backward).
   const int grid = std::min(tiles, args.max_ctas > 0 ? args.max_ctas : num_sms());
-  kern<<<grid, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  if (args.wait_prev) {
+    launch_overlapping(kern, dim3(grid), Cfg::SMEM, stream, a, b, z, b2, args);
+  } else {
+    kern<<<grid, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1367,7 +1407,11 @@ static void launch_pair(const CUtensorMap& a, const CUtensorMap& b, const CUtens
   }
   const int tiles = ((args.M + 2 * BM - 1) / (2 * BM)) * ((args.N + 255) / 256);
   const int pairs = std::min(tiles, args.max_ctas > 0 ? std::max(1, args.max_ctas / 2) : num_sms() / 2);
-  kern<<<2 * pairs, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  if (args.wait_prev) {
+    launch_overlapping(kern, dim3(2 * pairs), Cfg::SMEM, stream, a, b, z, b2, args);
+  } else {
+    kern<<<2 * pairs, 256, Cfg::SMEM, stream>>>(a, b, z, b2, args);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1436,7 +1480,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
                           c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, c10::optional<torch::Tensor> save,
                           int64_t save_lo, int64_t save_hi, int64_t save_dst, int64_t force_bn, int64_t max_ctas,
                           c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> aux_out,
-                          const dsv::GemmArgs* extra) {
+                          const dsv::GemmArgs* extra, bool overlap_prev = false) {
   using namespace dsv;
   const bool special = epi == kEpiCEStats || epi == kEpiCEGrad || epi == kEpiPushRows;
   TORCH_CHECK(special == (extra != nullptr), "dsv_gemm: epilogue needs its own entry point");
@@ -1483,6 +1527,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
     args.N = M;
     args.K = K;
     args.k_splits = splits;
+    args.wait_prev = (overlap_prev && lora_seg > 0) ? 1 : 0;
     args.C = out.data_ptr();
     args.ldc = (int)out.stride(0);
     at::Tensor partial;
@@ -1546,6 +1591,7 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
   }
   GemmArgs args{};
   args.k_splits = splits;
+  args.wait_prev = (overlap_prev && lora_seg > 0) ? 1 : 0;
   at::Tensor partial;
   if (splits > 1) {
     partial = at::empty({splits, M, N}, a.options().dtype(at::kFloat));
@@ -1658,9 +1704,9 @@ void dsv_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool b_mn, in
               c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2, c10::optional<torch::Tensor> tile_slots,
               int64_t lora_seg, c10::optional<torch::Tensor> save, int64_t save_lo, int64_t save_hi,
               int64_t save_dst, int64_t force_bn, int64_t max_ctas, c10::optional<torch::Tensor> aux,
-              c10::optional<torch::Tensor> aux_out) {
+              c10::optional<torch::Tensor> aux_out, bool overlap_prev) {
   dsv_gemm_impl(a, b, out, b_mn, epi, z, b2, tile_slots, lora_seg, save, save_lo, save_hi, save_dst, force_bn,
-                max_ctas, aux, aux_out, nullptr);
+                max_ctas, aux, aux_out, nullptr, overlap_prev);
 }
 
 // LM-head statistics for cross-entropy without storing logits: for

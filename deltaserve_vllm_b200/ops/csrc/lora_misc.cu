@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(256) lora_shrink_gemv_kernel(const __nv_bfloat
                                                                const int* __restrict__ slot_ids, __nv_bfloat16* Z,
                                                                int sz, int T, int K, int PR, int SEG, int slots) {
   __shared__ float part[8][SHV_OUT];
+  griddep_launch_dependents();   // the GEMM that reads Z may start its base K blocks now
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int row = blockIdx.x;
   const int o0 = blockIdx.y * SHV_OUT;

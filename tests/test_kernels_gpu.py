@@ -193,6 +193,49 @@ def test_lora_shrink_decode_sizes(T, K, P, R, slots):
     torch.testing.assert_close(Z.float().cpu(), Zr.float(), rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("M,N,K,graph", [(16, 6144, 4096, False), (16, 6144, 4096, True), (300, 1024, 512, False),
+                                          (2048, 4096, 1024, True)])
+def test_gemm_overlapping_the_shrink(M, N, K, graph):
+    """A LoRA GEMM launched to overlap the shrink right before it (programmatic
+    dependent launch: base K blocks first, a wait before the LoRA blocks) gives
+    the serialised result, eagerly and replayed from a CUDA graph; shapes cover
+    the swapped decode path, a one-CTA tile and the CTA-pair kernel."""
+    slots, PR, seg = 2, 48, 64
+    x, w = rnd(M, K, seed=71), rnd(N, K, scale=0.05, seed=72)
+    A = rnd(slots, PR, K, scale=0.05, seed=73)
+    B2 = rnd(N, slots * seg, scale=0.05, seed=74)
+    sid = (torch.arange(M, device=DEV, dtype=torch.int32) % slots)
+    mask = torch.full(((M + 127) // 128,), 3, dtype=torch.int32, device=DEV)
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device=DEV)
+    ref_out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    ops.lora_shrink(x, A, sid, Z, seg)
+    ops.gemm(x, w, ref_out, z=Z, b2=B2, tile_slots=mask, lora_seg=seg)
+    out = torch.zeros_like(ref_out)
+    Z2 = torch.zeros_like(Z)
+
+    def run():
+        ops.lora_shrink(x, A, sid, Z2, seg)
+        ops.gemm(x, w, out, z=Z2, b2=B2, tile_slots=mask, lora_seg=seg, after_shrink=True)
+
+    if graph:
+        run()                                  # warm (allocations, tensor maps)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        out.zero_()
+        Z2.zero_()
+        for _ in range(3):
+            g.replay()
+    else:
+        for _ in range(3):
+            run()
+    torch.cuda.synchronize()
+    assert ops.check_device_error() == 0
+    torch.testing.assert_close(Z2, Z, rtol=0, atol=0)
+    torch.testing.assert_close(out.float(), ref_out.float(), rtol=0, atol=0)
+
+
 def test_gemm_lora_expand_segmented():
     M, N, K, slots, P, R = 300, 384, 256, 4, 3, 16
     seg = 64
