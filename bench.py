@@ -92,6 +92,9 @@ def parse():
     p.add_argument("--run-ahead", type=int, default=6, help="backward layers queued ahead of the GPU")
     p.add_argument("--bwd-sm-pct", type=int, default=0,
                    help="backward_mps_percentage: cap the backward GEMMs at this share of the SMs (0 = no cap)")
+    p.add_argument("--fwd-small-gemm-ctas", type=int, default=0,
+                   help="grid cap of the forward GEMMs of batches <= 128 rows (decode): they are "
+                        "HBM-bound, fewer SMs keep the pace and leave the rest to the backward (0 = all)")
     p.add_argument("--pause", default="arrival", choices=["arrival", "off"],
                    help="pause_on_arrival: stop feeding the backward while an inference prefill is pending")
     p.add_argument("--phase", default="both", choices=["prefill", "both"],
@@ -202,6 +205,8 @@ def _exit_watchdog(seconds: float = 90.0) -> None:
 
 def main():
     args = parse()
+    if args.fwd_small_gemm_ctas:
+        os.environ["DSV_FWD_SMALL_GEMM_CTAS"] = str(args.fwd_small_gemm_ctas)   # read at package import
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) == 0:
             reference_arm(args)
@@ -375,7 +380,7 @@ def main():
                    "slo": {"ttft_s": args.ttft_slo, "tbt_s": args.tbt_slo},
                    "l2": "inputs larger than L2 (16 GB of weights stream every step)",
                    "tp_comm": args.tp_comm, "admission_phase": args.phase, "pause": args.pause,
-                   "bwd_sm_pct": args.bwd_sm_pct,
+                   "bwd_sm_pct": args.bwd_sm_pct, "fwd_small_gemm_ctas": args.fwd_small_gemm_ctas,
                    "run_ahead_layers": args.run_ahead},
         "fused_ar_active": eng.peer_ws is not None,
         "slo_attainment": attain, "p99_ttft_ms": (percentile(ttfts, 99) or 0) * 1e3 if ttfts else None,

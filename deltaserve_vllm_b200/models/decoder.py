@@ -36,6 +36,11 @@ from .weights import ModelWeights
 # Launch each LoRA GEMM to overlap the shrink kernel right before it (its base
 # K blocks stream while the shrink runs); DSV_OVERLAP_SHRINK=0 serialises them.
 OVERLAP_SHRINK = os.environ.get("DSV_OVERLAP_SHRINK", "1") != "0"
+# Grid cap of the forward's GEMMs when the batch has at most 128 rows
+# (decode): these stream weights at the HBM bound, so fewer SMs can keep the
+# same pace and the rest stay free for a concurrently running backward.
+# 0 = every SM.
+FWD_SMALL_GEMM_CTAS = int(os.environ.get("DSV_FWD_SMALL_GEMM_CTAS", "0"))
 
 
 @dataclass
@@ -147,8 +152,9 @@ class DecoderModel:
             ops.lora_shrink(x, A, b.slot_ids, z, seg)
             kw = dict(z=z, b2=self.lora.B2[layer][group], tile_slots=b.tile_slots, lora_seg=seg,
                       after_shrink=OVERLAP_SHRINK)
+        cap = FWD_SMALL_GEMM_CTAS if x.shape[0] <= 128 else 0
         return ops.gemm(x, w, out, epi=epi, save=save, save_lo=save_lo, save_hi=save_hi,
-                        save_dst=save_dst, **kw)
+                        save_dst=save_dst, max_ctas=cap, **kw)
 
     def _proj_reduce(self, x, w, out, layer: int, group: str, b: ForwardBatch):
         """Row-parallel projection followed by the TP all-reduce. With a peer

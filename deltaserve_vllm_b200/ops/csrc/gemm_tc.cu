@@ -1516,17 +1516,20 @@ static int dsv_gemm_impl(torch::Tensor a, torch::Tensor b, torch::Tensor out, bo
   // the operands so the weights fill the 128-row side of the MMA and stream
   // at full tile width; the tokens become a 64/128-wide N tile and the
   // epilogue stores the transposed accumulator.
-  if (!b_mn && M <= 128 && epi == kEpiBF16 && !save.has_value() && force_bn == 0 && max_ctas == 0 &&
-      N >= 256 && (N % 8) == 0) {
+  if (!b_mn && M <= 128 && epi == kEpiBF16 && !save.has_value() && force_bn == 0 &&
+      (max_ctas == 0 || max_ctas < num_sms()) && N >= 256 && (N % 8) == 0) {
     const int bnt = M <= 64 ? 64 : 128;
     const int tiles = (N + BM - 1) / BM;
     const int kbs = (K + BK - 1) / BK;
-    const int splits = kbs >= 8 ? balanced_splits(tiles, kbs, num_sms(), 16) : 1;
+    // A grid cap (a share of the SMs) is honoured: the units are balanced over the capped grid.
+    const int ctas = max_ctas > 0 ? (int)max_ctas : num_sms();
+    const int splits = kbs >= 8 ? balanced_splits(tiles, kbs, ctas, 16) : 1;
     GemmArgs args{};
     args.M = N;
     args.N = M;
     args.K = K;
     args.k_splits = splits;
+    args.max_ctas = (int)max_ctas;
     args.wait_prev = (overlap_prev && lora_seg > 0) ? 1 : 0;
     args.C = out.data_ptr();
     args.ldc = (int)out.stride(0);

@@ -46,10 +46,11 @@ def rnd(*shape, scale=1.0, dtype=torch.bfloat16, seed=0):
 # ------------------------------------------------------------------ cases
 # Each returns (launch fn, algorithmic bytes, algorithmic flops).
 
-def _gemm(M, N, K, epi=ops.EPI_BF16):
+def _gemm(M, N, K, epi=ops.EPI_BF16, max_ctas=0):
+    """``max_ctas``: grid cap (a share of the SMs; 0 = all)."""
     a, b = rnd(M, K, seed=1), rnd(N, K, scale=0.02, seed=2)
     out = torch.empty(M, N // 2 if epi == ops.EPI_SWIGLU else N, dtype=torch.bfloat16, device=DEV)
-    return (lambda: ops.gemm(a, b, out, epi=epi),
+    return (lambda: ops.gemm(a, b, out, epi=epi, max_ctas=max_ctas),
             2 * (M * K + N * K + out.numel()), 2 * M * N * K)
 
 
@@ -278,8 +279,14 @@ CASES = {
     "gemm_prefill_down": lambda: _gemm(4096, 4096, 14336),
     # decode step of 64 sequences (split-K, weight-streaming bound)
     "gemm_decode_qkv": lambda: _gemm(64, 6144, 4096),
+    "gemm_decode_qkv_cap74": lambda: _gemm(64, 6144, 4096, max_ctas=74),
+    "gemm_decode_qkv_cap96": lambda: _gemm(64, 6144, 4096, max_ctas=96),
     "gemm_decode_gateup_swiglu": lambda: _gemm(64, 28672, 4096, ops.EPI_SWIGLU),
+    "gemm_decode_gateup_swiglu_cap74": lambda: _gemm(64, 28672, 4096, ops.EPI_SWIGLU, max_ctas=74),
+    "gemm_decode_gateup_swiglu_cap96": lambda: _gemm(64, 28672, 4096, ops.EPI_SWIGLU, max_ctas=96),
     "gemm_decode_down": lambda: _gemm(64, 4096, 14336),
+    "gemm_decode_down_cap74": lambda: _gemm(64, 4096, 14336, max_ctas=74),
+    "gemm_decode_down_cap96": lambda: _gemm(64, 4096, 14336, max_ctas=96),
     # fused GEMM + all-reduce on one rank (the push / reduce / broadcast phases run locally)
     "gemm_ar_prefill_o": lambda: _gemm_ar(4096, 4096, 4096),
     "gemm_ar_decode_down": lambda: _gemm_ar(64, 4096, 14336),
