@@ -16,7 +16,10 @@
 //   GQA group's query heads and the 64-query tiles at or after the key
 //   tile: S^T = K Q^T and dP^T = V dO^T, then P^T and dS^T (bf16, shared
 //   memory), then dV += P^T dO and dK += dS^T Q (dO and Q MN-major). The
-//   group's heads accumulate in the same TMEM columns.
+//   group's heads accumulate in the same TMEM columns. When there are fewer
+//   (key tile, KV head) pairs than SMs (high TP degrees), each CTA takes one
+//   query head of the group instead and writes fp32 partials that a small
+//   finish kernel sums (then scale, RoPE, store) in a fixed order.
 //
 // TMEM: q-side S[2] 0/64, dP[2] 128/192, dQ 256-383; kv-side S^T[2] 0/64,
 // dP^T[2] 128/192, dV 256-383, dK 384-511 (512 allocated; 192 KB of shared
@@ -79,6 +82,13 @@ struct FaBwdArgs {
   const float* rope_cos;    // [n, 64] fp32 (row stride rope_stride) or null
   const float* rope_sin;
   int rope_stride;
+  // Head split of the dK/dV pass (few key tiles x KV heads for the SMs): one
+  // CTA per (key tile, query head of the group) writes raw fp32 dK / dV
+  // partials [group][n][Hkv*128]; kv_split_finish_kernel sums the group.
+  int split_heads;
+  float* part_dk;
+  float* part_dv;
+  int n_rows;
 };
 
 // Bounded wait that the whole warp agrees on (tcgen05.ld / st that follow are
@@ -387,11 +397,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int tile = blockIdx.x;       // earlier key tiles (more queries) first
-  const int g = blockIdx.y;
+  const int g = a.split_heads ? (int)blockIdx.y / a.group : (int)blockIdx.y;
+  const int h_first = a.split_heads ? (int)blockIdx.y % a.group : 0;   // first query head of the group
+  const int h_count = a.split_heads ? 1 : a.group;
   const int s0 = a.tiles[3 * tile], len = a.tiles[3 * tile + 1], k0 = a.tiles[3 * tile + 2];
   const int rows_valid = min(128, len - k0);
   const int nq = (len + 63) / 64 - k0 / 64;   // 64-query tiles at or after the key tile
-  const int n_it = a.group * nq;
+  const int n_it = h_count * nq;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -429,7 +441,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     int issued[2] = {0, 0};
     for (int it = 0; it < n_it; ++it) {
       const int st = it & 1;
-      const int head = g * a.group + it / nq;
+      const int head = g * a.group + h_first + it / nq;
       const int q0 = k0 + (it % nq) * 64;
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&qd_empty[st], ((uint32_t)(it >> 1) & 1u) ^ 1u, kErrAtEmpty) ? 1 : 0;
@@ -553,7 +565,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       fence_proxy_async_smem();
       mbar_arrive(&ds_full[st]);
     }
-    if (ok && warp_wait(dkv_done, 0, kErrAtDone)) {
+    if (ok && a.split_heads && warp_wait(dkv_done, 0, kErrAtDone)) {
+      tc_fence_after();
+      const size_t grow = (size_t)s0 + kpos;
+      const size_t off = ((size_t)h_first * a.n_rows + grow) * (size_t)(a.num_kv_heads * 128) + g * 128;
+      store_acc_row(t_lane + 256, 1.f, nullptr, nullptr, a.part_dv + off, nullptr, row_ok);
+      store_acc_row(t_lane + 384, 1.f, nullptr, nullptr, a.part_dk + off, nullptr, row_ok);
+    } else if (ok && warp_wait(dkv_done, 0, kErrAtDone)) {
       tc_fence_after();
       const size_t grow = (size_t)s0 + kpos;
       const int hkv128 = a.num_kv_heads * 128;
@@ -573,6 +591,64 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// Head-split finish: per row of the tile and KV head, sum the group's fp32
+// dK / dV partials, scale dK, undo RoPE on it and store both (fp32 rows or
+// bf16 into d(qkv)), the same outputs as the single-pass epilogue.
+__global__ void __launch_bounds__(128) kv_split_finish_kernel(FaBwdArgs a) {
+  const int tile = blockIdx.x, g = blockIdx.y, r = threadIdx.x;
+  const int s0 = a.tiles[3 * tile], len = a.tiles[3 * tile + 1], k0 = a.tiles[3 * tile + 2];
+  if (k0 + r >= len) return;
+  const size_t grow = (size_t)s0 + k0 + r;
+  const int hkv128 = a.num_kv_heads * 128;
+  const size_t plane = (size_t)a.n_rows * hkv128;
+  for (int which = 0; which < 2; ++which) {   // 0: dV, 1: dK
+    const float* src = (which == 0 ? a.part_dv : a.part_dk) + grow * hkv128 + g * 128;
+    const bool bf = (a.bf16_mask & (which == 0 ? 4 : 2)) != 0;
+    const float scale = which == 0 ? 1.f : a.scale;
+    const bool rope = which == 1 && a.rope_cos != nullptr;
+    for (int h = 0; h < 64; h += 32) {
+      float x[32], y[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 u = make_float4(0.f, 0.f, 0.f, 0.f), v = u;
+        for (int p = 0; p < a.group; ++p) {
+          const float4 pu = *reinterpret_cast<const float4*>(src + p * plane + h + i);
+          const float4 pv = *reinterpret_cast<const float4*>(src + p * plane + 64 + h + i);
+          u.x += pu.x; u.y += pu.y; u.z += pu.z; u.w += pu.w;
+          v.x += pv.x; v.y += pv.y; v.z += pv.z; v.w += pv.w;
+        }
+        x[i] = u.x * scale; x[i + 1] = u.y * scale; x[i + 2] = u.z * scale; x[i + 3] = u.w * scale;
+        y[i] = v.x * scale; y[i + 1] = v.y * scale; y[i + 2] = v.z * scale; y[i + 3] = v.w * scale;
+      }
+      if (rope) {
+        const float* cr = a.rope_cos + grow * a.rope_stride + h;
+        const float* sr = a.rope_sin + grow * a.rope_stride + h;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float xa = x[i], yb = y[i];
+          x[i] = xa * cr[i] + yb * sr[i];
+          y[i] = yb * cr[i] - xa * sr[i];
+        }
+      }
+      if (bf) {
+        __nv_bfloat16* dst = a.dqkv + grow * a.dqkv_stride + (which == 0 ? a.dv_col : a.dk_col) + g * 128;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          *reinterpret_cast<uint32_t*>(dst + h + i) = pack2_bf16(x[i], x[i + 1]);
+          *reinterpret_cast<uint32_t*>(dst + 64 + h + i) = pack2_bf16(y[i], y[i + 1]);
+        }
+      } else {
+        float* dst = (which == 0 ? a.dv : a.dk) + grow * hkv128 + g * 128;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          *reinterpret_cast<float4*>(dst + h + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+          *reinterpret_cast<float4*>(dst + 64 + h + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
+        }
+      }
+    }
   }
 }
 
@@ -689,8 +765,24 @@ void dsv_attn_bwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::T
     CUtensorMap tdo = make_tmap_bf16(d_o.data_ptr(), n, (uint64_t)hq * 128, d_o.stride(0), 64);
     CUtensorMap tk = make_tmap_bf16(k.data_ptr(), n, (uint64_t)hkv * 128, k.stride(0), 128);
     CUtensorMap tv = make_tmap_bf16(v.data_ptr(), n, (uint64_t)hkv * 128, v.stride(0), 128);
-    fa_bwd_kv_tc_kernel<<<dim3((unsigned)T, (unsigned)hkv), AT_THREADS, AKV_SMEM, stream>>>(tq, tdo, tk, tv, a);
+    // Few (key tile, KV head) CTAs for the SMs (high TP): one CTA per query
+    // head of the group instead, partials summed by a finish kernel.
+    const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    at::Tensor part;
+    if (a.group > 1 && (int64_t)T * hkv < sms) {
+      part = at::empty({2, (int64_t)a.group, n, hkv * 128}, q.options().dtype(at::kFloat));
+      a.split_heads = 1;
+      a.part_dk = part.data_ptr<float>();
+      a.part_dv = a.part_dk + (size_t)a.group * n * hkv * 128;
+      a.n_rows = (int)n;
+    }
+    fa_bwd_kv_tc_kernel<<<dim3((unsigned)T, (unsigned)(a.split_heads ? hkv * a.group : hkv)), AT_THREADS, AKV_SMEM,
+                          stream>>>(tq, tdo, tk, tv, a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+    if (a.split_heads) {
+      kv_split_finish_kernel<<<dim3((unsigned)T, (unsigned)hkv), 128, 0, stream>>>(a);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+    }
   }
 }
 

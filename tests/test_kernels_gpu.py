@@ -421,12 +421,15 @@ def test_attn_bwd_rope_epilogue_into_dqkv(mask):
     assert (dqkv[used:] == 7.0).all()                       # rows past the samples untouched
 
 
-@pytest.mark.parametrize("Hq,Hkv,lse_from_fwd", [(8, 2, True), (4, 4, False), (32, 8, True)])
-def test_attn_bwd_tc_varlen_gqa(Hq, Hkv, lse_from_fwd):
+@pytest.mark.parametrize("Hq,Hkv,lse_from_fwd,many", [(8, 2, True, False), (4, 4, False, False),
+                                                      (32, 8, True, False), (32, 8, True, True)])
+def test_attn_bwd_tc_varlen_gqa(Hq, Hkv, lse_from_fwd, many):
     """tcgen05 attention backward (dQ pass + dK/dV pass) against the fp32
     reference, elementwise; the forward's statistics either come from the
-    tcgen05 forward (the trainer's path) or are recomputed inside attn_bwd."""
-    lens = [1, 37, 64, 65, 130, 200, 513] if Hq <= 8 else [512, 512, 300, 7]
+    tcgen05 forward (the trainer's path) or are recomputed inside attn_bwd.
+    Few (key tile, KV head) pairs run the dK/dV pass split by query head
+    (partials + finish kernel); ``many`` has enough of them for one pass."""
+    lens = [1, 37, 64, 65, 130, 200, 513] if Hq <= 8 else ([512] * 6 if many else [512, 512, 300, 7])
     q, k, v, starts, n = _packed_qkv(lens, Hq, Hkv, seed=41)
     g = torch.Generator(device=DEV).manual_seed(42)
     d_o = torch.randn(n, Hq * 128, generator=g, device=DEV).to(torch.bfloat16)
