@@ -114,7 +114,12 @@ def main() -> None:
     ap.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
                     help="residual-gradient reductions over peer memory (fused) or NCCL all-reduces")
     ap.add_argument("--out", default="")
+    ap.add_argument("--profile-cycle", action="store_true",
+                    help="bracket one extra graph cycle with cudaProfilerStart/Stop (for "
+                         "`ncu --profile-from-start off` launch lists); skips the eager phase runs; one GPU only")
     args = ap.parse_args()
+    if args.profile_cycle and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--profile-cycle profiles one GPU; run it without torchrun")
 
     import torch.distributed as dist
 
@@ -169,6 +174,15 @@ def main() -> None:
         ms = trainer.run_cycle(cap, n, starts, lens).gpu_ms
         if i > 0:                      # the first replays upload the graphs
             gms.append(ms)
+    if args.profile_cycle:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        trainer.run_cycle(cap, n, starts, lens)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        trainer.release_graphs()
+        print(json.dumps({"graph_cycle_ms": sum(gms) / len(gms), "profiled": True}), flush=True)
+        return
     # ---- eager path with phase events (the graphs are dropped: a cached
     # graph set would otherwise be replayed)
     trainer.release_graphs()
