@@ -41,6 +41,7 @@ struct PrefillArgs {
   __nv_bfloat16* out;       // [T, Hq*128] row stride out_stride
   int out_stride;
   int num_kv_heads, group, block_size;
+  int num_blocks;           // pages in the cache (the bounds-check build checks page ids against it)
   float scale_log2;         // softmax scale * log2(e)
 };
 
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(PF_THREADS) paged_prefill_kernel(PrefillArgs a
       bool ok = kpos < kv_end;
       int kp = ok ? kpos : 0;
       int page = btab[kp / a.block_size];
+      if (!DSV_IN_BOUNDS(page, a.num_blocks)) page = 0;
       size_t off = (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
       cp_async16(sK + buf * PF_BN * HD + swz(r, c), a.k_cache + off, ok);
       cp_async16(sV + buf * PF_BN * HD + swz(r, c), a.v_cache + off, ok);
@@ -238,6 +240,7 @@ struct DecodeArgs {
   __nv_bfloat16* out;      // [B, Hq*128] row stride out_stride
   int out_stride;
   int num_heads, num_kv_heads, group, block_size, splits, keys_per_split;
+  int num_blocks;            // pages in the cache (bounds-check build); INT_MAX when unknown
   float scale_log2;
 };
 
@@ -281,7 +284,8 @@ __global__ void __launch_bounds__(DC_THREADS) paged_decode_kernel(DecodeArgs a) 
       const int kpos = k_begin + ci * DC_KEYS + r;
       const bool ok = kpos < k_end;
       const int kp = ok ? kpos : k_begin;
-      const int page = btab[kp / a.block_size];
+      int page = btab[kp / a.block_size];
+      if (!DSV_IN_BOUNDS(page, a.num_blocks)) page = 0;
       const size_t off =
           (((size_t)page * a.num_kv_heads + kvh) * a.block_size + (kp % a.block_size)) * HD + c * 8;
       cp_async16(sK + buf * DC_KEYS * HD + swz(r, c), a.k_cache + off, ok);
@@ -479,6 +483,7 @@ void dsv_paged_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
   a.out_stride = (int)out.stride(0);
   a.num_kv_heads = (int)k_cache.size(1);
   a.block_size = (int)k_cache.size(2);
+  a.num_blocks = (int)k_cache.size(0);
   a.group = (int)(num_heads / a.num_kv_heads);
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   const int smem = (PF_BM * HD + 4 * PF_BN * HD) * 2;
@@ -524,6 +529,7 @@ void dsv_paged_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   a.num_kv_heads = Hkv;
   a.group = G;
   a.block_size = (int)k_cache.size(2);
+  a.num_blocks = (int)k_cache.size(0);
   a.splits = (int)splits;
   a.keys_per_split = (int)keys_per_split;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
@@ -598,6 +604,7 @@ extern "C" int dsv_paged_decode_noalloc(const void* q, int q_stride, const void*
   a.num_kv_heads = num_kv_heads;
   a.group = G;
   a.block_size = block_size;
+  a.num_blocks = 0x7fffffff;   // the C entry point is not told the cache's page count
   a.splits = splits;
   a.keys_per_split = keys_per_split;
   a.scale_log2 = scale * 1.4426950408889634f;

@@ -74,6 +74,7 @@ struct FaFwdArgs {
   const int* cu_q;          // paged [S+1]
   const int* ctx_lens;      // paged [S]
   int block_size, box_rows; // paged: page size, rows per K/V box (min(block_size, 128))
+  int num_blocks;           // paged: pages in the cache (bounds-check build)
   int num_kv_heads, group;
   __nv_bfloat16* out;       // [T, ...] row stride out_stride, head h at h * 128
   int out_stride;
@@ -171,7 +172,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           for (int s = 0; s < FA_ROWS / R; ++s) {
             const int key0 = kb * FA_ROWS + s * R;
             const bool in = key0 < kv_end;
-            const int page = btab[in ? key0 / a.block_size : 0];
+            int page = btab[in ? key0 / a.block_size : 0];
+            if (!DSV_IN_BOUNDS(page, a.num_blocks)) page = 0;
             const int y = (page * a.num_kv_heads + kvh) * a.block_size + (in ? key0 % a.block_size : 0);
             tma_load_2d(dk + s * R * 128, &tmK, &k_full[st], 0, y);
             tma_load_2d(dk + FA_CHUNK + s * R * 128, &tmK, &k_full[st], 64, y);
@@ -187,7 +189,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
           for (int s = 0; s < FA_ROWS / R; ++s) {
             const int key0 = kb * FA_ROWS + s * R;
             const bool in = key0 < kv_end;
-            const int page = btab[in ? key0 / a.block_size : 0];
+            int page = btab[in ? key0 / a.block_size : 0];
+            if (!DSV_IN_BOUNDS(page, a.num_blocks)) page = 0;
             const int y = (page * a.num_kv_heads + kvh) * a.block_size + (in ? key0 % a.block_size : 0);
             tma_load_2d(dv + s * R * 128, &tmV, &v_full[st], 0, y);
             tma_load_2d(dv + FA_CHUNK + s * R * 128, &tmV, &v_full[st], 64, y);
@@ -444,6 +447,7 @@ void dsv_paged_prefill_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor 
   a.ctx_lens = ctx_lens.data_ptr<int>();
   a.block_size = bs;
   a.box_rows = box;
+  a.num_blocks = (int)k_cache.size(0);
   a.num_kv_heads = hkv;
   a.group = (int)(num_heads / hkv);
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());

@@ -32,6 +32,22 @@ static __device__ int g_error = 0;
 
 __device__ __forceinline__ void set_error(int code) { atomicCAS(&g_error, 0, code); }
 
+// Index checks of the bounds-check build (`DSV_BOUNDS_CHECK=1 python setup.py
+// build_ext --inplace` adds -DDSV_BOUNDS_CHECK): an index outside [0, n)
+// records 0x5000000 + the source line in the error word and the caller skips
+// or clamps the access. In the default build the check is the constant true.
+constexpr int kErrBoundsBase = 0x5000000;
+__device__ __forceinline__ bool bounds_ok(long long i, long long n, int line) {
+  if (i >= 0 && i < n) return true;
+  set_error(kErrBoundsBase + line);
+  return false;
+}
+#ifdef DSV_BOUNDS_CHECK
+#define DSV_IN_BOUNDS(i, n) ::dsv::bounds_ok((long long)(i), (long long)(n), __LINE__)
+#else
+#define DSV_IN_BOUNDS(i, n) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

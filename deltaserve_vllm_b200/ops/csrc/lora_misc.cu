@@ -141,7 +141,8 @@ __global__ void __launch_bounds__(256) lora_shrink_gemv_kernel(const __nv_bfloat
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int row = blockIdx.x;
   const int o0 = blockIdx.y * SHV_OUT;
-  const int s = slot_ids[row];
+  int s = slot_ids[row];
+  if (s >= 0 && !DSV_IN_BOUNDS(s, slots)) s = -1;    // bounds-check build: an unknown slot reads nothing
   if (blockIdx.y == 0) {
     const int W = slots * SEG;
     for (int c = threadIdx.x; c < W; c += blockDim.x) {

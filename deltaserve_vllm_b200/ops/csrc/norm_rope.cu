@@ -105,14 +105,16 @@ __global__ void qk_norm_rope_cache_kernel(__nv_bfloat16* qkv, int sq, const int6
                                           const float* __restrict__ cos_sin, const __nv_bfloat16* __restrict__ qn_w,
                                           const __nv_bfloat16* __restrict__ kn_w, float eps, int Hq, int Hkv,
                                           __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                                          const int64_t* __restrict__ slot_mapping, int block_size, int T) {
+                                          const int64_t* __restrict__ slot_mapping, int block_size, int T,
+                                          int64_t cache_slots) {
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   const int H = Hq + 2 * Hkv;
   if (gw >= T * H) return;
   const int tok = gw / H, h = gw % H;
   __nv_bfloat16* row = qkv + (size_t)tok * sq + h * 128;
-  const int64_t slot = slot_mapping != nullptr ? slot_mapping[tok] : -1;
+  int64_t slot = slot_mapping != nullptr ? slot_mapping[tok] : -1;
+  if (slot >= 0 && !DSV_IN_BOUNDS(slot, cache_slots)) slot = -1;   // bounds-check build: skip the write
   if (h >= Hq + Hkv) {
     // v: copy into the cache only.
     if (slot >= 0) {
@@ -211,7 +213,8 @@ void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::T
       cos_sin.data_ptr<float>(),
       q_norm.has_value() ? reinterpret_cast<const __nv_bfloat16*>(q_norm->data_ptr()) : nullptr,
       k_norm.has_value() ? reinterpret_cast<const __nv_bfloat16*>(k_norm->data_ptr()) : nullptr, (float)eps,
-      (int)num_heads, (int)num_kv_heads, kc, vc, sm, bs, T);
+      (int)num_heads, (int)num_kv_heads, kc, vc, sm, bs, T,
+      k_cache.has_value() ? (int64_t)k_cache->size(0) * bs : (int64_t)0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -23,6 +23,10 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("DSV_PTXAS_VERBOSE") == "1":
     NVCC_FLAGS.append("-Xptxas=-v")
+if os.environ.get("DSV_BOUNDS_CHECK") == "1":
+    # Index checks in the paged-KV, slot and LoRA-slot reads: a bad index is
+    # recorded in the device error word (ops.check_device_error) and skipped.
+    NVCC_FLAGS.append("-DDSV_BOUNDS_CHECK")
 
 setup(
     name="deltaserve_vllm_b200",
