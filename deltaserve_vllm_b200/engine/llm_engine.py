@@ -137,9 +137,14 @@ class CoServingEngine:
             if not self._self_test_fused(comm):
                 self.peer_ws.close()
                 self.peer_ws = comm.peer_ws = None
+        # ---- vocabulary-parallel embedding read over peer memory (no all-reduce)
+        self.embed_peer = None
+        if self.cuda and comm is not None and comm.size > 1 and ecfg.tp_comm == "fused":
+            self._setup_embed_peer(comm)
         # ---- KV cache sized from what is left
         self.kv = self._alloc_kv()
         self.model = DecoderModel(self.weights, self.kv.k, self.kv.v, self.lora, comm)
+        self.model.embed_peer = self.embed_peer
         num_sms = (torch.cuda.get_device_properties(self.device).multi_processor_count
                    if self.cuda else 148)
         self.scheduler = Scheduler(self.kv.allocator, ecfg.block_size, ecfg.max_num_seqs,
@@ -371,6 +376,41 @@ class CoServingEngine:
         if not ok:
             dprint("[tp] fused GEMM + all-reduce failed its self-test: using GEMM + NCCL")
         return bool(ok)
+
+    def _setup_embed_peer(self, comm) -> None:
+        """Move this rank's embedding shard into peer-mapped memory and check
+        the peer-read embedding against embedding + NCCL all-reduce (the MIN
+        over ranks decides; a failure keeps the all-reduce path)."""
+        from ..parallel.peer import PeerTable
+        w = self.weights
+        tied = w.lm_head.data_ptr() == w.embed.data_ptr()
+        ok = 1
+        pt = None
+        try:
+            pt = PeerTable(comm, w.embed, self.arch.vocab)
+            vl, V = w.v_local, self.arch.vocab
+            ids = torch.tensor([0, vl - 1, vl, V - 1, (V * 7) // 13, -1], dtype=torch.int64, device=self.device)
+            ref = torch.empty(ids.numel(), self.arch.hidden, dtype=self.dtype, device=self.device)
+            ops.embedding(ids, w.embed, ref, comm.rank * vl)
+            comm.all_reduce(ref)
+            got = torch.empty_like(ref)
+            ops.embedding_peer(ids, pt, got)
+            torch.cuda.synchronize(self.device)
+            if not torch.equal(ref, got) or ops.check_device_error() != 0:
+                ok = 0
+        except Exception as e:  # a failing setup must not take serving down
+            dprint(f"[tp] peer embedding setup raised {e!r}")
+            ok = 0
+        ok = -comm.all_reduce_max_int(-ok)
+        if ok and pt is not None:
+            w.embed = pt.local
+            if tied:
+                w.lm_head = pt.local
+            self.embed_peer = pt
+        else:
+            if pt is not None:
+                pt.close()
+            dprint("[tp] peer embedding failed its self-test: embedding + NCCL all-reduce")
 
     def _self_test_bwd(self, comm) -> bool:
         """Check the backward's push + reduce over peer memory against a GEMM
@@ -1264,6 +1304,9 @@ class CoServingEngine:
             self.runner.graphs.release()
         if self.cuda:
             torch.cuda.synchronize(self.device)
+        if self.embed_peer is not None:
+            self.embed_peer.close()
+            self.embed_peer = None
         if self.peer_ws is not None:
             self.peer_ws.close()
             self.peer_ws = None

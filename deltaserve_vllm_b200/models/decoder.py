@@ -140,6 +140,9 @@ class DecoderModel:
         self.hkv_l = self.arch.num_kv_heads // weights.tp.size
         self.scale = 1.0 / math.sqrt(self.arch.head_dim)
         self._dec_ws: tuple[torch.Tensor, torch.Tensor] | None = None
+        # A parallel.peer.PeerTable of the embedding shards (set by the engine
+        # under TP with the fused communication path) replaces embedding + all-reduce.
+        self.embed_peer = None
 
     # ------------------------------------------------------------------ helpers
     def _proj(self, x, w, out, layer: int, group: str, b: ForwardBatch, epi=EPI_BF16, save=None,
@@ -207,8 +210,11 @@ class DecoderModel:
         lo, hi, dst = (b.ft_lo, b.ft_hi, b.ft_dst) if cap_on else (0, 0, 0)
 
         residual = torch.empty(T, D, dtype=dt, device=dev)
-        ops.embedding(b.input_ids, w.embed, residual, w.tp.rank * w.v_local)
-        self.comm.all_reduce(residual)
+        if self.embed_peer is not None:
+            ops.embedding_peer(b.input_ids, self.embed_peer, residual)     # every shard over peer memory
+        else:
+            ops.embedding(b.input_ids, w.embed, residual, w.tp.rank * w.v_local)
+            self.comm.all_reduce(residual)
         if cap_on:
             cap.ids[dst:dst + hi - lo] = b.input_ids[lo:hi]
             cap.positions[dst:dst + hi - lo] = b.positions[lo:hi]

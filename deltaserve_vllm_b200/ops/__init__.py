@@ -300,6 +300,14 @@ def embedding(ids, table, out, v0=0):
     return ref.embedding(ids, table, out, v0)
 
 
+def embedding_peer(ids, ptable, out):
+    """Full embedding rows on every rank from the vocabulary shards of all
+    ranks (``ptable``: a :class:`~..parallel.peer.PeerTable`), read over peer
+    memory; replaces ``embedding`` + the all-reduce of the partial rows."""
+    _native().embedding_peer(ids, ptable.table, ptable.rows, ptable.vocab, out)
+    return out
+
+
 def ce_fwd_bwd(logits, targets, loss, grad=None, gscale=1.0):
     if logits.is_cuda:
         _native().ce_fwd_bwd(logits, targets, loss, grad, gscale)

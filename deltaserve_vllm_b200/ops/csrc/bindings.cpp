@@ -88,6 +88,7 @@ void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::T
                             int64_t num_heads, int64_t num_kv_heads, c10::optional<torch::Tensor> k_cache,
                             c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slot_mapping);
 void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t seg);
+void dsv_embedding_peer(torch::Tensor ids, torch::Tensor tables, int64_t v_local, int64_t vocab, torch::Tensor out);
 void dsv_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t v0);
 void dsv_ce_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss,
                     c10::optional<torch::Tensor> grad, double gscale);
@@ -139,6 +140,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm", &dsv_rms_norm, "RMSNorm / fused residual add + RMSNorm (+ row capture)");
   m.def("qk_norm_rope_cache", &dsv_qk_norm_rope_cache, "q/k norm + RoPE + paged KV write");
   m.def("lora_shrink", &dsv_lora_shrink, "segmented multi-LoRA shrink");
+  m.def("embedding_peer", &dsv_embedding_peer, "vocab-parallel embedding read from every rank's shard over peer memory");
   m.def("embedding", &dsv_embedding, "vocab-parallel embedding gather");
   m.def("ce_fwd_bwd", &dsv_ce_fwd_bwd, "cross-entropy loss + gradient rows");
   m.def("seg_sumsq", &dsv_seg_sumsq, "per-segment sum of squares");

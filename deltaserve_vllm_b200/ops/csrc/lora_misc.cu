@@ -206,6 +206,25 @@ __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfl
   }
 }
 
+// Vocab-parallel embedding without a collective: every rank's shard of the
+// table sits in peer-mapped memory (CUDA IPC, plain P2P mappings); each token's
+// row is read straight from the shard that holds it (`tables[owner]`, a P2P
+// load over NVLink when the owner is another GPU), so every rank gets the full
+// rows and no all-reduce of the summed partial rows is needed.
+__global__ void embedding_peer_kernel(const int64_t* __restrict__ ids, const int64_t* __restrict__ tables, int world,
+                                      int64_t v_local, int64_t vocab, __nv_bfloat16* out, int D) {
+  const int t = blockIdx.x;
+  const int64_t id = ids[t];
+  const bool ok = id >= 0 && id < vocab;
+  const int owner = ok ? (int)min((int64_t)(world - 1), id / v_local) : 0;
+  const __nv_bfloat16* table = reinterpret_cast<const __nv_bfloat16*>(tables[owner]);
+  const int64_t row = ok ? id - (int64_t)owner * v_local : 0;
+  for (int i = threadIdx.x * 8; i < D; i += blockDim.x * 8) {
+    uint4 v = ok ? *reinterpret_cast<const uint4*>(table + row * D + i) : make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(out + (size_t)t * D + i) = v;
+  }
+}
+
 // Cross-entropy over fp32 logits rows, forward and backward in one pass pair:
 // loss[r] = lse - logit[target]; grad (bf16) = (softmax - onehot) * gscale.
 // target < 0 rows produce zero loss and zero gradient.
@@ -516,6 +535,22 @@ void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, t
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(A.data_ptr()), slot_ids.data_ptr<int>(),
       reinterpret_cast<__nv_bfloat16*>(Z.data_ptr()), (int)Z.stride(0), T, K, PR, (int)seg, slots);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void dsv_embedding_peer(torch::Tensor ids, torch::Tensor tables, int64_t v_local, int64_t vocab, torch::Tensor out) {
+  using namespace dsv;
+  const int T = (int)ids.size(0);
+  if (T == 0) return;
+  const int D = (int)out.size(1);
+  TORCH_CHECK(tables.is_cuda() && tables.scalar_type() == at::kLong && tables.dim() == 1 && tables.numel() <= 8,
+              "embedding_peer: tables must be an int64 CUDA tensor of <= 8 shard addresses");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && D % 8 == 0 && ids.scalar_type() == at::kLong,
+              "embedding_peer: bf16 [T, D] output, int64 ids");
+  c10::cuda::CUDAGuard guard(ids.device());
+  embedding_peer_kernel<<<T, std::min(1024, std::max(32, D / 8)), 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int64_t>(), tables.data_ptr<int64_t>(), (int)tables.numel(), v_local, vocab,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

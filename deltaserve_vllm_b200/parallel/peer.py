@@ -105,6 +105,46 @@ class PeerWorkspace:
         self.base = None
 
 
+class PeerTable:
+    """A row-sharded table (the vocabulary-parallel embedding) in peer-mapped
+    memory: rank ``r``'s shard holds rows ``[r * rows, (r + 1) * rows)`` of a
+    ``vocab``-row table, and every rank can read every shard directly
+    (``ops.embedding_peer``). ``local`` is this rank's shard (it replaces the
+    weight tensor, so nothing is stored twice)."""
+
+    def __init__(self, comm, shard: torch.Tensor, vocab: int):
+        from .. import ops
+        ext = ops.native_ext()
+        if ext is None:
+            raise RuntimeError("the peer table needs the CUDA extension")
+        self.comm = comm
+        self.world, self.rank = comm.size, comm.rank
+        if self.world > 8:
+            raise ValueError("peer tables support up to 8 ranks")
+        self.rows, self.vocab = int(shard.shape[0]), int(vocab)
+        self._ext = ext
+        self.base, handle = ext.peer_alloc(_align(shard.numel() * shard.element_size()))
+        handles = comm.all_gather_object(handle)
+        self.ptrs = [self.base if r == self.rank else ext.peer_open(h) for r, h in enumerate(handles)]
+        self.local = _from_ptr(self.base, shard.shape, shard.dtype, shard.device.index)
+        self.local.copy_(shard)
+        self.table = torch.tensor(self.ptrs, dtype=torch.int64, device=shard.device)
+        torch.cuda.synchronize()
+        comm.barrier()            # every shard filled and mapped before the first read
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        self.comm.barrier()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.peer_close(p)
+        self.local = None
+        self._ext.peer_free(self.base)
+        self.base = None
+
+
 class BwdPeerWorkspace:
     """Peer-mapped buffers of the tensor-parallel backward's residual-gradient
     reductions (``ops.gemm_push`` + ``ops.tp_reduce_rows``): the dX GEMM

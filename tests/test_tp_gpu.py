@@ -240,3 +240,44 @@ def test_fused_replicated_optimizer(world):
         torch.testing.assert_close(r["total"], sq, rtol=1e-4, atol=1e-4)
         for got in r["ps"]:
             torch.testing.assert_close(got, p, rtol=1e-4, atol=1e-5)
+
+
+def _run_embedding_peer(rank, world, port, outdir):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from deltaserve_vllm_b200.parallel.peer import PeerTable
+    comm = TPComm(None, dist.new_group(backend="gloo"))
+    V, D = 1000 * world, 256
+    vl = V // world
+    full = torch.randn(V, D, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).cuda()
+    shard = full[rank * vl:(rank + 1) * vl].clone()
+    pt = PeerTable(comm, shard, V)
+    ids = torch.randint(-2, V + 2, (777,), generator=torch.Generator().manual_seed(6)).cuda()
+    got = torch.empty(ids.numel(), D, dtype=torch.bfloat16, device="cuda")
+    ops.embedding_peer(ids, pt, got)
+    ref = torch.empty_like(got)
+    ops.embedding(ids, pt.local, ref, rank * vl)
+    dist.all_reduce(ref)
+    torch.cuda.synchronize()
+    ok = torch.equal(got, ref) and torch.equal(pt.local, shard) and ops.check_device_error() == 0
+    oks = comm.all_gather_object(bool(ok))
+    pt.close()
+    if rank == 0:
+        torch.save({"oks": oks}, os.path.join(outdir, "emb.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_embedding_from_peer_shards(world):
+    """The vocabulary-parallel embedding read over peer memory equals the
+    sharded embedding + NCCL all-reduce of the partial rows on every rank,
+    including ids outside the vocabulary (zero rows)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run_embedding_peer, args=(world, _port(), d), nprocs=world, join=True,
+                           start_method="spawn")
+        assert all(torch.load(os.path.join(d, "emb.pt"))["oks"])
