@@ -455,7 +455,8 @@ def test_attn_bwd_tc_varlen_gqa(Hq, Hkv, lse_from_fwd, many):
         assert (got - exp).abs().max() < tol, float((got - exp).abs().max() / exp.abs().max())
         rel = (got - exp).norm() / exp.norm()
         assert rel < 1e-2, float(rel)
-    assert dq[used:].abs().max() == 0 and dk[used:].abs().max() == 0
+    if used < n:
+        assert dq[used:].abs().max() == 0 and dk[used:].abs().max() == 0
     dq2, dk2, dv2 = ops.attn_bwd(q, k, v, d_o, tiles, scale, o=o, lse=lse, tiles128=t128)
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)   # deterministic
 
