@@ -17,8 +17,9 @@
 //               and sum (base-2 domain), writes bf16 P into shared memory in
 //               the 128-byte-swizzled K-major layout the MMA reads, and
 //               rescales its O row in TMEM (tcgen05.ld / st) when its max
-//               moved. After the last tile: O / l stored as bf16, and the
-//               optional statistics.
+//               grew by more than 2^8 (lazy rescaling: below that the old
+//               reference max stays). After the last tile: O / l stored as
+//               bf16, and the optional statistics.
 //
 // Shared memory (all tiles are two 64-column chunks of [128 rows x 128 B],
 // 128-byte swizzle, i.e. the TMA box layout): Q, K[2], V[2], P = 192 KB, so
@@ -53,6 +54,7 @@ constexpr int FA_TILE = 2 * FA_CHUNK;        // a 128 x 128 bf16 tile
 constexpr int FA_SMEM = 6 * FA_TILE + 1024 + 256;
 constexpr uint32_t FA_TMEM_COLS = 512;
 constexpr uint32_t FA_O_COL = 256;
+constexpr float FA_RESCALE_LOG2 = 8.f;       // lazy-rescaling threshold (log2 units)
 
 enum : int {
   kErrFaQ = 0x4101,
@@ -309,8 +311,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       for (int i = 0; i < 128; ++i) red[i & 7] = fmaxf(red[i & 7], s[i]);
       const float tile_max = fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])),
                                    fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
-      const float mx = fmaxf(m, tile_max * a.scale_log2);  // running max, base-2 scaled domain
-      const float corr = (m == -INFINITY) ? 0.f : fast_exp2(m - mx);
+      // Lazy rescaling: the reference max m moves (and O, l are rescaled)
+      // only when the row max exceeds it by more than FA_RESCALE_LOG2; below
+      // that, P = exp2(s - m) stays under 2^FA_RESCALE_LOG2, exact enough in
+      // bf16 / fp32, and O and l keep one consistent reference.
+      const float row_max = tile_max * a.scale_log2;        // base-2 scaled domain
+      const bool move = m == -INFINITY || row_max > m + FA_RESCALE_LOG2;
+      const float mx = move ? fmaxf(m, row_max) : m;
+      const float corr = (m == -INFINITY) ? 0.f : (move ? fast_exp2(m - mx) : 1.f);
       const float mref = (mx == -INFINITY) ? 0.f : mx;
 #pragma unroll
       for (int c = 0; c < 8; ++c) red[c] = 0.f;
