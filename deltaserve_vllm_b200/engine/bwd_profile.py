@@ -2,7 +2,7 @@
 
     python -m deltaserve_vllm_b200.engine.bwd_profile [--model llama3-8b] [--seqs 8] [--seq-len 512]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
-        --master-port 29610 -m deltaserve_vllm_b200.engine.bwd_profile --out gpurun_out/bwd_tpN.json
+        --master-port 29610 -m deltaserve_vllm_b200.engine.bwd_profile --out bwd_tpN.json
 
 Builds the trainer exactly as the engine does (random-init base weights at this
 TP degree, the served LoRA slot of the trained adapter, the backward's own
