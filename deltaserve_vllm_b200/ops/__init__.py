@@ -81,6 +81,26 @@ def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=Non
                     save_dst, aux=aux, aux_out=aux_out)
 
 
+def gemm_ag(ws, rows_per_rank, b, out, *, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0):
+    """All-gather -> column-parallel GEMM over the ranks of ``ws`` (an
+    :class:`~..parallel.peer.AGPeerWorkspace`): ``out[M, N] = A_all @ b.T``
+    (+ the segmented LoRA expand ``z @ b2.T``; SwiGLU with ``EPI_SWIGLU``)
+    where rank ``r``'s rows ``ws.local[:rows_per_rank]`` are rows
+    ``[r * rows_per_rank, (r + 1) * rows_per_rank)`` of ``A_all``
+    (``rows_per_rank`` a multiple of 128), read by the GEMM straight from the
+    owning rank's memory."""
+    _native().gemm_ag(ws.maps, rows_per_rank, ws.world, ws.local, b, out, epi, z, b2, tile_slots, lora_seg)
+    return out
+
+
+def lora_shrink_ag(ws, rows_per_rank, A, slot_ids, Z, seg):
+    """The LoRA shrink of the all-gathered input of :func:`gemm_ag` (rows read
+    from their owners): ``Z[M, slots * seg]``, each row's own slot segment."""
+    slots, pr, K = A.shape
+    _native().lora_shrink_ag(ws.maps, rows_per_rank, ws.world, ws.local, A.reshape(slots * pr, K), slot_ids, Z, pr, seg)
+    return Z
+
+
 def gemm_ar(a, b, ws, *, z=None, b2=None, tile_slots=None, lora_seg=0, force_splits=0, force_reducers=-1):
     """All-reduce over the ranks of ``ws`` (a :class:`~..parallel.peer.PeerWorkspace`)
     of ``a @ b.T`` (+ the segmented LoRA expand), in ONE kernel: the GEMM

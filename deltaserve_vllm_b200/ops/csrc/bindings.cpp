@@ -88,6 +88,12 @@ void dsv_qk_norm_rope_cache(torch::Tensor qkv, torch::Tensor positions, torch::T
                             int64_t num_heads, int64_t num_kv_heads, c10::optional<torch::Tensor> k_cache,
                             c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slot_mapping);
 void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, torch::Tensor Z, int64_t seg);
+torch::Tensor dsv_peer_tmaps(torch::Tensor ptrs, int64_t rows, int64_t cols, int64_t ld);
+void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor a_local, torch::Tensor b,
+                 torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
+                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg);
+void dsv_lora_shrink_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor x_local, torch::Tensor A,
+                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg);
 void dsv_embedding_peer(torch::Tensor ids, torch::Tensor tables, int64_t v_local, int64_t vocab, torch::Tensor out);
 void dsv_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t v0);
 void dsv_ce_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss,
@@ -140,6 +146,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm", &dsv_rms_norm, "RMSNorm / fused residual add + RMSNorm (+ row capture)");
   m.def("qk_norm_rope_cache", &dsv_qk_norm_rope_cache, "q/k norm + RoPE + paged KV write");
   m.def("lora_shrink", &dsv_lora_shrink, "segmented multi-LoRA shrink");
+  m.def("peer_tmaps", &dsv_peer_tmaps, "TMA tensor maps of the ranks' peer buffers (A operand of the all-gather GEMMs)");
+  m.def("gemm_ag", &dsv_gemm_ag, "all-gather -> column-parallel GEMM: A row blocks read from their owner ranks by TMA");
+  m.def("lora_shrink_ag", &dsv_lora_shrink_ag, "LoRA shrink of an all-gathered input (rows read from their owners)");
   m.def("embedding_peer", &dsv_embedding_peer, "vocab-parallel embedding read from every rank's shard over peer memory");
   m.def("embedding", &dsv_embedding, "vocab-parallel embedding gather");
   m.def("ce_fwd_bwd", &dsv_ce_fwd_bwd, "cross-entropy loss + gradient rows");

@@ -24,6 +24,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -94,6 +95,12 @@ struct GemmArgs {
   // ends: the producer waits for it (griddep_wait) before its first LoRA block, or
   // at the end when none of its tiles has one (the grid never outlives the shrink).
   int wait_prev;
+  // All-gather -> GEMM: the 128-row blocks of A come from the rank that owns
+  // them (ag_rows rows per rank, a multiple of 128), each through that rank's
+  // tensor map (ag_maps: ag_world maps in global memory over the ranks' peer
+  // buffers; TMA loads from peer memory, no multicast). Null: A is local.
+  const CUtensorMap* ag_maps;
+  int ag_rows, ag_world;
   float* partial;         // [k_splits, M, N]
   PeerArgs peer;          // kEpiPeerAR only
   // kEpiShrink: B is the stacked LoRA A [slots * pr, K]; output column
@@ -768,6 +775,8 @@ __global__ void __launch_bounds__(256, 1)
     // ------------------------------------------------------------ producer
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.ag_maps != nullptr)
+      for (int r = 0; r < args.ag_world; ++r) tma_prefetch_desc(&args.ag_maps[r]);
     if (args.lora_seg > 0) {
       tma_prefetch_desc(&tmZ);
       tma_prefetch_desc(&tmB2);
@@ -798,7 +807,10 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int jj = 0; jj < BM / 64; ++jj) tma_load_2d(sA + jj * (64 * BK * 2), &tmA, &full_bar[stage], m0 + jj * 64, k0);
           } else {
-            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+            if (args.ag_maps != nullptr)   // this row block from its owner's shard
+              tma_load_2d(sA, &args.ag_maps[m0 / args.ag_rows], &full_bar[stage], k0, m0 % args.ag_rows);
+            else
+              tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
           }
           if constexpr (B_MN) {
 #pragma unroll
@@ -1874,6 +1886,112 @@ void dsv_lora_shrink_tc(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids
   args.shrink_pr = (int)pr;
   args.shrink_seg = (int)seg;
   CUtensorMap ta = make_tmap_bf16(x.data_ptr(), T, K, x.stride(0), BM);
+  CUtensorMap tb = make_tmap_bf16(A.data_ptr(), N, K, A.stride(0), BN);
+  launch<BN, false, kEpiShrink>(ta, tb, ta, tb, args, at::cuda::getCurrentCUDAStream());
+}
+
+// Tensor maps ({64 columns, 128 rows} boxes, 128-byte swizzle) of `rows` x
+// `cols` bf16 matrices with leading dimension `ld` at each address of `ptrs`
+// (int64 CPU tensor, one per rank): the A operand of the all-gather GEMMs.
+// Returns their bytes (uint8 CPU [n, 128]) for the caller to place on the device.
+torch::Tensor dsv_peer_tmaps(torch::Tensor ptrs, int64_t rows, int64_t cols, int64_t ld) {
+  using namespace dsv;
+  TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == at::kLong && ptrs.dim() == 1 && ptrs.numel() <= kMaxPeers,
+              "peer_tmaps: ptrs must be an int64 CPU tensor of <= 8 addresses");
+  static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap is 128 bytes");
+  auto out = torch::empty({ptrs.numel(), 128}, torch::dtype(torch::kUInt8));
+  for (int64_t r = 0; r < ptrs.numel(); ++r) {
+    const CUtensorMap m = make_tmap_bf16(reinterpret_cast<const void*>(ptrs[r].item<int64_t>()), rows, cols, ld, BM);
+    std::memcpy(out.data_ptr<uint8_t>() + r * 128, &m, 128);
+  }
+  return out;
+}
+
+namespace {
+void check_ag(const torch::Tensor& maps, int64_t ag_rows, int64_t world, const torch::Tensor& a_local) {
+  TORCH_CHECK(maps.is_cuda() && maps.scalar_type() == at::kByte && maps.is_contiguous() && maps.numel() == world * 128 &&
+                  reinterpret_cast<uintptr_t>(maps.data_ptr()) % 64 == 0,
+              "gemm_ag: maps must be a 64-byte aligned uint8 CUDA tensor [world, 128]");
+  TORCH_CHECK(world >= 1 && world <= dsv::kMaxPeers && ag_rows > 0 && ag_rows % dsv::BM == 0,
+              "gemm_ag: rows per rank must be a positive multiple of 128, world <= 8");
+  TORCH_CHECK(a_local.is_cuda() && a_local.scalar_type() == at::kBFloat16 && a_local.dim() == 2 &&
+                  a_local.stride(1) == 1 && a_local.size(0) >= ag_rows,
+              "gemm_ag: a_local must be this rank's bf16 shard [>= ag_rows, K]");
+}
+}  // namespace
+
+// out[M, N] = A_all @ b^T (+ LoRA expand) with M = ag_rows * world, where
+// A_all's rows [r * ag_rows, (r + 1) * ag_rows) are rank r's shard, read by
+// TMA straight from that rank's memory (the all-gather fused into the GEMM's
+// loads). epi: bf16 store or SwiGLU.
+void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor a_local, torch::Tensor b,
+                 torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
+                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg) {
+  using namespace dsv;
+  check_ag(maps, ag_rows, world, a_local);
+  TORCH_CHECK(epi == kEpiBF16 || epi == kEpiSwiGLU, "gemm_ag: bf16 or SwiGLU epilogue");
+  TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.stride(1) == 1 &&
+                  b.size(1) == a_local.size(1), "gemm_ag: b must be bf16 [N, K]");
+  const int M = (int)(ag_rows * world), K = (int)a_local.size(1), N = (int)b.size(0);
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(0) >= M &&
+                  out.size(1) == (epi == kEpiSwiGLU ? N / 2 : N), "gemm_ag: out must be bf16 [M, N (or N/2)]");
+  if (epi == kEpiSwiGLU) TORCH_CHECK(N % 128 == 0, "gemm_ag: SwiGLU needs N % 128 == 0");
+  c10::cuda::CUDAGuard guard(b.device());
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.k_splits = 1;
+  args.C = out.data_ptr();
+  args.ldc = (int)out.stride(0);
+  args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
+  args.ag_rows = (int)ag_rows;
+  args.ag_world = (int)world;
+  const int bn = (epi == kEpiSwiGLU) ? std::max(128, pick_bn(M, N, (int)epi, false)) : pick_bn(M, N, (int)epi, false);
+  CUtensorMap ta = make_tmap_bf16(a_local.data_ptr(), a_local.size(0), K, a_local.stride(0), BM);
+  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
+  CUtensorMap tz = ta, tb2 = tb;
+  if (lora_seg > 0) {
+    TORCH_CHECK(z.has_value() && b2.has_value() && tile_slots.has_value(), "gemm_ag: LoRA operands missing");
+    TORCH_CHECK(lora_seg % 64 == 0 && z->size(0) >= M && b2->size(0) == N && z->size(1) == b2->size(1) &&
+                    tile_slots->numel() >= (M + BM - 1) / BM, "gemm_ag: LoRA shapes");
+    tz = make_tmap_bf16(z->data_ptr(), M, z->size(1), z->stride(0), BM);
+    tb2 = make_tmap_bf16(b2->data_ptr(), N, b2->size(1), b2->stride(0), bn);
+    args.lora_seg = (int)lora_seg;
+    args.num_slots = (int)(z->size(1) / lora_seg);
+    args.tile_slots = reinterpret_cast<const uint32_t*>(tile_slots->data_ptr<int>());
+  }
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  if (epi == kEpiSwiGLU) dispatch_bn<false, kEpiSwiGLU>(bn, ta, tb, tz, tb2, args, s);
+  else dispatch_bn<false, kEpiBF16>(bn, ta, tb, tz, tb2, args, s);
+}
+
+// The LoRA shrink of an all-gathered input: Z[M, slots * seg] for the
+// M = ag_rows * world rows of every rank's shard (A rows read from their
+// owners as in dsv_gemm_ag), each row keeping its own slot's segment.
+void dsv_lora_shrink_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor x_local, torch::Tensor A,
+                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg) {
+  using namespace dsv;
+  check_ag(maps, ag_rows, world, x_local);
+  constexpr int BN = 64;
+  const int M = (int)(ag_rows * world), K = (int)x_local.size(1), N = (int)A.size(0);
+  TORCH_CHECK(A.size(1) == K && A.is_contiguous() && N % pr == 0 && Z.size(1) == (N / pr) * seg && Z.size(0) >= M &&
+                  slot_ids.numel() >= M, "lora_shrink_ag: shapes");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmArgs args{};
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.k_splits = 1;
+  args.C = Z.data_ptr();
+  args.ldc = (int)Z.stride(0);
+  args.shrink_slot_ids = slot_ids.data_ptr<int>();
+  args.shrink_pr = (int)pr;
+  args.shrink_seg = (int)seg;
+  args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
+  args.ag_rows = (int)ag_rows;
+  args.ag_world = (int)world;
+  CUtensorMap ta = make_tmap_bf16(x_local.data_ptr(), x_local.size(0), K, x_local.stride(0), BM);
   CUtensorMap tb = make_tmap_bf16(A.data_ptr(), N, K, A.stride(0), BN);
   launch<BN, false, kEpiShrink>(ta, tb, ta, tb, args, at::cuda::getCurrentCUDAStream());
 }

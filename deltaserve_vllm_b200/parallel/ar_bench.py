@@ -6,7 +6,8 @@
 Shapes are Llama-3-8B's row-parallel projections at this TP degree
 (o: K = 4096/tp, down: K = 14336/tp, N = 4096) for a decode step (M = 64) up
 to prefill steps (M = 4096, 8192), then the backward's residual-gradient
-reductions (see ``_backward_cases``). Each variant is timed with CUDA events over
+reductions (see ``_backward_cases``) and the all-gather -> column-parallel
+GEMMs (see ``_all_gather_cases``). Each variant is timed with CUDA events over
 ``iters`` launches after warm-up; the max over ranks is reported. The
 roofline of the fused path is the slower of its FLOPs at the measured bf16
 peak and the bytes each rank must send over NVLink at 770 GB/s per direction
@@ -99,6 +100,7 @@ def main(argv=None) -> None:
                               "roofline_ms": round(bound_ms, 4), "frac_roofline": round(bound_ms / t_fused, 3),
                               "max_rel_err": round(err, 5), "peaks": peak["src"]}), flush=True)
     _backward_cases(comm, args.iters, peak, g)
+    _all_gather_cases(comm, args.iters, peak, g)
     assert ops.check_device_error() == 0
     ws.close()
     dist.destroy_process_group()
@@ -148,6 +150,52 @@ def _backward_cases(comm, iters: int, peak: dict, g) -> None:
                               "speedup_vs_nccl_f32": round(t_n32 / t_f, 3), "roofline_ms": round(bound, 4),
                               "frac_roofline": round(bound / t_f, 3), "peaks": peak["src"]}), flush=True)
     bws.close()
+
+
+def _all_gather_cases(comm, iters: int, peak: dict, g) -> None:
+    """All-gather -> column-parallel GEMM (qkv, gate_up + SwiGLU) at Llama-3-8B
+    shapes: the GEMM reading each row block from its owner's memory by TMA
+    (``ops.gemm_ag``) against NCCL all-gather into a local tensor + GEMM.
+    Roofline: the slower of the GEMM at peak and the (tp-1)/tp of the rows
+    that cross NVLink at 770 GB/s."""
+    from .peer import AGPeerWorkspace
+    tp, rank = comm.size, comm.rank
+    D = 4096
+    ws = AGPeerWorkspace(comm, 8192 // tp, D)
+    for M in (1024, 4096, 8192):
+        rows = M // tp
+        if rows % 128:
+            continue
+        x = torch.randn(rows, D, generator=g, device="cuda").bfloat16()
+        ws.local[:rows].copy_(x)
+        full = torch.empty(M, D, dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        comm.barrier()
+        for name, N, epi in [("qkv", 6144 // tp, ops.EPI_BF16), ("gate_up_swiglu", 2 * 14336 // tp, ops.EPI_SWIGLU)]:
+            w = (torch.randn(N, D, generator=g, device="cuda") * 0.02).bfloat16()
+            out = torch.empty(M, N // 2 if epi == ops.EPI_SWIGLU else N, dtype=torch.bfloat16, device="cuda")
+
+            def fused():
+                ops.gemm_ag(ws, rows, w, out, epi=epi)
+
+            def nccl():
+                dist.all_gather_into_tensor(full, x)
+                ops.gemm(full, w, out, epi=epi)
+
+            def gemm_only():
+                ops.gemm(full, w, out, epi=epi)
+
+            t_f, t_n, t_g = _time(fused, iters), _time(nccl, iters), _time(gemm_only, iters)
+            flops = 2 * M * N * D
+            nvl = (tp - 1) / tp * M * D * 2
+            bound = max(flops / (peak["bf16_tflops"] * 1e9), nvl / (NVLINK_GBS * 1e6))
+            if rank == 0:
+                print(json.dumps({"case": f"ag_{name}_m{M}", "tp": tp, "M": M, "N": N, "K": D,
+                                  "gemm_ms": round(t_g, 4), "ag_nccl_gemm_ms": round(t_n, 4),
+                                  "fused_ms": round(t_f, 4), "speedup_vs_nccl": round(t_n / t_f, 3),
+                                  "roofline_ms": round(bound, 4), "frac_roofline": round(bound / t_f, 3),
+                                  "peaks": peak["src"]}), flush=True)
+    ws.close()
 
 
 if __name__ == "__main__":

@@ -145,6 +145,51 @@ class PeerTable:
         self.base = None
 
 
+class AGPeerWorkspace:
+    """Row shards of an activation in peer-mapped memory, for the all-gather
+    -> column-parallel GEMM (``ops.gemm_ag``): rank ``r`` writes its rows into
+    ``local`` ([max_rows_per_rank, cols] bf16); the GEMM reads row block ``b``
+    from rank ``b * 128 // rows_per_rank`` through that rank's TMA tensor map
+    (``maps``, in device memory), so the gather happens inside the GEMM's loads
+    and no rank holds the gathered activation."""
+
+    def __init__(self, comm, max_rows_per_rank: int, cols: int, device=None):
+        from .. import ops
+        ext = ops.native_ext()
+        if ext is None:
+            raise RuntimeError("the all-gather GEMM workspace needs the CUDA extension")
+        self.comm = comm
+        self.world = comm.size if comm is not None else 1
+        self.rank = comm.rank if comm is not None else 0
+        if self.world > 8:
+            raise ValueError("up to 8 ranks")
+        self.rows_cap = -(-int(max_rows_per_rank) // TILE) * TILE
+        self.cols = int(cols)
+        self._ext = ext
+        self.base, handle = ext.peer_alloc(_align(self.rows_cap * self.cols * 2))
+        handles = comm.all_gather_object(handle) if self.world > 1 else [handle]
+        self.ptrs = [self.base if r == self.rank else ext.peer_open(h) for r, h in enumerate(handles)]
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.local = _from_ptr(self.base, (self.rows_cap, self.cols), torch.bfloat16, dev.index)
+        host_maps = ext.peer_tmaps(torch.tensor(self.ptrs, dtype=torch.int64), self.rows_cap, self.cols, self.cols)
+        self.maps = host_maps.to(dev)           # 128 B per map, from a 256-byte aligned allocation
+        if comm is not None and self.world > 1:
+            comm.barrier()
+
+    def close(self) -> None:
+        if self.base is None:
+            return
+        torch.cuda.synchronize()
+        if self.comm is not None and self.world > 1:
+            self.comm.barrier()
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._ext.peer_close(p)
+        self.local = None
+        self._ext.peer_free(self.base)
+        self.base = None
+
+
 class BwdPeerWorkspace:
     """Peer-mapped buffers of the tensor-parallel backward's residual-gradient
     reductions (``ops.gemm_push`` + ``ops.tp_reduce_rows``): the dX GEMM

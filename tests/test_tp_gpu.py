@@ -281,3 +281,72 @@ def test_embedding_from_peer_shards(world):
         mp.start_processes(_run_embedding_peer, args=(world, _port(), d), nprocs=world, join=True,
                            start_method="spawn")
         assert all(torch.load(os.path.join(d, "emb.pt"))["oks"])
+
+
+def _run_gemm_ag(rank, world, port, outdir):
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank))
+    from deltaserve_vllm_b200 import ops
+    from deltaserve_vllm_b200.parallel.comm import TPComm
+    from deltaserve_vllm_b200.parallel.peer import AGPeerWorkspace
+    comm = TPComm(None, dist.new_group(backend="gloo"))
+    K, rows = 1024, 256                       # rows per rank (multiple of 128)
+    M = rows * world
+    ws = AGPeerWorkspace(comm, 384, K)
+    g = torch.Generator(device="cuda").manual_seed(10 + rank)
+    x = torch.randn(rows, K, generator=g, device="cuda").to(torch.bfloat16)
+    ws.local[:rows].copy_(x)
+    torch.cuda.synchronize()
+    comm.barrier()                            # every shard written before any rank reads it
+    gw = torch.Generator(device="cuda").manual_seed(99)
+    N = 768
+    w = (torch.randn(N, K, generator=gw, device="cuda") * 0.05).to(torch.bfloat16)
+    full = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")
+    dist.all_gather_into_tensor(full, x)
+    res = {}
+    # plain bf16
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm_ag(ws, rows, w, out)
+    ref = torch.empty_like(out)
+    ops.gemm(full, w, ref)
+    res["bf16"] = float((out.float() - ref.float()).abs().max() / ref.float().abs().max())
+    # SwiGLU + LoRA expand, with the shrink of the gathered rows
+    slots, pr, seg = 2, 32, 64
+    A = (torch.randn(slots, pr, K, generator=gw, device="cuda") * 0.05).to(torch.bfloat16)
+    B2 = (torch.randn(N, slots * seg, generator=gw, device="cuda") * 0.05).to(torch.bfloat16)
+    sid = (torch.arange(M, device="cuda", dtype=torch.int32) // 100) % slots
+    mask = torch.full(((M + 127) // 128,), 3, dtype=torch.int32, device="cuda")
+    Z = torch.empty(M, slots * seg, dtype=torch.bfloat16, device="cuda")
+    ops.lora_shrink_ag(ws, rows, A, sid, Z, seg)
+    Zr = torch.empty_like(Z)
+    ops.lora_shrink(full, A, sid, Zr, seg)
+    res["shrink"] = float((Z.float() - Zr.float()).abs().max() / Zr.float().abs().max())
+    o2 = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
+    ops.gemm_ag(ws, rows, w, o2, epi=ops.EPI_SWIGLU, z=Z, b2=B2, tile_slots=mask, lora_seg=seg)
+    r2 = torch.empty_like(o2)
+    ops.gemm(full, w, r2, epi=ops.EPI_SWIGLU, z=Zr, b2=B2, tile_slots=mask, lora_seg=seg)
+    res["swiglu_lora"] = float((o2.float() - r2.float()).abs().max() / r2.float().abs().max())
+    torch.cuda.synchronize()
+    res["code"] = ops.check_device_error()
+    allres = comm.all_gather_object(res)
+    comm.barrier()
+    ws.close()
+    if rank == 0:
+        torch.save({"res": allres}, os.path.join(outdir, "ag.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gemm_all_gather(world):
+    """All-gather -> GEMM with the row blocks read from their owners' memory
+    (bf16 and SwiGLU + LoRA expand epilogues, and the shrink of the gathered
+    rows) == NCCL all-gather then the local GEMM (which may split K: equal
+    to bf16 rounding)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_run_gemm_ag, args=(world, _port(), d), nprocs=world, join=True, start_method="spawn")
+        for r in torch.load(os.path.join(d, "ag.pt"))["res"]:
+            assert r["code"] == 0
+            assert r["bf16"] < 1e-2 and r["shrink"] < 1e-2 and r["swiglu_lora"] < 1e-2, r
