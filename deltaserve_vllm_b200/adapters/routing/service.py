@@ -9,6 +9,12 @@ a GPU slot) or is *held* until the pool can give its adapter a slot (evicting
 the least-used slot holder that no running request uses). The request keeps
 its real arrival time throughout, so TTFT includes the hold.
 
+With ``route_encode_async`` (default) the encoder call runs on a worker
+thread: ``tick`` hands the batch over and applies its decisions on the first
+tick after they are ready, so the engine keeps stepping (and its GPU work
+keeps flowing) while the encoder tokenizes and runs; at most one batch is in
+flight and the next one collects the requests that arrived meanwhile.
+
 Reference: ``deltaserve-plugin/deltaserve/adapter_routing/engine.py:37-391``
 and ``engine_router.py:178-380`` (held routed requests, encode step, slot
 placement), re-built around this engine's own slot table.
@@ -87,6 +93,10 @@ class AdapterRouter:
                              tier_of=lambda n: self.pool.entries[n].tier if n in self.pool.entries else "")
         self.pool.listeners.append(lambda p: self.router.set_index(p.index))
         self.pending: deque = deque()   # (rid, ids, params, text, adapter, arrival, future)
+        self._encode_pool = (cf.ThreadPoolExecutor(1, thread_name_prefix="dsv-route-encode")
+                             if cfg.route_encode_async else None)
+        self._inflight = None           # (batch, future of the decisions, t0) of the async encode step
+        self._cancelled: set = set()    # requests cancelled while their batch is being encoded
         self.held: deque = deque()      # (rid, ids, params, adapter, arrival)
         self.indexing: dict[str, tuple] = {}     # name -> (job, path, fingerprint)
         engine.request_listeners.append(self._on_request)
@@ -175,7 +185,7 @@ class AdapterRouter:
         return fut
 
     def has_pending(self) -> bool:
-        return bool(self.pending or self.held)
+        return bool(self.pending or self.held or self._inflight is not None)
 
     def cancel(self, rid: str) -> bool:
         """Drop a request still waiting for its route decision or for its
@@ -187,6 +197,9 @@ class AdapterRouter:
                     if q is self.pending and not item[-1].done():
                         item[-1].cancel()
                     return True
+        if self._inflight is not None and any(item[0] == rid for item in self._inflight[0]):
+            self._cancelled.add(rid)    # dropped when its batch's decisions are applied
+            return True
         return False
 
     def _in_use(self) -> set[str]:
@@ -201,32 +214,27 @@ class AdapterRouter:
             self.indexer_service.placement.note_inference()
         if self.indexing:
             self._poll_indexing()
-        if self.pending:
+        if self._inflight is not None and self._inflight[1].done():
+            batch, fut_dec, t0 = self._inflight
+            self._inflight = None
+            try:
+                decisions = fut_dec.result()
+            except Exception as e:  # the encoder failed: every request of the batch gets the error
+                for item in batch:
+                    if not item[-1].done():
+                        item[-1].set_exception(e)
+                decisions = None
+            if decisions is not None:
+                self._apply(batch, decisions, t0)
+        if self.pending and self._inflight is None:
             batch = list(self.pending)
             self.pending.clear()
             texts = [b[3] for b in batch if b[4] is None]
             t0 = time.perf_counter()
-            decisions = iter(self.router.route_many(texts)) if texts else iter(())
-            if texts:
-                self.stats["encode_calls"] += 1
-                self.stats["encode_ms"] += (time.perf_counter() - t0) * 1e3
-            for rid, ids, params, text, named, arrival, fut in batch:
-                d = RouteDecision(named) if named is not None else next(decisions)
-                try:
-                    if d.adapter is None:
-                        self.stats["fallback"] += 1
-                        self._enter(rid, ids, params, None, arrival)
-                    else:
-                        self.stats["routed"] += 1
-                        self.pool.note_hit(d.adapter, self._in_use(), place=True)
-                        if self.pool.entries[d.adapter].tier == GPU:
-                            self._enter(rid, ids, params, d.adapter, arrival)
-                        else:
-                            self.stats["held"] += 1
-                            self.held.append((rid, ids, params, d.adapter, arrival))
-                    fut.set_result(d)
-                except Exception as e:  # reported to the HTTP handler
-                    fut.set_exception(e)
+            if texts and self._encode_pool is not None:
+                self._inflight = (batch, self._encode_pool.submit(self.router.route_many, texts), t0)
+            else:
+                self._apply(batch, self.router.route_many(texts) if texts else [], t0)
         if self.held:
             keep = deque()
             while self.held:
@@ -239,6 +247,35 @@ class AdapterRouter:
                     keep.append((rid, ids, params, adapter, arrival))
             self.held = keep
 
+    def _apply(self, batch, decisions, t0: float) -> None:
+        """Enter, hold or fall back every request of an encoded batch."""
+        if any(b[4] is None for b in batch):
+            self.stats["encode_calls"] += 1
+            self.stats["encode_ms"] += (time.perf_counter() - t0) * 1e3
+        it = iter(decisions)
+        for rid, ids, params, text, named, arrival, fut in batch:
+            d = RouteDecision(named) if named is not None else next(it)
+            if rid in self._cancelled:
+                self._cancelled.discard(rid)
+                if not fut.done():
+                    fut.cancel()
+                continue
+            try:
+                if d.adapter is None:
+                    self.stats["fallback"] += 1
+                    self._enter(rid, ids, params, None, arrival)
+                else:
+                    self.stats["routed"] += 1
+                    self.pool.note_hit(d.adapter, self._in_use(), place=True)
+                    if self.pool.entries[d.adapter].tier == GPU:
+                        self._enter(rid, ids, params, d.adapter, arrival)
+                    else:
+                        self.stats["held"] += 1
+                        self.held.append((rid, ids, params, d.adapter, arrival))
+                fut.set_result(d)
+            except Exception as e:  # reported to the HTTP handler
+                fut.set_exception(e)
+
     def status(self) -> dict:
         return {"pool": self.pool.status(), "model": self.router.model.describe(),
                 "pending": len(self.pending), "held": len(self.held), "stats": dict(self.stats),
@@ -246,6 +283,9 @@ class AdapterRouter:
                 "indexer": self.indexer_service.describe() if self.indexer_service is not None else None}
 
     def stop(self) -> None:
+        if self._encode_pool is not None:
+            self._encode_pool.shutdown(wait=True)
+            self._encode_pool = None
         for job, _, _ in self.indexing.values():
             job.stop()
         if self.indexer_service is not None:

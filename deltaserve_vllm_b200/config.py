@@ -175,6 +175,7 @@ class AdapterRoutingConfig:
     router_device: str = "auto"
     router_gpu: int | None = None
     route_encode_max_tokens: int = 1024
+    route_encode_async: bool = True
     adapter_copy_ms: float = 4.5
     adapter_read_ms: float = 13.5
     encoder: str = "intfloat/e5-large-v2"

@@ -432,3 +432,42 @@ def test_routing_with_a_sentence_encoder_directory():
             hits += d.adapter == name
         assert hits >= 3, hits
         eng.close()
+
+
+def test_encode_step_runs_off_the_engine_thread():
+    """With the asynchronous encode step the engine thread only hands the
+    batch over: the decisions land on a later tick, a request cancelled while
+    its batch is encoded is dropped, and has_pending covers the batch in
+    flight."""
+    import threading
+    import time
+    with tempfile.TemporaryDirectory() as tmp:
+        eng = _routing_engine(tmp, slots=2)
+        t0 = time.time()
+        while eng.router.indexing and time.time() - t0 < 60:
+            eng.router.tick()
+            time.sleep(0.01)
+        r = eng.router
+        gate = threading.Event()
+        inner = r.router.encoder
+
+        class Slow:
+            def encode(self, texts):
+                gate.wait(10)
+                return inner.encode(texts)
+
+        r.router.encoder = Slow()
+        f1 = r.submit("a1", [1, 2, 3], None, text="bake bread with yeast and flour")
+        f2 = r.submit("a2", [1, 2, 3], None, text="bond yields and interest rates")
+        r.tick()
+        assert r._inflight is not None and r.has_pending() and not f1.done()
+        assert r.cancel("a2")
+        gate.set()
+        t0 = time.time()
+        while r._inflight is not None and time.time() - t0 < 10:
+            time.sleep(0.01)
+            r.tick()
+        assert f1.done() and f1.result().adapter == "cooking"
+        assert f2.cancelled()
+        assert "a1" in eng.requests and "a2" not in eng.requests
+        eng.close()
