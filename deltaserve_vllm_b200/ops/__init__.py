@@ -81,23 +81,42 @@ def gemm(a, b, out, *, b_mn=False, epi=EPI_BF16, z=None, b2=None, tile_slots=Non
                     save_dst, aux=aux, aux_out=aux_out)
 
 
-def gemm_ag(ws, rows_per_rank, b, out, *, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0):
+def gemm_ag(ws, rows_per_rank, b, out, *, epi=EPI_BF16, z=None, b2=None, tile_slots=None, lora_seg=0,
+            fresh=True, copy_once=True):
     """All-gather -> column-parallel GEMM over the ranks of ``ws`` (an
     :class:`~..parallel.peer.AGPeerWorkspace`): ``out[M, N] = A_all @ b.T``
     (+ the segmented LoRA expand ``z @ b2.T``; SwiGLU with ``EPI_SWIGLU``)
     where rank ``r``'s rows ``ws.local[:rows_per_rank]`` are rows
     ``[r * rows_per_rank, (r + 1) * rows_per_rank)`` of ``A_all``
-    (``rows_per_rank`` a multiple of 128), read by the GEMM straight from the
-    owning rank's memory."""
-    _native().gemm_ag(ws.maps, rows_per_rank, ws.world, ws.local, b, out, epi, z, b2, tile_slots, lora_seg)
+    (``rows_per_rank`` a multiple of 128). Every rank's shard must be written
+    before any rank calls this. ``fresh``: the shards hold new rows since the
+    last call (the copy-once gather starts over; ``False`` reuses the rows an
+    earlier call of the same shards gathered)."""
+    if copy_once:
+        if fresh:
+            ws.cnt.zero_()
+        _native().gemm_ag(ws.maps, rows_per_rank, ws.world, ws.local, b, out, epi, z, b2, tile_slots, lora_seg,
+                          ws.gathered, ws.cnt, ws.src, ws.rank)
+    else:
+        _native().gemm_ag(ws.maps, rows_per_rank, ws.world, ws.local, b, out, epi, z, b2, tile_slots, lora_seg,
+                          None, None, None, ws.rank)
     return out
 
 
-def lora_shrink_ag(ws, rows_per_rank, A, slot_ids, Z, seg):
-    """The LoRA shrink of the all-gathered input of :func:`gemm_ag` (rows read
-    from their owners): ``Z[M, slots * seg]``, each row's own slot segment."""
+def lora_shrink_ag(ws, rows_per_rank, A, slot_ids, Z, seg, fresh=True, copy_once=True):
+    """The LoRA shrink of the all-gathered input of :func:`gemm_ag`:
+    ``Z[M, slots * seg]``, each row's own slot segment (``fresh`` and
+    ``copy_once`` as for :func:`gemm_ag`; a following ``gemm_ag`` with
+    ``fresh=False`` reuses the rows this call gathered)."""
     slots, pr, K = A.shape
-    _native().lora_shrink_ag(ws.maps, rows_per_rank, ws.world, ws.local, A.reshape(slots * pr, K), slot_ids, Z, pr, seg)
+    if copy_once:
+        if fresh:
+            ws.cnt.zero_()
+        _native().lora_shrink_ag(ws.maps, rows_per_rank, ws.world, ws.local, A.reshape(slots * pr, K), slot_ids, Z,
+                                 pr, seg, ws.gathered, ws.cnt, ws.src, ws.rank)
+    else:
+        _native().lora_shrink_ag(ws.maps, rows_per_rank, ws.world, ws.local, A.reshape(slots * pr, K), slot_ids, Z,
+                                 pr, seg, None, None, None, ws.rank)
     return Z
 
 

@@ -91,9 +91,12 @@ void dsv_lora_shrink(torch::Tensor x, torch::Tensor A, torch::Tensor slot_ids, t
 torch::Tensor dsv_peer_tmaps(torch::Tensor ptrs, int64_t rows, int64_t cols, int64_t ld);
 void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor a_local, torch::Tensor b,
                  torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
-                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg);
+                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, c10::optional<torch::Tensor> gathered,
+                 c10::optional<torch::Tensor> cnt, c10::optional<torch::Tensor> src, int64_t rank);
 void dsv_lora_shrink_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor x_local, torch::Tensor A,
-                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg);
+                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg,
+                        c10::optional<torch::Tensor> gathered, c10::optional<torch::Tensor> cnt,
+                        c10::optional<torch::Tensor> src, int64_t rank);
 void dsv_embedding_peer(torch::Tensor ids, torch::Tensor tables, int64_t v_local, int64_t vocab, torch::Tensor out);
 void dsv_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t v0);
 void dsv_ce_fwd_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor loss,

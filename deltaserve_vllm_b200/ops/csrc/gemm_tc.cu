@@ -45,6 +45,8 @@ template <int EPI>
 constexpr bool a_mn_major() { return EPI == kEpiF32T || EPI == kEpiLoraBt; }
 
 constexpr int kMaxPeers = 8;
+constexpr int kAgChunk = 512;      // columns per copy unit of the gathered all-gather GEMM
+constexpr int kErrWaitGather = 0x4301;
 constexpr int kArSmReserve = 20;  // SMs a fused all-reduce launch leaves free (backward NCCL cap + its waits)
 
 // Fused all-reduce over peer memory (kEpiPeerAR). Every rank holds one
@@ -101,6 +103,20 @@ struct GemmArgs {
   // buffers; TMA loads from peer memory, no multicast). Null: A is local.
   const CUtensorMap* ag_maps;
   int ag_rows, ag_world;
+  // Copy-once gather: the epilogue warps of the running CTAs first copy the
+  // remote row blocks, in units of 128 rows x kAgChunk columns claimed from
+  // *ag_ticket, from the owners' shards (ag_src[r], plain P2P loads) into
+  // this rank's gathered buffer (ag_gathered [M, K], read by the producer
+  // through tmA), adding 1 to ag_cnt[block] per unit; a producer loads a
+  // remote block once its count reached ag_expect (own blocks come from
+  // ag_maps[ag_rank]). So each remote block crosses NVLink once, whatever the
+  // number of N tiles.
+  __nv_bfloat16* ag_gathered;
+  uint32_t* ag_cnt;
+  uint32_t* ag_ticket;
+  uint32_t ag_expect;
+  int ag_rank;
+  const __nv_bfloat16* ag_src[8];
   float* partial;         // [k_splits, M, N]
   PeerArgs peer;          // kEpiPeerAR only
   // kEpiShrink: B is the stacked LoRA A [slots * pr, K]; output column
@@ -792,6 +808,16 @@ __global__ void __launch_bounds__(256, 1)
       const int m0 = tl.mt * BM, n0 = tl.nt * BN;
       const uint32_t slots = tl.slots;
       const int n_lora = __popc(slots) * kb_per_slot;
+      if (args.ag_gathered != nullptr && m0 / args.ag_rows != args.ag_rank) {
+        // A remote row block: wait until every unit of it is in the gathered buffer.
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t n = 0;
+        while (ld_acquire_gpu(&args.ag_cnt[tl.mt]) < args.ag_expect) {
+          if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kWaitNs) { set_error(kErrWaitGather); ok = false; break; }
+        }
+        if (!ok) break;
+        fence_proxy_async_global();     // the copies (generic stores) before this thread's TMA reads
+      }
       for (int j = 0; j < tl.n_main + n_lora; ++j) {
         if (j == tl.n_main && !dep_done) {
           griddep_wait();
@@ -807,7 +833,9 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int jj = 0; jj < BM / 64; ++jj) tma_load_2d(sA + jj * (64 * BK * 2), &tmA, &full_bar[stage], m0 + jj * 64, k0);
           } else {
-            if (args.ag_maps != nullptr)   // this row block from its owner's shard
+            if (args.ag_maps != nullptr && m0 / args.ag_rows == args.ag_rank)
+              tma_load_2d(sA, &args.ag_maps[args.ag_rank], &full_bar[stage], k0, m0 % args.ag_rows);
+            else if (args.ag_maps != nullptr && args.ag_gathered == nullptr)   // straight from the owner
               tma_load_2d(sA, &args.ag_maps[m0 / args.ag_rows], &full_bar[stage], k0, m0 % args.ag_rows);
             else
               tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
@@ -899,6 +927,58 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp - 4;  // TMEM lane quarter
+    if (args.ag_gathered != nullptr) {
+      // Copy-once gather (see GemmArgs::ag_gathered). Units (row block,
+      // kAgChunk columns) are claimed from a ticket counter, so only CTAs that
+      // are running copy and a producer never waits on a CTA that has not
+      // started; a later launch over the same rows (ticket past the end)
+      // copies nothing. Within a unit, 32 lanes cover 512 contiguous bytes of
+      // a row, eight 16-byte loads in flight per thread.
+      const int e = threadIdx.x - 128;
+      const int chunks = (args.K + kAgChunk - 1) / kAgChunk;
+      const int units = num_m_tiles * chunks;
+      __shared__ int ag_unit;
+      for (;;) {
+        if (e == 0) ag_unit = (int)atomicAdd(args.ag_ticket, 1u);
+        named_bar_sync(1, 128);
+        const int u = ag_unit;
+        named_bar_sync(1, 128);
+        if (u >= units || u < 0) break;
+        const int blk = u / chunks, ch = u - blk * chunks;
+        const int owner = blk * BM / args.ag_rows;
+        if (owner == args.ag_rank) continue;                         // own rows are read in place
+        const int c0 = ch * kAgChunk;
+        const int n16 = (min(args.K, c0 + kAgChunk) - c0) / 8;      // 16-byte vectors per row
+        const int total = min(BM, args.M - blk * BM) * n16;
+        const __nv_bfloat16* sbase = args.ag_src[owner] + (size_t)(blk * BM % args.ag_rows) * args.K + c0;
+        __nv_bfloat16* dbase = args.ag_gathered + (size_t)blk * BM * args.K + c0;
+        for (int i0 = e; i0 < total; i0 += 128 * 8) {
+          uint4 v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int i = i0 + k * 128;
+            if (i < total) {
+              const int r = i / n16, c = i - r * n16;
+              v[k] = *reinterpret_cast<const uint4*>(sbase + (size_t)r * args.K + c * 8);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int i = i0 + k * 128;
+            if (i < total) {
+              const int r = i / n16, c = i - r * n16;
+              *reinterpret_cast<uint4*>(dbase + (size_t)r * args.K + c * 8) = v[k];
+            }
+          }
+        }
+        fence_proxy_async_global();        // this thread's stores before the consumers' TMA reads
+        named_bar_sync(1, 128);            // the four epilogue warps' copies of the unit
+        if (e == 0) {
+          __threadfence();
+          red_release_gpu_add(&args.ag_cnt[blk], 1u);
+        }
+      }
+    }
     int iter = 0;
     for (int t = cta0; t < num_tiles; t += ncta, ++iter) {
       const Tile tl = decode_tile(t, args, num_m_tiles, num_n_tiles, kb_main);
@@ -1908,6 +1988,28 @@ torch::Tensor dsv_peer_tmaps(torch::Tensor ptrs, int64_t rows, int64_t cols, int
 }
 
 namespace {
+// Copy-once gather arguments (see GemmArgs::ag_gathered): the gathered buffer
+// [>= M, K] of this rank, the per-block unit counters (zeroed by the caller
+// when the shards hold new rows) and the ranks' shard addresses.
+void set_gather(dsv::GemmArgs& args, const torch::Tensor& gathered, const torch::Tensor& cnt, const torch::Tensor& src,
+                int64_t rank, int M, int K) {
+  using namespace dsv;
+  TORCH_CHECK(gathered.is_cuda() && gathered.scalar_type() == at::kBFloat16 && gathered.is_contiguous() &&
+                  gathered.size(0) >= M && gathered.size(1) == K, "gemm_ag: gathered must be bf16 [>= M, K]");
+  TORCH_CHECK(cnt.is_cuda() && cnt.scalar_type() == at::kInt && cnt.numel() >= (M + BM - 1) / BM + 1,
+              "gemm_ag: cnt must be int32 [>= M / 128 + 1] on the device (block counters, then the ticket)");
+  TORCH_CHECK(src.device().is_cpu() && src.scalar_type() == at::kLong && src.numel() == args.ag_world,
+              "gemm_ag: src must hold the ranks' shard addresses (int64 CPU)");
+  TORCH_CHECK(K % 8 == 0, "gemm_ag: K must be a multiple of 8");
+  args.ag_gathered = reinterpret_cast<__nv_bfloat16*>(gathered.data_ptr());
+  args.ag_cnt = reinterpret_cast<uint32_t*>(cnt.data_ptr<int>());
+  args.ag_ticket = args.ag_cnt + (cnt.numel() - 1);
+  args.ag_expect = (uint32_t)((K + kAgChunk - 1) / kAgChunk);
+  args.ag_rank = (int)rank;
+  for (int r = 0; r < args.ag_world; ++r)
+    args.ag_src[r] = reinterpret_cast<const __nv_bfloat16*>(src[r].item<int64_t>());
+}
+
 void check_ag(const torch::Tensor& maps, int64_t ag_rows, int64_t world, const torch::Tensor& a_local) {
   TORCH_CHECK(maps.is_cuda() && maps.scalar_type() == at::kByte && maps.is_contiguous() && maps.numel() == world * 128 &&
                   reinterpret_cast<uintptr_t>(maps.data_ptr()) % 64 == 0,
@@ -1926,7 +2028,8 @@ void check_ag(const torch::Tensor& maps, int64_t ag_rows, int64_t world, const t
 // loads). epi: bf16 store or SwiGLU.
 void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor a_local, torch::Tensor b,
                  torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> z, c10::optional<torch::Tensor> b2,
-                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg) {
+                 c10::optional<torch::Tensor> tile_slots, int64_t lora_seg, c10::optional<torch::Tensor> gathered,
+                 c10::optional<torch::Tensor> cnt, c10::optional<torch::Tensor> src, int64_t rank) {
   using namespace dsv;
   check_ag(maps, ag_rows, world, a_local);
   TORCH_CHECK(epi == kEpiBF16 || epi == kEpiSwiGLU, "gemm_ag: bf16 or SwiGLU epilogue");
@@ -1947,8 +2050,16 @@ void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tens
   args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
   args.ag_rows = (int)ag_rows;
   args.ag_world = (int)world;
+  args.ag_rank = (int)rank;
   const int bn = (epi == kEpiSwiGLU) ? std::max(128, pick_bn(M, N, (int)epi, false)) : pick_bn(M, N, (int)epi, false);
-  CUtensorMap ta = make_tmap_bf16(a_local.data_ptr(), a_local.size(0), K, a_local.stride(0), BM);
+  CUtensorMap ta;
+  if (gathered.has_value()) {
+    TORCH_CHECK(cnt.has_value() && src.has_value(), "gemm_ag: the copy-once gather needs cnt and src");
+    set_gather(args, *gathered, *cnt, *src, rank, M, K);
+    ta = make_tmap_bf16(gathered->data_ptr(), gathered->size(0), K, K, BM);
+  } else {
+    ta = make_tmap_bf16(a_local.data_ptr(), a_local.size(0), K, a_local.stride(0), BM);
+  }
   CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
   CUtensorMap tz = ta, tb2 = tb;
   if (lora_seg > 0) {
@@ -1970,7 +2081,9 @@ void dsv_gemm_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tens
 // M = ag_rows * world rows of every rank's shard (A rows read from their
 // owners as in dsv_gemm_ag), each row keeping its own slot's segment.
 void dsv_lora_shrink_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torch::Tensor x_local, torch::Tensor A,
-                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg) {
+                        torch::Tensor slot_ids, torch::Tensor Z, int64_t pr, int64_t seg,
+                        c10::optional<torch::Tensor> gathered, c10::optional<torch::Tensor> cnt,
+                        c10::optional<torch::Tensor> src, int64_t rank) {
   using namespace dsv;
   check_ag(maps, ag_rows, world, x_local);
   constexpr int BN = 64;
@@ -1991,7 +2104,15 @@ void dsv_lora_shrink_ag(torch::Tensor maps, int64_t ag_rows, int64_t world, torc
   args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
   args.ag_rows = (int)ag_rows;
   args.ag_world = (int)world;
-  CUtensorMap ta = make_tmap_bf16(x_local.data_ptr(), x_local.size(0), K, x_local.stride(0), BM);
+  args.ag_rank = (int)rank;
+  CUtensorMap ta;
+  if (gathered.has_value()) {
+    TORCH_CHECK(cnt.has_value() && src.has_value(), "lora_shrink_ag: the copy-once gather needs cnt and src");
+    set_gather(args, *gathered, *cnt, *src, rank, M, K);
+    ta = make_tmap_bf16(gathered->data_ptr(), gathered->size(0), K, K, BM);
+  } else {
+    ta = make_tmap_bf16(x_local.data_ptr(), x_local.size(0), K, x_local.stride(0), BM);
+  }
   CUtensorMap tb = make_tmap_bf16(A.data_ptr(), N, K, A.stride(0), BN);
   launch<BN, false, kEpiShrink>(ta, tb, ta, tb, args, at::cuda::getCurrentCUDAStream());
 }

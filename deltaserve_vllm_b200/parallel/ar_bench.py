@@ -51,6 +51,8 @@ def _time(fn, iters: int) -> float:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", choices=["all_reduce", "backward", "all_gather"], default=None,
+                    help="run one group of cases")
     args = ap.parse_args(argv)
     comm = init_tp()
     tp, rank = comm.size, comm.rank
@@ -58,11 +60,13 @@ def main(argv=None) -> None:
     ws = PeerWorkspace(comm, 8192, 4096)
     peak = _peaks()
     g = torch.Generator(device="cuda").manual_seed(rank)
-    for name, M, K in [("o_decode", 64, 4096 // tp), ("down_decode", 64, 14336 // tp),
+    ar_cases = [] if args.only not in (None, "all_reduce") else [
+                       ("o_decode", 64, 4096 // tp), ("down_decode", 64, 14336 // tp),
                        ("o_m256", 256, 4096 // tp), ("o_m1024", 1024, 4096 // tp),
                        ("down_m1024", 1024, 14336 // tp), ("o_m2048", 2048, 4096 // tp),
                        ("o_prefill", 4096, 4096 // tp), ("down_prefill", 4096, 14336 // tp),
-                       ("o_m8192", 8192, 4096 // tp), ("down_m8192", 8192, 14336 // tp)]:
+                       ("o_m8192", 8192, 4096 // tp), ("down_m8192", 8192, 14336 // tp)]
+    for name, M, K in ar_cases:
         N = 4096
         a = torch.randn(M, K, generator=g, device="cuda").bfloat16()
         b = (torch.randn(N, K, generator=g, device="cuda") * 0.02).bfloat16()
@@ -99,8 +103,10 @@ def main(argv=None) -> None:
                               "speedup_vs_nccl": round(t_base / t_fused, 3),
                               "roofline_ms": round(bound_ms, 4), "frac_roofline": round(bound_ms / t_fused, 3),
                               "max_rel_err": round(err, 5), "peaks": peak["src"]}), flush=True)
-    _backward_cases(comm, args.iters, peak, g)
-    _all_gather_cases(comm, args.iters, peak, g)
+    if args.only in (None, "backward"):
+        _backward_cases(comm, args.iters, peak, g)
+    if args.only in (None, "all_gather"):
+        _all_gather_cases(comm, args.iters, peak, g)
     assert ops.check_device_error() == 0
     ws.close()
     dist.destroy_process_group()
@@ -154,8 +160,10 @@ def _backward_cases(comm, iters: int, peak: dict, g) -> None:
 
 def _all_gather_cases(comm, iters: int, peak: dict, g) -> None:
     """All-gather -> column-parallel GEMM (qkv, gate_up + SwiGLU) at Llama-3-8B
-    shapes: the GEMM reading each row block from its owner's memory by TMA
-    (``ops.gemm_ag``) against NCCL all-gather into a local tensor + GEMM.
+    shapes: the GEMM copying each remote row block once from its owner's
+    memory (``ops.gemm_ag``; ``tile_reads_from_owner_ms``: every tile read
+    from the owner by TMA instead) against NCCL all-gather into a local
+    tensor + GEMM.
     Roofline: the slower of the GEMM at peak and the (tp-1)/tp of the rows
     that cross NVLink at 770 GB/s."""
     from .peer import AGPeerWorkspace
@@ -178,6 +186,9 @@ def _all_gather_cases(comm, iters: int, peak: dict, g) -> None:
             def fused():
                 ops.gemm_ag(ws, rows, w, out, epi=epi)
 
+            def direct():
+                ops.gemm_ag(ws, rows, w, out, epi=epi, copy_once=False)
+
             def nccl():
                 dist.all_gather_into_tensor(full, x)
                 ops.gemm(full, w, out, epi=epi)
@@ -185,14 +196,15 @@ def _all_gather_cases(comm, iters: int, peak: dict, g) -> None:
             def gemm_only():
                 ops.gemm(full, w, out, epi=epi)
 
-            t_f, t_n, t_g = _time(fused, iters), _time(nccl, iters), _time(gemm_only, iters)
+            t_f, t_n, t_g, t_d = _time(fused, iters), _time(nccl, iters), _time(gemm_only, iters), _time(direct, iters)
             flops = 2 * M * N * D
             nvl = (tp - 1) / tp * M * D * 2
             bound = max(flops / (peak["bf16_tflops"] * 1e9), nvl / (NVLINK_GBS * 1e6))
             if rank == 0:
                 print(json.dumps({"case": f"ag_{name}_m{M}", "tp": tp, "M": M, "N": N, "K": D,
                                   "gemm_ms": round(t_g, 4), "ag_nccl_gemm_ms": round(t_n, 4),
-                                  "fused_ms": round(t_f, 4), "speedup_vs_nccl": round(t_n / t_f, 3),
+                                  "fused_ms": round(t_f, 4), "tile_reads_from_owner_ms": round(t_d, 4),
+                                  "speedup_vs_nccl": round(t_n / t_f, 3),
                                   "roofline_ms": round(bound, 4), "frac_roofline": round(bound / t_f, 3),
                                   "peaks": peak["src"]}), flush=True)
     ws.close()

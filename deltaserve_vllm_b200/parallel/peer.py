@@ -148,10 +148,12 @@ class PeerTable:
 class AGPeerWorkspace:
     """Row shards of an activation in peer-mapped memory, for the all-gather
     -> column-parallel GEMM (``ops.gemm_ag``): rank ``r`` writes its rows into
-    ``local`` ([max_rows_per_rank, cols] bf16); the GEMM reads row block ``b``
-    from rank ``b * 128 // rows_per_rank`` through that rank's TMA tensor map
-    (``maps``, in device memory), so the gather happens inside the GEMM's loads
-    and no rank holds the gathered activation."""
+    ``local`` ([max_rows_per_rank, cols] bf16). The GEMM reads its own row
+    blocks in place (TMA through ``maps[rank]``) and, by default, first copies
+    every remote row block once into ``gathered`` (P2P loads by the epilogue
+    warps of all its CTAs, counted per block in ``cnt``) and reads those from
+    there, so each remote row crosses NVLink once whatever the number of N
+    tiles; ``copy_once=False`` reads every tile from its owner instead.
 
     def __init__(self, comm, max_rows_per_rank: int, cols: int, device=None):
         from .. import ops
@@ -173,6 +175,11 @@ class AGPeerWorkspace:
         self.local = _from_ptr(self.base, (self.rows_cap, self.cols), torch.bfloat16, dev.index)
         host_maps = ext.peer_tmaps(torch.tensor(self.ptrs, dtype=torch.int64), self.rows_cap, self.cols, self.cols)
         self.maps = host_maps.to(dev)           # 128 B per map, from a 256-byte aligned allocation
+        self.src = torch.tensor(self.ptrs, dtype=torch.int64)
+        # Copy-once gather: this rank's copy of every shard's rows (its own
+        # rows stay unused there) and the per-128-row-block unit counters.
+        self.gathered = torch.empty(self.world * self.rows_cap, self.cols, dtype=torch.bfloat16, device=dev)
+        self.cnt = torch.zeros(self.world * self.rows_cap // TILE + 1, dtype=torch.int32, device=dev)  # + ticket
         if comm is not None and self.world > 1:
             comm.barrier()
 

@@ -311,7 +311,14 @@ def _run_gemm_ag(rank, world, port, outdir):
     ref = torch.empty_like(out)
     ops.gemm(full, w, ref)
     res["bf16"] = float((out.float() - ref.float()).abs().max() / ref.float().abs().max())
-    # SwiGLU + LoRA expand, with the shrink of the gathered rows
+    remote = torch.ones(M, dtype=torch.bool, device="cuda")
+    remote[rank * rows:(rank + 1) * rows] = False
+    res["gathered"] = float((ws.gathered[:M][remote].float() - full[remote].float()).abs().max())
+    out_d = torch.empty_like(out)
+    ops.gemm_ag(ws, rows, w, out_d, copy_once=False)          # every tile read from its owner
+    res["bf16_direct"] = float((out_d.float() - ref.float()).abs().max() / ref.float().abs().max())
+    # SwiGLU + LoRA expand, with the shrink of the gathered rows (the GEMM
+    # reuses the rows the shrink gathered: fresh=False)
     slots, pr, seg = 2, 32, 64
     A = (torch.randn(slots, pr, K, generator=gw, device="cuda") * 0.05).to(torch.bfloat16)
     B2 = (torch.randn(N, slots * seg, generator=gw, device="cuda") * 0.05).to(torch.bfloat16)
@@ -323,7 +330,7 @@ def _run_gemm_ag(rank, world, port, outdir):
     ops.lora_shrink(full, A, sid, Zr, seg)
     res["shrink"] = float((Z.float() - Zr.float()).abs().max() / Zr.float().abs().max())
     o2 = torch.empty(M, N // 2, dtype=torch.bfloat16, device="cuda")
-    ops.gemm_ag(ws, rows, w, o2, epi=ops.EPI_SWIGLU, z=Z, b2=B2, tile_slots=mask, lora_seg=seg)
+    ops.gemm_ag(ws, rows, w, o2, epi=ops.EPI_SWIGLU, z=Z, b2=B2, tile_slots=mask, lora_seg=seg, fresh=False)
     r2 = torch.empty_like(o2)
     ops.gemm(full, w, r2, epi=ops.EPI_SWIGLU, z=Zr, b2=B2, tile_slots=mask, lora_seg=seg)
     res["swiglu_lora"] = float((o2.float() - r2.float()).abs().max() / r2.float().abs().max())
@@ -339,10 +346,11 @@ def _run_gemm_ag(rank, world, port, outdir):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_gemm_all_gather(world):
-    """All-gather -> GEMM with the row blocks read from their owners' memory
-    (bf16 and SwiGLU + LoRA expand epilogues, and the shrink of the gathered
-    rows) == NCCL all-gather then the local GEMM (which may split K: equal
-    to bf16 rounding)."""
+    """All-gather -> GEMM with the remote row blocks copied once into the
+    gathered buffer (bf16 and SwiGLU + LoRA expand epilogues, the shrink of
+    the gathered rows, a second call reusing them) or read by every tile from
+    their owners' memory == NCCL all-gather then the local GEMM (which may
+    split K: equal to bf16 rounding); the gathered rows equal the shards."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
@@ -350,3 +358,4 @@ def test_gemm_all_gather(world):
         for r in torch.load(os.path.join(d, "ag.pt"))["res"]:
             assert r["code"] == 0
             assert r["bf16"] < 1e-2 and r["shrink"] < 1e-2 and r["swiglu_lora"] < 1e-2, r
+            assert r["gathered"] == 0.0 and r["bf16_direct"] < 1e-2, r
