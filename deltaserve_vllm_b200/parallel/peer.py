@@ -153,7 +153,7 @@ class AGPeerWorkspace:
     every remote row block once into ``gathered`` (P2P loads by the epilogue
     warps of all its CTAs, counted per block in ``cnt``) and reads those from
     there, so each remote row crosses NVLink once whatever the number of N
-    tiles; ``copy_once=False`` reads every tile from its owner instead.
+    tiles; ``copy_once=False`` reads every tile from its owner instead."""
 
     def __init__(self, comm, max_rows_per_rank: int, cols: int, device=None):
         from .. import ops
