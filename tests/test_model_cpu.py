@@ -141,3 +141,53 @@ def test_prefix_caching_with_preemption():
     ref, _ = _serve(256, prompts, 40)
     got, pre = _serve(16, prompts, 40, caching=True)
     assert pre > 0 and got == ref
+
+
+def test_mixed_rank_adapters_in_one_batch_match_dense():
+    """Adapters of ranks 2, 4, 8 and 16 (alpha = 2 x rank) in the slots of a
+    rank-16 engine, one request on each plus one on the base model, served in
+    the same batches: each request's logits == the dense forward with its own
+    adapter at its own rank (the smaller ranks are zero-padded in their
+    slots), as a pool of adapters with ranks drawn from {8, 16, 32, 64}
+    serves them."""
+    arch = PRESETS["llama3-tiny"]
+    w = init_weights(arch, seed=3, dtype=torch.float32)
+    kv = KVCache(arch.num_layers, 96, arch.num_kv_heads, 16, arch.head_dim, "cpu", torch.float32)
+    lora = LoraServeBuffers(arch, w.tp, slots=5, max_rank=16, device="cpu", dtype=torch.float32)
+    ranks = {1: 2, 2: 4, 3: 8, 4: 16}
+    ads = {}
+    for slot, r in ranks.items():
+        ads[slot] = random_adapter(arch, r, seed=20 + slot, b_std=0.05)
+        lora.load_slot(slot, ads[slot], rank=r, alpha=2 * r)
+    model = DecoderModel(w, kv.k, kv.v, lora)
+    full = [full_layer_tensors(arch, i, 3, "cpu", torch.float32) for i in range(arch.num_layers)]
+    sched = Scheduler(kv.allocator, 16, max_num_batched_tokens=48, max_model_len=256)
+    runner = ModelRunner(model, 16, "cpu")
+    g = torch.Generator().manual_seed(1)
+    reqs = []
+    for i, slot in enumerate([1, 2, 3, 4, -1]):
+        r = Request(f"m{i}", torch.randint(0, arch.vocab, (11 + 5 * i,), generator=g).tolist(),
+                    SamplingParams(max_tokens=3))
+        r.lora_slot = slot
+        reqs.append(r)
+        sched.add(r)
+    checked = 0
+    for _ in range(20):
+        out = sched.schedule()
+        if out.is_empty():
+            break
+        toks, logits = runner.execute(out)
+        i = 0
+        for s in out.seqs:
+            if not s.sample:
+                continue
+            req = s.req
+            seq = torch.tensor(req.all_ids[: s.start + s.num_new])
+            slot = req.lora_slot
+            ref = dense_forward(arch, full, w.embed, w.lm_head, w.final_norm, seq,
+                                lora=ads.get(slot), scaling=2.0)[-1]
+            torch.testing.assert_close(logits[i], ref, rtol=2e-4, atol=2e-4)
+            i += 1
+            checked += 1
+        sched.update(out, toks)
+    assert all(r.finished() for r in reqs) and checked == 15
