@@ -89,7 +89,8 @@ def gemm_ag(ws, rows_per_rank, b, out, *, epi=EPI_BF16, z=None, b2=None, tile_sl
     where rank ``r``'s rows ``ws.local[:rows_per_rank]`` are rows
     ``[r * rows_per_rank, (r + 1) * rows_per_rank)`` of ``A_all``
     (``rows_per_rank`` a multiple of 128). Every rank's shard must be written
-    before any rank calls this. ``fresh``: the shards hold new rows since the
+    before any rank calls this, and a shard rewritten only after every rank's
+    call over it has finished. ``fresh``: the shards hold new rows since the
     last call (the copy-once gather starts over; ``False`` reuses the rows an
     earlier call of the same shards gathered)."""
     if copy_once:
