@@ -30,6 +30,7 @@ async def _one(session, url: str, rec: dict, model: str | None, t0: float, speed
     if rec.get("model") or model:
         body["model"] = rec.get("model") or model
     sent = time.perf_counter()
+    sent_unix = time.time()        # joins the engine's step trace (wall clock)
     first, last, gaps, n = None, None, [], 0
     headers = {}
     status = 0
@@ -57,7 +58,7 @@ async def _one(session, url: str, rec: dict, model: str | None, t0: float, speed
     return {"t": rec["t"], "status": status, "prompt_tokens": len(rec["prompt"]), "output_tokens": n,
             "ttft_s": None if first is None else first - sent,
             "tbt_mean_s": sum(gaps) / len(gaps) if gaps else None, "tbt_max_s": max(gaps) if gaps else None,
-            "headers": headers}
+            "headers": headers, "sent_unix": sent_unix}
 
 
 async def replay(server: str, trace: list[dict], model: str | None = None, speed: float = 1.0) -> list[dict]:

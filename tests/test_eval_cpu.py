@@ -79,3 +79,50 @@ def test_pure_ft_throughput_cpu():
     r = pure_ft.run("qwen3-tiny", seq=32, batch=2, cycles=3, warmup=1, device="cpu", rank=8)
     assert r["cycles"] == 3 and r["ft_tokens"] == 3 * 2 * 32
     assert r["ft_tok_s"] > 0 and r["wall_s"] > 0
+
+
+def test_estimator_report_from_a_step_trace(tmp_path):
+    """The estimator report reads a trace written by the engine's step-trace
+    writer: per-regime accuracy of the raw model (a regime predicted 20 %
+    low shows ratio 1.25 and negative bias), the backward-in-flight split,
+    margin coverage, admission fidelity, the worst miss and the steps during
+    a request's TTFT violation."""
+    from deltaserve_vllm_b200.eval.estimator_report import load_trace, report
+    from deltaserve_vllm_b200.utils.step_trace import StepTraceWriter
+
+    path = str(tmp_path / "trace.csv")
+    w = StepTraceWriter(path)
+    t0 = 1_000_000.0
+    for i in range(40):
+        dec = i % 2 == 0
+        actual = 0.010 if dec else 0.025
+        pred_raw = actual if dec else actual / 1.25          # the prefill regime under-predicts
+        w.put_row(kind="decode" if dec else "prefill", t_done=t0 + 0.05 * i,
+                  regime="decode_only" if dec else "inf_prefill",
+                  regime_used="decode_only" if dec else "inf_prefill",
+                  t_in=0 if dec else 512, p=0 if dec else 1, t_ft=0 if dec else 128, b_d=8, k=1024, s=0,
+                  pred_raw=pred_raw, pred=pred_raw * 1.1, actual=actual,
+                  admit_code="A" if not dec else None, t_baseline=None,
+                  t_admit=0.02 if not dec else None, bwd_in_flight=not dec)
+    # one outlier step
+    w.put_row(kind="decode", t_done=t0 + 2.5, regime="decode_only", regime_used="decode_only", t_in=0, p=0,
+              t_ft=0, b_d=8, k=1024, s=0, pred_raw=0.010, pred=0.011, actual=0.050, bwd_in_flight=True)
+    w.close()
+    rows = load_trace(path)
+    assert len(rows) == 41
+    results = [{"t": 0.0, "ttft_s": 0.8, "sent_unix": t0 + 0.02},     # waits through steps 1..16
+               {"t": 1.0, "ttft_s": 0.1, "sent_unix": t0 + 1.0}]      # within the SLO
+    rep = report(rows, results, ttft_slo=0.5, top=3)
+    acc = rep["accuracy"]
+    pre = acc["by_regime"]["inf_prefill"]
+    assert pre["n"] == 20 and abs(pre["ratio_p50"] - 1.25) < 1e-3 and pre["bias_ms"] < 0
+    dec = acc["by_regime"]["decode_only"]
+    assert dec["n"] == 21 and abs(dec["ratio_p50"] - 1.0) < 1e-3 and dec["over_2x"] > 0
+    assert acc["margin_coverage"]["decode_only"] == round(20 / 21, 4)
+    assert acc["margin_coverage"]["inf_prefill"] == 0.0              # 1.1 x margin < 1.25 x miss
+    assert acc["by_backward_in_flight"]["True"]["n"] == 21
+    adm = rep["admission"]
+    assert adm["n"] == 20 and adm["actual_over_admit"] == 1.0 and adm["admit_codes"] == {"A": 20}
+    assert rep["worst_misses"][0]["ratio"] == 5.0 and rep["worst_misses"][0]["step"]["seq"] == 41
+    (v,) = rep["ttft_violations"]
+    assert v["steps_while_waiting"] == 16 and v["steps_by_kind"] == {"decode": 8, "prefill": 8}
