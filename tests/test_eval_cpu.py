@@ -126,3 +126,35 @@ def test_estimator_report_from_a_step_trace(tmp_path):
     assert rep["worst_misses"][0]["ratio"] == 5.0 and rep["worst_misses"][0]["step"]["seq"] == 41
     (v,) = rep["ttft_violations"]
     assert v["steps_while_waiting"] == 16 and v["steps_by_kind"] == {"decode": 8, "prefill": 8}
+
+
+def test_prefill_probe_against_an_idle_server():
+    """The prefill probe reports TTFT per prompt length (sequential, idle
+    server) and the concurrent phase's aggregate rate, with no errors."""
+    import asyncio
+    from deltaserve_vllm_b200.eval.prefill_probe import probe
+    ecfg = EngineConfig(model="qwen3-tiny", device="cpu", max_model_len=256, block_size=16,
+                        max_num_batched_tokens=256, max_loras=1, max_lora_rank=8, enable_prefix_caching=True)
+    eng = CoServingEngine(ecfg, FinetuneConfig(enable_finetuning=False))
+    app = create_app(eng)
+    port = _port()
+    srv = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="error"))
+    th = threading.Thread(target=srv.run, daemon=True)
+    th.start()
+    for _ in range(200):
+        if srv.started:
+            break
+        time.sleep(0.05)
+    try:
+        out = asyncio.run(probe(f"http://127.0.0.1:{port}", [32, 96], reps=2, conc=3, conc_len=64,
+                                vocab=1024, max_tokens=2))
+    finally:
+        srv.should_exit = True
+        th.join(timeout=30)
+        eng.shutdown()
+    s = out["summary"]
+    assert s["errors"] == 0
+    assert set(s["sequential"]) == {"32", "96"} and s["sequential"]["96"]["n"] == 2
+    assert s["sequential"]["32"]["ms_per_token"] > 0
+    assert s["concurrent"]["n"] == 3 and s["concurrent"]["aggregate_prefill_tok_s"] > 0
+    assert len(out["rows"]) == 7
