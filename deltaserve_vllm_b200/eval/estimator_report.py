@@ -1,7 +1,12 @@
 """Where the step-time estimator's prediction misses the measured step time.
 
     python -m deltaserve_vllm_b200.eval.estimator_report step_trace.csv \\
-        [--results results.jsonl --ttft-slo 0.5] [--top 10] [--json]
+        [--results results.jsonl --ttft-slo 0.5] [--max-tbt-slo 0.06] [--top 10] [--json]
+    python -m deltaserve_vllm_b200.eval.estimator_report --compare legacy.csv relative_1.5.csv
+
+``--compare`` prints one line per trace with the admission margin's scores,
+for an A/B of ``slo.admission_margin`` (one run per arm, each with its own
+``telemetry.step_trace_path``; the reference's ``eval-tp/margin_ab.py``).
 
 Reads the per-step trace the engine writes with ``telemetry.step_trace_path``
 (``utils/step_trace.py``: one row per timed step with the raw model
@@ -17,8 +22,11 @@ the measured GPU time ``actual`` and the step's features) and reports:
 4. admission fidelity: for steps where finetuning rows were admitted, the time
    the admission loop predicted for the composition it reasoned on
    (``t_admit``) against the step's own prediction and the measured time;
-5. the worst misses with their neighbouring steps;
-6. with ``--results`` (``eval.replay`` output, which records each request's
+5. over the TBT limit: FT-carrying steps next to running decodes that took
+   longer than ``--max-tbt-slo`` (what the margin is there to prevent), with
+   inference-only steps as the control;
+6. the worst misses with their neighbouring steps;
+7. with ``--results`` (``eval.replay`` output, which records each request's
    send wall time): every request over the TTFT SLO with the steps that
    finished while it waited for its first token.
 
@@ -126,8 +134,26 @@ def admission_fidelity(rows: list[dict]) -> dict:
             "admit_codes": dict(sorted(codes.items()))}
 
 
+def over_limit(rows: list[dict], max_tbt_slo: float) -> dict:
+    """What the admission margin is for: steps that carried finetuning rows
+    next to running decodes and still took longer than ``max_tbt_slo`` (the
+    admission promised the limit and missed), with the same share for
+    inference-only steps with decodes as the control, and the ratio of the
+    measured time to the admission's prediction on the FT-carrying steps."""
+    ft = [r for r in rows if r["t_ft"] and r["b_d"] and r["actual"] is not None]
+    ctl = [r for r in rows if not r["t_ft"] and r["b_d"] and r["actual"] is not None]
+    ratio = [r["actual"] / r["t_admit"] for r in ft if r["t_admit"]]
+    return {"max_tbt_slo_s": max_tbt_slo,
+            "ft_steps_with_decodes": len(ft),
+            "ft_over_limit": round(sum(r["actual"] > max_tbt_slo for r in ft) / len(ft), 4) if ft else None,
+            "inference_steps_with_decodes": len(ctl),
+            "inference_over_limit": round(sum(r["actual"] > max_tbt_slo for r in ctl) / len(ctl), 4) if ctl else None,
+            "ft_actual_over_admit_p50": round(float(np.percentile(ratio, 50)), 3) if ratio else None,
+            "ft_actual_over_admit_p95": round(float(np.percentile(ratio, 95)), 3) if ratio else None}
+
+
 def worst_misses(rows: list[dict], top: int = 10) -> list[dict]:
-    """Section 5: the steps with the largest actual / raw prediction, each with
+    """Section 6: the steps with the largest actual / raw prediction, each with
     the step before and after it."""
     idx = [i for i, r in enumerate(rows) if r["pred_raw"] and r["actual"] is not None]
     idx.sort(key=lambda i: rows[i]["actual"] / rows[i]["pred_raw"], reverse=True)
@@ -147,7 +173,7 @@ def worst_misses(rows: list[dict], top: int = 10) -> list[dict]:
 
 
 def ttft_violations(rows: list[dict], results: list[dict], ttft_slo: float) -> list[dict]:
-    """Section 6: requests over the TTFT SLO (with a send wall time) and the
+    """Section 7: requests over the TTFT SLO (with a send wall time) and the
     steps that finished while they waited for the first token."""
     done = sorted((r["t_done"], i) for i, r in enumerate(rows) if r["t_done"] is not None)
     times = [t for t, _ in done]
@@ -169,12 +195,23 @@ def ttft_violations(rows: list[dict], results: list[dict], ttft_slo: float) -> l
     return out
 
 
-def report(rows: list[dict], results: list[dict] | None = None, ttft_slo: float = 0.5, top: int = 10) -> dict:
+def report(rows: list[dict], results: list[dict] | None = None, ttft_slo: float = 0.5, top: int = 10,
+           max_tbt_slo: float = 0.06) -> dict:
     rep = {"steps": len(rows), "accuracy": accuracy(rows), "admission": admission_fidelity(rows),
-           "worst_misses": worst_misses(rows, top)}
+           "over_limit": over_limit(rows, max_tbt_slo), "worst_misses": worst_misses(rows, top)}
     if results is not None:
         rep["ttft_violations"] = ttft_violations(rows, results, ttft_slo)
     return rep
+
+
+def compare_row(name: str, rows: list[dict], max_tbt_slo: float) -> dict:
+    """One A/B arm: the margin's scores of one run's step trace."""
+    acc = accuracy(rows)
+    cov = [r for r in rows if r["pred"] is not None and r["actual"] is not None]
+    return {"trace": name, "steps": len(rows), **over_limit(rows, max_tbt_slo),
+            "margin_coverage": round(sum(r["actual"] <= r["pred"] for r in cov) / len(cov), 4) if cov else None,
+            "raw_ratio_p50": acc["overall"].get("ratio_p50"), "raw_ratio_p90": acc["overall"].get("ratio_p90"),
+            "ft_tokens": int(sum(r["t_ft"] or 0 for r in rows))}
 
 
 def _print_text(rep: dict) -> None:
@@ -191,6 +228,7 @@ def _print_text(rep: dict) -> None:
                   f"{s['ratio_p50']:>7}{s['ratio_p90']:>7}{s['ratio_p99']:>7}{s['over_1_5x']:>8}{s['over_2x']:>8}")
     print(f"\nmargin coverage (actual <= margined prediction): {acc['margin_coverage']}")
     print(f"admission fidelity: {json.dumps(rep['admission'])}")
+    print(f"over the TBT limit: {json.dumps(rep['over_limit'])}")
     print("\nworst misses:")
     for m in rep["worst_misses"]:
         print(f"  x{m['ratio']}: {json.dumps(m['step'])}")
@@ -202,18 +240,27 @@ def _print_text(rep: dict) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("trace")
+    ap.add_argument("trace", nargs="+", help="one step trace, or several (arms of an A/B) with --compare")
     ap.add_argument("--results", default=None, help="eval.replay results (jsonl)")
     ap.add_argument("--ttft-slo", type=float, default=0.5)
+    ap.add_argument("--max-tbt-slo", type=float, default=0.06)
+    ap.add_argument("--compare", action="store_true",
+                    help="one line per trace with the margin's scores (e.g. runs with different admission margins)")
     ap.add_argument("--top", type=int, default=10)
     ap.add_argument("--json", action="store_true", help="print the report as one JSON object")
     a = ap.parse_args(argv)
-    rows = load_trace(a.trace)
+    if a.compare:
+        for path in a.trace:
+            print(json.dumps(compare_row(path, load_trace(path), a.max_tbt_slo)))
+        return
+    if len(a.trace) != 1:
+        ap.error("several traces need --compare")
+    rows = load_trace(a.trace[0])
     results = None
     if a.results:
         with open(a.results) as f:
             results = [json.loads(line) for line in f if line.strip()]
-    rep = report(rows, results, a.ttft_slo, a.top)
+    rep = report(rows, results, a.ttft_slo, a.top, a.max_tbt_slo)
     if a.json:
         print(json.dumps(rep))
     else:

@@ -112,7 +112,7 @@ def test_estimator_report_from_a_step_trace(tmp_path):
     assert len(rows) == 41
     results = [{"t": 0.0, "ttft_s": 0.8, "sent_unix": t0 + 0.02},     # waits through steps 1..16
                {"t": 1.0, "ttft_s": 0.1, "sent_unix": t0 + 1.0}]      # within the SLO
-    rep = report(rows, results, ttft_slo=0.5, top=3)
+    rep = report(rows, results, ttft_slo=0.5, top=3, max_tbt_slo=0.02)
     acc = rep["accuracy"]
     pre = acc["by_regime"]["inf_prefill"]
     assert pre["n"] == 20 and abs(pre["ratio_p50"] - 1.25) < 1e-3 and pre["bias_ms"] < 0
@@ -126,6 +126,14 @@ def test_estimator_report_from_a_step_trace(tmp_path):
     assert rep["worst_misses"][0]["ratio"] == 5.0 and rep["worst_misses"][0]["step"]["seq"] == 41
     (v,) = rep["ttft_violations"]
     assert v["steps_while_waiting"] == 16 and v["steps_by_kind"] == {"decode": 8, "prefill": 8}
+    ol = rep["over_limit"]
+    assert ol["ft_steps_with_decodes"] == 20 and ol["ft_over_limit"] == 1.0
+    assert ol["inference_steps_with_decodes"] == 21 and ol["inference_over_limit"] == round(1 / 21, 4)
+    assert ol["ft_actual_over_admit_p50"] == 1.25
+    from deltaserve_vllm_b200.eval.estimator_report import compare_row
+    row = compare_row("arm", rows, 0.02)
+    assert row["ft_over_limit"] == 1.0 and row["ft_tokens"] == 20 * 128
+    assert row["margin_coverage"] == round(20 / 41, 4)
 
 
 def test_prefill_probe_against_an_idle_server():
