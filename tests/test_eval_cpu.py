@@ -166,3 +166,45 @@ def test_prefill_probe_against_an_idle_server():
     assert s["sequential"]["32"]["ms_per_token"] > 0
     assert s["concurrent"]["n"] == 3 and s["concurrent"]["aggregate_prefill_tok_s"] > 0
     assert len(out["rows"]) == 7
+
+
+def test_trace_schedule_scale_slice_and_csv(tmp_path):
+    """Trace generation with a rate schedule (peaks, valleys, an idle
+    stretch) and log-uniform prompts; scale keeps the arrival pattern at a
+    new rate; slice rebases a window; a timeline CSV becomes a trace."""
+    import numpy as np
+    from deltaserve_vllm_b200.eval.trace import from_timeline_csv, main, scale_trace, slice_trace
+    tr = make_trace(0.0, 120.0, 1000, seed=3, rates=[2.0, 8.0, 0.0], period_s=10.0, prompt_dist="loguniform",
+                    prompt_min=16, prompt_max=160, out_min=4, out_max=8)
+    ts = np.array([r["t"] for r in tr])
+    assert np.all(np.diff(ts) > 0)
+    phase = (ts // 10).astype(int) % 3
+    assert not np.any(phase == 2)                                # idle stretches stay empty
+    lo, hi = np.sum(phase == 0), np.sum(phase == 1)
+    assert 2.5 < hi / lo < 6.5                                   # 8 vs 2 req/s
+    lens = np.array([len(r["prompt"]) for r in tr])
+    assert lens.min() >= 16 and lens.max() <= 160 and np.median(lens) < 70   # log-uniform: median ~ 51
+    # the single-rate stream is unchanged by the schedule support
+    a = make_trace(5.0, 10.0, 1000, seed=1)
+    b = make_trace(5.0, 10.0, 1000, seed=1, rates=[5.0])
+    assert a == b
+    half = scale_trace(tr, 0.5, seed=0)
+    assert abs(len(half) - len(tr) / 2) <= 1 and set(r["t"] for r in half) <= set(ts.tolist())
+    dbl = scale_trace(tr, 2.0, seed=0)
+    assert len(dbl) == 2 * len(tr) and all(x["t"] <= y["t"] for x, y in zip(dbl, dbl[1:]))
+    assert not any(int(r["t"] // 10) % 3 == 2 and r["t"] % 10 > 1.0 for r in dbl)   # pattern kept
+    cut = slice_trace(tr, 30.0, 50.0)
+    assert cut and all(0 <= r["t"] < 20.0 for r in cut)
+    assert len(cut) == int(np.sum((ts >= 30.0) & (ts < 50.0)))
+    csv_path = tmp_path / "timeline.csv"
+    csv_path.write_text("timestamp_s,prompt_length,max_new_tokens,second,index_in_second\n"
+                        "0.5,12,7,0,0\n1.25,40,3,1,0\n")
+    got = from_timeline_csv(str(csv_path), vocab=500)
+    assert [(r["t"], len(r["prompt"]), r["max_tokens"]) for r in got] == [(0.5, 12, 7), (1.25, 40, 3)]
+    assert all(3 <= x < 500 for r in got for x in r["prompt"])
+    import contextlib
+    import io
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        main(["from-csv", "--input", str(csv_path), "--vocab", "500"])
+    assert len(buf.getvalue().splitlines()) == 2
