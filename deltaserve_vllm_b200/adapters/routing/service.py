@@ -221,6 +221,7 @@ class AdapterRouter:
                 decisions = fut_dec.result()
             except Exception as e:  # the encoder failed: every request of the batch gets the error
                 for item in batch:
+                    self._cancelled.discard(item[0])
                     if not item[-1].done():
                         item[-1].set_exception(e)
                 decisions = None
