@@ -208,3 +208,31 @@ def test_trace_schedule_scale_slice_and_csv(tmp_path):
     with contextlib.redirect_stdout(buf):
         main(["from-csv", "--input", str(csv_path), "--vocab", "500"])
     assert len(buf.getvalue().splitlines()) == 2
+
+
+def test_auto_bench_launches_replays_and_shuts_down(tmp_path):
+    """The one-command timeline benchmark on CPU: the launcher serves a
+    derived YAML (finetuning on, step trace on), the trace is replayed with a
+    warm-up slice first, finetuning tokens are trained during the recorded
+    window, the server exits 0 on /shutdown and every output file exists."""
+    from deltaserve_vllm_b200.eval.auto_bench import parse, run
+    lines = [f"sample {i} " + "the quick brown fox jumps over the lazy dog " * (1 + i % 4) for i in range(200)]
+    (tmp_path / "data.txt").write_text("\n".join(lines) + "\n")
+    (tmp_path / "co.yaml").write_text(
+        "model:\n  model: qwen3-tiny\n  max_model_len: 256\n  device: cpu\n"
+        "engine:\n  block_size: 16\n  max_num_batched_tokens: 128\n  max_loras: 2\n  max_lora_rank: 8\n"
+        "finetune_param:\n  enable_finetuning: true\n  data_path: data.txt\n  max_saved_finetuning_tokens: 64\n"
+        "slo:\n  ttft_slo: 30.0\n  avg_tbt_slo: 30.0\n  max_tbt_slo: 30.0\n  profile_on_launch: false\n")
+    out = tmp_path / "out"
+    s = run(parse(["--config", str(tmp_path / "co.yaml"), "--co", "--rate", "10", "--duration", "3",
+                   "--prompt-median", "24", "--prompt-min", "4", "--prompt-max", "64", "--out-min", "2",
+                   "--out-max", "6", "--warmup-s", "0.5", "--out-dir", str(out), "--tag", "t",
+                   "--step-trace", "--ttft-slo", "30", "--tbt-slo", "30", "--ready-timeout", "300"]))
+    assert s["errors"] == 0 and s["completed"] == s["requests"] > 0
+    assert s["server_exit_code"] == 0 and s["warmup_requests"] > 0
+    assert s["ft_tokens_trained"] > 0 and s["estimator"]["steps"] > 0
+    for name in ("config_t.yaml", "results_t.jsonl", "summary_t.json", "meta_t.json", "server_t.log",
+                 "step_trace_t.csv"):
+        assert (out / name).exists(), name
+    res = [json.loads(x) for x in (out / "results_t.jsonl").read_text().splitlines()]
+    assert len(res) == s["requests"] and all("sent_unix" in r for r in res)
