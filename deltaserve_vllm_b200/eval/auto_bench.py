@@ -20,6 +20,7 @@ being recorded, then the whole trace is replayed as streaming requests. Output:
                            over the recorded window, the estimator report with --step-trace
     meta_<tag>.json        wall-clock anchor of the recorded window, command, config path
     step_trace_<tag>.csv   with --step-trace (see eval.estimator_report)
+    gpu_util_<tag>.csv     with --gpu-util: NVML utilisation and memory per GPU every 0.2 s
 
 The reference's counterpart is ``eval-tp/auto_benchmark_tp.py`` (its timeline
 CSVs load with ``--timeline-csv``).
@@ -142,6 +143,64 @@ def _stop(url: str, proc: subprocess.Popen, timeout_s: float = 60.0) -> int:
     return proc.returncode if proc.returncode is not None else -1
 
 
+class GpuUtilSampler:
+    """Whole-device GPU utilisation and memory (NVML, read only) sampled on a
+    thread every ``period_s`` with unix timestamps, to set the served load
+    against the GPU's busy share over the same window."""
+
+    def __init__(self, path: str, period_s: float = 0.2, nvml=None):
+        import threading
+        self.path, self.period_s = path, float(period_s)
+        self.rows: list[tuple] = []
+        self.error = None
+        self._stop = threading.Event()
+        self._nvml = nvml
+        self._t = threading.Thread(target=self._run, daemon=True, name="dsv-gpu-util")
+
+    def _run(self) -> None:
+        try:
+            nv = self._nvml
+            if nv is None:
+                import pynvml as nv
+            nv.nvmlInit()
+            handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in range(nv.nvmlDeviceGetCount())]
+        except Exception as e:        # no driver or no NVML here: nothing to sample
+            self.error = repr(e)
+            return
+        while not self._stop.is_set():
+            t = time.time()
+            for i, h in enumerate(handles):
+                try:
+                    u = nv.nvmlDeviceGetUtilizationRates(h)
+                    m = nv.nvmlDeviceGetMemoryInfo(h)
+                    self.rows.append((round(t, 3), i, int(u.gpu), int(m.used) // (1 << 20)))
+                except Exception as e:
+                    self.error = repr(e)
+            self._stop.wait(self.period_s)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=5)
+        with open(self.path, "w") as f:
+            f.write("timestamp,gpu,util_pct,mem_used_mb\n")
+            for r in self.rows:
+                f.write(",".join(map(str, r)) + "\n")
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"samples": 0, "error": self.error}
+        by_gpu: dict = {}
+        for _, g, u, _m in self.rows:
+            by_gpu.setdefault(g, []).append(u)
+        return {"samples": len(self.rows),
+                "util_mean_pct": {str(g): round(sum(v) / len(v), 1) for g, v in sorted(by_gpu.items())},
+                "mem_used_max_mb": max(r[3] for r in self.rows)}
+
+
 def run(a) -> dict:
     from ..models.configs import resolve_arch
     from .replay import _status, replay
@@ -167,9 +226,16 @@ def run(a) -> dict:
         if warm:
             asyncio.run(replay(url, warm, a.model, a.speed))
         before = _status(url)
+        util = GpuUtilSampler(os.path.join(a.out_dir, f"gpu_util_{tag}.csv")) if a.gpu_util else None
+        if util is not None:
+            util.__enter__()
         t0 = time.time()
-        res = asyncio.run(replay(url, trace, a.model, a.speed))
-        wall = time.time() - t0
+        try:
+            res = asyncio.run(replay(url, trace, a.model, a.speed))
+        finally:
+            wall = time.time() - t0
+            if util is not None:
+                util.__exit__(None, None, None)
         after = _status(url)
     finally:
         rc = _stop(url, proc)
@@ -181,6 +247,8 @@ def run(a) -> dict:
     s.update({"tag": tag, "wall_s": round(wall, 3), "ft_tokens_trained": ft,
               "ft_tok_s": round(ft / wall, 1) if wall > 0 else None, "server_exit_code": rc,
               "warmup_requests": len(warm)})
+    if util is not None:
+        s["gpu_util"] = util.summary()
     if a.step_trace:
         from .estimator_report import load_trace, report
         tp = os.path.join(a.out_dir, f"step_trace_{tag}.csv")
@@ -207,6 +275,7 @@ def parse(argv=None):
     ap.add_argument("--out-dir", default="bench_out")
     ap.add_argument("--tag", default=None)
     ap.add_argument("--step-trace", action="store_true")
+    ap.add_argument("--gpu-util", action="store_true", help="sample GPU utilisation and memory (NVML) while recording")
     ap.add_argument("--ready-timeout", type=float, default=900.0)
     ap.add_argument("--warmup-s", type=float, default=0.0, help="replay the trace's first seconds unrecorded first")
     ap.add_argument("--model", default=None, help="request model field (e.g. auto for routing)")

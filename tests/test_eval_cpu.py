@@ -236,3 +236,37 @@ def test_auto_bench_launches_replays_and_shuts_down(tmp_path):
         assert (out / name).exists(), name
     res = [json.loads(x) for x in (out / "results_t.jsonl").read_text().splitlines()]
     assert len(res) == s["requests"] and all("sent_unix" in r for r in res)
+
+
+def test_gpu_util_sampler_with_a_fake_nvml(tmp_path):
+    """The utilisation sampler reads NVML only (a fake here): rows per GPU
+    with timestamps, a per-GPU mean, and a clean summary without NVML."""
+    import types
+    from deltaserve_vllm_b200.eval.auto_bench import GpuUtilSampler
+    calls = {"n": 0}
+
+    def util(h):
+        calls["n"] += 1
+        return types.SimpleNamespace(gpu=50 + 10 * h)
+
+    fake = types.SimpleNamespace(nvmlInit=lambda: None, nvmlDeviceGetCount=lambda: 2,
+                                 nvmlDeviceGetHandleByIndex=lambda i: i,
+                                 nvmlDeviceGetUtilizationRates=util,
+                                 nvmlDeviceGetMemoryInfo=lambda h: types.SimpleNamespace(used=(1000 + h) << 20))
+    path = tmp_path / "u.csv"
+    with GpuUtilSampler(str(path), period_s=0.01, nvml=fake) as smp:
+        for _ in range(200):
+            if calls["n"] >= 6:
+                break
+            time.sleep(0.01)
+    s = smp.summary()
+    assert s["samples"] >= 6 and s["util_mean_pct"] == {"0": 50.0, "1": 60.0} and s["mem_used_max_mb"] == 1001
+    lines = path.read_text().splitlines()
+    assert lines[0] == "timestamp,gpu,util_pct,mem_used_mb" and len(lines) == s["samples"] + 1
+
+    def broken():
+        raise RuntimeError("no NVML")
+
+    with GpuUtilSampler(str(tmp_path / "v.csv"), nvml=types.SimpleNamespace(nvmlInit=broken)) as smp2:
+        time.sleep(0.05)
+    assert smp2.summary()["samples"] == 0 and "no NVML" in smp2.summary()["error"]
