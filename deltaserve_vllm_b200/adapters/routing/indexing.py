@@ -55,11 +55,8 @@ def cached_centroid(directory: str, name: str, fp: str):
     and encoder, else None."""
     if _fingerprints(directory).get(name) != fp:
         return None
-    path = os.path.join(directory, CENTROIDS_FILE)
-    if not os.path.exists(path):
-        return None
-    idx = CentroidIndex.load(path)
-    if name not in idx:
+    idx = CentroidIndex.load_or_none(os.path.join(directory, CENTROIDS_FILE))
+    if idx is None or name not in idx:
         return None
     return idx.centroid_of(name), idx.refs.get(name)
 
@@ -69,7 +66,7 @@ def store_centroid(directory: str, name: str, fp: str, centroid, refs, enc_id: s
     with _CACHE_LOCK:
         os.makedirs(directory, exist_ok=True)
         path = os.path.join(directory, CENTROIDS_FILE)
-        idx = CentroidIndex.load(path) if os.path.exists(path) else CentroidIndex(enc_id, prefix, max_tokens)
+        idx = CentroidIndex.load_or_none(path) or CentroidIndex(enc_id, prefix, max_tokens)
         if len(idx) and (idx.encoder, idx.prefix, idx.max_tokens) != (enc_id, prefix, int(max_tokens)):
             raise RuntimeError(f"{path} was built with encoder '{idx.encoder}', not '{enc_id}'; "
                                "centroids of different encoders cannot mix")

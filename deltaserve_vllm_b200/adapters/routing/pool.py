@@ -447,7 +447,7 @@ class AdapterPool:
             return 0
         if centroids is None:
             f = os.path.join(directory, reg.get("routable") or "")
-            centroids = CentroidIndex.load(f) if reg.get("routable") and os.path.exists(f) else None
+            centroids = CentroidIndex.load_or_none(f) if reg.get("routable") else None
         self._hold_save += 1
         try:
             self.version = max(self.version, int(reg.get("version", 0)))

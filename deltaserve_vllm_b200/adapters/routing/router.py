@@ -110,9 +110,7 @@ class Router:
     def set_index(self, index: CentroidIndex) -> None:
         """Rebuild the decision model from a pool snapshot (one assignment,
         so a batch being routed keeps the model it started with)."""
-        snap = CentroidIndex(index.encoder, index.prefix, index.max_tokens)
-        snap.names, snap.matrix = list(index.names), index.matrix.copy()
-        snap.refs = dict(index.refs)
+        snap = index.snapshot()
         self.index, self.model = snap, PoolGeometry(snap, *self._args)
 
     def _prefer(self, name: str):
