@@ -192,7 +192,7 @@ def test_pool_admission_full_and_persistence():
         pool.pin("a4")
         reg = read_registry(d)
         assert {a["name"] for a in reg["adapters"]} == {"a0", "a1", "a2", "a3", "a4"}
-        assert os.path.exists(os.path.join(d, reg["routable"]))
+        assert os.path.exists(os.path.join(d, reg["index_file"]))
         # restore into a new pool: levels, pins and routable set survive
         p2 = AdapterPool(FakeBackend(), capacity=3, gpu_slots=1, clock=clk, directory=d)
         assert p2.restore(d) == 5
