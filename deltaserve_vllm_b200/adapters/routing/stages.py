@@ -14,18 +14,15 @@ from __future__ import annotations
 
 import os
 
-from ...engine.ft_job import Stage, register_stage
+from ...engine.ft_job import Stage
 from .indexing import store_centroid
 
 
-@register_stage
-class IndexingStage(Stage):
-    name = "indexing"
+class IndexingStage(Stage, key="indexing"):
+    def prerequisites(self, listed):
+        return tuple(k for k in ("init",) if k in listed)
 
-    def requirements(self, names):
-        return ("init",) if "init" in names else ()
-
-    def start(self, job, ctx) -> None:
+    def begin(self, job, ctx) -> None:
         router = getattr(ctx, "router", None)
         if router is None:
             raise RuntimeError("adapter routing is not running")
@@ -34,7 +31,7 @@ class IndexingStage(Stage):
         ijob, hit = router.index_job(job.spec.name, job.spec.data_path)
         job.data["indexing"] = (router, ijob, hit)
 
-    def poll(self, job, ctx) -> bool:
+    def settled(self, job, ctx) -> bool:
         router, ijob, hit = job.data["indexing"]
         if hit is not None:
             job.data["centroid"] = hit
@@ -50,14 +47,11 @@ class IndexingStage(Stage):
         return True
 
 
-@register_stage
-class AdmissionStage(Stage):
-    name = "admission"
+class AdmissionStage(Stage, key="admission"):
+    def prerequisites(self, listed):
+        return tuple(k for k in listed if k not in (self.key, "ready"))   # after every other stage but ready
 
-    def requirements(self, names):
-        return tuple(s for s in names if s not in (self.name, "ready"))
-
-    def start(self, job, ctx) -> None:
+    def begin(self, job, ctx) -> None:
         router = getattr(ctx, "router", None)
         if router is None:
             raise RuntimeError("adapter routing is not running")
@@ -70,6 +64,3 @@ class AdmissionStage(Stage):
             raise RuntimeError("the job has no adapter to admit (no save_path / adapter_path)")
         c, r = job.data.get("centroid") or (None, None)
         job.report = router.pool.admit(job.spec.name, path, c, r, job=job.spec.name, load=True)
-
-    def poll(self, job, ctx) -> bool:
-        return True

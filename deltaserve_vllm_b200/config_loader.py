@@ -100,6 +100,15 @@ def _is_path_key(key: str) -> bool:
     return "path" in k or k.endswith("_dir")
 
 
+def _absolutize(mapping: dict, base: Path, is_path) -> None:
+    """Rewrite, in place, the relative string values of ``mapping`` whose key
+    ``is_path`` accepts as absolute paths under ``base``."""
+    for key in [k for k, v in mapping.items() if isinstance(v, str) and is_path(k)]:
+        p = Path(mapping[key])
+        if not p.is_absolute():
+            mapping[key] = str((base / p).resolve())
+
+
 def load_yaml_config(path: str | Path, verbose: bool = False) -> dict[str, Any]:
     """Read a sectioned YAML file into ``{section: {key: value}}`` with
     relative paths made absolute against the file's directory."""
@@ -116,18 +125,14 @@ def load_yaml_config(path: str | Path, verbose: bool = False) -> dict[str, Any]:
             raise ValueError(f"{path}: section '{section}' must be a mapping "
                              f"(got {type(body).__name__})")
     base = path.resolve().parent
-    for section in (*ALL_FINETUNE_SECTIONS, "adapters", ADAPTER_ROUTING_SECTION,
-                    FT_JOB_SECTION):
-        body = raw.get(section) or {}
-        for key, val in body.items():
-            if _is_path_key(key) and isinstance(val, str) and not Path(val).is_absolute():
-                body[key] = str((base / val).resolve())
-    for entry in (raw.get(ADAPTER_ROUTING_SECTION) or {}).get("adapters") or []:
-        if isinstance(entry, dict):
-            for key, val in entry.items():
-                if "path" in key.lower() and isinstance(val, str) \
-                        and not Path(val).is_absolute():
-                    entry[key] = str((base / val).resolve())
+    mappings = [raw.get(s) or {} for s in (*ALL_FINETUNE_SECTIONS, "adapters", ADAPTER_ROUTING_SECTION,
+                                           FT_JOB_SECTION)]
+    listed = (raw.get(ADAPTER_ROUTING_SECTION) or {}).get("adapters") or []
+    for m in mappings:
+        _absolutize(m, base, _is_path_key)
+    for m in listed:                      # routing's adapter list: {name, path, data_path, ...}
+        if isinstance(m, dict):
+            _absolutize(m, base, lambda k: "path" in k.lower())
     if verbose:
         dprint(f"loaded config ({path}):")
         for section, body in raw.items():
@@ -236,13 +241,16 @@ def additional_config(config: dict[str, Any], **overrides: Any) -> dict:
     """The finetune sections as one JSON-able dict (the reference passed this to
     ``vllm serve --additional-config``; here it round-trips a config between
     processes)."""
-    kw = {**finetune_kwargs(config), **{k: v for k, v in overrides.items() if v is not None}}
-    out = {"deltaserve": {k: v for k, v in kw.items() if v is not None}}
-    routing = {k: v for k, v in (config.get(ADAPTER_ROUTING_SECTION) or {}).items()
-               if v is not None}
+    def given(d: dict) -> dict:
+        return dict(filter(lambda kv: kv[1] is not None, d.items()))
+
+    settings = finetune_kwargs(config)
+    settings.update(given(overrides))
+    doc = {"deltaserve": given(settings)}
+    routing = given(config.get(ADAPTER_ROUTING_SECTION) or {})
     if routing:
-        out["deltaserve_adapter_routing"] = routing
-    return out
+        doc["deltaserve_adapter_routing"] = routing
+    return doc
 
 
 def finetune_cli_args(config: dict[str, Any], **overrides: Any) -> list[str]:

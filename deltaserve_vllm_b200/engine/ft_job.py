@@ -16,91 +16,88 @@ JOB_META_KEYS = ("name", "stages", "auto_routing", "adapter_init", "save_path")
 
 
 class Stage:
-    name: str = ""
+    """One step of a finetuning job. A subclass declares itself with
+    ``class Foo(Stage, key="foo")`` and job specs can then list ``foo``.
+    ``begin`` runs once, when every prerequisite stage of the job is done;
+    ``settled`` is asked on every engine tick after that until it is True.
+    Stage objects hold no state of their own (they are made afresh each
+    tick); a stage keeps its working state in ``job.data``."""
 
-    def requirements(self, stage_names: tuple[str, ...]) -> tuple[str, ...]:
+    key: str = ""
+    _kinds: dict[str, type["Stage"]] = {}
+
+    def __init_subclass__(cls, key: str = "", **kw):
+        super().__init_subclass__(**kw)
+        if not key:
+            raise TypeError(f"{cls.__name__}: a stage needs a key (class {cls.__name__}(Stage, key=...))")
+        cls.key = key
+        Stage._kinds[key] = cls
+
+    def prerequisites(self, listed: tuple[str, ...]) -> tuple[str, ...]:
+        """The stages of this job (``listed``) that must be done first."""
         return ()
 
-    def start(self, job: "FinetuneJob", ctx: Any) -> None:
+    def begin(self, job: "FinetuneJob", ctx: Any) -> None:
         pass
 
-    def poll(self, job: "FinetuneJob", ctx: Any) -> bool:
+    def settled(self, job: "FinetuneJob", ctx: Any) -> bool:
         return True
 
 
-_STAGES: dict[str, type[Stage]] = {}
-
-
-def register_stage(cls: type[Stage]) -> type[Stage]:
-    if not cls.name:
-        raise ValueError(f"{cls.__name__} has no stage name")
-    _STAGES[cls.name] = cls
-    return cls
-
-
-def known_stages() -> tuple[str, ...]:
-    return tuple(_STAGES)
+def stage_keys() -> tuple[str, ...]:
+    return tuple(Stage._kinds)
 
 
 def load_gated_stages(adapter_routing: bool) -> None:
-    if adapter_routing and "indexing" not in _STAGES:
-        from ..adapters.routing import stages  # noqa: F401  (registers)
+    if adapter_routing and "indexing" not in Stage._kinds:
+        from ..adapters.routing import stages  # noqa: F401  (declares them)
 
 
-@register_stage
-class InitStage(Stage):
+class InitStage(Stage, key="init"):
     """The job's adapter weights and dataset are in place. The launch job's
     were loaded at engine start; a later job switches the trainer (adapter
     init, optimiser settings) and the corpus once the previous job's samples
     have all been trained (``ctx.begin_job`` returns False until then)."""
-    name = "init"
 
-    def poll(self, job, ctx) -> bool:
-        begin = getattr(ctx, "begin_job", None)
-        if begin is not None and not begin(job):
+    def settled(self, job, ctx) -> bool:
+        switch = getattr(ctx, "begin_job", None)
+        if switch is not None and not switch(job):
             return False
         store = getattr(ctx, "store", None)
         return store is None or len(store) > 0
 
 
-@register_stage
-class TrainingStage(Stage):
+class TrainingStage(Stage, key="training"):
     """Done once the corpus finished every epoch and the last backward landed."""
-    name = "training"
 
-    def requirements(self, names):
-        return ("init",) if "init" in names else ()
+    def prerequisites(self, listed):
+        return tuple(k for k in ("init",) if k in listed)
 
-    def start(self, job, ctx) -> None:
-        # Open admission unless the launch config keeps it closed until
+    def begin(self, job, ctx) -> None:
+        # Admission opens now unless the launch config keeps it closed until
         # POST /start_finetuning.
-        coord = getattr(ctx, "coord", None)
-        cfg = getattr(ctx, "ftcfg", None)
+        coord, cfg = getattr(ctx, "coord", None), getattr(ctx, "ftcfg", None)
         if coord is not None and getattr(cfg, "start_on_launch", True):
             coord.start()
 
-    def poll(self, job, ctx) -> bool:
+    def settled(self, job, ctx) -> bool:
         store, coord = getattr(ctx, "store", None), getattr(ctx, "coord", None)
         if store is None or coord is None:
             return True
-        return store.finished() and not coord.pending_backward and coord.fill_count == 0
+        drained = not coord.pending_backward and coord.fill_count == 0
+        return drained and store.finished()
 
 
-@register_stage
-class ReadyStage(Stage):
+class ReadyStage(Stage, key="ready"):
     """The trained adapter is saved (when the job names a save path)."""
-    name = "ready"
 
-    def requirements(self, names):
+    def prerequisites(self, listed):
         return ("training",)
 
-    def start(self, job, ctx) -> None:
+    def begin(self, job, ctx) -> None:
         save = getattr(ctx, "save_job_adapter", None)
         if save is not None and job.spec.save_path:
             save(job)
-
-    def poll(self, job, ctx) -> bool:
-        return True
 
 
 @dataclass
@@ -138,14 +135,14 @@ class FinetuneJobSpec:
         for s in self.stages:
             if s in GATED_STAGES and not adapter_routing:
                 raise ValueError(f"ft_job stage '{s}' needs {GATED_STAGES[s]}: true")
-            if s not in _STAGES:
-                raise ValueError(f"unknown ft_job stage '{s}' (known: {sorted(_STAGES)})")
+            if s not in Stage._kinds:
+                raise ValueError(f"unknown ft_job stage '{s}' (known: {sorted(Stage._kinds)})")
         if len(set(self.stages)) != len(self.stages):
             raise ValueError("ft_job.stages lists a stage twice")
         for s in self.stages:
-            for req in _STAGES[s]().requirements(self.stages):
-                if req not in self.stages:
-                    raise ValueError(f"stage '{s}' needs stage '{req}'")
+            missing = [k for k in Stage._kinds[s]().prerequisites(self.stages) if k not in self.stages]
+            if missing:
+                raise ValueError(f"stage '{s}' needs stage '{missing[0]}'")
         if self.adapter_init not in (None, "from_path", "random"):
             raise ValueError(f"ft_job.adapter_init '{self.adapter_init}' is not supported; "
                              "available: ['from_path', 'random']")
@@ -207,24 +204,23 @@ class FtJobManager:
         if job.state == "queued":
             job.state = "running"
             job.started = time.time()
-        names = job.spec.stages
-        for s in names:
-            st = job.stage_state[s]
-            if st == "done":
+        listed = job.spec.stages
+        for key in listed:
+            phase = job.stage_state[key]
+            if phase == "done":
                 continue
-            stage = _STAGES[s]()
-            reqs = stage.requirements(names)
-            if any(job.stage_state.get(r) != "done" for r in reqs):
+            stage = Stage._kinds[key]()
+            if not all(job.stage_state.get(k) == "done" for k in stage.prerequisites(listed)):
                 continue
             try:
-                if st == "pending":
-                    stage.start(job, ctx)
-                    job.stage_state[s] = "running"
-                if stage.poll(job, ctx):
-                    job.stage_state[s] = "done"
+                if phase == "pending":
+                    stage.begin(job, ctx)
+                    job.stage_state[key] = "running"
+                if stage.settled(job, ctx):
+                    job.stage_state[key] = "done"
             except Exception as e:  # a failing stage fails the job, not the engine
                 job.state = "failed"
-                job.error = f"{s}: {e!r}"
+                job.error = f"{key}: {e!r}"
                 job.finished = time.time()
                 return
         if all(v == "done" for v in job.stage_state.values()):

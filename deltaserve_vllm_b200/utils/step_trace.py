@@ -15,13 +15,14 @@ COLUMNS = ("seq", "kind", "t_done", "regime", "regime_used", "t_in", "p", "t_ft"
 
 
 def _f(v) -> str:
+    """One CSV cell: empty for a missing value, 0/1 for flags, six
+    significant digits for floats (six decimals for wall-clock stamps, whose
+    integer part alone has ten digits)."""
     if v is None:
         return ""
-    if isinstance(v, bool):
-        return "1" if v else "0"
     if isinstance(v, float):
-        return f"{v:.6f}" if v >= 1e6 else f"{v:.6g}"
-    return str(v)
+        return format(v, ".6f" if abs(v) >= 1e6 else ".6g")
+    return str(int(v)) if isinstance(v, bool) else str(v)
 
 
 class StepTraceWriter:
