@@ -23,6 +23,7 @@ import csv
 import os
 import time
 from collections import deque
+from dataclasses import dataclass, field
 
 from ... import dprint
 
@@ -41,6 +42,46 @@ class RpsTracker:
         return len(self._t) / self.window_s if self.window_s > 0 else 0.0
 
 
+@dataclass
+class _FillBuffer:
+    """The activation buffer's row accounting. ``reserved`` rows belong to
+    finetuning rows admitted into a step that has not run yet; they become
+    ``committed`` when the step's forward captured them (or go back when the
+    step is rolled back). ``lens`` are the committed samples' lengths and
+    ``samples`` the store items the next backward will train."""
+    committed: int = 0
+    reserved: int = 0
+    lens: list = field(default_factory=list)
+    samples: list = field(default_factory=list)
+
+    def used(self) -> int:
+        return self.committed + self.reserved
+
+    def take(self, n: int, samples) -> int:
+        """Reserve ``n`` rows; returns their first row."""
+        first = self.used()
+        self.reserved += int(n)
+        self.samples.extend(samples or ())
+        return first
+
+    def give_back(self, n: int, samples) -> None:
+        self.reserved = max(0, self.reserved - int(n))
+        if samples:
+            gone = {id(x) for x in samples}
+            self.samples = [x for x in self.samples if id(x) not in gone]
+
+    def commit(self, n: int, lens) -> None:
+        self.committed += n
+        self.reserved = max(0, self.reserved - n)
+        self.lens.extend(int(x) for x in (lens or ()))
+
+    def drain(self) -> list:
+        """Empty the buffer after a backward; returns the trained samples."""
+        out, self.samples = self.samples, []
+        self.committed, self.lens = 0, []
+        return out
+
+
 class FinetuneCoordinator:
     def __init__(self, capacity: int, ft_started: bool = True, per_step_budget: int | None = None,
                  bwd_log_path: str | None = None, stuck_warn_s: float = 5.0,
@@ -52,10 +93,7 @@ class FinetuneCoordinator:
         self.pending_backward = False
         self.disabled = False
         self.disabled_reason: str | None = None
-        self.fill_count = 0
-        self.reserved_fill = 0
-        self.sample_lens: list[int] = []
-        self.buffer_samples: list = []
+        self.buf = _FillBuffer()
         self.min_sample_len = 1
         self.epoch_flush_pending = False
         self.current_epoch = 0
@@ -77,9 +115,38 @@ class FinetuneCoordinator:
         self.bwd_log_path = bwd_log_path
         self.history: list[dict] = []
 
+    # Views of the buffer under the names the engine and the status use.
+    @property
+    def fill_count(self) -> int:
+        return self.buf.committed
+
+    @fill_count.setter
+    def fill_count(self, v: int) -> None:
+        self.buf.committed = int(v)
+
+    @property
+    def reserved_fill(self) -> int:
+        return self.buf.reserved
+
+    @property
+    def sample_lens(self) -> list:
+        return self.buf.lens
+
+    @sample_lens.setter
+    def sample_lens(self, v) -> None:
+        self.buf.lens = list(v)
+
+    @property
+    def buffer_samples(self) -> list:
+        return self.buf.samples
+
+    @buffer_samples.setter
+    def buffer_samples(self, v) -> None:
+        self.buf.samples = list(v)
+
     # ------------------------------------------------------------ flags
     def space_remaining(self) -> int:
-        return max(0, self.capacity - self.fill_count - self.reserved_fill)
+        return max(0, self.capacity - self.buf.used())
 
     def next_ft_budget(self) -> int:
         if self.disabled or not self.ft_started or not self.admission_open or self.pending_backward:
@@ -105,20 +172,13 @@ class FinetuneCoordinator:
 
     # ------------------------------------------------------------ buffer
     def reserve(self, n: int, samples: list | None = None) -> int:
-        off = self.fill_count + self.reserved_fill
-        self.reserved_fill += int(n)
-        if samples:
-            self.buffer_samples.extend(samples)
-        return off
+        return self.buf.take(n, samples)
 
     def unreserve(self, n: int, samples: list | None = None) -> None:
         """Roll back a reservation whose step did not run (or was pre-empted).
         The admission that made it may have closed the buffer for a flush;
         with its rows gone that decision is re-made at the next admission."""
-        self.reserved_fill = max(0, self.reserved_fill - int(n))
-        if samples:
-            ids = {id(s) for s in samples}
-            self.buffer_samples = [s for s in self.buffer_samples if id(s) not in ids]
+        self.buf.give_back(n, samples)
         if not self.pending_backward and not self.disabled and self.ft_started:
             self.epoch_flush_pending = False
             self.admission_open = True
@@ -126,7 +186,7 @@ class FinetuneCoordinator:
     def note_injection(self, next_sample_len: int | None, admitted_now: int = 0) -> None:
         """After an admission: close the buffer (flush pending) when the
         smallest remaining sample can no longer fit, or the corpus/epoch is done."""
-        if self.pending_backward or self.fill_count + self.reserved_fill + admitted_now <= 0:
+        if self.pending_backward or self.buf.used() + admitted_now <= 0:
             return
         space = self.space_remaining() - admitted_now
         if next_sample_len is None or next_sample_len > space:
@@ -137,20 +197,18 @@ class FinetuneCoordinator:
         """Commit ``n`` captured rows; returns True when a backward should start."""
         if n <= 0:
             return False
-        self.fill_count += n
-        self.reserved_fill = max(0, self.reserved_fill - n)
-        if sample_lens:
-            self.sample_lens.extend(int(x) for x in sample_lens)
-        if self.pending_backward or self.reserved_fill > 0:
-            return False
-        if self.space_remaining() < self.min_sample_len or self.epoch_flush_pending:
+        self.buf.commit(n, sample_lens)
+        # A backward starts once nothing is in flight and either no sample
+        # fits any more or a flush was asked for.
+        full = self.space_remaining() < self.min_sample_len
+        if not self.pending_backward and self.buf.reserved == 0 and (full or self.epoch_flush_pending):
             return self._trigger()
         return False
 
     def try_flush(self) -> bool:
         """Train a partial buffer that no further FT forward will fill."""
-        if (self.epoch_flush_pending and self.reserved_fill == 0 and self.fill_count > 0
-                and not self.pending_backward and not self.disabled):
+        idle = not self.pending_backward and not self.disabled and self.buf.reserved == 0
+        if idle and self.epoch_flush_pending and self.buf.committed > 0:
             return self._trigger()
         return False
 
@@ -167,8 +225,7 @@ class FinetuneCoordinator:
     def backward_done(self, n: int, loss: float, gpu_ms: float, wall_ms: float,
                       epoch: int | None = None) -> list:
         """A cycle finished: returns the samples it trained (to commit)."""
-        trained = self.buffer_samples
-        self.buffer_samples = []
+        trained = self.buf.drain()
         self.total_trained_tokens += int(n)
         self.completed_cycles += 1
         self.last_loss = loss
@@ -179,8 +236,6 @@ class FinetuneCoordinator:
         self._t_free = time.monotonic()
         self.history.append(rec)
         self._log(rec)
-        self.fill_count = 0
-        self.sample_lens = []
         self.pending_backward = False
         self._t_trigger = None
         if not self.disabled and not self.rps_throttle_active:
