@@ -71,8 +71,9 @@ class StepFeatures:
     def has_ft(self) -> bool:
         return self.t_ft > 0
 
-    def row(self) -> list[float]:
-        return [self.s, float(self.t_in), float(self.t_ft), float(self.b_d), float(self.k), 1.0]
+    def row(self) -> np.ndarray:
+        """The model's feature row: ``[s, T_in, T_ft, B_d, K, 1]``."""
+        return np.array((self.s, self.t_in, self.t_ft, self.b_d, self.k, 1.0), np.float64)
 
     def regime(self, split_mixed: bool = False) -> str:
         """The regime of this step. ``split_mixed`` (the ``graph_ft_batches``
@@ -93,23 +94,45 @@ def _regime(t_in, t_ft, b_d, bwd, split_mixed: bool) -> str:
     return REGIME_DECODE_BWD if bwd else REGIME_DECODE_ONLY
 
 
-@dataclass
+_NAMES = ("alpha", "beta", "gamma", "delta", "epsilon", "c")
+
+
 class StepParams:
-    alpha: float | None = None
-    beta: float | None = None
-    gamma: float | None = None
-    delta: float | None = None
-    epsilon: float | None = None
-    c: float | None = None
+    """One regime's fitted model: the coefficient vector ``coef`` over the
+    feature row ``[s, T_in, T_ft, B_d, K, 1]`` (named alpha, beta, gamma,
+    delta, epsilon, c), or None while the regime has too few samples."""
+
+    __slots__ = ("coef",)
+
+    def __init__(self, *coef):
+        vals = list(coef[0]) if len(coef) == 1 and isinstance(coef[0], (list, tuple, np.ndarray)) else list(coef)
+        self.coef = (np.asarray(vals, np.float64)
+                     if len(vals) == len(_NAMES) and all(v is not None for v in vals) else None)
 
     @property
     def is_fitted(self) -> bool:
-        return all(v is not None for v in (self.alpha, self.beta, self.gamma, self.delta,
-                                           self.epsilon, self.c))
+        return self.coef is not None
 
     def eval(self, f: StepFeatures) -> float:
-        return (self.alpha * f.s + self.beta * f.t_in + self.gamma * f.t_ft + self.delta * f.b_d
-                + self.epsilon * f.k + self.c)
+        return float(self.coef @ f.row())
+
+    def as_list(self) -> list:
+        return [None] * len(_NAMES) if self.coef is None else [float(v) for v in self.coef]
+
+    def __getattr__(self, name):          # alpha .. c by name
+        try:
+            i = _NAMES.index(name)
+        except ValueError:
+            raise AttributeError(name) from None
+        return None if self.coef is None else float(self.coef[i])
+
+
+# When a step's own regime has no fit yet, the first fitted one of these.
+_FALLBACK = {
+    REGIME_DECODE_BWD: (REGIME_DECODE_ONLY, REGIME_EAGER, REGIME_FT_MIXED, REGIME_INF_PREFILL),
+    REGIME_FT_MIXED: (REGIME_EAGER, REGIME_INF_PREFILL, REGIME_DECODE_ONLY),
+}
+_FALLBACK_DEFAULT = (REGIME_EAGER, REGIME_FT_MIXED, REGIME_INF_PREFILL, REGIME_DECODE_ONLY)
 
 
 class StepLog:
@@ -247,9 +270,6 @@ _COLS = {
     REGIME_DECODE_ONLY: (3, 4, 5),
     REGIME_DECODE_BWD: (3, 4, 5),
 }
-_NAMES = ("alpha", "beta", "gamma", "delta", "epsilon", "c")
-
-
 class MergedExecutionEstimator:
     MARGIN_MODES = ("legacy", "relative", "absolute")
 
@@ -290,7 +310,7 @@ class MergedExecutionEstimator:
         """Per regime: the six coefficients (alpha .. c, None when unfitted)
         and the fit's RMSE / relative RMSE."""
         return {"split_mixed": self.split_mixed,
-                "regimes": {r: {"coef": [getattr(self._params[r], n) for n in _NAMES],
+                "regimes": {r: {"coef": self._params[r].as_list(),
                                 "rmse": self._rmse[r], "rel_rmse": self._rel_rmse[r]} for r in REGIMES}}
 
     def import_state(self, state: dict) -> None:
@@ -324,18 +344,10 @@ class MergedExecutionEstimator:
 
     def _select(self, f: StepFeatures, regime: str | None = None):
         regime = regime or self.regime_of(f)
-        p = self._params[regime]
-        if p.is_fitted:
-            return regime, p
-        order = (REGIME_EAGER, REGIME_FT_MIXED, REGIME_INF_PREFILL, REGIME_DECODE_ONLY)
-        if regime == REGIME_DECODE_BWD:
-            order = (REGIME_DECODE_ONLY,) + order
-        elif regime == REGIME_FT_MIXED:
-            order = (REGIME_EAGER,) + order
-        for r in order:
+        for r in (regime, *_FALLBACK.get(regime, _FALLBACK_DEFAULT)):
             if self._params[r].is_fitted:
                 return r, self._params[r]
-        return regime, p
+        return regime, self._params[regime]
 
     def select_regime(self, f: StepFeatures, regime: str | None = None) -> str | None:
         return self._select(f, regime)[0] if self.is_ready else None
@@ -369,7 +381,7 @@ class MergedExecutionEstimator:
             coef = np.linalg.lstsq(A, y, rcond=None)[0]
             full = np.zeros(6)
             full[cols] = coef
-            self._params[r] = StepParams(*map(float, full))
+            self._params[r] = StepParams(full)
             err = A @ coef - y
             self._rmse[r] = float(np.sqrt(np.mean(err ** 2)))
             pos = y > 1e-6
