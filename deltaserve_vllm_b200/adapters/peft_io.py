@@ -78,11 +78,18 @@ def merge_tp_shards(shards: list[dict[str, torch.Tensor]]) -> dict[str, torch.Te
     return out
 
 
-def _atomic_json(path: str, obj: dict) -> None:
-    tmp = path + ".tmp"
-    with open(tmp, "w") as f:
-        json.dump(obj, f, indent=2)
-    os.replace(tmp, path)
+def write_json_atomic(path: str, obj, indent: int | None = 2) -> None:
+    """``obj`` as JSON at ``path`` (folders made), through a sibling file and
+    one rename, so a reader sees the old document or the new one."""
+    folder = os.path.dirname(os.path.abspath(path))
+    os.makedirs(folder, exist_ok=True)
+    part = os.path.join(folder, f".{os.path.basename(path)}.{os.getpid()}.part")
+    with open(part, "w") as f:
+        json.dump(obj, f, indent=indent)
+    os.replace(part, path)
+
+
+_atomic_json = write_json_atomic
 
 
 def write_peft_adapter(path: str, tensors: dict[str, torch.Tensor], adapter_config: dict,

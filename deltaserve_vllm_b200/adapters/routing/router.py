@@ -136,21 +136,14 @@ class Router:
     def route_many(self, texts: list) -> list[RouteDecision]:
         """One decision per text with ONE encoder call for the batch."""
         self.requests += len(texts)
-        model = self.model
-        out: list = [None] * len(texts)
-        todo = []
-        for i, t in enumerate(texts):
-            if not t or not str(t).strip():
-                out[i] = RouteDecision(None, None, NO_TEXT)
-            elif not model.names:
-                out[i] = RouteDecision(None, None, NO_ADAPTERS)
-            else:
-                todo.append(i)
-        if todo:
-            embs = self.encoder.encode([texts[i] for i in todo])
-            for i, e in zip(todo, embs):
-                out[i] = self._decide(model, e)
-        return out
+        model = self.model                 # one snapshot for the whole batch
+        has_text = [bool(t) and bool(str(t).strip()) for t in texts]
+        if not model.names:
+            return [RouteDecision(None, None, NO_ADAPTERS if ok else NO_TEXT) for ok in has_text]
+        wanted = [t for t, ok in zip(texts, has_text) if ok]
+        embs = iter(self.encoder.encode(wanted) if wanted else ())
+        return [self._decide(model, next(embs)) if ok else RouteDecision(None, None, NO_TEXT)
+                for ok in has_text]
 
     def route_embeddings(self, embs: list) -> list[RouteDecision]:
         self.requests += len(embs)

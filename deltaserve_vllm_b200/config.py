@@ -230,17 +230,18 @@ class AdapterRoutingConfig:
                 raise ValueError(f"adapter_routing.{name} must be >= 0")
         if not 0.0 <= float(self.route_keep_percent) <= 100.0:
             raise ValueError("adapter_routing.route_keep_percent is in [0, 100]")
-        seen: set[str] = set()
-        for a in self.adapters or []:
-            if not isinstance(a, dict) or not a.get("path"):
-                raise ValueError("adapter_routing.adapters: each entry needs a 'path'")
-            unknown = set(a) - {"path", "name", "data_path", "centroid_path", "prewarm"}
-            if unknown:
-                raise ValueError(f"adapter_routing.adapters: unknown key(s) {sorted(unknown)}")
-            if a.get("name"):
-                if a["name"] in seen:
-                    raise ValueError(f"adapter_routing.adapters: duplicate name '{a['name']}'")
-                seen.add(a["name"])
+        entries = list(self.adapters or [])
+        allowed = {"path", "name", "data_path", "centroid_path", "prewarm"}
+        bad = [a for a in entries if not isinstance(a, dict) or not a.get("path")]
+        if bad:
+            raise ValueError("adapter_routing.adapters: each entry needs a 'path'")
+        extra = sorted(set().union(*(set(a) - allowed for a in entries))) if entries else []
+        if extra:
+            raise ValueError(f"adapter_routing.adapters: unknown key(s) {extra}")
+        named = [a["name"] for a in entries if a.get("name")]
+        dup = sorted({n for n in named if named.count(n) > 1})
+        if dup:
+            raise ValueError(f"adapter_routing.adapters: duplicate name '{dup[0]}'")
         if self.router_gpu is not None and int(self.router_gpu) < 0:
             raise ValueError("adapter_routing.router_gpu must be a GPU index >= 0")
         if not -1.0 <= float(self.fallback_score_threshold) <= 1.0:

@@ -190,11 +190,9 @@ def finetune_kwargs(config: dict[str, Any]) -> dict[str, Any]:
 
 
 def finetune_value(config: dict[str, Any], key: str, default: Any = None) -> Any:
-    for section in ALL_FINETUNE_SECTIONS:
-        body = config.get(section) or {}
-        if key in body:
-            return body[key]
-    return default
+    """``key`` from whichever finetune section sets it (first one wins)."""
+    found = (config[s][key] for s in ALL_FINETUNE_SECTIONS if key in (config.get(s) or {}))
+    return next(found, default)
 
 
 def adapter_routing_config(config: dict[str, Any]) -> AdapterRoutingConfig:

@@ -684,11 +684,8 @@ class CoServingEngine:
         self._drain_timing(block=True)
         state = {"version": 1, "estimator": self.estimator.export_state(),
                  "tracker": self.tracker.export_state()}
-        os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
-        tmp = f"{path}.tmp"
-        with open(tmp, "w") as f:
-            json.dump(state, f)
-        os.replace(tmp, path)
+        from ..adapters.peft_io import write_json_atomic
+        write_json_atomic(path, state, indent=None)
         dprint(f"[estimator] state saved to {path}: {self.tracker.size()} samples")
         return path
 

@@ -342,11 +342,10 @@ def dense_attn_bwd(q, k, v, d_o, tiles, scale, dq, dk, dv):
 
 
 def rope_bwd(g: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """Transpose of the NeoX rotate-half RoPE on g [n, H, d] (cos / sin [n, d/2])."""
-    h = g.shape[-1] // 2
-    g1, g2 = g[..., :h], g[..., h:]
-    c, s = cos[:, None, :].float(), sin[:, None, :].float()
-    return torch.cat([g1 * c + g2 * s, g2 * c - g1 * s], dim=-1)
+    """Transpose of the NeoX rotate-half RoPE on g [n, H, d] (cos / sin [n, d/2]),
+    in fp32: the rotation by the opposite angles."""
+    from ..models.rope import rope_backward
+    return rope_backward(g.float(), cos.float(), sin.float())
 
 
 # ----------------------------------------------------------------- LM head + CE on vocabulary slices
