@@ -100,14 +100,17 @@ _NAMES = ("alpha", "beta", "gamma", "delta", "epsilon", "c")
 class StepParams:
     """One regime's fitted model: the coefficient vector ``coef`` over the
     feature row ``[s, T_in, T_ft, B_d, K, 1]`` (named alpha, beta, gamma,
-    delta, epsilon, c), or None while the regime has too few samples."""
+    delta, epsilon, c), or None while the regime has too few samples; and
+    the fit's quality on its own samples (``rmse`` in seconds, ``rel_rmse``
+    relative), which the admission margins use."""
 
-    __slots__ = ("coef",)
+    __slots__ = ("coef", "rmse", "rel_rmse")
 
-    def __init__(self, *coef):
+    def __init__(self, *coef, rmse: float | None = None, rel_rmse: float | None = None):
         vals = list(coef[0]) if len(coef) == 1 and isinstance(coef[0], (list, tuple, np.ndarray)) else list(coef)
         self.coef = (np.asarray(vals, np.float64)
                      if len(vals) == len(_NAMES) and all(v is not None for v in vals) else None)
+        self.rmse, self.rel_rmse = rmse, rel_rmse
 
     @property
     def is_fitted(self) -> bool:
@@ -274,9 +277,7 @@ class MergedExecutionEstimator:
     MARGIN_MODES = ("legacy", "relative", "absolute")
 
     def __init__(self):
-        self._params = {r: StepParams() for r in REGIMES}
-        self._rmse: dict[str, float | None] = {r: None for r in REGIMES}
-        self._rel_rmse: dict[str, float | None] = {r: None for r in REGIMES}
+        self._params = {r: StepParams() for r in REGIMES}     # per regime: coefficients and fit quality
         self.margin_mode = "legacy"
         self.margin_k = 1.5
         # graph_ft_batches: FT rows that share a step with inference work are
@@ -293,12 +294,12 @@ class MergedExecutionEstimator:
 
     def _with_margin(self, pred: float, regime: str) -> float:
         if self.margin_mode == "legacy":
-            r = self._rmse[regime]
+            r = self._params[regime].rmse
             return pred * (1.0 + 1.5 * r) if r else pred
         if self.margin_mode == "relative":
-            r = self._rel_rmse[regime]
+            r = self._params[regime].rel_rmse
             return pred * (1.0 + self.margin_k * r) if r else pred
-        r = self._rmse[regime]
+        r = self._params[regime].rmse
         return pred + self.margin_k * r if r else pred
 
     @property
@@ -310,8 +311,8 @@ class MergedExecutionEstimator:
         """Per regime: the six coefficients (alpha .. c, None when unfitted)
         and the fit's RMSE / relative RMSE."""
         return {"split_mixed": self.split_mixed,
-                "regimes": {r: {"coef": self._params[r].as_list(),
-                                "rmse": self._rmse[r], "rel_rmse": self._rel_rmse[r]} for r in REGIMES}}
+                "regimes": {r: {"coef": p.as_list(), "rmse": p.rmse, "rel_rmse": p.rel_rmse}
+                            for r, p in self._params.items()}}
 
     def import_state(self, state: dict) -> None:
         regimes = state.get("regimes")
@@ -323,21 +324,20 @@ class MergedExecutionEstimator:
         for r, ent in regimes.items():
             if r not in self._params:
                 continue
-            self._params[r] = StepParams(*ent["coef"])
-            self._rmse[r], self._rel_rmse[r] = ent.get("rmse"), ent.get("rel_rmse")
+            self._params[r] = StepParams(*ent["coef"], rmse=ent.get("rmse"), rel_rmse=ent.get("rel_rmse"))
 
     @property
     def fit_rmse(self) -> float | None:
         """RMSE of the most informative fitted regime (FT steps first)."""
-        fitted = [self._rmse[r] for r in (REGIME_EAGER, REGIME_INF_PREFILL, REGIME_DECODE_ONLY)
-                  if self._rmse[r] is not None]
+        fitted = [self._params[r].rmse for r in (REGIME_EAGER, REGIME_INF_PREFILL, REGIME_DECODE_ONLY)
+                  if self._params[r].rmse is not None]
         return fitted[0] if fitted else None
 
     def rmse(self, regime: str) -> float | None:
-        return self._rmse[regime]
+        return self._params[regime].rmse
 
     def rel_rmse(self, regime: str) -> float | None:
-        return self._rel_rmse[regime]
+        return self._params[regime].rel_rmse
 
     def params(self, regime: str) -> StepParams:
         return self._params[regime]
@@ -381,12 +381,12 @@ class MergedExecutionEstimator:
             coef = np.linalg.lstsq(A, y, rcond=None)[0]
             full = np.zeros(6)
             full[cols] = coef
-            self._params[r] = StepParams(full)
             err = A @ coef - y
-            self._rmse[r] = float(np.sqrt(np.mean(err ** 2)))
             pos = y > 1e-6
-            self._rel_rmse[r] = float(np.sqrt(np.mean((err[pos] / y[pos]) ** 2))) if pos.any() else None
-            msg.append(f"{r}={int(sel.sum())}(rmse={self._rmse[r]:.5f})")
+            fit = StepParams(full, rmse=float(np.sqrt(np.mean(err ** 2))),
+                             rel_rmse=float(np.sqrt(np.mean((err[pos] / y[pos]) ** 2))) if pos.any() else None)
+            self._params[r] = fit
+            msg.append(f"{r}={int(sel.sum())}(rmse={fit.rmse:.5f})")
         if msg:
             dprint("[estimator] fit: " + ", ".join(msg))
         return self._params
