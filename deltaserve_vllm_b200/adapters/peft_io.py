@@ -89,8 +89,6 @@ def write_json_atomic(path: str, obj, indent: int | None = 2) -> None:
     os.replace(part, path)
 
 
-_atomic_json = write_json_atomic
-
 
 def write_peft_adapter(path: str, tensors: dict[str, torch.Tensor], adapter_config: dict,
                        state: dict) -> None:
@@ -99,16 +97,16 @@ def write_peft_adapter(path: str, tensors: dict[str, torch.Tensor], adapter_conf
     save_file({k: v.detach().float().contiguous().cpu() for k, v in tensors.items()}, tmp,
               metadata={"format": "pt"})
     os.replace(tmp, os.path.join(path, WEIGHTS_FILE))
-    _atomic_json(os.path.join(path, CONFIG_FILE), adapter_config)
+    write_json_atomic(os.path.join(path, CONFIG_FILE), adapter_config)
     err = os.path.join(path, ERROR_FILE)
     if os.path.exists(err):
         os.remove(err)
-    _atomic_json(os.path.join(path, STATE_FILE), state)
+    write_json_atomic(os.path.join(path, STATE_FILE), state)
 
 
 def write_save_error(path: str, save_id: str, error: str) -> None:
     os.makedirs(path, exist_ok=True)
-    _atomic_json(os.path.join(path, ERROR_FILE), {"save_id": save_id, "error": error})
+    write_json_atomic(os.path.join(path, ERROR_FILE), {"save_id": save_id, "error": error})
 
 
 def read_save_result(path: str, save_id: str) -> dict | None:
