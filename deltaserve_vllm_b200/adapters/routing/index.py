@@ -223,8 +223,9 @@ class CentroidIndex:
     def add(self, name: str, centroid, refs=None) -> None:
         """Insert or replace ``name`` (a replaced adapter keeps its position)."""
         c = l2_normalize(np.asarray(centroid, np.float32).reshape(-1)).astype(np.float32)
-        if self._cent and name not in self._cent and c.shape[0] != self.dim:
-            raise ValueError(f"centroid dim {c.shape[0]} != index dim {self.dim}")
+        others = [v for k, v in self._cent.items() if k != name]
+        if others and c.shape[0] != others[0].shape[0]:
+            raise ValueError(f"centroid dim {c.shape[0]} != index dim {others[0].shape[0]}")
         self._cent[name] = c
         if refs is not None and len(refs):
             self._refs[name] = np.asarray(refs, np.float32)

@@ -27,6 +27,9 @@ def test_index_round_trip_replace_and_snapshot(tmp_path):
     q = rng.normal(size=8)
     np.testing.assert_allclose(back.scores(q), idx.matrix @ l2_normalize(q), rtol=1e-5)
     assert idx.remove("b") and not idx.remove("b") and idx.names == ["a", "c"] and idx.matrix.shape == (2, 8)
+    import pytest
+    with pytest.raises(ValueError, match="dim"):
+        idx.add("a", np.ones(5))                               # even when replacing an entry
     np.savez(str(tmp_path / "other.npz"), meta=np.array("x"))
     assert CentroidIndex.load_or_none(str(tmp_path / "other.npz")) is None
     assert CentroidIndex.load_or_none(str(tmp_path / "missing.npz")) is None
