@@ -166,6 +166,18 @@ PEFT_MODULE = {"q": "self_attn.q_proj", "k": "self_attn.k_proj",
                "down": "mlp.down_proj"}
 
 
+# Lower bounds of the numeric routing knobs: counts and sizes need at least
+# one; times, shares and slot counts may be zero.
+_ROUTING_LOWER_BOUNDS = {
+    **dict.fromkeys(("encoder_max_tokens", "max_active_adapters", "route_encode_max_tokens",
+                     "indexing_max_samples", "indexing_chunk_samples", "indexing_cpu_max_threads",
+                     "indexing_gpu_chunk_samples", "route_min_pool"), 1),
+    **dict.fromkeys(("indexing_gpu_after_quiet_s", "pool_protected_slots", "indexing_cpu_busy_threads",
+                     "pool_hit_half_life_s", "route_close_band", "route_confidence_slack", "retire_grace_s",
+                     "route_reference_samples"), 0),
+}
+
+
 @dataclass
 class AdapterRoutingConfig:
     """Adapter routing knobs (``adapter_routing`` YAML section)."""
@@ -215,19 +227,9 @@ class AdapterRoutingConfig:
             raise ValueError("adapter_routing.encoder must not be empty")
         _check_choice("adapter_routing.when_full", self.when_full,
                       ("retire_least_used", "admit_retired", "reject"))
-        for name in ("encoder_max_tokens", "max_active_adapters",
-                     "route_encode_max_tokens", "indexing_max_samples",
-                     "indexing_chunk_samples", "indexing_cpu_max_threads",
-                     "indexing_gpu_chunk_samples",
-                     "route_min_pool"):
-            if int(getattr(self, name)) < 1:
-                raise ValueError(f"adapter_routing.{name} must be >= 1")
-        for name in ("indexing_gpu_after_quiet_s", "pool_protected_slots", "indexing_cpu_busy_threads",
-                     "pool_hit_half_life_s", "route_close_band",
-                     "route_confidence_slack", "retire_grace_s",
-                     "route_reference_samples"):
-            if float(getattr(self, name)) < 0:
-                raise ValueError(f"adapter_routing.{name} must be >= 0")
+        below = [(k, lo) for k, lo in _ROUTING_LOWER_BOUNDS.items() if float(getattr(self, k)) < lo]
+        if below:
+            raise ValueError(f"adapter_routing.{below[0][0]} must be >= {below[0][1]}")
         if not 0.0 <= float(self.route_keep_percent) <= 100.0:
             raise ValueError("adapter_routing.route_keep_percent is in [0, 100]")
         entries = list(self.adapters or [])
